@@ -1,0 +1,357 @@
+"""Benchmark: ResNet-50 bf16 inference, batch 256 per GPU, 224x224.
+
+One process per GPU (torchrun for N > 1). Each rank builds the fused NHWC bf16 inference
+plan (BatchNorm folded into tcgen05 implicit-GEMM convs, captured in one CUDA graph) and
+processes its own 256 images: inference needs no collective, so scaling is weak and the
+only cross-rank traffic is the host-side barrier and the max-over-ranks of the timings.
+
+Printed JSON line (rank 0):
+  value   images/s of the whole job, device-resident inputs, graph replay, max over ranks
+  e2e     images/s through the public C-ABI path with host buffers: per step the pinned
+          host->device copy of the step's NCHW fp32 input, the forward, and the
+          device->host copy of the logits, all inside the timed region
+  roofline  the dominant kernel (conv_tc_kernel): algorithmic conv+FC FLOPs of one step
+          divided by the summed duration of its launches, from CUDA events around each
+          launch in an instrumented eager pass of the same steps
+  cpu_baseline  the reference engine's own CPU ResNet-50 forward (oracle/_ref/libomref.so,
+          AVX2 + OpenMP on every host core) on a bounded sample, rank 0 at N=1 only
+
+--impl reference times that reference CPU implementation on the host cores instead.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "ResNet-50 bf16 images/s at 1/2/4/8 B200; conv implicit-GEMM % of TC peak"
+BATCH = 256
+
+
+def _peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return d["bf16_tflops"], d["bf16_tflops_sustained"], d["hbm_gbs"], "measured"
+    except Exception:
+        return 1590.0, 1400.0, 6650.0, "fallback"
+
+
+def _dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
+        return world, rank, local, dist
+    return world, rank, local, None
+
+
+def _barrier(dist):
+    if dist is not None:
+        dist.barrier()
+
+
+def _max_over_ranks(dist, v: float) -> float:
+    if dist is None:
+        return v
+    import torch
+    t = torch.tensor([v], dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.file, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.file.flush()
+        self.file.seek(0)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.file.read().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(nm)
+        os.unlink(self.file.name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def _reference_cpu(batch: int, iters_min: int, seconds: float):
+    """The reference engine's CPU ResNet-50 forward on `batch` images (or the oracle port
+    when the reference library was not built). Returns (images/s, kind, cores, sample)."""
+    import numpy as np
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as orc
+    from omnimatchdeeplearningtool_b200 import synth
+    net = synth.resnet_spec(50)
+    w = synth.make_weights(net)
+    x = synth.normal_input(batch)
+    cores = os.cpu_count() or 1
+    h = orc.ref_model(1, 1000, w, net)
+    out = np.empty((batch, 1000), np.float32)
+    if h is not None:
+        kind = "reference"
+        run = lambda: orc.ref().omref_model_forward(h, x.ctypes.data, batch, 224, 224, out.ctypes.data)
+    else:
+        kind = "port"
+        run = lambda: orc.forward(net, w, x)
+    run()  # warm-up
+    t0 = time.perf_counter()
+    n = 0
+    while n < iters_min or time.perf_counter() - t0 < seconds:
+        run()
+        n += 1
+    dt = time.perf_counter() - t0
+    sample = (f"ResNet-50 fp32 forward, batch {batch} at 224x224, {n} iterations "
+              f"({dt:.1f} s), OMP threads={cores}")
+    return n * batch / dt, kind, cores, sample
+
+
+def run_reference(args, world, rank, dist):
+    if rank != 0:
+        return
+    import numpy as np
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as orc
+    from omnimatchdeeplearningtool_b200 import synth
+    net = synth.resnet_spec(50)
+    w = synth.make_weights(net)
+    batch = args.ref_batch
+    x = synth.normal_input(batch)
+    h = orc.ref_model(1, 1000, w, net)
+    out = np.empty((batch, 1000), np.float32)
+    if h is not None:
+        kind = "reference"
+        run = lambda: orc.ref().omref_model_forward(h, x.ctypes.data, batch, 224, 224, out.ctypes.data)
+    else:
+        kind = "port"
+        run = lambda: orc.forward(net, w, x)
+    for _ in range(args.warmup):
+        run()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        run()
+    dt = time.perf_counter() - t0
+    v = args.steps * batch / dt
+    cores = os.cpu_count() or 1
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "images/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,1) inputs, He-normal weights)",
+        "config": {"workload": f"resnet50 inference (reference CPUBackend, fp32), batch {batch} "
+                               "per step at 224x224", "batch": batch},
+        "cpu_baseline": {"value": v, "unit": "images/s", "cores": cores, "kind": kind,
+                         "sample": f"ResNet-50 fp32 forward, batch {batch} per step"},
+        "e2e": {"value": v, "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, world, rank, local, dist):
+    import numpy as np
+    import torch
+    from omnimatchdeeplearningtool_b200 import _lib, backend, synth
+    from omnimatchdeeplearningtool_b200._lib import call
+    from omnimatchdeeplearningtool_b200.backend import DeviceBuffer
+    from omnimatchdeeplearningtool_b200.plan import InferencePlan
+
+    backend.init(local)
+    torch.cuda.set_device(local)
+    stream = torch.cuda.ExternalStream(backend.stream_handle(), device=local)
+    net = synth.resnet_spec(50)
+    weights = synth.make_weights(net)
+    plan = InferencePlan(net, weights, batch=BATCH, dtype=_lib.DTYPE_BF16)
+    x = synth.normal_input(BATCH, seed=rank)
+    plan.set_input(x)
+    plan.launch()
+    call("omCudaSynchronize")
+    plan.capture()
+    kernels_per_step = plan.n_launches
+
+    def ev():
+        return torch.cuda.Event(enable_timing=True)
+
+    # ---------------------------------------------------------------- device-resident value
+    for _ in range(args.warmup):
+        plan.launch()
+    call("omCudaSynchronize")
+    clocks = ClockSampler(local)
+    clocks.start()
+    _barrier(dist)
+    torch.cuda.synchronize()
+    e0, e1 = ev(), ev()
+    with torch.cuda.stream(stream):
+        e0.record()
+        for _ in range(args.steps):
+            plan.launch()
+        e1.record()
+    e1.synchronize()
+    torch.cuda.synchronize()
+    _barrier(dist)
+    clk = clocks.stop()
+    t_dev = e0.elapsed_time(e1) / 1e3
+    t_dev_max = _max_over_ranks(dist, t_dev)
+    value = args.steps * BATCH * world / t_dev_max
+
+    # ---------------------------------------------------------------- end to end, host buffers
+    in_bytes = BATCH * 3 * 224 * 224 * 4
+    out_bytes = BATCH * net.classes * 4
+    import ctypes
+    hin, hout = ctypes.c_void_p(), ctypes.c_void_p()
+    call("omCudaMallocHost", ctypes.byref(hin), in_bytes)
+    call("omCudaMallocHost", ctypes.byref(hout), out_bytes)
+    ctypes.memmove(hin.value, x.ctypes.data, in_bytes)
+    for _ in range(max(1, args.warmup // 2)):
+        call("omCudaAsyncCopyH2D", plan.in_f32.ptr, hin.value, in_bytes)
+        plan.launch()
+        call("omCudaAsyncCopyD2H", hout.value, plan.logits.ptr, out_bytes)
+    call("omCudaSynchronize")
+    _barrier(dist)
+    torch.cuda.synchronize()
+    e2, e3 = ev(), ev()
+    with torch.cuda.stream(stream):
+        e2.record()
+        for _ in range(args.steps):
+            call("omCudaAsyncCopyH2D", plan.in_f32.ptr, hin.value, in_bytes)
+            plan.launch()
+            call("omCudaAsyncCopyD2H", hout.value, plan.logits.ptr, out_bytes)
+        e3.record()
+    e3.synchronize()
+    _barrier(dist)
+    t_e2e = _max_over_ranks(dist, e2.elapsed_time(e3) / 1e3)
+    e2e = args.steps * BATCH * world / t_e2e
+    logits = np.frombuffer(ctypes.string_at(hout.value, out_bytes), np.float32)
+    finite = bool(np.isfinite(logits).all())
+    call("omCudaFreeHost", hin.value)
+    call("omCudaFreeHost", hout.value)
+
+    # ---------------------------------------------------------------- instrumented pass
+    conv_ms, total_ms, conv_launches = 0.0, 0.0, 0
+    prof_steps = max(1, min(args.steps, 5))
+    with torch.cuda.stream(stream):
+        for _ in range(prof_steps):
+            marks = [ev() for _ in range(len(plan.ops) + 1)]
+            marks[0].record()
+            for i, fn in enumerate(plan.ops):
+                fn()
+                marks[i + 1].record()
+            marks[-1].synchronize()
+            for i in range(len(plan.ops)):
+                d = marks[i].elapsed_time(marks[i + 1])
+                total_ms += d
+                if i in plan.tc_op_index:
+                    conv_ms += d
+                    conv_launches += 1
+    achieved = plan.conv_flops * prof_steps / (conv_ms / 1e3) / 1e12
+    peak_burst, peak_sust, _, peak_src = _peaks()
+    share = conv_ms / total_ms if total_ms else None
+    err = backend.kernel_error()
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "images/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": t_dev_max / args.steps * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) inputs, He-normal weights, BN running stats seeded)",
+            "config": {"workload": "resnet50 (ImageNet stem) bf16 inference, NHWC fused plan, "
+                                   "CUDA-graph replay", "batch_per_gpu": BATCH,
+                       "global_batch": BATCH * world, "image": "3x224x224",
+                       "parallelism": f"batch-sharded x{world}, no collective",
+                       "l2": "inputs larger than L2 (154 MB fp32 input, >1 GB activations "
+                             "per step)"},
+            "e2e": {"value": e2e, "unit": "images/s", "h2d_bytes_per_step": in_bytes,
+                    "d2h_bytes_per_step": out_bytes},
+            "roofline": {"bound": "tensor", "kernel": "conv_tc_kernel (tcgen05 implicit GEMM)",
+                         "achieved": achieved, "peak": peak_sust, "unit": "TFLOP/s",
+                         "frac": achieved / peak_sust,
+                         "peak_kind": f"bf16_tflops_sustained ({peak_src})",
+                         "frac_of_burst": achieved / peak_burst,
+                         "conv_share_of_step": share, "traffic": None,
+                         "flops_per_step": plan.conv_flops,
+                         "launches_per_step": len(plan.tc_op_index)},
+            "gpu_launches": kernels_per_step * args.steps,
+            "clocks": clk,
+            "kernel_error": err,
+            "logits_finite": finite,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            v, kind, cores, sample = _reference_cpu(8, 2, 10.0)
+            line["cpu_baseline"] = {"value": v, "unit": "images/s", "cores": cores,
+                                    "kind": kind, "sample": sample}
+        print(json.dumps(line), flush=True)
+    plan.close()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--ref-batch", type=int, default=4)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    world, rank, local, dist = _dist()
+    try:
+        if args.impl == "reference":
+            run_reference(args, world, rank, dist)
+        else:
+            run_ours(args, world, rank, local, dist)
+    finally:
+        if dist is not None:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,206 @@
+/*
+ * om_cuda.h — C ABI of the B200 (sm_100a) compute backend for the OmniMatch engine.
+ *
+ * Drop-in for the hot-path subset of the reference's src/cuda/cuda_kernels.cuh: every
+ * function below that carries a "replaces" line has the same name, argument order and
+ * argument meaning as the reference entry point it names (cuda_kernels.cu:<line>), so the
+ * reference's CUDABackend (src/hal/om.hal.cuda_backend.ixx) links against this library
+ * unchanged. Functions marked "new" extend the ABI for NHWC / bf16 / fp16 fused execution.
+ *
+ * Conventions (same as the reference unless stated):
+ *   - return 0 on success, a negative OM_* status on failure (the reference returns -1 for
+ *     every failure; all our codes are negative, so `!= 0` checks keep working);
+ *   - all pointers are device pointers unless the name says Host;
+ *   - calls are asynchronous on the calling thread's current device's compute stream and
+ *     stream-ordered with each other; omCudaSynchronize waits for them;
+ *   - layouts of the reference ops are NCHW fp32; weights [Cout, Cin/groups, KH, KW];
+ *   - one host thread may drive one device at a time (omCudaInit/omCudaSetDevice select it
+ *     for the calling thread), so one process can drive all 8 GPUs from 8 threads.
+ */
+#ifndef OM_CUDA_H
+#define OM_CUDA_H
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes (all failures are negative) */
+#define OM_OK 0
+#define OM_ERR_CUDA (-1)          /* a CUDA runtime call failed */
+#define OM_ERR_INVALID (-2)       /* bad argument: size, alignment, null pointer */
+#define OM_ERR_UNSUPPORTED (-3)   /* shape/dtype combination this kernel does not cover */
+#define OM_ERR_NOT_INIT (-4)      /* omCudaInit was not called on this thread */
+#define OM_ERR_OOM (-5)           /* device allocation failed after releasing the cache */
+#define OM_ERR_KERNEL_TIMEOUT (-6)/* a bounded in-kernel wait gave up (see omCudaGetKernelError) */
+#define OM_ERR_DRIVER (-7)        /* a driver entry point (tensor-map encode) was unavailable */
+
+/* element types for the NHWC entry points */
+#define OM_DTYPE_F32 0
+#define OM_DTYPE_BF16 1
+#define OM_DTYPE_F16 2
+
+/* fused epilogue activations */
+#define OM_ACT_NONE 0
+#define OM_ACT_RELU 1
+#define OM_ACT_RELU6 2
+
+/* ---------------- device, memory, streams ---------------- */
+int omCudaInit(int nDeviceId);                                         /* replaces :287 */
+int omCudaGetDeviceCount(void);                                        /* replaces :299 */
+int omCudaGetDeviceName(int nDeviceId, char* pNameBuf, int nBufSize);  /* replaces :306 */
+int omCudaGetMemInfo(int nDeviceId, size_t* pFreeMem, size_t* pTotalMem); /* replaces :314 */
+int omCudaGetComputeCapability(int nDeviceId, int* pMajor, int* pMinor);  /* replaces :324 */
+int omCudaMalloc(void** ppDevPtr, size_t nBytes);                      /* replaces :336 */
+int omCudaFree(void* pDevPtr);                                         /* replaces :345 */
+int omCudaCopyH2D(void* pDst, const void* pSrc, size_t nBytes);        /* replaces :353 */
+int omCudaCopyD2H(void* pDst, const void* pSrc, size_t nBytes);        /* replaces :365 */
+int omCudaCopyD2D(void* pDst, const void* pSrc, size_t nBytes);        /* replaces :371 */
+int omCudaMemset(void* pDev, int nValue, size_t nBytes);               /* replaces :377 */
+int omCudaSynchronize(void);                                           /* replaces :383 */
+int omCudaAsyncCopyH2D(void* pDst, const void* pSrc, size_t nBytes);   /* replaces :390 */
+int omCudaAsyncCopyD2H(void* pDst, const void* pSrc, size_t nBytes);   /* replaces :397 */
+int omCudaSyncTransferStream(void);                                    /* replaces :404 */
+int omCudaSyncComputeStream(void);                                     /* replaces :412 */
+int omCudaCleanup(void);                                               /* replaces :420 */
+int omCudaMallocHost(void** ppPtr, size_t nBytes);                     /* replaces :4887 */
+int omCudaFreeHost(void* pPtr);                                        /* replaces :4895 */
+int omCudaGraphBeginCapture(void);                                     /* replaces :4909 */
+int omCudaGraphEndCapture(void** pGraphExec);                          /* replaces :4919 */
+int omCudaGraphLaunch(void* pGraphExec);                               /* replaces :4941 */
+int omCudaGraphDestroy(void* pGraphExec);                              /* replaces :4949 */
+/* new: select the calling thread's device (must have been omCudaInit'ed once per thread) */
+int omCudaSetDevice(int nDeviceId);
+/* new: the compute stream of the calling thread's device, as a cudaStream_t */
+void* omCudaGetStream(void);
+/* new: read and clear the device error word that bounded in-kernel waits set; *pCode is 0
+ * when no kernel gave up since the last call. Synchronises the compute stream. */
+int omCudaGetKernelError(unsigned int* pCode);
+/* new: number of kernels this library has launched on the calling thread's device */
+int omCudaGetLaunchCount(unsigned long long* pCount);
+
+/* ---------------- elementwise / fills (fp32) ---------------- */
+int omCudaAdd(const float* pA, const float* pB, float* pC, int nCount);          /* replaces :467 */
+int omCudaMulScalar(const float* pA, float fScalar, float* pC, int nCount);      /* replaces :542 */
+int omCudaReLU(const float* pIn, float* pOut, int nCount);                       /* replaces :585 */
+int omCudaReLUBackward(const float* pIn, const float* pGradOut, float* pGradIn, int nCount); /* :600 */
+int omCudaClip(const float* pIn, float* pOut, int nCount, float fMin, float fMax); /* replaces :3763 */
+int omCudaFillZeros(float* pData, int nCount);                                   /* replaces :2346 */
+int omCudaFillOnes(float* pData, int nCount);                                    /* replaces :2363 */
+int omCudaFillValue(float* pData, int nCount, float fValue);                     /* replaces :2380 */
+int omCudaCopy(const float* pSrc, float* pDst, int nCount);                      /* replaces :2388 */
+int omCudaSum(const float* pData, float* pResult, int nCount);                   /* replaces :1473 */
+int omCudaArgmax(const float* pData, int* pOut, int nBatch, int nClasses);       /* replaces :2415 */
+int omCudaTranspose(const float* pIn, float* pOut, int nRows, int nCols);        /* replaces :707 */
+
+/* ---------------- dense contractions (fp32, reference layouts) ---------------- */
+/* C[M,N] = A[M,K] . B[K,N], row-major */
+int omCudaMatmul(const float* pA, const float* pB, float* pC, int nM, int nK, int nN); /* :768 */
+/* out = conv(in, w) + b, NCHW; pBias may be NULL */
+int omCudaConv2d(const float* pInput, const float* pWeight, const float* pBias, float* pOutput,
+                 int nBatch, int nCin, int nH, int nW, int nCout, int nKH, int nKW,
+                 int nStride, int nPad);                                         /* replaces :1076 */
+/* grouped / dilated direct conv (groups == Cin == Cout is depthwise) */
+int omCudaDilatedConv2d(const float* pInput, const float* pWeight, const float* pBias,
+                        float* pOutput, int nBatch, int nCin, int nH, int nW, int nCout,
+                        int nKH, int nKW, int nStride, int nPad, int nDilation,
+                        int nGroups);                                            /* replaces :1201 */
+/* dX = conv^T(dY, W); overwrites pGradInput */
+int omCudaConv2dBackwardInput(const float* pGradOutput, const float* pWeight, float* pGradInput,
+                              int nBatch, int nCin, int nH, int nW, int nCout, int nKH, int nKW,
+                              int nStride, int nPad);                            /* replaces :2600 */
+/* dW = sum_n dY (x) im2col(X), dB = sum dY; overwrites both (pGradBias may be NULL) */
+int omCudaConv2dBackwardWeight(const float* pInput, const float* pGradOutput, float* pGradWeight,
+                               float* pGradBias, int nBatch, int nCin, int nH, int nW,
+                               int nCout, int nKH, int nKW, int nStride, int nPad); /* :2739 */
+
+/* ---------------- normalisation, pooling, losses, optimiser (fp32 NCHW) ---------------- */
+int omCudaBatchNorm2d(const float* pInput, float* pOutput, const float* pGamma,
+                      const float* pBeta, float* pRunMean, float* pRunVar, float* pSavedMean,
+                      float* pSavedInvStd, int nBatch, int nChannels, int nH, int nW,
+                      float fEps, float fMomentum, int bTraining);              /* replaces :1648 */
+int omCudaBatchNorm2dBackward(const float* pGradOutput, const float* pInput, const float* pMean,
+                              const float* pInvStd, const float* pGamma, float* pGradInput,
+                              float* pGradGamma, float* pGradBeta, int nBatch, int nChannels,
+                              int nH, int nW, float fEps);                       /* replaces :3130 */
+int omCudaMaxPool2d(const float* pIn, float* pOut, int* pIndices, int nN, int nC, int nH, int nW,
+                    int nKH, int nKW, int nSH, int nSW, int nPH, int nPW);       /* replaces :2052 */
+/* accumulates into pGradIn (callers zero it first, as CUDABackend::maxPool2dBackward does) */
+int omCudaMaxPool2dBackward(const float* pGradOut, const int* pIndices, float* pGradIn, int nN,
+                            int nC, int nH, int nW, int nHout, int nWout);       /* replaces :2083 */
+int omCudaAvgPool2d(const float* pIn, float* pOut, int nN, int nC, int nH, int nW, int nKH,
+                    int nKW, int nSH, int nSW, int nPH, int nPW);                /* replaces :2127 */
+/* accumulates into pGradIn (callers zero it first) */
+int omCudaAvgPool2dBackward(const float* pGradOut, float* pGradIn, int nN, int nC, int nH,
+                            int nW, int nKH, int nKW, int nSH, int nSW, int nPH, int nPW); /* :2175 */
+int omCudaAdaptiveAvgPool2d(const float* pIn, float* pOut, int nN, int nC, int nH, int nW,
+                            int nOutH, int nOutW);                               /* replaces :2225 */
+int omCudaAdaptiveAvgPool2dBackward(const float* pGradOut, float* pGradIn, int nBatch,
+                                    int nChannels, int nH, int nW, int nOutH, int nOutW); /* :3532 */
+/* out[n,c,hw] = in[n,c,hw] + bias[c] */
+int omCudaAddBias(const float* pData, const float* pBias, float* pOut, int nN, int nC, int nHW); /* :2253 */
+/* gradBias[c] = sum_{n,hw} gradOut[n,c,hw] (overwrites) */
+int omCudaAddBiasBackward(const float* pGradOut, float* pGradBias, int nN, int nC, int nHW); /* :3569 */
+/* row softmax; divides by the plain sum as the CPU backend does (cpu_backend.ixx:352-370) */
+int omCudaSoftmax(const float* pIn, float* pOut, int nBatch, int nClasses);      /* replaces :1456 */
+/* *pResult (device) = -sum_{target>0.5} log(max(p,1e-7)) / nBatch (cpu_backend.ixx:375-388) */
+int omCudaCrossEntropy(const float* pSoftmax, const float* pTarget, float* pResult, int nBatch,
+                       int nClasses);                                            /* replaces :3973 */
+int omCudaSoftmaxCrossEntropyBackward(const float* pSoftmax, const float* pTarget,
+                                      float* pGradLogits, int nBatch, int nClasses); /* :2539 */
+/* v = m*v + g; p -= lr*v (m == 0 or pVelocity == NULL: p -= lr*g) */
+int omCudaSgdStep(float* pParam, const float* pGrad, float* pVelocity, int nCount, float fLr,
+                  float fMomentum);                                              /* replaces :2511 */
+
+/* ---------------- new: NHWC bf16/fp16 fused inference path ---------------- */
+/* Elements of the packed K-major weight [Cout, Kpad] that omCudaPackConvWeight writes, where
+ * Kpad = round_up(KH*KW*Cs, 64) and Cs = stored input channels (omCudaStoredChannels). */
+long long omCudaPackedConvWeightElems(int nCout, int nKH, int nKW, int nCs);
+/* stored channel count for an NHWC activation with nC logical channels: nC when it is a
+ * multiple of 64, else nC rounded up to a multiple of 8 */
+int omCudaStoredChannels(int nC);
+/* Fold eval-mode BatchNorm (gamma,beta,mean,var,eps; any may be NULL for "no BN") and an
+ * optional conv bias into a packed K-major weight (dtype) and an fp32 bias[Cout]:
+ * w' = w*gamma/sqrt(var+eps), b' = beta + (b - mean)*gamma/sqrt(var+eps). */
+int omCudaPackConvWeight(const float* pWeight, const float* pConvBias, const float* pGamma,
+                         const float* pBeta, const float* pMean, const float* pVar, float fEps,
+                         void* pPacked, float* pBiasOut, int nCout, int nCin, int nKH, int nKW,
+                         int nCs, int nDtype);
+/* Implicit-GEMM conv on tcgen05 tensor cores, NHWC, no im2col buffer:
+ *   out[n,p,q,k] = act( sum_{r,s,c} in[n, p*st-pad+r, q*st-pad+s, c] * W'[k,(r,s,c)]
+ *                       + bias[k] + residual[n,p,q,k] )
+ * in: [N,H,W,Cs] (nDtype), out/residual: [N,P,Q,Cout] (nOutDtype; residual may be NULL),
+ * bias fp32 [Cout] (may be NULL), W' from omCudaPackConvWeight. Cs % 8 == 0, Cout % 8 == 0. */
+int omCudaConv2dBnAct(const void* pInput, const void* pPacked, const float* pBias,
+                      const void* pResidual, void* pOutput, int nBatch, int nH, int nW, int nCs,
+                      int nCout, int nKH, int nKW, int nStride, int nPad, int nAct, int nDtype,
+                      int nOutDtype);
+/* NCHW fp32 -> NHWC (nDtype) with channels zero-padded to nCs */
+int omCudaNchwToNhwc(const float* pIn, void* pOut, int nN, int nC, int nH, int nW, int nCs,
+                     int nDtype);
+/* NHWC (nDtype, nCs stored channels) -> NCHW fp32 with nC channels */
+int omCudaNhwcToNchw(const void* pIn, float* pOut, int nN, int nC, int nH, int nW, int nCs,
+                     int nDtype);
+/* NHWC max pool (nDtype), same window semantics as omCudaMaxPool2d, no indices */
+int omCudaMaxPool2dNhwc(const void* pIn, void* pOut, int nN, int nH, int nW, int nCs, int nK,
+                        int nStride, int nPad, int nDtype);
+/* NHWC global average pool: out[n,c] = mean_{h,w} in[n,h,w,c] (out in nOutDtype) */
+int omCudaGlobalAvgPoolNhwc(const void* pIn, void* pOut, int nN, int nHW, int nCs, int nDtype,
+                            int nOutDtype);
+/* Fold BN into a depthwise weight [C,1,KH,KW] -> fp32 [KH*KW, Cs] plus bias [Cs] */
+int omCudaPackDepthwiseWeight(const float* pWeight, const float* pGamma, const float* pBeta,
+                              const float* pMean, const float* pVar, float fEps, float* pPacked,
+                              float* pBiasOut, int nC, int nKH, int nKW, int nCs);
+/* NHWC depthwise conv with fused bias + activation (bandwidth-bound, CUDA cores) */
+int omCudaDepthwiseConv2dNhwc(const void* pIn, const float* pPacked, const float* pBias,
+                              void* pOut, int nN, int nH, int nW, int nCs, int nKH, int nKW,
+                              int nStride, int nPad, int nAct, int nDtype);
+/* elementwise NHWC residual add + activation: out = act(a + b) (nDtype) */
+int omCudaAddActNhwc(const void* pA, const void* pB, void* pOut, long long nCount, int nAct,
+                     int nDtype);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* OM_CUDA_H */

@@ -1,0 +1,229 @@
+"""Host-side mirror of the reference's ``om::CUDABackend`` (src/hal/om.hal.cuda_backend.ixx).
+
+Each static method keeps the reference method's name and argument order (including the
+argument orders that differ from the C ABI, e.g. ``conv2d``'s pad-before-stride and
+``batchNorm2d``'s gamma/beta-before-output) and forwards to one C-ABI entry point of
+libomcuda.so. Unlike the reference wrapper, which discards every return code
+(cuda_backend.ixx:325-329, :438-452), a non-zero status raises :class:`OmCudaError`.
+
+Pointers are plain device addresses (``int``) such as :attr:`DeviceBuffer.ptr`.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+
+from ._lib import OmCudaError, call, lib  # noqa: F401  (re-exported)
+
+_NP_FROM_DT = {0: np.float32}
+
+
+def init(device: int = 0) -> None:
+    """omCudaInit for the calling thread (cuda_kernels.cu:287)."""
+    call("omCudaInit", device)
+
+
+def synchronize() -> None:
+    call("omCudaSynchronize")
+
+
+def stream_handle() -> int:
+    """The library's compute stream on the calling thread's device (cudaStream_t)."""
+    return int(lib.omCudaGetStream() or 0)
+
+
+def kernel_error() -> int:
+    code = ctypes.c_uint(0)
+    call("omCudaGetKernelError", ctypes.byref(code))
+    return int(code.value)
+
+
+def launch_count() -> int:
+    n = ctypes.c_ulonglong(0)
+    call("omCudaGetLaunchCount", ctypes.byref(n))
+    return int(n.value)
+
+
+class DeviceBuffer:
+    """A device allocation from omCudaMalloc, freed with omCudaFree."""
+
+    def __init__(self, nbytes: int):
+        self.nbytes = int(max(nbytes, 1))
+        p = ctypes.c_void_p()
+        call("omCudaMalloc", ctypes.byref(p), self.nbytes)
+        self.ptr = int(p.value)
+
+    @classmethod
+    def from_numpy(cls, arr: np.ndarray) -> "DeviceBuffer":
+        arr = np.ascontiguousarray(arr)
+        buf = cls(arr.nbytes)
+        call("omCudaCopyH2D", buf.ptr, arr.ctypes.data, arr.nbytes)
+        return buf
+
+    @classmethod
+    def zeros(cls, nbytes: int) -> "DeviceBuffer":
+        buf = cls(nbytes)
+        call("omCudaMemset", buf.ptr, 0, buf.nbytes)
+        return buf
+
+    def upload(self, arr: np.ndarray) -> None:
+        arr = np.ascontiguousarray(arr)
+        assert arr.nbytes <= self.nbytes
+        call("omCudaCopyH2D", self.ptr, arr.ctypes.data, arr.nbytes)
+
+    def to_numpy(self, shape, dtype=np.float32) -> np.ndarray:
+        out = np.empty(shape, dtype=dtype)
+        assert out.nbytes <= self.nbytes
+        call("omCudaCopyD2H", out.ctypes.data, self.ptr, out.nbytes)
+        return out
+
+    def free(self) -> None:
+        if getattr(self, "ptr", 0):
+            try:
+                lib.omCudaFree(self.ptr)
+            finally:
+                self.ptr = 0
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+class CUDABackend:
+    """Static methods named and ordered as om::CUDABackend (om.hal.cuda_backend.ixx:283-984)."""
+
+    @staticmethod
+    def add(a, b, out, n):  # :288
+        call("omCudaAdd", a, b, out, n)
+
+    @staticmethod
+    def mulScalar(a, s, out, n):
+        call("omCudaMulScalar", a, s, out, n)
+
+    @staticmethod
+    def matmul(a, b, c, m, k, n):  # :325
+        call("omCudaMatmul", a, b, c, m, k, n)
+
+    @staticmethod
+    def transpose(inp, out, rows, cols):
+        call("omCudaTranspose", inp, out, rows, cols)
+
+    @staticmethod
+    def relu(inp, out, n):  # :349
+        call("omCudaReLU", inp, out, n)
+
+    @staticmethod
+    def reluBackward(inp, grad_out, grad_in, n):
+        call("omCudaReLUBackward", inp, grad_out, grad_in, n)
+
+    @staticmethod
+    def conv2d(inp, w, b, out, N, Cin, H, W, Cout, KH, KW, padH, padW, strH, strW):  # :438
+        if KH != KW or padH != padW or strH != strW:
+            raise OmCudaError("conv2d (asymmetric kernel/pad/stride)", -3)
+        call("omCudaConv2d", inp, w, b, out, N, Cin, H, W, Cout, KH, KW, strH, padH)
+
+    @staticmethod
+    def dilatedConv2d(inp, w, b, out, N, Cin, H, W, Cout, KH, KW, stride, pad, dil, groups):
+        call("omCudaDilatedConv2d", inp, w, b, out, N, Cin, H, W, Cout, KH, KW, stride, pad,
+             dil, groups)
+
+    @staticmethod
+    def conv2dBackwardInput(dy, w, dx, N, Cin, H, W, Cout, KH, KW, padH, padW, strH, strW):  # :480
+        call("omCudaConv2dBackwardInput", dy, w, dx, N, Cin, H, W, Cout, KH, KW, strH, padH)
+
+    @staticmethod
+    def conv2dBackwardWeight(x, dy, dw, db, N, Cin, H, W, Cout, KH, KW, padH, padW, strH, strW):  # :492
+        call("omCudaConv2dBackwardWeight", x, dy, dw, db, N, Cin, H, W, Cout, KH, KW, strH, padH)
+
+    @staticmethod
+    def maxPool2d(inp, out, idx, N, C, H, W, KH, KW, stride, pad):  # :506
+        call("omCudaMaxPool2d", inp, out, idx, N, C, H, W, KH, KW, stride, stride, pad, pad)
+
+    @staticmethod
+    def maxPool2dBackward(dy, idx, dx, N, C, H, W, Hout, Wout):  # :519
+        call("omCudaMemset", dx, 0, N * C * H * W * 4)
+        call("omCudaMaxPool2dBackward", dy, idx, dx, N, C, H, W, Hout, Wout)
+
+    @staticmethod
+    def avgPool2d(inp, out, N, C, H, W, KH, KW, stride, pad):
+        call("omCudaAvgPool2d", inp, out, N, C, H, W, KH, KW, stride, stride, pad, pad)
+
+    @staticmethod
+    def avgPool2dBackward(dy, dx, N, C, H, W, KH, KW, stride, pad):
+        call("omCudaMemset", dx, 0, N * C * H * W * 4)
+        call("omCudaAvgPool2dBackward", dy, dx, N, C, H, W, KH, KW, stride, stride, pad, pad)
+
+    @staticmethod
+    def adaptiveAvgPool2d(inp, out, N, C, H, W, OH, OW):  # :560
+        call("omCudaAdaptiveAvgPool2d", inp, out, N, C, H, W, OH, OW)
+
+    @staticmethod
+    def adaptiveAvgPool2dBackward(dy, dx, N, C, H, W, OH, OW):
+        call("omCudaAdaptiveAvgPool2dBackward", dy, dx, N, C, H, W, OH, OW)
+
+    @staticmethod
+    def batchNorm2d(inp, gamma, beta, out, run_mean, run_var, saved_mean, saved_invstd, N, C,
+                    HW, eps, momentum, training):  # :571 (note: gamma/beta before out)
+        call("omCudaBatchNorm2d", inp, out, gamma, beta, run_mean, run_var, saved_mean,
+             saved_invstd, N, C, 1, HW, eps, momentum, 1 if training else 0)
+
+    @staticmethod
+    def batchNorm2dBackward(dy, x, mean, invstd, gamma, dx, dgamma, dbeta, N, C, H, W,
+                            eps=1e-5):  # :590
+        call("omCudaBatchNorm2dBackward", dy, x, mean, invstd, gamma, dx, dgamma, dbeta, N, C,
+             H, W, eps)
+
+    @staticmethod
+    def softmax(inp, out, N, C):  # :652
+        call("omCudaSoftmax", inp, out, N, C)
+
+    @staticmethod
+    def crossEntropySoftmaxBackward(p, target, grad, N, C):  # :659
+        call("omCudaSoftmaxCrossEntropyBackward", p, target, grad, N, C)
+
+    @staticmethod
+    def crossEntropyForward(p, target, result, N, C):  # :823
+        call("omCudaCrossEntropy", p, target, result, N, C)
+
+    @staticmethod
+    def sgdStep(param, grad, vel, n, lr, momentum):  # :679
+        call("omCudaSgdStep", param, grad, vel, n, lr, momentum)
+
+    @staticmethod
+    def fillZeros(data, n):  # :689
+        call("omCudaFillZeros", data, n)
+
+    @staticmethod
+    def fillOnes(data, n):
+        call("omCudaFillOnes", data, n)
+
+    @staticmethod
+    def fillValue(data, n, v):
+        call("omCudaFillValue", data, n, v)
+
+    @staticmethod
+    def copy(src, dst, n):  # :710
+        call("omCudaCopy", src, dst, n)
+
+    @staticmethod
+    def addBias(data, bias, out, N, C, HW):  # :717
+        call("omCudaAddBias", data, bias, out, N, C, HW)
+
+    @staticmethod
+    def addBiasBackward(dy, db, N, C, HW):
+        call("omCudaAddBiasBackward", dy, db, N, C, HW)
+
+    @staticmethod
+    def clip(inp, out, n, lo, hi):  # :789
+        call("omCudaClip", inp, out, n, lo, hi)
+
+    @staticmethod
+    def argmax(data, out, N, C):
+        call("omCudaArgmax", data, out, N, C)
+
+    @staticmethod
+    def sum(data, result, n):
+        call("omCudaSum", data, result, n)

@@ -1,0 +1,88 @@
+// Internal helpers shared by the backend's translation units: per-device context,
+// status handling, launch accounting and small device utilities.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "om_cuda.h"
+
+namespace omb {
+
+// One context per device: the compute stream every entry point launches on, a transfer
+// stream, the device error word that bounded waits write, and the SM count.
+struct DeviceCtx {
+    int device = -1;
+    cudaStream_t compute = nullptr;
+    cudaStream_t transfer = nullptr;
+    unsigned int* err_word = nullptr;   // device memory, 0 = no error
+    int num_sms = 0;
+    unsigned long long launches = 0;    // kernels launched through this library
+    bool inited = false;
+};
+
+// Context of the calling thread's current device, or nullptr before omCudaInit.
+DeviceCtx* ctx();
+
+inline int status_of(cudaError_t e) { return e == cudaSuccess ? OM_OK : OM_ERR_CUDA; }
+
+// Called after every launch: records the launch and turns a launch error into a status.
+inline int after_launch(DeviceCtx* c) {
+    c->launches++;
+    return status_of(cudaGetLastError());
+}
+
+#define OMB_CTX_OR_FAIL(c)                       \
+    omb::DeviceCtx* c = omb::ctx();              \
+    if (!c) return OM_ERR_NOT_INIT;
+
+#define OMB_CHECK(call)                          \
+    do {                                         \
+        cudaError_t e_ = (call);                 \
+        if (e_ != cudaSuccess) return OM_ERR_CUDA; \
+    } while (0)
+
+// Grid size for grid-stride elementwise kernels: a multiple of the SM count.
+inline int ew_grid(DeviceCtx* c, long long n, int block) {
+    long long want = (n + block - 1) / block;
+    long long cap = (long long)c->num_sms * 8;
+    if (want > cap) want = cap;
+    return want < 1 ? 1 : (int)want;
+}
+
+// device error codes written into DeviceCtx::err_word by bounded waits
+enum : unsigned int {
+    ERRBIT_TC_PRODUCER = 1u << 0,
+    ERRBIT_TC_MMA = 1u << 1,
+    ERRBIT_TC_EPILOGUE = 1u << 2,
+    ERRBIT_TC_DRAIN = 1u << 3,
+};
+
+// 16-bit storage type helpers for the NHWC path
+template <int DT> struct Half16;
+template <> struct Half16<OM_DTYPE_BF16> {
+    using T = __nv_bfloat16;
+    using T2 = __nv_bfloat162;
+    static __device__ __forceinline__ float to_f(T v) { return __bfloat162float(v); }
+    static __device__ __forceinline__ T from_f(float v) { return __float2bfloat16_rn(v); }
+    static __device__ __forceinline__ T2 pack(float a, float b) { return __floats2bfloat162_rn(a, b); }
+    static __device__ __forceinline__ float2 unpack(T2 v) { return __bfloat1622float2(v); }
+};
+template <> struct Half16<OM_DTYPE_F16> {
+    using T = __half;
+    using T2 = __half2;
+    static __device__ __forceinline__ float to_f(T v) { return __half2float(v); }
+    static __device__ __forceinline__ T from_f(float v) { return __float2half_rn(v); }
+    static __device__ __forceinline__ T2 pack(float a, float b) { return __floats2half2_rn(a, b); }
+    static __device__ __forceinline__ float2 unpack(T2 v) { return __half22float2(v); }
+};
+
+__device__ __forceinline__ float apply_act(float v, int act) {
+    if (act == OM_ACT_RELU) return v > 0.f ? v : 0.f;
+    if (act == OM_ACT_RELU6) return v < 0.f ? 0.f : (v > 6.f ? 6.f : v);
+    return v;
+}
+
+}  // namespace omb

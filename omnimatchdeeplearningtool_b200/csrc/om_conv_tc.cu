@@ -1,0 +1,653 @@
+// Implicit-GEMM convolution on 5th-generation tensor cores (tcgen05 + TMEM), fed by TMA in
+// im2col mode. This is the B200 replacement for the reference's conv forward path
+// (omCudaConv2d, cuda_kernels.cu:1076-1200: cuDNN Find per call, or per-sample im2col +
+// Sgemm), specialised for NHWC 16-bit activations with BatchNorm folded into the weights.
+//
+// GEMM view: D[m, k] = sum_kk A[m, kk] * B[k, kk]
+//   m  = output pixel (n, p, q), M = N*P*Q                  (rows, TMEM lanes)
+//   k  = output channel, Cout                               (columns, TMEM columns)
+//   kk = (r, s, c) filter tap and input channel, Kpad = round_up(R*S*Cs, 64)
+// A is never materialised: each 128-row A tile for tap (r, s) and a 64-channel (or 8-channel)
+// slice is one TMA im2col load of 128 consecutive output pixels, with padding zero-filled by
+// the TMA unit. B is the packed K-major weight [Cout, Kpad] (omCudaPackConvWeight).
+//
+// CTA = 6 warps, persistent over output tiles (grid = #SMs):
+//   warp 0      TMA producer (one elected lane)
+//   warp 1      TMEM allocator + MMA issuer (one elected lane): tcgen05.mma.cta_group::1
+//               .kind::f16, M=128, N=BN, K=16, fp32 accumulators in TMEM
+//   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns, + bias, + residual, activation,
+//               16-bit or fp32 store
+// Two TMEM accumulators (2*BN columns) let the epilogue of tile i overlap the MMAs of i+1.
+//
+// Operand layouts in shared memory (K-major, matching the UMMA canonical layouts):
+//   MODE_SW128: Cs % 64 == 0. One im2col box = 128 pixels x 64 channels = 128 rows of 128 B,
+//               written by TMA with the 128-byte swizzle; SBO = 1024 B; the K=16 steps advance
+//               the descriptor start address by 32 B inside the swizzle atom.
+//   MODE_INTERLEAVE: Cs % 8 == 0 (the 3-channel stem padded to 8, the 32-channel MobileNet
+//               layers). A stage holds 8 im2col boxes of 128 pixels x 8 channels (2 KB each,
+//               no swizzle): core matrices of 8 rows x 16 B, SBO = 128 B (next 8 rows),
+//               LBO = 2 KB (next 8 K-elements).
+//
+// Every mbarrier wait is bounded (OMB_WAIT_NS); a wait that gives up records a bit in the
+// device error word, raises a CTA-wide abort flag, and the CTA drains its in-flight TMA
+// loads and MMAs (again with bounded waits) before it frees TMEM and exits.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "om_common.cuh"
+
+namespace omb {
+namespace tc {
+
+constexpr int BM = 128;                 // output pixels per tile (TMEM lanes)
+constexpr int BK = 64;                  // K elements per pipeline stage
+constexpr int A_STAGE_BYTES = BM * BK * 2;
+constexpr int NUM_THREADS = 192;
+constexpr unsigned long long OMB_WAIT_NS = 2000000000ull;  // 2 s per wait
+
+enum { MODE_SW128 = 0, MODE_INTERLEAVE = 1 };
+
+struct Params {
+    int N, H, W, Cs;
+    int K;
+    int R, S, stride, pad;
+    int P, Q, M;
+    int num_kb;
+    int num_m_tiles, num_n_tiles;
+    const float* bias;
+    const void* residual;
+    void* out;
+    int act;
+    int out_f32;
+    unsigned int* err;
+};
+
+// ---------------------------------------------------------------- PTX wrappers
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ unsigned long long gtimer() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait for the phase with the given parity to complete. Returns false when it gave
+// up, either on its own timeout or because another role raised the abort flag.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
+                                          volatile int* abort_flag) {
+    if (mbar_try_wait(bar, parity)) return true;
+    unsigned long long t0 = gtimer();
+    while (true) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (*abort_flag) return false;
+        if (gtimer() - t0 > OMB_WAIT_NS) return false;
+    }
+}
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                            int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+        : "memory");
+}
+__device__ __forceinline__ void tma_load_im2col(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                                int c, int w, int h, int n, uint16_t off_w,
+                                                uint16_t off_h) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.im2col.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5, %6}], [%2], {%7, %8};" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c), "r"(w), "r"(h),
+        "r"(n), "h"(off_w), "h"(off_h)
+        : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+            smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                       uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+          "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]),
+          "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]),
+          "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+          "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]),
+          "=r"(v[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// UMMA shared-memory descriptor (SM100 format): start>>4 [0,14), LBO>>4 [16,30),
+// SBO>>4 [32,46), version=1 [46,48), layout type [61,64).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo,
+                                              uint32_t layout) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+    d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
+    d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)layout << 61;
+    return d;
+}
+constexpr uint32_t LAYOUT_NONE = 0, LAYOUT_SW128 = 2;
+
+// Instruction descriptor for kind::f16: D fp32, A/B bf16 (1) or f16 (0), both K-major,
+// N>>3 at [17,23), M>>4 at [24,29).
+template <int BN, bool F16>
+__host__ __device__ constexpr uint32_t instr_desc() {
+    return (1u << 4) | ((F16 ? 0u : 1u) << 7) | ((F16 ? 0u : 1u) << 10) |
+           ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
+template <int BN>
+struct Cfg {
+    static constexpr int B_STAGE_BYTES = BN * BK * 2;
+    static constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
+    static constexpr int STAGES_RAW = (196 * 1024) / STAGE_BYTES;
+    static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
+    static constexpr int TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
+    // operand stages + barriers/flags + slack for the 1024-byte alignment of the base
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 256 + 1024;
+};
+
+template <int DT>
+__device__ __forceinline__ void store_row_chunk(const Params& p, int m, int n0,
+                                                const uint32_t (&v)[32]) {
+    // 32 consecutive output channels n0..n0+31 of output pixel m
+    using H = Half16<DT>;
+    float f[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]);
+    if (p.bias) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+            if (n0 + j < p.K) {
+                float4 b = *reinterpret_cast<const float4*>(p.bias + n0 + j);
+                f[j] += b.x;
+                f[j + 1] += b.y;
+                f[j + 2] += b.z;
+                f[j + 3] += b.w;
+            }
+        }
+    }
+    const size_t row = (size_t)m * p.K;
+    if (p.out_f32) {
+        // fp32 output (classifier logits); the residual, when given, is fp32 as well
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+            if (n0 + j >= p.K) break;
+            float4 o = make_float4(f[j], f[j + 1], f[j + 2], f[j + 3]);
+            if (p.residual) {
+                float4 r = *reinterpret_cast<const float4*>(
+                    static_cast<const float*>(p.residual) + row + n0 + j);
+                o.x += r.x; o.y += r.y; o.z += r.z; o.w += r.w;
+            }
+            o.x = apply_act(o.x, p.act); o.y = apply_act(o.y, p.act);
+            o.z = apply_act(o.z, p.act); o.w = apply_act(o.w, p.act);
+            *reinterpret_cast<float4*>(static_cast<float*>(p.out) + row + n0 + j) = o;
+        }
+    } else {
+        using T = typename H::T;
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) {
+            if (n0 + j >= p.K) break;
+            if (p.residual) {
+                uint4 rv = *reinterpret_cast<const uint4*>(static_cast<const T*>(p.residual) + row + n0 + j);
+                const typename H::T2* r2 = reinterpret_cast<const typename H::T2*>(&rv);
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                    float2 rr = H::unpack(r2[t]);
+                    f[j + 2 * t] += rr.x;
+                    f[j + 2 * t + 1] += rr.y;
+                }
+            }
+            uint4 ov;
+            typename H::T2* o2 = reinterpret_cast<typename H::T2*>(&ov);
+#pragma unroll
+            for (int t = 0; t < 4; ++t)
+                o2[t] = H::pack(apply_act(f[j + 2 * t], p.act), apply_act(f[j + 2 * t + 1], p.act));
+            *reinterpret_cast<uint4*>(static_cast<T*>(p.out) + row + n0 + j) = ov;
+        }
+    }
+}
+
+template <int BN, int MODE, int DT>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const Params p) {
+    using C = Cfg<BN>;
+    constexpr int STAGES = C::STAGES;
+    constexpr bool F16 = (DT == OM_DTYPE_F16);
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + STAGES * A_STAGE_BYTES;
+    uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * C::B_STAGE_BYTES);
+    uint64_t* empty = full + STAGES;
+    uint64_t* tfull = empty + STAGES;
+    uint64_t* tempty = tfull + 2;
+    uint64_t* drain = tempty + 2;
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+    volatile int* consumed = abort_flag + 1;  // stage loads the MMA issuer has consumed
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < STAGES; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&tfull[i], 1);
+            mbar_init(&tempty[i], 4);
+        }
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        *consumed = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(tmem_holder)),
+                     "r"((uint32_t)C::TMEM_COLS));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_holder;
+
+    const int num_tiles = p.num_m_tiles * p.num_n_tiles;
+    const int PQ = p.P * p.Q;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ------------------------------------------------------------ TMA producer
+            int stage = 0;
+            uint32_t phase = 0;
+            long long issued = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+                const int m_tile = tile / p.num_n_tiles;
+                const int n_tile = tile - m_tile * p.num_n_tiles;
+                const int m0 = m_tile * BM;
+                const int n0 = n_tile * BN;
+                const int img = m0 / PQ;
+                const int rem = m0 - img * PQ;
+                const int pp = rem / p.Q;
+                const int qq = rem - pp * p.Q;
+                const int wb = qq * p.stride - p.pad;
+                const int hb = pp * p.stride - p.pad;
+                for (int kb = 0; kb < p.num_kb; ++kb) {
+                    if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_expect_tx(&full[stage], C::STAGE_BYTES);
+                    uint8_t* a_dst = sA + stage * A_STAGE_BYTES;
+                    uint8_t* b_dst = sB + stage * C::B_STAGE_BYTES;
+                    if (MODE == MODE_SW128) {
+                        const int kk = kb * BK;
+                        const int rs = kk / p.Cs;
+                        const int c0 = kk - rs * p.Cs;
+                        const int r = rs / p.S;
+                        const int s = rs - r * p.S;
+                        tma_load_im2col(a_dst, &tmA, &full[stage], c0, wb, hb, img, (uint16_t)s,
+                                        (uint16_t)r);
+                        tma_load_2d(b_dst, &tmB, &full[stage], kk, n0);
+                    } else {
+                        const int RS = p.R * p.S;
+#pragma unroll 1
+                        for (int j = 0; j < 8; ++j) {
+                            const int kk = kb * BK + j * 8;
+                            int rs = kk / p.Cs;
+                            const int c0 = kk - rs * p.Cs;
+                            if (rs >= RS) rs = RS - 1;  // K padding: weights are zero there
+                            const int r = rs / p.S;
+                            const int s = rs - r * p.S;
+                            tma_load_im2col(a_dst + j * (BM * 16), &tmA, &full[stage], c0, wb, hb,
+                                            img, (uint16_t)s, (uint16_t)r);
+                            tma_load_2d(b_dst + j * (BN * 16), &tmB, &full[stage], kk, n0);
+                        }
+                    }
+                    ++issued;
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+            }
+            if (!ok) {
+                atomicOr(p.err, ERRBIT_TC_PRODUCER);
+                *abort_flag = 1;
+            }
+            // Never leave with a TMA write in flight: wait (bounded) for every load that was
+            // issued but not consumed by the MMA issuer.
+            long long done = *consumed;
+            for (long long j = (done > issued - STAGES ? done : issued - STAGES); j < issued; ++j) {
+                if (j < 0) continue;
+                const int st = (int)(j % STAGES);
+                const uint32_t ph = (uint32_t)((j / STAGES) & 1);
+                unsigned long long t0 = gtimer();
+                while (!mbar_try_wait(&full[st], ph)) {
+                    if (gtimer() - t0 > OMB_WAIT_NS) {
+                        atomicOr(p.err, ERRBIT_TC_DRAIN);
+                        break;
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ------------------------------------------------------------ MMA issuer
+            constexpr uint32_t IDESC = instr_desc<BN, F16>();
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            int local = 0;
+            for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+                const int acc = local & 1;
+                const uint32_t acc_phase = (uint32_t)((local >> 1) & 1);
+                if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+                for (int kb = 0; kb < p.num_kb; ++kb) {
+                    if (!mbar_wait(&full[stage], phase, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_base = smem_u32(sA + stage * A_STAGE_BYTES);
+                    const uint32_t b_base = smem_u32(sB + stage * C::B_STAGE_BYTES);
+#pragma unroll
+                    for (int k = 0; k < BK / 16; ++k) {
+                        uint64_t ad, bd;
+                        if (MODE == MODE_SW128) {
+                            ad = smem_desc(a_base + k * 32, 16, 1024, LAYOUT_SW128);
+                            bd = smem_desc(b_base + k * 32, 16, 1024, LAYOUT_SW128);
+                        } else {
+                            ad = smem_desc(a_base + k * 2 * (BM * 16), BM * 16, 128, LAYOUT_NONE);
+                            bd = smem_desc(b_base + k * 2 * (BN * 16), BN * 16, 128, LAYOUT_NONE);
+                        }
+                        tc_mma(d_tmem, ad, bd, IDESC, (kb > 0 || k > 0) ? 1u : 0u);
+                    }
+                    tc_commit(&empty[stage]);
+                    *consumed = *consumed + 1;
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+                if (!ok) break;
+                tc_commit(&tfull[acc]);
+            }
+            if (!ok) {
+                atomicOr(p.err, ERRBIT_TC_MMA);
+                *abort_flag = 1;
+            }
+            // Drain: every MMA issued by this thread has completed once `drain` flips.
+            tc_commit(drain);
+            unsigned long long t0 = gtimer();
+            while (!mbar_try_wait(drain, 0)) {
+                if (gtimer() - t0 > OMB_WAIT_NS) {
+                    atomicOr(p.err, ERRBIT_TC_DRAIN);
+                    break;
+                }
+            }
+        }
+    } else {
+        // ---------------------------------------------------------------- epilogue
+        const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+        const int row = quarter * 32 + lane;
+        int local = 0;
+        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+            const int acc = local & 1;
+            const uint32_t acc_phase = (uint32_t)((local >> 1) & 1);
+            if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) {
+                if (lane == 0) {
+                    atomicOr(p.err, ERRBIT_TC_EPILOGUE);
+                    *abort_flag = 1;
+                }
+                break;
+            }
+            tc_fence_after();
+            const int m_tile = tile / p.num_n_tiles;
+            const int n_tile = tile - m_tile * p.num_n_tiles;
+            const int m = m_tile * BM + row;
+            const int nbase = n_tile * BN;
+            const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+                uint32_t v[32];
+                tmem_ld32(t_row + (uint32_t)(c * 32), v);
+                if (m < p.M && nbase + c * 32 < p.K) store_row_chunk<DT>(p, m, nbase + c * 32, v);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[acc]);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) {
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                     "r"((uint32_t)C::TMEM_COLS));
+    }
+}
+
+// ---------------------------------------------------------------- host side
+static PFN_cuTensorMapEncodeTiled_v12000 g_encode_tiled = nullptr;
+static PFN_cuTensorMapEncodeIm2col_v12000 g_encode_im2col = nullptr;
+static int g_driver_version = 0;
+static std::once_flag g_once;
+
+static bool load_driver_entry_points() {
+    std::call_once(g_once, [] {
+        cudaDriverEntryPointQueryResult q;
+        void* fn = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) ==
+                cudaSuccess && q == cudaDriverEntryPointSuccess)
+            g_encode_tiled = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+        fn = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeIm2col", &fn, cudaEnableDefault, &q) ==
+                cudaSuccess && q == cudaDriverEntryPointSuccess)
+            g_encode_im2col = reinterpret_cast<PFN_cuTensorMapEncodeIm2col_v12000>(fn);
+        cudaDriverGetVersion(&g_driver_version);
+    });
+    return g_encode_tiled && g_encode_im2col;
+}
+
+template <int BN, int MODE, int DT>
+static int launch(DeviceCtx* c, const CUtensorMap& ta, const CUtensorMap& tb, const Params& p) {
+    using Cf = Cfg<BN>;
+    auto kern = conv_tc_kernel<BN, MODE, DT>;
+    static bool attr_set[64] = {false};
+    if (!attr_set[c->device]) {
+        OMB_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       Cf::SMEM_BYTES));
+        attr_set[c->device] = true;
+    }
+    const int tiles = p.num_m_tiles * p.num_n_tiles;
+    const int grid = tiles < c->num_sms ? tiles : c->num_sms;
+    kern<<<grid, NUM_THREADS, Cf::SMEM_BYTES, c->compute>>>(ta, tb, p);
+    return after_launch(c);
+}
+
+template <int MODE, int DT>
+static int dispatch_bn(DeviceCtx* c, int bn, const CUtensorMap& ta, const CUtensorMap& tb,
+                       const Params& p) {
+    switch (bn) {
+        case 32: return launch<32, MODE, DT>(c, ta, tb, p);
+        case 64: return launch<64, MODE, DT>(c, ta, tb, p);
+        case 128: return launch<128, MODE, DT>(c, ta, tb, p);
+        case 256: return launch<256, MODE, DT>(c, ta, tb, p);
+    }
+    return OM_ERR_UNSUPPORTED;
+}
+
+static int choose_bn(int K, long long m_tiles, int num_sms) {
+    if (K <= 32) return 32;
+    if (K <= 64) return 64;
+    if (K <= 128) return 128;
+    // Prefer 256-wide tiles (half the A re-reads) unless that leaves SMs idle.
+    long long tiles256 = m_tiles * ((K + 255) / 256);
+    if (tiles256 >= 2LL * num_sms) return 256;
+    return 128;
+}
+
+}  // namespace tc
+}  // namespace omb
+
+using namespace omb;
+
+extern "C" long long omCudaPackedConvWeightElems(int nCout, int nKH, int nKW, int nCs) {
+    long long kk = (long long)nKH * nKW * nCs;
+    long long kpad = (kk + tc::BK - 1) / tc::BK * tc::BK;
+    return (long long)nCout * kpad;
+}
+
+extern "C" int omCudaStoredChannels(int nC) {
+    if (nC % 64 == 0) return nC;
+    return (nC + 7) / 8 * 8;
+}
+
+extern "C" int omCudaConv2dBnAct(const void* pInput, const void* pPacked, const float* pBias,
+                                 const void* pResidual, void* pOutput, int nBatch, int nH, int nW,
+                                 int nCs, int nCout, int nKH, int nKW, int nStride, int nPad,
+                                 int nAct, int nDtype, int nOutDtype) {
+    OMB_CTX_OR_FAIL(c);
+    using namespace omb::tc;
+    if (!pInput || !pPacked || !pOutput) return OM_ERR_INVALID;
+    if (nBatch <= 0 || nH <= 0 || nW <= 0 || nCs <= 0 || nCout <= 0 || nKH <= 0 || nKW <= 0 ||
+        nStride <= 0 || nPad < 0)
+        return OM_ERR_INVALID;
+    if (nDtype != OM_DTYPE_BF16 && nDtype != OM_DTYPE_F16) return OM_ERR_UNSUPPORTED;
+    if (nOutDtype != nDtype && nOutDtype != OM_DTYPE_F32) return OM_ERR_UNSUPPORTED;
+    if (nCs % 8 != 0 || nCout % 8 != 0) return OM_ERR_UNSUPPORTED;
+    if ((reinterpret_cast<uintptr_t>(pInput) | reinterpret_cast<uintptr_t>(pPacked) |
+         reinterpret_cast<uintptr_t>(pOutput) | reinterpret_cast<uintptr_t>(pResidual) |
+         reinterpret_cast<uintptr_t>(pBias)) & 15)
+        return OM_ERR_INVALID;
+    const int P = (nH + 2 * nPad - nKH) / nStride + 1;
+    const int Q = (nW + 2 * nPad - nKW) / nStride + 1;
+    if (P <= 0 || Q <= 0) return OM_ERR_INVALID;
+    // im2col corners are signed 8-bit per spatial dim for a 4-D tensor: [-128, 127]
+    const int lower = -nPad, upper = nPad - (nKH - 1), upper_w = nPad - (nKW - 1);
+    if (lower < -128 || upper < -128 || upper > 127 || upper_w < -128 || upper_w > 127)
+        return OM_ERR_UNSUPPORTED;
+    if (nKH > 256 || nKW > 256) return OM_ERR_UNSUPPORTED;
+    const long long Mll = (long long)nBatch * P * Q;
+    if (Mll >= (1LL << 31)) return OM_ERR_UNSUPPORTED;
+    if (!load_driver_entry_points()) return OM_ERR_DRIVER;
+
+    const int mode = (nCs % 64 == 0) ? MODE_SW128 : MODE_INTERLEAVE;
+    const long long kk_total = (long long)nKH * nKW * nCs;
+    const long long kpad = (kk_total + BK - 1) / BK * BK;
+
+    Params p;
+    p.N = nBatch; p.H = nH; p.W = nW; p.Cs = nCs; p.K = nCout;
+    p.R = nKH; p.S = nKW; p.stride = nStride; p.pad = nPad;
+    p.P = P; p.Q = Q; p.M = (int)Mll;
+    p.num_kb = (int)(kpad / BK);
+    p.num_m_tiles = (int)((Mll + BM - 1) / BM);
+    const int bn = choose_bn(nCout, p.num_m_tiles, c->num_sms);
+    p.num_n_tiles = (nCout + bn - 1) / bn;
+    p.bias = pBias;
+    p.residual = pResidual;
+    p.out = pOutput;
+    p.act = nAct;
+    p.out_f32 = (nOutDtype == OM_DTYPE_F32);
+    p.err = c->err_word;
+
+    const CUtensorMapDataType dt =
+        nDtype == OM_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+
+    // A: im2col view of the NHWC input, dims innermost-first (C, W, H, N)
+    CUtensorMap ta, tb;
+    cuuint64_t a_dims[4] = {(cuuint64_t)nCs, (cuuint64_t)nW, (cuuint64_t)nH, (cuuint64_t)nBatch};
+    cuuint64_t a_strides[3] = {(cuuint64_t)nCs * 2, (cuuint64_t)nW * nCs * 2,
+                               (cuuint64_t)nH * nW * nCs * 2};
+    int lo[2] = {-nPad, -nPad};                                   // (W, H)
+    int hi[2] = {nPad - (nKW - 1), nPad - (nKH - 1)};
+    cuuint32_t a_estr[4] = {1, (cuuint32_t)nStride, (cuuint32_t)nStride, 1};
+    CUresult r = g_encode_im2col(
+        &ta, dt, 4, const_cast<void*>(pInput), a_dims, a_strides, lo, hi,
+        mode == MODE_SW128 ? 64 : 8, BM, a_estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+        mode == MODE_SW128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return OM_ERR_DRIVER;
+    // Drivers up to 13.1 mis-handle this descriptor bit for im2col tensors under 128 KiB;
+    // CUTLASS clears it the same way (cute/atom/copy_traits_sm90_im2col.hpp).
+    if (g_driver_version <= 13010 && (unsigned long long)nBatch * nH * nW * nCs * 2 < 131072ull)
+        reinterpret_cast<uint64_t*>(&ta)[1] &= ~(1ull << 21);
+
+    // B: packed weights [Cout, Kpad], K-major
+    cuuint64_t b_dims[2] = {(cuuint64_t)kpad, (cuuint64_t)nCout};
+    cuuint64_t b_strides[1] = {(cuuint64_t)kpad * 2};
+    cuuint32_t b_estr[2] = {1, 1};
+    cuuint32_t b_box[2] = {mode == MODE_SW128 ? 64u : 8u, (cuuint32_t)bn};
+    r = g_encode_tiled(&tb, dt, 2, const_cast<void*>(pPacked), b_dims, b_strides, b_box, b_estr,
+                       CU_TENSOR_MAP_INTERLEAVE_NONE,
+                       mode == MODE_SW128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return OM_ERR_DRIVER;
+
+    if (nDtype == OM_DTYPE_BF16) {
+        return mode == MODE_SW128 ? dispatch_bn<MODE_SW128, OM_DTYPE_BF16>(c, bn, ta, tb, p)
+                                  : dispatch_bn<MODE_INTERLEAVE, OM_DTYPE_BF16>(c, bn, ta, tb, p);
+    }
+    return mode == MODE_SW128 ? dispatch_bn<MODE_SW128, OM_DTYPE_F16>(c, bn, ta, tb, p)
+                              : dispatch_bn<MODE_INTERLEAVE, OM_DTYPE_F16>(c, bn, ta, tb, p);
+}

@@ -1,0 +1,688 @@
+// fp32 NCHW bandwidth-bound ops behind the reference C ABI: BatchNorm forward/backward,
+// pooling, softmax / cross-entropy, SGD, bias add and elementwise kernels.
+//
+// Numerics follow the reference CPU backend (the parity target), not the reference GPU
+// kernels where the two disagree:
+//   - softmax divides by the plain sum (cpu_backend.ixx:352-370; the reference GPU kernel
+//     adds 1e-7, cuda_kernels.cu:1450);
+//   - cross-entropy clamps p at 1e-7 and counts targets > 0.5 (cpu_backend.ixx:375-388; the
+//     GPU kernel uses log(p + 1e-10), cuda_kernels.cu:3934);
+//   - BatchNorm updates the running variance with the biased batch variance, as the CPU
+//     backend does (cpu_backend.ixx:781-842).
+// BatchNorm statistics are reduced per channel over N*H*W by a (channel x split) grid whose
+// per-split partial sums go to a small scratch buffer, then combined in a fixed order, so
+// the result is deterministic and large feature maps still fill all SMs.
+#include "om_common.cuh"
+
+namespace omb {
+namespace ops {
+
+__device__ __forceinline__ float warp_sum(float v) {
+    for (int o = 16; o; o >>= 1) v += __shfl_down_sync(0xffffffffu, v, o);
+    return v;
+}
+// block-wide sum, result valid in thread 0
+__device__ __forceinline__ float block_sum(float v) {
+    __shared__ float sh[32];
+    v = warp_sum(v);
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = v;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        v = threadIdx.x < ((blockDim.x + 31) >> 5) ? sh[threadIdx.x] : 0.f;
+        v = warp_sum(v);
+    }
+    return v;
+}
+
+// ---------------------------------------------------------------- BatchNorm
+// element j of channel c's reduction domain (n-major, hw-minor)
+__device__ __forceinline__ long long bn_index(long long j, int c, int C, int HW) {
+    long long n = j / HW;
+    return (n * C + c) * HW + (j - n * HW);
+}
+
+__global__ void bn_partial_sum_kernel(const float* __restrict__ x, float* __restrict__ part,
+                                      int C, int HW, long long cnt, long long chunk) {
+    const int c = blockIdx.x, z = blockIdx.y;
+    long long beg = z * chunk, end = min(cnt, beg + chunk);
+    float s = 0.f;
+    for (long long j = beg + threadIdx.x; j < end; j += blockDim.x) s += x[bn_index(j, c, C, HW)];
+    s = block_sum(s);
+    if (threadIdx.x == 0) part[(long long)c * gridDim.y + z] = s;
+}
+
+__global__ void bn_partial_m2_kernel(const float* __restrict__ x, const float* __restrict__ psum,
+                                     float* __restrict__ part, int C, int HW, long long cnt,
+                                     long long chunk) {
+    const int c = blockIdx.x, z = blockIdx.y, S = gridDim.y;
+    float tot = 0.f;
+    for (int i = 0; i < S; ++i) tot += psum[(long long)c * S + i];
+    const float mean = tot / (float)cnt;
+    long long beg = z * chunk, end = min(cnt, beg + chunk);
+    float s = 0.f;
+    for (long long j = beg + threadIdx.x; j < end; j += blockDim.x) {
+        float d = x[bn_index(j, c, C, HW)] - mean;
+        s += d * d;
+    }
+    s = block_sum(s);
+    if (threadIdx.x == 0) part[(long long)c * S + z] = s;
+}
+
+// mean/invstd per channel into saved buffers; running statistics updated in training mode
+__global__ void bn_finalize_kernel(const float* __restrict__ psum, const float* __restrict__ pm2,
+                                   int S, long long cnt, float* run_mean, float* run_var,
+                                   float* saved_mean, float* saved_invstd, float eps,
+                                   float momentum, int training, int C) {
+    int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= C) return;
+    float mean, var;
+    if (training) {
+        float s = 0.f, m2 = 0.f;
+        for (int i = 0; i < S; ++i) {
+            s += psum[(long long)c * S + i];
+            m2 += pm2[(long long)c * S + i];
+        }
+        mean = s / (float)cnt;
+        var = m2 / (float)cnt;
+        run_mean[c] = (1.f - momentum) * run_mean[c] + momentum * mean;
+        run_var[c] = (1.f - momentum) * run_var[c] + momentum * var;
+    } else {
+        mean = run_mean[c];
+        var = run_var[c];
+    }
+    saved_mean[c] = mean;
+    saved_invstd[c] = 1.f / sqrtf(var + eps);
+}
+
+__global__ void bn_apply_kernel(const float* __restrict__ x, float* __restrict__ y,
+                                const float* __restrict__ gamma, const float* __restrict__ beta,
+                                const float* __restrict__ mean, const float* __restrict__ invstd,
+                                long long total, int C, int HW) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        int c = (int)((i / HW) % C);
+        y[i] = gamma[c] * (x[i] - mean[c]) * invstd[c] + beta[c];
+    }
+}
+
+__global__ void bn_bwd_partial_kernel(const float* __restrict__ dy, const float* __restrict__ x,
+                                      const float* __restrict__ mean, const float* __restrict__ invstd,
+                                      float* __restrict__ pg, float* __restrict__ pb, int C, int HW,
+                                      long long cnt, long long chunk) {
+    const int c = blockIdx.x, z = blockIdx.y;
+    const float mu = mean[c], is = invstd[c];
+    long long beg = z * chunk, end = min(cnt, beg + chunk);
+    float sg = 0.f, sb = 0.f;
+    for (long long j = beg + threadIdx.x; j < end; j += blockDim.x) {
+        long long idx = bn_index(j, c, C, HW);
+        float g = dy[idx];
+        sg += g * (x[idx] - mu) * is;
+        sb += g;
+    }
+    sg = block_sum(sg);
+    if (threadIdx.x == 0) pg[(long long)c * gridDim.y + z] = sg;
+    sb = block_sum(sb);
+    if (threadIdx.x == 0) pb[(long long)c * gridDim.y + z] = sb;
+}
+
+__global__ void bn_bwd_finalize_kernel(const float* __restrict__ pg, const float* __restrict__ pb,
+                                       int S, float* dgamma, float* dbeta, int C) {
+    int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= C) return;
+    float g = 0.f, b = 0.f;
+    for (int i = 0; i < S; ++i) {
+        g += pg[(long long)c * S + i];
+        b += pb[(long long)c * S + i];
+    }
+    dgamma[c] = g;
+    dbeta[c] = b;
+}
+
+// dx = gamma*invstd/M * (M*dy - dbeta - xhat*dgamma)   (cpu_backend.ixx:847-892)
+__global__ void bn_bwd_apply_kernel(const float* __restrict__ dy, const float* __restrict__ x,
+                                    const float* __restrict__ mean, const float* __restrict__ invstd,
+                                    const float* __restrict__ gamma, const float* __restrict__ dgamma,
+                                    const float* __restrict__ dbeta, float* __restrict__ dx,
+                                    long long total, int C, int HW, float M) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        int c = (int)((i / HW) % C);
+        float is = invstd[c];
+        float xh = (x[i] - mean[c]) * is;
+        dx[i] = gamma[c] * is / M * (M * dy[i] - dbeta[c] - xh * dgamma[c]);
+    }
+}
+
+// ---------------------------------------------------------------- pooling (NCHW)
+__global__ void maxpool_kernel(const float* __restrict__ in, float* __restrict__ out,
+                               int* __restrict__ idx, int N, int C, int H, int W, int kh, int kw,
+                               int sh, int sw, int ph, int pw, int P, int Q) {
+    long long total = (long long)N * C * P * Q;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        int q = (int)(i % Q);
+        long long t = i / Q;
+        int p = (int)(t % P);
+        long long nc = t / P;
+        float m = -1e30f;
+        int mi = -1;
+        for (int r = 0; r < kh; ++r) {
+            int ih = p * sh - ph + r;
+            if (ih < 0 || ih >= H) continue;
+            for (int s = 0; s < kw; ++s) {
+                int iw = q * sw - pw + s;
+                if (iw < 0 || iw >= W) continue;
+                long long ii = (nc * H + ih) * W + iw;
+                float v = in[ii];
+                if (v > m) {
+                    m = v;
+                    mi = (int)ii;
+                }
+            }
+        }
+        out[i] = m;
+        if (idx) idx[i] = mi;
+    }
+}
+
+__global__ void maxpool_bwd_kernel(const float* __restrict__ dy, const int* __restrict__ idx,
+                                   float* __restrict__ dx, long long nout) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < nout;
+         i += (long long)gridDim.x * blockDim.x) {
+        int s = idx[i];
+        if (s >= 0) atomicAdd(&dx[s], dy[i]);
+    }
+}
+
+__global__ void avgpool_kernel(const float* __restrict__ in, float* __restrict__ out, int N, int C,
+                               int H, int W, int kh, int kw, int sh, int sw, int ph, int pw, int P,
+                               int Q) {
+    long long total = (long long)N * C * P * Q;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        int q = (int)(i % Q);
+        long long t = i / Q;
+        int p = (int)(t % P);
+        long long nc = t / P;
+        float s = 0.f;
+        for (int r = 0; r < kh; ++r) {
+            int ih = p * sh - ph + r;
+            if (ih < 0 || ih >= H) continue;
+            for (int u = 0; u < kw; ++u) {
+                int iw = q * sw - pw + u;
+                if (iw >= 0 && iw < W) s += in[(nc * H + ih) * W + iw];
+            }
+        }
+        out[i] = s / (float)(kh * kw);
+    }
+}
+
+__global__ void avgpool_bwd_kernel(const float* __restrict__ dy, float* __restrict__ dx, int N,
+                                   int C, int H, int W, int kh, int kw, int sh, int sw, int ph,
+                                   int pw, int P, int Q) {
+    long long total = (long long)N * C * P * Q;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        int q = (int)(i % Q);
+        long long t = i / Q;
+        int p = (int)(t % P);
+        long long nc = t / P;
+        float g = dy[i] / (float)(kh * kw);
+        for (int r = 0; r < kh; ++r) {
+            int ih = p * sh - ph + r;
+            if (ih < 0 || ih >= H) continue;
+            for (int u = 0; u < kw; ++u) {
+                int iw = q * sw - pw + u;
+                if (iw >= 0 && iw < W) atomicAdd(&dx[(nc * H + ih) * W + iw], g);
+            }
+        }
+    }
+}
+
+__global__ void adaptive_avgpool_kernel(const float* __restrict__ in, float* __restrict__ out,
+                                        int N, int C, int H, int W, int OH, int OW) {
+    // one warp per output element: the window can be the whole plane (global pooling)
+    long long total = (long long)N * C * OH * OW;
+    long long warp = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
+    long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
+    int lane = threadIdx.x & 31;
+    for (long long i = warp; i < total; i += nwarps) {
+        int ow = (int)(i % OW);
+        long long t = i / OW;
+        int oh = (int)(t % OH);
+        long long nc = t / OH;
+        int h0 = oh * H / OH, h1 = (oh + 1) * H / OH, w0 = ow * W / OW, w1 = (ow + 1) * W / OW;
+        int wn = w1 - w0, cnt = (h1 - h0) * wn;
+        float s = 0.f;
+        for (int j = lane; j < cnt; j += 32) {
+            int ih = h0 + j / wn, iw = w0 + j % wn;
+            s += in[(nc * H + ih) * W + iw];
+        }
+        s = warp_sum(s);
+        if (lane == 0) out[i] = s / (float)cnt;
+    }
+}
+
+__global__ void adaptive_avgpool_bwd_kernel(const float* __restrict__ dy, float* __restrict__ dx,
+                                            int N, int C, int H, int W, int OH, int OW) {
+    long long total = (long long)N * C * H * W;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        int w = (int)(i % W);
+        long long t = i / W;
+        int h = (int)(t % H);
+        long long nc = t / H;
+        float g = 0.f;
+        for (int oh = 0; oh < OH; ++oh) {
+            int h0 = oh * H / OH, h1 = (oh + 1) * H / OH;
+            if (h < h0 || h >= h1) continue;
+            for (int ow = 0; ow < OW; ++ow) {
+                int w0 = ow * W / OW, w1 = (ow + 1) * W / OW;
+                if (w < w0 || w >= w1) continue;
+                g += dy[(nc * OH + oh) * OW + ow] / (float)((h1 - h0) * (w1 - w0));
+            }
+        }
+        dx[i] = g;
+    }
+}
+
+// ---------------------------------------------------------------- softmax / CE
+__global__ void softmax_kernel(const float* __restrict__ in, float* __restrict__ out, int N, int C) {
+    long long warp = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
+    int lane = threadIdx.x & 31;
+    if (warp >= N) return;
+    const float* x = in + warp * C;
+    float* y = out + warp * C;
+    float m = -INFINITY;
+    for (int j = lane; j < C; j += 32) m = fmaxf(m, x[j]);
+    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float s = 0.f;
+    for (int j = lane; j < C; j += 32) s += expf(x[j] - m);
+    for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    const float inv = 1.f / s;
+    for (int j = lane; j < C; j += 32) y[j] = expf(x[j] - m) * inv;
+}
+
+__global__ void cross_entropy_kernel(const float* __restrict__ p, const float* __restrict__ t,
+                                     float* __restrict__ result, long long n, int N) {
+    float s = 0.f;
+    for (long long i = threadIdx.x; i < n; i += blockDim.x)
+        if (t[i] > 0.5f) s -= logf(fmaxf(p[i], 1e-7f));
+    s = block_sum(s);
+    if (threadIdx.x == 0) *result = s / (float)N;
+}
+
+__global__ void ce_softmax_bwd_kernel(const float* __restrict__ p, const float* __restrict__ t,
+                                      float* __restrict__ g, long long n, float scale) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+         i += (long long)gridDim.x * blockDim.x)
+        g[i] = (p[i] - t[i]) * scale;
+}
+
+// ---------------------------------------------------------------- optimiser, elementwise
+__global__ void sgd_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ v,
+                           long long n, float lr, float mom) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+         i += (long long)gridDim.x * blockDim.x) {
+        if (v) {
+            float nv = mom * v[i] + g[i];
+            v[i] = nv;
+            p[i] -= lr * nv;
+        } else {
+            p[i] -= lr * g[i];
+        }
+    }
+}
+
+template <class F>
+__global__ void map_kernel(long long n, F f) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+         i += (long long)gridDim.x * blockDim.x)
+        f(i);
+}
+
+__global__ void sum_kernel(const float* __restrict__ x, float* __restrict__ out, long long n) {
+    float s = 0.f;
+    for (long long i = threadIdx.x; i < n; i += blockDim.x) s += x[i];
+    s = block_sum(s);
+    if (threadIdx.x == 0) *out = s;
+}
+
+__global__ void argmax_kernel(const float* __restrict__ x, int* __restrict__ out, int N, int C) {
+    long long warp = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
+    int lane = threadIdx.x & 31;
+    if (warp >= N) return;
+    const float* r = x + warp * C;
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int j = lane; j < C; j += 32)
+        if (r[j] > best) { best = r[j]; bi = j; }
+    for (int o = 16; o; o >>= 1) {
+        float ob = __shfl_xor_sync(0xffffffffu, best, o);
+        int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
+    }
+    if (lane == 0) out[warp] = bi == 0x7fffffff ? 0 : bi;
+}
+
+__global__ void transpose_kernel(const float* __restrict__ in, float* __restrict__ out, int R, int C) {
+    __shared__ float tile[32][33];
+    int x = blockIdx.x * 32 + threadIdx.x, y = blockIdx.y * 32 + threadIdx.y;
+    for (int j = 0; j < 32; j += 8)
+        if (x < C && y + j < R) tile[threadIdx.y + j][threadIdx.x] = in[(long long)(y + j) * C + x];
+    __syncthreads();
+    x = blockIdx.y * 32 + threadIdx.x;
+    y = blockIdx.x * 32 + threadIdx.y;
+    for (int j = 0; j < 32; j += 8)
+        if (x < R && y + j < C) out[(long long)(y + j) * R + x] = tile[threadIdx.x][threadIdx.y + j];
+}
+
+__global__ void bias_grad_kernel(const float* __restrict__ dy, float* __restrict__ db, int N, int C,
+                                 int HW) {
+    int c = blockIdx.x;
+    float s = 0.f;
+    for (long long j = threadIdx.x; j < (long long)N * HW; j += blockDim.x) s += dy[bn_index(j, c, C, HW)];
+    s = block_sum(s);
+    if (threadIdx.x == 0) db[c] = s;
+}
+
+static int bn_splits(DeviceCtx* c, int C, long long cnt) {
+    // aim for >= 4 blocks per SM overall, each split covering at least 4096 elements
+    long long want = (4LL * c->num_sms + C - 1) / C;
+    long long maxs = cnt / 4096 > 0 ? cnt / 4096 : 1;
+    long long s = want < maxs ? want : maxs;
+    if (s > 64) s = 64;
+    return s < 1 ? 1 : (int)s;
+}
+
+}  // namespace ops
+}  // namespace omb
+
+using namespace omb;
+using namespace omb::ops;
+
+#define OMB_EW(n) ew_grid(c, (n), 256), 256, 0, c->compute
+
+extern "C" int omCudaBatchNorm2d(const float* pInput, float* pOutput, const float* pGamma,
+                                 const float* pBeta, float* pRunMean, float* pRunVar,
+                                 float* pSavedMean, float* pSavedInvStd, int nBatch, int nChannels,
+                                 int nH, int nW, float fEps, float fMomentum, int bTraining) {
+    OMB_CTX_OR_FAIL(c);
+    if (!pInput || !pOutput || !pGamma || !pBeta || !pRunMean || !pRunVar || !pSavedMean ||
+        !pSavedInvStd || nBatch <= 0 || nChannels <= 0 || nH <= 0 || nW <= 0)
+        return OM_ERR_INVALID;
+    const int HW = nH * nW;
+    const long long cnt = (long long)nBatch * HW;
+    int S = 1;
+    float* scratch = nullptr;
+    if (bTraining) {
+        S = bn_splits(c, nChannels, cnt);
+        OMB_CHECK(cudaMallocAsync(&scratch, sizeof(float) * 2 * nChannels * S, c->compute));
+        long long chunk = (cnt + S - 1) / S;
+        bn_partial_sum_kernel<<<dim3(nChannels, S), 256, 0, c->compute>>>(pInput, scratch, nChannels, HW, cnt, chunk);
+        int st = after_launch(c);
+        if (st == OM_OK) {
+            bn_partial_m2_kernel<<<dim3(nChannels, S), 256, 0, c->compute>>>(
+                pInput, scratch, scratch + (long long)nChannels * S, nChannels, HW, cnt, chunk);
+            st = after_launch(c);
+        }
+        if (st != OM_OK) {
+            cudaFreeAsync(scratch, c->compute);
+            return st;
+        }
+    }
+    bn_finalize_kernel<<<(nChannels + 127) / 128, 128, 0, c->compute>>>(
+        scratch, scratch ? scratch + (long long)nChannels * S : nullptr, S, cnt, pRunMean, pRunVar,
+        pSavedMean, pSavedInvStd, fEps, fMomentum, bTraining, nChannels);
+    int st = after_launch(c);
+    if (scratch) cudaFreeAsync(scratch, c->compute);
+    if (st != OM_OK) return st;
+    const long long total = cnt * nChannels;
+    bn_apply_kernel<<<OMB_EW(total)>>>(pInput, pOutput, pGamma, pBeta, pSavedMean, pSavedInvStd,
+                                       total, nChannels, HW);
+    return after_launch(c);
+}
+
+extern "C" int omCudaBatchNorm2dBackward(const float* pGradOutput, const float* pInput,
+                                         const float* pMean, const float* pInvStd,
+                                         const float* pGamma, float* pGradInput, float* pGradGamma,
+                                         float* pGradBeta, int nBatch, int nChannels, int nH,
+                                         int nW, float fEps) {
+    (void)fEps;
+    OMB_CTX_OR_FAIL(c);
+    if (!pGradOutput || !pInput || !pMean || !pInvStd || !pGamma || !pGradInput || !pGradGamma ||
+        !pGradBeta)
+        return OM_ERR_INVALID;
+    const int HW = nH * nW;
+    const long long cnt = (long long)nBatch * HW;
+    const int S = bn_splits(c, nChannels, cnt);
+    float* scratch = nullptr;
+    OMB_CHECK(cudaMallocAsync(&scratch, sizeof(float) * 2 * nChannels * S, c->compute));
+    long long chunk = (cnt + S - 1) / S;
+    bn_bwd_partial_kernel<<<dim3(nChannels, S), 256, 0, c->compute>>>(
+        pGradOutput, pInput, pMean, pInvStd, scratch, scratch + (long long)nChannels * S, nChannels,
+        HW, cnt, chunk);
+    int st = after_launch(c);
+    if (st == OM_OK) {
+        bn_bwd_finalize_kernel<<<(nChannels + 127) / 128, 128, 0, c->compute>>>(
+            scratch, scratch + (long long)nChannels * S, S, pGradGamma, pGradBeta, nChannels);
+        st = after_launch(c);
+    }
+    cudaFreeAsync(scratch, c->compute);
+    if (st != OM_OK) return st;
+    const long long total = cnt * nChannels;
+    bn_bwd_apply_kernel<<<OMB_EW(total)>>>(pGradOutput, pInput, pMean, pInvStd, pGamma, pGradGamma,
+                                           pGradBeta, pGradInput, total, nChannels, HW, (float)cnt);
+    return after_launch(c);
+}
+
+extern "C" int omCudaMaxPool2d(const float* pIn, float* pOut, int* pIndices, int nN, int nC,
+                               int nH, int nW, int nKH, int nKW, int nSH, int nSW, int nPH,
+                               int nPW) {
+    OMB_CTX_OR_FAIL(c);
+    if (!pIn || !pOut || nSH <= 0 || nSW <= 0) return OM_ERR_INVALID;
+    int P = (nH + 2 * nPH - nKH) / nSH + 1, Q = (nW + 2 * nPW - nKW) / nSW + 1;
+    if (P <= 0 || Q <= 0) return OM_ERR_INVALID;
+    if ((long long)nN * nC * nH * nW >= (1LL << 31)) return OM_ERR_UNSUPPORTED;  // int32 indices
+    long long total = (long long)nN * nC * P * Q;
+    maxpool_kernel<<<OMB_EW(total)>>>(pIn, pOut, pIndices, nN, nC, nH, nW, nKH, nKW, nSH, nSW, nPH, nPW, P, Q);
+    return after_launch(c);
+}
+
+extern "C" int omCudaMaxPool2dBackward(const float* pGradOut, const int* pIndices, float* pGradIn,
+                                       int nN, int nC, int nH, int nW, int nHout, int nWout) {
+    (void)nH; (void)nW;
+    OMB_CTX_OR_FAIL(c);
+    if (!pGradOut || !pIndices || !pGradIn) return OM_ERR_INVALID;
+    long long n = (long long)nN * nC * nHout * nWout;
+    maxpool_bwd_kernel<<<OMB_EW(n)>>>(pGradOut, pIndices, pGradIn, n);
+    return after_launch(c);
+}
+
+extern "C" int omCudaAvgPool2d(const float* pIn, float* pOut, int nN, int nC, int nH, int nW,
+                               int nKH, int nKW, int nSH, int nSW, int nPH, int nPW) {
+    OMB_CTX_OR_FAIL(c);
+    if (!pIn || !pOut || nSH <= 0 || nSW <= 0) return OM_ERR_INVALID;
+    int P = (nH + 2 * nPH - nKH) / nSH + 1, Q = (nW + 2 * nPW - nKW) / nSW + 1;
+    if (P <= 0 || Q <= 0) return OM_ERR_INVALID;
+    long long total = (long long)nN * nC * P * Q;
+    avgpool_kernel<<<OMB_EW(total)>>>(pIn, pOut, nN, nC, nH, nW, nKH, nKW, nSH, nSW, nPH, nPW, P, Q);
+    return after_launch(c);
+}
+
+extern "C" int omCudaAvgPool2dBackward(const float* pGradOut, float* pGradIn, int nN, int nC,
+                                       int nH, int nW, int nKH, int nKW, int nSH, int nSW, int nPH,
+                                       int nPW) {
+    OMB_CTX_OR_FAIL(c);
+    if (!pGradOut || !pGradIn || nSH <= 0 || nSW <= 0) return OM_ERR_INVALID;
+    int P = (nH + 2 * nPH - nKH) / nSH + 1, Q = (nW + 2 * nPW - nKW) / nSW + 1;
+    if (P <= 0 || Q <= 0) return OM_ERR_INVALID;
+    long long total = (long long)nN * nC * P * Q;
+    avgpool_bwd_kernel<<<OMB_EW(total)>>>(pGradOut, pGradIn, nN, nC, nH, nW, nKH, nKW, nSH, nSW, nPH, nPW, P, Q);
+    return after_launch(c);
+}
+
+extern "C" int omCudaAdaptiveAvgPool2d(const float* pIn, float* pOut, int nN, int nC, int nH,
+                                       int nW, int nOutH, int nOutW) {
+    OMB_CTX_OR_FAIL(c);
+    if (!pIn || !pOut || nOutH <= 0 || nOutW <= 0 || nOutH > nH || nOutW > nW) return OM_ERR_INVALID;
+    long long total = (long long)nN * nC * nOutH * nOutW;
+    adaptive_avgpool_kernel<<<OMB_EW(total * 32)>>>(pIn, pOut, nN, nC, nH, nW, nOutH, nOutW);
+    return after_launch(c);
+}
+
+extern "C" int omCudaAdaptiveAvgPool2dBackward(const float* pGradOut, float* pGradIn, int nBatch,
+                                               int nChannels, int nH, int nW, int nOutH,
+                                               int nOutW) {
+    OMB_CTX_OR_FAIL(c);
+    if (!pGradOut || !pGradIn || nOutH <= 0 || nOutW <= 0) return OM_ERR_INVALID;
+    long long total = (long long)nBatch * nChannels * nH * nW;
+    adaptive_avgpool_bwd_kernel<<<OMB_EW(total)>>>(pGradOut, pGradIn, nBatch, nChannels, nH, nW, nOutH, nOutW);
+    return after_launch(c);
+}
+
+extern "C" int omCudaAddBias(const float* pData, const float* pBias, float* pOut, int nN, int nC,
+                             int nHW) {
+    OMB_CTX_OR_FAIL(c);
+    if (!pData || !pBias || !pOut) return OM_ERR_INVALID;
+    long long total = (long long)nN * nC * nHW;
+    map_kernel<<<OMB_EW(total)>>>(total, [=] __device__(long long i) {
+        pOut[i] = pData[i] + pBias[(i / nHW) % nC];
+    });
+    return after_launch(c);
+}
+
+extern "C" int omCudaAddBiasBackward(const float* pGradOut, float* pGradBias, int nN, int nC,
+                                     int nHW) {
+    OMB_CTX_OR_FAIL(c);
+    if (!pGradOut || !pGradBias) return OM_ERR_INVALID;
+    bias_grad_kernel<<<nC, 256, 0, c->compute>>>(pGradOut, pGradBias, nN, nC, nHW);
+    return after_launch(c);
+}
+
+extern "C" int omCudaSoftmax(const float* pIn, float* pOut, int nBatch, int nClasses) {
+    OMB_CTX_OR_FAIL(c);
+    if (!pIn || !pOut || nBatch <= 0 || nClasses <= 0) return OM_ERR_INVALID;
+    long long threads = (long long)nBatch * 32;
+    softmax_kernel<<<(int)((threads + 255) / 256), 256, 0, c->compute>>>(pIn, pOut, nBatch, nClasses);
+    return after_launch(c);
+}
+
+extern "C" int omCudaCrossEntropy(const float* pSoftmax, const float* pTarget, float* pResult,
+                                  int nBatch, int nClasses) {
+    OMB_CTX_OR_FAIL(c);
+    if (!pSoftmax || !pTarget || !pResult || nBatch <= 0) return OM_ERR_INVALID;
+    cross_entropy_kernel<<<1, 1024, 0, c->compute>>>(pSoftmax, pTarget, pResult,
+                                                     (long long)nBatch * nClasses, nBatch);
+    return after_launch(c);
+}
+
+extern "C" int omCudaSoftmaxCrossEntropyBackward(const float* pSoftmax, const float* pTarget,
+                                                 float* pGradLogits, int nBatch, int nClasses) {
+    OMB_CTX_OR_FAIL(c);
+    if (!pSoftmax || !pTarget || !pGradLogits || nBatch <= 0) return OM_ERR_INVALID;
+    long long n = (long long)nBatch * nClasses;
+    ce_softmax_bwd_kernel<<<OMB_EW(n)>>>(pSoftmax, pTarget, pGradLogits, n, 1.f / (float)nBatch);
+    return after_launch(c);
+}
+
+extern "C" int omCudaSgdStep(float* pParam, const float* pGrad, float* pVelocity, int nCount,
+                             float fLr, float fMomentum) {
+    OMB_CTX_OR_FAIL(c);
+    if (!pParam || !pGrad || nCount < 0) return OM_ERR_INVALID;
+    float* v = fMomentum > 0.f ? pVelocity : nullptr;
+    if (fMomentum > 0.f && !pVelocity) return OM_ERR_INVALID;
+    sgd_kernel<<<OMB_EW(nCount)>>>(pParam, pGrad, v, nCount, fLr, fMomentum);
+    return after_launch(c);
+}
+
+extern "C" int omCudaAdd(const float* pA, const float* pB, float* pC, int nCount) {
+    OMB_CTX_OR_FAIL(c);
+    if (!pA || !pB || !pC || nCount < 0) return OM_ERR_INVALID;
+    map_kernel<<<OMB_EW(nCount)>>>((long long)nCount, [=] __device__(long long i) { pC[i] = pA[i] + pB[i]; });
+    return after_launch(c);
+}
+
+extern "C" int omCudaMulScalar(const float* pA, float fScalar, float* pC, int nCount) {
+    OMB_CTX_OR_FAIL(c);
+    if (!pA || !pC || nCount < 0) return OM_ERR_INVALID;
+    map_kernel<<<OMB_EW(nCount)>>>((long long)nCount, [=] __device__(long long i) { pC[i] = pA[i] * fScalar; });
+    return after_launch(c);
+}
+
+extern "C" int omCudaReLU(const float* pIn, float* pOut, int nCount) {
+    OMB_CTX_OR_FAIL(c);
+    if (!pIn || !pOut || nCount < 0) return OM_ERR_INVALID;
+    map_kernel<<<OMB_EW(nCount)>>>((long long)nCount, [=] __device__(long long i) {
+        float v = pIn[i];
+        pOut[i] = v > 0.f ? v : 0.f;
+    });
+    return after_launch(c);
+}
+
+extern "C" int omCudaReLUBackward(const float* pIn, const float* pGradOut, float* pGradIn,
+                                  int nCount) {
+    OMB_CTX_OR_FAIL(c);
+    if (!pIn || !pGradOut || !pGradIn || nCount < 0) return OM_ERR_INVALID;
+    map_kernel<<<OMB_EW(nCount)>>>((long long)nCount, [=] __device__(long long i) {
+        pGradIn[i] = pIn[i] > 0.f ? pGradOut[i] : 0.f;
+    });
+    return after_launch(c);
+}
+
+extern "C" int omCudaClip(const float* pIn, float* pOut, int nCount, float fMin, float fMax) {
+    OMB_CTX_OR_FAIL(c);
+    if (!pIn || !pOut || nCount < 0) return OM_ERR_INVALID;
+    map_kernel<<<OMB_EW(nCount)>>>((long long)nCount, [=] __device__(long long i) {
+        float v = pIn[i];
+        v = v < fMin ? fMin : v;
+        pOut[i] = v > fMax ? fMax : v;
+    });
+    return after_launch(c);
+}
+
+extern "C" int omCudaFillValue(float* pData, int nCount, float fValue) {
+    OMB_CTX_OR_FAIL(c);
+    if (!pData || nCount < 0) return OM_ERR_INVALID;
+    map_kernel<<<OMB_EW(nCount)>>>((long long)nCount, [=] __device__(long long i) { pData[i] = fValue; });
+    return after_launch(c);
+}
+
+extern "C" int omCudaFillZeros(float* pData, int nCount) {
+    OMB_CTX_OR_FAIL(c);
+    if (!pData || nCount < 0) return OM_ERR_INVALID;
+    return omb::status_of(cudaMemsetAsync(pData, 0, sizeof(float) * (size_t)nCount, c->compute));
+}
+
+extern "C" int omCudaFillOnes(float* pData, int nCount) { return omCudaFillValue(pData, nCount, 1.f); }
+
+extern "C" int omCudaCopy(const float* pSrc, float* pDst, int nCount) {
+    OMB_CTX_OR_FAIL(c);
+    if (!pSrc || !pDst || nCount < 0) return OM_ERR_INVALID;
+    return omb::status_of(cudaMemcpyAsync(pDst, pSrc, sizeof(float) * (size_t)nCount,
+                                          cudaMemcpyDeviceToDevice, c->compute));
+}
+
+extern "C" int omCudaSum(const float* pData, float* pResult, int nCount) {
+    OMB_CTX_OR_FAIL(c);
+    if (!pData || !pResult || nCount < 0) return OM_ERR_INVALID;
+    sum_kernel<<<1, 1024, 0, c->compute>>>(pData, pResult, nCount);
+    return after_launch(c);
+}
+
+extern "C" int omCudaArgmax(const float* pData, int* pOut, int nBatch, int nClasses) {
+    OMB_CTX_OR_FAIL(c);
+    if (!pData || !pOut || nBatch <= 0 || nClasses <= 0) return OM_ERR_INVALID;
+    long long threads = (long long)nBatch * 32;
+    argmax_kernel<<<(int)((threads + 255) / 256), 256, 0, c->compute>>>(pData, pOut, nBatch, nClasses);
+    return after_launch(c);
+}
+
+extern "C" int omCudaTranspose(const float* pIn, float* pOut, int nRows, int nCols) {
+    OMB_CTX_OR_FAIL(c);
+    if (!pIn || !pOut || nRows <= 0 || nCols <= 0) return OM_ERR_INVALID;
+    dim3 grid((nCols + 31) / 32, (nRows + 31) / 32);
+    transpose_kernel<<<grid, dim3(32, 8), 0, c->compute>>>(pIn, pOut, nRows, nCols);
+    return after_launch(c);
+}

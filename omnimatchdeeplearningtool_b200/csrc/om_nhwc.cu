@@ -1,0 +1,426 @@
+// NHWC 16-bit support kernels for the fused inference path: layout conversion, BatchNorm
+// folding into packed weights, max/global-average pooling, depthwise convolution and the
+// residual add. All are bandwidth-bound and use 128-bit accesses along the channel dim.
+//
+// Window semantics follow the reference CPU backend: max pool starts from -1e30 and skips
+// padding (cpu_backend.ixx:897-934); global pooling is the 1x1 adaptive average pool
+// (:1467-1489); depthwise is the grouped direct conv with groups == C (:454-502).
+#include "om_common.cuh"
+
+namespace omb {
+
+// ---------------------------------------------------------------- weight packing
+// w [K, C, R, S] fp32 -> packed [K, Kpad] (16-bit), index kk = (r*S + s)*Cs + c, with the
+// eval-mode BatchNorm scale folded in; zero where c >= C or kk >= R*S*Cs.
+template <typename T>
+__global__ void pack_conv_weight_kernel(const float* __restrict__ w, const float* __restrict__ scale,
+                                        T* __restrict__ out, int K, int C, int R, int S, int Cs,
+                                        long long kpad) {
+    long long total = (long long)K * kpad;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        int k = (int)(i / kpad);
+        long long kk = i - (long long)k * kpad;
+        float v = 0.f;
+        if (kk < (long long)R * S * Cs) {
+            int rs = (int)(kk / Cs);
+            int c = (int)(kk - (long long)rs * Cs);
+            int r = rs / S, s = rs - r * S;
+            if (c < C) v = w[(((long long)k * C + c) * R + r) * S + s] * (scale ? scale[k] : 1.f);
+        }
+        if constexpr (sizeof(T) == 2) {
+            if constexpr (std::is_same<T, __nv_bfloat16>::value) out[i] = __float2bfloat16_rn(v);
+            else out[i] = __float2half_rn(v);
+        }
+    }
+}
+
+// scale[k] = gamma/sqrt(var+eps); bias[k] = beta + (b - mean)*scale (BN absent -> identity)
+__global__ void fold_bn_kernel(const float* conv_bias, const float* gamma, const float* beta,
+                               const float* mean, const float* var, float eps, float* scale,
+                               float* bias, int K) {
+    int k = blockIdx.x * blockDim.x + threadIdx.x;
+    if (k >= K) return;
+    float g = gamma ? gamma[k] : 1.f;
+    float v = var ? var[k] : 1.f;
+    float sc = (gamma || var) ? g / sqrtf(v + eps) : 1.f;
+    float b = conv_bias ? conv_bias[k] : 0.f;
+    float mu = mean ? mean[k] : 0.f;
+    float be = beta ? beta[k] : 0.f;
+    scale[k] = sc;
+    bias[k] = be + (b - mu) * sc;
+}
+
+// ---------------------------------------------------------------- layout conversion
+template <int DT>
+__global__ void nchw_to_nhwc_kernel(const float* __restrict__ in, typename Half16<DT>::T* __restrict__ out,
+                                    int N, int C, int H, int W, int Cs) {
+    // one thread per (n, h, w, c) output element; consecutive threads walk c
+    long long total = (long long)N * H * W * Cs;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        int c = (int)(i % Cs);
+        long long pix = i / Cs;
+        int w = (int)(pix % W);
+        long long t = pix / W;
+        int h = (int)(t % H);
+        int n = (int)(t / H);
+        float v = c < C ? in[(((long long)n * C + c) * H + h) * W + w] : 0.f;
+        out[i] = Half16<DT>::from_f(v);
+    }
+}
+
+template <int DT>
+__global__ void nhwc_to_nchw_kernel(const typename Half16<DT>::T* __restrict__ in, float* __restrict__ out,
+                                    int N, int C, int H, int W, int Cs) {
+    long long total = (long long)N * C * H * W;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        int w = (int)(i % W);
+        long long t = i / W;
+        int h = (int)(t % H);
+        t /= H;
+        int c = (int)(t % C);
+        int n = (int)(t / C);
+        out[i] = Half16<DT>::to_f(in[(((long long)n * H + h) * W + w) * Cs + c]);
+    }
+}
+
+// ---------------------------------------------------------------- pooling
+// Each thread owns 8 consecutive channels (one 16-byte vector) of one output pixel.
+template <int DT>
+__global__ void maxpool_nhwc_kernel(const uint4* __restrict__ in, uint4* __restrict__ out, int N,
+                                    int H, int W, int C8, int P, int Q, int k, int stride, int pad) {
+    using H16 = Half16<DT>;
+    long long total = (long long)N * P * Q * C8;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        int c8 = (int)(i % C8);
+        long long pix = i / C8;
+        int q = (int)(pix % Q);
+        long long t = pix / Q;
+        int p = (int)(t % P);
+        int n = (int)(t / P);
+        float m[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) m[j] = -1e30f;
+        for (int r = 0; r < k; ++r) {
+            int ih = p * stride - pad + r;
+            if (ih < 0 || ih >= H) continue;
+            for (int s = 0; s < k; ++s) {
+                int iw = q * stride - pad + s;
+                if (iw < 0 || iw >= W) continue;
+                uint4 v = in[(((long long)n * H + ih) * W + iw) * C8 + c8];
+                const typename H16::T2* v2 = reinterpret_cast<const typename H16::T2*>(&v);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    float2 f = H16::unpack(v2[j]);
+                    m[2 * j] = f.x > m[2 * j] ? f.x : m[2 * j];
+                    m[2 * j + 1] = f.y > m[2 * j + 1] ? f.y : m[2 * j + 1];
+                }
+            }
+        }
+        uint4 o;
+        typename H16::T2* o2 = reinterpret_cast<typename H16::T2*>(&o);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) o2[j] = H16::pack(m[2 * j], m[2 * j + 1]);
+        out[i] = o;
+    }
+}
+
+// One block of 256 threads per image. Thread t owns channel group (t % C8) and walks the
+// pixels t/C8, t/C8 + rows, ... (rows = 256/C8); the per-row partial sums are combined in
+// shared memory. Channel counts up to 2048 (C8 <= 256) are covered.
+template <int DT>
+__global__ void gap_nhwc_kernel(const uint4* __restrict__ in, void* __restrict__ out, int HW,
+                                int C8, int out_f32) {
+    using H16 = Half16<DT>;
+    extern __shared__ float sh[];  // C8*8 channel sums
+    const int n = blockIdx.x;
+    const int rows = (int)blockDim.x / C8;
+    const int cg = threadIdx.x % C8;
+    const int row = threadIdx.x / C8;
+    const bool active = row < rows;
+    const long long base = (long long)n * HW * C8;
+    float acc[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+    if (active) {
+        for (int pix = row; pix < HW; pix += rows) {
+            uint4 v = in[base + (long long)pix * C8 + cg];
+            const typename H16::T2* v2 = reinterpret_cast<const typename H16::T2*>(&v);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                float2 f = H16::unpack(v2[j]);
+                acc[2 * j] += f.x;
+                acc[2 * j + 1] += f.y;
+            }
+        }
+    }
+    for (int c = threadIdx.x; c < C8 * 8; c += blockDim.x) sh[c] = 0.f;
+    __syncthreads();
+    if (active) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) atomicAdd(&sh[cg * 8 + j], acc[j]);
+    }
+    __syncthreads();
+    const float inv = 1.f / (float)HW;
+    for (int c = threadIdx.x; c < C8 * 8; c += blockDim.x) {
+        float v = sh[c] * inv;
+        if (out_f32)
+            static_cast<float*>(out)[(long long)n * C8 * 8 + c] = v;
+        else
+            static_cast<typename H16::T*>(out)[(long long)n * C8 * 8 + c] = H16::from_f(v);
+    }
+}
+
+// ---------------------------------------------------------------- depthwise conv
+// packed weight: fp32 [R*S, Cs] (BN scale folded), bias fp32 [Cs]. One thread per output
+// pixel and 8-channel group.
+template <int DT>
+__global__ void depthwise_nhwc_kernel(const uint4* __restrict__ in, const float* __restrict__ wpk,
+                                      const float* __restrict__ bias, uint4* __restrict__ out,
+                                      int N, int H, int W, int C8, int P, int Q, int R, int S,
+                                      int stride, int pad, int act) {
+    using H16 = Half16<DT>;
+    long long total = (long long)N * P * Q * C8;
+    const int Cs = C8 * 8;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        int c8 = (int)(i % C8);
+        long long pix = i / C8;
+        int q = (int)(pix % Q);
+        long long t = pix / Q;
+        int p = (int)(t % P);
+        int n = (int)(t / P);
+        float acc[8];
+        const float4* b4 = reinterpret_cast<const float4*>(bias + c8 * 8);
+        float4 b0 = b4[0], b1 = b4[1];
+        acc[0] = b0.x; acc[1] = b0.y; acc[2] = b0.z; acc[3] = b0.w;
+        acc[4] = b1.x; acc[5] = b1.y; acc[6] = b1.z; acc[7] = b1.w;
+        for (int r = 0; r < R; ++r) {
+            int ih = p * stride - pad + r;
+            if (ih < 0 || ih >= H) continue;
+            for (int s = 0; s < S; ++s) {
+                int iw = q * stride - pad + s;
+                if (iw < 0 || iw >= W) continue;
+                uint4 v = in[(((long long)n * H + ih) * W + iw) * C8 + c8];
+                const typename H16::T2* v2 = reinterpret_cast<const typename H16::T2*>(&v);
+                const float4* w4 = reinterpret_cast<const float4*>(wpk + (long long)(r * S + s) * Cs + c8 * 8);
+                float4 w0 = w4[0], w1 = w4[1];
+                float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    float2 f = H16::unpack(v2[j]);
+                    acc[2 * j] += f.x * wv[2 * j];
+                    acc[2 * j + 1] += f.y * wv[2 * j + 1];
+                }
+            }
+        }
+        uint4 o;
+        typename H16::T2* o2 = reinterpret_cast<typename H16::T2*>(&o);
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            o2[j] = H16::pack(apply_act(acc[2 * j], act), apply_act(acc[2 * j + 1], act));
+        out[i] = o;
+    }
+}
+
+__global__ void pack_depthwise_kernel(const float* __restrict__ w, const float* __restrict__ scale,
+                                      const float* __restrict__ bias_in, float* __restrict__ wpk,
+                                      float* __restrict__ bias_out, int C, int RS, int Cs) {
+    int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= RS * Cs) return;
+    int rs = i / Cs, c = i - rs * Cs;
+    wpk[i] = c < C ? w[(long long)c * RS + rs] * scale[c] : 0.f;
+    if (rs == 0) bias_out[c] = c < C ? bias_in[c] : 0.f;
+}
+
+// ---------------------------------------------------------------- residual add
+template <int DT>
+__global__ void add_act_kernel(const uint4* __restrict__ a, const uint4* __restrict__ b,
+                               uint4* __restrict__ out, long long n8, int act) {
+    using H16 = Half16<DT>;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n8;
+         i += (long long)gridDim.x * blockDim.x) {
+        uint4 va = a[i], vb = b[i], o;
+        const typename H16::T2* a2 = reinterpret_cast<const typename H16::T2*>(&va);
+        const typename H16::T2* b2 = reinterpret_cast<const typename H16::T2*>(&vb);
+        typename H16::T2* o2 = reinterpret_cast<typename H16::T2*>(&o);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            float2 x = H16::unpack(a2[j]), y = H16::unpack(b2[j]);
+            o2[j] = H16::pack(apply_act(x.x + y.x, act), apply_act(x.y + y.y, act));
+        }
+        out[i] = o;
+    }
+}
+
+}  // namespace omb
+
+using namespace omb;
+
+static inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+extern "C" int omCudaPackConvWeight(const float* pWeight, const float* pConvBias,
+                                    const float* pGamma, const float* pBeta, const float* pMean,
+                                    const float* pVar, float fEps, void* pPacked, float* pBiasOut,
+                                    int nCout, int nCin, int nKH, int nKW, int nCs, int nDtype) {
+    OMB_CTX_OR_FAIL(c);
+    if (!pWeight || !pPacked || !pBiasOut || nCout <= 0 || nCin <= 0 || nCs < nCin) return OM_ERR_INVALID;
+    if (nDtype != OM_DTYPE_BF16 && nDtype != OM_DTYPE_F16) return OM_ERR_UNSUPPORTED;
+    long long kpad = omCudaPackedConvWeightElems(1, nKH, nKW, nCs);
+    float* scale = nullptr;
+    OMB_CHECK(cudaMallocAsync(&scale, sizeof(float) * nCout, c->compute));
+    fold_bn_kernel<<<(nCout + 255) / 256, 256, 0, c->compute>>>(pConvBias, pGamma, pBeta, pMean,
+                                                                 pVar, fEps, scale, pBiasOut, nCout);
+    int st = after_launch(c);
+    if (st == OM_OK) {
+        long long total = (long long)nCout * kpad;
+        int grid = ew_grid(c, total, 256);
+        if (nDtype == OM_DTYPE_BF16)
+            pack_conv_weight_kernel<__nv_bfloat16><<<grid, 256, 0, c->compute>>>(
+                pWeight, scale, static_cast<__nv_bfloat16*>(pPacked), nCout, nCin, nKH, nKW, nCs, kpad);
+        else
+            pack_conv_weight_kernel<__half><<<grid, 256, 0, c->compute>>>(
+                pWeight, scale, static_cast<__half*>(pPacked), nCout, nCin, nKH, nKW, nCs, kpad);
+        st = after_launch(c);
+    }
+    cudaFreeAsync(scale, c->compute);
+    return st;
+}
+
+extern "C" int omCudaNchwToNhwc(const float* pIn, void* pOut, int nN, int nC, int nH, int nW,
+                                int nCs, int nDtype) {
+    OMB_CTX_OR_FAIL(c);
+    if (!pIn || !pOut || nCs < nC || nN <= 0 || nC <= 0 || nH <= 0 || nW <= 0) return OM_ERR_INVALID;
+    long long total = (long long)nN * nH * nW * nCs;
+    int grid = ew_grid(c, total, 256);
+    if (nDtype == OM_DTYPE_BF16)
+        nchw_to_nhwc_kernel<OM_DTYPE_BF16><<<grid, 256, 0, c->compute>>>(
+            pIn, static_cast<__nv_bfloat16*>(pOut), nN, nC, nH, nW, nCs);
+    else if (nDtype == OM_DTYPE_F16)
+        nchw_to_nhwc_kernel<OM_DTYPE_F16><<<grid, 256, 0, c->compute>>>(
+            pIn, static_cast<__half*>(pOut), nN, nC, nH, nW, nCs);
+    else
+        return OM_ERR_UNSUPPORTED;
+    return after_launch(c);
+}
+
+extern "C" int omCudaNhwcToNchw(const void* pIn, float* pOut, int nN, int nC, int nH, int nW,
+                                int nCs, int nDtype) {
+    OMB_CTX_OR_FAIL(c);
+    if (!pIn || !pOut || nCs < nC) return OM_ERR_INVALID;
+    long long total = (long long)nN * nC * nH * nW;
+    int grid = ew_grid(c, total, 256);
+    if (nDtype == OM_DTYPE_BF16)
+        nhwc_to_nchw_kernel<OM_DTYPE_BF16><<<grid, 256, 0, c->compute>>>(
+            static_cast<const __nv_bfloat16*>(pIn), pOut, nN, nC, nH, nW, nCs);
+    else if (nDtype == OM_DTYPE_F16)
+        nhwc_to_nchw_kernel<OM_DTYPE_F16><<<grid, 256, 0, c->compute>>>(
+            static_cast<const __half*>(pIn), pOut, nN, nC, nH, nW, nCs);
+    else
+        return OM_ERR_UNSUPPORTED;
+    return after_launch(c);
+}
+
+extern "C" int omCudaMaxPool2dNhwc(const void* pIn, void* pOut, int nN, int nH, int nW, int nCs,
+                                   int nK, int nStride, int nPad, int nDtype) {
+    OMB_CTX_OR_FAIL(c);
+    if (!pIn || !pOut || nCs % 8 || !aligned16(pIn) || !aligned16(pOut)) return OM_ERR_INVALID;
+    int P = (nH + 2 * nPad - nK) / nStride + 1, Q = (nW + 2 * nPad - nK) / nStride + 1;
+    if (P <= 0 || Q <= 0) return OM_ERR_INVALID;
+    long long total = (long long)nN * P * Q * (nCs / 8);
+    int grid = ew_grid(c, total, 256);
+    if (nDtype == OM_DTYPE_BF16)
+        maxpool_nhwc_kernel<OM_DTYPE_BF16><<<grid, 256, 0, c->compute>>>(
+            static_cast<const uint4*>(pIn), static_cast<uint4*>(pOut), nN, nH, nW, nCs / 8, P, Q, nK, nStride, nPad);
+    else if (nDtype == OM_DTYPE_F16)
+        maxpool_nhwc_kernel<OM_DTYPE_F16><<<grid, 256, 0, c->compute>>>(
+            static_cast<const uint4*>(pIn), static_cast<uint4*>(pOut), nN, nH, nW, nCs / 8, P, Q, nK, nStride, nPad);
+    else
+        return OM_ERR_UNSUPPORTED;
+    return after_launch(c);
+}
+
+extern "C" int omCudaGlobalAvgPoolNhwc(const void* pIn, void* pOut, int nN, int nHW, int nCs,
+                                       int nDtype, int nOutDtype) {
+    OMB_CTX_OR_FAIL(c);
+    if (!pIn || !pOut || nCs % 8 || nCs > 2048 || !aligned16(pIn)) return OM_ERR_INVALID;
+    if (nOutDtype != OM_DTYPE_F32 && nOutDtype != nDtype) return OM_ERR_UNSUPPORTED;
+    int C8 = nCs / 8;
+    size_t sh = sizeof(float) * (size_t)nCs;
+    int of32 = nOutDtype == OM_DTYPE_F32;
+    if (nDtype == OM_DTYPE_BF16)
+        gap_nhwc_kernel<OM_DTYPE_BF16><<<nN, 256, sh, c->compute>>>(static_cast<const uint4*>(pIn), pOut, nHW, C8, of32);
+    else if (nDtype == OM_DTYPE_F16)
+        gap_nhwc_kernel<OM_DTYPE_F16><<<nN, 256, sh, c->compute>>>(static_cast<const uint4*>(pIn), pOut, nHW, C8, of32);
+    else
+        return OM_ERR_UNSUPPORTED;
+    return after_launch(c);
+}
+
+extern "C" int omCudaPackDepthwiseWeight(const float* pWeight, const float* pGamma,
+                                         const float* pBeta, const float* pMean, const float* pVar,
+                                         float fEps, float* pPacked, float* pBiasOut, int nC,
+                                         int nKH, int nKW, int nCs) {
+    OMB_CTX_OR_FAIL(c);
+    if (!pWeight || !pPacked || !pBiasOut || nCs < nC) return OM_ERR_INVALID;
+    float *scale = nullptr, *bias = nullptr;
+    OMB_CHECK(cudaMallocAsync(&scale, sizeof(float) * nC, c->compute));
+    OMB_CHECK(cudaMallocAsync(&bias, sizeof(float) * nC, c->compute));
+    fold_bn_kernel<<<(nC + 255) / 256, 256, 0, c->compute>>>(nullptr, pGamma, pBeta, pMean, pVar,
+                                                             fEps, scale, bias, nC);
+    int st = after_launch(c);
+    if (st == OM_OK) {
+        int total = nKH * nKW * nCs;
+        pack_depthwise_kernel<<<(total + 255) / 256, 256, 0, c->compute>>>(
+            pWeight, scale, bias, pPacked, pBiasOut, nC, nKH * nKW, nCs);
+        st = after_launch(c);
+    }
+    cudaFreeAsync(scale, c->compute);
+    cudaFreeAsync(bias, c->compute);
+    return st;
+}
+
+extern "C" int omCudaDepthwiseConv2dNhwc(const void* pIn, const float* pPacked, const float* pBias,
+                                         void* pOut, int nN, int nH, int nW, int nCs, int nKH,
+                                         int nKW, int nStride, int nPad, int nAct, int nDtype) {
+    OMB_CTX_OR_FAIL(c);
+    if (!pIn || !pOut || !pPacked || !pBias || nCs % 8 || !aligned16(pIn) || !aligned16(pOut) ||
+        !aligned16(pPacked) || !aligned16(pBias))
+        return OM_ERR_INVALID;
+    int P = (nH + 2 * nPad - nKH) / nStride + 1, Q = (nW + 2 * nPad - nKW) / nStride + 1;
+    if (P <= 0 || Q <= 0) return OM_ERR_INVALID;
+    long long total = (long long)nN * P * Q * (nCs / 8);
+    int grid = ew_grid(c, total, 256);
+    if (nDtype == OM_DTYPE_BF16)
+        depthwise_nhwc_kernel<OM_DTYPE_BF16><<<grid, 256, 0, c->compute>>>(
+            static_cast<const uint4*>(pIn), pPacked, pBias, static_cast<uint4*>(pOut), nN, nH, nW,
+            nCs / 8, P, Q, nKH, nKW, nStride, nPad, nAct);
+    else if (nDtype == OM_DTYPE_F16)
+        depthwise_nhwc_kernel<OM_DTYPE_F16><<<grid, 256, 0, c->compute>>>(
+            static_cast<const uint4*>(pIn), pPacked, pBias, static_cast<uint4*>(pOut), nN, nH, nW,
+            nCs / 8, P, Q, nKH, nKW, nStride, nPad, nAct);
+    else
+        return OM_ERR_UNSUPPORTED;
+    return after_launch(c);
+}
+
+extern "C" int omCudaAddActNhwc(const void* pA, const void* pB, void* pOut, long long nCount,
+                                int nAct, int nDtype) {
+    OMB_CTX_OR_FAIL(c);
+    if (!pA || !pB || !pOut || nCount % 8 || !aligned16(pA) || !aligned16(pB) || !aligned16(pOut))
+        return OM_ERR_INVALID;
+    long long n8 = nCount / 8;
+    int grid = ew_grid(c, n8, 256);
+    if (nDtype == OM_DTYPE_BF16)
+        add_act_kernel<OM_DTYPE_BF16><<<grid, 256, 0, c->compute>>>(
+            static_cast<const uint4*>(pA), static_cast<const uint4*>(pB), static_cast<uint4*>(pOut), n8, nAct);
+    else if (nDtype == OM_DTYPE_F16)
+        add_act_kernel<OM_DTYPE_F16><<<grid, 256, 0, c->compute>>>(
+            static_cast<const uint4*>(pA), static_cast<const uint4*>(pB), static_cast<uint4*>(pOut), n8, nAct);
+    else
+        return OM_ERR_UNSUPPORTED;
+    return after_launch(c);
+}

@@ -1,0 +1,129 @@
+"""Parity of the tcgen05 implicit-GEMM conv (omCudaConv2dBnAct) with the CPU oracle.
+
+Each case runs conv -> eval BatchNorm -> (+ residual) -> activation on seeded inputs in the
+reference layout (NCHW fp32) through the oracle, and the same through the NHWC 16-bit fused
+kernel. Two checks per case, both with max|a-b|/max|b|:
+  * against the oracle fed the same 16-bit-rounded input, weights (BN folded) and residual:
+    <= 1e-2 (only accumulation order and the 16-bit output rounding differ);
+  * against the fp32 oracle on the unrounded data: <= 2e-2 (the 16-bit tolerance).
+"""
+import numpy as np
+import pytest
+
+from conftest import rel_err
+
+pytestmark = pytest.mark.gpu
+
+# n, c, h, k, ksize, stride, pad, dtype, residual, act, out_f32
+CASES = [
+    (2, 64, 14, 64, 3, 1, 1, "bf16", False, "relu", False),       # SW128, BN=64
+    (4, 128, 7, 256, 1, 1, 0, "bf16", False, "relu", False),      # 1x1, M < one wave
+    (3, 64, 15, 128, 3, 2, 1, "bf16", False, "relu", False),      # stride 2, ragged M
+    (2, 64, 14, 256, 1, 2, 0, "bf16", False, "none", False),      # strided 1x1 downsample
+    (2, 3, 32, 64, 7, 2, 3, "bf16", False, "relu", False),        # ImageNet stem, Cs=8
+    (2, 32, 16, 128, 1, 1, 0, "f16", False, "relu6", False),      # C=32 interleaved
+    (2, 128, 8, 32, 1, 1, 0, "f16", True, "none", False),         # BN=32 + residual
+    (2, 64, 14, 64, 3, 1, 1, "f16", True, "relu", False),         # fp16 + residual
+    (16, 64, 56, 256, 1, 1, 0, "bf16", True, "relu", False),      # BN=256 tiles
+    (16, 256, 14, 256, 3, 1, 1, "bf16", False, "relu", False),    # 36 k-blocks
+    (5, 2048, 1, 1000, 1, 1, 0, "bf16", False, "none", True),     # FC: M=5, K=1000, fp32 out
+    (2, 3, 31, 32, 3, 2, 1, "f16", False, "relu6", False),        # MobileNet stem, odd H
+]
+
+
+def _round16(a, dtype):
+    import torch
+    t = torch.from_numpy(np.ascontiguousarray(a, np.float32))
+    t = t.to(torch.bfloat16 if dtype == "bf16" else torch.float16).to(torch.float32)
+    return t.numpy()
+
+
+def _reference(x, w, bn, res, stride, pad, act):
+    import oracle as orc
+    y = orc.conv2d(x, w, None, stride, pad)
+    y = orc.batchnorm_eval(y, *bn)
+    if res is not None:
+        y = y + res
+    if act == "relu":
+        y = orc.relu(y)
+    elif act == "relu6":
+        y = orc.relu6(y)
+    return y
+
+
+@pytest.mark.parametrize("case", CASES, ids=[f"c{i}" for i in range(len(CASES))])
+def test_conv_bn_act(gpu, case):
+    from omnimatchdeeplearningtool_b200 import _lib
+    from omnimatchdeeplearningtool_b200.backend import DeviceBuffer
+    from omnimatchdeeplearningtool_b200._lib import call, lib
+
+    n, c, h, k, ks, stride, pad, dt, use_res, act, out_f32 = case
+    rng = np.random.Generator(np.random.PCG64(1234 + c * 7 + k))
+    x = rng.standard_normal((n, c, h, h), dtype=np.float32)
+    w = (rng.standard_normal((k, c, ks, ks)) * np.sqrt(2.0 / (c * ks * ks))).astype(np.float32)
+    gamma = rng.uniform(0.5, 1.5, k).astype(np.float32)
+    beta = (rng.standard_normal(k) * 0.1).astype(np.float32)
+    mean = (rng.standard_normal(k) * 0.1).astype(np.float32)
+    var = rng.uniform(0.5, 1.5, k).astype(np.float32)
+    p = (h + 2 * pad - ks) // stride + 1
+    res = rng.standard_normal((n, k, p, p), dtype=np.float32) if use_res else None
+    dtype = _lib.DTYPE_BF16 if dt == "bf16" else _lib.DTYPE_F16
+    odt = _lib.DTYPE_F32 if out_f32 else dtype
+    act_id = {"none": 0, "relu": 1, "relu6": 2}[act]
+
+    cs = int(lib.omCudaStoredChannels(c))
+    dx32 = DeviceBuffer.from_numpy(x)
+    dx = DeviceBuffer(n * h * h * cs * 2)
+    call("omCudaNchwToNhwc", dx32.ptr, dx.ptr, n, c, h, h, cs, dtype)
+    dw = DeviceBuffer.from_numpy(w)
+    bufs = [DeviceBuffer.from_numpy(a) for a in (gamma, beta, mean, var)]
+    packed = DeviceBuffer(int(lib.omCudaPackedConvWeightElems(k, ks, ks, cs)) * 2)
+    bias = DeviceBuffer(k * 4)
+    call("omCudaPackConvWeight", dw.ptr, None, *[b.ptr for b in bufs], 1e-5, packed.ptr, bias.ptr,
+         k, c, ks, ks, cs, dtype)
+    dres = None
+    if use_res:
+        r32 = DeviceBuffer.from_numpy(res)
+        if out_f32:
+            dres = DeviceBuffer.from_numpy(np.ascontiguousarray(res.transpose(0, 2, 3, 1)))
+        else:
+            dres = DeviceBuffer(n * p * p * k * 2)
+            call("omCudaNchwToNhwc", r32.ptr, dres.ptr, n, k, p, p, k, dtype)
+    out = DeviceBuffer(n * p * p * k * (4 if out_f32 else 2))
+    call("omCudaConv2dBnAct", dx.ptr, packed.ptr, bias.ptr, dres.ptr if dres else None, out.ptr,
+         n, h, h, cs, k, ks, ks, stride, pad, act_id, dtype, odt)
+    if out_f32:
+        got = out.to_numpy((n, p, p, k)).transpose(0, 3, 1, 2)
+    else:
+        o32 = DeviceBuffer(n * k * p * p * 4)
+        call("omCudaNhwcToNchw", out.ptr, o32.ptr, n, k, p, p, k, dtype)
+        got = o32.to_numpy((n, k, p, p))
+    assert gpu.kernel_error() == 0
+
+    # fp32 reference on the original data
+    want = _reference(x, w, (gamma, beta, mean, var), res, stride, pad, act)
+    assert np.isfinite(got).all()
+    e32 = rel_err(got, want)
+    # reference on 16-bit-rounded operands with the BN scale folded as the kernel does
+    scale = gamma / np.sqrt(var + 1e-5)
+    wf = _round16(w * scale[:, None, None, None], dt)
+    bf = beta - mean * scale
+    xr = _round16(x, dt)
+    rr = None if res is None else (res if out_f32 else _round16(res, dt))
+    import oracle as orc
+    y = orc.conv2d(xr, wf, bf, stride, pad)
+    if rr is not None:
+        y = y + rr
+    y = orc.relu(y) if act == "relu" else (orc.relu6(y) if act == "relu6" else y)
+    e16 = rel_err(got, y)
+    assert e16 <= 1e-2, f"vs rounded-operand oracle: {e16}"
+    assert e32 <= 2e-2, f"vs fp32 oracle: {e32}"
+
+
+def test_conv_rejects_bad_shapes(gpu):
+    from omnimatchdeeplearningtool_b200._lib import lib
+    # Cs not a multiple of 8 and Cout not a multiple of 8 are reported, not launched
+    assert lib.omCudaConv2dBnAct(16, 16, None, None, 16, 1, 8, 8, 12, 64, 3, 3, 1, 1, 0, 1, 1) == -3
+    assert lib.omCudaConv2dBnAct(16, 16, None, None, 16, 1, 8, 8, 64, 60, 3, 3, 1, 1, 0, 1, 1) == -3
+    # misaligned pointers are rejected
+    assert lib.omCudaConv2dBnAct(18, 16, None, None, 16, 1, 8, 8, 64, 64, 3, 3, 1, 1, 0, 1, 1) == -2

@@ -1,0 +1,272 @@
+"""Parity of the fp32 NCHW entry points (the reference-named C ABI) with the CPU oracle.
+
+Tolerance: the fp32 path's 1e-4, measured as max |a-b| / max |b| over each output tensor
+(the oracle sums in double; fp32 accumulation over hundreds of terms puts isolated
+near-zero elements further off in element-wise relative terms). Integer outputs (max-pool
+argmax indices) and elementwise ops must match exactly.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+
+from conftest import rel_err as rel_err_floor
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-4
+
+
+_KEEP = []  # device buffers stay alive until the test ends (kernels run asynchronously)
+
+
+@pytest.fixture(autouse=True)
+def _release_buffers():
+    yield
+    _KEEP.clear()
+
+
+def _dev(a):
+    from omnimatchdeeplearningtool_b200.backend import DeviceBuffer
+    b = DeviceBuffer.from_numpy(np.ascontiguousarray(a))
+    _KEEP.append(b)
+    return b
+
+
+def _out(shape, dtype=np.float32):
+    from omnimatchdeeplearningtool_b200.backend import DeviceBuffer
+    b = DeviceBuffer.zeros(int(np.prod(shape)) * np.dtype(dtype).itemsize)
+    _KEEP.append(b)
+    return b
+
+
+def _rng(seed):
+    return np.random.Generator(np.random.PCG64(seed))
+
+
+CONV = [  # n, c, h, k, r, stride, pad, bias
+    (2, 3, 32, 16, 7, 2, 3, True),
+    (2, 16, 15, 32, 3, 1, 1, False),
+    (3, 32, 14, 24, 3, 2, 1, True),
+    (2, 64, 8, 128, 1, 2, 0, False),
+    (1, 8, 9, 8, 5, 1, 2, True),
+]
+
+
+@pytest.mark.parametrize("case", CONV)
+def test_conv2d_fwd_bwd(gpu, case):
+    import oracle as orc
+    from omnimatchdeeplearningtool_b200.backend import CUDABackend as B
+    n, c, h, k, r, s, p, use_b = case
+    rng = _rng(n * 100 + c)
+    x = rng.standard_normal((n, c, h, h), dtype=np.float32)
+    w = rng.standard_normal((k, c, r, r), dtype=np.float32) * np.float32(np.sqrt(2 / (c * r * r)))
+    b = rng.standard_normal(k, dtype=np.float32) if use_b else None
+    P = (h + 2 * p - r) // s + 1
+    dy = rng.standard_normal((n, k, P, P), dtype=np.float32)
+    dX, dW, dDY = _dev(x), _dev(w), _dev(dy)
+    dB = _dev(b) if use_b else None
+    y = _out((n, k, P, P))
+    B.conv2d(dX.ptr, dW.ptr, dB.ptr if dB else None, y.ptr, n, c, h, h, k, r, r, p, p, s, s)
+    want = orc.conv2d(x, w, b, s, p)
+    assert rel_err_floor(y.to_numpy(want.shape), want) <= TOL
+    # backward input
+    dx = _out(x.shape)
+    B.conv2dBackwardInput(dDY.ptr, dW.ptr, dx.ptr, n, c, h, h, k, r, r, p, p, s, s)
+    want_dx = np.empty_like(x)
+    orc.O.oracle_conv2d_backward_input(dy.ctypes.data, w.ctypes.data, want_dx.ctypes.data, n, c, h,
+                                       h, k, r, r, s, p)
+    assert rel_err_floor(dx.to_numpy(x.shape), want_dx) <= TOL
+    # backward weight (+ bias)
+    dw = _out(w.shape)
+    db = _out((k,))
+    B.conv2dBackwardWeight(dX.ptr, dDY.ptr, dw.ptr, db.ptr, n, c, h, h, k, r, r, p, p, s, s)
+    want_dw = np.empty_like(w)
+    want_db = np.empty(k, np.float32)
+    orc.O.oracle_conv2d_backward_weight(x.ctypes.data, dy.ctypes.data, want_dw.ctypes.data,
+                                        want_db.ctypes.data, n, c, h, h, k, r, r, s, p)
+    assert rel_err_floor(dw.to_numpy(w.shape), want_dw) <= TOL
+    assert rel_err_floor(db.to_numpy((k,)), want_db) <= TOL
+
+
+def test_grouped_depthwise_conv(gpu):
+    import oracle as orc
+    from omnimatchdeeplearningtool_b200.backend import CUDABackend as B
+    rng = _rng(7)
+    n, c, h = 2, 24, 13
+    x = rng.standard_normal((n, c, h, h), dtype=np.float32)
+    w = rng.standard_normal((c, 1, 3, 3), dtype=np.float32)
+    y = _out((n, c, 7, 7))
+    B.dilatedConv2d(_dev(x).ptr, _dev(w).ptr, None, y.ptr, n, c, h, h, c, 3, 3, 2, 1, 1, c)
+    want = orc.conv2d(x, w, None, 2, 1, groups=c)
+    assert rel_err_floor(y.to_numpy(want.shape), want) <= TOL
+
+
+@pytest.mark.parametrize("training", [0, 1])
+def test_batchnorm_fwd_bwd(gpu, training):
+    import oracle as orc
+    rng = _rng(11 + training)
+    n, c, h, w = 4, 16, 9, 7
+    x = (rng.standard_normal((n, c, h, w)) * 2 + 0.5).astype(np.float32)
+    g = rng.uniform(0.5, 1.5, c).astype(np.float32)
+    b = rng.standard_normal(c).astype(np.float32)
+    rm = (rng.standard_normal(c) * 0.1).astype(np.float32)
+    rv = rng.uniform(0.5, 1.5, c).astype(np.float32)
+    dX, dG, dB, dRM, dRV = _dev(x), _dev(g), _dev(b), _dev(rm), _dev(rv)
+    y, sm, si = _out(x.shape), _out((c,)), _out((c,))
+    from omnimatchdeeplearningtool_b200._lib import call
+    call("omCudaBatchNorm2d", dX.ptr, y.ptr, dG.ptr, dB.ptr, dRM.ptr, dRV.ptr, sm.ptr, si.ptr, n,
+         c, h, w, 1e-5, 0.1, training)
+    wy, wrm, wrv = np.empty_like(x), rm.copy(), rv.copy()
+    wsm, wsi = np.empty(c, np.float32), np.empty(c, np.float32)
+    orc.O.oracle_batchnorm2d(x.ctypes.data, wy.ctypes.data, g.ctypes.data, b.ctypes.data,
+                             wrm.ctypes.data, wrv.ctypes.data, wsm.ctypes.data, wsi.ctypes.data,
+                             n, c, h, w, 1e-5, 0.1, training)
+    assert rel_err_floor(y.to_numpy(x.shape), wy) <= TOL
+    assert rel_err_floor(dRM.to_numpy((c,)), wrm) <= TOL
+    assert rel_err_floor(dRV.to_numpy((c,)), wrv) <= TOL
+    assert rel_err_floor(si.to_numpy((c,)), wsi) <= TOL
+    # backward with the saved statistics
+    dy = rng.standard_normal(x.shape).astype(np.float32)
+    dx, dg, db = _out(x.shape), _out((c,)), _out((c,))
+    call("omCudaBatchNorm2dBackward", _dev(dy).ptr, dX.ptr, sm.ptr, si.ptr, dG.ptr, dx.ptr, dg.ptr,
+         db.ptr, n, c, h, w, 1e-5)
+    wdx, wdg, wdb = np.empty_like(x), np.empty(c, np.float32), np.empty(c, np.float32)
+    orc.O.oracle_batchnorm2d_backward(dy.ctypes.data, x.ctypes.data, wsm.ctypes.data,
+                                      wsi.ctypes.data, g.ctypes.data, wdx.ctypes.data,
+                                      wdg.ctypes.data, wdb.ctypes.data, n, c, h, w)
+    assert rel_err_floor(dg.to_numpy((c,)), wdg) <= TOL
+    assert rel_err_floor(db.to_numpy((c,)), wdb) <= TOL
+    assert rel_err_floor(dx.to_numpy(x.shape), wdx) <= TOL
+
+
+def test_pooling(gpu):
+    import oracle as orc
+    from omnimatchdeeplearningtool_b200.backend import CUDABackend as B
+    rng = _rng(5)
+    n, c, h = 2, 8, 17
+    x = rng.standard_normal((n, c, h, h), dtype=np.float32)
+    dX = _dev(x)
+    P = (h + 2 - 3) // 2 + 1
+    y, idx = _out((n, c, P, P)), _out((n, c, P, P), np.int32)
+    B.maxPool2d(dX.ptr, y.ptr, idx.ptr, n, c, h, h, 3, 3, 2, 1)
+    wy, widx = np.empty((n, c, P, P), np.float32), np.empty((n, c, P, P), np.int32)
+    orc.O.oracle_maxpool2d(x.ctypes.data, wy.ctypes.data, widx.ctypes.data, n, c, h, h, 3, 2, 1)
+    assert np.array_equal(y.to_numpy(wy.shape), wy)
+    assert np.array_equal(idx.to_numpy(widx.shape, np.int32), widx)
+    dy = rng.standard_normal(wy.shape, dtype=np.float32)
+    dx = _out(x.shape)
+    B.maxPool2dBackward(_dev(dy).ptr, idx.ptr, dx.ptr, n, c, h, h, P, P)
+    wdx = np.empty_like(x)
+    orc.O.oracle_maxpool2d_backward(dy.ctypes.data, widx.ctypes.data, wdx.ctypes.data, n, c, P, P, h, h)
+    assert rel_err_floor(dx.to_numpy(x.shape), wdx) <= TOL
+    # average pool 3/2/1 and its backward
+    ay = _out((n, c, P, P))
+    B.avgPool2d(dX.ptr, ay.ptr, n, c, h, h, 3, 3, 2, 1)
+    way = np.empty((n, c, P, P), np.float32)
+    orc.O.oracle_avgpool2d(x.ctypes.data, way.ctypes.data, n, c, h, h, 3, 2, 1)
+    assert rel_err_floor(ay.to_numpy(way.shape), way) <= TOL
+    adx = _out(x.shape)
+    B.avgPool2dBackward(_dev(dy).ptr, adx.ptr, n, c, h, h, 3, 3, 2, 1)
+    wadx = np.empty_like(x)
+    orc.O.oracle_avgpool2d_backward(dy.ctypes.data, wadx.ctypes.data, n, c, h, h, 3, 2, 1)
+    assert rel_err_floor(adx.to_numpy(x.shape), wadx) <= TOL
+    # adaptive average pool to 1x1 and 3x2
+    for oh, ow in ((1, 1), (3, 2)):
+        g = _out((n, c, oh, ow))
+        B.adaptiveAvgPool2d(dX.ptr, g.ptr, n, c, h, h, oh, ow)
+        wg = np.empty((n, c, oh, ow), np.float32)
+        orc.O.oracle_adaptive_avgpool2d(x.ctypes.data, wg.ctypes.data, n, c, h, h, oh, ow)
+        assert rel_err_floor(g.to_numpy(wg.shape), wg) <= TOL
+        gd = rng.standard_normal(wg.shape, dtype=np.float32)
+        gx = _out(x.shape)
+        B.adaptiveAvgPool2dBackward(_dev(gd).ptr, gx.ptr, n, c, h, h, oh, ow)
+        wgx = np.empty_like(x)
+        orc.O.oracle_adaptive_avgpool2d_backward(gd.ctypes.data, wgx.ctypes.data, n, c, h, h, oh, ow)
+        assert rel_err_floor(gx.to_numpy(x.shape), wgx) <= TOL
+
+
+def test_softmax_ce_sgd_matmul(gpu):
+    import oracle as orc
+    from omnimatchdeeplearningtool_b200.backend import CUDABackend as B
+    rng = _rng(9)
+    n, k = 8, 1000
+    logits = (rng.standard_normal((n, k)) * 3).astype(np.float32)
+    oh = np.zeros((n, k), np.float32)
+    oh[np.arange(n), rng.integers(0, k, n)] = 1
+    dL, dT = _dev(logits), _dev(oh)
+    p = _out((n, k))
+    B.softmax(dL.ptr, p.ptr, n, k)
+    wp = np.empty_like(logits)
+    orc.O.oracle_softmax(logits.ctypes.data, wp.ctypes.data, n, k)
+    assert rel_err_floor(p.to_numpy((n, k)), wp) <= TOL
+    loss = _out((1,))
+    B.crossEntropyForward(p.ptr, dT.ptr, loss.ptr, n, k)
+    wl = orc.O.oracle_cross_entropy(wp.ctypes.data, oh.ctypes.data, n, k)
+    assert abs(loss.to_numpy((1,))[0] - wl) <= TOL * abs(wl)
+    g = _out((n, k))
+    B.crossEntropySoftmaxBackward(p.ptr, dT.ptr, g.ptr, n, k)
+    wg = np.empty_like(logits)
+    orc.O.oracle_ce_softmax_backward(wp.ctypes.data, oh.ctypes.data, wg.ctypes.data, n, k)
+    assert rel_err_floor(g.to_numpy((n, k)), wg) <= TOL
+    # SGD with momentum, two steps (test_nn.cpp:70-104 pins 1 - 0.1*2 = 0.8 for one plain step)
+    prm = rng.standard_normal(1000).astype(np.float32)
+    grd = rng.standard_normal(1000).astype(np.float32)
+    vel = np.zeros(1000, np.float32)
+    dP, dG, dV = _dev(prm), _dev(grd), _dev(vel)
+    wprm, wvel = prm.copy(), vel.copy()
+    for _ in range(2):
+        B.sgdStep(dP.ptr, dG.ptr, dV.ptr, 1000, 0.01, 0.9)
+        orc.O.oracle_sgd_step(wprm.ctypes.data, grd.ctypes.data, wvel.ctypes.data, 1000, 0.01, 0.9)
+    assert rel_err_floor(dP.to_numpy((1000,)), wprm) <= TOL
+    one = _dev(np.array([1.0], np.float32))
+    B.sgdStep(one.ptr, _dev(np.array([2.0], np.float32)).ptr, None, 1, 0.1, 0.0)
+    assert abs(one.to_numpy((1,))[0] - 0.8) < 1e-7
+    # matmul, including the reference KATs (test_tensor_ops.cpp:55-82)
+    a = rng.standard_normal((37, 70)).astype(np.float32)
+    bm = rng.standard_normal((70, 45)).astype(np.float32)
+    c = _out((37, 45))
+    B.matmul(_dev(a).ptr, _dev(bm).ptr, c.ptr, 37, 70, 45)
+    wc = np.empty((37, 45), np.float32)
+    orc.O.oracle_matmul(a.ctypes.data, bm.ctypes.data, wc.ctypes.data, 37, 70, 45)
+    assert rel_err_floor(c.to_numpy((37, 45)), wc) <= TOL
+    c2 = _out((2, 2))
+    B.matmul(_dev(np.array([[1, 2], [3, 4]], np.float32)).ptr,
+             _dev(np.array([[5, 6], [7, 8]], np.float32)).ptr, c2.ptr, 2, 2, 2)
+    assert np.array_equal(c2.to_numpy((2, 2)), np.array([[19, 22], [43, 50]], np.float32))
+    c3 = _out((2, 2))
+    B.matmul(_dev(np.array([[1, 2, 3], [4, 5, 6]], np.float32)).ptr,
+             _dev(np.array([[7, 8], [9, 10], [11, 12]], np.float32)).ptr, c3.ptr, 2, 3, 2)
+    assert np.array_equal(c3.to_numpy((2, 2)), np.array([[58, 64], [139, 154]], np.float32))
+
+
+def test_elementwise_and_bias(gpu):
+    from omnimatchdeeplearningtool_b200.backend import CUDABackend as B
+    rng = _rng(13)
+    x = rng.standard_normal(1003).astype(np.float32)
+    y = rng.standard_normal(1003).astype(np.float32)
+    dX, dY = _dev(x), _dev(y)
+    o = _out((1003,))
+    B.add(dX.ptr, dY.ptr, o.ptr, 1003)
+    assert np.array_equal(o.to_numpy((1003,)), x + y)
+    B.relu(dX.ptr, o.ptr, 1003)
+    assert np.array_equal(o.to_numpy((1003,)), np.maximum(x, 0))
+    B.reluBackward(dX.ptr, dY.ptr, o.ptr, 1003)
+    assert np.array_equal(o.to_numpy((1003,)), np.where(x > 0, y, 0))
+    B.clip(dX.ptr, o.ptr, 1003, 0.0, 0.5)
+    assert np.array_equal(o.to_numpy((1003,)), np.clip(x, 0, 0.5))
+    n, c, hw = 3, 5, 7
+    a = rng.standard_normal((n, c, hw)).astype(np.float32)
+    bias = rng.standard_normal(c).astype(np.float32)
+    ob = _out(a.shape)
+    B.addBias(_dev(a).ptr, _dev(bias).ptr, ob.ptr, n, c, hw)
+    assert np.allclose(ob.to_numpy(a.shape), a + bias[None, :, None], atol=0, rtol=0)
+    gb = _out((c,))
+    B.addBiasBackward(_dev(a).ptr, gb.ptr, n, c, hw)
+    assert rel_err_floor(gb.to_numpy((c,)), a.sum(axis=(0, 2))) <= TOL
+    am = _out((n,), np.int32)
+    m = rng.standard_normal((n, 1000)).astype(np.float32)
+    B.argmax(_dev(m).ptr, am.ptr, n, 1000)
+    assert np.array_equal(am.to_numpy((n,), np.int32), m.argmax(1))
+    t = _out((1003,))
+    B.transpose(_dev(x[:1000].reshape(20, 50)).ptr, t.ptr, 20, 50)
+    assert np.array_equal(t.to_numpy((50, 20)), x[:1000].reshape(20, 50).T)
