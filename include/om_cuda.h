@@ -35,6 +35,7 @@ extern "C" {
 #define OM_ERR_OOM (-5)           /* device allocation failed after releasing the cache */
 #define OM_ERR_KERNEL_TIMEOUT (-6)/* a bounded in-kernel wait gave up (see omCudaGetKernelError) */
 #define OM_ERR_DRIVER (-7)        /* a driver entry point (tensor-map encode) was unavailable */
+#define OM_ERR_TOO_LARGE (-8)     /* request exceeds the fixed capacity of an allocation-free entry point */
 
 /* element types for the NHWC entry points */
 #define OM_DTYPE_F32 0
@@ -120,6 +121,18 @@ int omCudaBatchNorm2d(const float* pInput, float* pOutput, const float* pGamma,
                       const float* pBeta, float* pRunMean, float* pRunVar, float* pSavedMean,
                       float* pSavedInvStd, int nBatch, int nChannels, int nH, int nW,
                       float fEps, float fMomentum, int bTraining);              /* replaces :1648 */
+/* No counterpart in the reference. Same arguments and results as omCudaBatchNorm2d, for
+ * callers that must not allocate device memory once they are running (for example an
+ * inspection loop that reserved its whole VRAM budget at start-up, or an engine embedded in a
+ * host whose allocator owns the device): it never calls cudaMalloc/cudaFree or an allocating
+ * routine. Training-mode statistics use a fixed 2 MiB per-device array inside this library
+ * (up to 4096 channels; more returns OM_ERR_TOO_LARGE without launching). The first call on a
+ * device looks that array up; make that first call before any stream capture. All calls on a
+ * device share the array, so calls whose kernels overlap on the GPU race with each other. */
+int omCudaBatchNorm2dNoAlloc(const float* pInput, float* pOutput, const float* pGamma,
+                             const float* pBeta, float* pRunMean, float* pRunVar,
+                             float* pSavedMean, float* pSavedInvStd, int nBatch, int nChannels,
+                             int nH, int nW, float fEps, float fMomentum, int bTraining);
 int omCudaBatchNorm2dBackward(const float* pGradOutput, const float* pInput, const float* pMean,
                               const float* pInvStd, const float* pGamma, float* pGradInput,
                               float* pGradGamma, float* pGradBeta, int nBatch, int nChannels,

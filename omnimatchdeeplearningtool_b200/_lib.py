@@ -22,6 +22,7 @@ STATUS_NAMES = {
     -5: "OM_ERR_OOM",
     -6: "OM_ERR_KERNEL_TIMEOUT",
     -7: "OM_ERR_DRIVER",
+    -8: "OM_ERR_TOO_LARGE",
 }
 DTYPE_F32, DTYPE_BF16, DTYPE_F16 = 0, 1, 2
 ACT_NONE, ACT_RELU, ACT_RELU6 = 0, 1, 2
@@ -79,6 +80,7 @@ _SIGS = {
     # norm / pool / loss / optimiser
     "omCudaBatchNorm2d": [P, P, P, P, P, P, P, P, I, I, I, I, F, F, I],
     "omCudaBatchNorm2dBackward": [P, P, P, P, P, P, P, P, I, I, I, I, F],
+    "omCudaBatchNorm2dNoAlloc": [P, P, P, P, P, P, P, P, I, I, I, I, F, F, I],
     "omCudaMaxPool2d": [P, P, P, I, I, I, I, I, I, I, I, I, I],
     "omCudaMaxPool2dBackward": [P, P, P, I, I, I, I, I, I],
     "omCudaAvgPool2d": [P, P, I, I, I, I, I, I, I, I, I, I],

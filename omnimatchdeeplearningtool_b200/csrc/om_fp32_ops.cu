@@ -12,6 +12,8 @@
 // BatchNorm statistics are reduced per channel over N*H*W by a (channel x split) grid whose
 // per-split partial sums go to a small scratch buffer, then combined in a fixed order, so
 // the result is deterministic and large feature maps still fill all SMs.
+#include <mutex>
+
 #include "om_common.cuh"
 
 namespace omb {
@@ -684,5 +686,70 @@ extern "C" int omCudaTranspose(const float* pIn, float* pOut, int nRows, int nCo
     if (!pIn || !pOut || nRows <= 0 || nCols <= 0) return OM_ERR_INVALID;
     dim3 grid((nCols + 31) / 32, (nRows + 31) / 32);
     transpose_kernel<<<grid, dim3(32, 8), 0, c->compute>>>(pIn, pOut, nRows, nCols);
+    return after_launch(c);
+}
+
+// ---------------------------------------------------------------- allocation-free BatchNorm
+// For callers that cannot allocate device memory while they run (a fixed VRAM budget reserved
+// up front, or a host process that owns the device allocator): the training-mode partial sums
+// live in a file-scope device array instead of pool memory. The array costs 2 MiB on every
+// device that loads this library, for as long as the process lives.
+namespace omb {
+namespace ops {
+constexpr int kNoAllocMaxChannels = 4096;
+constexpr int kNoAllocMaxSplits = 64;  // bn_splits never returns more
+static __device__ __align__(256) float g_bnNoAllocScratch[2 * kNoAllocMaxChannels * kNoAllocMaxSplits];
+// Device address of the array per device. In host code the array's name is only a host-side
+// stand-in, so the real address is looked up once per device with that device current.
+static float* g_bnNoAllocAddr[64] = {nullptr};
+static std::mutex g_bnNoAllocMu;
+}  // namespace ops
+}  // namespace omb
+
+extern "C" int omCudaBatchNorm2dNoAlloc(const float* pInput, float* pOutput, const float* pGamma,
+                                        const float* pBeta, float* pRunMean, float* pRunVar,
+                                        float* pSavedMean, float* pSavedInvStd, int nBatch,
+                                        int nChannels, int nH, int nW, float fEps,
+                                        float fMomentum, int bTraining) {
+    OMB_CTX_OR_FAIL(c);
+    if (!pInput || !pOutput || !pGamma || !pBeta || !pRunMean || !pRunVar || !pSavedMean ||
+        !pSavedInvStd || nBatch <= 0 || nChannels <= 0 || nH <= 0 || nW <= 0)
+        return OM_ERR_INVALID;
+    if (nChannels > kNoAllocMaxChannels) return OM_ERR_TOO_LARGE;
+    const int HW = nH * nW;
+    const long long cnt = (long long)nBatch * HW;
+    int S = 1;
+    float* scratch = nullptr;
+    if (bTraining) {
+        {
+            std::lock_guard<std::mutex> lock(g_bnNoAllocMu);
+            if (!g_bnNoAllocAddr[c->device]) {
+                void* addr = nullptr;
+                OMB_CHECK(cudaGetSymbolAddress(&addr, g_bnNoAllocScratch));
+                g_bnNoAllocAddr[c->device] = static_cast<float*>(addr);
+            }
+            scratch = g_bnNoAllocAddr[c->device];
+        }
+        S = bn_splits(c, nChannels, cnt);
+        if (S > kNoAllocMaxSplits) S = kNoAllocMaxSplits;
+        // Nothing needs clearing: each call writes every partial-sum slot it later reads.
+        const long long chunk = (cnt + S - 1) / S;
+        bn_partial_sum_kernel<<<dim3(nChannels, S), 256, 0, c->compute>>>(pInput, scratch, nChannels,
+                                                                          HW, cnt, chunk);
+        int st = after_launch(c);
+        if (st != OM_OK) return st;
+        bn_partial_m2_kernel<<<dim3(nChannels, S), 256, 0, c->compute>>>(
+            pInput, scratch, scratch + (long long)nChannels * S, nChannels, HW, cnt, chunk);
+        st = after_launch(c);
+        if (st != OM_OK) return st;
+    }
+    bn_finalize_kernel<<<(nChannels + 127) / 128, 128, 0, c->compute>>>(
+        scratch, scratch ? scratch + (long long)nChannels * S : nullptr, S, cnt, pRunMean, pRunVar,
+        pSavedMean, pSavedInvStd, fEps, fMomentum, bTraining, nChannels);
+    int st = after_launch(c);
+    if (st != OM_OK) return st;
+    const long long total = cnt * nChannels;
+    bn_apply_kernel<<<OMB_EW(total)>>>(pInput, pOutput, pGamma, pBeta, pSavedMean, pSavedInvStd,
+                                       total, nChannels, HW);
     return after_launch(c);
 }
