@@ -196,6 +196,8 @@ def run_reference(args, world, rank, dist):
 
 
 def run_ours(args, world, rank, local, dist):
+    global BATCH
+    BATCH = args.batch
     import numpy as np
     import torch
     from omnimatchdeeplearningtool_b200 import _lib, backend, synth
@@ -339,6 +341,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--ref-batch", type=int, default=4)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=BATCH,
+                    help="images per GPU (the metric is quoted at 256; smaller sizes are for "
+                         "profiler captures)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

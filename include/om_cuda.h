@@ -189,6 +189,18 @@ int omCudaConv2dBnAct(const void* pInput, const void* pPacked, const float* pBia
                       const void* pResidual, void* pOutput, int nBatch, int nH, int nW, int nCs,
                       int nCout, int nKH, int nKW, int nStride, int nPad, int nAct, int nDtype,
                       int nOutDtype);
+/* new: the image stem (few input channels, KW <= 8) straight from the NCHW fp32 image:
+ * out[n,p,q,k] = act(sum_{r,s,c} x[n,c,p*st-pad+r,q*st-pad+s] * W'[k,(r,c,s)] + bias[k]),
+ * NHWC 16-bit output, W' from omCudaPackStemWeight (BN folded as in omCudaPackConvWeight).
+ * Same tcgen05 kernel as omCudaConv2dBnAct; the A tile is gathered by threads. */
+long long omCudaPackedStemWeightElems(int nCout, int nCin, int nKH);
+int omCudaPackStemWeight(const float* pWeight, const float* pConvBias, const float* pGamma,
+                         const float* pBeta, const float* pMean, const float* pVar, float fEps,
+                         void* pPacked, float* pBiasOut, int nCout, int nCin, int nKH, int nKW,
+                         int nDtype);
+int omCudaStemConvBnAct(const float* pInput, const void* pPacked, const float* pBias,
+                        void* pOutput, int nBatch, int nCin, int nH, int nW, int nCout, int nKH,
+                        int nKW, int nStride, int nPad, int nAct, int nDtype);
 /* NCHW fp32 -> NHWC (nDtype) with channels zero-padded to nCs */
 int omCudaNchwToNhwc(const float* pIn, void* pOut, int nN, int nC, int nH, int nW, int nCs,
                      int nDtype);

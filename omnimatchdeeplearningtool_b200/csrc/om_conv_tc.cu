@@ -11,22 +11,29 @@
 // slice is one TMA im2col load of 128 consecutive output pixels, with padding zero-filled by
 // the TMA unit. B is the packed K-major weight [Cout, Kpad] (omCudaPackConvWeight).
 //
-// CTA = 6 warps, persistent over output tiles (grid = #SMs):
+// CTA, persistent over output tiles (grid = #SMs):
 //   warp 0      TMA producer (one elected lane)
 //   warp 1      TMEM allocator + MMA issuer (one elected lane): tcgen05.mma.cta_group::1
 //               .kind::f16, M=128, N=BN, K=16, fp32 accumulators in TMEM
-//   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns, + bias, + residual, activation,
-//               16-bit or fp32 store
+//   warps 2..5  epilogue, one per TMEM lane quarter (32 output pixels), in 32-column chunks:
+//               tcgen05.ld -> + bias -> + residual -> activation -> 16-bit, with the residual
+//               sub-tile brought in by TMA one chunk ahead and the output sub-tile written by
+//               a TMA store from a 64-byte-swizzled staging buffer (fp32 outputs, i.e. the
+//               classifier, store directly)
+//   warps 6..13 MODE_STEM only: build the A tile from the NCHW fp32 image (see below)
 // Two TMEM accumulators (2*BN columns) let the epilogue of tile i overlap the MMAs of i+1.
 //
 // Operand layouts in shared memory (K-major, matching the UMMA canonical layouts):
 //   MODE_SW128: Cs % 64 == 0. One im2col box = 128 pixels x 64 channels = 128 rows of 128 B,
 //               written by TMA with the 128-byte swizzle; SBO = 1024 B; the K=16 steps advance
 //               the descriptor start address by 32 B inside the swizzle atom.
-//   MODE_INTERLEAVE: Cs % 8 == 0 (the 3-channel stem padded to 8, the 32-channel MobileNet
-//               layers). A stage holds 8 im2col boxes of 128 pixels x 8 channels (2 KB each,
-//               no swizzle): core matrices of 8 rows x 16 B, SBO = 128 B (next 8 rows),
-//               LBO = 2 KB (next 8 K-elements).
+//   MODE_INTERLEAVE: Cs % 8 == 0 (the 32-channel MobileNet layers). A stage holds 8 im2col
+//               boxes of 128 pixels x 8 channels (2 KB each, no swizzle): core matrices of
+//               8 rows x 16 B, SBO = 128 B (next 8 rows), LBO = 2 KB (next 8 K-elements).
+//   MODE_STEM:  the image stem (3 channels, KW <= 8). K is ordered (r, c, s) with the taps s
+//               padded to 8, so one 16-byte chunk of an A row holds 8 horizontal taps of one
+//               image plane row; gather warps read them from the NCHW fp32 image, round to
+//               16 bits and store them at their 128-byte-swizzled positions. B is SW128.
 //
 // Every mbarrier wait is bounded (OMB_WAIT_NS); a wait that gives up records a bit in the
 // device error word, raises a CTA-wide abort flag, and the CTA drains its in-flight TMA
@@ -44,10 +51,16 @@ namespace tc {
 constexpr int BM = 128;                 // output pixels per tile (TMEM lanes)
 constexpr int BK = 64;                  // K elements per pipeline stage
 constexpr int A_STAGE_BYTES = BM * BK * 2;
-constexpr int NUM_THREADS = 192;
+constexpr int NUM_EPI_WARPS = 4;        // one per TMEM lane quarter
+constexpr int NUM_GATHER_WARPS = 8;     // MODE_STEM only
+constexpr int NUM_THREADS = 64 + 32 * NUM_EPI_WARPS;
+constexpr int EPI_SUB_BYTES = 32 * 32 * 2;             // one 32x32 16-bit sub-tile
+constexpr int EPI_WARP_BYTES = 4 * EPI_SUB_BYTES;      // 2 residual + 2 output buffers
+constexpr int EPI_BYTES = NUM_EPI_WARPS * EPI_WARP_BYTES;
+constexpr int MAX_DYN_SMEM = 232448;                   // 227 KB per CTA on sm_100
 constexpr unsigned long long OMB_WAIT_NS = 2000000000ull;  // 2 s per wait
 
-enum { MODE_SW128 = 0, MODE_INTERLEAVE = 1 };
+enum { MODE_SW128 = 0, MODE_INTERLEAVE = 1, MODE_STEM = 2 };
 
 struct Params {
     int N, H, W, Cs;
@@ -56,11 +69,13 @@ struct Params {
     int P, Q, M;
     int num_kb;
     int num_m_tiles, num_n_tiles;
+    const float* x;       // MODE_STEM: the NCHW fp32 image
+    int C;                // MODE_STEM: its channel count
     const float* bias;
     const void* residual;
     void* out;
     int act;
-    int out_f32;
+    int out_f32;          // 1: fp32 output stored directly (classifier logits)
     unsigned int* err;
 };
 
@@ -107,6 +122,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
         if (gtimer() - t0 > OMB_WAIT_NS) return false;
     }
 }
+// Bounded wait used on exit paths (no abort flag: it must not give up early).
+__device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity) {
+    unsigned long long t0 = gtimer();
+    while (!mbar_try_wait(bar, parity)) {
+        if (gtimer() - t0 > OMB_WAIT_NS) return false;
+    }
+    return true;
+}
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar,
                                             int x, int y) {
     asm volatile(
@@ -114,6 +137,24 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
         " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
         : "memory");
+}
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+            reinterpret_cast<uint64_t>(map)),
+        "r"(smem_u32(src)), "r"(x), "r"(y)
+        : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// wait until at most N committed bulk groups still read shared memory
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() {
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 __device__ __forceinline__ void tma_load_im2col(void* dst, const CUtensorMap* map, uint64_t* bar,
                                                 int c, int w, int h, int n, uint16_t off_w,
@@ -124,6 +165,9 @@ __device__ __forceinline__ void tma_load_im2col(void* dst, const CUtensorMap* ma
         "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c), "r"(w), "r"(h),
         "r"(n), "h"(off_w), "h"(off_h)
         : "memory");
+}
+__device__ __forceinline__ void fence_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 __device__ __forceinline__ void tc_fence_before() {
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -182,83 +226,62 @@ __host__ __device__ constexpr uint32_t instr_desc() {
            ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
 }
 
-template <int BN>
+// Byte offset of 16-byte chunk j (0..3) of row r in a 32-row x 64-byte sub-tile laid out
+// with the 64-byte TMA swizzle (address bits [4,6) ^= bits [7,9)).
+__device__ __forceinline__ uint32_t sw64(int r, int j) {
+    return (uint32_t)(r * 64 + ((j ^ ((r >> 1) & 3)) << 4));
+}
+
+// OCC = CTAs per SM. OCC 2 (BN <= 128, so two CTAs' TMEM fit in 512 columns) halves the
+// stages and doubles the independent pipelines per SM; it is chosen for short-K, memory-bound
+// layers where one CTA cannot keep enough loads and stores in flight.
+template <int BN, int OCC>
 struct Cfg {
     static constexpr int B_STAGE_BYTES = BN * BK * 2;
     static constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
-    static constexpr int STAGES_RAW = (196 * 1024) / STAGE_BYTES;
+    static constexpr int BAR_BYTES = 512;
+    static constexpr int BUDGET = OCC == 1 ? MAX_DYN_SMEM : (233472 - 2048) / 2 - 1024;
+    static constexpr int STAGES_RAW = (BUDGET - 1024 - BAR_BYTES - EPI_BYTES) / STAGE_BYTES;
     static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
     static constexpr int TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
-    // operand stages + barriers/flags + slack for the 1024-byte alignment of the base
-    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 256 + 1024;
+    // operand stages + epilogue buffers + barriers/flags + slack for 1024-byte alignment
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES + 1024;
+    static_assert(SMEM_BYTES <= BUDGET, "shared memory budget");
+    static_assert(STAGES >= 2, "pipeline depth");
+    static_assert(OCC == 1 || TMEM_COLS * OCC <= 512, "TMEM budget");
 };
 
-template <int DT>
-__device__ __forceinline__ void store_row_chunk(const Params& p, int m, int n0,
+// fp32-output chunk (classifier logits): + bias, + fp32 residual, activation, direct store
+__device__ __forceinline__ void store_chunk_f32(const Params& p, int m, int n0,
                                                 const uint32_t (&v)[32]) {
-    // 32 consecutive output channels n0..n0+31 of output pixel m
-    using H = Half16<DT>;
-    float f[32];
-#pragma unroll
-    for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]);
-    if (p.bias) {
-#pragma unroll
-        for (int j = 0; j < 32; j += 4) {
-            if (n0 + j < p.K) {
-                float4 b = *reinterpret_cast<const float4*>(p.bias + n0 + j);
-                f[j] += b.x;
-                f[j + 1] += b.y;
-                f[j + 2] += b.z;
-                f[j + 3] += b.w;
-            }
-        }
-    }
     const size_t row = (size_t)m * p.K;
-    if (p.out_f32) {
-        // fp32 output (classifier logits); the residual, when given, is fp32 as well
 #pragma unroll
-        for (int j = 0; j < 32; j += 4) {
-            if (n0 + j >= p.K) break;
-            float4 o = make_float4(f[j], f[j + 1], f[j + 2], f[j + 3]);
-            if (p.residual) {
-                float4 r = *reinterpret_cast<const float4*>(
-                    static_cast<const float*>(p.residual) + row + n0 + j);
-                o.x += r.x; o.y += r.y; o.z += r.z; o.w += r.w;
-            }
-            o.x = apply_act(o.x, p.act); o.y = apply_act(o.y, p.act);
-            o.z = apply_act(o.z, p.act); o.w = apply_act(o.w, p.act);
-            *reinterpret_cast<float4*>(static_cast<float*>(p.out) + row + n0 + j) = o;
+    for (int j = 0; j < 32; j += 4) {
+        if (n0 + j >= p.K) break;
+        float4 o = make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]),
+                               __uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]));
+        if (p.bias) {
+            float4 b = __ldg(reinterpret_cast<const float4*>(p.bias + n0 + j));
+            o.x += b.x; o.y += b.y; o.z += b.z; o.w += b.w;
         }
-    } else {
-        using T = typename H::T;
-#pragma unroll
-        for (int j = 0; j < 32; j += 8) {
-            if (n0 + j >= p.K) break;
-            if (p.residual) {
-                uint4 rv = *reinterpret_cast<const uint4*>(static_cast<const T*>(p.residual) + row + n0 + j);
-                const typename H::T2* r2 = reinterpret_cast<const typename H::T2*>(&rv);
-#pragma unroll
-                for (int t = 0; t < 4; ++t) {
-                    float2 rr = H::unpack(r2[t]);
-                    f[j + 2 * t] += rr.x;
-                    f[j + 2 * t + 1] += rr.y;
-                }
-            }
-            uint4 ov;
-            typename H::T2* o2 = reinterpret_cast<typename H::T2*>(&ov);
-#pragma unroll
-            for (int t = 0; t < 4; ++t)
-                o2[t] = H::pack(apply_act(f[j + 2 * t], p.act), apply_act(f[j + 2 * t + 1], p.act));
-            *reinterpret_cast<uint4*>(static_cast<T*>(p.out) + row + n0 + j) = ov;
+        if (p.residual) {
+            float4 r = __ldg(reinterpret_cast<const float4*>(
+                static_cast<const float*>(p.residual) + row + n0 + j));
+            o.x += r.x; o.y += r.y; o.z += r.z; o.w += r.w;
         }
+        o.x = apply_act(o.x, p.act); o.y = apply_act(o.y, p.act);
+        o.z = apply_act(o.z, p.act); o.w = apply_act(o.w, p.act);
+        *reinterpret_cast<float4*>(static_cast<float*>(p.out) + row + n0 + j) = o;
     }
 }
 
-template <int BN, int MODE, int DT>
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+template <int BN, int MODE, int DT, int OCC>
+__global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GATHER_WARPS : NUM_THREADS, OCC)
     conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const Params p) {
-    using C = Cfg<BN>;
+                   const __grid_constant__ CUtensorMap tmOut,
+                   const __grid_constant__ CUtensorMap tmRes, const Params p) {
+    using C = Cfg<BN, OCC>;
+    using H16 = Half16<DT>;
     constexpr int STAGES = C::STAGES;
     constexpr bool F16 = (DT == OM_DTYPE_F16);
     extern __shared__ uint8_t smem_raw[];
@@ -266,12 +289,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     uint8_t* sA = smem;
     uint8_t* sB = smem + STAGES * A_STAGE_BYTES;
-    uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * C::B_STAGE_BYTES);
+    uint8_t* sEpi = sB + STAGES * C::B_STAGE_BYTES;
+    uint64_t* full = reinterpret_cast<uint64_t*>(sEpi + EPI_BYTES);
     uint64_t* empty = full + STAGES;
     uint64_t* tfull = empty + STAGES;
     uint64_t* tempty = tfull + 2;
     uint64_t* drain = tempty + 2;
-    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+    uint64_t* resfull = drain + 1;  // [NUM_EPI_WARPS][2]
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(resfull + 2 * NUM_EPI_WARPS);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
     volatile int* consumed = abort_flag + 1;  // stage loads the MMA issuer has consumed
 
@@ -280,18 +305,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < STAGES; ++i) {
-            mbar_init(&full[i], 1);
+            // MODE_STEM: the producer's expect_tx arrival plus one per gather warp
+            mbar_init(&full[i], MODE == MODE_STEM ? 1 + NUM_GATHER_WARPS : 1);
             mbar_init(&empty[i], 1);
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&tfull[i], 1);
-            mbar_init(&tempty[i], 4);
+            mbar_init(&tempty[i], NUM_EPI_WARPS);
         }
+        for (int i = 0; i < 2 * NUM_EPI_WARPS; ++i) mbar_init(&resfull[i], 1);
         mbar_init(drain, 1);
         *abort_flag = 0;
         *consumed = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        fence_async_smem();
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -330,10 +357,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         ok = false;
                         break;
                     }
-                    mbar_expect_tx(&full[stage], C::STAGE_BYTES);
                     uint8_t* a_dst = sA + stage * A_STAGE_BYTES;
                     uint8_t* b_dst = sB + stage * C::B_STAGE_BYTES;
-                    if (MODE == MODE_SW128) {
+                    if (MODE == MODE_STEM) {
+                        // A comes from the gather warps; only the weights travel by TMA
+                        mbar_expect_tx(&full[stage], C::B_STAGE_BYTES);
+                        tma_load_2d(b_dst, &tmB, &full[stage], kb * BK, n0);
+                    } else if (MODE == MODE_SW128) {
+                        mbar_expect_tx(&full[stage], C::STAGE_BYTES);
                         const int kk = kb * BK;
                         const int rs = kk / p.Cs;
                         const int c0 = kk - rs * p.Cs;
@@ -343,6 +374,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                                         (uint16_t)r);
                         tma_load_2d(b_dst, &tmB, &full[stage], kk, n0);
                     } else {
+                        mbar_expect_tx(&full[stage], C::STAGE_BYTES);
                         const int RS = p.R * p.S;
 #pragma unroll 1
                         for (int j = 0; j < 8; ++j) {
@@ -373,14 +405,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             long long done = *consumed;
             for (long long j = (done > issued - STAGES ? done : issued - STAGES); j < issued; ++j) {
                 if (j < 0) continue;
-                const int st = (int)(j % STAGES);
-                const uint32_t ph = (uint32_t)((j / STAGES) & 1);
-                unsigned long long t0 = gtimer();
-                while (!mbar_try_wait(&full[st], ph)) {
-                    if (gtimer() - t0 > OMB_WAIT_NS) {
-                        atomicOr(p.err, ERRBIT_TC_DRAIN);
-                        break;
-                    }
+                if (!mbar_wait_drain(&full[(int)(j % STAGES)], (uint32_t)((j / STAGES) & 1))) {
+                    atomicOr(p.err, ERRBIT_TC_DRAIN);
+                    break;
                 }
             }
         }
@@ -412,7 +439,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
                     for (int k = 0; k < BK / 16; ++k) {
                         uint64_t ad, bd;
-                        if (MODE == MODE_SW128) {
+                        if (MODE != MODE_INTERLEAVE) {
                             ad = smem_desc(a_base + k * 32, 16, 1024, LAYOUT_SW128);
                             bd = smem_desc(b_base + k * 32, 16, 1024, LAYOUT_SW128);
                         } else {
@@ -437,44 +464,225 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             }
             // Drain: every MMA issued by this thread has completed once `drain` flips.
             tc_commit(drain);
-            unsigned long long t0 = gtimer();
-            while (!mbar_try_wait(drain, 0)) {
-                if (gtimer() - t0 > OMB_WAIT_NS) {
+            if (!mbar_wait_drain(drain, 0)) atomicOr(p.err, ERRBIT_TC_DRAIN);
+        }
+    } else if (warp < 2 + NUM_EPI_WARPS) {
+        // ---------------------------------------------------------------- epilogue
+        const int ew = warp - 2;
+        const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+        constexpr int NCH = BN / 32;
+        uint8_t* res_buf = sEpi + ew * EPI_WARP_BYTES;          // 2 residual sub-tiles
+        uint8_t* out_buf = res_buf + 2 * EPI_SUB_BYTES;         // 2 output sub-tiles
+        uint64_t* rbar = resfull + 2 * ew;
+        const bool use_tma = !p.out_f32;
+        const bool has_res = use_tma && p.residual != nullptr;
+        uint32_t g = 0;     // chunks started by this warp (buffer and phase bookkeeping)
+        uint32_t rg = 0;    // residual loads issued by this warp
+        bool ok = true;
+        int local = 0;
+        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+            const int acc = local & 1;
+            const uint32_t acc_phase = (uint32_t)((local >> 1) & 1);
+            const int m_tile = tile / p.num_n_tiles;
+            const int n_tile = tile - m_tile * p.num_n_tiles;
+            const int mw = m_tile * BM + quarter * 32;  // first output pixel of this warp
+            const int nbase = n_tile * BN;
+            if (has_res && lane == 0) {
+                // first chunk's residual, requested before the accumulator is ready
+                fence_async_smem();
+                mbar_expect_tx(&rbar[g & 1], EPI_SUB_BYTES);
+                tma_load_2d(res_buf + (g & 1) * EPI_SUB_BYTES, &tmRes, &rbar[g & 1], nbase, mw);
+            }
+            if (has_res) ++rg;
+            if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
+#pragma unroll 1
+            for (int c = 0; c < NCH; ++c, ++g) {
+                const int n0 = nbase + c * 32;
+                if (has_res && c + 1 < NCH) {
+                    if (lane == 0) {
+                        // the buffer was last read (generic proxy) two chunks ago
+                        fence_async_smem();
+                        const uint32_t nb = (g + 1) & 1;
+                        mbar_expect_tx(&rbar[nb], EPI_SUB_BYTES);
+                        tma_load_2d(res_buf + nb * EPI_SUB_BYTES, &tmRes, &rbar[nb], n0 + 32, mw);
+                    }
+                    ++rg;
+                }
+                uint32_t v[32];
+                tmem_ld32(t_row + (uint32_t)(c * 32), v);
+                const uint32_t b = g & 1;
+                if (!use_tma) {
+                    if (mw + lane < p.M && n0 < p.K) store_chunk_f32(p, mw + lane, n0, v);
+                    continue;
+                }
+                float f[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]);
+                if (p.bias) {
+#pragma unroll
+                    for (int j = 0; j < 32; j += 4) {
+                        if (n0 + j < p.K) {
+                            float4 bb = __ldg(reinterpret_cast<const float4*>(p.bias + n0 + j));
+                            f[j] += bb.x;
+                            f[j + 1] += bb.y;
+                            f[j + 2] += bb.z;
+                            f[j + 3] += bb.w;
+                        }
+                    }
+                }
+                if (has_res) {
+                    // every residual load is waited for, even for chunks past Cout, so that the
+                    // barrier phases stay in step
+                    if (!mbar_wait(&rbar[b], (g >> 1) & 1, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint8_t* rb = res_buf + b * EPI_SUB_BYTES;
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        uint4 rv = *reinterpret_cast<const uint4*>(rb + sw64(lane, j));
+                        const typename H16::T2* r2 = reinterpret_cast<const typename H16::T2*>(&rv);
+#pragma unroll
+                        for (int t = 0; t < 4; ++t) {
+                            float2 rr = H16::unpack(r2[t]);
+                            f[8 * j + 2 * t] += rr.x;
+                            f[8 * j + 2 * t + 1] += rr.y;
+                        }
+                    }
+                }
+                if (n0 >= p.K) continue;  // whole chunk beyond Cout: nothing to store
+                // the store issued two chunks ago from this staging buffer must have been read
+                if (lane == 0) bulk_wait_read<1>();
+                __syncwarp();
+                uint8_t* ob = out_buf + b * EPI_SUB_BYTES;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    uint4 ov;
+                    typename H16::T2* o2 = reinterpret_cast<typename H16::T2*>(&ov);
+#pragma unroll
+                    for (int t = 0; t < 4; ++t)
+                        o2[t] = H16::pack(apply_act(f[8 * j + 2 * t], p.act),
+                                          apply_act(f[8 * j + 2 * t + 1], p.act));
+                    *reinterpret_cast<uint4*>(ob + sw64(lane, j)) = ov;
+                }
+                fence_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    tma_store_2d(&tmOut, ob, n0, mw);
+                    bulk_commit();
+                }
+            }
+            if (!ok) break;
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[acc]);
+        }
+        if (!ok && lane == 0) {
+            atomicOr(p.err, ERRBIT_TC_EPILOGUE);
+            *abort_flag = 1;
+        }
+        if (lane == 0) {
+            // no bulk store may still read shared memory (or be in flight) when the CTA exits
+            bulk_wait_all();
+            // abort path: residual loads issued but never waited for are drained (bounded)
+            for (uint32_t k = g; k < rg; ++k) {
+                if (!mbar_wait_drain(&rbar[k & 1], (k >> 1) & 1)) {
                     atomicOr(p.err, ERRBIT_TC_DRAIN);
                     break;
                 }
             }
         }
-    } else {
-        // ---------------------------------------------------------------- epilogue
-        const int quarter = warp & 3;  // TMEM lane quarter this warp may access
-        const int row = quarter * 32 + lane;
-        int local = 0;
-        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
-            const int acc = local & 1;
-            const uint32_t acc_phase = (uint32_t)((local >> 1) & 1);
-            if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) {
-                if (lane == 0) {
-                    atomicOr(p.err, ERRBIT_TC_EPILOGUE);
-                    *abort_flag = 1;
+        __syncwarp();
+    } else if (MODE == MODE_STEM) {
+        // ---------------------------------------------------------------- gather (stem)
+        // Warps g and g+4 share the 32 rows of lane quarter g % 4 and split each row's 8
+        // chunks. The CTA's (tile, k-block) items form one sequence; two register buffers
+        // alternate so that one item's loads are in flight while the other is stored.
+        const int gw = warp - 2 - NUM_EPI_WARPS;
+        const int row = (gw & 3) * 32 + lane;
+        const int j0 = (gw >> 2) * 4;
+        const int nchunks = p.R * p.C;
+        const size_t plane = (size_t)p.H * p.W;
+        const int my_tiles =
+            (int)blockIdx.x < num_tiles ? (num_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+        const int n_items = my_tiles * p.num_kb;
+        auto load_item = [&](int item, float (&f)[4][8]) {
+            const int tile = (int)blockIdx.x + (item / p.num_kb) * (int)gridDim.x;
+            const int kb = item % p.num_kb;
+            const int m = (tile / p.num_n_tiles) * BM + row;
+            const bool row_ok = m < p.M;
+            const int mm = row_ok ? m : 0;
+            const int img = mm / PQ;
+            const int rem = mm - img * PQ;
+            const int pp = rem / p.Q;
+            const int qq = rem - pp * p.Q;
+            const int ih0 = pp * p.stride - p.pad;
+            const int iw0 = qq * p.stride - p.pad;
+            const bool interior = iw0 >= 0 && iw0 + 8 <= p.W;  // whole 8-wide window inside
+            const float* xim = p.x + (size_t)img * p.C * plane;
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) {
+                const int t = kb * 8 + j0 + jj;
+                const int r = t / p.C;
+                const int ch = t - r * p.C;
+                const int ih = ih0 + r;
+                const bool live = row_ok && t < nchunks && ih >= 0 && ih < p.H;
+                const float* src = xim + ch * plane + (size_t)(live ? ih : 0) * p.W + iw0;
+                if (live && interior) {
+                    // taps beyond S meet zero weights, so the whole window loads unguarded
+#pragma unroll
+                    for (int sx = 0; sx < 8; ++sx) f[jj][sx] = __ldg(src + sx);
+                } else {
+#pragma unroll
+                    for (int sx = 0; sx < 8; ++sx) {
+                        const int iw = iw0 + sx;
+                        f[jj][sx] = (live && iw >= 0 && iw < p.W) ? __ldg(src + sx) : 0.f;
+                    }
                 }
-                break;
             }
-            tc_fence_after();
-            const int m_tile = tile / p.num_n_tiles;
-            const int n_tile = tile - m_tile * p.num_n_tiles;
-            const int m = m_tile * BM + row;
-            const int nbase = n_tile * BN;
-            const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
-#pragma unroll 1
-            for (int c = 0; c < BN / 32; ++c) {
-                uint32_t v[32];
-                tmem_ld32(t_row + (uint32_t)(c * 32), v);
-                if (m < p.M && nbase + c * 32 < p.K) store_row_chunk<DT>(p, m, nbase + c * 32, v);
+        };
+        int stage = 0;
+        uint32_t phase = 0;
+        bool ok = true;
+        auto store_item = [&](const float (&f)[4][8]) -> bool {
+            if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) return false;
+            uint8_t* a_row = sA + stage * A_STAGE_BYTES + row * 128;
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) {
+                const int j = j0 + jj;
+                uint4 v;
+                typename H16::T2* v2 = reinterpret_cast<typename H16::T2*>(&v);
+#pragma unroll
+                for (int u = 0; u < 4; ++u) v2[u] = H16::pack(f[jj][2 * u], f[jj][2 * u + 1]);
+                *reinterpret_cast<uint4*>(a_row + ((j ^ (row & 7)) << 4)) = v;
             }
-            tc_fence_before();
+            // make this thread's generic-proxy smem writes visible to the tensor cores
+            fence_async_smem();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&tempty[acc]);
+            if (lane == 0) mbar_arrive(&full[stage]);
+            if (++stage == STAGES) {
+                stage = 0;
+                phase ^= 1;
+            }
+            return true;
+        };
+        float fa[4][8], fb[4][8];
+        if (n_items > 0) load_item(0, fa);
+        for (int item = 0; item < n_items && ok; item += 2) {
+            if (item + 1 < n_items) load_item(item + 1, fb);
+            if (!store_item(fa)) { ok = false; break; }
+            if (item + 1 >= n_items) break;
+            if (item + 2 < n_items) load_item(item + 2, fa);
+            if (!store_item(fb)) { ok = false; break; }
+        }
+        if (!ok && lane == 0) {
+            atomicOr(p.err, ERRBIT_TC_PRODUCER);
+            *abort_flag = 1;
         }
     }
 
@@ -509,10 +717,26 @@ static bool load_driver_entry_points() {
     return g_encode_tiled && g_encode_im2col;
 }
 
-template <int BN, int MODE, int DT>
-static int launch(DeviceCtx* c, const CUtensorMap& ta, const CUtensorMap& tb, const Params& p) {
-    using Cf = Cfg<BN>;
-    auto kern = conv_tc_kernel<BN, MODE, DT>;
+// 2-D map over a row-major [rows, cols] 16-bit matrix with 32x32 boxes and the 64-byte
+// swizzle, for the epilogue's residual loads and output stores.
+static int encode_epilogue_map(CUtensorMap* map, const void* base, int rows, int cols,
+                               CUtensorMapDataType dt) {
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+    cuuint32_t box[2] = {32, 32};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = g_encode_tiled(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? OM_OK : OM_ERR_DRIVER;
+}
+
+template <int BN, int MODE, int DT, int OCC>
+static int launch(DeviceCtx* c, const CUtensorMap& ta, const CUtensorMap& tb,
+                  const CUtensorMap& to, const CUtensorMap& tr, const Params& p) {
+    using Cf = Cfg<BN, OCC>;
+    auto kern = conv_tc_kernel<BN, MODE, DT, OCC>;
     static bool attr_set[64] = {false};
     if (!attr_set[c->device]) {
         OMB_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -520,31 +744,68 @@ static int launch(DeviceCtx* c, const CUtensorMap& ta, const CUtensorMap& tb, co
         attr_set[c->device] = true;
     }
     const int tiles = p.num_m_tiles * p.num_n_tiles;
-    const int grid = tiles < c->num_sms ? tiles : c->num_sms;
-    kern<<<grid, NUM_THREADS, Cf::SMEM_BYTES, c->compute>>>(ta, tb, p);
+    const int slots = OCC * c->num_sms;
+    const int grid = tiles < slots ? tiles : slots;
+    const int threads = MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GATHER_WARPS : NUM_THREADS;
+    kern<<<grid, threads, Cf::SMEM_BYTES, c->compute>>>(ta, tb, to, tr, p);
     return after_launch(c);
 }
 
 template <int MODE, int DT>
-static int dispatch_bn(DeviceCtx* c, int bn, const CUtensorMap& ta, const CUtensorMap& tb,
-                       const Params& p) {
+static int dispatch_bn(DeviceCtx* c, int bn, int occ, const CUtensorMap& ta, const CUtensorMap& tb,
+                       const CUtensorMap& to, const CUtensorMap& tr, const Params& p) {
+    if constexpr (MODE != MODE_STEM) {  // the stem's 14 warps run one CTA per SM
+        if (occ == 2) {
+            switch (bn) {
+                case 32: return launch<32, MODE, DT, 2>(c, ta, tb, to, tr, p);
+                case 64: return launch<64, MODE, DT, 2>(c, ta, tb, to, tr, p);
+                case 128: return launch<128, MODE, DT, 2>(c, ta, tb, to, tr, p);
+            }
+            return OM_ERR_UNSUPPORTED;
+        }
+    }
     switch (bn) {
-        case 32: return launch<32, MODE, DT>(c, ta, tb, p);
-        case 64: return launch<64, MODE, DT>(c, ta, tb, p);
-        case 128: return launch<128, MODE, DT>(c, ta, tb, p);
-        case 256: return launch<256, MODE, DT>(c, ta, tb, p);
+        case 32: return launch<32, MODE, DT, 1>(c, ta, tb, to, tr, p);
+        case 64: return launch<64, MODE, DT, 1>(c, ta, tb, to, tr, p);
+        case 128: return launch<128, MODE, DT, 1>(c, ta, tb, to, tr, p);
+        case 256: return launch<256, MODE, DT, 1>(c, ta, tb, to, tr, p);
     }
     return OM_ERR_UNSUPPORTED;
 }
 
-static int choose_bn(int K, long long m_tiles, int num_sms) {
-    if (K <= 32) return 32;
-    if (K <= 64) return 64;
-    if (K <= 128) return 128;
-    // Prefer 256-wide tiles (half the A re-reads) unless that leaves SMs idle.
-    long long tiles256 = m_tiles * ((K + 255) / 256);
-    if (tiles256 >= 2LL * num_sms) return 256;
-    return 128;
+// Tile width and CTAs per SM. Short reductions (K <= 512, i.e. 1x1 convs up to 512 input
+// channels) are memory-bound: they take 128-wide tiles at two CTAs per SM. Longer ones prefer
+// 256-wide tiles (half the A re-reads) unless that leaves SMs idle.
+static void choose_tile(int K, int num_kb, long long m_tiles, int num_sms, int* bn, int* occ) {
+    *occ = 1;
+    if (K <= 32) *bn = 32;
+    else if (K <= 64) *bn = 64;
+    else if (K <= 128) *bn = 128;
+    else *bn = (m_tiles * ((K + 255) / 256) >= 2LL * num_sms) ? 256 : 128;
+    if (num_kb <= 8) {
+        if (*bn == 256) *bn = 128;
+        long long tiles = m_tiles * ((K + *bn - 1) / *bn);
+        if (tiles >= 2LL * num_sms) *occ = 2;
+    }
+}
+
+// Encodes the output and residual maps (16-bit outputs) and launches the kernel.
+template <int MODE>
+static int finish_and_launch(DeviceCtx* c, int bn, int occ, int nDtype, const CUtensorMap& ta,
+                             const CUtensorMap& tb, const Params& p) {
+    const CUtensorMapDataType dt =
+        nDtype == OM_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    CUtensorMap to = tb, tr = tb;  // unused slots carry a valid map
+    if (!p.out_f32) {
+        int st = encode_epilogue_map(&to, p.out, p.M, p.K, dt);
+        if (st != OM_OK) return st;
+        if (p.residual) {
+            st = encode_epilogue_map(&tr, p.residual, p.M, p.K, dt);
+            if (st != OM_OK) return st;
+        }
+    }
+    if (nDtype == OM_DTYPE_BF16) return dispatch_bn<MODE, OM_DTYPE_BF16>(c, bn, occ, ta, tb, to, tr, p);
+    return dispatch_bn<MODE, OM_DTYPE_F16>(c, bn, occ, ta, tb, to, tr, p);
 }
 
 }  // namespace tc
@@ -602,8 +863,11 @@ extern "C" int omCudaConv2dBnAct(const void* pInput, const void* pPacked, const 
     p.P = P; p.Q = Q; p.M = (int)Mll;
     p.num_kb = (int)(kpad / BK);
     p.num_m_tiles = (int)((Mll + BM - 1) / BM);
-    const int bn = choose_bn(nCout, p.num_m_tiles, c->num_sms);
+    int bn, occ;
+    choose_tile(nCout, p.num_kb, p.num_m_tiles, c->num_sms, &bn, &occ);
     p.num_n_tiles = (nCout + bn - 1) / bn;
+    p.x = nullptr;
+    p.C = nCs;
     p.bias = pBias;
     p.residual = pResidual;
     p.out = pOutput;
@@ -644,10 +908,68 @@ extern "C" int omCudaConv2dBnAct(const void* pInput, const void* pPacked, const 
                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return OM_ERR_DRIVER;
 
-    if (nDtype == OM_DTYPE_BF16) {
-        return mode == MODE_SW128 ? dispatch_bn<MODE_SW128, OM_DTYPE_BF16>(c, bn, ta, tb, p)
-                                  : dispatch_bn<MODE_INTERLEAVE, OM_DTYPE_BF16>(c, bn, ta, tb, p);
-    }
-    return mode == MODE_SW128 ? dispatch_bn<MODE_SW128, OM_DTYPE_F16>(c, bn, ta, tb, p)
-                              : dispatch_bn<MODE_INTERLEAVE, OM_DTYPE_F16>(c, bn, ta, tb, p);
+    return mode == MODE_SW128 ? finish_and_launch<MODE_SW128>(c, bn, occ, nDtype, ta, tb, p)
+                              : finish_and_launch<MODE_INTERLEAVE>(c, bn, occ, nDtype, ta, tb, p);
+}
+
+// ---------------------------------------------------------------- image stem
+// K layout of the stem's packed weight: kk = (r * Cin + c) * 8 + s, s < KW (taps padded to 8).
+extern "C" long long omCudaPackedStemWeightElems(int nCout, int nCin, int nKH) {
+    long long kk = (long long)nKH * nCin * 8;
+    return (long long)nCout * ((kk + tc::BK - 1) / tc::BK * tc::BK);
+}
+
+extern "C" int omCudaStemConvBnAct(const float* pInput, const void* pPacked, const float* pBias,
+                                   void* pOutput, int nBatch, int nCin, int nH, int nW, int nCout,
+                                   int nKH, int nKW, int nStride, int nPad, int nAct, int nDtype) {
+    OMB_CTX_OR_FAIL(c);
+    using namespace omb::tc;
+    if (!pInput || !pPacked || !pOutput) return OM_ERR_INVALID;
+    if (nBatch <= 0 || nCin <= 0 || nH <= 0 || nW <= 0 || nCout <= 0 || nKH <= 0 || nKW <= 0 ||
+        nStride <= 0 || nPad < 0)
+        return OM_ERR_INVALID;
+    if (nKW > 8 || nCout % 8 != 0) return OM_ERR_UNSUPPORTED;
+    if (nDtype != OM_DTYPE_BF16 && nDtype != OM_DTYPE_F16) return OM_ERR_UNSUPPORTED;
+    if ((reinterpret_cast<uintptr_t>(pPacked) | reinterpret_cast<uintptr_t>(pOutput) |
+         reinterpret_cast<uintptr_t>(pBias)) & 15)
+        return OM_ERR_INVALID;
+    const int P = (nH + 2 * nPad - nKH) / nStride + 1;
+    const int Q = (nW + 2 * nPad - nKW) / nStride + 1;
+    if (P <= 0 || Q <= 0) return OM_ERR_INVALID;
+    const long long Mll = (long long)nBatch * P * Q;
+    if (Mll >= (1LL << 31)) return OM_ERR_UNSUPPORTED;
+    if (!load_driver_entry_points()) return OM_ERR_DRIVER;
+    const long long kpad = omCudaPackedStemWeightElems(1, nCin, nKH);
+
+    Params p;
+    p.N = nBatch; p.H = nH; p.W = nW; p.Cs = nCin; p.K = nCout;
+    p.R = nKH; p.S = nKW; p.stride = nStride; p.pad = nPad;
+    p.P = P; p.Q = Q; p.M = (int)Mll;
+    p.num_kb = (int)(kpad / BK);
+    p.num_m_tiles = (int)((Mll + BM - 1) / BM);
+    int bn, occ;
+    choose_tile(nCout, 1 << 20, p.num_m_tiles, c->num_sms, &bn, &occ);  // one CTA per SM
+    p.num_n_tiles = (nCout + bn - 1) / bn;
+    p.x = pInput;
+    p.C = nCin;
+    p.bias = pBias;
+    p.residual = nullptr;
+    p.out = pOutput;
+    p.act = nAct;
+    p.out_f32 = 0;
+    p.err = c->err_word;
+
+    const CUtensorMapDataType dt =
+        nDtype == OM_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    CUtensorMap tb;
+    cuuint64_t b_dims[2] = {(cuuint64_t)kpad, (cuuint64_t)nCout};
+    cuuint64_t b_strides[1] = {(cuuint64_t)kpad * 2};
+    cuuint32_t b_estr[2] = {1, 1};
+    cuuint32_t b_box[2] = {64u, (cuuint32_t)bn};
+    CUresult r = g_encode_tiled(&tb, dt, 2, const_cast<void*>(pPacked), b_dims, b_strides, b_box,
+                                b_estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return OM_ERR_DRIVER;
+    // the A operand is gathered by threads; the unused A map slot carries the B map
+    return finish_and_launch<MODE_STEM>(c, bn, occ, nDtype, tb, tb, p);
 }

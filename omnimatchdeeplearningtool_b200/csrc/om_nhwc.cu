@@ -35,6 +35,26 @@ __global__ void pack_conv_weight_kernel(const float* __restrict__ w, const float
     }
 }
 
+// Stem packing: w [K, C, R, S] -> [K, Kpad] with kk = (r*C + c)*8 + s (s < S <= 8), the
+// layout the stem's gather warps build A in (8 horizontal taps of one plane row per chunk).
+template <typename T>
+__global__ void pack_stem_weight_kernel(const float* __restrict__ w, const float* __restrict__ scale,
+                                        T* __restrict__ out, int K, int C, int R, int S,
+                                        long long kpad) {
+    long long total = (long long)K * kpad;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        int k = (int)(i / kpad);
+        long long kk = i - (long long)k * kpad;
+        int chunk = (int)(kk / 8), s = (int)(kk % 8);
+        int r = chunk / C, c = chunk - r * C;
+        float v = 0.f;
+        if (r < R && s < S) v = w[(((long long)k * C + c) * R + r) * S + s] * scale[k];
+        if constexpr (std::is_same<T, __nv_bfloat16>::value) out[i] = __float2bfloat16_rn(v);
+        else out[i] = __float2half_rn(v);
+    }
+}
+
 // scale[k] = gamma/sqrt(var+eps); bias[k] = beta + (b - mean)*scale (BN absent -> identity)
 __global__ void fold_bn_kernel(const float* conv_bias, const float* gamma, const float* beta,
                                const float* mean, const float* var, float eps, float* scale,
@@ -52,21 +72,30 @@ __global__ void fold_bn_kernel(const float* conv_bias, const float* gamma, const
 }
 
 // ---------------------------------------------------------------- layout conversion
+// One thread per pixel: the C plane reads are coalesced along w across the warp and the
+// pixel's Cs stored channels (zero-padded) go out as 16-byte vectors.
 template <int DT>
 __global__ void nchw_to_nhwc_kernel(const float* __restrict__ in, typename Half16<DT>::T* __restrict__ out,
                                     int N, int C, int H, int W, int Cs) {
-    // one thread per (n, h, w, c) output element; consecutive threads walk c
-    long long total = (long long)N * H * W * Cs;
-    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
-         i += (long long)gridDim.x * blockDim.x) {
-        int c = (int)(i % Cs);
-        long long pix = i / Cs;
-        int w = (int)(pix % W);
-        long long t = pix / W;
-        int h = (int)(t % H);
-        int n = (int)(t / H);
-        float v = c < C ? in[(((long long)n * C + c) * H + h) * W + w] : 0.f;
-        out[i] = Half16<DT>::from_f(v);
+    using H16 = Half16<DT>;
+    const long long pixels = (long long)N * H * W;
+    const long long plane = (long long)H * W;
+    for (long long pix = blockIdx.x * (long long)blockDim.x + threadIdx.x; pix < pixels;
+         pix += (long long)gridDim.x * blockDim.x) {
+        const long long n = pix / plane;
+        const long long hw = pix - n * plane;
+        const float* src = in + n * C * plane + hw;
+        uint4* dst = reinterpret_cast<uint4*>(out + pix * Cs);
+        for (int c8 = 0; c8 < Cs; c8 += 8) {
+            float v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = (c8 + j < C) ? __ldg(src + (long long)(c8 + j) * plane) : 0.f;
+            uint4 o;
+            typename H16::T2* o2 = reinterpret_cast<typename H16::T2*>(&o);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) o2[j] = H16::pack(v[2 * j], v[2 * j + 1]);
+            dst[c8 / 8] = o;
+        }
     }
 }
 
@@ -293,8 +322,10 @@ extern "C" int omCudaPackConvWeight(const float* pWeight, const float* pConvBias
 extern "C" int omCudaNchwToNhwc(const float* pIn, void* pOut, int nN, int nC, int nH, int nW,
                                 int nCs, int nDtype) {
     OMB_CTX_OR_FAIL(c);
-    if (!pIn || !pOut || nCs < nC || nN <= 0 || nC <= 0 || nH <= 0 || nW <= 0) return OM_ERR_INVALID;
-    long long total = (long long)nN * nH * nW * nCs;
+    if (!pIn || !pOut || nCs < nC || nCs % 8 || nN <= 0 || nC <= 0 || nH <= 0 || nW <= 0 ||
+        !aligned16(pOut))
+        return OM_ERR_INVALID;
+    long long total = (long long)nN * nH * nW;
     int grid = ew_grid(c, total, 256);
     if (nDtype == OM_DTYPE_BF16)
         nchw_to_nhwc_kernel<OM_DTYPE_BF16><<<grid, 256, 0, c->compute>>>(
@@ -423,4 +454,32 @@ extern "C" int omCudaAddActNhwc(const void* pA, const void* pB, void* pOut, long
     else
         return OM_ERR_UNSUPPORTED;
     return after_launch(c);
+}
+
+extern "C" int omCudaPackStemWeight(const float* pWeight, const float* pConvBias,
+                                    const float* pGamma, const float* pBeta, const float* pMean,
+                                    const float* pVar, float fEps, void* pPacked, float* pBiasOut,
+                                    int nCout, int nCin, int nKH, int nKW, int nDtype) {
+    OMB_CTX_OR_FAIL(c);
+    if (!pWeight || !pPacked || !pBiasOut || nCout <= 0 || nCin <= 0 || nKW > 8) return OM_ERR_INVALID;
+    if (nDtype != OM_DTYPE_BF16 && nDtype != OM_DTYPE_F16) return OM_ERR_UNSUPPORTED;
+    long long kpad = omCudaPackedStemWeightElems(1, nCin, nKH);
+    float* scale = nullptr;
+    OMB_CHECK(cudaMallocAsync(&scale, sizeof(float) * nCout, c->compute));
+    fold_bn_kernel<<<(nCout + 255) / 256, 256, 0, c->compute>>>(pConvBias, pGamma, pBeta, pMean,
+                                                                 pVar, fEps, scale, pBiasOut, nCout);
+    int st = after_launch(c);
+    if (st == OM_OK) {
+        long long total = (long long)nCout * kpad;
+        int grid = ew_grid(c, total, 256);
+        if (nDtype == OM_DTYPE_BF16)
+            pack_stem_weight_kernel<__nv_bfloat16><<<grid, 256, 0, c->compute>>>(
+                pWeight, scale, static_cast<__nv_bfloat16*>(pPacked), nCout, nCin, nKH, nKW, kpad);
+        else
+            pack_stem_weight_kernel<__half><<<grid, 256, 0, c->compute>>>(
+                pWeight, scale, static_cast<__half*>(pPacked), nCout, nCin, nKH, nKW, kpad);
+        st = after_launch(c);
+    }
+    cudaFreeAsync(scale, c->compute);
+    return st;
 }

@@ -57,18 +57,14 @@ class InferencePlan:
         self.meta: List[dict] = []         # one descriptor per op (kind, buffers, shape)
         # input staging: NCHW fp32 as the engine hands it over
         self.in_f32 = self._buf(batch * 3 * h * w * 4)
-        cs = stored_channels(3)
-        x = self._buf(batch * h * w * cs * 2)
-        # every recorded op binds its arguments as defaults: names such as `cs` are reused
-        # further down this constructor and a late-binding closure would see the last value
-        src32 = self.in_f32
-        self._op(lambda src32=src32, x=x, cs=cs: call(
-            "omCudaNchwToNhwc", src32.ptr, x.ptr, batch, 3, h, w, cs, dtype),
-            dict(kind="to_nhwc", out=x, c=3, cs=cs, h=h, w=w))
-        cur, hh, ww, c = x, h, w, 3
+        # the image stem reads the NCHW fp32 input directly (tcgen05 kernel, gathered A tile)
+        cur, hh, ww, c = self.in_f32, h, w, 3
         act0 = _ACT[net.stem_act]
-        for cv in net.stem:
-            cur, hh, ww, c = self._conv(cv, weights, cur, hh, ww, c, act0)
+        for i, cv in enumerate(net.stem):
+            if i == 0 and cv.k <= 8 and cv.groups == 1:
+                cur, hh, ww, c = self._stem(cv, weights, hh, ww, act0)
+            else:
+                cur, hh, ww, c = self._conv(cv, weights, cur, hh, ww, c, act0)
         if net.maxpool:
             p, q = (hh + 2 - 3) // 2 + 1, (ww + 2 - 3) // 2 + 1
             cs = stored_channels(c)
@@ -161,6 +157,31 @@ class InferencePlan:
         self.tc_op_index.append(len(self.ops) - 1)
         self.conv_flops += 2 * n * p * q * cout * cin * k * k
         return out, p, q, cout
+
+    def _stem(self, cv: ConvSpec, weights, hh, ww, act):
+        """First conv on the NCHW fp32 image with its BN folded (omCudaStemConvBnAct)."""
+        n, dt = self.batch, self.dtype
+        wbuf = self._upload(weights[cv.name + ".weight"])
+        g, b_, m, v = (self._upload(a) for a in self._bn_params(weights, cv.bn))
+        packed = self._buf(int(lib.omCudaPackedStemWeightElems(cv.cout, cv.cin, cv.k)) * 2)
+        bias = self._buf(cv.cout * 4)
+        call("omCudaPackStemWeight", wbuf.ptr, None, g.ptr, b_.ptr, m.ptr, v.ptr, 1e-5, packed.ptr,
+             bias.ptr, cv.cout, cv.cin, cv.k, cv.k, dt)
+        p = (hh + 2 * cv.pad - cv.k) // cv.stride + 1
+        q = (ww + 2 * cv.pad - cv.k) // cv.stride + 1
+        out = self._buf(n * p * q * cv.cout * 2)
+        x = self.in_f32
+        self._need(x, n * cv.cin * hh * ww * 4)
+        self._op(lambda x=x, out=out: call(
+            "omCudaStemConvBnAct", x.ptr, packed.ptr, bias.ptr, out.ptr, n, cv.cin, hh, ww,
+            cv.cout, cv.k, cv.k, cv.stride, cv.pad, act, dt),
+            dict(kind="stem", inp=x, out=out, w=weights[cv.name + ".weight"],
+                 bn=self._bn_params(weights, cv.bn), c=cv.cin, k=cv.cout, ks=cv.k,
+                 stride=cv.stride, pad=cv.pad, act=act, h=hh, wd=ww, p=p, q=q))
+        self.n_tc_launches += 1
+        self.tc_op_index.append(len(self.ops) - 1)
+        self.conv_flops += 2 * n * p * q * cv.cout * cv.cin * cv.k * cv.k
+        return out, p, q, cv.cout
 
     def _bn_params(self, weights, bn: str):
         return (weights[bn + ".gamma"], weights[bn + ".beta"], weights[bn + ".running_mean"],

@@ -127,3 +127,43 @@ def test_conv_rejects_bad_shapes(gpu):
     assert lib.omCudaConv2dBnAct(16, 16, None, None, 16, 1, 8, 8, 64, 60, 3, 3, 1, 1, 0, 1, 1) == -3
     # misaligned pointers are rejected
     assert lib.omCudaConv2dBnAct(18, 16, None, None, 16, 1, 8, 8, 64, 64, 3, 3, 1, 1, 0, 1, 1) == -2
+
+
+@pytest.mark.parametrize("n,h,k,ks,stride,pad,dt", [(2, 224, 64, 7, 2, 3, "bf16"),
+                                                    (3, 37, 64, 7, 2, 3, "bf16"),
+                                                    (2, 31, 32, 3, 2, 1, "f16")])
+def test_stem_conv_from_nchw_image(gpu, n, h, k, ks, stride, pad, dt):
+    """omCudaStemConvBnAct: the image stem straight from NCHW fp32 (ImageNet 7x7/2 and the
+    MobileNet 3x3/2 stem), checked like the other fused convs."""
+    import oracle as orc
+    from omnimatchdeeplearningtool_b200 import _lib
+    from omnimatchdeeplearningtool_b200._lib import call, lib
+    from omnimatchdeeplearningtool_b200.backend import DeviceBuffer
+    rng = np.random.Generator(np.random.PCG64(77 + h))
+    c = 3
+    x = rng.standard_normal((n, c, h, h), dtype=np.float32)
+    w = (rng.standard_normal((k, c, ks, ks)) * np.sqrt(2.0 / (c * ks * ks))).astype(np.float32)
+    g = rng.uniform(0.5, 1.5, k).astype(np.float32)
+    b = (rng.standard_normal(k) * 0.1).astype(np.float32)
+    mu = (rng.standard_normal(k) * 0.1).astype(np.float32)
+    var = rng.uniform(0.5, 1.5, k).astype(np.float32)
+    dtype = _lib.DTYPE_BF16 if dt == "bf16" else _lib.DTYPE_F16
+    p = (h + 2 * pad - ks) // stride + 1
+    keep = [DeviceBuffer.from_numpy(a) for a in (x, w, g, b, mu, var)]
+    packed = DeviceBuffer(int(lib.omCudaPackedStemWeightElems(k, c, ks)) * 2)
+    bias = DeviceBuffer(k * 4)
+    call("omCudaPackStemWeight", keep[1].ptr, None, keep[2].ptr, keep[3].ptr, keep[4].ptr,
+         keep[5].ptr, 1e-5, packed.ptr, bias.ptr, k, c, ks, ks, dtype)
+    out = DeviceBuffer(n * p * p * k * 2)
+    call("omCudaStemConvBnAct", keep[0].ptr, packed.ptr, bias.ptr, out.ptr, n, c, h, h, k, ks, ks,
+         stride, pad, 1, dtype)
+    o32 = DeviceBuffer(n * k * p * p * 4)
+    call("omCudaNhwcToNchw", out.ptr, o32.ptr, n, k, p, p, k, dtype)
+    got = o32.to_numpy((n, k, p, p))
+    assert gpu.kernel_error() == 0
+    want = orc.relu(orc.batchnorm_eval(orc.conv2d(x, w, None, stride, pad), g, b, mu, var))
+    scale = g / np.sqrt(var + 1e-5)
+    y16 = orc.relu(orc.conv2d(_round16(x, dt), _round16(w * scale[:, None, None, None], dt),
+                              b - mu * scale, stride, pad))
+    assert rel_err(got, y16) <= 1e-2
+    assert rel_err(got, want) <= 2e-2
