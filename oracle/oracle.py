@@ -135,7 +135,8 @@ def batchnorm_eval(x, gamma, beta, mean, var, eps=1e-5):
     out = np.empty_like(x)
     rm, rv = f32(mean).copy(), f32(var).copy()
     sm, si = np.empty(c, np.float32), np.empty(c, np.float32)
-    O.oracle_batchnorm2d(_p(x), _p(out), _p(f32(gamma)), _p(f32(beta)), _p(rm), _p(rv), _p(sm),
+    gamma, beta = f32(gamma), f32(beta)
+    O.oracle_batchnorm2d(_p(x), _p(out), _p(gamma), _p(beta), _p(rm), _p(rv), _p(sm),
                          _p(si), n, c, h, w, eps, 0.1, 0)
     return out
 
@@ -177,7 +178,8 @@ def linear(x, w, b):
     out = np.empty((x.shape[0], w.shape[1]), np.float32)
     O.oracle_matmul(_p(x), _p(w), _p(out), x.shape[0], x.shape[1], w.shape[1])
     res = np.empty_like(out)
-    O.oracle_add_bias(_p(out), _p(f32(b).reshape(-1)), _p(res), out.shape[0], out.shape[1])
+    bb = f32(b).reshape(-1)
+    O.oracle_add_bias(_p(out), _p(bb), _p(res), out.shape[0], out.shape[1])
     return res
 
 
@@ -208,7 +210,8 @@ def forward(net, weights, x):
             for i, cv in enumerate(blk.convs):
                 out = _conv_bn(weights, cv, out, "none" if i == len(blk.convs) - 1 else "relu")
             s = np.empty_like(out)
-            O.oracle_add(_p(out), _p(f32(sc)), _p(s), out.size)
+            sc = f32(sc)
+            O.oracle_add(_p(out), _p(sc), _p(s), out.size)
             y = relu(s)
         else:
             e, d, pj = blk.convs
@@ -235,10 +238,12 @@ def ref_model(kind, classes, weights, net):
     shp = (c_int * 4)()
     for i in range(L.omref_model_num_params(h)):
         L.omref_model_param_info(h, i, buf, 256, shp)
-        L.omref_model_set_param(h, i, _p(f32(weights[buf.value.decode()])))
+        arr = f32(weights[buf.value.decode()])
+        L.omref_model_set_param(h, i, _p(arr))
     for i in range(L.omref_model_num_buffers(h)):
         L.omref_model_buffer_info(h, i, buf, 256, shp)
-        L.omref_model_set_buffer(h, i, _p(f32(weights[buf.value.decode()])))
+        arr = f32(weights[buf.value.decode()])
+        L.omref_model_set_buffer(h, i, _p(arr))
     return h
 
 
@@ -254,3 +259,154 @@ def ref_names(h):
         r = L.omref_model_buffer_info(h, i, buf, 256, shp)
         bs.append((buf.value.decode(), tuple(shp[j] for j in range(r))))
     return ps, bs
+
+
+# ------------------------------------------------------------------ training step (config 3)
+def _bn_train(x, gamma, beta, rm, rv, eps=1e-5, mom=0.1):
+    """Train-mode BN (cpu_backend.ixx:781-842); updates rm/rv in place, returns y, mean, invstd."""
+    x = f32(x)
+    n, c, h, w = x.shape
+    y = np.empty_like(x)
+    sm, si = np.empty(c, np.float32), np.empty(c, np.float32)
+    gamma, beta = f32(gamma), f32(beta)
+    O.oracle_batchnorm2d(_p(x), _p(y), _p(gamma), _p(beta), _p(rm), _p(rv), _p(sm),
+                         _p(si), n, c, h, w, eps, mom, 1)
+    return y, sm, si
+
+
+def _conv_bwd(x, w, dy, stride, pad):
+    x, w, dy = f32(x), f32(w), f32(dy)
+    n, c, h, wd = x.shape
+    k, _, r, s = w.shape
+    dx = np.empty_like(x)
+    dw = np.empty_like(w)
+    O.oracle_conv2d_backward_input(_p(dy), _p(w), _p(dx), n, c, h, wd, k, r, s, stride, pad)
+    O.oracle_conv2d_backward_weight(_p(x), _p(dy), _p(dw), None, n, c, h, wd, k, r, s, stride, pad)
+    return dx, dw
+
+
+def _bn_bwd(dy, x, mean, invstd, gamma):
+    dy, x = f32(dy), f32(x)
+    n, c, h, w = x.shape
+    dx = np.empty_like(x)
+    dg, db = np.empty(c, np.float32), np.empty(c, np.float32)
+    gamma = f32(gamma)
+    O.oracle_batchnorm2d_backward(_p(dy), _p(x), _p(mean), _p(invstd), _p(gamma), _p(dx),
+                                  _p(dg), _p(db), n, c, h, w)
+    return dx, dg, db
+
+
+def _relu_bwd(x, dy):
+    x, dy = f32(x), f32(dy)
+    dx = np.empty_like(x)
+    O.oracle_relu_backward(_p(x), _p(dy), _p(dx), x.size)
+    return dx
+
+
+def train_step(net, weights, x, onehot, lr=0.01, momentum=0.9, velocities=None):
+    """One reference training step on a BasicBlock/Bottleneck ResNet in NCHW fp32: train-mode
+    forward, softmax cross-entropy on one-hot targets (loss.ixx:33-55, tensor_ops.ixx:583-643),
+    backward in the reference autograd's formulas (autograd.ixx: Conv2dBackward :492-662,
+    BatchNorm2dBackward :722-782, MaxPool2dBackward :900-952, ReLUBackward :368,
+    AdaptiveAvgPool2dBackwardFn :1397, MatMulBackward :226, AddBiasBackward :399) and, when
+    `velocities` is given, SGD with momentum (optimizer.ixx:103-120).
+    Updates BN running statistics in `weights`. Returns (loss, grads)."""
+    grads = {}
+    rs = {k: f32(v).copy() for k, v in weights.items() if k.endswith("running_mean") or k.endswith("running_var")}
+    tape = []
+
+    def conv_bn(cv, inp, act):
+        z = conv2d(inp, weights[cv.name + ".weight"], None, cv.stride, cv.pad)
+        y, mu, si = _bn_train(z, weights[cv.bn + ".gamma"], weights[cv.bn + ".beta"],
+                              rs[cv.bn + ".running_mean"], rs[cv.bn + ".running_var"])
+        out = relu(y) if act else y
+        tape.append(("conv_bn", cv, inp, z, mu, si, y, act))
+        return out
+
+    h = f32(x)
+    for cv in net.stem:
+        h = conv_bn(cv, h, True)
+    pool_in = h
+    n, c, hh, ww = h.shape
+    P = (hh + 2 - 3) // 2 + 1
+    pooled = np.empty((n, c, P, P), np.float32)
+    idx = np.empty((n, c, P, P), np.int32)
+    O.oracle_maxpool2d(_p(pool_in), _p(pooled), _p(idx), n, c, hh, ww, 3, 2, 1)
+    h = pooled
+    block_caches = []
+    for blk in net.blocks:
+        start = len(tape)
+        inp = h
+        sc = inp
+        if blk.downsample is not None:
+            sc = conv_bn(blk.downsample, inp, False)
+        out = inp
+        for i, cv in enumerate(blk.convs):
+            out = conv_bn(cv, out, i < len(blk.convs) - 1)
+        s = out + sc
+        h = relu(s)
+        block_caches.append((blk, start, len(tape), inp, s))
+    feat_in = h
+    n, c, hh, ww = h.shape
+    feat = global_avgpool(h).reshape(n, c)
+    logits = linear(feat, weights["fc.weight"], weights["fc.bias"])
+    p = np.empty_like(logits)
+    O.oracle_softmax(_p(logits), _p(p), n, logits.shape[1])
+    onehot = f32(onehot)
+    loss = O.oracle_cross_entropy(_p(p), _p(onehot), n, logits.shape[1])
+    dlogits = np.empty_like(logits)
+    O.oracle_ce_softmax_backward(_p(p), _p(onehot), _p(dlogits), n, logits.shape[1])
+
+    # FC: logits = feat @ W + b
+    W = f32(weights["fc.weight"])
+    dW = np.empty_like(W)
+    featT = np.ascontiguousarray(feat.T)   # bound to a name: the C call must see live memory
+    O.oracle_matmul(_p(featT), _p(dlogits), _p(dW), W.shape[0], n, W.shape[1])
+    db = np.empty(W.shape[1], np.float32)
+    O.oracle_add_bias_backward(_p(dlogits), _p(db), n, W.shape[1])
+    grads["fc.weight"], grads["fc.bias"] = dW, db.reshape(1, -1)
+    dfeat = np.empty((n, W.shape[0]), np.float32)
+    WT = np.ascontiguousarray(W.T)
+    O.oracle_matmul(_p(dlogits), _p(WT), _p(dfeat), n, W.shape[1], W.shape[0])
+    dh = np.empty_like(feat_in)
+    dfeat4 = dfeat.reshape(n, c, 1, 1)
+    O.oracle_adaptive_avgpool2d_backward(_p(dfeat4), _p(dh), n, c, hh, ww, 1, 1)
+
+    def conv_bn_bwd(entry, dout):
+        _, cv, inp, z, mu, si, y, act = entry
+        if act:
+            dout = _relu_bwd(y, dout)
+        dz, dg, dbeta = _bn_bwd(dout, z, mu, si, weights[cv.bn + ".gamma"])
+        grads[cv.bn + ".gamma"], grads[cv.bn + ".beta"] = dg, dbeta
+        dx, dw = _conv_bwd(inp, weights[cv.name + ".weight"], dz, cv.stride, cv.pad)
+        grads[cv.name + ".weight"] = dw
+        return dx
+
+    for blk, start, end, inp, s in reversed(block_caches):
+        ds = _relu_bwd(s, dh)
+        entries = tape[start:end]
+        main = [e for e in entries if blk.downsample is None or e[1] is not blk.downsample]
+        d = ds
+        for e in reversed(main):
+            d = conv_bn_bwd(e, d)
+        if blk.downsample is not None:
+            dsc = conv_bn_bwd([e for e in entries if e[1] is blk.downsample][0], ds)
+        else:
+            dsc = ds
+        dh = d + dsc
+    dpool_in = np.empty_like(pool_in)
+    n, c, hh, ww = pool_in.shape
+    O.oracle_maxpool2d_backward(_p(dh), _p(idx), _p(dpool_in), n, c, P, P, hh, ww)
+    d = dpool_in
+    for e in reversed(tape[:len(net.stem)]):
+        d = conv_bn_bwd(e, d)
+    for k, v in rs.items():
+        weights[k] = v
+    if velocities is not None:
+        for name, _ in net.params:
+            g = f32(grads[name]).reshape(-1)
+            prm = f32(weights[name]).reshape(-1).copy()
+            vel = velocities.setdefault(name, np.zeros_like(prm))
+            O.oracle_sgd_step(_p(prm), _p(g), _p(vel), prm.size, lr, momentum)
+            weights[name] = prm.reshape(weights[name].shape)
+    return float(loss), grads
