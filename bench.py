@@ -54,14 +54,16 @@ def _dist():
         import datetime
 
         import torch.distributed as dist
-        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
+        dist.init_process_group("cpu:gloo,cuda:nccl", timeout=datetime.timedelta(seconds=300))
         return world, rank, local, dist
     return world, rank, local, None
 
 
 def _barrier(dist):
+    """Host-side barrier over gloo (a CPU-tensor all-reduce), independent of NCCL."""
     if dist is not None:
-        dist.barrier()
+        import torch
+        dist.all_reduce(torch.zeros(1))
 
 
 def _max_over_ranks(dist, v: float) -> float:
@@ -152,6 +154,112 @@ def _reference_cpu(batch: int, iters_min: int, seconds: float):
     sample = (f"ResNet-50 fp32 forward, batch {batch} at 224x224, {n} iterations "
               f"({dt:.1f} s), OMP threads={cores}")
     return n * batch / dt, kind, cores, sample
+
+
+def run_train(args, world, rank, local, dist):
+    """Config 3: ResNet-18 fp32 training step (forward with batch-statistics BN, softmax CE,
+    backward, NCCL all-reduce of the flat gradient, SGD momentum 0.9, lr 0.01), batch 128 per
+    GPU, weak scaling."""
+    import torch
+    from omnimatchdeeplearningtool_b200 import backend, synth
+    from omnimatchdeeplearningtool_b200._lib import call
+    from omnimatchdeeplearningtool_b200.backend import DeviceBuffer
+    from omnimatchdeeplearningtool_b200.distributed import DataParallel, DistributedConfig
+    from omnimatchdeeplearningtool_b200.plan import Fp32Net
+
+    backend.init(local)
+    torch.cuda.set_device(local)
+    stream = torch.cuda.ExternalStream(backend.stream_handle(), device=local)
+    batch = args.batch if args.batch != BATCH else 128
+    net = synth.resnet_spec(18, 1000)
+    weights = synth.make_weights(net)
+    n_params = sum(int(__import__("numpy").prod(s)) for _, s in net.params)
+    grad = torch.zeros(n_params, dtype=torch.float32, device=f"cuda:{local}")
+    fnet = Fp32Net(net, weights, batch, 224, 224, grad_ptr=grad.data_ptr())
+    dp = DataParallel(fnet, DistributedConfig(world, rank))
+    x = DeviceBuffer.from_numpy(synth.normal_input(batch, seed=rank))
+    y = DeviceBuffer.from_numpy(synth.onehot_labels(batch, 1000, seed=100 + rank))
+    loss = DeviceBuffer.zeros(4)
+
+    def one_step():
+        fnet.forward_backward(x.ptr, y.ptr, loss.ptr)
+        with torch.cuda.stream(stream):
+            dp.synchronize_gradients(grad)
+        dp.step(0.01, 0.9)
+
+    for _ in range(args.warmup):
+        one_step()
+    call("omCudaSynchronize")
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    _barrier(dist)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record()
+    for _ in range(args.steps):
+        one_step()
+    with torch.cuda.stream(stream):
+        e1.record()
+    e1.synchronize()
+    torch.cuda.synchronize()
+    _barrier(dist)
+    clk = clocks.stop()
+    t = _max_over_ranks(dist, e0.elapsed_time(e1) / 1e3)
+    lv = float(loss.to_numpy((1,))[0])
+    if rank == 0:
+        line = {
+            "metric": "ResNet-18 fp32 training images/s (config 3)", "value": args.steps * batch * world / t,
+            "unit": "images/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": t / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded N(0,1) inputs, uniform labels, He-normal weights)",
+            "config": {"workload": "resnet18 fp32 training step, SGD momentum 0.9 lr 0.01",
+                       "batch_per_gpu": batch, "global_batch": batch * world,
+                       "parallelism": f"dp{world}, NCCL all-reduce of gradients"},
+            "loss_last_step": lv, "clocks": clk, "kernel_error": backend.kernel_error(),
+        }
+        print(json.dumps(line), flush=True)
+    fnet.close()
+
+
+def run_mobilenet(args, world, rank, local, dist):
+    """Config 5: MobileNet-style stack fp16 inference, batch 256 per GPU."""
+    import torch
+    from omnimatchdeeplearningtool_b200 import _lib, backend, synth
+    from omnimatchdeeplearningtool_b200._lib import call
+    from omnimatchdeeplearningtool_b200.plan import InferencePlan
+    backend.init(local)
+    torch.cuda.set_device(local)
+    stream = torch.cuda.ExternalStream(backend.stream_handle(), device=local)
+    net = synth.mobilenet_spec()
+    plan = InferencePlan(net, synth.make_weights(net), batch=args.batch, dtype=_lib.DTYPE_F16)
+    plan.set_input(synth.normal_input(args.batch, seed=rank))
+    plan.launch()
+    call("omCudaSynchronize")
+    plan.capture()
+    for _ in range(args.warmup):
+        plan.launch()
+    call("omCudaSynchronize")
+    _barrier(dist)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record()
+        for _ in range(args.steps):
+            plan.launch()
+        e1.record()
+    e1.synchronize()
+    _barrier(dist)
+    t = _max_over_ranks(dist, e0.elapsed_time(e1) / 1e3)
+    if rank == 0:
+        print(json.dumps({
+            "metric": "MobileNet-style stack fp16 images/s (config 5)",
+            "value": args.steps * args.batch * world / t, "unit": "images/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": t / args.steps * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic", "config": {"workload": "mobilenet-style stack fp16 inference",
+                                            "batch_per_gpu": args.batch}}), flush=True)
+    plan.close()
 
 
 def run_reference(args, world, rank, dist):
@@ -339,6 +447,9 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="r50-infer",
+                    choices=["r50-infer", "r18-train", "mobilenet-infer"],
+                    help="r50-infer is the headline metric; the others are configs 3 and 5")
     ap.add_argument("--ref-batch", type=int, default=4)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=BATCH,
@@ -351,6 +462,10 @@ def main():
     try:
         if args.impl == "reference":
             run_reference(args, world, rank, dist)
+        elif args.workload == "r18-train":
+            run_train(args, world, rank, local, dist)
+        elif args.workload == "mobilenet-infer":
+            run_mobilenet(args, world, rank, local, dist)
         else:
             run_ours(args, world, rank, local, dist)
     finally:

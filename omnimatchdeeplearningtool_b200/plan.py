@@ -274,3 +274,227 @@ class InferencePlan:
         for b in self.keep:
             b.free()
         self.keep.clear()
+
+
+class Fp32Net:
+    """A ResNet (BasicBlock or Bottleneck) in the reference's own layout, NCHW fp32, run through
+    the reference-named C-ABI entry points exactly as the engine's tensor_ops / autograd call
+    them: train-mode forward (BatchNorm batch statistics, running-stat update), softmax
+    cross-entropy on one-hot targets, the backward pass of every node in the reference
+    autograd's formulas (autograd.ixx: Conv2dBackward :492-662, BatchNorm2dBackward :722-782,
+    MaxPool2dBackward :900-952, ReLUBackward :368, AdaptiveAvgPool2dBackwardFn :1397,
+    MatMulBackward :226, AddBiasBackward :399) and SGD with momentum (optimizer.ixx:71-130).
+
+    Gradients live in one flat fp32 buffer in parameter order, so a data-parallel step needs a
+    single all-reduce (``grad_flat`` / ``grad_bytes``) between :meth:`backward` and :meth:`step`.
+    """
+
+    def __init__(self, net: NetSpec, weights: Dict[str, np.ndarray], batch: int, h: int = 224,
+                 w: int = 224, grad_ptr: Optional[int] = None):
+        self.net, self.batch, self.h, self.w = net, batch, h, w
+        self.keep: List[DeviceBuffer] = []
+        self.param = {}
+        self.vel = {}
+        self.offsets = {}
+        off = 0
+        for name, shape in net.params:
+            n = int(np.prod(shape))
+            self.offsets[name] = (off, n, shape)
+            off += n
+        self.n_params = off
+        self.grad_bytes = off * 4
+        if grad_ptr is None:
+            self._grad_buf = DeviceBuffer.zeros(self.grad_bytes)
+            self.keep.append(self._grad_buf)
+            grad_ptr = self._grad_buf.ptr
+        self.grad_flat = grad_ptr
+        for name, shape in net.params:
+            self.param[name] = self._dev(weights[name])
+            self.vel[name] = self._zeros(int(np.prod(shape)) * 4)
+        self.buffers = {name: self._dev(weights[name]) for name, _ in net.buffers}
+        self.acts = {}
+
+    # ------------------------------------------------------------------ memory helpers
+    def _dev(self, a: np.ndarray) -> DeviceBuffer:
+        b = DeviceBuffer.from_numpy(np.ascontiguousarray(a, dtype=np.float32))
+        self.keep.append(b)
+        return b
+
+    def _zeros(self, nbytes: int) -> DeviceBuffer:
+        b = DeviceBuffer.zeros(nbytes)
+        self.keep.append(b)
+        return b
+
+    def _buf(self, key, nbytes: int) -> DeviceBuffer:
+        """Activation buffers are allocated once per shape role and reused every step."""
+        b = self.acts.get(key)
+        if b is None or b.nbytes < nbytes:
+            b = DeviceBuffer(nbytes)
+            self.keep.append(b)
+            self.acts[key] = b
+        return b
+
+    def grad(self, name: str) -> int:
+        off, _, _ = self.offsets[name]
+        return self.grad_flat + off * 4
+
+    # ------------------------------------------------------------------ forward pieces
+    def _conv_bn(self, key, cv: ConvSpec, x: DeviceBuffer, n, c, hh, ww, relu: bool):
+        p = (hh + 2 * cv.pad - cv.k) // cv.stride + 1
+        q = (ww + 2 * cv.pad - cv.k) // cv.stride + 1
+        cnt = n * cv.cout * p * q
+        z = self._buf(key + ".z", cnt * 4)
+        B.conv2d(x.ptr, self.param[cv.name + ".weight"].ptr, None, z.ptr, n, c, hh, ww, cv.cout,
+                 cv.k, cv.k, cv.pad, cv.pad, cv.stride, cv.stride)
+        y = self._buf(key + ".y", cnt * 4)
+        mean = self._buf(key + ".mean", cv.cout * 4)
+        invstd = self._buf(key + ".invstd", cv.cout * 4)
+        B.batchNorm2d(z.ptr, self.param[cv.bn + ".gamma"].ptr, self.param[cv.bn + ".beta"].ptr,
+                      y.ptr, self.buffers[cv.bn + ".running_mean"].ptr,
+                      self.buffers[cv.bn + ".running_var"].ptr, mean.ptr, invstd.ptr, n, cv.cout,
+                      p * q, 1e-5, 0.1, True)
+        out = y
+        if relu:
+            out = self._buf(key + ".a", cnt * 4)
+            B.relu(y.ptr, out.ptr, cnt)
+        rec = dict(cv=cv, x=x, z=z, y=y, mean=mean, invstd=invstd, relu=relu, n=n, c=c, h=hh,
+                   w=ww, p=p, q=q)
+        return out, p, q, rec
+
+    def forward_backward(self, x_ptr: int, onehot_ptr: int, loss_ptr: int) -> None:
+        """Train-mode forward from device NCHW fp32 input and one-hot targets, loss into
+        loss_ptr (device float), gradients into the flat gradient buffer (overwritten)."""
+        net, n = self.net, self.batch
+        recs = []
+        x = _Ptr(x_ptr)
+        cur, c, hh, ww = x, 3, self.h, self.w
+        for i, cv in enumerate(net.stem):
+            cur, hh, ww, rec = self._conv_bn(f"stem{i}", cv, cur, n, c, hh, ww, True)
+            c = cv.cout
+            recs.append(rec)
+        pool_in, pc, ph, pw = cur, c, hh, ww
+        P = (hh + 2 - 3) // 2 + 1
+        pooled = self._buf("pool.y", n * c * P * P * 4)
+        idx = self._buf("pool.idx", n * c * P * P * 4)
+        B.maxPool2d(cur.ptr, pooled.ptr, idx.ptr, n, c, hh, ww, 3, 3, 2, 1)
+        cur, hh, ww = pooled, P, P
+        blocks = []
+        for bi, blk in enumerate(net.blocks):
+            inp, ic, ih, iw = cur, c, hh, ww
+            sc, ds_rec = inp, None
+            if blk.downsample is not None:
+                sc, _, _, ds_rec = self._conv_bn(f"b{bi}.ds", blk.downsample, inp, n, ic, ih, iw, False)
+            main = []
+            out, oc, oh, ow = inp, ic, ih, iw
+            for j, cv in enumerate(blk.convs):
+                last = j == len(blk.convs) - 1
+                out, oh, ow, rec = self._conv_bn(f"b{bi}.c{j}", cv, out, n, oc, oh, ow, not last)
+                oc = cv.cout
+                main.append(rec)
+            cnt = n * oc * oh * ow
+            s = self._buf(f"b{bi}.sum", cnt * 4)
+            B.add(out.ptr, sc.ptr, s.ptr, cnt)
+            a = self._buf(f"b{bi}.out", cnt * 4)
+            B.relu(s.ptr, a.ptr, cnt)
+            blocks.append(dict(inp=inp, c=ic, h=ih, w=iw, main=main, ds=ds_rec, s=s, oc=oc, oh=oh,
+                               ow=ow))
+            cur, c, hh, ww = a, oc, oh, ow
+        feat = self._buf("feat", n * c * 4)
+        B.adaptiveAvgPool2d(cur.ptr, feat.ptr, n, c, hh, ww, 1, 1)
+        K = net.classes
+        logits = self._buf("logits", n * K * 4)
+        B.matmul(feat.ptr, self.param["fc.weight"].ptr, logits.ptr, n, c, K)
+        logits_b = self._buf("logits_b", n * K * 4)
+        B.addBias(logits.ptr, self.param["fc.bias"].ptr, logits_b.ptr, n, K, 1)
+        prob = self._buf("prob", n * K * 4)
+        B.softmax(logits_b.ptr, prob.ptr, n, K)
+        B.crossEntropyForward(prob.ptr, onehot_ptr, loss_ptr, n, K)
+        self.logits = logits_b
+
+        # ---------------------------------------------------------------- backward
+        dlog = self._buf("dlogits", n * K * 4)
+        B.crossEntropySoftmaxBackward(prob.ptr, onehot_ptr, dlog.ptr, n, K)
+        featT = self._buf("featT", n * c * 4)
+        B.transpose(feat.ptr, featT.ptr, n, c)
+        B.matmul(featT.ptr, dlog.ptr, self.grad("fc.weight"), c, n, K)
+        B.addBiasBackward(dlog.ptr, self.grad("fc.bias"), n, K, 1)
+        WT = self._buf("fcWT", c * K * 4)
+        B.transpose(self.param["fc.weight"].ptr, WT.ptr, c, K)
+        dfeat = self._buf("dfeat", n * c * 4)
+        B.matmul(dlog.ptr, WT.ptr, dfeat.ptr, n, K, c)
+        dcur = self._buf("dtop", n * c * hh * ww * 4)
+        B.adaptiveAvgPool2dBackward(dfeat.ptr, dcur.ptr, n, c, hh, ww, 1, 1)
+        for bi in reversed(range(len(blocks))):
+            blk = blocks[bi]
+            cnt = n * blk["oc"] * blk["oh"] * blk["ow"]
+            ds_ = self._buf(f"g{bi}.ds", cnt * 4)
+            B.reluBackward(blk["s"].ptr, dcur.ptr, ds_.ptr, cnt)
+            d = ds_
+            for j in reversed(range(len(blk["main"]))):
+                d = self._conv_bn_backward(f"g{bi}.m{j}", blk["main"][j], d)
+            if blk["ds"] is not None:
+                dsc = self._conv_bn_backward(f"g{bi}.d", blk["ds"], ds_)
+            else:
+                dsc = ds_
+            incnt = n * blk["c"] * blk["h"] * blk["w"]
+            dsum = self._buf(f"g{bi}.in", incnt * 4)
+            B.add(d.ptr, dsc.ptr, dsum.ptr, incnt)
+            dcur = dsum
+        dpool = self._buf("g.pool", n * pc * ph * pw * 4)
+        B.maxPool2dBackward(dcur.ptr, idx.ptr, dpool.ptr, n, pc, ph, pw, P, P)
+        d = dpool
+        for i in reversed(range(len(recs))):
+            d = self._conv_bn_backward(f"g.stem{i}", recs[i], d, need_dx=i > 0)
+
+    def _conv_bn_backward(self, key, rec, dout, need_dx: bool = True) -> Optional[DeviceBuffer]:
+        cv, n = rec["cv"], rec["n"]
+        cnt = n * cv.cout * rec["p"] * rec["q"]
+        if rec["relu"]:
+            dr = self._buf(key + ".dr", cnt * 4)
+            B.reluBackward(rec["y"].ptr, dout.ptr, dr.ptr, cnt)
+            dout = dr
+        dz = self._buf(key + ".dz", cnt * 4)
+        B.batchNorm2dBackward(dout.ptr, rec["z"].ptr, rec["mean"].ptr, rec["invstd"].ptr,
+                              self.param[cv.bn + ".gamma"].ptr, dz.ptr, self.grad(cv.bn + ".gamma"),
+                              self.grad(cv.bn + ".beta"), n, cv.cout, rec["p"], rec["q"])
+        dx = None
+        if need_dx:  # the image itself needs no gradient
+            dx = self._buf(key + ".dx", n * rec["c"] * rec["h"] * rec["w"] * 4)
+            B.conv2dBackwardInput(dz.ptr, self.param[cv.name + ".weight"].ptr, dx.ptr, n, rec["c"],
+                                  rec["h"], rec["w"], cv.cout, cv.k, cv.k, cv.pad, cv.pad, cv.stride,
+                                  cv.stride)
+        B.conv2dBackwardWeight(rec["x"].ptr, dz.ptr, self.grad(cv.name + ".weight"), None, n,
+                               rec["c"], rec["h"], rec["w"], cv.cout, cv.k, cv.k, cv.pad, cv.pad,
+                               cv.stride, cv.stride)
+        return dx
+
+    def step(self, lr: float = 0.01, momentum: float = 0.9, grad_scale: float = 1.0) -> None:
+        """SGD with momentum on every parameter; grad_scale (1/world after a summing
+        all-reduce) is applied to the flat gradient first."""
+        if grad_scale != 1.0:
+            B.mulScalar(self.grad_flat, grad_scale, self.grad_flat, self.n_params)
+        for name, _ in self.net.params:
+            off, cnt, _ = self.offsets[name]
+            B.sgdStep(self.param[name].ptr, self.grad_flat + off * 4, self.vel[name].ptr, cnt, lr,
+                      momentum)
+
+    def read_grads(self) -> Dict[str, np.ndarray]:
+        flat = np.empty(self.n_params, np.float32)
+        call("omCudaCopyD2H", flat.ctypes.data, self.grad_flat, self.grad_bytes)
+        return {name: flat[off:off + n].reshape(shape) for name, (off, n, shape) in self.offsets.items()}
+
+    def read_param(self, name: str) -> np.ndarray:
+        _, n, shape = self.offsets[name]
+        return self.param[name].to_numpy(shape)
+
+    def close(self) -> None:
+        for b in self.keep:
+            b.free()
+        self.keep.clear()
+
+
+class _Ptr:
+    """A borrowed device pointer with the DeviceBuffer interface the plan code uses."""
+
+    def __init__(self, ptr: int):
+        self.ptr = int(ptr)

@@ -146,6 +146,29 @@ def main():
     g["train_r18_grad_summary"] = np.array(summ, np.float64)
     L.omref_model_destroy(h)
 
+    # Config 3 at its parity size (ResNet-18, 1000 classes, batch 8 at 224x224): how far the
+    # reference's own fp32 gradients sit from the oracle's double-precision ones, per parameter
+    # as max|ref - oracle| / max|oracle|. The GPU training step is held to this spread.
+    net = synth.resnet_spec(18, 1000)
+    w = synth.make_weights(net)
+    h = orc.ref_model(0, 1000, w, net)
+    x = synth.normal_input(8, 3, 224, 224, seed=11)
+    y = synth.onehot_labels(8, 1000, seed=12)
+    tot = sum(int(np.prod(s)) for _, s in net.params)
+    gref = np.empty(tot, np.float32)
+    loss = L.omref_model_train_step(h, P(x), P(y), 8, 224, 224, 1000, 0.01, 0.9, 0, P(gref))
+    _, gor = orc.train_step(net, {k: v.copy() for k, v in w.items()}, x, y)
+    errs = []
+    off = 0
+    for name, shape in net.params:
+        m = int(np.prod(shape))
+        o = gor[name].reshape(-1)
+        errs.append(float(np.abs(gref[off:off + m] - o).max() / np.abs(o).max()))
+        off += m
+    g["train_r18_224_ref_loss"] = np.array([loss], np.float32)
+    g["train_r18_224_ref_grad_err"] = np.array(errs, np.float64)
+    L.omref_model_destroy(h)
+
     out = os.path.join(HERE, "golden.npz")
     np.savez_compressed(out, **g)
     print(f"wrote {out} ({os.path.getsize(out)} bytes, {len(g)} arrays)")
