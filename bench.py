@@ -1,4 +1,4 @@
-"""Benchmark: ResNet-50 bf16 inference, batch 256 per GPU, 224x224.
+"""Benchmark: ResNet-50 bf16 inference, batch 256 per GPU, 224x224 (the headline workload).
 
 One process per GPU (torchrun for N > 1). Each rank builds the fused NHWC bf16 inference
 plan (BatchNorm folded into tcgen05 implicit-GEMM convs, captured in one CUDA graph) and
@@ -7,9 +7,10 @@ only cross-rank traffic is the host-side barrier and the max-over-ranks of the t
 
 Printed JSON line (rank 0):
   value   images/s of the whole job, device-resident inputs, graph replay, max over ranks
-  e2e     images/s through the public C-ABI path with host buffers: per step the pinned
-          host->device copy of the step's NCHW fp32 input, the forward, and the
-          device->host copy of the logits, all inside the timed region
+  e2e     images/s through InferencePlan.serve with host buffers: per step the pinned
+          host->device copy of the step's NCHW fp32 input (on the transfer stream, overlapping
+          the previous step's forward), the forward, and the device->host copy of the logits,
+          all inside the timed region
   roofline  the dominant kernel (conv_tc_kernel): algorithmic conv+FC FLOPs of one step
           divided by the summed duration of its launches, from CUDA events around each
           launch in an instrumented eager pass of the same steps
@@ -34,6 +35,9 @@ sys.path.insert(0, ROOT)
 
 METRIC = "ResNet-50 bf16 images/s at 1/2/4/8 B200; conv implicit-GEMM % of TC peak"
 BATCH = 256
+# DRAM read+write bytes of the 54 conv_tc_kernel launches of one batch-64 forward, from one ncu
+# capture (profiles/conv_tc_kernel_traffic_resnet50_b64.md); traffic grows with the batch.
+CONV_TRAFFIC_B64 = 2.341e9
 
 
 def _peaks():
@@ -352,36 +356,39 @@ def run_ours(args, world, rank, local, dist):
     value = args.steps * BATCH * world / t_dev_max
 
     # ---------------------------------------------------------------- end to end, host buffers
-    in_bytes = BATCH * 3 * 224 * 224 * 4
+    # InferencePlan.serve: per step, the step's NCHW fp32 batch goes host->device on the
+    # transfer stream (pinned source) and its logits come back device->host; the copy of step
+    # i+1 overlaps the forward of step i. Two pinned input and output buffers alternate.
+    in_bytes = plan.in_bytes
     out_bytes = BATCH * net.classes * 4
     import ctypes
-    hin, hout = ctypes.c_void_p(), ctypes.c_void_p()
-    call("omCudaMallocHost", ctypes.byref(hin), in_bytes)
-    call("omCudaMallocHost", ctypes.byref(hout), out_bytes)
-    ctypes.memmove(hin.value, x.ctypes.data, in_bytes)
-    for _ in range(max(1, args.warmup // 2)):
-        call("omCudaAsyncCopyH2D", plan.in_f32.ptr, hin.value, in_bytes)
-        plan.launch()
-        call("omCudaAsyncCopyD2H", hout.value, plan.logits.ptr, out_bytes)
+    hin = [ctypes.c_void_p() for _ in range(2)]
+    hout = [ctypes.c_void_p() for _ in range(2)]
+    for b in hin:
+        call("omCudaMallocHost", ctypes.byref(b), in_bytes)
+        ctypes.memmove(b.value, x.ctypes.data, in_bytes)
+    for b in hout:
+        call("omCudaMallocHost", ctypes.byref(b), out_bytes)
+    ins = [hin[i % 2].value for i in range(args.steps)]
+    outs = [hout[i % 2].value for i in range(args.steps)]
+    plan.serve(ins[:max(3, args.warmup)], outs[:max(3, args.warmup)])
     call("omCudaSynchronize")
     _barrier(dist)
     torch.cuda.synchronize()
     e2, e3 = ev(), ev()
     with torch.cuda.stream(stream):
         e2.record()
-        for _ in range(args.steps):
-            call("omCudaAsyncCopyH2D", plan.in_f32.ptr, hin.value, in_bytes)
-            plan.launch()
-            call("omCudaAsyncCopyD2H", hout.value, plan.logits.ptr, out_bytes)
+        plan.serve(ins, outs)
         e3.record()
     e3.synchronize()
+    call("omCudaSynchronize")
     _barrier(dist)
     t_e2e = _max_over_ranks(dist, e2.elapsed_time(e3) / 1e3)
     e2e = args.steps * BATCH * world / t_e2e
-    logits = np.frombuffer(ctypes.string_at(hout.value, out_bytes), np.float32)
+    logits = np.frombuffer(ctypes.string_at(outs[-1], out_bytes), np.float32)
     finite = bool(np.isfinite(logits).all())
-    call("omCudaFreeHost", hin.value)
-    call("omCudaFreeHost", hout.value)
+    for b in hin + hout:
+        call("omCudaFreeHost", b.value)
 
     # ---------------------------------------------------------------- instrumented pass
     conv_ms, total_ms, conv_launches = 0.0, 0.0, 0
@@ -425,7 +432,10 @@ def run_ours(args, world, rank, local, dist):
                          "frac": achieved / peak_sust,
                          "peak_kind": f"bf16_tflops_sustained ({peak_src})",
                          "frac_of_burst": achieved / peak_burst,
-                         "conv_share_of_step": share, "traffic": None,
+                         "conv_share_of_step": share,
+                         "traffic": CONV_TRAFFIC_B64 * BATCH / 64,
+                         "traffic_unit": "bytes per step, conv launches (ncu at batch 64, "
+                                         "scaled by batch)",
                          "flops_per_step": plan.conv_flops,
                          "launches_per_step": len(plan.tc_op_index)},
             "gpu_launches": kernels_per_step * args.steps,

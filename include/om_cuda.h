@@ -71,6 +71,15 @@ int omCudaGraphBeginCapture(void);                                     /* replac
 int omCudaGraphEndCapture(void** pGraphExec);                          /* replaces :4919 */
 int omCudaGraphLaunch(void* pGraphExec);                               /* replaces :4941 */
 int omCudaGraphDestroy(void* pGraphExec);                              /* replaces :4949 */
+/* new: copies on the device's transfer stream, and ordering between the transfer and compute
+ * streams, so a serving loop can upload step i+1's input while step i computes:
+ * omCudaTransferH2D/D2H enqueue on the transfer stream; omCudaComputeWaitTransfer makes later
+ * compute work wait for the transfer work issued so far, omCudaTransferWaitCompute the
+ * opposite (e.g. before overwriting an input buffer the previous step still reads). */
+int omCudaTransferH2D(void* pDst, const void* pSrcHost, size_t nBytes);
+int omCudaTransferD2H(void* pDstHost, const void* pSrc, size_t nBytes);
+int omCudaComputeWaitTransfer(void);
+int omCudaTransferWaitCompute(void);
 /* new: select the calling thread's device (must have been omCudaInit'ed once per thread) */
 int omCudaSetDevice(int nDeviceId);
 /* new: the compute stream of the calling thread's device, as a cudaStream_t */

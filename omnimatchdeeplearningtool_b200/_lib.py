@@ -61,6 +61,8 @@ _SIGS = {
     "omCudaSynchronize": [], "omCudaAsyncCopyH2D": [P, P, c_size_t],
     "omCudaAsyncCopyD2H": [P, P, c_size_t], "omCudaSyncTransferStream": [],
     "omCudaSyncComputeStream": [], "omCudaCleanup": [],
+    "omCudaTransferH2D": [P, P, c_size_t], "omCudaTransferD2H": [P, P, c_size_t],
+    "omCudaComputeWaitTransfer": [], "omCudaTransferWaitCompute": [],
     "omCudaMallocHost": [POINTER(c_void_p), c_size_t], "omCudaFreeHost": [P],
     "omCudaGraphBeginCapture": [], "omCudaGraphEndCapture": [POINTER(c_void_p)],
     "omCudaGraphLaunch": [P], "omCudaGraphDestroy": [P],

@@ -17,6 +17,8 @@ struct DeviceCtx {
     int device = -1;
     cudaStream_t compute = nullptr;
     cudaStream_t transfer = nullptr;
+    cudaEvent_t transfer_done = nullptr;  // recorded on `transfer`, waited on by `compute`
+    cudaEvent_t compute_done = nullptr;   // recorded on `compute`, waited on by `transfer`
     unsigned int* err_word = nullptr;   // device memory, 0 = no error
     int num_sms = 0;
     unsigned long long launches = 0;    // kernels launched through this library

@@ -33,6 +33,8 @@ static int init_device(int dev) {
     if (!c->inited) {
         OMB_CHECK(cudaStreamCreateWithFlags(&c->compute, cudaStreamNonBlocking));
         OMB_CHECK(cudaStreamCreateWithFlags(&c->transfer, cudaStreamNonBlocking));
+        OMB_CHECK(cudaEventCreateWithFlags(&c->transfer_done, cudaEventDisableTiming));
+        OMB_CHECK(cudaEventCreateWithFlags(&c->compute_done, cudaEventDisableTiming));
         OMB_CHECK(cudaMalloc(&c->err_word, sizeof(unsigned int)));
         OMB_CHECK(cudaMemset(c->err_word, 0, sizeof(unsigned int)));
         OMB_CHECK(cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, dev));
@@ -169,6 +171,33 @@ int omCudaAsyncCopyH2D(void* pDst, const void* pSrc, size_t nBytes) {
 int omCudaAsyncCopyD2H(void* pDst, const void* pSrc, size_t nBytes) {
     OMB_CTX_OR_FAIL(c);
     return omb::status_of(cudaMemcpyAsync(pDst, pSrc, nBytes, cudaMemcpyDeviceToHost, c->compute));
+}
+
+int omCudaTransferH2D(void* pDst, const void* pSrcHost, size_t nBytes) {
+    OMB_CTX_OR_FAIL(c);
+    return omb::status_of(cudaMemcpyAsync(pDst, pSrcHost, nBytes, cudaMemcpyHostToDevice, c->transfer));
+}
+
+int omCudaTransferD2H(void* pDstHost, const void* pSrc, size_t nBytes) {
+    OMB_CTX_OR_FAIL(c);
+    return omb::status_of(cudaMemcpyAsync(pDstHost, pSrc, nBytes, cudaMemcpyDeviceToHost, c->transfer));
+}
+
+// One reusable event per direction and device: a stream wait binds to the event's most recent
+// record at the time the wait is enqueued, so re-recording it afterwards is safe.
+static int stream_wait(cudaStream_t waiter, cudaStream_t producer, cudaEvent_t e) {
+    OMB_CHECK(cudaEventRecord(e, producer));
+    return omb::status_of(cudaStreamWaitEvent(waiter, e, 0));
+}
+
+int omCudaComputeWaitTransfer(void) {
+    OMB_CTX_OR_FAIL(c);
+    return stream_wait(c->compute, c->transfer, c->transfer_done);
+}
+
+int omCudaTransferWaitCompute(void) {
+    OMB_CTX_OR_FAIL(c);
+    return stream_wait(c->transfer, c->compute, c->compute_done);
 }
 
 int omCudaSyncTransferStream(void) {

@@ -23,7 +23,7 @@ training step (forward, CE loss, backward, SGD momentum) of the reference engine
 from __future__ import annotations
 
 import ctypes
-from typing import Dict, List, Optional
+from typing import Dict, List, Optional, Sequence
 
 import numpy as np
 
@@ -44,19 +44,25 @@ class InferencePlan:
     """Fused NHWC inference of a :class:`NetSpec` at a fixed batch size."""
 
     def __init__(self, net: NetSpec, weights: Dict[str, np.ndarray], batch: int,
-                 dtype: int = DTYPE_BF16, h: int = 224, w: int = 224):
+                 dtype: int = DTYPE_BF16, h: int = 224, w: int = 224, input_slots: int = 2):
         assert dtype in (DTYPE_BF16, DTYPE_F16)
+        if input_slots not in (1, 2):
+            raise ValueError("input_slots must be 1 or 2")
         self.net, self.batch, self.dtype, self.h, self.w = net, batch, dtype, h, w
         self.ops: List = []           # callables, each issuing one C-ABI launch
         self.keep: List[DeviceBuffer] = []
-        self.graph = None
+        self.graphs: List[int] = []   # one captured graph per input slot
         self.conv_flops = 0           # algorithmic FLOPs of the tensor-core convs + FC
         self.n_tc_launches = 0
         self.n_launches = 0
         self.tc_op_index: List[int] = []   # positions in self.ops of tensor-core launches
         self.meta: List[dict] = []         # one descriptor per op (kind, buffers, shape)
-        # input staging: NCHW fp32 as the engine hands it over
-        self.in_f32 = self._buf(batch * 3 * h * w * 4)
+        # input staging: NCHW fp32 as the engine hands it over. With two slots the next batch's
+        # host->device copy lands in one slot while the forward reads the other (serve()).
+        self.in_bytes = batch * 3 * h * w * 4
+        self.inputs = [self._buf(self.in_bytes) for _ in range(input_slots)]
+        self.in_f32 = self.inputs[0]
+        self._slot = 0                # the slot the stem reads when ops are issued
         # the image stem reads the NCHW fp32 input directly (tcgen05 kernel, gathered A tile)
         cur, hh, ww, c = self.in_f32, h, w, 3
         act0 = _ACT[net.stem_act]
@@ -170,12 +176,14 @@ class InferencePlan:
         p = (hh + 2 * cv.pad - cv.k) // cv.stride + 1
         q = (ww + 2 * cv.pad - cv.k) // cv.stride + 1
         out = self._buf(n * p * q * cv.cout * 2)
-        x = self.in_f32
-        self._need(x, n * cv.cin * hh * ww * 4)
-        self._op(lambda x=x, out=out: call(
-            "omCudaStemConvBnAct", x.ptr, packed.ptr, bias.ptr, out.ptr, n, cv.cin, hh, ww,
-            cv.cout, cv.k, cv.k, cv.stride, cv.pad, act, dt),
-            dict(kind="stem", inp=x, out=out, w=weights[cv.name + ".weight"],
+        for x in self.inputs:
+            self._need(x, n * cv.cin * hh * ww * 4)
+        # The input pointer is the one op argument looked up when the op is issued: the slot
+        # being captured or launched (every other argument is bound here).
+        self._op(lambda out=out: call(
+            "omCudaStemConvBnAct", self.inputs[self._slot].ptr, packed.ptr, bias.ptr, out.ptr,
+            n, cv.cin, hh, ww, cv.cout, cv.k, cv.k, cv.stride, cv.pad, act, dt),
+            dict(kind="stem", inp=self.in_f32, out=out, w=weights[cv.name + ".weight"],
                  bn=self._bn_params(weights, cv.bn), c=cv.cin, k=cv.cout, ks=cv.k,
                  stride=cv.stride, pad=cv.pad, act=act, h=hh, wd=ww, p=p, q=q))
         self.n_tc_launches += 1
@@ -237,29 +245,40 @@ class InferencePlan:
         return cur, h2, w2, c2
 
     # -------------------------------------------------------------- execution
-    def launch(self) -> None:
-        """Issue the whole forward (graph replay when captured) on the compute stream."""
-        if self.graph is not None:
-            call("omCudaGraphLaunch", self.graph)
+    @property
+    def graph(self):
+        """The graph of input slot 0 (None before :meth:`capture`)."""
+        return self.graphs[0] if self.graphs else None
+
+    def launch(self, slot: int = 0) -> None:
+        """Issue the whole forward on input slot `slot` (graph replay when captured) on the
+        compute stream."""
+        if self.graphs:
+            call("omCudaGraphLaunch", self.graphs[slot])
         else:
+            self._slot = slot
             for fn in self.ops:
                 fn()
 
     def capture(self) -> None:
+        """Capture one CUDA graph per input slot; they differ only in the stem's input."""
         call("omCudaSynchronize")
-        call("omCudaGraphBeginCapture")
-        try:
-            for fn in self.ops:
-                fn()
-        finally:
-            g = ctypes.c_void_p()
-            st = lib.omCudaGraphEndCapture(ctypes.byref(g))
-        _lib.check(st, "omCudaGraphEndCapture")
-        self.graph = g.value
+        for slot in range(len(self.inputs)):
+            self._slot = slot
+            call("omCudaGraphBeginCapture")
+            try:
+                for fn in self.ops:
+                    fn()
+            finally:
+                g = ctypes.c_void_p()
+                st = lib.omCudaGraphEndCapture(ctypes.byref(g))
+            _lib.check(st, "omCudaGraphEndCapture")
+            self.graphs.append(g.value)
+        self._slot = 0
 
-    def set_input(self, x: np.ndarray) -> None:
+    def set_input(self, x: np.ndarray, slot: int = 0) -> None:
         assert x.shape == (self.batch, 3, self.h, self.w)
-        self.in_f32.upload(np.ascontiguousarray(x, dtype=np.float32))
+        self.inputs[slot].upload(np.ascontiguousarray(x, dtype=np.float32))
 
     def run(self, x: np.ndarray) -> np.ndarray:
         """Host NCHW fp32 input -> host fp32 logits [N, classes]."""
@@ -267,10 +286,40 @@ class InferencePlan:
         self.launch()
         return self.logits.to_numpy((self.batch, self.net.classes))
 
+    def serve(self, host_inputs: Sequence[int], host_outputs: Sequence[int]) -> None:
+        """Enqueue len(host_inputs) forwards without waiting: batch i is copied from the pinned
+        host buffer host_inputs[i] (NCHW fp32, ``in_bytes``) and its fp32 logits are copied to
+        the pinned host buffer host_outputs[i]. Returns once everything is enqueued;
+        ``omCudaSynchronize`` waits for it.
+
+        The copy of batch i+1 runs on the transfer stream while batch i's forward runs on the
+        compute stream: with two slots, the copy into slot (i+1) % 2 waits only for forward
+        i-1, the last one that read that slot. With one slot, copy and forward alternate."""
+        n, slots = len(host_inputs), len(self.inputs)
+        if len(host_outputs) != n:
+            raise ValueError("serve: host_inputs and host_outputs differ in length")
+        if n == 0:
+            return
+        out_bytes = self.batch * self.net.classes * 4
+        call("omCudaTransferWaitCompute")     # slot 0 may still be read by earlier work
+        call("omCudaTransferH2D", self.inputs[0].ptr, host_inputs[0], self.in_bytes)
+        for i in range(n):
+            s = i % slots
+            call("omCudaComputeWaitTransfer")     # batch i has landed in slot s
+            if slots == 2:
+                call("omCudaTransferWaitCompute")  # forward i-1 (the other slot's reader) done
+            self.launch(s)
+            call("omCudaAsyncCopyD2H", host_outputs[i], self.logits.ptr, out_bytes)
+            if slots == 1:
+                call("omCudaTransferWaitCompute")  # forward i done with the only slot
+            if i + 1 < n:
+                call("omCudaTransferH2D", self.inputs[(i + 1) % slots].ptr, host_inputs[i + 1],
+                     self.in_bytes)
+
     def close(self) -> None:
-        if self.graph is not None:
-            lib.omCudaGraphDestroy(self.graph)
-            self.graph = None
+        for g in self.graphs:
+            lib.omCudaGraphDestroy(g)
+        self.graphs = []
         for b in self.keep:
             b.free()
         self.keep.clear()

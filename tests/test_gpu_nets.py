@@ -34,3 +34,41 @@ def test_inference_plan_matches_oracle(gpu, name, dtype):
     assert np.array_equal(got, got2)
     assert rel_err(got, want) <= 2e-2, rel_err(got, want)
     assert np.array_equal(got.argmax(1), want.argmax(1))
+
+
+@pytest.mark.parametrize("slots", [1, 2])
+def test_serve_pipeline_matches_run(gpu, slots):
+    """InferencePlan.serve (copies on the transfer stream, two input slots, one graph each)
+    gives, batch by batch, the same bits as the synchronous run() of the same batch."""
+    import ctypes
+    from omnimatchdeeplearningtool_b200 import _lib, synth
+    from omnimatchdeeplearningtool_b200._lib import call
+    from omnimatchdeeplearningtool_b200.plan import InferencePlan
+    net = synth.resnet_spec(18)
+    w = synth.make_weights(net)
+    n_steps, batch = 5, 4
+    xs = [synth.normal_input(batch, seed=20 + i) for i in range(n_steps)]
+    plan = InferencePlan(net, w, batch=batch, dtype=_lib.DTYPE_BF16, input_slots=slots)
+    hin, hout = [], []
+    try:
+        want = [plan.run(x) for x in xs]
+        plan.capture()
+        out_bytes = batch * net.classes * 4
+        for x in xs:
+            a, b = ctypes.c_void_p(), ctypes.c_void_p()
+            call("omCudaMallocHost", ctypes.byref(a), plan.in_bytes)
+            hin.append(a.value)
+            ctypes.memmove(a.value, x.ctypes.data, plan.in_bytes)
+            call("omCudaMallocHost", ctypes.byref(b), out_bytes)
+            hout.append(b.value)
+        plan.serve(hin, hout)
+        call("omCudaSynchronize")
+        got = [np.frombuffer(ctypes.string_at(p, out_bytes), np.float32).reshape(batch, -1)
+               for p in hout]
+    finally:
+        plan.close()
+        for p in hin + hout:
+            call("omCudaFreeHost", p)
+    for g, wnt in zip(got, want):
+        assert np.array_equal(g, wnt)
+    assert not np.array_equal(got[0], got[1])
