@@ -30,10 +30,14 @@
 //   MODE_INTERLEAVE: Cs % 8 == 0 (the 32-channel MobileNet layers). A stage holds 8 im2col
 //               boxes of 128 pixels x 8 channels (2 KB each, no swizzle): core matrices of
 //               8 rows x 16 B, SBO = 128 B (next 8 rows), LBO = 2 KB (next 8 K-elements).
-//   MODE_STEM:  the image stem (3 channels, KW <= 8). K is ordered (r, c, s) with the taps s
+//   MODE_STEM:  the image stem (few channels, KW <= 8, stride 1 or 2). A tile is one output
+//               row (n, p) and up to 128 output columns; K is ordered (c, r, s) with the taps s
 //               padded to 8, so one 16-byte chunk of an A row holds 8 horizontal taps of one
-//               image plane row; gather warps read them from the NCHW fp32 image, round to
-//               16 bits and store them at their 128-byte-swizzled positions. B is SW128.
+//               image plane row. A pre-pass writes the image as 16-bit NCHW rows shifted right
+//               by `pad` columns; one or two TMA boxes per tile bring the tile's rows into
+//               shared memory, and the gather warps copy each A chunk from there (for stride 2,
+//               four aligned 32-bit words) to its 128-byte-swizzled position. B is SW128. The
+//               output is stored through a 3-D map (Cout, Q, N*P) so columns past Q are clipped.
 //
 // Every mbarrier wait is bounded (OMB_WAIT_NS); a wait that gives up records a bit in the
 // device error word, raises a CTA-wide abort flag, and the CTA drains its in-flight TMA
@@ -42,6 +46,7 @@
 #include <cudaTypedefs.h>
 
 #include <mutex>
+#include <type_traits>
 
 #include "om_common.cuh"
 
@@ -58,6 +63,14 @@ constexpr int EPI_SUB_BYTES = 32 * 32 * 2;             // one 32x32 16-bit sub-t
 constexpr int EPI_WARP_BYTES = 4 * EPI_SUB_BYTES;      // 2 residual + 2 output buffers
 constexpr int EPI_BYTES = NUM_EPI_WARPS * EPI_WARP_BYTES;
 constexpr int MAX_DYN_SMEM = 232448;                   // 227 KB per CTA on sm_100
+// MODE_STEM input patch: per tile, C*R image rows of 136 16-bit columns, one box for stride 1
+// (columns q0 + [0, 135)), two for stride 2 (the second starting 128 columns later).
+constexpr int STEM_MAX_ROWS = 24;                      // R * C (7x7 on 3 channels: 21)
+constexpr int STEM_BOX_W = 136;
+constexpr int STEM_PATCH_BYTES = 2 * STEM_BOX_W * STEM_MAX_ROWS * 2 + 256;  // 13312, 128-B multiple
+static_assert(STEM_PATCH_BYTES % 128 == 0, "patch buffers stay 128-byte aligned");
+constexpr int STEM_PATCH_BUFS = 3;                     // two tiles' loads in flight
+constexpr int STEM_EXTRA_BYTES = STEM_PATCH_BUFS * STEM_PATCH_BYTES;
 constexpr unsigned long long OMB_WAIT_NS = 2000000000ull;  // 2 s per wait
 
 enum { MODE_SW128 = 0, MODE_INTERLEAVE = 1, MODE_STEM = 2 };
@@ -71,6 +84,7 @@ struct Params {
     int num_m_tiles, num_n_tiles;
     const float* x;       // MODE_STEM: the NCHW fp32 image
     int C;                // MODE_STEM: its channel count
+    int QT;               // MODE_STEM: tiles per output row, ceil(Q / 128)
     const float* bias;
     const void* residual;
     void* out;
@@ -144,6 +158,36 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void*
             reinterpret_cast<uint64_t>(map)),
         "r"(smem_u32(src)), "r"(x), "r"(y)
         : "memory");
+}
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                            int x, int y, int z, int w) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "r"(w)
+        : "memory");
+}
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int x, int y,
+                                             int z) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+            reinterpret_cast<uint64_t>(map)),
+        "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
+        : "memory");
+}
+// Named barrier over `nthreads` threads that also ORs a predicate across them, so every
+// participant leaves with the same answer.
+__device__ __forceinline__ bool bar_or(int id, int nthreads, bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.or.pred q, %2, %3, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}\n"
+        : "=r"(r)
+        : "r"((uint32_t)pred), "r"(id), "r"(nthreads)
+        : "memory");
+    return r != 0;
 }
 __device__ __forceinline__ void bulk_commit() {
     asm volatile("cp.async.bulk.commit_group;" ::: "memory");
@@ -235,17 +279,19 @@ __device__ __forceinline__ uint32_t sw64(int r, int j) {
 // OCC = CTAs per SM. OCC 2 (BN <= 128, so two CTAs' TMEM fit in 512 columns) halves the
 // stages and doubles the independent pipelines per SM; it is chosen for short-K, memory-bound
 // layers where one CTA cannot keep enough loads and stores in flight.
-template <int BN, int OCC>
+// EXTRA = mode-specific shared memory after the epilogue buffers (the stem's patch buffers).
+template <int BN, int OCC, int EXTRA = 0>
 struct Cfg {
     static constexpr int B_STAGE_BYTES = BN * BK * 2;
     static constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
     static constexpr int BAR_BYTES = 512;
     static constexpr int BUDGET = OCC == 1 ? MAX_DYN_SMEM : (233472 - 2048) / 2 - 1024;
-    static constexpr int STAGES_RAW = (BUDGET - 1024 - BAR_BYTES - EPI_BYTES) / STAGE_BYTES;
+    static constexpr int STAGES_RAW =
+        (BUDGET - 1024 - BAR_BYTES - EPI_BYTES - EXTRA) / STAGE_BYTES;
     static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
     static constexpr int TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
-    // operand stages + epilogue buffers + barriers/flags + slack for 1024-byte alignment
-    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + BAR_BYTES + 1024;
+    // operand stages + epilogue buffers + extra + barriers/flags + slack for 1024-byte alignment
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + EXTRA + BAR_BYTES + 1024;
     static_assert(SMEM_BYTES <= BUDGET, "shared memory budget");
     static_assert(STAGES >= 2, "pipeline depth");
     static_assert(OCC == 1 || TMEM_COLS * OCC <= 512, "TMEM budget");
@@ -280,7 +326,7 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
     conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmOut,
                    const __grid_constant__ CUtensorMap tmRes, const Params p) {
-    using C = Cfg<BN, OCC>;
+    using C = Cfg<BN, OCC, MODE == MODE_STEM ? STEM_EXTRA_BYTES : 0>;
     using H16 = Half16<DT>;
     constexpr int STAGES = C::STAGES;
     constexpr bool F16 = (DT == OM_DTYPE_F16);
@@ -290,13 +336,15 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
     uint8_t* sA = smem;
     uint8_t* sB = smem + STAGES * A_STAGE_BYTES;
     uint8_t* sEpi = sB + STAGES * C::B_STAGE_BYTES;
-    uint64_t* full = reinterpret_cast<uint64_t*>(sEpi + EPI_BYTES);
+    uint8_t* sExtra = sEpi + EPI_BYTES;
+    uint64_t* full = reinterpret_cast<uint64_t*>(sExtra + (MODE == MODE_STEM ? STEM_EXTRA_BYTES : 0));
     uint64_t* empty = full + STAGES;
     uint64_t* tfull = empty + STAGES;
     uint64_t* tempty = tfull + 2;
     uint64_t* drain = tempty + 2;
     uint64_t* resfull = drain + 1;  // [NUM_EPI_WARPS][2]
-    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(resfull + 2 * NUM_EPI_WARPS);
+    uint64_t* patch_full = resfull + 2 * NUM_EPI_WARPS;  // [STEM_PATCH_BUFS], MODE_STEM
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(patch_full + STEM_PATCH_BUFS);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
     volatile int* consumed = abort_flag + 1;  // stage loads the MMA issuer has consumed
 
@@ -314,6 +362,7 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
             mbar_init(&tempty[i], NUM_EPI_WARPS);
         }
         for (int i = 0; i < 2 * NUM_EPI_WARPS; ++i) mbar_init(&resfull[i], 1);
+        for (int i = 0; i < STEM_PATCH_BUFS; ++i) mbar_init(&patch_full[i], 1);
         mbar_init(drain, 1);
         *abort_flag = 0;
         *consumed = 0;
@@ -487,6 +536,13 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
             const int n_tile = tile - m_tile * p.num_n_tiles;
             const int mw = m_tile * BM + quarter * 32;  // first output pixel of this warp
             const int nbase = n_tile * BN;
+            // MODE_STEM: the tile is output row `srow` (= n*P + p), columns from `sq`
+            int srow = 0, sq = 0;
+            if (MODE == MODE_STEM) {
+                srow = m_tile / p.QT;
+                sq = (m_tile - srow * p.QT) * BM + quarter * 32;
+            }
+            const bool dead = MODE == MODE_STEM && sq >= p.Q;  // whole sub-tile past Q
             if (has_res && lane == 0) {
                 // first chunk's residual, requested before the accumulator is ready
                 fence_async_smem();
@@ -555,7 +611,7 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
                         }
                     }
                 }
-                if (n0 >= p.K) continue;  // whole chunk beyond Cout: nothing to store
+                if (n0 >= p.K || dead) continue;  // nothing of this chunk to store
                 // the store issued two chunks ago from this staging buffer must have been read
                 if (lane == 0) bulk_wait_read<1>();
                 __syncwarp();
@@ -573,7 +629,8 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
                 fence_async_smem();
                 __syncwarp();
                 if (lane == 0) {
-                    tma_store_2d(&tmOut, ob, n0, mw);
+                    if (MODE == MODE_STEM) tma_store_3d(&tmOut, ob, n0, sq, srow);
+                    else tma_store_2d(&tmOut, ob, n0, mw);
                     bulk_commit();
                 }
             }
@@ -600,87 +657,114 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
         __syncwarp();
     } else if (MODE == MODE_STEM) {
         // ---------------------------------------------------------------- gather (stem)
-        // Warps g and g+4 share the 32 rows of lane quarter g % 4 and split each row's 8
-        // chunks. The CTA's (tile, k-block) items form one sequence; two register buffers
-        // alternate so that one item's loads are in flight while the other is stored.
+        // Tile i = output row (img, pp), columns q0 .. q0+127. Its patch (buffer i % 3) holds,
+        // for patch row t = c*R + r, image row pp*stride - pad + r of channel c at padded
+        // columns q0*stride + [0, 136) (box 0) and, for stride 2, + 128 + [0, 136) (box 1);
+        // TMA zero-fills rows outside the image and columns past the padded row. A row m,
+        // chunk t holds columns m*stride + [0, 8) of patch row t: for stride 2 that is box
+        // m / 64, 32-bit words (m % 64) + [0, 4) of the row, already in element order.
+        // Gather thread 0 loads each tile's patch two tiles ahead; the 256 gather threads meet
+        // at a named barrier (id 1) per tile, which also agrees on whether to stop.
         const int gw = warp - 2 - NUM_EPI_WARPS;
-        const int row = (gw & 3) * 32 + lane;
-        const int j0 = (gw >> 2) * 4;
-        const int nchunks = p.R * p.C;
-        const size_t plane = (size_t)p.H * p.W;
+        const int gt = gw * 32 + lane;
+        const int row = (gw & 3) * 32 + lane;   // A row this thread builds
+        const int j0 = (gw >> 2) * 4;           // its first chunk in each k-block
+        const int RC = p.R * p.C;
+        const int nbox = p.stride == 2 ? 2 : 1;
+        const uint32_t box_bytes = (uint32_t)(STEM_BOX_W * RC * 2);
+        const uint32_t box1_off = (box_bytes + 127u) & ~127u;   // TMA destinations 128-byte aligned
         const int my_tiles =
             (int)blockIdx.x < num_tiles ? (num_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-        const int n_items = my_tiles * p.num_kb;
-        auto load_item = [&](int item, float (&f)[4][8]) {
-            const int tile = (int)blockIdx.x + (item / p.num_kb) * (int)gridDim.x;
-            const int kb = item % p.num_kb;
-            const int m = (tile / p.num_n_tiles) * BM + row;
-            const bool row_ok = m < p.M;
-            const int mm = row_ok ? m : 0;
-            const int img = mm / PQ;
-            const int rem = mm - img * PQ;
-            const int pp = rem / p.Q;
-            const int qq = rem - pp * p.Q;
-            const int ih0 = pp * p.stride - p.pad;
-            const int iw0 = qq * p.stride - p.pad;
-            const bool interior = iw0 >= 0 && iw0 + 8 <= p.W;  // whole 8-wide window inside
-            const float* xim = p.x + (size_t)img * p.C * plane;
-#pragma unroll
-            for (int jj = 0; jj < 4; ++jj) {
-                const int t = kb * 8 + j0 + jj;
-                const int r = t / p.C;
-                const int ch = t - r * p.C;
-                const int ih = ih0 + r;
-                const bool live = row_ok && t < nchunks && ih >= 0 && ih < p.H;
-                const float* src = xim + ch * plane + (size_t)(live ? ih : 0) * p.W + iw0;
-                if (live && interior) {
-                    // taps beyond S meet zero weights, so the whole window loads unguarded
-#pragma unroll
-                    for (int sx = 0; sx < 8; ++sx) f[jj][sx] = __ldg(src + sx);
-                } else {
-#pragma unroll
-                    for (int sx = 0; sx < 8; ++sx) {
-                        const int iw = iw0 + sx;
-                        f[jj][sx] = (live && iw >= 0 && iw < p.W) ? __ldg(src + sx) : 0.f;
-                    }
-                }
-            }
+        auto tile_row = [&](int i, int& rowid, int& q0) {
+            const int mt = ((int)blockIdx.x + i * (int)gridDim.x) / p.num_n_tiles;
+            rowid = mt / p.QT;
+            q0 = (mt - rowid * p.QT) * BM;
+        };
+        auto issue = [&](int i) {
+            int rowid, q0;
+            tile_row(i, rowid, q0);
+            const int img = rowid / p.P;
+            const int pp = rowid - img * p.P;
+            uint8_t* dst = sExtra + (i % STEM_PATCH_BUFS) * STEM_PATCH_BYTES;
+            uint64_t* bar = &patch_full[i % STEM_PATCH_BUFS];
+            fence_async_smem();   // generic reads of this buffer (tile i-3) precede the TMA write
+            mbar_expect_tx(bar, box_bytes * nbox);
+            tma_load_4d(dst, &tmA, bar, q0 * p.stride, pp * p.stride - p.pad, 0, img);
+            if (nbox == 2)
+                tma_load_4d(dst + box1_off, &tmA, bar, q0 * p.stride + 128, pp * p.stride - p.pad, 0,
+                            img);
         };
         int stage = 0;
         uint32_t phase = 0;
-        bool ok = true;
-        auto store_item = [&](const float (&f)[4][8]) -> bool {
-            if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) return false;
-            uint8_t* a_row = sA + stage * A_STAGE_BYTES + row * 128;
+        auto build = [&](int i) -> bool {
+            int rowid, q0;
+            tile_row(i, rowid, q0);
+            const bool row_ok = q0 + row < p.Q;
+            const uint8_t* pb = sExtra + (i % STEM_PATCH_BUFS) * STEM_PATCH_BYTES;
+            for (int kb = 0; kb < p.num_kb; ++kb) {
+                if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) return false;
+                uint8_t* a_row = sA + stage * A_STAGE_BYTES + row * 128;
 #pragma unroll
-            for (int jj = 0; jj < 4; ++jj) {
-                const int j = j0 + jj;
-                uint4 v;
-                typename H16::T2* v2 = reinterpret_cast<typename H16::T2*>(&v);
-#pragma unroll
-                for (int u = 0; u < 4; ++u) v2[u] = H16::pack(f[jj][2 * u], f[jj][2 * u + 1]);
-                *reinterpret_cast<uint4*>(a_row + ((j ^ (row & 7)) << 4)) = v;
-            }
-            // make this thread's generic-proxy smem writes visible to the tensor cores
-            fence_async_smem();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&full[stage]);
-            if (++stage == STAGES) {
-                stage = 0;
-                phase ^= 1;
+                for (int jj = 0; jj < 4; ++jj) {
+                    const int j = j0 + jj;
+                    const int t = kb * 8 + j;
+                    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+                    if (row_ok && t < RC) {
+                        if (nbox == 2) {
+                            const uint32_t* w = reinterpret_cast<const uint32_t*>(
+                                pb + (row >> 6) * box1_off + t * (STEM_BOX_W * 2)) + (row & 63);
+                            v = make_uint4(w[0], w[1], w[2], w[3]);
+                        } else {
+                            const uint16_t* h = reinterpret_cast<const uint16_t*>(
+                                pb + t * (STEM_BOX_W * 2)) + row;
+                            v = make_uint4(h[0] | ((uint32_t)h[1] << 16), h[2] | ((uint32_t)h[3] << 16),
+                                           h[4] | ((uint32_t)h[5] << 16), h[6] | ((uint32_t)h[7] << 16));
+                        }
+                    }
+                    *reinterpret_cast<uint4*>(a_row + ((j ^ (row & 7)) << 4)) = v;
+                }
+                // make this thread's generic-proxy smem writes visible to the tensor cores
+                fence_async_smem();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&full[stage]);
+                if (++stage == STAGES) {
+                    stage = 0;
+                    phase ^= 1;
+                }
             }
             return true;
         };
-        float fa[4][8], fb[4][8];
-        if (n_items > 0) load_item(0, fa);
-        for (int item = 0; item < n_items && ok; item += 2) {
-            if (item + 1 < n_items) load_item(item + 1, fb);
-            if (!store_item(fa)) { ok = false; break; }
-            if (item + 1 >= n_items) break;
-            if (item + 2 < n_items) load_item(item + 2, fa);
-            if (!store_item(fb)) { ok = false; break; }
+        constexpr int NG = 32 * NUM_GATHER_WARPS;
+        bool failed = false;
+        int issued = 0, waited = 0;   // patch loads issued / waited for (thread gt == 0)
+        if (gt == 0) {
+            for (; issued < 2 && issued < my_tiles; ++issued) issue(issued);
         }
-        if (!ok && lane == 0) {
+        for (int i = 0; i < my_tiles; ++i) {
+            // buffer (i+2) % 3 was last read while building tile i-1, before the last barrier
+            if (gt == 0 && i + 2 < my_tiles) issue(issued++);
+            if (!failed) {
+                if (!mbar_wait(&patch_full[i % STEM_PATCH_BUFS], (uint32_t)((i / STEM_PATCH_BUFS) & 1),
+                               abort_flag))
+                    failed = true;
+                else {
+                    ++waited;
+                    if (!build(i)) failed = true;
+                }
+            }
+            if (bar_or(1, NG, failed || *abort_flag != 0)) break;
+        }
+        if (gt == 0) {
+            // no patch load may land after the CTA exits
+            for (int j = waited; j < issued; ++j) {
+                if (!mbar_wait_drain(&patch_full[j % STEM_PATCH_BUFS],
+                                     (uint32_t)((j / STEM_PATCH_BUFS) & 1))) {
+                    atomicOr(p.err, ERRBIT_TC_DRAIN);
+                    break;
+                }
+            }
+        }
+        if (failed && lane == 0) {
             atomicOr(p.err, ERRBIT_TC_PRODUCER);
             *abort_flag = 1;
         }
@@ -735,7 +819,7 @@ static int encode_epilogue_map(CUtensorMap* map, const void* base, int rows, int
 template <int BN, int MODE, int DT, int OCC>
 static int launch(DeviceCtx* c, const CUtensorMap& ta, const CUtensorMap& tb,
                   const CUtensorMap& to, const CUtensorMap& tr, const Params& p) {
-    using Cf = Cfg<BN, OCC>;
+    using Cf = Cfg<BN, OCC, MODE == MODE_STEM ? STEM_EXTRA_BYTES : 0>;
     auto kern = conv_tc_kernel<BN, MODE, DT, OCC>;
     static bool attr_set[64] = {false};
     if (!attr_set[c->device]) {
@@ -796,7 +880,18 @@ static int finish_and_launch(DeviceCtx* c, int bn, int occ, int nDtype, const CU
     const CUtensorMapDataType dt =
         nDtype == OM_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     CUtensorMap to = tb, tr = tb;  // unused slots carry a valid map
-    if (!p.out_f32) {
+    if (MODE == MODE_STEM) {
+        // (Cout, Q, N*P) with 32 x 32 x 1 boxes: stores past column Q are clipped
+        cuuint64_t dims[3] = {(cuuint64_t)p.K, (cuuint64_t)p.Q, (cuuint64_t)p.N * p.P};
+        cuuint64_t strides[2] = {(cuuint64_t)p.K * 2, (cuuint64_t)p.Q * p.K * 2};
+        cuuint32_t box[3] = {32, 32, 1};
+        cuuint32_t estr[3] = {1, 1, 1};
+        CUresult r = g_encode_tiled(&to, dt, 3, p.out, dims, strides, box, estr,
+                                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) return OM_ERR_DRIVER;
+    } else if (!p.out_f32) {
         int st = encode_epilogue_map(&to, p.out, p.M, p.K, dt);
         if (st != OM_OK) return st;
         if (p.residual) {
@@ -868,6 +963,7 @@ extern "C" int omCudaConv2dBnAct(const void* pInput, const void* pPacked, const 
     p.num_n_tiles = (nCout + bn - 1) / bn;
     p.x = nullptr;
     p.C = nCs;
+    p.QT = 1;
     p.bias = pBias;
     p.residual = pResidual;
     p.out = pOutput;
@@ -913,40 +1009,105 @@ extern "C" int omCudaConv2dBnAct(const void* pInput, const void* pPacked, const 
 }
 
 // ---------------------------------------------------------------- image stem
-// K layout of the stem's packed weight: kk = (r * Cin + c) * 8 + s, s < KW (taps padded to 8).
+// K layout of the stem's packed weight: kk = (c * KH + r) * 8 + s, s < KW (taps padded to 8).
 extern "C" long long omCudaPackedStemWeightElems(int nCout, int nCin, int nKH) {
     long long kk = (long long)nKH * nCin * 8;
     return (long long)nCout * ((kk + tc::BK - 1) / tc::BK * tc::BK);
 }
 
-extern "C" int omCudaStemConvBnAct(const float* pInput, const void* pPacked, const float* pBias,
-                                   void* pOutput, int nBatch, int nCin, int nH, int nW, int nCout,
-                                   int nKH, int nKW, int nStride, int nPad, int nAct, int nDtype) {
+namespace omb {
+namespace tc {
+// Padded row length of the stem's 16-bit copy of the image: `pad` zero columns on the left,
+// the image row, zeros up to a multiple of 8 (16 bytes).
+static long long stem_row_elems(int nW, int nPad) { return ((long long)nW + nPad + 7) / 8 * 8; }
+
+// NCHW fp32 -> [N*C*H, Wp] 16-bit rows shifted right by `pad`, zero elsewhere; one thread per
+// 8 output elements (16-byte store).
+template <typename T>
+__global__ void stem_pad_kernel(const float* __restrict__ x, T* __restrict__ out, long long rows,
+                                int W, int Wp, int pad) {
+    const int groups = Wp / 8;
+    const long long total = rows * groups;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const long long r = i / groups;
+        const int x0 = (int)(i - r * groups) * 8 - pad;
+        const float* src = x + r * W;
+        uint4 v;
+        uint32_t* w = reinterpret_cast<uint32_t*>(&v);
+#pragma unroll
+        for (int e = 0; e < 8; e += 2) {
+            const int c0 = x0 + e, c1 = x0 + e + 1;
+            const float f0 = (c0 >= 0 && c0 < W) ? __ldg(src + c0) : 0.f;
+            const float f1 = (c1 >= 0 && c1 < W) ? __ldg(src + c1) : 0.f;
+            typename Half16<std::is_same<T, __half>::value ? OM_DTYPE_F16 : OM_DTYPE_BF16>::T2 h2 =
+                Half16<std::is_same<T, __half>::value ? OM_DTYPE_F16 : OM_DTYPE_BF16>::pack(f0, f1);
+            w[e / 2] = *reinterpret_cast<uint32_t*>(&h2);
+        }
+        *reinterpret_cast<uint4*>(out + r * Wp + (long long)(i - r * groups) * 8) = v;
+    }
+}
+}  // namespace tc
+}  // namespace omb
+
+extern "C" long long omCudaStemWorkspaceBytes(int nBatch, int nCin, int nH, int nW, int nPad) {
+    if (nBatch <= 0 || nCin <= 0 || nH <= 0 || nW <= 0 || nPad < 0) return 0;
+    return (long long)nBatch * nCin * nH * omb::tc::stem_row_elems(nW, nPad) * 2;
+}
+
+extern "C" int omCudaStemConvBnAct(const float* pInput, void* pWorkspace, const void* pPacked,
+                                   const float* pBias, void* pOutput, int nBatch, int nCin, int nH,
+                                   int nW, int nCout, int nKH, int nKW, int nStride, int nPad,
+                                   int nAct, int nDtype) {
     OMB_CTX_OR_FAIL(c);
     using namespace omb::tc;
-    if (!pInput || !pPacked || !pOutput) return OM_ERR_INVALID;
+    if (!pInput || !pWorkspace || !pPacked || !pOutput) return OM_ERR_INVALID;
     if (nBatch <= 0 || nCin <= 0 || nH <= 0 || nW <= 0 || nCout <= 0 || nKH <= 0 || nKW <= 0 ||
         nStride <= 0 || nPad < 0)
         return OM_ERR_INVALID;
     if (nKW > 8 || nCout % 8 != 0) return OM_ERR_UNSUPPORTED;
+    if (nStride != 1 && nStride != 2) return OM_ERR_UNSUPPORTED;
+    if (nKH * nCin > STEM_MAX_ROWS || nKH > 256 || nCin > 256) return OM_ERR_UNSUPPORTED;
     if (nDtype != OM_DTYPE_BF16 && nDtype != OM_DTYPE_F16) return OM_ERR_UNSUPPORTED;
-    if ((reinterpret_cast<uintptr_t>(pPacked) | reinterpret_cast<uintptr_t>(pOutput) |
-         reinterpret_cast<uintptr_t>(pBias)) & 15)
+    if ((reinterpret_cast<uintptr_t>(pWorkspace) | reinterpret_cast<uintptr_t>(pPacked) |
+         reinterpret_cast<uintptr_t>(pOutput) | reinterpret_cast<uintptr_t>(pBias)) & 15)
         return OM_ERR_INVALID;
     const int P = (nH + 2 * nPad - nKH) / nStride + 1;
     const int Q = (nW + 2 * nPad - nKW) / nStride + 1;
     if (P <= 0 || Q <= 0) return OM_ERR_INVALID;
     const long long Mll = (long long)nBatch * P * Q;
-    if (Mll >= (1LL << 31)) return OM_ERR_UNSUPPORTED;
+    const int qt = (Q + BM - 1) / BM;
+    const long long m_tiles = (long long)nBatch * P * qt;
+    const long long wp = stem_row_elems(nW, nPad);
+    const long long rows = (long long)nBatch * nCin * nH;
+    if (Mll >= (1LL << 31) || m_tiles >= (1LL << 31) / 4 || wp >= (1LL << 31) ||
+        rows >= (1LL << 31))
+        return OM_ERR_UNSUPPORTED;
     if (!load_driver_entry_points()) return OM_ERR_DRIVER;
     const long long kpad = omCudaPackedStemWeightElems(1, nCin, nKH);
+
+    // 16-bit padded copy of the image
+    {
+        const long long groups = rows * (wp / 8);
+        long long blocks = (groups + 255) / 256;
+        const int grid = (int)(blocks < 8LL * c->num_sms ? blocks : 8LL * c->num_sms);
+        if (nDtype == OM_DTYPE_BF16)
+            stem_pad_kernel<__nv_bfloat16><<<grid, 256, 0, c->compute>>>(
+                pInput, static_cast<__nv_bfloat16*>(pWorkspace), rows, nW, (int)wp, nPad);
+        else
+            stem_pad_kernel<__half><<<grid, 256, 0, c->compute>>>(
+                pInput, static_cast<__half*>(pWorkspace), rows, nW, (int)wp, nPad);
+        int st = after_launch(c);
+        if (st != OM_OK) return st;
+    }
 
     Params p;
     p.N = nBatch; p.H = nH; p.W = nW; p.Cs = nCin; p.K = nCout;
     p.R = nKH; p.S = nKW; p.stride = nStride; p.pad = nPad;
     p.P = P; p.Q = Q; p.M = (int)Mll;
     p.num_kb = (int)(kpad / BK);
-    p.num_m_tiles = (int)((Mll + BM - 1) / BM);
+    p.num_m_tiles = (int)m_tiles;
+    p.QT = qt;
     int bn, occ;
     choose_tile(nCout, 1 << 20, p.num_m_tiles, c->num_sms, &bn, &occ);  // one CTA per SM
     p.num_n_tiles = (nCout + bn - 1) / bn;
@@ -961,15 +1122,24 @@ extern "C" int omCudaStemConvBnAct(const float* pInput, const void* pPacked, con
 
     const CUtensorMapDataType dt =
         nDtype == OM_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-    CUtensorMap tb;
+    // A source: the padded image as (Wp, H, C, N), box (136, KH, C, 1)
+    CUtensorMap ta, tb;
+    cuuint64_t a_dims[4] = {(cuuint64_t)wp, (cuuint64_t)nH, (cuuint64_t)nCin, (cuuint64_t)nBatch};
+    cuuint64_t a_strides[3] = {(cuuint64_t)wp * 2, (cuuint64_t)nH * wp * 2,
+                               (cuuint64_t)nCin * nH * wp * 2};
+    cuuint32_t a_box[4] = {(cuuint32_t)STEM_BOX_W, (cuuint32_t)nKH, (cuuint32_t)nCin, 1};
+    cuuint32_t a_estr[4] = {1, 1, 1, 1};
+    CUresult r = g_encode_tiled(&ta, dt, 4, pWorkspace, a_dims, a_strides, a_box, a_estr,
+                                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return OM_ERR_DRIVER;
     cuuint64_t b_dims[2] = {(cuuint64_t)kpad, (cuuint64_t)nCout};
     cuuint64_t b_strides[1] = {(cuuint64_t)kpad * 2};
     cuuint32_t b_estr[2] = {1, 1};
     cuuint32_t b_box[2] = {64u, (cuuint32_t)bn};
-    CUresult r = g_encode_tiled(&tb, dt, 2, const_cast<void*>(pPacked), b_dims, b_strides, b_box,
-                                b_estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    r = g_encode_tiled(&tb, dt, 2, const_cast<void*>(pPacked), b_dims, b_strides, b_box, b_estr,
+                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return OM_ERR_DRIVER;
-    // the A operand is gathered by threads; the unused A map slot carries the B map
-    return finish_and_launch<MODE_STEM>(c, bn, occ, nDtype, tb, tb, p);
+    return finish_and_launch<MODE_STEM>(c, bn, occ, nDtype, ta, tb, p);
 }

@@ -47,9 +47,9 @@ __global__ void pack_stem_weight_kernel(const float* __restrict__ w, const float
         int k = (int)(i / kpad);
         long long kk = i - (long long)k * kpad;
         int chunk = (int)(kk / 8), s = (int)(kk % 8);
-        int r = chunk / C, c = chunk - r * C;
+        int c = chunk / R, r = chunk - c * R;   // kk = (c * R + r) * 8 + s
         float v = 0.f;
-        if (r < R && s < S) v = w[(((long long)k * C + c) * R + r) * S + s] * scale[k];
+        if (c < C && s < S) v = w[(((long long)k * C + c) * R + r) * S + s] * scale[k];
         if constexpr (std::is_same<T, __nv_bfloat16>::value) out[i] = __float2bfloat16_rn(v);
         else out[i] = __float2half_rn(v);
     }

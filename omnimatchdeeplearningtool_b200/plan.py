@@ -176,13 +176,14 @@ class InferencePlan:
         p = (hh + 2 * cv.pad - cv.k) // cv.stride + 1
         q = (ww + 2 * cv.pad - cv.k) // cv.stride + 1
         out = self._buf(n * p * q * cv.cout * 2)
+        ws = self._buf(int(lib.omCudaStemWorkspaceBytes(n, cv.cin, hh, ww, cv.pad)))
         for x in self.inputs:
             self._need(x, n * cv.cin * hh * ww * 4)
         # The input pointer is the one op argument looked up when the op is issued: the slot
         # being captured or launched (every other argument is bound here).
-        self._op(lambda out=out: call(
-            "omCudaStemConvBnAct", self.inputs[self._slot].ptr, packed.ptr, bias.ptr, out.ptr,
-            n, cv.cin, hh, ww, cv.cout, cv.k, cv.k, cv.stride, cv.pad, act, dt),
+        self._op(lambda out=out, ws=ws: call(
+            "omCudaStemConvBnAct", self.inputs[self._slot].ptr, ws.ptr, packed.ptr, bias.ptr,
+            out.ptr, n, cv.cin, hh, ww, cv.cout, cv.k, cv.k, cv.stride, cv.pad, act, dt),
             dict(kind="stem", inp=self.in_f32, out=out, w=weights[cv.name + ".weight"],
                  bn=self._bn_params(weights, cv.bn), c=cv.cin, k=cv.cout, ks=cv.k,
                  stride=cv.stride, pad=cv.pad, act=act, h=hh, wd=ww, p=p, q=q))

@@ -131,7 +131,9 @@ def test_conv_rejects_bad_shapes(gpu):
 
 @pytest.mark.parametrize("n,h,k,ks,stride,pad,dt", [(2, 224, 64, 7, 2, 3, "bf16"),
                                                     (3, 37, 64, 7, 2, 3, "bf16"),
-                                                    (2, 31, 32, 3, 2, 1, "f16")])
+                                                    (2, 31, 32, 3, 2, 1, "f16"),
+                                                    (1, 300, 64, 7, 2, 3, "bf16"),  # 2 tiles/row
+                                                    (2, 20, 32, 7, 1, 3, "bf16")])  # stride 1
 def test_stem_conv_from_nchw_image(gpu, n, h, k, ks, stride, pad, dt):
     """omCudaStemConvBnAct: the image stem straight from NCHW fp32 (ImageNet 7x7/2 and the
     MobileNet 3x3/2 stem), checked like the other fused convs."""
@@ -155,8 +157,10 @@ def test_stem_conv_from_nchw_image(gpu, n, h, k, ks, stride, pad, dt):
     call("omCudaPackStemWeight", keep[1].ptr, None, keep[2].ptr, keep[3].ptr, keep[4].ptr,
          keep[5].ptr, 1e-5, packed.ptr, bias.ptr, k, c, ks, ks, dtype)
     out = DeviceBuffer(n * p * p * k * 2)
-    call("omCudaStemConvBnAct", keep[0].ptr, packed.ptr, bias.ptr, out.ptr, n, c, h, h, k, ks, ks,
-         stride, pad, 1, dtype)
+    ws = DeviceBuffer(int(lib.omCudaStemWorkspaceBytes(n, c, h, h, pad)))
+    keep.append(ws)
+    call("omCudaStemConvBnAct", keep[0].ptr, ws.ptr, packed.ptr, bias.ptr, out.ptr, n, c, h, h, k,
+         ks, ks, stride, pad, 1, dtype)
     o32 = DeviceBuffer(n * k * p * p * 4)
     call("omCudaNhwcToNchw", out.ptr, o32.ptr, n, k, p, p, k, dtype)
     got = o32.to_numpy((n, k, p, p))
