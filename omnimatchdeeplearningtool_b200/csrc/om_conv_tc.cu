@@ -60,7 +60,8 @@ constexpr int NUM_EPI_WARPS = 4;        // one per TMEM lane quarter
 constexpr int NUM_GATHER_WARPS = 8;     // MODE_STEM only
 constexpr int NUM_THREADS = 64 + 32 * NUM_EPI_WARPS;
 constexpr int EPI_SUB_BYTES = 32 * 32 * 2;             // one 32x32 16-bit sub-tile
-constexpr int EPI_WARP_BYTES = 4 * EPI_SUB_BYTES;      // 2 residual + 2 output buffers
+constexpr int EPI_BUFS = 4;                            // staging sub-tiles per epilogue warp
+constexpr int EPI_WARP_BYTES = EPI_BUFS * EPI_SUB_BYTES;
 constexpr int EPI_BYTES = NUM_EPI_WARPS * EPI_WARP_BYTES;
 constexpr int MAX_DYN_SMEM = 232448;                   // 227 KB per CTA on sm_100
 // MODE_STEM input patch: per tile, C*R image rows of 136 16-bit columns, one box for stride 1
@@ -342,8 +343,8 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
     uint64_t* tfull = empty + STAGES;
     uint64_t* tempty = tfull + 2;
     uint64_t* drain = tempty + 2;
-    uint64_t* resfull = drain + 1;  // [NUM_EPI_WARPS][2]
-    uint64_t* patch_full = resfull + 2 * NUM_EPI_WARPS;  // [STEM_PATCH_BUFS], MODE_STEM
+    uint64_t* resfull = drain + 1;  // [NUM_EPI_WARPS][EPI_BUFS]
+    uint64_t* patch_full = resfull + EPI_BUFS * NUM_EPI_WARPS;  // [STEM_PATCH_BUFS], MODE_STEM
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(patch_full + STEM_PATCH_BUFS);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
     volatile int* consumed = abort_flag + 1;  // stage loads the MMA issuer has consumed
@@ -361,7 +362,7 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
             mbar_init(&tfull[i], 1);
             mbar_init(&tempty[i], NUM_EPI_WARPS);
         }
-        for (int i = 0; i < 2 * NUM_EPI_WARPS; ++i) mbar_init(&resfull[i], 1);
+        for (int i = 0; i < EPI_BUFS * NUM_EPI_WARPS; ++i) mbar_init(&resfull[i], 1);
         for (int i = 0; i < STEM_PATCH_BUFS; ++i) mbar_init(&patch_full[i], 1);
         mbar_init(drain, 1);
         *abort_flag = 0;
@@ -517,18 +518,33 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
         }
     } else if (warp < 2 + NUM_EPI_WARPS) {
         // ---------------------------------------------------------------- epilogue
+        // Each warp owns TMEM lane quarter `warp % 4` (32 output pixels) and four 2 KB staging
+        // sub-tiles used round-robin, one per 32-column chunk: the chunk's residual is brought
+        // into its sub-tile by TMA two chunks ahead, read, and overwritten in place by the
+        // output (each lane reads and writes only its own row), which a TMA store then writes
+        // out. The bias of the chunk's 32 columns is held one value per lane (loaded a chunk
+        // ahead) and broadcast with shuffles.
         const int ew = warp - 2;
         const int quarter = warp & 3;  // TMEM lane quarter this warp may access
         constexpr int NCH = BN / 32;
-        uint8_t* res_buf = sEpi + ew * EPI_WARP_BYTES;          // 2 residual sub-tiles
-        uint8_t* out_buf = res_buf + 2 * EPI_SUB_BYTES;         // 2 output sub-tiles
-        uint64_t* rbar = resfull + 2 * ew;
+        uint8_t* ebuf = sEpi + ew * EPI_WARP_BYTES;
+        uint64_t* rbar = resfull + EPI_BUFS * ew;
         const bool use_tma = !p.out_f32;
         const bool has_res = use_tma && p.residual != nullptr;
-        uint32_t g = 0;     // chunks started by this warp (buffer and phase bookkeeping)
-        uint32_t rg = 0;    // residual loads issued by this warp
+        const bool clamp = p.act != OM_ACT_NONE;
+        const float act_hi = p.act == OM_ACT_RELU6 ? 6.f : INFINITY;
+        uint32_t g = 0;       // chunks started by this warp; chunk g uses sub-tile g % EPI_BUFS
+        uint32_t rph = 0;     // per sub-tile: parity of its next residual load
+        uint32_t rpend = 0;   // per sub-tile: a residual load is in flight
         bool ok = true;
         int local = 0;
+        // lane 0 only: request the residual of chunk h (sub-tile h % EPI_BUFS)
+        auto issue_res = [&](uint32_t h, int col, int row0) {
+            const uint32_t u = h % EPI_BUFS;
+            fence_async_smem();
+            mbar_expect_tx(&rbar[u], EPI_SUB_BYTES);
+            tma_load_2d(ebuf + u * EPI_SUB_BYTES, &tmRes, &rbar[u], col, row0);
+        };
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
             const int acc = local & 1;
             const uint32_t acc_phase = (uint32_t)((local >> 1) & 1);
@@ -543,13 +559,19 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
                 sq = (m_tile - srow * p.QT) * BM + quarter * 32;
             }
             const bool dead = MODE == MODE_STEM && sq >= p.Q;  // whole sub-tile past Q
-            if (has_res && lane == 0) {
-                // first chunk's residual, requested before the accumulator is ready
-                fence_async_smem();
-                mbar_expect_tx(&rbar[g & 1], EPI_SUB_BYTES);
-                tma_load_2d(res_buf + (g & 1) * EPI_SUB_BYTES, &tmRes, &rbar[g & 1], nbase, mw);
+            const int rem_cols = p.K - nbase;
+            const int nvalid = rem_cols >= BN ? NCH : (rem_cols + 31) / 32;  // chunks with n0 < K
+            if (has_res) {
+                // the first two chunks' residuals, requested before the accumulator is ready;
+                // their sub-tiles were last read by the stores of chunks g-4 and g-3
+                if (lane == 0) bulk_wait_read<2>();
+                __syncwarp();
+                for (int c = 0; c < 2 && c < nvalid; ++c) {
+                    if (lane == 0) issue_res(g + c, nbase + c * 32, mw);
+                    rpend |= 1u << ((g + c) % EPI_BUFS);
+                }
             }
-            if (has_res) ++rg;
+            float bnext = (p.bias && nbase + lane < p.K) ? __ldg(p.bias + nbase + lane) : 0.f;
             if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) {
                 ok = false;
                 break;
@@ -557,51 +579,39 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
             tc_fence_after();
             const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
 #pragma unroll 1
-            for (int c = 0; c < NCH; ++c, ++g) {
+            for (int c = 0; c < nvalid; ++c, ++g) {
+                const uint32_t u = g % EPI_BUFS;
                 const int n0 = nbase + c * 32;
-                if (has_res && c + 1 < NCH) {
-                    if (lane == 0) {
-                        // the buffer was last read (generic proxy) two chunks ago
-                        fence_async_smem();
-                        const uint32_t nb = (g + 1) & 1;
-                        mbar_expect_tx(&rbar[nb], EPI_SUB_BYTES);
-                        tma_load_2d(res_buf + nb * EPI_SUB_BYTES, &tmRes, &rbar[nb], n0 + 32, mw);
-                    }
-                    ++rg;
+                const float bcur = bnext;
+                if (c + 1 < nvalid)
+                    bnext = (p.bias && n0 + 32 + lane < p.K) ? __ldg(p.bias + n0 + 32 + lane) : 0.f;
+                if (has_res && c + 2 < nvalid) {
+                    // sub-tile (g+2) % 4 was last read by the store of chunk g-2
+                    if (lane == 0) bulk_wait_read<1>();
+                    __syncwarp();
+                    if (lane == 0) issue_res(g + 2, n0 + 64, mw);
+                    rpend |= 1u << ((g + 2) % EPI_BUFS);
                 }
                 uint32_t v[32];
                 tmem_ld32(t_row + (uint32_t)(c * 32), v);
-                const uint32_t b = g & 1;
                 if (!use_tma) {
-                    if (mw + lane < p.M && n0 < p.K) store_chunk_f32(p, mw + lane, n0, v);
+                    if (mw + lane < p.M) store_chunk_f32(p, mw + lane, n0, v);
                     continue;
                 }
                 float f[32];
 #pragma unroll
-                for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]);
-                if (p.bias) {
-#pragma unroll
-                    for (int j = 0; j < 32; j += 4) {
-                        if (n0 + j < p.K) {
-                            float4 bb = __ldg(reinterpret_cast<const float4*>(p.bias + n0 + j));
-                            f[j] += bb.x;
-                            f[j + 1] += bb.y;
-                            f[j + 2] += bb.z;
-                            f[j + 3] += bb.w;
-                        }
-                    }
-                }
+                for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]) + __shfl_sync(0xffffffffu, bcur, j);
+                uint8_t* sb = ebuf + u * EPI_SUB_BYTES;
                 if (has_res) {
-                    // every residual load is waited for, even for chunks past Cout, so that the
-                    // barrier phases stay in step
-                    if (!mbar_wait(&rbar[b], (g >> 1) & 1, abort_flag)) {
+                    if (!mbar_wait(&rbar[u], (rph >> u) & 1u, abort_flag)) {
                         ok = false;
                         break;
                     }
-                    const uint8_t* rb = res_buf + b * EPI_SUB_BYTES;
+                    rph ^= 1u << u;
+                    rpend &= ~(1u << u);
 #pragma unroll
                     for (int j = 0; j < 4; ++j) {
-                        uint4 rv = *reinterpret_cast<const uint4*>(rb + sw64(lane, j));
+                        uint4 rv = *reinterpret_cast<const uint4*>(sb + sw64(lane, j));
                         const typename H16::T2* r2 = reinterpret_cast<const typename H16::T2*>(&rv);
 #pragma unroll
                         for (int t = 0; t < 4; ++t) {
@@ -610,27 +620,29 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
                             f[8 * j + 2 * t + 1] += rr.y;
                         }
                     }
+                } else {
+                    // sub-tile u was last read by the store of chunk g-4
+                    if (lane == 0) bulk_wait_read<3>();
+                    __syncwarp();
                 }
-                if (n0 >= p.K || dead) continue;  // nothing of this chunk to store
-                // the store issued two chunks ago from this staging buffer must have been read
-                if (lane == 0) bulk_wait_read<1>();
-                __syncwarp();
-                uint8_t* ob = out_buf + b * EPI_SUB_BYTES;
+                if (dead) continue;  // stem sub-tile entirely past Q: nothing to store
+                if (clamp) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) f[j] = fminf(fmaxf(f[j], 0.f), act_hi);
+                }
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     uint4 ov;
                     typename H16::T2* o2 = reinterpret_cast<typename H16::T2*>(&ov);
 #pragma unroll
-                    for (int t = 0; t < 4; ++t)
-                        o2[t] = H16::pack(apply_act(f[8 * j + 2 * t], p.act),
-                                          apply_act(f[8 * j + 2 * t + 1], p.act));
-                    *reinterpret_cast<uint4*>(ob + sw64(lane, j)) = ov;
+                    for (int t = 0; t < 4; ++t) o2[t] = H16::pack(f[8 * j + 2 * t], f[8 * j + 2 * t + 1]);
+                    *reinterpret_cast<uint4*>(sb + sw64(lane, j)) = ov;
                 }
                 fence_async_smem();
                 __syncwarp();
                 if (lane == 0) {
-                    if (MODE == MODE_STEM) tma_store_3d(&tmOut, ob, n0, sq, srow);
-                    else tma_store_2d(&tmOut, ob, n0, mw);
+                    if (MODE == MODE_STEM) tma_store_3d(&tmOut, sb, n0, sq, srow);
+                    else tma_store_2d(&tmOut, sb, n0, mw);
                     bulk_commit();
                 }
             }
@@ -647,8 +659,8 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
             // no bulk store may still read shared memory (or be in flight) when the CTA exits
             bulk_wait_all();
             // abort path: residual loads issued but never waited for are drained (bounded)
-            for (uint32_t k = g; k < rg; ++k) {
-                if (!mbar_wait_drain(&rbar[k & 1], (k >> 1) & 1)) {
+            for (uint32_t u = 0; u < (uint32_t)EPI_BUFS; ++u) {
+                if (((rpend >> u) & 1u) && !mbar_wait_drain(&rbar[u], (rph >> u) & 1u)) {
                     atomicOr(p.err, ERRBIT_TC_DRAIN);
                     break;
                 }
