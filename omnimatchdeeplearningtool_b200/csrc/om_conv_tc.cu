@@ -347,7 +347,6 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
     uint64_t* patch_full = resfull + EPI_BUFS * NUM_EPI_WARPS;  // [STEM_PATCH_BUFS], MODE_STEM
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(patch_full + STEM_PATCH_BUFS);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
-    volatile int* consumed = abort_flag + 1;  // stage loads the MMA issuer has consumed
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -366,7 +365,6 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
         for (int i = 0; i < STEM_PATCH_BUFS; ++i) mbar_init(&patch_full[i], 1);
         mbar_init(drain, 1);
         *abort_flag = 0;
-        *consumed = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         fence_async_smem();
     }
@@ -402,6 +400,7 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
                 const int qq = rem - pp * p.Q;
                 const int wb = qq * p.stride - p.pad;
                 const int hb = pp * p.stride - p.pad;
+                int c0 = 0, fs = 0, fr = 0;   // MODE_SW128: channel slice and filter tap of kb
                 for (int kb = 0; kb < p.num_kb; ++kb) {
                     if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) {
                         ok = false;
@@ -415,14 +414,18 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
                         tma_load_2d(b_dst, &tmB, &full[stage], kb * BK, n0);
                     } else if (MODE == MODE_SW128) {
                         mbar_expect_tx(&full[stage], C::STAGE_BYTES);
-                        const int kk = kb * BK;
-                        const int rs = kk / p.Cs;
-                        const int c0 = kk - rs * p.Cs;
-                        const int r = rs / p.S;
-                        const int s = rs - r * p.S;
-                        tma_load_im2col(a_dst, &tmA, &full[stage], c0, wb, hb, img, (uint16_t)s,
-                                        (uint16_t)r);
-                        tma_load_2d(b_dst, &tmB, &full[stage], kk, n0);
+                        tma_load_im2col(a_dst, &tmA, &full[stage], c0, wb, hb, img, (uint16_t)fs,
+                                        (uint16_t)fr);
+                        tma_load_2d(b_dst, &tmB, &full[stage], kb * BK, n0);
+                        // kk = kb * 64 = (fr * S + fs) * Cs + c0 with Cs % 64 == 0
+                        c0 += BK;
+                        if (c0 == p.Cs) {
+                            c0 = 0;
+                            if (++fs == p.S) {
+                                fs = 0;
+                                ++fr;
+                            }
+                        }
                     } else {
                         mbar_expect_tx(&full[stage], C::STAGE_BYTES);
                         const int RS = p.R * p.S;
@@ -450,10 +453,10 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
                 atomicOr(p.err, ERRBIT_TC_PRODUCER);
                 *abort_flag = 1;
             }
-            // Never leave with a TMA write in flight: wait (bounded) for every load that was
-            // issued but not consumed by the MMA issuer.
-            long long done = *consumed;
-            for (long long j = (done > issued - STAGES ? done : issued - STAGES); j < issued; ++j) {
+            // Never leave with a TMA write in flight: wait (bounded) for the last STAGES loads
+            // issued (every earlier one was consumed before its stage was refilled). A load that
+            // was already consumed shows its phase as completed.
+            for (long long j = issued - STAGES; j < issued; ++j) {
                 if (j < 0) continue;
                 if (!mbar_wait_drain(&full[(int)(j % STAGES)], (uint32_t)((j / STAGES) & 1))) {
                     atomicOr(p.err, ERRBIT_TC_DRAIN);
@@ -465,6 +468,16 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
         if (lane == 0) {
             // ------------------------------------------------------------ MMA issuer
             constexpr uint32_t IDESC = instr_desc<BN, F16>();
+            // descriptors of stage 0, k step 0; stage and k offsets are added to the start
+            // address field (address >> 4, no carry out of its 14 bits below 256 KB)
+            const uint64_t adesc0 = MODE != MODE_INTERLEAVE
+                                        ? smem_desc(smem_u32(sA), 16, 1024, LAYOUT_SW128)
+                                        : smem_desc(smem_u32(sA), BM * 16, 128, LAYOUT_NONE);
+            const uint64_t bdesc0 = MODE != MODE_INTERLEAVE
+                                        ? smem_desc(smem_u32(sB), 16, 1024, LAYOUT_SW128)
+                                        : smem_desc(smem_u32(sB), BN * 16, 128, LAYOUT_NONE);
+            constexpr uint32_t A_K_STEP = MODE != MODE_INTERLEAVE ? 32 >> 4 : (2 * BM * 16) >> 4;
+            constexpr uint32_t B_K_STEP = MODE != MODE_INTERLEAVE ? 32 >> 4 : (2 * BN * 16) >> 4;
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
@@ -484,22 +497,13 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t a_base = smem_u32(sA + stage * A_STAGE_BYTES);
-                    const uint32_t b_base = smem_u32(sB + stage * C::B_STAGE_BYTES);
+                    const uint64_t ad = adesc0 + (uint64_t)(stage * (A_STAGE_BYTES >> 4));
+                    const uint64_t bd = bdesc0 + (uint64_t)(stage * (C::B_STAGE_BYTES >> 4));
 #pragma unroll
-                    for (int k = 0; k < BK / 16; ++k) {
-                        uint64_t ad, bd;
-                        if (MODE != MODE_INTERLEAVE) {
-                            ad = smem_desc(a_base + k * 32, 16, 1024, LAYOUT_SW128);
-                            bd = smem_desc(b_base + k * 32, 16, 1024, LAYOUT_SW128);
-                        } else {
-                            ad = smem_desc(a_base + k * 2 * (BM * 16), BM * 16, 128, LAYOUT_NONE);
-                            bd = smem_desc(b_base + k * 2 * (BN * 16), BN * 16, 128, LAYOUT_NONE);
-                        }
-                        tc_mma(d_tmem, ad, bd, IDESC, (kb > 0 || k > 0) ? 1u : 0u);
-                    }
+                    for (int k = 0; k < BK / 16; ++k)
+                        tc_mma(d_tmem, ad + k * A_K_STEP, bd + k * B_K_STEP, IDESC,
+                               (kb > 0 || k > 0) ? 1u : 0u);
                     tc_commit(&empty[stage]);
-                    *consumed = *consumed + 1;
                     if (++stage == STAGES) {
                         stage = 0;
                         phase ^= 1;
