@@ -22,6 +22,9 @@
 //               classifier, store directly)
 //   warps 6..13 MODE_STEM only: build the A tile from the NCHW fp32 image (see below)
 // Two TMEM accumulators (2*BN columns) let the epilogue of tile i overlap the MMAs of i+1.
+// MT = 2 (BN <= 128, one CTA per SM): a tile is two 128-row sub-tiles that share each B stage;
+// every k-block then issues 8 MMAs into two accumulators behind one barrier wait and commit,
+// halving the issuing thread's fixed cost per MMA and the B traffic per output row.
 //
 // Operand layouts in shared memory (K-major, matching the UMMA canonical layouts):
 //   MODE_SW128: Cs % 64 == 0. One im2col box = 128 pixels x 64 channels = 128 rows of 128 B,
@@ -281,21 +284,22 @@ __device__ __forceinline__ uint32_t sw64(int r, int j) {
 // stages and doubles the independent pipelines per SM; it is chosen for short-K, memory-bound
 // layers where one CTA cannot keep enough loads and stores in flight.
 // EXTRA = mode-specific shared memory after the epilogue buffers (the stem's patch buffers).
-template <int BN, int OCC, int EXTRA = 0>
+template <int BN, int OCC, int EXTRA = 0, int MT = 1>
 struct Cfg {
+    static constexpr int A_BYTES = MT * A_STAGE_BYTES;   // A bytes per stage
     static constexpr int B_STAGE_BYTES = BN * BK * 2;
-    static constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
+    static constexpr int STAGE_BYTES = A_BYTES + B_STAGE_BYTES;
     static constexpr int BAR_BYTES = 512;
     static constexpr int BUDGET = OCC == 1 ? MAX_DYN_SMEM : (233472 - 2048) / 2 - 1024;
     static constexpr int STAGES_RAW =
         (BUDGET - 1024 - BAR_BYTES - EPI_BYTES - EXTRA) / STAGE_BYTES;
     static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
-    static constexpr int TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
+    static constexpr int TMEM_COLS = 2 * MT * BN < 32 ? 32 : 2 * MT * BN;
     // operand stages + epilogue buffers + extra + barriers/flags + slack for 1024-byte alignment
     static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + EXTRA + BAR_BYTES + 1024;
     static_assert(SMEM_BYTES <= BUDGET, "shared memory budget");
     static_assert(STAGES >= 2, "pipeline depth");
-    static_assert(OCC == 1 || TMEM_COLS * OCC <= 512, "TMEM budget");
+    static_assert(TMEM_COLS * OCC <= 512, "TMEM budget");
 };
 
 // fp32-output chunk (classifier logits): + bias, + fp32 residual, activation, direct store
@@ -322,12 +326,14 @@ __device__ __forceinline__ void store_chunk_f32(const Params& p, int m, int n0,
     }
 }
 
-template <int BN, int MODE, int DT, int OCC>
+template <int BN, int MODE, int DT, int OCC, int MT>
 __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GATHER_WARPS : NUM_THREADS, OCC)
     conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmOut,
                    const __grid_constant__ CUtensorMap tmRes, const Params p) {
-    using C = Cfg<BN, OCC, MODE == MODE_STEM ? STEM_EXTRA_BYTES : 0>;
+    static_assert(MT == 1 || (MODE == MODE_SW128 && BN <= 128 && OCC == 1), "MT = 2 tiles");
+    using C = Cfg<BN, OCC, MODE == MODE_STEM ? STEM_EXTRA_BYTES : 0, MT>;
+    constexpr int TM = BM * MT;   // output pixels per tile
     using H16 = Half16<DT>;
     constexpr int STAGES = C::STAGES;
     constexpr bool F16 = (DT == OM_DTYPE_F16);
@@ -335,7 +341,7 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     uint8_t* sA = smem;
-    uint8_t* sB = smem + STAGES * A_STAGE_BYTES;
+    uint8_t* sB = smem + STAGES * C::A_BYTES;
     uint8_t* sEpi = sB + STAGES * C::B_STAGE_BYTES;
     uint8_t* sExtra = sEpi + EPI_BYTES;
     uint64_t* full = reinterpret_cast<uint64_t*>(sExtra + (MODE == MODE_STEM ? STEM_EXTRA_BYTES : 0));
@@ -392,7 +398,7 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
             for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
                 const int m_tile = tile / p.num_n_tiles;
                 const int n_tile = tile - m_tile * p.num_n_tiles;
-                const int m0 = m_tile * BM;
+                const int m0 = m_tile * TM;
                 const int n0 = n_tile * BN;
                 const int img = m0 / PQ;
                 const int rem = m0 - img * PQ;
@@ -400,13 +406,24 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
                 const int qq = rem - pp * p.Q;
                 const int wb = qq * p.stride - p.pad;
                 const int hb = pp * p.stride - p.pad;
+                // MT = 2: the second sub-tile's first pixel (a sub-tile wholly past M reloads
+                // the first one; its rows are never stored)
+                int img1 = img, wb1 = wb, hb1 = hb;
+                if (MT == 2 && m0 + BM < p.M) {
+                    const int m1 = m0 + BM;
+                    img1 = m1 / PQ;
+                    const int rem1 = m1 - img1 * PQ;
+                    const int pp1 = rem1 / p.Q;
+                    wb1 = (rem1 - pp1 * p.Q) * p.stride - p.pad;
+                    hb1 = pp1 * p.stride - p.pad;
+                }
                 int c0 = 0, fs = 0, fr = 0;   // MODE_SW128: channel slice and filter tap of kb
                 for (int kb = 0; kb < p.num_kb; ++kb) {
                     if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) {
                         ok = false;
                         break;
                     }
-                    uint8_t* a_dst = sA + stage * A_STAGE_BYTES;
+                    uint8_t* a_dst = sA + stage * C::A_BYTES;
                     uint8_t* b_dst = sB + stage * C::B_STAGE_BYTES;
                     if (MODE == MODE_STEM) {
                         // A comes from the gather warps; only the weights travel by TMA
@@ -416,6 +433,9 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
                         mbar_expect_tx(&full[stage], C::STAGE_BYTES);
                         tma_load_im2col(a_dst, &tmA, &full[stage], c0, wb, hb, img, (uint16_t)fs,
                                         (uint16_t)fr);
+                        if (MT == 2)
+                            tma_load_im2col(a_dst + A_STAGE_BYTES, &tmA, &full[stage], c0, wb1, hb1,
+                                            img1, (uint16_t)fs, (uint16_t)fr);
                         tma_load_2d(b_dst, &tmB, &full[stage], kb * BK, n0);
                         // kk = kb * 64 = (fr * S + fs) * Cs + c0 with Cs % 64 == 0
                         c0 += BK;
@@ -490,19 +510,22 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
                     break;
                 }
                 tc_fence_after();
-                const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+                const uint32_t d_tmem = tmem_base + (uint32_t)(acc * MT * BN);
                 for (int kb = 0; kb < p.num_kb; ++kb) {
                     if (!mbar_wait(&full[stage], phase, abort_flag)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint64_t ad = adesc0 + (uint64_t)(stage * (A_STAGE_BYTES >> 4));
+                    const uint64_t ad = adesc0 + (uint64_t)(stage * (C::A_BYTES >> 4));
                     const uint64_t bd = bdesc0 + (uint64_t)(stage * (C::B_STAGE_BYTES >> 4));
 #pragma unroll
                     for (int k = 0; k < BK / 16; ++k)
-                        tc_mma(d_tmem, ad + k * A_K_STEP, bd + k * B_K_STEP, IDESC,
-                               (kb > 0 || k > 0) ? 1u : 0u);
+#pragma unroll
+                        for (int mt = 0; mt < MT; ++mt)
+                            tc_mma(d_tmem + (uint32_t)(mt * BN),
+                                   ad + (uint64_t)(mt * (A_STAGE_BYTES >> 4)) + k * A_K_STEP,
+                                   bd + k * B_K_STEP, IDESC, (kb > 0 || k > 0) ? 1u : 0u);
                     tc_commit(&empty[stage]);
                     if (++stage == STAGES) {
                         stage = 0;
@@ -554,7 +577,8 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
             const uint32_t acc_phase = (uint32_t)((local >> 1) & 1);
             const int m_tile = tile / p.num_n_tiles;
             const int n_tile = tile - m_tile * p.num_n_tiles;
-            const int mw = m_tile * BM + quarter * 32;  // first output pixel of this warp
+          for (int mt = 0; mt < MT; ++mt) {
+            const int mw = m_tile * TM + mt * BM + quarter * 32;  // first output pixel of this warp
             const int nbase = n_tile * BN;
             // MODE_STEM: the tile is output row `srow` (= n*P + p), columns from `sq`
             int srow = 0, sq = 0;
@@ -562,10 +586,13 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
                 srow = m_tile / p.QT;
                 sq = (m_tile - srow * p.QT) * BM + quarter * 32;
             }
-            const bool dead = MODE == MODE_STEM && sq >= p.Q;  // whole sub-tile past Q
+            // a warp sub-tile wholly past the output (rows >= M, or stem columns >= Q) loads
+            // and stores nothing
+            const bool dead = MODE == MODE_STEM ? sq >= p.Q : mw >= p.M;
+            const bool res_here = has_res && !dead;
             const int rem_cols = p.K - nbase;
             const int nvalid = rem_cols >= BN ? NCH : (rem_cols + 31) / 32;  // chunks with n0 < K
-            if (has_res) {
+            if (res_here) {
                 // the first two chunks' residuals, requested before the accumulator is ready;
                 // their sub-tiles were last read by the stores of chunks g-4 and g-3
                 if (lane == 0) bulk_wait_read<2>();
@@ -576,12 +603,16 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
                 }
             }
             float bnext = (p.bias && nbase + lane < p.K) ? __ldg(p.bias + nbase + lane) : 0.f;
-            if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) {
-                ok = false;
-                break;
+            if (mt == 0) {
+                if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
             }
-            tc_fence_after();
-            const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * BN);
+            if (dead) continue;
+            const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) +
+                                   (uint32_t)(acc * MT * BN + mt * BN);
 #pragma unroll 1
             for (int c = 0; c < nvalid; ++c, ++g) {
                 const uint32_t u = g % EPI_BUFS;
@@ -589,7 +620,7 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
                 const float bcur = bnext;
                 if (c + 1 < nvalid)
                     bnext = (p.bias && n0 + 32 + lane < p.K) ? __ldg(p.bias + n0 + 32 + lane) : 0.f;
-                if (has_res && c + 2 < nvalid) {
+                if (res_here && c + 2 < nvalid) {
                     // sub-tile (g+2) % 4 was last read by the store of chunk g-2
                     if (lane == 0) bulk_wait_read<1>();
                     __syncwarp();
@@ -606,7 +637,7 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
 #pragma unroll
                 for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]) + __shfl_sync(0xffffffffu, bcur, j);
                 uint8_t* sb = ebuf + u * EPI_SUB_BYTES;
-                if (has_res) {
+                if (res_here) {
                     if (!mbar_wait(&rbar[u], (rph >> u) & 1u, abort_flag)) {
                         ok = false;
                         break;
@@ -629,7 +660,6 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
                     if (lane == 0) bulk_wait_read<3>();
                     __syncwarp();
                 }
-                if (dead) continue;  // stem sub-tile entirely past Q: nothing to store
                 if (clamp) {
 #pragma unroll
                     for (int j = 0; j < 32; ++j) f[j] = fminf(fmaxf(f[j], 0.f), act_hi);
@@ -650,6 +680,8 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
                     bulk_commit();
                 }
             }
+            if (!ok) break;
+          }
             if (!ok) break;
             tc_fence_before();
             __syncwarp();
@@ -719,7 +751,7 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
             const uint8_t* pb = sExtra + (i % STEM_PATCH_BUFS) * STEM_PATCH_BYTES;
             for (int kb = 0; kb < p.num_kb; ++kb) {
                 if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) return false;
-                uint8_t* a_row = sA + stage * A_STAGE_BYTES + row * 128;
+                uint8_t* a_row = sA + stage * C::A_BYTES + row * 128;
 #pragma unroll
                 for (int jj = 0; jj < 4; ++jj) {
                     const int j = j0 + jj;
@@ -832,11 +864,11 @@ static int encode_epilogue_map(CUtensorMap* map, const void* base, int rows, int
     return r == CUDA_SUCCESS ? OM_OK : OM_ERR_DRIVER;
 }
 
-template <int BN, int MODE, int DT, int OCC>
+template <int BN, int MODE, int DT, int OCC, int MT = 1>
 static int launch(DeviceCtx* c, const CUtensorMap& ta, const CUtensorMap& tb,
                   const CUtensorMap& to, const CUtensorMap& tr, const Params& p) {
-    using Cf = Cfg<BN, OCC, MODE == MODE_STEM ? STEM_EXTRA_BYTES : 0>;
-    auto kern = conv_tc_kernel<BN, MODE, DT, OCC>;
+    using Cf = Cfg<BN, OCC, MODE == MODE_STEM ? STEM_EXTRA_BYTES : 0, MT>;
+    auto kern = conv_tc_kernel<BN, MODE, DT, OCC, MT>;
     static bool attr_set[64] = {false};
     if (!attr_set[c->device]) {
         OMB_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -852,8 +884,18 @@ static int launch(DeviceCtx* c, const CUtensorMap& ta, const CUtensorMap& tb,
 }
 
 template <int MODE, int DT>
-static int dispatch_bn(DeviceCtx* c, int bn, int occ, const CUtensorMap& ta, const CUtensorMap& tb,
-                       const CUtensorMap& to, const CUtensorMap& tr, const Params& p) {
+static int dispatch_bn(DeviceCtx* c, int bn, int occ, int mt, const CUtensorMap& ta,
+                       const CUtensorMap& tb, const CUtensorMap& to, const CUtensorMap& tr,
+                       const Params& p) {
+    if constexpr (MODE == MODE_SW128) {
+        if (mt == 2) {
+            switch (bn) {
+                case 64: return launch<64, MODE, DT, 1, 2>(c, ta, tb, to, tr, p);
+                case 128: return launch<128, MODE, DT, 1, 2>(c, ta, tb, to, tr, p);
+            }
+            return OM_ERR_UNSUPPORTED;
+        }
+    }
     if constexpr (MODE != MODE_STEM) {  // the stem's 14 warps run one CTA per SM
         if (occ == 2) {
             switch (bn) {
@@ -873,26 +915,34 @@ static int dispatch_bn(DeviceCtx* c, int bn, int occ, const CUtensorMap& ta, con
     return OM_ERR_UNSUPPORTED;
 }
 
-// Tile width and CTAs per SM. Short reductions (K <= 512, i.e. 1x1 convs up to 512 input
-// channels) are memory-bound: they take 128-wide tiles at two CTAs per SM. Longer ones prefer
-// 256-wide tiles (half the A re-reads) unless that leaves SMs idle.
-static void choose_tile(int K, int num_kb, long long m_tiles, int num_sms, int* bn, int* occ) {
+// Tile shape and CTAs per SM, for Cout output channels, num_kb 64-wide k-blocks and m_tiles
+// 128-row tiles. Short reductions (num_kb <= 8, i.e. 1x1 convs up to 512 input channels) are
+// memory-bound: they take at most 128-wide tiles at two CTAs per SM. Longer ones prefer
+// 256-wide tiles (half the A re-reads) unless that leaves SMs idle; when they stay at 64 or
+// 128 wide, two 128-row sub-tiles per tile (mt = 2) are used if that still fills two waves.
+static void choose_tile(int Cout, int num_kb, long long m_tiles, int num_sms, bool allow_mt2,
+                        int* bn, int* occ, int* mt) {
     *occ = 1;
-    if (K <= 32) *bn = 32;
-    else if (K <= 64) *bn = 64;
-    else if (K <= 128) *bn = 128;
-    else *bn = (m_tiles * ((K + 255) / 256) >= 2LL * num_sms) ? 256 : 128;
+    *mt = 1;
+    if (Cout <= 32) *bn = 32;
+    else if (Cout <= 64) *bn = 64;
+    else if (Cout <= 128) *bn = 128;
+    else *bn = (m_tiles * ((Cout + 255) / 256) >= 2LL * num_sms) ? 256 : 128;
     if (num_kb <= 8) {
         if (*bn == 256) *bn = 128;
-        long long tiles = m_tiles * ((K + *bn - 1) / *bn);
+        long long tiles = m_tiles * ((Cout + *bn - 1) / *bn);
         if (tiles >= 2LL * num_sms) *occ = 2;
+    }
+    if (allow_mt2 && *occ == 1 && (*bn == 64 || *bn == 128)) {
+        long long tiles2 = (m_tiles + 1) / 2 * ((Cout + *bn - 1) / *bn);
+        if (tiles2 >= 2LL * num_sms) *mt = 2;
     }
 }
 
 // Encodes the output and residual maps (16-bit outputs) and launches the kernel.
 template <int MODE>
-static int finish_and_launch(DeviceCtx* c, int bn, int occ, int nDtype, const CUtensorMap& ta,
-                             const CUtensorMap& tb, const Params& p) {
+static int finish_and_launch(DeviceCtx* c, int bn, int occ, int mt, int nDtype,
+                             const CUtensorMap& ta, const CUtensorMap& tb, const Params& p) {
     const CUtensorMapDataType dt =
         nDtype == OM_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     CUtensorMap to = tb, tr = tb;  // unused slots carry a valid map
@@ -915,8 +965,9 @@ static int finish_and_launch(DeviceCtx* c, int bn, int occ, int nDtype, const CU
             if (st != OM_OK) return st;
         }
     }
-    if (nDtype == OM_DTYPE_BF16) return dispatch_bn<MODE, OM_DTYPE_BF16>(c, bn, occ, ta, tb, to, tr, p);
-    return dispatch_bn<MODE, OM_DTYPE_F16>(c, bn, occ, ta, tb, to, tr, p);
+    if (nDtype == OM_DTYPE_BF16)
+        return dispatch_bn<MODE, OM_DTYPE_BF16>(c, bn, occ, mt, ta, tb, to, tr, p);
+    return dispatch_bn<MODE, OM_DTYPE_F16>(c, bn, occ, mt, ta, tb, to, tr, p);
 }
 
 }  // namespace tc
@@ -974,8 +1025,9 @@ extern "C" int omCudaConv2dBnAct(const void* pInput, const void* pPacked, const 
     p.P = P; p.Q = Q; p.M = (int)Mll;
     p.num_kb = (int)(kpad / BK);
     p.num_m_tiles = (int)((Mll + BM - 1) / BM);
-    int bn, occ;
-    choose_tile(nCout, p.num_kb, p.num_m_tiles, c->num_sms, &bn, &occ);
+    int bn, occ, mt;
+    choose_tile(nCout, p.num_kb, p.num_m_tiles, c->num_sms, mode == MODE_SW128, &bn, &occ, &mt);
+    p.num_m_tiles = (int)((Mll + BM * mt - 1) / (BM * mt));
     p.num_n_tiles = (nCout + bn - 1) / bn;
     p.x = nullptr;
     p.C = nCs;
@@ -1020,8 +1072,8 @@ extern "C" int omCudaConv2dBnAct(const void* pInput, const void* pPacked, const 
                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return OM_ERR_DRIVER;
 
-    return mode == MODE_SW128 ? finish_and_launch<MODE_SW128>(c, bn, occ, nDtype, ta, tb, p)
-                              : finish_and_launch<MODE_INTERLEAVE>(c, bn, occ, nDtype, ta, tb, p);
+    return mode == MODE_SW128 ? finish_and_launch<MODE_SW128>(c, bn, occ, mt, nDtype, ta, tb, p)
+                              : finish_and_launch<MODE_INTERLEAVE>(c, bn, occ, mt, nDtype, ta, tb, p);
 }
 
 // ---------------------------------------------------------------- image stem
@@ -1124,8 +1176,8 @@ extern "C" int omCudaStemConvBnAct(const float* pInput, void* pWorkspace, const 
     p.num_kb = (int)(kpad / BK);
     p.num_m_tiles = (int)m_tiles;
     p.QT = qt;
-    int bn, occ;
-    choose_tile(nCout, 1 << 20, p.num_m_tiles, c->num_sms, &bn, &occ);  // one CTA per SM
+    int bn, occ, mt;
+    choose_tile(nCout, 1 << 20, p.num_m_tiles, c->num_sms, false, &bn, &occ, &mt);  // 1 CTA/SM
     p.num_n_tiles = (nCout + bn - 1) / bn;
     p.x = pInput;
     p.C = nCin;
@@ -1157,5 +1209,5 @@ extern "C" int omCudaStemConvBnAct(const float* pInput, void* pWorkspace, const 
                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return OM_ERR_DRIVER;
-    return finish_and_launch<MODE_STEM>(c, bn, occ, nDtype, ta, tb, p);
+    return finish_and_launch<MODE_STEM>(c, bn, occ, mt, nDtype, ta, tb, p);
 }

@@ -28,6 +28,10 @@ CASES = [
     (16, 256, 14, 256, 3, 1, 1, "bf16", False, "relu", False),    # 36 k-blocks
     (5, 2048, 1, 1000, 1, 1, 0, "bf16", False, "none", True),     # FC: M=5, K=1000, fp32 out
     (2, 3, 31, 32, 3, 2, 1, "f16", False, "relu6", False),        # MobileNet stem, odd H
+    # two 128-row sub-tiles per tile (>= 2 waves of 256-row tiles), last sub-tile past M
+    (25, 64, 56, 64, 3, 1, 1, "bf16", False, "relu", False),      # BN=64, M = 78400
+    (25, 64, 56, 128, 3, 1, 1, "bf16", True, "relu", False),      # BN=128 + residual
+    (100, 128, 56, 128, 3, 2, 1, "f16", False, "relu", False),    # stride 2, fp16
 ]
 
 
