@@ -116,44 +116,41 @@ __global__ void nhwc_to_nchw_kernel(const typename Half16<DT>::T* __restrict__ i
 }
 
 // ---------------------------------------------------------------- pooling
-// Each thread owns 8 consecutive channels (one 16-byte vector) of one output pixel.
+// One block per output row (n, p); its threads walk the row's (q, 8-channel group) items, each
+// the max of up to k*k 16-byte vectors taken on packed 16-bit pairs (a max is one of its
+// operands, so no rounding is involved). Windows with no pixel inside the image give -1e30,
+// the reference's starting value (cpu_backend.ixx maxPool2d).
 template <int DT>
-__global__ void maxpool_nhwc_kernel(const uint4* __restrict__ in, uint4* __restrict__ out, int N,
-                                    int H, int W, int C8, int P, int Q, int k, int stride, int pad) {
+__global__ void maxpool_nhwc_kernel(const uint4* __restrict__ in, uint4* __restrict__ out, int H,
+                                    int W, int C8, int P, int Q, int k, int stride, int pad) {
     using H16 = Half16<DT>;
-    long long total = (long long)N * P * Q * C8;
-    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
-         i += (long long)gridDim.x * blockDim.x) {
-        int c8 = (int)(i % C8);
-        long long pix = i / C8;
-        int q = (int)(pix % Q);
-        long long t = pix / Q;
-        int p = (int)(t % P);
-        int n = (int)(t / P);
-        float m[8];
+    using T2 = typename H16::T2;
+    const int row = blockIdx.x;          // n * P + p
+    const int n = row / P;
+    const int p = row - n * P;
+    const int h0 = p * stride - pad;
+    const int r0 = h0 < 0 ? -h0 : 0;
+    const int r1 = (H - h0) < k ? (H - h0) : k;
+    const uint4* img = in + (size_t)n * H * W * C8;
+    uint4* orow = out + (size_t)row * Q * C8;
+    const T2 lowest = H16::pack(-1e30f, -1e30f);
+    for (int i = threadIdx.x; i < Q * C8; i += blockDim.x) {
+        const int q = i / C8;
+        const int c8 = i - q * C8;
+        const int w0 = q * stride - pad;
+        const int s0 = w0 < 0 ? -w0 : 0;
+        const int s1 = (W - w0) < k ? (W - w0) : k;
+        T2 m[4] = {lowest, lowest, lowest, lowest};
+        for (int r = r0; r < r1; ++r) {
+            const uint4* src = img + ((size_t)(h0 + r) * W + w0) * C8 + c8;
+            for (int s = s0; s < s1; ++s) {
+                uint4 v = __ldg(src + (size_t)s * C8);
+                const T2* v2 = reinterpret_cast<const T2*>(&v);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) m[j] = -1e30f;
-        for (int r = 0; r < k; ++r) {
-            int ih = p * stride - pad + r;
-            if (ih < 0 || ih >= H) continue;
-            for (int s = 0; s < k; ++s) {
-                int iw = q * stride - pad + s;
-                if (iw < 0 || iw >= W) continue;
-                uint4 v = in[(((long long)n * H + ih) * W + iw) * C8 + c8];
-                const typename H16::T2* v2 = reinterpret_cast<const typename H16::T2*>(&v);
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    float2 f = H16::unpack(v2[j]);
-                    m[2 * j] = f.x > m[2 * j] ? f.x : m[2 * j];
-                    m[2 * j + 1] = f.y > m[2 * j + 1] ? f.y : m[2 * j + 1];
-                }
+                for (int j = 0; j < 4; ++j) m[j] = __hmax2(m[j], v2[j]);
             }
         }
-        uint4 o;
-        typename H16::T2* o2 = reinterpret_cast<typename H16::T2*>(&o);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) o2[j] = H16::pack(m[2 * j], m[2 * j + 1]);
-        out[i] = o;
+        orow[i] = *reinterpret_cast<const uint4*>(m);
     }
 }
 
@@ -361,14 +358,15 @@ extern "C" int omCudaMaxPool2dNhwc(const void* pIn, void* pOut, int nN, int nH, 
     if (!pIn || !pOut || nCs % 8 || !aligned16(pIn) || !aligned16(pOut)) return OM_ERR_INVALID;
     int P = (nH + 2 * nPad - nK) / nStride + 1, Q = (nW + 2 * nPad - nK) / nStride + 1;
     if (P <= 0 || Q <= 0) return OM_ERR_INVALID;
-    long long total = (long long)nN * P * Q * (nCs / 8);
-    int grid = ew_grid(c, total, 256);
+    const long long rows = (long long)nN * P;
+    if (rows >= (1LL << 31) || (long long)Q * (nCs / 8) >= (1LL << 31)) return OM_ERR_UNSUPPORTED;
+    const int threads = Q * (nCs / 8) >= 256 ? 256 : 128;
     if (nDtype == OM_DTYPE_BF16)
-        maxpool_nhwc_kernel<OM_DTYPE_BF16><<<grid, 256, 0, c->compute>>>(
-            static_cast<const uint4*>(pIn), static_cast<uint4*>(pOut), nN, nH, nW, nCs / 8, P, Q, nK, nStride, nPad);
+        maxpool_nhwc_kernel<OM_DTYPE_BF16><<<(unsigned)rows, threads, 0, c->compute>>>(
+            static_cast<const uint4*>(pIn), static_cast<uint4*>(pOut), nH, nW, nCs / 8, P, Q, nK, nStride, nPad);
     else if (nDtype == OM_DTYPE_F16)
-        maxpool_nhwc_kernel<OM_DTYPE_F16><<<grid, 256, 0, c->compute>>>(
-            static_cast<const uint4*>(pIn), static_cast<uint4*>(pOut), nN, nH, nW, nCs / 8, P, Q, nK, nStride, nPad);
+        maxpool_nhwc_kernel<OM_DTYPE_F16><<<(unsigned)rows, threads, 0, c->compute>>>(
+            static_cast<const uint4*>(pIn), static_cast<uint4*>(pOut), nH, nW, nCs / 8, P, Q, nK, nStride, nPad);
     else
         return OM_ERR_UNSUPPORTED;
     return after_launch(c);

@@ -1,0 +1,148 @@
+"""Parity of the NHWC 16-bit bandwidth kernels with the CPU oracle, on the same 16-bit values.
+
+* max pool (omCudaMaxPool2dNhwc): a max returns one of its operands, so the result must equal
+  the oracle's max pool of the 16-bit-rounded input bit for bit;
+* global average pool (omCudaGlobalAvgPoolNhwc) with an fp32 output: fp32 sums of the 16-bit
+  values, max|a-b|/max|b| <= 1e-5 against the oracle on the rounded input;
+* depthwise conv + BN + ReLU6 (omCudaDepthwiseConv2dNhwc): fp32 accumulation, 16-bit output:
+  <= 1e-2 against the oracle on rounded input and BN-folded fp32 weights;
+* residual add + activation (omCudaAddActNhwc): one 16-bit rounding of act(a + b).
+Ragged sizes (odd H and W, channels stored padded to a multiple of 8) are included.
+"""
+import numpy as np
+import pytest
+
+from conftest import rel_err
+
+pytestmark = pytest.mark.gpu
+
+_KEEP = []
+
+
+def _round16(a, dt):
+    import torch
+    t = torch.from_numpy(np.ascontiguousarray(a, np.float32))
+    return t.to(torch.bfloat16 if dt == "bf16" else torch.float16).to(torch.float32).numpy()
+
+
+def _to_nhwc(x, cs, dtype):
+    from omnimatchdeeplearningtool_b200._lib import call
+    from omnimatchdeeplearningtool_b200.backend import DeviceBuffer
+    n, c, h, w = x.shape
+    d32 = DeviceBuffer.from_numpy(np.ascontiguousarray(x, np.float32))
+    d16 = DeviceBuffer(n * h * w * cs * 2)
+    call("omCudaNchwToNhwc", d32.ptr, d16.ptr, n, c, h, w, cs, dtype)
+    _KEEP.extend([d32, d16])
+    return d16
+
+
+def _from_nhwc(buf, n, c, h, w, cs, dtype):
+    from omnimatchdeeplearningtool_b200._lib import call
+    from omnimatchdeeplearningtool_b200.backend import DeviceBuffer
+    o32 = DeviceBuffer(n * c * h * w * 4)
+    call("omCudaNhwcToNchw", buf.ptr, o32.ptr, n, c, h, w, cs, dtype)
+    _KEEP.append(o32)
+    return o32.to_numpy((n, c, h, w))
+
+
+@pytest.fixture(autouse=True)
+def _release():
+    yield
+    _KEEP.clear()
+
+
+@pytest.mark.parametrize("n,c,h,w,k,stride,pad,dt", [
+    (4, 64, 112, 112, 3, 2, 1, "bf16"),   # the ResNet max pool
+    (3, 24, 9, 7, 3, 2, 1, "f16"),        # ragged H, W; 24 channels
+    (2, 5, 8, 8, 2, 2, 0, "bf16"),        # 5 channels stored as 8; 2x2/2
+    (1, 16, 5, 6, 3, 1, 1, "bf16"),       # stride 1
+])
+def test_maxpool_nhwc_bit_exact(gpu, n, c, h, w, k, stride, pad, dt):
+    import oracle as orc
+    from omnimatchdeeplearningtool_b200 import _lib
+    from omnimatchdeeplearningtool_b200._lib import call, lib
+    from omnimatchdeeplearningtool_b200.backend import DeviceBuffer
+    dtype = _lib.DTYPE_BF16 if dt == "bf16" else _lib.DTYPE_F16
+    rng = np.random.Generator(np.random.PCG64(40 + h + c))
+    x = rng.standard_normal((n, c, h, w), dtype=np.float32) * 3
+    cs = int(lib.omCudaStoredChannels(c))
+    din = _to_nhwc(x, cs, dtype)
+    p, q = (h + 2 * pad - k) // stride + 1, (w + 2 * pad - k) // stride + 1
+    out = DeviceBuffer(n * p * q * cs * 2)
+    _KEEP.append(out)
+    call("omCudaMaxPool2dNhwc", din.ptr, out.ptr, n, h, w, cs, k, stride, pad, dtype)
+    got = _from_nhwc(out, n, c, p, q, cs, dtype)
+    want = orc.maxpool(_round16(x, dt), k, stride, pad)
+    assert gpu.kernel_error() == 0
+    assert np.array_equal(got, want)
+
+
+@pytest.mark.parametrize("n,c,h,w,dt", [(4, 2048, 7, 7, "bf16"), (3, 40, 5, 3, "f16")])
+def test_global_avgpool_nhwc(gpu, n, c, h, w, dt):
+    import oracle as orc
+    from omnimatchdeeplearningtool_b200 import _lib
+    from omnimatchdeeplearningtool_b200._lib import call, lib
+    from omnimatchdeeplearningtool_b200.backend import DeviceBuffer
+    dtype = _lib.DTYPE_BF16 if dt == "bf16" else _lib.DTYPE_F16
+    rng = np.random.Generator(np.random.PCG64(70 + c))
+    x = np.abs(rng.standard_normal((n, c, h, w), dtype=np.float32))
+    cs = int(lib.omCudaStoredChannels(c))
+    din = _to_nhwc(x, cs, dtype)
+    out = DeviceBuffer(n * cs * 4)
+    _KEEP.append(out)
+    call("omCudaGlobalAvgPoolNhwc", din.ptr, out.ptr, n, h * w, cs, dtype, _lib.DTYPE_F32)
+    got = out.to_numpy((n, cs))[:, :c]
+    want = orc.global_avgpool(_round16(x, dt)).reshape(n, c)
+    assert gpu.kernel_error() == 0
+    assert rel_err(got, want) <= 1e-5
+
+
+@pytest.mark.parametrize("n,c,h,k,stride,dt", [(2, 144, 28, 3, 2, "f16"), (3, 32, 15, 3, 1, "bf16")])
+def test_depthwise_nhwc(gpu, n, c, h, k, stride, dt):
+    import oracle as orc
+    from omnimatchdeeplearningtool_b200 import _lib
+    from omnimatchdeeplearningtool_b200._lib import call, lib
+    from omnimatchdeeplearningtool_b200.backend import DeviceBuffer
+    dtype = _lib.DTYPE_BF16 if dt == "bf16" else _lib.DTYPE_F16
+    rng = np.random.Generator(np.random.PCG64(90 + c))
+    x = rng.standard_normal((n, c, h, h), dtype=np.float32)
+    wt = (rng.standard_normal((c, 1, k, k)) * 0.5).astype(np.float32)
+    g = rng.uniform(0.5, 1.5, c).astype(np.float32)
+    b = (rng.standard_normal(c) * 0.1).astype(np.float32)
+    mu = (rng.standard_normal(c) * 0.1).astype(np.float32)
+    var = rng.uniform(0.5, 1.5, c).astype(np.float32)
+    pad = k // 2
+    cs = int(lib.omCudaStoredChannels(c))
+    din = _to_nhwc(x, cs, dtype)
+    bufs = [DeviceBuffer.from_numpy(a) for a in (wt, g, b, mu, var)]
+    packed, bias = DeviceBuffer(k * k * cs * 4), DeviceBuffer(cs * 4)
+    _KEEP.extend(bufs + [packed, bias])
+    call("omCudaPackDepthwiseWeight", *[t.ptr for t in bufs], 1e-5, packed.ptr, bias.ptr, c, k, k, cs)
+    p = (h + 2 * pad - k) // stride + 1
+    out = DeviceBuffer(n * p * p * cs * 2)
+    _KEEP.append(out)
+    call("omCudaDepthwiseConv2dNhwc", din.ptr, packed.ptr, bias.ptr, out.ptr, n, h, h, cs, k, k,
+         stride, pad, 2, dtype)
+    got = _from_nhwc(out, n, c, p, p, cs, dtype)
+    scale = g / np.sqrt(var + 1e-5)
+    want = orc.relu6(orc.conv2d(_round16(x, dt), wt * scale[:, None, None, None], b - mu * scale,
+                                stride, pad, groups=c))
+    assert gpu.kernel_error() == 0
+    assert rel_err(got, want) <= 1e-2
+
+
+def test_add_act_nhwc(gpu):
+    from omnimatchdeeplearningtool_b200 import _lib
+    from omnimatchdeeplearningtool_b200._lib import call
+    from omnimatchdeeplearningtool_b200.backend import DeviceBuffer
+    rng = np.random.Generator(np.random.PCG64(5))
+    a = rng.standard_normal((3, 8, 5, 7), dtype=np.float32)
+    bb = rng.standard_normal((3, 8, 5, 7), dtype=np.float32)
+    da, db = _to_nhwc(a, 8, _lib.DTYPE_BF16), _to_nhwc(bb, 8, _lib.DTYPE_BF16)
+    out = DeviceBuffer(a.size * 2)
+    _KEEP.append(out)
+    call("omCudaAddActNhwc", da.ptr, db.ptr, out.ptr, a.size, 1, _lib.DTYPE_BF16)
+    got = _from_nhwc(out, 3, 8, 5, 7, 8, _lib.DTYPE_BF16)
+    want = _round16(np.maximum(_round16(a, "bf16") + _round16(bb, "bf16"), 0), "bf16")
+    assert gpu.kernel_error() == 0
+    assert np.array_equal(got, want)
