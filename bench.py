@@ -129,6 +129,14 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def _host_threads() -> int:
+    """Host cores this process may run on."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def _reference_cpu(batch: int, iters_min: int, seconds: float):
     """The reference engine's CPU ResNet-50 forward on `batch` images (or the oracle port
     when the reference library was not built). Returns (images/s, kind, cores, sample)."""
@@ -139,7 +147,8 @@ def _reference_cpu(batch: int, iters_min: int, seconds: float):
     net = synth.resnet_spec(50)
     w = synth.make_weights(net)
     x = synth.normal_input(batch)
-    cores = os.cpu_count() or 1
+    cores = _host_threads()
+    orc.set_threads(cores)
     h = orc.ref_model(1, 1000, w, net)
     out = np.empty((batch, 1000), np.float32)
     if h is not None:
@@ -277,6 +286,8 @@ def run_reference(args, world, rank, dist):
     w = synth.make_weights(net)
     batch = args.ref_batch
     x = synth.normal_input(batch)
+    cores = _host_threads()
+    orc.set_threads(cores)
     h = orc.ref_model(1, 1000, w, net)
     out = np.empty((batch, 1000), np.float32)
     if h is not None:
@@ -292,7 +303,6 @@ def run_reference(args, world, rank, dist):
         run()
     dt = time.perf_counter() - t0
     v = args.steps * batch / dt
-    cores = os.cpu_count() or 1
     line = {
         "impl": "reference", "metric": METRIC, "value": v, "unit": "images/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
@@ -301,7 +311,8 @@ def run_reference(args, world, rank, dist):
         "config": {"workload": f"resnet50 inference (reference CPUBackend, fp32), batch {batch} "
                                "per step at 224x224", "batch": batch},
         "cpu_baseline": {"value": v, "unit": "images/s", "cores": cores, "kind": kind,
-                         "sample": f"ResNet-50 fp32 forward, batch {batch} per step"},
+                         "sample": f"ResNet-50 fp32 forward, batch {batch} per step, "
+                                   f"OMP threads={cores}"},
         "e2e": {"value": v, "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)

@@ -45,6 +45,7 @@ float oracle_cross_entropy(const float* p, const float* onehot, int N, int C);
 void oracle_ce_softmax_backward(const float* p, const float* onehot, float* grad, int N, int C);
 void oracle_sgd_step(float* param, const float* grad, float* vel, size_t n, float lr,
                      float momentum);
+void oracle_set_num_threads(int n);
 #ifdef __cplusplus
 }
 #endif

@@ -53,6 +53,8 @@ def _load_oracle():
         f = getattr(L, n)
         f.argtypes = a
         f.restype = c_float if n == "oracle_cross_entropy" else None
+    L.oracle_set_num_threads.argtypes = [I]
+    L.oracle_set_num_threads.restype = None
     return L
 
 
@@ -95,6 +97,10 @@ def ref():
         for n, a in sigs.items():
             f = getattr(L, n)
             f.argtypes = a
+        L.omref_set_num_threads.argtypes = [I]
+        L.omref_set_num_threads.restype = None
+        L.omref_get_max_threads.argtypes = []
+        L.omref_get_max_threads.restype = c_int
         L.omref_model_create.restype = c_void_p
         L.omref_cross_entropy.restype = c_float
         L.omref_model_train_step.restype = c_float
@@ -103,6 +109,15 @@ def ref():
             getattr(L, n).restype = c_int
         _REF = L
     return _REF
+
+
+def set_threads(n: int) -> None:
+    """OpenMP threads for the oracle and, when built, the reference engine (a process launcher
+    such as torchrun may have set OMP_NUM_THREADS=1)."""
+    O.oracle_set_num_threads(int(n))
+    L = ref()
+    if L is not None:
+        L.omref_set_num_threads(int(n))
 
 
 def _p(a):

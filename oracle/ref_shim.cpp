@@ -12,6 +12,7 @@
 // own ResNet18/ResNet50 classes use a CIFAR stem (om.engine.resnet.ixx:195-197,
 // om.engine.resnet50.ixx:205).
 #include <cmath>
+#include <omp.h>
 namespace std { using ::sqrtf; }  // om.engine.tensor_ops.ixx:901 names std::sqrtf
 
 #include "om.hal.cpu_backend.hpp"
@@ -305,5 +306,9 @@ float omref_model_train_step(void* h, const float* x, const float* onehot, int N
     if (apply_sgd) m->sgd->step();
     return lv;
 }
+
+// OpenMP threads for the reference engine's parallel loops (a launcher may have set 1).
+void omref_set_num_threads(int n) { omp_set_num_threads(n); }
+int omref_get_max_threads(void) { return omp_get_max_threads(); }
 
 }  // extern "C"
