@@ -236,6 +236,74 @@ def run_train(args, world, rank, local, dist):
     fnet.close()
 
 
+def run_sweep(args, world, rank, local, dist):
+    """Config 2: one conv2d + BatchNorm2d (eval) + ReLU layer per shape -- 3x3 s1 p1 and 1x1 s1,
+    C = K in {64,128,256,512}, H = W in {56,28,14,7}, N = 32 -- in fp32, bf16 and fp16. Each
+    timed run is preceded by a 256 MB write that flushes L2; CUDA events bracket the layer
+    alone. Parity of the same layers is checked in tests/test_gpu_conv_sweep.py."""
+    import torch
+    from omnimatchdeeplearningtool_b200 import backend, synth
+    from omnimatchdeeplearningtool_b200._lib import call
+    from omnimatchdeeplearningtool_b200.backend import DeviceBuffer
+    from omnimatchdeeplearningtool_b200.layers import ConvBnReluLayer
+
+    backend.init(local)
+    torch.cuda.set_device(local)
+    stream = torch.cuda.ExternalStream(backend.stream_handle(), device=local)
+    flush = DeviceBuffer(256 << 20)
+    peak_burst, _, _, peak_src = _peaks()
+    n = 32
+    rows = []
+    clocks = ClockSampler(local)
+    clocks.start()
+    launches0 = backend.launch_count()
+    for ks in (3, 1):
+        for c in (64, 128, 256, 512):
+            for h in (56, 28, 14, 7):
+                data = synth.conv_layer_data(c, h, ks, n, seed=900 + c + h + ks)
+                for dt in ("fp32", "bf16", "fp16"):
+                    layer = ConvBnReluLayer(*data, 1, ks // 2, dt)
+                    for _ in range(args.warmup):
+                        layer.run()
+                    total = 0.0
+                    with torch.cuda.stream(stream):
+                        for _ in range(args.steps):
+                            call("omCudaMemset", flush.ptr, 1, flush.nbytes)
+                            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                            e0.record()
+                            layer.run()
+                            e1.record()
+                            e1.synchronize()
+                            total += e0.elapsed_time(e1) / 1e3
+                    t = total / args.steps
+                    tf = layer.flops / t / 1e12
+                    rows.append({"k": ks, "c": c, "h": h, "dtype": dt, "us": round(t * 1e6, 2),
+                                 "tflops": round(tf, 1),
+                                 "frac_of_peak": round(tf / peak_burst, 3) if dt != "fp32" else None})
+                    layer.close()
+    clk = clocks.stop()
+    launches = backend.launch_count() - launches0
+    flush.free()
+    if rank == 0:
+        def agg(dt):
+            sel = [r for r in rows if r["dtype"] == dt]
+            fl = sum(2 * n * r["h"] * r["h"] * r["c"] * r["c"] * r["k"] * r["k"] for r in sel)
+            return fl / sum(r["us"] * 1e-6 for r in sel) / 1e12
+        line = {
+            "metric": "conv2d+BN+ReLU layer sweep TFLOP/s (config 2)", "value": agg("bf16"),
+            "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) inputs, He-normal weights)",
+            "config": {"workload": "32 layer shapes x {fp32, bf16, fp16}, N=32, L2 flushed "
+                                   "before every timed run", "batch": n},
+            "aggregate_tflops": {dt: round(agg(dt), 1) for dt in ("fp32", "bf16", "fp16")},
+            "peak": peak_burst, "peak_kind": f"bf16_tflops burst ({peak_src})",
+            "sweep": rows, "clocks": clk, "gpu_launches": launches,
+            "kernel_error": backend.kernel_error(),
+        }
+        print(json.dumps(line), flush=True)
+
+
 def run_mobilenet(args, world, rank, local, dist):
     """Config 5: MobileNet-style stack fp16 inference, batch 256 per GPU."""
     import torch
@@ -469,8 +537,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="r50-infer",
-                    choices=["r50-infer", "r18-train", "mobilenet-infer"],
-                    help="r50-infer is the headline metric; the others are configs 3 and 5")
+                    choices=["r50-infer", "r18-train", "mobilenet-infer", "conv-sweep"],
+                    help="r50-infer is the headline metric; the others are configs 3, 5 and 2")
     ap.add_argument("--ref-batch", type=int, default=4)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=BATCH,
@@ -487,6 +555,8 @@ def main():
             run_train(args, world, rank, local, dist)
         elif args.workload == "mobilenet-infer":
             run_mobilenet(args, world, rank, local, dist)
+        elif args.workload == "conv-sweep":
+            run_sweep(args, world, rank, local, dist)
         else:
             run_ours(args, world, rank, local, dist)
     finally:

@@ -389,7 +389,8 @@ class Fp32Net:
         return self.grad_flat + off * 4
 
     # ------------------------------------------------------------------ forward pieces
-    def _conv_bn(self, key, cv: ConvSpec, x: DeviceBuffer, n, c, hh, ww, relu: bool):
+    def _conv_bn(self, key, cv: ConvSpec, x: DeviceBuffer, n, c, hh, ww, relu: bool,
+                 train: bool = True):
         p = (hh + 2 * cv.pad - cv.k) // cv.stride + 1
         q = (ww + 2 * cv.pad - cv.k) // cv.stride + 1
         cnt = n * cv.cout * p * q
@@ -402,7 +403,7 @@ class Fp32Net:
         B.batchNorm2d(z.ptr, self.param[cv.bn + ".gamma"].ptr, self.param[cv.bn + ".beta"].ptr,
                       y.ptr, self.buffers[cv.bn + ".running_mean"].ptr,
                       self.buffers[cv.bn + ".running_var"].ptr, mean.ptr, invstd.ptr, n, cv.cout,
-                      p * q, 1e-5, 0.1, True)
+                      p * q, 1e-5, 0.1, train)
         out = y
         if relu:
             out = self._buf(key + ".a", cnt * 4)
@@ -411,15 +412,28 @@ class Fp32Net:
                    w=ww, p=p, q=q)
         return out, p, q, rec
 
+    def forward_eval(self, x_ptr: int) -> np.ndarray:
+        """Eval-mode forward (BatchNorm on the running statistics, which are left unchanged)
+        from device NCHW fp32 input; returns the host fp32 logits [N, classes]."""
+        self._forward(x_ptr, train=False)
+        out = np.empty((self.batch, self.net.classes), np.float32)
+        call("omCudaCopyD2H", out.ctypes.data, self.logits.ptr, out.nbytes)
+        return out
+
     def forward_backward(self, x_ptr: int, onehot_ptr: int, loss_ptr: int) -> None:
         """Train-mode forward from device NCHW fp32 input and one-hot targets, loss into
         loss_ptr (device float), gradients into the flat gradient buffer (overwritten)."""
+        st = self._forward(x_ptr, train=True)
+        self._loss_backward(st, onehot_ptr, loss_ptr)
+
+    def _forward(self, x_ptr: int, train: bool) -> dict:
+        """Forward to the logits (self.logits); returns what the backward pass needs."""
         net, n = self.net, self.batch
         recs = []
         x = _Ptr(x_ptr)
         cur, c, hh, ww = x, 3, self.h, self.w
         for i, cv in enumerate(net.stem):
-            cur, hh, ww, rec = self._conv_bn(f"stem{i}", cv, cur, n, c, hh, ww, True)
+            cur, hh, ww, rec = self._conv_bn(f"stem{i}", cv, cur, n, c, hh, ww, True, train)
             c = cv.cout
             recs.append(rec)
         pool_in, pc, ph, pw = cur, c, hh, ww
@@ -433,12 +447,14 @@ class Fp32Net:
             inp, ic, ih, iw = cur, c, hh, ww
             sc, ds_rec = inp, None
             if blk.downsample is not None:
-                sc, _, _, ds_rec = self._conv_bn(f"b{bi}.ds", blk.downsample, inp, n, ic, ih, iw, False)
+                sc, _, _, ds_rec = self._conv_bn(f"b{bi}.ds", blk.downsample, inp, n, ic, ih, iw,
+                                                 False, train)
             main = []
             out, oc, oh, ow = inp, ic, ih, iw
             for j, cv in enumerate(blk.convs):
                 last = j == len(blk.convs) - 1
-                out, oh, ow, rec = self._conv_bn(f"b{bi}.c{j}", cv, out, n, oc, oh, ow, not last)
+                out, oh, ow, rec = self._conv_bn(f"b{bi}.c{j}", cv, out, n, oc, oh, ow, not last,
+                                                 train)
                 oc = cv.cout
                 main.append(rec)
             cnt = n * oc * oh * ow
@@ -456,10 +472,19 @@ class Fp32Net:
         B.matmul(feat.ptr, self.param["fc.weight"].ptr, logits.ptr, n, c, K)
         logits_b = self._buf("logits_b", n * K * 4)
         B.addBias(logits.ptr, self.param["fc.bias"].ptr, logits_b.ptr, n, K, 1)
+        self.logits = logits_b
+        return dict(recs=recs, pool=(pc, ph, pw, P, idx), blocks=blocks, feat=feat, c=c, hh=hh,
+                    ww=ww)
+
+    def _loss_backward(self, st: dict, onehot_ptr: int, loss_ptr: int) -> None:
+        """Softmax cross-entropy on self.logits, then the backward pass of every node."""
+        n, K = self.batch, self.net.classes
+        recs, blocks, feat, c, hh, ww = (st[k] for k in ("recs", "blocks", "feat", "c", "hh", "ww"))
+        pc, ph, pw, P, idx = st["pool"]
+        logits_b = self.logits
         prob = self._buf("prob", n * K * 4)
         B.softmax(logits_b.ptr, prob.ptr, n, K)
         B.crossEntropyForward(prob.ptr, onehot_ptr, loss_ptr, n, K)
-        self.logits = logits_b
 
         # ---------------------------------------------------------------- backward
         dlog = self._buf("dlogits", n * K * 4)

@@ -219,3 +219,17 @@ def conv_flops(net: NetSpec, h: int = 224, w: int = 224) -> int:
             conv(blk.downsample, h0, w0)
     total += 2 * net.fc_in * net.classes
     return total
+
+
+def conv_layer_data(c: int, h: int, ks: int, n: int, seed: int):
+    """Config 2's single conv2d + BatchNorm2d + ReLU layer with C = K = c on an h x h input:
+    N(0,1) input, He-normal weights, BN gamma U(0.5,1.5), beta N(0,0.1), running mean N(0,0.1),
+    running var U(0.5,1.5), all from one seed. Returns (x, w, gamma, beta, mean, var)."""
+    rng = np.random.Generator(np.random.PCG64(seed))
+    x = rng.standard_normal((n, c, h, h), dtype=np.float32)
+    w = (rng.standard_normal((c, c, ks, ks)) * np.sqrt(2.0 / (c * ks * ks))).astype(np.float32)
+    g = rng.uniform(0.5, 1.5, c).astype(np.float32)
+    b = (rng.standard_normal(c) * 0.1).astype(np.float32)
+    mu = (rng.standard_normal(c) * 0.1).astype(np.float32)
+    var = rng.uniform(0.5, 1.5, c).astype(np.float32)
+    return x, w, g, b, mu, var

@@ -1,4 +1,7 @@
-"""Config 3 parity: the fp32 ResNet-18 training step (forward with batch-statistics BN,
+"""Configs 1 and 3, the fp32 ResNet-18 through the reference-named C ABI.
+
+Config 1 (inference, eval-mode BN) is checked at the end of this file. Config 3 parity: the fp32
+ResNet-18 training step (forward with batch-statistics BN,
 softmax cross-entropy, backward, SGD momentum 0.9, lr 0.01) through the reference-named C ABI,
 against the CPU oracle's training step on the same seeded weights, inputs and labels.
 
@@ -69,3 +72,31 @@ def test_resnet18_training_step_config3(gpu):
     assert np.median(errs) <= np.median(ref), (np.median(errs), np.median(ref))
     assert errs.max() <= ref.max(), (errs.max(), ref.max())
     assert rel_err(new_fc, ow["fc.weight"]) <= 1e-4
+
+
+def test_config1_resnet18_fp32_inference(gpu):
+    """Config 1: ResNet-18 fp32 inference, batch 8, the normalised U[0,1) image input, eval-mode
+    BatchNorm on the seeded running statistics, through the reference-layout fp32 entry points
+    (omCudaConv2d, omCudaBatchNorm2d, ...): 1000 logits within max|a-b|/max|b| <= 1e-4 of the
+    oracle, identical top-1."""
+    import oracle as orc
+    from omnimatchdeeplearningtool_b200 import synth
+    from omnimatchdeeplearningtool_b200.backend import DeviceBuffer
+    from omnimatchdeeplearningtool_b200.plan import Fp32Net
+    net = synth.resnet_spec(18, 1000)
+    w = synth.make_weights(net)
+    x = synth.imagenet_input(8)
+    want = orc.forward(net, w, x)
+    fnet = Fp32Net(net, w, 8, 224, 224)
+    dx = DeviceBuffer.from_numpy(x)
+    try:
+        got = fnet.forward_eval(dx.ptr)
+        # eval mode leaves the running statistics untouched: a second pass gives the same bits
+        again = fnet.forward_eval(dx.ptr)
+    finally:
+        fnet.close()
+        dx.free()
+    assert gpu.kernel_error() == 0
+    assert np.array_equal(got, again)
+    assert rel_err(got, want) <= 1e-4, rel_err(got, want)
+    assert np.array_equal(got.argmax(1), want.argmax(1))
