@@ -142,9 +142,10 @@ __global__ void maxpool_nhwc_kernel(const uint4* __restrict__ in, uint4* __restr
         const int s1 = (W - w0) < k ? (W - w0) : k;
         T2 m[4] = {lowest, lowest, lowest, lowest};
         for (int r = r0; r < r1; ++r) {
-            const uint4* src = img + ((size_t)(h0 + r) * W + w0) * C8 + c8;
+            // first in-image pixel of the window row; the pointer never leaves the image
+            const uint4* src = img + ((size_t)(h0 + r) * W + (w0 + s0)) * C8 + c8;
             for (int s = s0; s < s1; ++s) {
-                uint4 v = __ldg(src + (size_t)s * C8);
+                uint4 v = __ldg(src + (size_t)(s - s0) * C8);
                 const T2* v2 = reinterpret_cast<const T2*>(&v);
 #pragma unroll
                 for (int j = 0; j < 4; ++j) m[j] = __hmax2(m[j], v2[j]);
@@ -201,40 +202,44 @@ __global__ void gap_nhwc_kernel(const uint4* __restrict__ in, void* __restrict__
 }
 
 // ---------------------------------------------------------------- depthwise conv
-// packed weight: fp32 [R*S, Cs] (BN scale folded), bias fp32 [Cs]. One thread per output
-// pixel and 8-channel group.
+// packed weight: fp32 [R*S, Cs] (BN scale folded), bias fp32 [Cs]. One block per output row
+// (n, p); its threads walk the row's (q, 8-channel group) items with 32-bit indices.
 template <int DT>
 __global__ void depthwise_nhwc_kernel(const uint4* __restrict__ in, const float* __restrict__ wpk,
                                       const float* __restrict__ bias, uint4* __restrict__ out,
-                                      int N, int H, int W, int C8, int P, int Q, int R, int S,
+                                      int H, int W, int C8, int P, int Q, int R, int S,
                                       int stride, int pad, int act) {
     using H16 = Half16<DT>;
-    long long total = (long long)N * P * Q * C8;
     const int Cs = C8 * 8;
-    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
-         i += (long long)gridDim.x * blockDim.x) {
-        int c8 = (int)(i % C8);
-        long long pix = i / C8;
-        int q = (int)(pix % Q);
-        long long t = pix / Q;
-        int p = (int)(t % P);
-        int n = (int)(t / P);
+    const int row = blockIdx.x;          // n * P + p
+    const int n = row / P;
+    const int p = row - n * P;
+    const int h0 = p * stride - pad;
+    const int r0 = h0 < 0 ? -h0 : 0;
+    const int r1 = (H - h0) < R ? (H - h0) : R;
+    const uint4* img = in + (size_t)n * H * W * C8;
+    uint4* orow = out + (size_t)row * Q * C8;
+    for (int i = threadIdx.x; i < Q * C8; i += blockDim.x) {
+        const int q = i / C8;
+        const int c8 = i - q * C8;
+        const int w0 = q * stride - pad;
+        const int s0 = w0 < 0 ? -w0 : 0;
+        const int s1 = (W - w0) < S ? (W - w0) : S;
         float acc[8];
         const float4* b4 = reinterpret_cast<const float4*>(bias + c8 * 8);
-        float4 b0 = b4[0], b1 = b4[1];
+        float4 b0 = __ldg(b4), b1 = __ldg(b4 + 1);
         acc[0] = b0.x; acc[1] = b0.y; acc[2] = b0.z; acc[3] = b0.w;
         acc[4] = b1.x; acc[5] = b1.y; acc[6] = b1.z; acc[7] = b1.w;
-        for (int r = 0; r < R; ++r) {
-            int ih = p * stride - pad + r;
-            if (ih < 0 || ih >= H) continue;
-            for (int s = 0; s < S; ++s) {
-                int iw = q * stride - pad + s;
-                if (iw < 0 || iw >= W) continue;
-                uint4 v = in[(((long long)n * H + ih) * W + iw) * C8 + c8];
+        for (int r = r0; r < r1; ++r) {
+            // first in-image pixel of the window row; the pointer never leaves the image
+            const uint4* src = img + ((size_t)(h0 + r) * W + (w0 + s0)) * C8 + c8;
+            const float* wr = wpk + (size_t)(r * S) * Cs + c8 * 8;
+            for (int s = s0; s < s1; ++s) {
+                uint4 v = __ldg(src + (size_t)(s - s0) * C8);
                 const typename H16::T2* v2 = reinterpret_cast<const typename H16::T2*>(&v);
-                const float4* w4 = reinterpret_cast<const float4*>(wpk + (long long)(r * S + s) * Cs + c8 * 8);
-                float4 w0 = w4[0], w1 = w4[1];
-                float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+                const float4* w4 = reinterpret_cast<const float4*>(wr + (size_t)s * Cs);
+                float4 wa = __ldg(w4), wb = __ldg(w4 + 1);
+                float wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     float2 f = H16::unpack(v2[j]);
@@ -248,7 +253,7 @@ __global__ void depthwise_nhwc_kernel(const uint4* __restrict__ in, const float*
 #pragma unroll
         for (int j = 0; j < 4; ++j)
             o2[j] = H16::pack(apply_act(acc[2 * j], act), apply_act(acc[2 * j + 1], act));
-        out[i] = o;
+        orow[i] = o;
     }
 }
 
@@ -421,15 +426,16 @@ extern "C" int omCudaDepthwiseConv2dNhwc(const void* pIn, const float* pPacked, 
         return OM_ERR_INVALID;
     int P = (nH + 2 * nPad - nKH) / nStride + 1, Q = (nW + 2 * nPad - nKW) / nStride + 1;
     if (P <= 0 || Q <= 0) return OM_ERR_INVALID;
-    long long total = (long long)nN * P * Q * (nCs / 8);
-    int grid = ew_grid(c, total, 256);
+    const long long rows = (long long)nN * P;
+    if (rows >= (1LL << 31) || (long long)Q * (nCs / 8) >= (1LL << 31)) return OM_ERR_UNSUPPORTED;
+    const int threads = Q * (nCs / 8) >= 256 ? 256 : 128;
     if (nDtype == OM_DTYPE_BF16)
-        depthwise_nhwc_kernel<OM_DTYPE_BF16><<<grid, 256, 0, c->compute>>>(
-            static_cast<const uint4*>(pIn), pPacked, pBias, static_cast<uint4*>(pOut), nN, nH, nW,
+        depthwise_nhwc_kernel<OM_DTYPE_BF16><<<(unsigned)rows, threads, 0, c->compute>>>(
+            static_cast<const uint4*>(pIn), pPacked, pBias, static_cast<uint4*>(pOut), nH, nW,
             nCs / 8, P, Q, nKH, nKW, nStride, nPad, nAct);
     else if (nDtype == OM_DTYPE_F16)
-        depthwise_nhwc_kernel<OM_DTYPE_F16><<<grid, 256, 0, c->compute>>>(
-            static_cast<const uint4*>(pIn), pPacked, pBias, static_cast<uint4*>(pOut), nN, nH, nW,
+        depthwise_nhwc_kernel<OM_DTYPE_F16><<<(unsigned)rows, threads, 0, c->compute>>>(
+            static_cast<const uint4*>(pIn), pPacked, pBias, static_cast<uint4*>(pOut), nH, nW,
             nCs / 8, P, Q, nKH, nKW, nStride, nPad, nAct);
     else
         return OM_ERR_UNSUPPORTED;

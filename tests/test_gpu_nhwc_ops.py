@@ -97,7 +97,9 @@ def test_global_avgpool_nhwc(gpu, n, c, h, w, dt):
     assert rel_err(got, want) <= 1e-5
 
 
-@pytest.mark.parametrize("n,c,h,k,stride,dt", [(2, 144, 28, 3, 2, "f16"), (3, 32, 15, 3, 1, "bf16")])
+@pytest.mark.parametrize("n,c,h,k,stride,dt", [(2, 144, 28, 3, 2, "f16"), (3, 32, 15, 3, 1, "bf16"),
+                                                (2, 40, 13, 5, 2, "bf16"),   # generic window
+                                                (1, 2048, 9, 3, 1, "f16")])  # C/8 = 256 threads
 def test_depthwise_nhwc(gpu, n, c, h, k, stride, dt):
     import oracle as orc
     from omnimatchdeeplearningtool_b200 import _lib
