@@ -326,13 +326,20 @@ __device__ __forceinline__ void store_chunk_f32(const Params& p, int m, int n0,
     }
 }
 
+// Mode-specific shared memory after the epilogue buffers: the stem's patch buffers, or, at two
+// CTAs per SM (epilogue-bound layers), each epilogue warp's copy of the tile's bias.
+template <int BN, int MODE, int OCC>
+__host__ __device__ constexpr int extra_bytes() {
+    return MODE == MODE_STEM ? STEM_EXTRA_BYTES : (OCC == 2 ? NUM_EPI_WARPS * BN * 4 : 0);
+}
+
 template <int BN, int MODE, int DT, int OCC, int MT>
 __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GATHER_WARPS : NUM_THREADS, OCC)
     conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmOut,
                    const __grid_constant__ CUtensorMap tmRes, const Params p) {
     static_assert(MT == 1 || (MODE == MODE_SW128 && BN <= 128 && OCC == 1), "MT = 2 tiles");
-    using C = Cfg<BN, OCC, MODE == MODE_STEM ? STEM_EXTRA_BYTES : 0, MT>;
+    using C = Cfg<BN, OCC, extra_bytes<BN, MODE, OCC>(), MT>;
     constexpr int TM = BM * MT;   // output pixels per tile
     using H16 = Half16<DT>;
     constexpr int STAGES = C::STAGES;
@@ -344,7 +351,7 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
     uint8_t* sB = smem + STAGES * C::A_BYTES;
     uint8_t* sEpi = sB + STAGES * C::B_STAGE_BYTES;
     uint8_t* sExtra = sEpi + EPI_BYTES;
-    uint64_t* full = reinterpret_cast<uint64_t*>(sExtra + (MODE == MODE_STEM ? STEM_EXTRA_BYTES : 0));
+    uint64_t* full = reinterpret_cast<uint64_t*>(sExtra + extra_bytes<BN, MODE, OCC>());
     uint64_t* empty = full + STAGES;
     uint64_t* tfull = empty + STAGES;
     uint64_t* tempty = tfull + 2;
@@ -560,6 +567,10 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
         const bool has_res = use_tma && p.residual != nullptr;
         const bool clamp = p.act != OM_ACT_NONE;
         const float act_hi = p.act == OM_ACT_RELU6 ? 6.f : INFINITY;
+        // at two CTAs per SM the tile's bias is copied once into this warp's shared memory and
+        // read as broadcast float4s; otherwise one value per lane is broadcast by shuffles
+        constexpr bool BIAS_SMEM = OCC == 2;
+        float* sbias = reinterpret_cast<float*>(sExtra) + ew * BN;
         uint32_t g = 0;       // chunks started by this warp; chunk g uses sub-tile g % EPI_BUFS
         uint32_t rph = 0;     // per sub-tile: parity of its next residual load
         uint32_t rpend = 0;   // per sub-tile: a residual load is in flight
@@ -592,17 +603,33 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
             const bool res_here = has_res && !dead;
             const int rem_cols = p.K - nbase;
             const int nvalid = rem_cols >= BN ? NCH : (rem_cols + 31) / 32;  // chunks with n0 < K
+            // residuals requested before the accumulator is ready: every chunk's when the tile
+            // has at most EPI_BUFS chunks (their sub-tiles were last read by the stores of
+            // earlier chunks, all waited for), else the first two (those of chunks g-4, g-3)
+            const bool res_all = nvalid <= EPI_BUFS;
             if (res_here) {
-                // the first two chunks' residuals, requested before the accumulator is ready;
-                // their sub-tiles were last read by the stores of chunks g-4 and g-3
-                if (lane == 0) bulk_wait_read<2>();
+                if (lane == 0) {
+                    if (res_all) bulk_wait_read<0>();
+                    else bulk_wait_read<2>();
+                }
                 __syncwarp();
-                for (int c = 0; c < 2 && c < nvalid; ++c) {
+                const int first = res_all ? nvalid : 2;
+                for (int c = 0; c < first && c < nvalid; ++c) {
                     if (lane == 0) issue_res(g + c, nbase + c * 32, mw);
                     rpend |= 1u << ((g + c) % EPI_BUFS);
                 }
             }
-            float bnext = (p.bias && nbase + lane < p.K) ? __ldg(p.bias + nbase + lane) : 0.f;
+            float bnext = 0.f;
+            if (BIAS_SMEM) {
+#pragma unroll
+                for (int j = 0; j < NCH; ++j) {
+                    const int col = nbase + j * 32 + lane;
+                    sbias[j * 32 + lane] = (p.bias && col < p.K) ? __ldg(p.bias + col) : 0.f;
+                }
+                __syncwarp();
+            } else {
+                bnext = (p.bias && nbase + lane < p.K) ? __ldg(p.bias + nbase + lane) : 0.f;
+            }
             if (mt == 0) {
                 if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) {
                     ok = false;
@@ -618,9 +645,9 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
                 const uint32_t u = g % EPI_BUFS;
                 const int n0 = nbase + c * 32;
                 const float bcur = bnext;
-                if (c + 1 < nvalid)
+                if (!BIAS_SMEM && c + 1 < nvalid)
                     bnext = (p.bias && n0 + 32 + lane < p.K) ? __ldg(p.bias + n0 + 32 + lane) : 0.f;
-                if (res_here && c + 2 < nvalid) {
+                if (res_here && !res_all && c + 2 < nvalid) {
                     // sub-tile (g+2) % 4 was last read by the store of chunk g-2
                     if (lane == 0) bulk_wait_read<1>();
                     __syncwarp();
@@ -634,8 +661,21 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
                     continue;
                 }
                 float f[32];
+                if (BIAS_SMEM) {
+                    const float4* b4 = reinterpret_cast<const float4*>(sbias + c * 32);
 #pragma unroll
-                for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]) + __shfl_sync(0xffffffffu, bcur, j);
+                    for (int j = 0; j < 8; ++j) {
+                        const float4 bb = b4[j];
+                        f[4 * j] = __uint_as_float(v[4 * j]) + bb.x;
+                        f[4 * j + 1] = __uint_as_float(v[4 * j + 1]) + bb.y;
+                        f[4 * j + 2] = __uint_as_float(v[4 * j + 2]) + bb.z;
+                        f[4 * j + 3] = __uint_as_float(v[4 * j + 3]) + bb.w;
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        f[j] = __uint_as_float(v[j]) + __shfl_sync(0xffffffffu, bcur, j);
+                }
                 uint8_t* sb = ebuf + u * EPI_SUB_BYTES;
                 if (res_here) {
                     if (!mbar_wait(&rbar[u], (rph >> u) & 1u, abort_flag)) {
@@ -867,7 +907,7 @@ static int encode_epilogue_map(CUtensorMap* map, const void* base, int rows, int
 template <int BN, int MODE, int DT, int OCC, int MT = 1>
 static int launch(DeviceCtx* c, const CUtensorMap& ta, const CUtensorMap& tb,
                   const CUtensorMap& to, const CUtensorMap& tr, const Params& p) {
-    using Cf = Cfg<BN, OCC, MODE == MODE_STEM ? STEM_EXTRA_BYTES : 0, MT>;
+    using Cf = Cfg<BN, OCC, extra_bytes<BN, MODE, OCC>(), MT>;
     auto kern = conv_tc_kernel<BN, MODE, DT, OCC, MT>;
     static bool attr_set[64] = {false};
     if (!attr_set[c->device]) {
