@@ -574,6 +574,8 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
         uint32_t g = 0;       // chunks started by this warp; chunk g uses sub-tile g % EPI_BUFS
         uint32_t rph = 0;     // per sub-tile: parity of its next residual load
         uint32_t rpend = 0;   // per sub-tile: a residual load is in flight
+        // residual chunks of this warp's next tile already requested during the current one
+        int pre_next = 0;
         bool ok = true;
         int local = 0;
         // lane 0 only: request the residual of chunk h (sub-tile h % EPI_BUFS)
@@ -607,6 +609,8 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
             // has at most EPI_BUFS chunks (their sub-tiles were last read by the stores of
             // earlier chunks, all waited for), else the first two (those of chunks g-4, g-3)
             const bool res_all = nvalid <= EPI_BUFS;
+            const int pre = pre_next;   // chunks of this tile requested during the previous one
+            pre_next = 0;
             if (res_here) {
                 if (lane == 0) {
                     if (res_all) bulk_wait_read<0>();
@@ -614,9 +618,24 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
                 }
                 __syncwarp();
                 const int first = res_all ? nvalid : 2;
-                for (int c = 0; c < first && c < nvalid; ++c) {
+                for (int c = pre; c < first && c < nvalid; ++c) {
                     if (lane == 0) issue_res(g + c, nbase + c * 32, mw);
                     rpend |= 1u << ((g + c) % EPI_BUFS);
+                }
+            }
+            // Cross-tile residual prefetch (one sub-tile per tile, exactly EPI_BUFS chunks): while
+            // chunk c of this tile is processed, chunk c-1 of this warp's next tile is requested
+            // into the sub-tile chunk c-1 used, so its load overlaps the rest of this tile.
+            int nx_mw = 0, nx_nbase = 0;
+            bool chain = false;
+            if (MT == 1 && res_here && nvalid == EPI_BUFS) {
+                const int nt = tile + (int)gridDim.x;
+                if (nt < num_tiles) {
+                    const int nm = nt / p.num_n_tiles;
+                    nx_nbase = (nt - nm * p.num_n_tiles) * BN;
+                    nx_mw = nm * TM + quarter * 32;
+                    const int nrem = p.K - nx_nbase;
+                    chain = nx_mw < p.M && (nrem >= BN || (nrem + 31) / 32 == EPI_BUFS);
                 }
             }
             float bnext = 0.f;
@@ -656,6 +675,16 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
                 }
                 uint32_t v[32];
                 tmem_ld32(t_row + (uint32_t)(c * 32), v);
+                if (chain && c >= 1) {
+                    // sub-tile of chunk c-1 (g-1): its store was issued a chunk ago
+                    if (lane == 0) {
+                        bulk_wait_read<0>();
+                        issue_res(g - 1 + EPI_BUFS, nx_nbase + (c - 1) * 32, nx_mw);
+                    }
+                    __syncwarp();
+                    rpend |= 1u << ((g - 1) % EPI_BUFS);
+                    pre_next = c;
+                }
                 if (!use_tma) {
                     if (mw + lane < p.M) store_chunk_f32(p, mw + lane, n0, v);
                     continue;
