@@ -198,7 +198,7 @@ int omCudaConv2dBnAct(const void* pInput, const void* pPacked, const float* pBia
                       const void* pResidual, void* pOutput, int nBatch, int nH, int nW, int nCs,
                       int nCout, int nKH, int nKW, int nStride, int nPad, int nAct, int nDtype,
                       int nOutDtype);
-/* new: the image stem (KH * Cin <= 24, KW <= 8, stride 1 or 2) straight from the NCHW fp32
+/* new: the image stem (KH * Cin <= 24, KW <= 8, Cout <= 128, stride 1 or 2) from the NCHW fp32
  * image: out[n,p,q,k] = act(sum_{c,r,s} x[n,c,p*st-pad+r,q*st-pad+s] * W'[k,(c,r,s)] + bias[k]),
  * NHWC 16-bit output, W' from omCudaPackStemWeight (BN folded as in omCudaPackConvWeight).
  * Same tcgen05 kernel as omCudaConv2dBnAct; a first launch writes a 16-bit copy of the image

@@ -75,6 +75,10 @@ constexpr int STEM_PATCH_BYTES = 2 * STEM_BOX_W * STEM_MAX_ROWS * 2 + 256;  // 1
 static_assert(STEM_PATCH_BYTES % 128 == 0, "patch buffers stay 128-byte aligned");
 constexpr int STEM_PATCH_BUFS = 3;                     // two tiles' loads in flight
 constexpr int STEM_EXTRA_BYTES = STEM_PATCH_BUFS * STEM_PATCH_BYTES;
+// MODE_STEM tensor memory: the two accumulators (2 * BN columns, BN <= 128), then two A
+// buffers of up to 3 k-blocks (96 columns: 192 16-bit K elements per row) each.
+constexpr uint32_t STEM_TMEM_COLS = 512;
+constexpr int STEM_A_COLS = 96;
 constexpr unsigned long long OMB_WAIT_NS = 2000000000ull;  // 2 s per wait
 
 enum { MODE_SW128 = 0, MODE_INTERLEAVE = 1, MODE_STEM = 2 };
@@ -237,6 +241,28 @@ __device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
 }
+// MMA with the A operand in tensor memory (lanes = rows, 16-bit K pairs per 32-bit column)
+__device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc,
+                                          uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+// 16 consecutive 32-bit columns of this thread's TMEM lane
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+        "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
+        "r"(v[15])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
@@ -358,7 +384,9 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
     uint64_t* drain = tempty + 2;
     uint64_t* resfull = drain + 1;  // [NUM_EPI_WARPS][EPI_BUFS]
     uint64_t* patch_full = resfull + EPI_BUFS * NUM_EPI_WARPS;  // [STEM_PATCH_BUFS], MODE_STEM
-    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(patch_full + STEM_PATCH_BUFS);
+    uint64_t* a_full = patch_full + STEM_PATCH_BUFS;  // [2], MODE_STEM: A buffer written
+    uint64_t* a_empty = a_full + 2;                   // [2], MODE_STEM: A buffer consumed
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(a_empty + 2);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -366,8 +394,7 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < STAGES; ++i) {
-            // MODE_STEM: the producer's expect_tx arrival plus one per gather warp
-            mbar_init(&full[i], MODE == MODE_STEM ? 1 + NUM_GATHER_WARPS : 1);
+            mbar_init(&full[i], 1);
             mbar_init(&empty[i], 1);
         }
         for (int i = 0; i < 2; ++i) {
@@ -376,15 +403,21 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
         }
         for (int i = 0; i < EPI_BUFS * NUM_EPI_WARPS; ++i) mbar_init(&resfull[i], 1);
         for (int i = 0; i < STEM_PATCH_BUFS; ++i) mbar_init(&patch_full[i], 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&a_full[i], NUM_GATHER_WARPS);
+            mbar_init(&a_empty[i], 1);
+        }
         mbar_init(drain, 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         fence_async_smem();
     }
+    constexpr uint32_t TMEM_ALLOC = MODE == MODE_STEM ? STEM_TMEM_COLS : (uint32_t)C::TMEM_COLS;
+    static_assert(MODE != MODE_STEM || (BN <= 128 && OCC == 1), "stem TMEM layout");
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                          smem_u32(tmem_holder)),
-                     "r"((uint32_t)C::TMEM_COLS));
+                     "r"(TMEM_ALLOC));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     tc_fence_before();
@@ -402,7 +435,16 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
             uint32_t phase = 0;
             long long issued = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+            if (MODE == MODE_STEM) {
+                // the stem's packed weight (num_kb <= 3 k-blocks) stays resident in the first
+                // B stages for the whole kernel: one load, one barrier
+                mbar_expect_tx(&full[0], (uint32_t)(p.num_kb * C::B_STAGE_BYTES));
+                for (int kb = 0; kb < p.num_kb; ++kb)
+                    tma_load_2d(sB + kb * C::B_STAGE_BYTES, &tmB, &full[0], kb * BK, 0);
+                issued = 1;
+            }
+            for (int tile = blockIdx.x; tile < num_tiles && ok && MODE != MODE_STEM;
+                 tile += gridDim.x) {
                 const int m_tile = tile / p.num_n_tiles;
                 const int n_tile = tile - m_tile * p.num_n_tiles;
                 const int m0 = m_tile * TM;
@@ -432,11 +474,7 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
                     }
                     uint8_t* a_dst = sA + stage * C::A_BYTES;
                     uint8_t* b_dst = sB + stage * C::B_STAGE_BYTES;
-                    if (MODE == MODE_STEM) {
-                        // A comes from the gather warps; only the weights travel by TMA
-                        mbar_expect_tx(&full[stage], C::B_STAGE_BYTES);
-                        tma_load_2d(b_dst, &tmB, &full[stage], kb * BK, n0);
-                    } else if (MODE == MODE_SW128) {
+                    if (MODE == MODE_SW128) {
                         mbar_expect_tx(&full[stage], C::STAGE_BYTES);
                         tma_load_im2col(a_dst, &tmA, &full[stage], c0, wb, hb, img, (uint16_t)fs,
                                         (uint16_t)fr);
@@ -509,7 +547,33 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
             uint32_t phase = 0;
             bool ok = true;
             int local = 0;
-            for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+            if (MODE == MODE_STEM) {
+                // A from tensor memory (written by the gather warps, two buffers), B resident
+                ok = mbar_wait(&full[0], 0, abort_flag);
+                for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+                    const int acc = local & 1;
+                    const uint32_t par = (uint32_t)((local >> 1) & 1);
+                    if (!mbar_wait(&tempty[acc], par ^ 1, abort_flag) ||
+                        !mbar_wait(&a_full[acc], par, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+                    const uint32_t a_tmem = tmem_base + (uint32_t)(2 * BN + acc * STEM_A_COLS);
+                    for (int kb = 0; kb < p.num_kb; ++kb) {
+                        const uint64_t bd = bdesc0 + (uint64_t)(kb * (C::B_STAGE_BYTES >> 4));
+#pragma unroll
+                        for (int k = 0; k < BK / 16; ++k)
+                            tc_mma_ts(d_tmem, a_tmem + (uint32_t)(kb * 32 + k * 8), bd + k * B_K_STEP,
+                                      IDESC, (kb > 0 || k > 0) ? 1u : 0u);
+                    }
+                    tc_commit(&a_empty[acc]);
+                    tc_commit(&tfull[acc]);
+                }
+            }
+            for (int tile = blockIdx.x; tile < num_tiles && ok && MODE != MODE_STEM;
+                 tile += gridDim.x, ++local) {
                 const int acc = local & 1;
                 const uint32_t acc_phase = (uint32_t)((local >> 1) & 1);
                 if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag)) {
@@ -784,8 +848,10 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
         // at a named barrier (id 1) per tile, which also agrees on whether to stop.
         const int gw = warp - 2 - NUM_EPI_WARPS;
         const int gt = gw * 32 + lane;
-        const int row = (gw & 3) * 32 + lane;   // A row this thread builds
-        const int j0 = (gw >> 2) * 4;           // its first chunk in each k-block
+        // a warp writes only its TMEM lane quarter (warp % 4): A row = that quarter's 32 rows
+        const int row = (warp & 3) * 32 + lane;  // A row this thread builds
+        const int j0 = (gw >> 2) * 4;            // its first chunk in each k-block
+        const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
         const int RC = p.R * p.C;
         const int nbox = p.stride == 2 ? 2 : 1;
         const uint32_t box_bytes = (uint32_t)(STEM_BOX_W * RC * 2);
@@ -811,44 +877,46 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
                 tma_load_4d(dst + box1_off, &tmA, bar, q0 * p.stride + 128, pp * p.stride - p.pad, 0,
                             img);
         };
-        int stage = 0;
-        uint32_t phase = 0;
+        // Tile i's A goes to TMEM buffer i % 2 (columns 2*BN + (i % 2) * STEM_A_COLS, K pairs
+        // per column), once the MMAs of tile i-2 have consumed it.
         auto build = [&](int i) -> bool {
+            const int buf = i & 1;
+            if (!mbar_wait(&a_empty[buf], (uint32_t)(((i >> 1) & 1) ^ 1), abort_flag)) return false;
+            tc_fence_after();
             int rowid, q0;
             tile_row(i, rowid, q0);
             const bool row_ok = q0 + row < p.Q;
             const uint8_t* pb = sExtra + (i % STEM_PATCH_BUFS) * STEM_PATCH_BYTES;
+            const uint32_t a_col = tmem_base + lane_base + (uint32_t)(2 * BN + buf * STEM_A_COLS);
             for (int kb = 0; kb < p.num_kb; ++kb) {
-                if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) return false;
-                uint8_t* a_row = sA + stage * C::A_BYTES + row * 128;
+                uint32_t w16[16];
 #pragma unroll
                 for (int jj = 0; jj < 4; ++jj) {
-                    const int j = j0 + jj;
-                    const int t = kb * 8 + j;
-                    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+                    const int t = kb * 8 + j0 + jj;
+                    uint32_t w0 = 0, w1 = 0, w2 = 0, w3 = 0;
                     if (row_ok && t < RC) {
                         if (nbox == 2) {
                             const uint32_t* w = reinterpret_cast<const uint32_t*>(
                                 pb + (row >> 6) * box1_off + t * (STEM_BOX_W * 2)) + (row & 63);
-                            v = make_uint4(w[0], w[1], w[2], w[3]);
+                            w0 = w[0]; w1 = w[1]; w2 = w[2]; w3 = w[3];
                         } else {
                             const uint16_t* h = reinterpret_cast<const uint16_t*>(
                                 pb + t * (STEM_BOX_W * 2)) + row;
-                            v = make_uint4(h[0] | ((uint32_t)h[1] << 16), h[2] | ((uint32_t)h[3] << 16),
-                                           h[4] | ((uint32_t)h[5] << 16), h[6] | ((uint32_t)h[7] << 16));
+                            w0 = h[0] | ((uint32_t)h[1] << 16);
+                            w1 = h[2] | ((uint32_t)h[3] << 16);
+                            w2 = h[4] | ((uint32_t)h[5] << 16);
+                            w3 = h[6] | ((uint32_t)h[7] << 16);
                         }
                     }
-                    *reinterpret_cast<uint4*>(a_row + ((j ^ (row & 7)) << 4)) = v;
+                    w16[4 * jj] = w0; w16[4 * jj + 1] = w1; w16[4 * jj + 2] = w2; w16[4 * jj + 3] = w3;
                 }
-                // make this thread's generic-proxy smem writes visible to the tensor cores
-                fence_async_smem();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&full[stage]);
-                if (++stage == STAGES) {
-                    stage = 0;
-                    phase ^= 1;
-                }
+                tmem_st16(a_col + (uint32_t)(kb * 32 + j0 * 4), w16);
             }
+            // the stores are complete before the MMA issuer may read them
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&a_full[buf]);
             return true;
         };
         constexpr int NG = 32 * NUM_GATHER_WARPS;
@@ -892,7 +960,7 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
     tc_fence_after();
     if (warp == 1) {
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
-                     "r"((uint32_t)C::TMEM_COLS));
+                     "r"(TMEM_ALLOC));
     }
 }
 
@@ -979,7 +1047,9 @@ static int dispatch_bn(DeviceCtx* c, int bn, int occ, int mt, const CUtensorMap&
         case 32: return launch<32, MODE, DT, 1>(c, ta, tb, to, tr, p);
         case 64: return launch<64, MODE, DT, 1>(c, ta, tb, to, tr, p);
         case 128: return launch<128, MODE, DT, 1>(c, ta, tb, to, tr, p);
-        case 256: return launch<256, MODE, DT, 1>(c, ta, tb, to, tr, p);
+    }
+    if constexpr (MODE != MODE_STEM) {  // the stem keeps A in TMEM beside <= 128-wide tiles
+        if (bn == 256) return launch<256, MODE, DT, 1>(c, ta, tb, to, tr, p);
     }
     return OM_ERR_UNSUPPORTED;
 }
@@ -1202,7 +1272,7 @@ extern "C" int omCudaStemConvBnAct(const float* pInput, void* pWorkspace, const 
     if (nBatch <= 0 || nCin <= 0 || nH <= 0 || nW <= 0 || nCout <= 0 || nKH <= 0 || nKW <= 0 ||
         nStride <= 0 || nPad < 0)
         return OM_ERR_INVALID;
-    if (nKW > 8 || nCout % 8 != 0) return OM_ERR_UNSUPPORTED;
+    if (nKW > 8 || nCout % 8 != 0 || nCout > 128) return OM_ERR_UNSUPPORTED;
     if (nStride != 1 && nStride != 2) return OM_ERR_UNSUPPORTED;
     if (nKH * nCin > STEM_MAX_ROWS || nKH > 256 || nCin > 256) return OM_ERR_UNSUPPORTED;
     if (nDtype != OM_DTYPE_BF16 && nDtype != OM_DTYPE_F16) return OM_ERR_UNSUPPORTED;
