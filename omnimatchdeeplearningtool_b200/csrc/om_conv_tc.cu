@@ -59,13 +59,19 @@ namespace tc {
 constexpr int BM = 128;                 // output pixels per tile (TMEM lanes)
 constexpr int BK = 64;                  // K elements per pipeline stage
 constexpr int A_STAGE_BYTES = BM * BK * 2;
-constexpr int NUM_EPI_WARPS = 4;        // one per TMEM lane quarter
 constexpr int NUM_GATHER_WARPS = 8;     // MODE_STEM only
-constexpr int NUM_THREADS = 64 + 32 * NUM_EPI_WARPS;
 constexpr int EPI_SUB_BYTES = 32 * 32 * 2;             // one 32x32 16-bit sub-tile
-constexpr int EPI_BUFS = 4;                            // staging sub-tiles per epilogue warp
-constexpr int EPI_WARP_BYTES = EPI_BUFS * EPI_SUB_BYTES;
-constexpr int EPI_BYTES = NUM_EPI_WARPS * EPI_WARP_BYTES;
+// EW epilogue warps (4 or 16; EW / 4 per TMEM lane quarter), each with epi_bufs<EW>() 2 KB
+// staging sub-tiles; every CTA also has a producer warp and an MMA warp (and, for the stem,
+// NUM_GATHER_WARPS gather warps after the epilogue warps).
+template <int EW>
+__host__ __device__ constexpr int epi_bufs() { return EW == 4 ? 4 : 2; }
+template <int EW>
+__host__ __device__ constexpr int epi_bytes() { return EW * epi_bufs<EW>() * EPI_SUB_BYTES; }
+template <int MODE, int EW>
+__host__ __device__ constexpr int cta_threads() {
+    return 64 + 32 * EW + (MODE == 2 ? 32 * NUM_GATHER_WARPS : 0);
+}
 constexpr int MAX_DYN_SMEM = 232448;                   // 227 KB per CTA on sm_100
 // MODE_STEM input patch: per tile, C*R image rows of 136 16-bit columns, one box for stride 1
 // (columns q0 + [0, 135)), two for stride 2 (the second starting 128 columns later).
@@ -251,7 +257,11 @@ __device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint
         "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate));
 }
 // 16 consecutive 32-bit columns of this thread's TMEM lane
+// The tcgen05 .sync.aligned instructions must be executed by the whole warp together: every
+// helper reconverges the warp first (callers reach them after per-lane spin waits and
+// lane-0-only TMA issue).
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+    __syncwarp();
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
         "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
@@ -261,9 +271,11 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16
         : "memory");
 }
 __device__ __forceinline__ void tmem_wait_st() {
+    __syncwarp();
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+    __syncwarp();
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
         "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
@@ -310,12 +322,13 @@ __device__ __forceinline__ uint32_t sw64(int r, int j) {
 // stages and doubles the independent pipelines per SM; it is chosen for short-K, memory-bound
 // layers where one CTA cannot keep enough loads and stores in flight.
 // EXTRA = mode-specific shared memory after the epilogue buffers (the stem's patch buffers).
-template <int BN, int OCC, int EXTRA = 0, int MT = 1>
+template <int BN, int OCC, int EXTRA = 0, int MT = 1, int EW = 4>
 struct Cfg {
+    static constexpr int EPI_BYTES = epi_bytes<EW>();
     static constexpr int A_BYTES = MT * A_STAGE_BYTES;   // A bytes per stage
     static constexpr int B_STAGE_BYTES = BN * BK * 2;
     static constexpr int STAGE_BYTES = A_BYTES + B_STAGE_BYTES;
-    static constexpr int BAR_BYTES = 512;
+    static constexpr int BAR_BYTES = 1024;
     static constexpr int BUDGET = OCC == 1 ? MAX_DYN_SMEM : (233472 - 2048) / 2 - 1024;
     static constexpr int STAGES_RAW =
         (BUDGET - 1024 - BAR_BYTES - EPI_BYTES - EXTRA) / STAGE_BYTES;
@@ -352,20 +365,23 @@ __device__ __forceinline__ void store_chunk_f32(const Params& p, int m, int n0,
     }
 }
 
-// Mode-specific shared memory after the epilogue buffers: the stem's patch buffers, or, at two
-// CTAs per SM (epilogue-bound layers), each epilogue warp's copy of the tile's bias.
-template <int BN, int MODE, int OCC>
+// Mode-specific shared memory after the epilogue buffers: the stem's patch buffers, or, for
+// the epilogue-bound configurations (two CTAs per SM, or 16 epilogue warps), each epilogue
+// warp's copy of the tile's bias.
+template <int BN, int MODE, int OCC, int EW>
 __host__ __device__ constexpr int extra_bytes() {
-    return MODE == MODE_STEM ? STEM_EXTRA_BYTES : (OCC == 2 ? NUM_EPI_WARPS * BN * 4 : 0);
+    return MODE == MODE_STEM ? STEM_EXTRA_BYTES : ((OCC == 2 || EW > 4) ? EW * BN * 4 : 0);
 }
 
-template <int BN, int MODE, int DT, int OCC, int MT>
-__global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GATHER_WARPS : NUM_THREADS, OCC)
+template <int BN, int MODE, int DT, int OCC, int MT, int EW>
+__global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
     conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmOut,
                    const __grid_constant__ CUtensorMap tmRes, const Params p) {
     static_assert(MT == 1 || (MODE == MODE_SW128 && BN <= 128 && OCC == 1), "MT = 2 tiles");
-    using C = Cfg<BN, OCC, extra_bytes<BN, MODE, OCC>(), MT>;
+    static_assert(EW == 4 || (EW == 16 && OCC == 1 && MODE != MODE_STEM), "epilogue warps");
+    using C = Cfg<BN, OCC, extra_bytes<BN, MODE, OCC, EW>(), MT, EW>;
+    constexpr int EPI_BUFS = epi_bufs<EW>();
     constexpr int TM = BM * MT;   // output pixels per tile
     using H16 = Half16<DT>;
     constexpr int STAGES = C::STAGES;
@@ -376,14 +392,14 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
     uint8_t* sA = smem;
     uint8_t* sB = smem + STAGES * C::A_BYTES;
     uint8_t* sEpi = sB + STAGES * C::B_STAGE_BYTES;
-    uint8_t* sExtra = sEpi + EPI_BYTES;
-    uint64_t* full = reinterpret_cast<uint64_t*>(sExtra + extra_bytes<BN, MODE, OCC>());
+    uint8_t* sExtra = sEpi + C::EPI_BYTES;
+    uint64_t* full = reinterpret_cast<uint64_t*>(sExtra + extra_bytes<BN, MODE, OCC, EW>());
     uint64_t* empty = full + STAGES;
     uint64_t* tfull = empty + STAGES;
     uint64_t* tempty = tfull + 2;
     uint64_t* drain = tempty + 2;
-    uint64_t* resfull = drain + 1;  // [NUM_EPI_WARPS][EPI_BUFS]
-    uint64_t* patch_full = resfull + EPI_BUFS * NUM_EPI_WARPS;  // [STEM_PATCH_BUFS], MODE_STEM
+    uint64_t* resfull = drain + 1;  // [EW][EPI_BUFS]
+    uint64_t* patch_full = resfull + EPI_BUFS * EW;  // [STEM_PATCH_BUFS], MODE_STEM
     uint64_t* a_full = patch_full + STEM_PATCH_BUFS;  // [2], MODE_STEM: A buffer written
     uint64_t* a_empty = a_full + 2;                   // [2], MODE_STEM: A buffer consumed
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(a_empty + 2);
@@ -399,9 +415,9 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&tfull[i], 1);
-            mbar_init(&tempty[i], NUM_EPI_WARPS);
+            mbar_init(&tempty[i], EW);
         }
-        for (int i = 0; i < EPI_BUFS * NUM_EPI_WARPS; ++i) mbar_init(&resfull[i], 1);
+        for (int i = 0; i < EPI_BUFS * EW; ++i) mbar_init(&resfull[i], 1);
         for (int i = 0; i < STEM_PATCH_BUFS; ++i) mbar_init(&patch_full[i], 1);
         for (int i = 0; i < 2; ++i) {
             mbar_init(&a_full[i], NUM_GATHER_WARPS);
@@ -614,32 +630,36 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
             tc_commit(drain);
             if (!mbar_wait_drain(drain, 0)) atomicOr(p.err, ERRBIT_TC_DRAIN);
         }
-    } else if (warp < 2 + NUM_EPI_WARPS) {
+    } else if (warp < 2 + EW) {
         // ---------------------------------------------------------------- epilogue
-        // Each warp owns TMEM lane quarter `warp % 4` (32 output pixels) and four 2 KB staging
-        // sub-tiles used round-robin, one per 32-column chunk: the chunk's residual is brought
-        // into its sub-tile by TMA two chunks ahead, read, and overwritten in place by the
-        // output (each lane reads and writes only its own row), which a TMA store then writes
-        // out. The bias of the chunk's 32 columns is held one value per lane (loaded a chunk
-        // ahead) and broadcast with shuffles.
+        // Warp `warp` may read TMEM lane quarter warp % 4 (32 output pixels of each 128-row
+        // sub-tile); the EW / 4 warps of a quarter split the tile's 32-column chunks (sub-tile
+        // mt, chunk c; unit u = mt * NCH + c) round-robin: this warp takes u = slot, slot +
+        // EW / 4, ... Per chunk: tcgen05.ld -> + bias -> + residual -> clamp -> 16-bit ->
+        // staging sub-tile (64-byte swizzle) -> TMA store. The residual is brought into the
+        // chunk's staging sub-tile by TMA ahead of time (every chunk's at tile start when the
+        // warp's chunks fit its sub-tiles, also the next tile's while this one is processed;
+        // else two chunks ahead) and overwritten in place by the output (each lane reads and
+        // writes only its own row). The bias comes from a per-warp shared-memory copy of the
+        // tile's slice (epilogue-bound configurations) or one value per lane by shuffles.
+        constexpr int SLOTS = EW / 4;
+        constexpr int NCH = BN / 32;
+        constexpr int KMAX = (MT * NCH + SLOTS - 1) / SLOTS;   // chunks per warp per tile, max
         const int ew = warp - 2;
         const int quarter = warp & 3;  // TMEM lane quarter this warp may access
-        constexpr int NCH = BN / 32;
-        uint8_t* ebuf = sEpi + ew * EPI_WARP_BYTES;
+        const int slot = ew >> 2;
+        uint8_t* ebuf = sEpi + ew * (EPI_BUFS * EPI_SUB_BYTES);
         uint64_t* rbar = resfull + EPI_BUFS * ew;
         const bool use_tma = !p.out_f32;
         const bool has_res = use_tma && p.residual != nullptr;
         const bool clamp = p.act != OM_ACT_NONE;
         const float act_hi = p.act == OM_ACT_RELU6 ? 6.f : INFINITY;
-        // at two CTAs per SM the tile's bias is copied once into this warp's shared memory and
-        // read as broadcast float4s; otherwise one value per lane is broadcast by shuffles
-        constexpr bool BIAS_SMEM = OCC == 2;
+        constexpr bool BIAS_SMEM = OCC == 2 || EW > 4;
         float* sbias = reinterpret_cast<float*>(sExtra) + ew * BN;
         uint32_t g = 0;       // chunks started by this warp; chunk g uses sub-tile g % EPI_BUFS
         uint32_t rph = 0;     // per sub-tile: parity of its next residual load
         uint32_t rpend = 0;   // per sub-tile: a residual load is in flight
-        // residual chunks of this warp's next tile already requested during the current one
-        int pre_next = 0;
+        int pre_next = 0;     // live chunks of the next tile whose residual is already requested
         bool ok = true;
         int local = 0;
         // lane 0 only: request the residual of chunk h (sub-tile h % EPI_BUFS)
@@ -649,60 +669,83 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
             mbar_expect_tx(&rbar[u], EPI_SUB_BYTES);
             tma_load_2d(ebuf + u * EPI_SUB_BYTES, &tmRes, &rbar[u], col, row0);
         };
+        // this warp's live chunks of tile `t`: bit k set when unit slot + k * SLOTS exists,
+        // lies below Cout and in a sub-tile with output rows
+        auto live_mask = [&](int t, int& m_tile_o, int& nbase_o) -> uint32_t {
+            const int mtl = t / p.num_n_tiles;
+            m_tile_o = mtl;
+            nbase_o = (t - mtl * p.num_n_tiles) * BN;
+            const int rem = p.K - nbase_o;
+            const int nvalid = rem >= BN ? NCH : (rem + 31) / 32;
+            uint32_t mask = 0;
+#pragma unroll
+            for (int k = 0; k < KMAX; ++k) {
+                const int u = slot + k * SLOTS;
+                if (u >= MT * NCH) continue;
+                const int mt = u / NCH, c = u - (u / NCH) * NCH;
+                bool live = c < nvalid;
+                if (MODE == MODE_STEM) {
+                    const int srow = mtl / p.QT;
+                    live = live && (mtl - srow * p.QT) * BM + quarter * 32 < p.Q;
+                } else {
+                    live = live && mtl * TM + mt * BM + quarter * 32 < p.M;
+                }
+                if (live) mask |= 1u << k;
+            }
+            return mask;
+        };
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
             const int acc = local & 1;
             const uint32_t acc_phase = (uint32_t)((local >> 1) & 1);
-            const int m_tile = tile / p.num_n_tiles;
-            const int n_tile = tile - m_tile * p.num_n_tiles;
-          for (int mt = 0; mt < MT; ++mt) {
-            const int mw = m_tile * TM + mt * BM + quarter * 32;  // first output pixel of this warp
-            const int nbase = n_tile * BN;
-            // MODE_STEM: the tile is output row `srow` (= n*P + p), columns from `sq`
-            int srow = 0, sq = 0;
+            int m_tile, nbase;
+            const uint32_t lmask = live_mask(tile, m_tile, nbase);
+            const int nlive = __popc(lmask);
+            // MODE_STEM: the tile is output row `srow` (= n*P + p), columns from `sq0`
+            int srow = 0, sq0 = 0;
             if (MODE == MODE_STEM) {
                 srow = m_tile / p.QT;
-                sq = (m_tile - srow * p.QT) * BM + quarter * 32;
+                sq0 = (m_tile - srow * p.QT) * BM + quarter * 32;
             }
-            // a warp sub-tile wholly past the output (rows >= M, or stem columns >= Q) loads
-            // and stores nothing
-            const bool dead = MODE == MODE_STEM ? sq >= p.Q : mw >= p.M;
-            const bool res_here = has_res && !dead;
-            const int rem_cols = p.K - nbase;
-            const int nvalid = rem_cols >= BN ? NCH : (rem_cols + 31) / 32;  // chunks with n0 < K
-            // residuals requested before the accumulator is ready: every chunk's when the tile
-            // has at most EPI_BUFS chunks (their sub-tiles were last read by the stores of
-            // earlier chunks, all waited for), else the first two (those of chunks g-4, g-3)
-            const bool res_all = nvalid <= EPI_BUFS;
-            const int pre = pre_next;   // chunks of this tile requested during the previous one
+            auto row_of = [&](int u) { return m_tile * TM + (u / NCH) * BM + quarter * 32; };
+            // residuals requested before the accumulator is ready
+            const bool res_all = nlive <= EPI_BUFS;
+            const int pre = pre_next;
             pre_next = 0;
-            if (res_here) {
+            // (no `nlive > 0` in this condition: the loop below issues nothing for an empty tile,
+            // and that form of the test was observed to skip the block for live warps)
+            if (has_res) {
                 if (lane == 0) {
                     if (res_all) bulk_wait_read<0>();
-                    else bulk_wait_read<2>();
+                    else bulk_wait_read<EPI_BUFS - 2>();
                 }
                 __syncwarp();
-                const int first = res_all ? nvalid : 2;
-                for (int c = pre; c < first && c < nvalid; ++c) {
-                    if (lane == 0) issue_res(g + c, nbase + c * 32, mw);
-                    rpend |= 1u << ((g + c) % EPI_BUFS);
+                const int first = res_all ? nlive : 2;
+                int j = 0;
+                for (int k = 0; k < KMAX; ++k) {
+                    if ((lmask >> k) & 1u) {
+                        if (j >= pre && j < first) {
+                            const int u = slot + k * SLOTS;
+                            if (lane == 0)
+                                issue_res(g + j, nbase + (u % NCH) * 32, row_of(u));
+                            rpend |= 1u << ((g + j) % EPI_BUFS);
+                        }
+                        ++j;
+                    }
                 }
             }
-            // Cross-tile residual prefetch (one sub-tile per tile, exactly EPI_BUFS chunks): while
-            // chunk c of this tile is processed, chunk c-1 of this warp's next tile is requested
-            // into the sub-tile chunk c-1 used, so its load overlaps the rest of this tile.
-            int nx_mw = 0, nx_nbase = 0;
+            // Cross-tile residual prefetch when the warp's chunks exactly fill its sub-tiles:
+            // while live chunk j of this tile is processed, live chunk j-1 of the warp's next
+            // tile is requested into the sub-tile chunk j-1 used.
+            int nx_m = 0, nx_nbase = 0;
+            uint32_t nx_mask = 0;
             bool chain = false;
-            if (MT == 1 && res_here && nvalid == EPI_BUFS) {
+            if (has_res && nlive == EPI_BUFS) {
                 const int nt = tile + (int)gridDim.x;
                 if (nt < num_tiles) {
-                    const int nm = nt / p.num_n_tiles;
-                    nx_nbase = (nt - nm * p.num_n_tiles) * BN;
-                    nx_mw = nm * TM + quarter * 32;
-                    const int nrem = p.K - nx_nbase;
-                    chain = nx_mw < p.M && (nrem >= BN || (nrem + 31) / 32 == EPI_BUFS);
+                    nx_mask = live_mask(nt, nx_m, nx_nbase);
+                    chain = __popc(nx_mask) == EPI_BUFS;
                 }
             }
-            float bnext = 0.f;
             if (BIAS_SMEM) {
 #pragma unroll
                 for (int j = 0; j < NCH; ++j) {
@@ -710,111 +753,132 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
                     sbias[j * 32 + lane] = (p.bias && col < p.K) ? __ldg(p.bias + col) : 0.f;
                 }
                 __syncwarp();
-            } else {
-                bnext = (p.bias && nbase + lane < p.K) ? __ldg(p.bias + nbase + lane) : 0.f;
             }
-            if (mt == 0) {
-                if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
+            if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) {
+                ok = false;
+                break;
             }
-            if (dead) continue;
-            const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) +
-                                   (uint32_t)(acc * MT * BN + mt * BN);
+            tc_fence_after();
+            const uint32_t t_quarter = tmem_base + ((uint32_t)(quarter * 32) << 16) +
+                                       (uint32_t)(acc * MT * BN);
+            int j = 0;   // live chunk index within this tile
 #pragma unroll 1
-            for (int c = 0; c < nvalid; ++c, ++g) {
-                const uint32_t u = g % EPI_BUFS;
+            for (int k = 0; k < KMAX; ++k) {
+                if (!((lmask >> k) & 1u)) continue;
+                const int u = slot + k * SLOTS;
+                const int mt = u / NCH;
+                const int c = u - mt * NCH;
                 const int n0 = nbase + c * 32;
-                const float bcur = bnext;
-                if (!BIAS_SMEM && c + 1 < nvalid)
-                    bnext = (p.bias && n0 + 32 + lane < p.K) ? __ldg(p.bias + n0 + 32 + lane) : 0.f;
-                if (res_here && !res_all && c + 2 < nvalid) {
-                    // sub-tile (g+2) % 4 was last read by the store of chunk g-2
-                    if (lane == 0) bulk_wait_read<1>();
+                const int mw = row_of(u);
+                const uint32_t ub = g % EPI_BUFS;
+                float bcur = 0.f;
+                if (!BIAS_SMEM) bcur = (p.bias && n0 + lane < p.K) ? __ldg(p.bias + n0 + lane) : 0.f;
+                if (has_res && !res_all && j + 2 < nlive) {
+                    // the live chunk two ahead: find its unit
+                    int jj = 0, uu = 0;
+#pragma unroll
+                    for (int kk = 0; kk < KMAX; ++kk)
+                        if ((lmask >> kk) & 1u) {
+                            if (jj == j + 2) uu = slot + kk * SLOTS;
+                            ++jj;
+                        }
+                    // sub-tile (g+2) % EPI_BUFS was last read by the store of chunk g+2-EPI_BUFS
+                    if (lane == 0) {
+                        bulk_wait_read<EPI_BUFS - 3 >= 0 ? EPI_BUFS - 3 : 0>();
+                        issue_res(g + 2, nbase + (uu - (uu / NCH) * NCH) * 32, row_of(uu));
+                    }
                     __syncwarp();
-                    if (lane == 0) issue_res(g + 2, n0 + 64, mw);
                     rpend |= 1u << ((g + 2) % EPI_BUFS);
                 }
                 uint32_t v[32];
-                tmem_ld32(t_row + (uint32_t)(c * 32), v);
-                if (chain && c >= 1) {
-                    // sub-tile of chunk c-1 (g-1): its store was issued a chunk ago
+                tmem_ld32(t_quarter + (uint32_t)(mt * BN + c * 32), v);
+                if (chain && j >= 1) {
+                    // live chunk j-1 of the next tile into the sub-tile of chunk g-1, whose store
+                    // was issued a chunk ago
+                    int jj = 0, uu = 0;
+#pragma unroll
+                    for (int kk = 0; kk < KMAX; ++kk)
+                        if ((nx_mask >> kk) & 1u) {
+                            if (jj == j - 1) uu = slot + kk * SLOTS;
+                            ++jj;
+                        }
                     if (lane == 0) {
                         bulk_wait_read<0>();
-                        issue_res(g - 1 + EPI_BUFS, nx_nbase + (c - 1) * 32, nx_mw);
+                        issue_res(g - 1 + EPI_BUFS, nx_nbase + (uu - (uu / NCH) * NCH) * 32,
+                                  nx_m * TM + (uu / NCH) * BM + quarter * 32);
                     }
                     __syncwarp();
                     rpend |= 1u << ((g - 1) % EPI_BUFS);
-                    pre_next = c;
+                    pre_next = j;
                 }
                 if (!use_tma) {
                     if (mw + lane < p.M) store_chunk_f32(p, mw + lane, n0, v);
+                    ++g;
+                    ++j;
                     continue;
                 }
                 float f[32];
                 if (BIAS_SMEM) {
                     const float4* b4 = reinterpret_cast<const float4*>(sbias + c * 32);
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        const float4 bb = b4[j];
-                        f[4 * j] = __uint_as_float(v[4 * j]) + bb.x;
-                        f[4 * j + 1] = __uint_as_float(v[4 * j + 1]) + bb.y;
-                        f[4 * j + 2] = __uint_as_float(v[4 * j + 2]) + bb.z;
-                        f[4 * j + 3] = __uint_as_float(v[4 * j + 3]) + bb.w;
+                    for (int q = 0; q < 8; ++q) {
+                        const float4 bb = b4[q];
+                        f[4 * q] = __uint_as_float(v[4 * q]) + bb.x;
+                        f[4 * q + 1] = __uint_as_float(v[4 * q + 1]) + bb.y;
+                        f[4 * q + 2] = __uint_as_float(v[4 * q + 2]) + bb.z;
+                        f[4 * q + 3] = __uint_as_float(v[4 * q + 3]) + bb.w;
                     }
                 } else {
 #pragma unroll
-                    for (int j = 0; j < 32; ++j)
-                        f[j] = __uint_as_float(v[j]) + __shfl_sync(0xffffffffu, bcur, j);
+                    for (int q = 0; q < 32; ++q)
+                        f[q] = __uint_as_float(v[q]) + __shfl_sync(0xffffffffu, bcur, q);
                 }
-                uint8_t* sb = ebuf + u * EPI_SUB_BYTES;
-                if (res_here) {
-                    if (!mbar_wait(&rbar[u], (rph >> u) & 1u, abort_flag)) {
+                uint8_t* sb = ebuf + ub * EPI_SUB_BYTES;
+                if (has_res) {
+                    if (!mbar_wait(&rbar[ub], (rph >> ub) & 1u, abort_flag)) {
                         ok = false;
                         break;
                     }
-                    rph ^= 1u << u;
-                    rpend &= ~(1u << u);
+                    rph ^= 1u << ub;
+                    rpend &= ~(1u << ub);
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        uint4 rv = *reinterpret_cast<const uint4*>(sb + sw64(lane, j));
+                    for (int q = 0; q < 4; ++q) {
+                        uint4 rv = *reinterpret_cast<const uint4*>(sb + sw64(lane, q));
                         const typename H16::T2* r2 = reinterpret_cast<const typename H16::T2*>(&rv);
 #pragma unroll
                         for (int t = 0; t < 4; ++t) {
                             float2 rr = H16::unpack(r2[t]);
-                            f[8 * j + 2 * t] += rr.x;
-                            f[8 * j + 2 * t + 1] += rr.y;
+                            f[8 * q + 2 * t] += rr.x;
+                            f[8 * q + 2 * t + 1] += rr.y;
                         }
                     }
                 } else {
-                    // sub-tile u was last read by the store of chunk g-4
-                    if (lane == 0) bulk_wait_read<3>();
+                    // sub-tile ub was last read by the store of chunk g - EPI_BUFS
+                    if (lane == 0) bulk_wait_read<EPI_BUFS - 1>();
                     __syncwarp();
                 }
                 if (clamp) {
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) f[j] = fminf(fmaxf(f[j], 0.f), act_hi);
+                    for (int q = 0; q < 32; ++q) f[q] = fminf(fmaxf(f[q], 0.f), act_hi);
                 }
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
+                for (int q = 0; q < 4; ++q) {
                     uint4 ov;
                     typename H16::T2* o2 = reinterpret_cast<typename H16::T2*>(&ov);
 #pragma unroll
-                    for (int t = 0; t < 4; ++t) o2[t] = H16::pack(f[8 * j + 2 * t], f[8 * j + 2 * t + 1]);
-                    *reinterpret_cast<uint4*>(sb + sw64(lane, j)) = ov;
+                    for (int t = 0; t < 4; ++t) o2[t] = H16::pack(f[8 * q + 2 * t], f[8 * q + 2 * t + 1]);
+                    *reinterpret_cast<uint4*>(sb + sw64(lane, q)) = ov;
                 }
                 fence_async_smem();
                 __syncwarp();
                 if (lane == 0) {
-                    if (MODE == MODE_STEM) tma_store_3d(&tmOut, sb, n0, sq, srow);
+                    if (MODE == MODE_STEM) tma_store_3d(&tmOut, sb, n0, sq0, srow);
                     else tma_store_2d(&tmOut, sb, n0, mw);
                     bulk_commit();
                 }
+                ++g;
+                ++j;
             }
-            if (!ok) break;
-          }
             if (!ok) break;
             tc_fence_before();
             __syncwarp();
@@ -846,7 +910,7 @@ __global__ void __launch_bounds__(MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GAT
         // m / 64, 32-bit words (m % 64) + [0, 4) of the row, already in element order.
         // Gather thread 0 loads each tile's patch two tiles ahead; the 256 gather threads meet
         // at a named barrier (id 1) per tile, which also agrees on whether to stop.
-        const int gw = warp - 2 - NUM_EPI_WARPS;
+        const int gw = warp - 2 - EW;
         const int gt = gw * 32 + lane;
         // a warp writes only its TMEM lane quarter (warp % 4): A row = that quarter's 32 rows
         const int row = (warp & 3) * 32 + lane;  // A row this thread builds
@@ -1001,11 +1065,11 @@ static int encode_epilogue_map(CUtensorMap* map, const void* base, int rows, int
     return r == CUDA_SUCCESS ? OM_OK : OM_ERR_DRIVER;
 }
 
-template <int BN, int MODE, int DT, int OCC, int MT = 1>
+template <int BN, int MODE, int DT, int OCC, int MT = 1, int EW = 4>
 static int launch(DeviceCtx* c, const CUtensorMap& ta, const CUtensorMap& tb,
                   const CUtensorMap& to, const CUtensorMap& tr, const Params& p) {
-    using Cf = Cfg<BN, OCC, extra_bytes<BN, MODE, OCC>(), MT>;
-    auto kern = conv_tc_kernel<BN, MODE, DT, OCC, MT>;
+    using Cf = Cfg<BN, OCC, extra_bytes<BN, MODE, OCC, EW>(), MT, EW>;
+    auto kern = conv_tc_kernel<BN, MODE, DT, OCC, MT, EW>;
     static bool attr_set[64] = {false};
     if (!attr_set[c->device]) {
         OMB_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1015,16 +1079,24 @@ static int launch(DeviceCtx* c, const CUtensorMap& ta, const CUtensorMap& tb,
     const int tiles = p.num_m_tiles * p.num_n_tiles;
     const int slots = OCC * c->num_sms;
     const int grid = tiles < slots ? tiles : slots;
-    const int threads = MODE == MODE_STEM ? NUM_THREADS + 32 * NUM_GATHER_WARPS : NUM_THREADS;
-    kern<<<grid, threads, Cf::SMEM_BYTES, c->compute>>>(ta, tb, to, tr, p);
+    kern<<<grid, cta_threads<MODE, EW>(), Cf::SMEM_BYTES, c->compute>>>(ta, tb, to, tr, p);
     return after_launch(c);
 }
 
 template <int MODE, int DT>
-static int dispatch_bn(DeviceCtx* c, int bn, int occ, int mt, const CUtensorMap& ta,
+static int dispatch_bn(DeviceCtx* c, int bn, int occ, int mt, int ew, const CUtensorMap& ta,
                        const CUtensorMap& tb, const CUtensorMap& to, const CUtensorMap& tr,
                        const Params& p) {
     if constexpr (MODE == MODE_SW128) {
+        if (ew == 16) {
+            if (mt != 2) return OM_ERR_UNSUPPORTED;
+            switch (bn) {
+                case 32: return launch<32, MODE, DT, 1, 2, 16>(c, ta, tb, to, tr, p);
+                case 64: return launch<64, MODE, DT, 1, 2, 16>(c, ta, tb, to, tr, p);
+                case 128: return launch<128, MODE, DT, 1, 2, 16>(c, ta, tb, to, tr, p);
+            }
+            return OM_ERR_UNSUPPORTED;
+        }
         if (mt == 2) {
             switch (bn) {
                 case 64: return launch<64, MODE, DT, 1, 2>(c, ta, tb, to, tr, p);
@@ -1054,25 +1126,34 @@ static int dispatch_bn(DeviceCtx* c, int bn, int occ, int mt, const CUtensorMap&
     return OM_ERR_UNSUPPORTED;
 }
 
-// Tile shape and CTAs per SM, for Cout output channels, num_kb 64-wide k-blocks and m_tiles
-// 128-row tiles. Short reductions (num_kb <= 8, i.e. 1x1 convs up to 512 input channels) are
-// memory-bound: they take at most 128-wide tiles at two CTAs per SM. Longer ones prefer
-// 256-wide tiles (half the A re-reads) unless that leaves SMs idle; when they stay at 64 or
-// 128 wide, two 128-row sub-tiles per tile (mt = 2) are used if that still fills two waves.
+// Tile shape, CTAs per SM and epilogue warps, for Cout output channels, num_kb 64-wide
+// k-blocks and m_tiles 128-row tiles.
+//  * Short reductions (num_kb <= 8, i.e. 1x1 convs up to 512 input channels) are bound by the
+//    epilogue and HBM: at most 128-wide tiles; two 128-row sub-tiles per tile (mt = 2) with 16
+//    epilogue warps when that fills the SMs (allow_mt2), else two CTAs per SM.
+//  * Longer ones prefer 256-wide tiles (half the A re-reads) unless that leaves SMs idle; when
+//    they stay at 64 or 128 wide, mt = 2 is used if that still fills two waves.
 static void choose_tile(int Cout, int num_kb, long long m_tiles, int num_sms, bool allow_mt2,
-                        int* bn, int* occ, int* mt) {
+                        int* bn, int* occ, int* mt, int* ew) {
     *occ = 1;
     *mt = 1;
+    *ew = 4;
     if (Cout <= 32) *bn = 32;
     else if (Cout <= 64) *bn = 64;
     else if (Cout <= 128) *bn = 128;
     else *bn = (m_tiles * ((Cout + 255) / 256) >= 2LL * num_sms) ? 256 : 128;
     if (num_kb <= 8) {
         if (*bn == 256) *bn = 128;
-        long long tiles = m_tiles * ((Cout + *bn - 1) / *bn);
-        if (tiles >= 2LL * num_sms) *occ = 2;
+        const long long nt = (Cout + *bn - 1) / *bn;
+        if (allow_mt2 && (m_tiles + 1) / 2 * nt >= num_sms) {
+            *mt = 2;
+            *ew = 16;
+        } else if (m_tiles * nt >= 2LL * num_sms) {
+            *occ = 2;
+        }
+        return;
     }
-    if (allow_mt2 && *occ == 1 && (*bn == 64 || *bn == 128)) {
+    if (allow_mt2 && (*bn == 64 || *bn == 128)) {
         long long tiles2 = (m_tiles + 1) / 2 * ((Cout + *bn - 1) / *bn);
         if (tiles2 >= 2LL * num_sms) *mt = 2;
     }
@@ -1080,7 +1161,7 @@ static void choose_tile(int Cout, int num_kb, long long m_tiles, int num_sms, bo
 
 // Encodes the output and residual maps (16-bit outputs) and launches the kernel.
 template <int MODE>
-static int finish_and_launch(DeviceCtx* c, int bn, int occ, int mt, int nDtype,
+static int finish_and_launch(DeviceCtx* c, int bn, int occ, int mt, int ew, int nDtype,
                              const CUtensorMap& ta, const CUtensorMap& tb, const Params& p) {
     const CUtensorMapDataType dt =
         nDtype == OM_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -1105,8 +1186,8 @@ static int finish_and_launch(DeviceCtx* c, int bn, int occ, int mt, int nDtype,
         }
     }
     if (nDtype == OM_DTYPE_BF16)
-        return dispatch_bn<MODE, OM_DTYPE_BF16>(c, bn, occ, mt, ta, tb, to, tr, p);
-    return dispatch_bn<MODE, OM_DTYPE_F16>(c, bn, occ, mt, ta, tb, to, tr, p);
+        return dispatch_bn<MODE, OM_DTYPE_BF16>(c, bn, occ, mt, ew, ta, tb, to, tr, p);
+    return dispatch_bn<MODE, OM_DTYPE_F16>(c, bn, occ, mt, ew, ta, tb, to, tr, p);
 }
 
 }  // namespace tc
@@ -1164,8 +1245,9 @@ extern "C" int omCudaConv2dBnAct(const void* pInput, const void* pPacked, const 
     p.P = P; p.Q = Q; p.M = (int)Mll;
     p.num_kb = (int)(kpad / BK);
     p.num_m_tiles = (int)((Mll + BM - 1) / BM);
-    int bn, occ, mt;
-    choose_tile(nCout, p.num_kb, p.num_m_tiles, c->num_sms, mode == MODE_SW128, &bn, &occ, &mt);
+    int bn, occ, mt, ew;
+    choose_tile(nCout, p.num_kb, p.num_m_tiles, c->num_sms, mode == MODE_SW128, &bn, &occ, &mt,
+                &ew);
     p.num_m_tiles = (int)((Mll + BM * mt - 1) / (BM * mt));
     p.num_n_tiles = (nCout + bn - 1) / bn;
     p.x = nullptr;
@@ -1211,8 +1293,9 @@ extern "C" int omCudaConv2dBnAct(const void* pInput, const void* pPacked, const 
                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return OM_ERR_DRIVER;
 
-    return mode == MODE_SW128 ? finish_and_launch<MODE_SW128>(c, bn, occ, mt, nDtype, ta, tb, p)
-                              : finish_and_launch<MODE_INTERLEAVE>(c, bn, occ, mt, nDtype, ta, tb, p);
+    return mode == MODE_SW128
+               ? finish_and_launch<MODE_SW128>(c, bn, occ, mt, ew, nDtype, ta, tb, p)
+               : finish_and_launch<MODE_INTERLEAVE>(c, bn, occ, mt, ew, nDtype, ta, tb, p);
 }
 
 // ---------------------------------------------------------------- image stem
@@ -1315,8 +1398,8 @@ extern "C" int omCudaStemConvBnAct(const float* pInput, void* pWorkspace, const 
     p.num_kb = (int)(kpad / BK);
     p.num_m_tiles = (int)m_tiles;
     p.QT = qt;
-    int bn, occ, mt;
-    choose_tile(nCout, 1 << 20, p.num_m_tiles, c->num_sms, false, &bn, &occ, &mt);  // 1 CTA/SM
+    int bn, occ, mt, ew;
+    choose_tile(nCout, 1 << 20, p.num_m_tiles, c->num_sms, false, &bn, &occ, &mt, &ew);  // 1 CTA/SM
     p.num_n_tiles = (nCout + bn - 1) / bn;
     p.x = pInput;
     p.C = nCin;
@@ -1348,5 +1431,5 @@ extern "C" int omCudaStemConvBnAct(const float* pInput, void* pWorkspace, const 
                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return OM_ERR_DRIVER;
-    return finish_and_launch<MODE_STEM>(c, bn, occ, mt, nDtype, ta, tb, p);
+    return finish_and_launch<MODE_STEM>(c, bn, occ, mt, ew, nDtype, ta, tb, p);
 }
