@@ -365,12 +365,15 @@ __device__ __forceinline__ void store_chunk_f32(const Params& p, int m, int n0,
     }
 }
 
-// Mode-specific shared memory after the epilogue buffers: the stem's patch buffers, or, for
-// the epilogue-bound configurations (two CTAs per SM, or 16 epilogue warps), each epilogue
-// warp's copy of the tile's bias.
+// Mode-specific shared memory after the epilogue buffers: the stem's patch buffers, then, for
+// the epilogue-bound configurations (the stem, two CTAs per SM, or 16 epilogue warps), each
+// epilogue warp's copy of the tile's bias.
+template <int BN, int MODE, int OCC, int EW>
+__host__ __device__ constexpr bool bias_smem() { return MODE == MODE_STEM || OCC == 2 || EW > 4; }
 template <int BN, int MODE, int OCC, int EW>
 __host__ __device__ constexpr int extra_bytes() {
-    return MODE == MODE_STEM ? STEM_EXTRA_BYTES : ((OCC == 2 || EW > 4) ? EW * BN * 4 : 0);
+    return (MODE == MODE_STEM ? STEM_EXTRA_BYTES : 0) +
+           (bias_smem<BN, MODE, OCC, EW>() ? EW * BN * 4 : 0);
 }
 
 template <int BN, int MODE, int DT, int OCC, int MT, int EW>
@@ -654,8 +657,9 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
         const bool has_res = use_tma && p.residual != nullptr;
         const bool clamp = p.act != OM_ACT_NONE;
         const float act_hi = p.act == OM_ACT_RELU6 ? 6.f : INFINITY;
-        constexpr bool BIAS_SMEM = OCC == 2 || EW > 4;
-        float* sbias = reinterpret_cast<float*>(sExtra) + ew * BN;
+        constexpr bool BIAS_SMEM = bias_smem<BN, MODE, OCC, EW>();
+        float* sbias = reinterpret_cast<float*>(sExtra + (MODE == MODE_STEM ? STEM_EXTRA_BYTES : 0)) +
+                       ew * BN;
         uint32_t g = 0;       // chunks started by this warp; chunk g uses sub-tile g % EPI_BUFS
         uint32_t rph = 0;     // per sub-tile: parity of its next residual load
         uint32_t rpend = 0;   // per sub-tile: a residual load is in flight
@@ -677,20 +681,21 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
             nbase_o = (t - mtl * p.num_n_tiles) * BN;
             const int rem = p.K - nbase_o;
             const int nvalid = rem >= BN ? NCH : (rem + 31) / 32;
+            // rows of this quarter that exist: stem columns below Q, else pixels below M
+            int rows_left;
+            if (MODE == MODE_STEM) {
+                const int srow = mtl / p.QT;
+                rows_left = p.Q - ((mtl - srow * p.QT) * BM + quarter * 32);
+            } else {
+                rows_left = p.M - (mtl * TM + quarter * 32);
+            }
             uint32_t mask = 0;
 #pragma unroll
             for (int k = 0; k < KMAX; ++k) {
                 const int u = slot + k * SLOTS;
                 if (u >= MT * NCH) continue;
                 const int mt = u / NCH, c = u - (u / NCH) * NCH;
-                bool live = c < nvalid;
-                if (MODE == MODE_STEM) {
-                    const int srow = mtl / p.QT;
-                    live = live && (mtl - srow * p.QT) * BM + quarter * 32 < p.Q;
-                } else {
-                    live = live && mtl * TM + mt * BM + quarter * 32 < p.M;
-                }
-                if (live) mask |= 1u << k;
+                if (c < nvalid && mt * BM < rows_left) mask |= 1u << k;
             }
             return mask;
         };
@@ -746,6 +751,8 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
                     chain = __popc(nx_mask) == EPI_BUFS;
                 }
             }
+            // shuffle path: the bias of the first live chunk, loaded before the accumulator wait
+            float bnext = 0.f;
             if (BIAS_SMEM) {
 #pragma unroll
                 for (int j = 0; j < NCH; ++j) {
@@ -753,6 +760,10 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
                     sbias[j * 32 + lane] = (p.bias && col < p.K) ? __ldg(p.bias + col) : 0.f;
                 }
                 __syncwarp();
+            } else if (lmask) {
+                const int u0 = slot + (__ffs(lmask) - 1) * SLOTS;
+                const int col = nbase + (u0 % NCH) * 32 + lane;
+                bnext = (p.bias && col < p.K) ? __ldg(p.bias + col) : 0.f;
             }
             if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) {
                 ok = false;
@@ -771,8 +782,16 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
                 const int n0 = nbase + c * 32;
                 const int mw = row_of(u);
                 const uint32_t ub = g % EPI_BUFS;
-                float bcur = 0.f;
-                if (!BIAS_SMEM) bcur = (p.bias && n0 + lane < p.K) ? __ldg(p.bias + n0 + lane) : 0.f;
+                // shuffle path: this chunk's bias was loaded a chunk ago; load the next live one's
+                const float bcur = bnext;
+                if (!BIAS_SMEM) {
+                    const uint32_t rest = lmask & ~((2u << k) - 1u);
+                    if (rest) {
+                        const int un = slot + (__ffs(rest) - 1) * SLOTS;
+                        const int col = nbase + (un % NCH) * 32 + lane;
+                        bnext = (p.bias && col < p.K) ? __ldg(p.bias + col) : 0.f;
+                    }
+                }
                 if (has_res && !res_all && j + 2 < nlive) {
                     // the live chunk two ahead: find its unit
                     int jj = 0, uu = 0;
