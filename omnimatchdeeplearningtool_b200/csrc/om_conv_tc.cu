@@ -1150,8 +1150,9 @@ static int dispatch_bn(DeviceCtx* c, int bn, int occ, int mt, int ew, const CUte
 //  * Short reductions (num_kb <= 8, i.e. 1x1 convs up to 512 input channels) are bound by the
 //    epilogue and HBM: at most 128-wide tiles; two 128-row sub-tiles per tile (mt = 2) with 16
 //    epilogue warps when that fills the SMs (allow_mt2), else two CTAs per SM.
-//  * Longer ones prefer 256-wide tiles (half the A re-reads) unless that leaves SMs idle; when
-//    they stay at 64 or 128 wide, mt = 2 is used if that still fills two waves.
+//  * Longer ones prefer 256-wide tiles (half the A re-reads, twice the work per MMA) unless that
+//    leaves SMs idle; when they stay at 64 or 128 wide, mt = 2 is used if that still fills two
+//    waves.
 static void choose_tile(int Cout, int num_kb, long long m_tiles, int num_sms, bool allow_mt2,
                         int* bn, int* occ, int* mt, int* ew) {
     *occ = 1;
@@ -1160,7 +1161,9 @@ static void choose_tile(int Cout, int num_kb, long long m_tiles, int num_sms, bo
     if (Cout <= 32) *bn = 32;
     else if (Cout <= 64) *bn = 64;
     else if (Cout <= 128) *bn = 128;
-    else *bn = (m_tiles * ((Cout + 255) / 256) >= 2LL * num_sms) ? 256 : 128;
+    // 256-wide tiles do twice the work per issued MMA; they win whenever they fill the SMs
+    // once (the alternative's extra waves of issue-bound 128-wide tiles cost more)
+    else *bn = (m_tiles * ((Cout + 255) / 256) >= num_sms) ? 256 : 128;
     if (num_kb <= 8) {
         if (*bn == 256) *bn = 128;
         const long long nt = (Cout + *bn - 1) / *bn;
