@@ -61,7 +61,8 @@ constexpr int BK = 64;                  // K elements per pipeline stage
 constexpr int A_STAGE_BYTES = BM * BK * 2;
 constexpr int NUM_GATHER_WARPS = 8;     // MODE_STEM only
 constexpr int EPI_SUB_BYTES = 32 * 32 * 2;             // one 32x32 16-bit sub-tile
-// EW epilogue warps (4 or 16; EW / 4 per TMEM lane quarter), each with epi_bufs<EW>() 2 KB
+// EW epilogue warps (4, 8 for the stem, or 16; EW / 4 per TMEM lane quarter), each with
+// epi_bufs<EW>() 2 KB
 // staging sub-tiles; every CTA also has a producer warp and an MMA warp (and, for the stem,
 // NUM_GATHER_WARPS gather warps after the epilogue warps).
 template <int EW>
@@ -382,7 +383,8 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
                    const __grid_constant__ CUtensorMap tmOut,
                    const __grid_constant__ CUtensorMap tmRes, const Params p) {
     static_assert(MT == 1 || (MODE == MODE_SW128 && BN <= 128 && OCC == 1), "MT = 2 tiles");
-    static_assert(EW == 4 || (EW == 16 && OCC == 1 && MODE != MODE_STEM), "epilogue warps");
+    static_assert(EW == 4 || (EW == 16 && OCC == 1 && MODE != MODE_STEM) ||
+                      (EW == 8 && MODE == MODE_STEM), "epilogue warps");
     using C = Cfg<BN, OCC, extra_bytes<BN, MODE, OCC, EW>(), MT, EW>;
     constexpr int EPI_BUFS = epi_bufs<EW>();
     constexpr int TM = BM * MT;   // output pixels per tile
@@ -1133,6 +1135,14 @@ static int dispatch_bn(DeviceCtx* c, int bn, int occ, int mt, int ew, const CUte
             }
             return OM_ERR_UNSUPPORTED;
         }
+    }
+    if constexpr (MODE == MODE_STEM) {  // 8 epilogue warps beside the 8 gather warps
+        switch (bn) {
+            case 32: return launch<32, MODE, DT, 1, 1, 8>(c, ta, tb, to, tr, p);
+            case 64: return launch<64, MODE, DT, 1, 1, 8>(c, ta, tb, to, tr, p);
+            case 128: return launch<128, MODE, DT, 1, 1, 8>(c, ta, tb, to, tr, p);
+        }
+        return OM_ERR_UNSUPPORTED;
     }
     switch (bn) {
         case 32: return launch<32, MODE, DT, 1>(c, ta, tb, to, tr, p);
