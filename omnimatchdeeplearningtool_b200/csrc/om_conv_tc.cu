@@ -190,20 +190,6 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void*
         "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
         : "memory");
 }
-// Named barrier over `nthreads` threads that also ORs a predicate across them, so every
-// participant leaves with the same answer.
-__device__ __forceinline__ bool bar_or(int id, int nthreads, bool pred) {
-    uint32_t r;
-    asm volatile(
-        "{\n\t.reg .pred p, q;\n\t"
-        "setp.ne.u32 p, %1, 0;\n\t"
-        "bar.red.or.pred q, %2, %3, p;\n\t"
-        "selp.u32 %0, 1, 0, q;\n\t}\n"
-        : "=r"(r)
-        : "r"((uint32_t)pred), "r"(id), "r"(nthreads)
-        : "memory");
-    return r != 0;
-}
 __device__ __forceinline__ void bulk_commit() {
     asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
@@ -407,7 +393,8 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
     uint64_t* patch_full = resfull + EPI_BUFS * EW;  // [STEM_PATCH_BUFS], MODE_STEM
     uint64_t* a_full = patch_full + STEM_PATCH_BUFS;  // [2], MODE_STEM: A buffer written
     uint64_t* a_empty = a_full + 2;                   // [2], MODE_STEM: A buffer consumed
-    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(a_empty + 2);
+    uint64_t* patch_empty = a_empty + 2;              // [STEM_PATCH_BUFS], MODE_STEM: patch read
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(patch_empty + STEM_PATCH_BUFS);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -423,7 +410,10 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
             mbar_init(&tempty[i], EW);
         }
         for (int i = 0; i < EPI_BUFS * EW; ++i) mbar_init(&resfull[i], 1);
-        for (int i = 0; i < STEM_PATCH_BUFS; ++i) mbar_init(&patch_full[i], 1);
+        for (int i = 0; i < STEM_PATCH_BUFS; ++i) {
+            mbar_init(&patch_full[i], 1);
+            mbar_init(&patch_empty[i], NUM_GATHER_WARPS);
+        }
         for (int i = 0; i < 2; ++i) {
             mbar_init(&a_full[i], NUM_GATHER_WARPS);
             mbar_init(&a_empty[i], 1);
@@ -929,8 +919,8 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
         // TMA zero-fills rows outside the image and columns past the padded row. A row m,
         // chunk t holds columns m*stride + [0, 8) of patch row t: for stride 2 that is box
         // m / 64, 32-bit words (m % 64) + [0, 4) of the row, already in element order.
-        // Gather thread 0 loads each tile's patch two tiles ahead; the 256 gather threads meet
-        // at a named barrier (id 1) per tile, which also agrees on whether to stop.
+        // Gather thread 0 loads each tile's patch two tiles ahead, into a buffer every gather
+        // warp has released (patch_empty); the warps otherwise run independently.
         const int gw = warp - 2 - EW;
         const int gt = gw * 32 + lane;
         // a warp writes only its TMEM lane quarter (warp % 4): A row = that quarter's 32 rows
@@ -966,7 +956,8 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
         // per column), once the MMAs of tile i-2 have consumed it.
         auto build = [&](int i) -> bool {
             const int buf = i & 1;
-            if (!mbar_wait(&a_empty[buf], (uint32_t)(((i >> 1) & 1) ^ 1), abort_flag)) return false;
+            const bool got = mbar_wait(&a_empty[buf], (uint32_t)(((i >> 1) & 1) ^ 1), abort_flag);
+            if (!__all_sync(0xffffffffu, got)) return false;   // warp-uniform
             tc_fence_after();
             int rowid, q0;
             tile_row(i, rowid, q0);
@@ -1004,25 +995,41 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
             if (lane == 0) mbar_arrive(&a_full[buf]);
             return true;
         };
-        constexpr int NG = 32 * NUM_GATHER_WARPS;
         bool failed = false;
         int issued = 0, waited = 0;   // patch loads issued / waited for (thread gt == 0)
         if (gt == 0) {
             for (; issued < 2 && issued < my_tiles; ++issued) issue(issued);
         }
+        // every stop decision is taken by the whole warp (__any_sync), so that the warp stays
+        // converged for the tcgen05 stores
         for (int i = 0; i < my_tiles; ++i) {
-            // buffer (i+2) % 3 was last read while building tile i-1, before the last barrier
-            if (gt == 0 && i + 2 < my_tiles) issue(issued++);
-            if (!failed) {
-                if (!mbar_wait(&patch_full[i % STEM_PATCH_BUFS], (uint32_t)((i / STEM_PATCH_BUFS) & 1),
-                               abort_flag))
-                    failed = true;
-                else {
-                    ++waited;
-                    if (!build(i)) failed = true;
-                }
+            bool bad = false;
+            if (gt == 0 && i + 2 < my_tiles) {
+                // buffer (i+2) % 3 held tile i-1's patch: wait until every gather warp read it
+                if (i >= 1 && !mbar_wait(&patch_empty[(i - 1) % STEM_PATCH_BUFS],
+                                         (uint32_t)(((i - 1) / STEM_PATCH_BUFS) & 1), abort_flag))
+                    bad = true;
+                else
+                    issue(issued++);
             }
-            if (bar_or(1, NG, failed || *abort_flag != 0)) break;
+            if (__any_sync(0xffffffffu, bad)) {
+                failed = true;
+                break;
+            }
+            bad = !mbar_wait(&patch_full[i % STEM_PATCH_BUFS], (uint32_t)((i / STEM_PATCH_BUFS) & 1),
+                             abort_flag);
+            if (__any_sync(0xffffffffu, bad)) {
+                failed = true;
+                break;
+            }
+            if (gt == 0) ++waited;
+            if (!build(i)) {
+                failed = true;
+                break;
+            }
+            // this warp is done reading tile i's patch
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&patch_empty[i % STEM_PATCH_BUFS]);
         }
         if (gt == 0) {
             // no patch load may land after the CTA exits
