@@ -37,7 +37,7 @@ METRIC = "ResNet-50 bf16 images/s at 1/2/4/8 B200; conv implicit-GEMM % of TC pe
 BATCH = 256
 # DRAM read+write bytes of the 54 conv_tc_kernel launches of one batch-64 forward, from one ncu
 # capture (profiles/conv_tc_kernel_traffic_resnet50_b64.md); traffic grows with the batch.
-CONV_TRAFFIC_B64 = 2.325e9
+CONV_TRAFFIC_B64 = 2.311e9
 
 
 def _peaks():
