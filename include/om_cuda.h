@@ -198,18 +198,20 @@ int omCudaConv2dBnAct(const void* pInput, const void* pPacked, const float* pBia
                       const void* pResidual, void* pOutput, int nBatch, int nH, int nW, int nCs,
                       int nCout, int nKH, int nKW, int nStride, int nPad, int nAct, int nDtype,
                       int nOutDtype);
-/* new: the image stem (KH * Cin <= 24, KW <= 8, Cout <= 128, stride 1 or 2) from the NCHW fp32
- * image: out[n,p,q,k] = act(sum_{c,r,s} x[n,c,p*st-pad+r,q*st-pad+s] * W'[k,(c,r,s)] + bias[k]),
- * NHWC 16-bit output, W' from omCudaPackStemWeight (BN folded as in omCudaPackConvWeight).
- * Same tcgen05 kernel as omCudaConv2dBnAct; a first launch writes a 16-bit copy of the image
- * into pWorkspace (omCudaStemWorkspaceBytes bytes, 16-byte aligned), from which the A tiles
- * are built. */
-long long omCudaPackedStemWeightElems(int nCout, int nCin, int nKH);
-long long omCudaStemWorkspaceBytes(int nBatch, int nCin, int nH, int nW, int nPad);
+/* new: the image stem (stride 1 or 2, Cin * stride^2 <= 16, Cout % 8 == 0) from the NCHW fp32
+ * image: out[n,p,q,k] = act(sum_{c,r,s} x[n,c,p*st-pad+r,q*st-pad+s] * W[k,c,r,s] * scale[k]
+ * + bias[k]), NHWC 16-bit output, BN folded as in omCudaPackConvWeight. A first launch writes a
+ * space-to-depth 16-bit copy of the image into pWorkspace (omCudaStemWorkspaceBytes bytes,
+ * 16-byte aligned): 16 channels (c, py, px) per pixel, padding included, so the stem runs as a
+ * stride-1 ceil(KH/st) x ceil(KW/st) convolution through the same tcgen05 kernel as
+ * omCudaConv2dBnAct; omCudaPackStemWeight packs the filter for it. */
+long long omCudaPackedStemWeightElems(int nCout, int nCin, int nKH, int nKW, int nStride);
+long long omCudaStemWorkspaceBytes(int nBatch, int nCin, int nH, int nW, int nKH, int nKW,
+                                   int nStride, int nPad);
 int omCudaPackStemWeight(const float* pWeight, const float* pConvBias, const float* pGamma,
                          const float* pBeta, const float* pMean, const float* pVar, float fEps,
                          void* pPacked, float* pBiasOut, int nCout, int nCin, int nKH, int nKW,
-                         int nDtype);
+                         int nStride, int nDtype);
 int omCudaStemConvBnAct(const float* pInput, void* pWorkspace, const void* pPacked,
                         const float* pBias, void* pOutput, int nBatch, int nCin, int nH, int nW,
                         int nCout, int nKH, int nKW, int nStride, int nPad, int nAct, int nDtype);

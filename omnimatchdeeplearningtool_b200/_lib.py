@@ -96,7 +96,7 @@ _SIGS = {
     # NHWC fused path
     "omCudaPackConvWeight": [P, P, P, P, P, P, F, P, P, I, I, I, I, I, I],
     "omCudaConv2dBnAct": [P, P, P, P, P, I, I, I, I, I, I, I, I, I, I, I, I],
-    "omCudaPackStemWeight": [P, P, P, P, P, P, F, P, P, I, I, I, I, I],
+    "omCudaPackStemWeight": [P, P, P, P, P, P, F, P, P, I, I, I, I, I, I],
     "omCudaStemConvBnAct": [P, P, P, P, P, I, I, I, I, I, I, I, I, I, I, I],
     "omCudaNchwToNhwc": [P, P, I, I, I, I, I, I], "omCudaNhwcToNchw": [P, P, I, I, I, I, I, I],
     "omCudaMaxPool2dNhwc": [P, P, I, I, I, I, I, I, I, I],
@@ -113,9 +113,9 @@ lib.omCudaGetStream.argtypes = []
 lib.omCudaGetStream.restype = c_void_p
 lib.omCudaPackedConvWeightElems.argtypes = [I, I, I, I]
 lib.omCudaPackedConvWeightElems.restype = c_longlong
-lib.omCudaPackedStemWeightElems.argtypes = [I, I, I]
+lib.omCudaPackedStemWeightElems.argtypes = [I, I, I, I, I]
 lib.omCudaPackedStemWeightElems.restype = c_longlong
-lib.omCudaStemWorkspaceBytes.argtypes = [I, I, I, I, I]
+lib.omCudaStemWorkspaceBytes.argtypes = [I, I, I, I, I, I, I, I]
 lib.omCudaStemWorkspaceBytes.restype = c_longlong
 lib.omCudaStoredChannels.argtypes = [I]
 lib.omCudaStoredChannels.restype = c_int

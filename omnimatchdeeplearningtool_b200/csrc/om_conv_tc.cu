@@ -30,6 +30,11 @@
 //   MODE_SW128: Cs % 64 == 0. One im2col box = 128 pixels x 64 channels = 128 rows of 128 B,
 //               written by TMA with the 128-byte swizzle; SBO = 1024 B; the K=16 steps advance
 //               the descriptor start address by 32 B inside the swizzle atom.
+//   MODE_SW32:  Cs == 16 (the space-to-depth image stem, 16-channel layers). A k-block is four
+//               filter taps; each is one im2col box of 128 pixels x 16 channels = 128 rows of
+//               32 B, written with the 32-byte swizzle (SBO = 256 B) and consumed by one K=16
+//               MMA. A k-block past the last tap loads and multiplies only the taps that exist.
+//               B is SW128 as above.
 //   MODE_INTERLEAVE: Cs % 8 == 0 (the 32-channel MobileNet layers). A stage holds 8 im2col
 //               boxes of 128 pixels x 8 channels (2 KB each, no swizzle): core matrices of
 //               8 rows x 16 B, SBO = 128 B (next 8 rows), LBO = 2 KB (next 8 K-elements).
@@ -74,21 +79,23 @@ __host__ __device__ constexpr int cta_threads() {
     return 64 + 32 * EW + (MODE == 2 ? 32 * NUM_GATHER_WARPS : 0);
 }
 constexpr int MAX_DYN_SMEM = 232448;                   // 227 KB per CTA on sm_100
-// MODE_STEM input patch: per tile, C*R image rows of 136 16-bit columns, one box for stride 1
-// (columns q0 + [0, 135)), two for stride 2 (the second starting 128 columns later).
-constexpr int STEM_MAX_ROWS = 24;                      // R * C (7x7 on 3 channels: 21)
-constexpr int STEM_BOX_W = 136;
-constexpr int STEM_PATCH_BYTES = 2 * STEM_BOX_W * STEM_MAX_ROWS * 2 + 256;  // 13312, 128-B multiple
-static_assert(STEM_PATCH_BYTES % 128 == 0, "patch buffers stay 128-byte aligned");
+// MODE_STEM input patch: per tile (output row p, columns q0 .. q0+127), the R space-to-depth
+// rows p .. p+R-1 at pixels q0 + [0, 127 + S), 16 channels (32 bytes) per pixel, written by one
+// TMA box with the 32-byte swizzle. R <= 4 and S <= 8 (R * S <= 16 taps).
+constexpr int STEM_MAX_R = 4, STEM_MAX_S = 8, STEM_MAX_TAPS = 16;
+constexpr int STEM_PATCH_BYTES = 17408;                // >= 4 * (127 + 8) * 32, 1 KB multiple
+static_assert(STEM_PATCH_BYTES >= STEM_MAX_R * (BM - 1 + STEM_MAX_S) * 32, "patch size");
+static_assert(STEM_PATCH_BYTES % 1024 == 0, "patch buffers stay 1024-byte aligned");
 constexpr int STEM_PATCH_BUFS = 3;                     // two tiles' loads in flight
 constexpr int STEM_EXTRA_BYTES = STEM_PATCH_BUFS * STEM_PATCH_BYTES;
 // MODE_STEM tensor memory: the two accumulators (2 * BN columns, BN <= 128), then two A
-// buffers of up to 3 k-blocks (96 columns: 192 16-bit K elements per row) each.
+// buffers of up to 16 taps (8 columns, i.e. 16 16-bit K elements, per tap) each.
 constexpr uint32_t STEM_TMEM_COLS = 512;
-constexpr int STEM_A_COLS = 96;
+constexpr int STEM_A_COLS = STEM_MAX_TAPS * 8;
 constexpr unsigned long long OMB_WAIT_NS = 2000000000ull;  // 2 s per wait
 
-enum { MODE_SW128 = 0, MODE_INTERLEAVE = 1, MODE_STEM = 2 };
+enum { MODE_SW128 = 0, MODE_INTERLEAVE = 1, MODE_STEM = 2, MODE_SW32 = 3 };
+constexpr int SW32_BOX_BYTES = BM * 16 * 2;            // MODE_SW32: one tap, 128 px x 16 ch
 
 struct Params {
     int N, H, W, Cs;
@@ -97,9 +104,8 @@ struct Params {
     int P, Q, M;
     int num_kb;
     int num_m_tiles, num_n_tiles;
-    const float* x;       // MODE_STEM: the NCHW fp32 image
-    int C;                // MODE_STEM: its channel count
     int QT;               // MODE_STEM: tiles per output row, ceil(Q / 128)
+    int box_w;            // MODE_STEM: patch pixels per row, 127 + S
     const float* bias;
     const void* residual;
     void* out;
@@ -107,6 +113,12 @@ struct Params {
     int out_f32;          // 1: fp32 output stored directly (classifier logits)
     unsigned int* err;
 };
+
+// MODE_SW32: filter taps in k-block kb (4, or what is left of the R*S taps in the last one)
+__device__ __forceinline__ int sw32_taps(const Params& p, int kb) {
+    const int left = p.R * p.S - kb * (BK / 16);
+    return left < BK / 16 ? left : BK / 16;
+}
 
 // ---------------------------------------------------------------- PTX wrappers
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -289,7 +301,7 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint
     d |= (uint64_t)layout << 61;
     return d;
 }
-constexpr uint32_t LAYOUT_NONE = 0, LAYOUT_SW128 = 2;
+constexpr uint32_t LAYOUT_NONE = 0, LAYOUT_SW128 = 2, LAYOUT_SW32 = 6;
 
 // Instruction descriptor for kind::f16: D fp32, A/B bf16 (1) or f16 (0), both K-major,
 // N>>3 at [17,23), M>>4 at [24,29).
@@ -368,7 +380,8 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
     conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmOut,
                    const __grid_constant__ CUtensorMap tmRes, const Params p) {
-    static_assert(MT == 1 || (MODE == MODE_SW128 && BN <= 128 && OCC == 1), "MT = 2 tiles");
+    static_assert(MT == 1 || ((MODE == MODE_SW128 || MODE == MODE_SW32) && BN <= 128 && OCC == 1),
+                  "MT = 2 tiles");
     static_assert(EW == 4 || (EW == 16 && OCC == 1 && MODE != MODE_STEM) ||
                       (EW == 8 && MODE == MODE_STEM), "epilogue warps");
     using C = Cfg<BN, OCC, extra_bytes<BN, MODE, OCC, EW>(), MT, EW>;
@@ -425,6 +438,8 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
     }
     constexpr uint32_t TMEM_ALLOC = MODE == MODE_STEM ? STEM_TMEM_COLS : (uint32_t)C::TMEM_COLS;
     static_assert(MODE != MODE_STEM || (BN <= 128 && OCC == 1), "stem TMEM layout");
+    static_assert(MODE != MODE_STEM || C::STAGES * BK >= STEM_MAX_TAPS * 16,
+                  "the stem's whole packed weight stays resident in the B stages");
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                          smem_u32(tmem_holder)),
@@ -502,6 +517,25 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
                                 ++fr;
                             }
                         }
+                    } else if (MODE == MODE_SW32) {
+                        // kk = kb * 64 + j * 16 = (fr * S + fs) * 16: box j is filter tap
+                        // kb * 4 + j; the k-block holds nt of them (fewer only in the last)
+                        const int nt = sw32_taps(p, kb);
+                        mbar_expect_tx(&full[stage],
+                                       (uint32_t)(MT * nt * SW32_BOX_BYTES + C::B_STAGE_BYTES));
+                        for (int j = 0; j < nt; ++j) {
+                            tma_load_im2col(a_dst + j * SW32_BOX_BYTES, &tmA, &full[stage], 0, wb,
+                                            hb, img, (uint16_t)fs, (uint16_t)fr);
+                            if (MT == 2)
+                                tma_load_im2col(a_dst + A_STAGE_BYTES + j * SW32_BOX_BYTES, &tmA,
+                                                &full[stage], 0, wb1, hb1, img1, (uint16_t)fs,
+                                                (uint16_t)fr);
+                            if (++fs == p.S) {
+                                fs = 0;
+                                ++fr;
+                            }
+                        }
+                        tma_load_2d(b_dst, &tmB, &full[stage], kb * BK, n0);
                     } else {
                         mbar_expect_tx(&full[stage], C::STAGE_BYTES);
                         const int RS = p.R * p.S;
@@ -546,13 +580,16 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
             constexpr uint32_t IDESC = instr_desc<BN, F16>();
             // descriptors of stage 0, k step 0; stage and k offsets are added to the start
             // address field (address >> 4, no carry out of its 14 bits below 256 KB)
-            const uint64_t adesc0 = MODE != MODE_INTERLEAVE
-                                        ? smem_desc(smem_u32(sA), 16, 1024, LAYOUT_SW128)
-                                        : smem_desc(smem_u32(sA), BM * 16, 128, LAYOUT_NONE);
+            const uint64_t adesc0 =
+                MODE == MODE_INTERLEAVE ? smem_desc(smem_u32(sA), BM * 16, 128, LAYOUT_NONE)
+                : MODE == MODE_SW32     ? smem_desc(smem_u32(sA), 16, 256, LAYOUT_SW32)
+                                        : smem_desc(smem_u32(sA), 16, 1024, LAYOUT_SW128);
             const uint64_t bdesc0 = MODE != MODE_INTERLEAVE
                                         ? smem_desc(smem_u32(sB), 16, 1024, LAYOUT_SW128)
                                         : smem_desc(smem_u32(sB), BN * 16, 128, LAYOUT_NONE);
-            constexpr uint32_t A_K_STEP = MODE != MODE_INTERLEAVE ? 32 >> 4 : (2 * BM * 16) >> 4;
+            constexpr uint32_t A_K_STEP = MODE == MODE_INTERLEAVE ? (2 * BM * 16) >> 4
+                                          : MODE == MODE_SW32     ? SW32_BOX_BYTES >> 4
+                                                                  : 32 >> 4;
             constexpr uint32_t B_K_STEP = MODE != MODE_INTERLEAVE ? 32 >> 4 : (2 * BN * 16) >> 4;
             int stage = 0;
             uint32_t phase = 0;
@@ -572,13 +609,13 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
                     tc_fence_after();
                     const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
                     const uint32_t a_tmem = tmem_base + (uint32_t)(2 * BN + acc * STEM_A_COLS);
-                    for (int kb = 0; kb < p.num_kb; ++kb) {
-                        const uint64_t bd = bdesc0 + (uint64_t)(kb * (C::B_STAGE_BYTES >> 4));
-#pragma unroll
-                        for (int k = 0; k < BK / 16; ++k)
-                            tc_mma_ts(d_tmem, a_tmem + (uint32_t)(kb * 32 + k * 8), bd + k * B_K_STEP,
-                                      IDESC, (kb > 0 || k > 0) ? 1u : 0u);
-                    }
+                    // tap t: A columns 8t .. 8t+7, B k-block t / 4, K step t % 4
+                    const int taps = p.R * p.S;
+                    for (int t = 0; t < taps; ++t)
+                        tc_mma_ts(d_tmem, a_tmem + (uint32_t)(t * 8),
+                                  bdesc0 + (uint64_t)((t >> 2) * (C::B_STAGE_BYTES >> 4)) +
+                                      (t & 3) * B_K_STEP,
+                                  IDESC, t > 0 ? 1u : 0u);
                     tc_commit(&a_empty[acc]);
                     tc_commit(&tfull[acc]);
                 }
@@ -601,13 +638,23 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
                     tc_fence_after();
                     const uint64_t ad = adesc0 + (uint64_t)(stage * (C::A_BYTES >> 4));
                     const uint64_t bd = bdesc0 + (uint64_t)(stage * (C::B_STAGE_BYTES >> 4));
+                    if (MODE == MODE_SW32) {
+                        const int nt = sw32_taps(p, kb);
+                        for (int k = 0; k < nt; ++k)
 #pragma unroll
-                    for (int k = 0; k < BK / 16; ++k)
+                            for (int mt = 0; mt < MT; ++mt)
+                                tc_mma(d_tmem + (uint32_t)(mt * BN),
+                                       ad + (uint64_t)(mt * (A_STAGE_BYTES >> 4)) + k * A_K_STEP,
+                                       bd + k * B_K_STEP, IDESC, (kb > 0 || k > 0) ? 1u : 0u);
+                    } else {
 #pragma unroll
-                        for (int mt = 0; mt < MT; ++mt)
-                            tc_mma(d_tmem + (uint32_t)(mt * BN),
-                                   ad + (uint64_t)(mt * (A_STAGE_BYTES >> 4)) + k * A_K_STEP,
-                                   bd + k * B_K_STEP, IDESC, (kb > 0 || k > 0) ? 1u : 0u);
+                        for (int k = 0; k < BK / 16; ++k)
+#pragma unroll
+                            for (int mt = 0; mt < MT; ++mt)
+                                tc_mma(d_tmem + (uint32_t)(mt * BN),
+                                       ad + (uint64_t)(mt * (A_STAGE_BYTES >> 4)) + k * A_K_STEP,
+                                       bd + k * B_K_STEP, IDESC, (kb > 0 || k > 0) ? 1u : 0u);
+                    }
                     tc_commit(&empty[stage]);
                     if (++stage == STAGES) {
                         stage = 0;
@@ -913,24 +960,29 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
         __syncwarp();
     } else if (MODE == MODE_STEM) {
         // ---------------------------------------------------------------- gather (stem)
-        // Tile i = output row (img, pp), columns q0 .. q0+127. Its patch (buffer i % 3) holds,
-        // for patch row t = c*R + r, image row pp*stride - pad + r of channel c at padded
-        // columns q0*stride + [0, 136) (box 0) and, for stride 2, + 128 + [0, 136) (box 1);
-        // TMA zero-fills rows outside the image and columns past the padded row. A row m,
-        // chunk t holds columns m*stride + [0, 8) of patch row t: for stride 2 that is box
-        // m / 64, 32-bit words (m % 64) + [0, 4) of the row, already in element order.
-        // Gather thread 0 loads each tile's patch two tiles ahead, into a buffer every gather
-        // warp has released (patch_empty); the warps otherwise run independently.
+        // Input: the space-to-depth image Y [N, H, W, 16] (16-bit); the stem is a stride-1 R x S
+        // convolution over it. Tile i = output row (img, pp), columns q0 .. q0+127. Its patch
+        // (buffer i % 3) holds Y rows pp .. pp+R-1 at pixels q0 + [0, box_w), written by one
+        // TMA box with the 32-byte swizzle (the two 16-byte halves of a pixel swap when bit 2
+        // of its index in the box is set), so that a warp's 16-byte reads of 32 consecutive
+        // pixels are free of bank conflicts. A row m, tap t = (r, s): the 32 bytes of patch pixel
+        // (r, m + s), i.e. K elements 16t .. 16t+15 = TMEM columns 8t .. 8t+7. Pixels past the
+        // image are zero-filled by TMA; rows m with q0 + m >= Q are computed but never stored.
+        // Two gather warps per TMEM lane quarter split the taps. Gather thread 0 loads each
+        // tile's patch two tiles ahead, into a buffer every gather warp has released
+        // (patch_empty); the warps otherwise run independently.
         const int gw = warp - 2 - EW;
         const int gt = gw * 32 + lane;
         // a warp writes only its TMEM lane quarter (warp % 4): A row = that quarter's 32 rows
         const int row = (warp & 3) * 32 + lane;  // A row this thread builds
-        const int j0 = (gw >> 2) * 4;            // its first chunk in each k-block
         const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
-        const int RC = p.R * p.C;
-        const int nbox = p.stride == 2 ? 2 : 1;
-        const uint32_t box_bytes = (uint32_t)(STEM_BOX_W * RC * 2);
-        const uint32_t box1_off = (box_bytes + 127u) & ~127u;   // TMA destinations 128-byte aligned
+        const int taps = p.R * p.S;
+        // taps per gather warp, even: a lone last tap is stored with a zero partner, which
+        // lands in columns no other warp writes
+        const int tpw = (((taps + 1) >> 1) + 1) & ~1;
+        const int t_begin = (gw >> 2) * tpw;
+        const int t_end = t_begin + tpw < taps ? t_begin + tpw : taps;
+        const uint32_t box_bytes = (uint32_t)(p.R * p.box_w * 32);
         const int my_tiles =
             (int)blockIdx.x < num_tiles ? (num_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
         auto tile_row = [&](int i, int& rowid, int& q0) {
@@ -946,47 +998,43 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
             uint8_t* dst = sExtra + (i % STEM_PATCH_BUFS) * STEM_PATCH_BYTES;
             uint64_t* bar = &patch_full[i % STEM_PATCH_BUFS];
             fence_async_smem();   // generic reads of this buffer (tile i-3) precede the TMA write
-            mbar_expect_tx(bar, box_bytes * nbox);
-            tma_load_4d(dst, &tmA, bar, q0 * p.stride, pp * p.stride - p.pad, 0, img);
-            if (nbox == 2)
-                tma_load_4d(dst + box1_off, &tmA, bar, q0 * p.stride + 128, pp * p.stride - p.pad, 0,
-                            img);
+            mbar_expect_tx(bar, box_bytes);
+            tma_load_4d(dst, &tmA, bar, 0, q0, pp, img);
         };
-        // Tile i's A goes to TMEM buffer i % 2 (columns 2*BN + (i % 2) * STEM_A_COLS, K pairs
-        // per column), once the MMAs of tile i-2 have consumed it.
+        // Tile i's A goes to TMEM buffer i % 2 (columns 2*BN + (i % 2) * STEM_A_COLS), once the
+        // MMAs of tile i-2 have consumed it.
         auto build = [&](int i) -> bool {
             const int buf = i & 1;
             const bool got = mbar_wait(&a_empty[buf], (uint32_t)(((i >> 1) & 1) ^ 1), abort_flag);
             if (!__all_sync(0xffffffffu, got)) return false;   // warp-uniform
             tc_fence_after();
-            int rowid, q0;
-            tile_row(i, rowid, q0);
-            const bool row_ok = q0 + row < p.Q;
             const uint8_t* pb = sExtra + (i % STEM_PATCH_BUFS) * STEM_PATCH_BYTES;
             const uint32_t a_col = tmem_base + lane_base + (uint32_t)(2 * BN + buf * STEM_A_COLS);
-            for (int kb = 0; kb < p.num_kb; ++kb) {
+            int r = t_begin / p.S, sx = t_begin - r * p.S;
+            for (int t = t_begin; t < t_end; t += 2) {
                 uint32_t w16[16];
 #pragma unroll
-                for (int jj = 0; jj < 4; ++jj) {
-                    const int t = kb * 8 + j0 + jj;
-                    uint32_t w0 = 0, w1 = 0, w2 = 0, w3 = 0;
-                    if (row_ok && t < RC) {
-                        if (nbox == 2) {
-                            const uint32_t* w = reinterpret_cast<const uint32_t*>(
-                                pb + (row >> 6) * box1_off + t * (STEM_BOX_W * 2)) + (row & 63);
-                            w0 = w[0]; w1 = w[1]; w2 = w[2]; w3 = w[3];
-                        } else {
-                            const uint16_t* h = reinterpret_cast<const uint16_t*>(
-                                pb + t * (STEM_BOX_W * 2)) + row;
-                            w0 = h[0] | ((uint32_t)h[1] << 16);
-                            w1 = h[2] | ((uint32_t)h[3] << 16);
-                            w2 = h[4] | ((uint32_t)h[5] << 16);
-                            w3 = h[6] | ((uint32_t)h[7] << 16);
+                for (int jj = 0; jj < 2; ++jj) {
+                    uint4 lo = make_uint4(0, 0, 0, 0), hi = lo;
+                    if (t + jj < t_end) {
+                        // flattened box index: the swizzle follows shared-memory address
+                        // bit 7 (buffers are 1024-byte aligned)
+                        const int idx = r * p.box_w + row + sx;
+                        const uint8_t* pix = pb + idx * 32;
+                        const int swap = (idx >> 2) & 1;
+                        lo = *reinterpret_cast<const uint4*>(pix + (swap << 4));
+                        hi = *reinterpret_cast<const uint4*>(pix + ((swap ^ 1) << 4));
+                        if (++sx == p.S) {
+                            sx = 0;
+                            ++r;
                         }
                     }
-                    w16[4 * jj] = w0; w16[4 * jj + 1] = w1; w16[4 * jj + 2] = w2; w16[4 * jj + 3] = w3;
+                    w16[8 * jj + 0] = lo.x; w16[8 * jj + 1] = lo.y;
+                    w16[8 * jj + 2] = lo.z; w16[8 * jj + 3] = lo.w;
+                    w16[8 * jj + 4] = hi.x; w16[8 * jj + 5] = hi.y;
+                    w16[8 * jj + 6] = hi.z; w16[8 * jj + 7] = hi.w;
                 }
-                tmem_st16(a_col + (uint32_t)(kb * 32 + j0 * 4), w16);
+                tmem_st16(a_col + (uint32_t)(t * 8), w16);
             }
             // the stores are complete before the MMA issuer may read them
             tmem_wait_st();
@@ -1115,7 +1163,7 @@ template <int MODE, int DT>
 static int dispatch_bn(DeviceCtx* c, int bn, int occ, int mt, int ew, const CUtensorMap& ta,
                        const CUtensorMap& tb, const CUtensorMap& to, const CUtensorMap& tr,
                        const Params& p) {
-    if constexpr (MODE == MODE_SW128) {
+    if constexpr (MODE == MODE_SW128 || MODE == MODE_SW32) {
         if (ew == 16) {
             if (mt != 2) return OM_ERR_UNSUPPORTED;
             switch (bn) {
@@ -1274,9 +1322,10 @@ extern "C" int omCudaConv2dBnAct(const void* pInput, const void* pPacked, const 
     if (Mll >= (1LL << 31)) return OM_ERR_UNSUPPORTED;
     if (!load_driver_entry_points()) return OM_ERR_DRIVER;
 
-    const int mode = (nCs % 64 == 0) ? MODE_SW128 : MODE_INTERLEAVE;
+    const int mode = (nCs % 64 == 0) ? MODE_SW128 : (nCs == 16 ? MODE_SW32 : MODE_INTERLEAVE);
     const long long kk_total = (long long)nKH * nKW * nCs;
     const long long kpad = (kk_total + BK - 1) / BK * BK;
+    const bool sw128 = mode == MODE_SW128;
 
     Params p;
     p.N = nBatch; p.H = nH; p.W = nW; p.Cs = nCs; p.K = nCout;
@@ -1285,13 +1334,12 @@ extern "C" int omCudaConv2dBnAct(const void* pInput, const void* pPacked, const 
     p.num_kb = (int)(kpad / BK);
     p.num_m_tiles = (int)((Mll + BM - 1) / BM);
     int bn, occ, mt, ew;
-    choose_tile(nCout, p.num_kb, p.num_m_tiles, c->num_sms, mode == MODE_SW128, &bn, &occ, &mt,
-                &ew);
+    choose_tile(nCout, p.num_kb, p.num_m_tiles, c->num_sms, mode != MODE_INTERLEAVE, &bn, &occ,
+                &mt, &ew);
     p.num_m_tiles = (int)((Mll + BM * mt - 1) / (BM * mt));
     p.num_n_tiles = (nCout + bn - 1) / bn;
-    p.x = nullptr;
-    p.C = nCs;
     p.QT = 1;
+    p.box_w = 0;
     p.bias = pBias;
     p.residual = pResidual;
     p.out = pOutput;
@@ -1312,8 +1360,9 @@ extern "C" int omCudaConv2dBnAct(const void* pInput, const void* pPacked, const 
     cuuint32_t a_estr[4] = {1, (cuuint32_t)nStride, (cuuint32_t)nStride, 1};
     CUresult r = g_encode_im2col(
         &ta, dt, 4, const_cast<void*>(pInput), a_dims, a_strides, lo, hi,
-        mode == MODE_SW128 ? 64 : 8, BM, a_estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-        mode == MODE_SW128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+        sw128 ? 64 : (mode == MODE_SW32 ? 16 : 8), BM, a_estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+        sw128 ? CU_TENSOR_MAP_SWIZZLE_128B
+              : (mode == MODE_SW32 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_NONE),
         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return OM_ERR_DRIVER;
     // Drivers up to 13.1 mis-handle this descriptor bit for im2col tensors under 128 KiB;
@@ -1325,63 +1374,109 @@ extern "C" int omCudaConv2dBnAct(const void* pInput, const void* pPacked, const 
     cuuint64_t b_dims[2] = {(cuuint64_t)kpad, (cuuint64_t)nCout};
     cuuint64_t b_strides[1] = {(cuuint64_t)kpad * 2};
     cuuint32_t b_estr[2] = {1, 1};
-    cuuint32_t b_box[2] = {mode == MODE_SW128 ? 64u : 8u, (cuuint32_t)bn};
+    const bool b_sw128 = mode != MODE_INTERLEAVE;
+    cuuint32_t b_box[2] = {b_sw128 ? 64u : 8u, (cuuint32_t)bn};
     r = g_encode_tiled(&tb, dt, 2, const_cast<void*>(pPacked), b_dims, b_strides, b_box, b_estr,
                        CU_TENSOR_MAP_INTERLEAVE_NONE,
-                       mode == MODE_SW128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                       b_sw128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return OM_ERR_DRIVER;
 
-    return mode == MODE_SW128
-               ? finish_and_launch<MODE_SW128>(c, bn, occ, mt, ew, nDtype, ta, tb, p)
-               : finish_and_launch<MODE_INTERLEAVE>(c, bn, occ, mt, ew, nDtype, ta, tb, p);
+    if (mode == MODE_SW128) return finish_and_launch<MODE_SW128>(c, bn, occ, mt, ew, nDtype, ta, tb, p);
+    if (mode == MODE_SW32) return finish_and_launch<MODE_SW32>(c, bn, occ, mt, ew, nDtype, ta, tb, p);
+    return finish_and_launch<MODE_INTERLEAVE>(c, bn, occ, mt, ew, nDtype, ta, tb, p);
 }
 
 // ---------------------------------------------------------------- image stem
-// K layout of the stem's packed weight: kk = (c * KH + r) * 8 + s, s < KW (taps padded to 8).
-extern "C" long long omCudaPackedStemWeightElems(int nCout, int nCin, int nKH) {
-    long long kk = (long long)nKH * nCin * 8;
-    return (long long)nCout * ((kk + tc::BK - 1) / tc::BK * tc::BK);
-}
-
+// The stem runs as an ordinary stride-1 convolution (MODE_SW32) over a space-to-depth copy of
+// the image. With f = stride (1 or 2), the copy is NHWC 16-bit with 16 channels:
+//   Y[n, u, v, (c * f + py) * f + px] = x[n, c, f*u + py - pad, f*v + px - pad]  (0 outside)
+// for u < P + ceil(KH / f) - 1, v < Q + ceil(KW / f) - 1; the K x C x KH x KW filter becomes a
+// ceil(KH / f) x ceil(KW / f) filter over those 16 channels (omCudaPackStemWeight), since
+// output (p, q) reads Y[p + tr, q + ts] and tap (f*tr + py, f*ts + px) of the original filter.
+// For the 7x7/2 ImageNet stem that is 4 x 4 taps x 16 channels = 4 k-blocks of 4 MMAs; for the
+// 3x3/2 MobileNet stem 2 x 2 taps, one k-block.
 namespace omb {
 namespace tc {
-// Padded row length of the stem's 16-bit copy of the image: `pad` zero columns on the left,
-// the image row, zeros up to a multiple of 8 (16 bytes).
-static long long stem_row_elems(int nW, int nPad) { return ((long long)nW + nPad + 7) / 8 * 8; }
+struct StemGeom {
+    int f, th, tw, P, Q, Hs, Ws;
+};
+static bool stem_geom(int nCin, int nH, int nW, int nKH, int nKW, int nStride, int nPad,
+                      StemGeom* g) {
+    if (nCin <= 0 || nH <= 0 || nW <= 0 || nKH <= 0 || nKW <= 0 || nPad < 0) return false;
+    if (nStride != 1 && nStride != 2) return false;
+    if (nCin * nStride * nStride > 16) return false;
+    g->f = nStride;
+    g->th = (nKH + nStride - 1) / nStride;
+    g->tw = (nKW + nStride - 1) / nStride;
+    g->P = (nH + 2 * nPad - nKH) / nStride + 1;
+    g->Q = (nW + 2 * nPad - nKW) / nStride + 1;
+    if (g->P <= 0 || g->Q <= 0 || g->th > 64 || g->tw > 64) return false;
+    g->Hs = g->P + g->th - 1;
+    g->Ws = g->Q + g->tw - 1;
+    return true;
+}
 
-// NCHW fp32 -> [N*C*H, Wp] 16-bit rows shifted right by `pad`, zero elsewhere; one thread per
-// 8 output elements (16-byte store).
-template <typename T>
-__global__ void stem_pad_kernel(const float* __restrict__ x, T* __restrict__ out, long long rows,
-                                int W, int Wp, int pad) {
-    const int groups = Wp / 8;
-    const long long total = rows * groups;
-    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
-         i += (long long)gridDim.x * blockDim.x) {
-        const long long r = i / groups;
-        const int x0 = (int)(i - r * groups) * 8 - pad;
-        const float* src = x + r * W;
-        uint4 v;
-        uint32_t* w = reinterpret_cast<uint32_t*>(&v);
+// One thread per space-to-depth pixel (n, u, v): 16 channels, two 16-byte stores. F (the
+// stride) is a template parameter so the channel decomposition is resolved at compile time.
+template <typename T, int F>
+__global__ void stem_s2d_kernel(const float* __restrict__ x, T* __restrict__ out, int N, int C,
+                                int H, int W, int Hs, int Ws, int pad) {
+    using H16 = Half16<std::is_same<T, __half>::value ? OM_DTYPE_F16 : OM_DTYPE_BF16>;
+    constexpr int CMAX = 16 / (F * F);
+    const long long total = (long long)N * Hs * Ws;   // < 2^31, checked by the caller
+    for (long long li = blockIdx.x * (long long)blockDim.x + threadIdx.x; li < total;
+         li += (long long)gridDim.x * blockDim.x) {
+        const int i = (int)li;
+        const int nu = i / Ws;
+        const int v = i - nu * Ws;
+        const int n = nu / Hs;
+        const int u = nu - n * Hs;
+        float vals[16];
 #pragma unroll
-        for (int e = 0; e < 8; e += 2) {
-            const int c0 = x0 + e, c1 = x0 + e + 1;
-            const float f0 = (c0 >= 0 && c0 < W) ? __ldg(src + c0) : 0.f;
-            const float f1 = (c1 >= 0 && c1 < W) ? __ldg(src + c1) : 0.f;
-            typename Half16<std::is_same<T, __half>::value ? OM_DTYPE_F16 : OM_DTYPE_BF16>::T2 h2 =
-                Half16<std::is_same<T, __half>::value ? OM_DTYPE_F16 : OM_DTYPE_BF16>::pack(f0, f1);
-            w[e / 2] = *reinterpret_cast<uint32_t*>(&h2);
+        for (int c = 0; c < CMAX; ++c) {
+#pragma unroll
+            for (int py = 0; py < F; ++py) {
+                const int yy = F * u + py - pad;
+                const bool row_ok = c < C && yy >= 0 && yy < H;
+                const float* src = x + (((long long)n * C + (row_ok ? c : 0)) * H + (row_ok ? yy : 0)) * W;
+#pragma unroll
+                for (int px = 0; px < F; ++px) {
+                    const int xx = F * v + px - pad;
+                    vals[(c * F + py) * F + px] =
+                        (row_ok && xx >= 0 && xx < W) ? __ldg(src + xx) : 0.f;
+                }
+            }
         }
-        *reinterpret_cast<uint4*>(out + r * Wp + (long long)(i - r * groups) * 8) = v;
+        uint4 o[2];
+        uint32_t* w32 = reinterpret_cast<uint32_t*>(o);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            typename H16::T2 h2 = H16::pack(vals[2 * e], vals[2 * e + 1]);
+            w32[e] = *reinterpret_cast<uint32_t*>(&h2);
+        }
+        uint4* dst = reinterpret_cast<uint4*>(out + (long long)i * 16);
+        dst[0] = o[0];
+        dst[1] = o[1];
     }
 }
 }  // namespace tc
 }  // namespace omb
 
-extern "C" long long omCudaStemWorkspaceBytes(int nBatch, int nCin, int nH, int nW, int nPad) {
-    if (nBatch <= 0 || nCin <= 0 || nH <= 0 || nW <= 0 || nPad < 0) return 0;
-    return (long long)nBatch * nCin * nH * omb::tc::stem_row_elems(nW, nPad) * 2;
+// K layout of the stem's packed weight: kk = (tr * ceil(KW / f) + ts) * 16 + ch over the
+// space-to-depth channels ch (see above), padded to a multiple of 64.
+extern "C" long long omCudaPackedStemWeightElems(int nCout, int nCin, int nKH, int nKW,
+                                                 int nStride) {
+    if (nCout <= 0 || nCin <= 0 || nKH <= 0 || nKW <= 0 || nStride <= 0) return 0;
+    const long long th = (nKH + nStride - 1) / nStride, tw = (nKW + nStride - 1) / nStride;
+    return omCudaPackedConvWeightElems(nCout, (int)th, (int)tw, 16);
+}
+
+extern "C" long long omCudaStemWorkspaceBytes(int nBatch, int nCin, int nH, int nW, int nKH,
+                                              int nKW, int nStride, int nPad) {
+    omb::tc::StemGeom g;
+    if (nBatch <= 0 || !omb::tc::stem_geom(nCin, nH, nW, nKH, nKW, nStride, nPad, &g)) return 0;
+    return (long long)nBatch * g.Hs * g.Ws * 16 * 2;
 }
 
 extern "C" int omCudaStemConvBnAct(const float* pInput, void* pWorkspace, const void* pPacked,
@@ -1394,54 +1489,63 @@ extern "C" int omCudaStemConvBnAct(const float* pInput, void* pWorkspace, const 
     if (nBatch <= 0 || nCin <= 0 || nH <= 0 || nW <= 0 || nCout <= 0 || nKH <= 0 || nKW <= 0 ||
         nStride <= 0 || nPad < 0)
         return OM_ERR_INVALID;
-    if (nKW > 8 || nCout % 8 != 0 || nCout > 128) return OM_ERR_UNSUPPORTED;
-    if (nStride != 1 && nStride != 2) return OM_ERR_UNSUPPORTED;
-    if (nKH * nCin > STEM_MAX_ROWS || nKH > 256 || nCin > 256) return OM_ERR_UNSUPPORTED;
     if (nDtype != OM_DTYPE_BF16 && nDtype != OM_DTYPE_F16) return OM_ERR_UNSUPPORTED;
-    if ((reinterpret_cast<uintptr_t>(pWorkspace) | reinterpret_cast<uintptr_t>(pPacked) |
-         reinterpret_cast<uintptr_t>(pOutput) | reinterpret_cast<uintptr_t>(pBias)) & 15)
-        return OM_ERR_INVALID;
-    const int P = (nH + 2 * nPad - nKH) / nStride + 1;
-    const int Q = (nW + 2 * nPad - nKW) / nStride + 1;
-    if (P <= 0 || Q <= 0) return OM_ERR_INVALID;
-    const long long Mll = (long long)nBatch * P * Q;
-    const int qt = (Q + BM - 1) / BM;
-    const long long m_tiles = (long long)nBatch * P * qt;
-    const long long wp = stem_row_elems(nW, nPad);
-    const long long rows = (long long)nBatch * nCin * nH;
-    if (Mll >= (1LL << 31) || m_tiles >= (1LL << 31) / 4 || wp >= (1LL << 31) ||
-        rows >= (1LL << 31))
+    if (nCout % 8 != 0) return OM_ERR_UNSUPPORTED;
+    StemGeom g;
+    if (!stem_geom(nCin, nH, nW, nKH, nKW, nStride, nPad, &g)) {
+        const int P = (nH + 2 * nPad - nKH) / nStride + 1;
+        const int Q = (nW + 2 * nPad - nKW) / nStride + 1;
+        return (P <= 0 || Q <= 0) ? OM_ERR_INVALID : OM_ERR_UNSUPPORTED;
+    }
+    if ((reinterpret_cast<uintptr_t>(pWorkspace) & 15) != 0) return OM_ERR_INVALID;
+    const long long pixels = (long long)nBatch * g.Hs * g.Ws;
+    if (pixels >= (1LL << 31) || (long long)nBatch * nCin * nH * nW >= (1LL << 40))
         return OM_ERR_UNSUPPORTED;
-    if (!load_driver_entry_points()) return OM_ERR_DRIVER;
-    const long long kpad = omCudaPackedStemWeightElems(1, nCin, nKH);
-
-    // 16-bit padded copy of the image
     {
-        const long long groups = rows * (wp / 8);
-        long long blocks = (groups + 255) / 256;
+        const long long blocks = (pixels + 255) / 256;
         const int grid = (int)(blocks < 8LL * c->num_sms ? blocks : 8LL * c->num_sms);
-        if (nDtype == OM_DTYPE_BF16)
-            stem_pad_kernel<__nv_bfloat16><<<grid, 256, 0, c->compute>>>(
-                pInput, static_cast<__nv_bfloat16*>(pWorkspace), rows, nW, (int)wp, nPad);
-        else
-            stem_pad_kernel<__half><<<grid, 256, 0, c->compute>>>(
-                pInput, static_cast<__half*>(pWorkspace), rows, nW, (int)wp, nPad);
-        int st = after_launch(c);
+        auto launch_s2d = [&](auto tag, auto f) {
+            using T = decltype(tag);
+            stem_s2d_kernel<T, decltype(f)::value><<<grid, 256, 0, c->compute>>>(
+                pInput, static_cast<T*>(pWorkspace), nBatch, nCin, nH, nW, g.Hs, g.Ws, nPad);
+        };
+        using F1 = std::integral_constant<int, 1>;
+        using F2 = std::integral_constant<int, 2>;
+        if (nDtype == OM_DTYPE_BF16) {
+            if (g.f == 2) launch_s2d(__nv_bfloat16(), F2());
+            else launch_s2d(__nv_bfloat16(), F1());
+        } else {
+            if (g.f == 2) launch_s2d(__half(), F2());
+            else launch_s2d(__half(), F1());
+        }
+        const int st = after_launch(c);
         if (st != OM_OK) return st;
     }
+    // Stems with at most 16 taps of at most 4 x 8 and at most 128 output channels keep A in
+    // tensor memory (MODE_STEM); any other runs through the generic 16-channel path.
+    if (g.th > STEM_MAX_R || g.tw > STEM_MAX_S || g.th * g.tw > STEM_MAX_TAPS || nCout > 128 ||
+        (reinterpret_cast<uintptr_t>(pPacked) | reinterpret_cast<uintptr_t>(pOutput) |
+         reinterpret_cast<uintptr_t>(pBias)) & 15)
+        return omCudaConv2dBnAct(pWorkspace, pPacked, pBias, nullptr, pOutput, nBatch, g.Hs, g.Ws,
+                                 16, nCout, g.th, g.tw, 1, 0, nAct, nDtype, nDtype);
+    const long long Mll = (long long)nBatch * g.P * g.Q;
+    const int qt = (g.Q + BM - 1) / BM;
+    const long long m_tiles = (long long)nBatch * g.P * qt;
+    if (Mll >= (1LL << 31) || m_tiles >= (1LL << 31) / 4) return OM_ERR_UNSUPPORTED;
+    if (!load_driver_entry_points()) return OM_ERR_DRIVER;
+    const long long kpad = omCudaPackedStemWeightElems(1, nCin, nKH, nKW, nStride);
 
     Params p;
-    p.N = nBatch; p.H = nH; p.W = nW; p.Cs = nCin; p.K = nCout;
-    p.R = nKH; p.S = nKW; p.stride = nStride; p.pad = nPad;
-    p.P = P; p.Q = Q; p.M = (int)Mll;
+    p.N = nBatch; p.H = g.Hs; p.W = g.Ws; p.Cs = 16; p.K = nCout;
+    p.R = g.th; p.S = g.tw; p.stride = 1; p.pad = 0;
+    p.P = g.P; p.Q = g.Q; p.M = (int)Mll;
     p.num_kb = (int)(kpad / BK);
     p.num_m_tiles = (int)m_tiles;
     p.QT = qt;
+    p.box_w = BM - 1 + g.tw;
     int bn, occ, mt, ew;
     choose_tile(nCout, 1 << 20, p.num_m_tiles, c->num_sms, false, &bn, &occ, &mt, &ew);  // 1 CTA/SM
     p.num_n_tiles = (nCout + bn - 1) / bn;
-    p.x = pInput;
-    p.C = nCin;
     p.bias = pBias;
     p.residual = nullptr;
     p.out = pOutput;
@@ -1451,15 +1555,14 @@ extern "C" int omCudaStemConvBnAct(const float* pInput, void* pWorkspace, const 
 
     const CUtensorMapDataType dt =
         nDtype == OM_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-    // A source: the padded image as (Wp, H, C, N), box (136, KH, C, 1)
+    // A source: the space-to-depth image as (16, W, H, N), box (16, 127 + S, R, 1), 32-byte swizzle
     CUtensorMap ta, tb;
-    cuuint64_t a_dims[4] = {(cuuint64_t)wp, (cuuint64_t)nH, (cuuint64_t)nCin, (cuuint64_t)nBatch};
-    cuuint64_t a_strides[3] = {(cuuint64_t)wp * 2, (cuuint64_t)nH * wp * 2,
-                               (cuuint64_t)nCin * nH * wp * 2};
-    cuuint32_t a_box[4] = {(cuuint32_t)STEM_BOX_W, (cuuint32_t)nKH, (cuuint32_t)nCin, 1};
+    cuuint64_t a_dims[4] = {16, (cuuint64_t)g.Ws, (cuuint64_t)g.Hs, (cuuint64_t)nBatch};
+    cuuint64_t a_strides[3] = {32, (cuuint64_t)g.Ws * 32, (cuuint64_t)g.Hs * g.Ws * 32};
+    cuuint32_t a_box[4] = {16, (cuuint32_t)p.box_w, (cuuint32_t)g.th, 1};
     cuuint32_t a_estr[4] = {1, 1, 1, 1};
     CUresult r = g_encode_tiled(&ta, dt, 4, pWorkspace, a_dims, a_strides, a_box, a_estr,
-                                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_32B,
                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return OM_ERR_DRIVER;
     cuuint64_t b_dims[2] = {(cuuint64_t)kpad, (cuuint64_t)nCout};

@@ -37,19 +37,26 @@ __global__ void pack_conv_weight_kernel(const float* __restrict__ w, const float
 
 // Stem packing: w [K, C, R, S] -> [K, Kpad] with kk = (r*C + c)*8 + s (s < S <= 8), the
 // layout the stem's gather warps build A in (8 horizontal taps of one plane row per chunk).
+// Stem filter over the space-to-depth channels (f = stride): kk = (tr * tw + ts) * 16 + ch,
+// ch = (c * f + py) * f + px holds W[k, c, f*tr + py, f*ts + px] * scale[k] (zero past the
+// filter, the channels and the taps).
 template <typename T>
 __global__ void pack_stem_weight_kernel(const float* __restrict__ w, const float* __restrict__ scale,
-                                        T* __restrict__ out, int K, int C, int R, int S,
-                                        long long kpad) {
+                                        T* __restrict__ out, int K, int C, int R, int S, int f,
+                                        int th, int tw, long long kpad) {
     long long total = (long long)K * kpad;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
          i += (long long)gridDim.x * blockDim.x) {
         int k = (int)(i / kpad);
         long long kk = i - (long long)k * kpad;
-        int chunk = (int)(kk / 8), s = (int)(kk % 8);
-        int c = chunk / R, r = chunk - c * R;   // kk = (c * R + r) * 8 + s
+        int tap = (int)(kk / 16), ch = (int)(kk % 16);
         float v = 0.f;
-        if (c < C && s < S) v = w[(((long long)k * C + c) * R + r) * S + s] * scale[k];
+        if (tap < th * tw && ch < C * f * f) {
+            const int tr = tap / tw, ts = tap - tr * tw;
+            const int c = ch / (f * f), py = (ch / f) % f, px = ch % f;
+            const int r = f * tr + py, s = f * ts + px;
+            if (r < R && s < S) v = w[(((long long)k * C + c) * R + r) * S + s] * scale[k];
+        }
         if constexpr (std::is_same<T, __nv_bfloat16>::value) out[i] = __float2bfloat16_rn(v);
         else out[i] = __float2half_rn(v);
     }
@@ -155,26 +162,43 @@ __global__ void maxpool_nhwc_kernel(const uint4* __restrict__ in, uint4* __restr
     }
 }
 
-// One block of 256 threads per image. Thread t owns channel group (t % C8) and walks the
-// pixels t/C8, t/C8 + rows, ... (rows = 256/C8); the per-row partial sums are combined in
-// shared memory. Channel counts up to 2048 (C8 <= 256) are covered.
+// One block per image: thread t owns channel group t % C8 and pixel row t / C8, and walks the
+// pixels row, row + rows, ... (rows = blockDim / C8) with four 16-byte loads in flight. Each row's
+// partial sums go to shared memory and are added in row order, so the result does not depend
+// on scheduling.
 template <int DT>
 __global__ void gap_nhwc_kernel(const uint4* __restrict__ in, void* __restrict__ out, int HW,
                                 int C8, int out_f32) {
     using H16 = Half16<DT>;
-    extern __shared__ float sh[];  // C8*8 channel sums
+    extern __shared__ float sh[];  // [rows][C8 * 8] partial sums
     const int n = blockIdx.x;
     const int rows = (int)blockDim.x / C8;
     const int cg = threadIdx.x % C8;
     const int row = threadIdx.x / C8;
-    const bool active = row < rows;
-    const long long base = (long long)n * HW * C8;
-    float acc[8];
+    const int C = C8 * 8;
+    if (row < rows) {
+        const uint4* src = in + (long long)n * HW * C8 + cg;
+        float acc[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) acc[j] = 0.f;
-    if (active) {
-        for (int pix = row; pix < HW; pix += rows) {
-            uint4 v = in[base + (long long)pix * C8 + cg];
+        for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+        int pix = row;
+        for (; pix + 3 * rows < HW; pix += 4 * rows) {
+            uint4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) v[u] = __ldg(src + (long long)(pix + u * rows) * C8);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const typename H16::T2* v2 = reinterpret_cast<const typename H16::T2*>(&v[u]);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    float2 f = H16::unpack(v2[j]);
+                    acc[2 * j] += f.x;
+                    acc[2 * j + 1] += f.y;
+                }
+            }
+        }
+        for (; pix < HW; pix += rows) {
+            uint4 v = __ldg(src + (long long)pix * C8);
             const typename H16::T2* v2 = reinterpret_cast<const typename H16::T2*>(&v);
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
@@ -183,21 +207,19 @@ __global__ void gap_nhwc_kernel(const uint4* __restrict__ in, void* __restrict__
                 acc[2 * j + 1] += f.y;
             }
         }
-    }
-    for (int c = threadIdx.x; c < C8 * 8; c += blockDim.x) sh[c] = 0.f;
-    __syncthreads();
-    if (active) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) atomicAdd(&sh[cg * 8 + j], acc[j]);
+        for (int j = 0; j < 8; ++j) sh[row * C + cg * 8 + j] = acc[j];
     }
     __syncthreads();
     const float inv = 1.f / (float)HW;
-    for (int c = threadIdx.x; c < C8 * 8; c += blockDim.x) {
-        float v = sh[c] * inv;
+    for (int c = threadIdx.x; c < C; c += blockDim.x) {
+        float v = 0.f;
+        for (int r = 0; r < rows; ++r) v += sh[r * C + c];
+        v *= inv;
         if (out_f32)
-            static_cast<float*>(out)[(long long)n * C8 * 8 + c] = v;
+            static_cast<float*>(out)[(long long)n * C + c] = v;
         else
-            static_cast<typename H16::T*>(out)[(long long)n * C8 * 8 + c] = H16::from_f(v);
+            static_cast<typename H16::T*>(out)[(long long)n * C + c] = H16::from_f(v);
     }
 }
 
@@ -383,12 +405,16 @@ extern "C" int omCudaGlobalAvgPoolNhwc(const void* pIn, void* pOut, int nN, int 
     if (!pIn || !pOut || nCs % 8 || nCs > 2048 || !aligned16(pIn)) return OM_ERR_INVALID;
     if (nOutDtype != OM_DTYPE_F32 && nOutDtype != nDtype) return OM_ERR_UNSUPPORTED;
     int C8 = nCs / 8;
-    size_t sh = sizeof(float) * (size_t)nCs;
+    // up to 1024 threads: C8 channel groups x as many pixel rows as fit (one row at least)
+    const int rows = C8 >= 1024 ? 1 : 1024 / C8;
+    const int threads = C8 * rows;
+    if (threads > 1024) return OM_ERR_UNSUPPORTED;
+    size_t sh = sizeof(float) * (size_t)rows * nCs;
     int of32 = nOutDtype == OM_DTYPE_F32;
     if (nDtype == OM_DTYPE_BF16)
-        gap_nhwc_kernel<OM_DTYPE_BF16><<<nN, 256, sh, c->compute>>>(static_cast<const uint4*>(pIn), pOut, nHW, C8, of32);
+        gap_nhwc_kernel<OM_DTYPE_BF16><<<nN, threads, sh, c->compute>>>(static_cast<const uint4*>(pIn), pOut, nHW, C8, of32);
     else if (nDtype == OM_DTYPE_F16)
-        gap_nhwc_kernel<OM_DTYPE_F16><<<nN, 256, sh, c->compute>>>(static_cast<const uint4*>(pIn), pOut, nHW, C8, of32);
+        gap_nhwc_kernel<OM_DTYPE_F16><<<nN, threads, sh, c->compute>>>(static_cast<const uint4*>(pIn), pOut, nHW, C8, of32);
     else
         return OM_ERR_UNSUPPORTED;
     return after_launch(c);
@@ -463,11 +489,15 @@ extern "C" int omCudaAddActNhwc(const void* pA, const void* pB, void* pOut, long
 extern "C" int omCudaPackStemWeight(const float* pWeight, const float* pConvBias,
                                     const float* pGamma, const float* pBeta, const float* pMean,
                                     const float* pVar, float fEps, void* pPacked, float* pBiasOut,
-                                    int nCout, int nCin, int nKH, int nKW, int nDtype) {
+                                    int nCout, int nCin, int nKH, int nKW, int nStride, int nDtype) {
     OMB_CTX_OR_FAIL(c);
-    if (!pWeight || !pPacked || !pBiasOut || nCout <= 0 || nCin <= 0 || nKW > 8) return OM_ERR_INVALID;
+    if (!pWeight || !pPacked || !pBiasOut || nCout <= 0 || nCin <= 0 || nKH <= 0 || nKW <= 0)
+        return OM_ERR_INVALID;
+    if (nStride != 1 && nStride != 2) return OM_ERR_UNSUPPORTED;
+    if (nCin * nStride * nStride > 16) return OM_ERR_UNSUPPORTED;
     if (nDtype != OM_DTYPE_BF16 && nDtype != OM_DTYPE_F16) return OM_ERR_UNSUPPORTED;
-    long long kpad = omCudaPackedStemWeightElems(1, nCin, nKH);
+    const int th = (nKH + nStride - 1) / nStride, tw = (nKW + nStride - 1) / nStride;
+    const long long kpad = omCudaPackedStemWeightElems(1, nCin, nKH, nKW, nStride);
     float* scale = nullptr;
     OMB_CHECK(cudaMallocAsync(&scale, sizeof(float) * nCout, c->compute));
     fold_bn_kernel<<<(nCout + 255) / 256, 256, 0, c->compute>>>(pConvBias, pGamma, pBeta, pMean,
@@ -478,10 +508,12 @@ extern "C" int omCudaPackStemWeight(const float* pWeight, const float* pConvBias
         int grid = ew_grid(c, total, 256);
         if (nDtype == OM_DTYPE_BF16)
             pack_stem_weight_kernel<__nv_bfloat16><<<grid, 256, 0, c->compute>>>(
-                pWeight, scale, static_cast<__nv_bfloat16*>(pPacked), nCout, nCin, nKH, nKW, kpad);
+                pWeight, scale, static_cast<__nv_bfloat16*>(pPacked), nCout, nCin, nKH, nKW,
+                nStride, th, tw, kpad);
         else
             pack_stem_weight_kernel<__half><<<grid, 256, 0, c->compute>>>(
-                pWeight, scale, static_cast<__half*>(pPacked), nCout, nCin, nKH, nKW, kpad);
+                pWeight, scale, static_cast<__half*>(pPacked), nCout, nCin, nKH, nKW, nStride, th,
+                tw, kpad);
         st = after_launch(c);
     }
     cudaFreeAsync(scale, c->compute);

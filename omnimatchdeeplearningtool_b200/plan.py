@@ -169,14 +169,16 @@ class InferencePlan:
         n, dt = self.batch, self.dtype
         wbuf = self._upload(weights[cv.name + ".weight"])
         g, b_, m, v = (self._upload(a) for a in self._bn_params(weights, cv.bn))
-        packed = self._buf(int(lib.omCudaPackedStemWeightElems(cv.cout, cv.cin, cv.k)) * 2)
+        packed = self._buf(int(lib.omCudaPackedStemWeightElems(cv.cout, cv.cin, cv.k, cv.k,
+                                                               cv.stride)) * 2)
         bias = self._buf(cv.cout * 4)
         call("omCudaPackStemWeight", wbuf.ptr, None, g.ptr, b_.ptr, m.ptr, v.ptr, 1e-5, packed.ptr,
-             bias.ptr, cv.cout, cv.cin, cv.k, cv.k, dt)
+             bias.ptr, cv.cout, cv.cin, cv.k, cv.k, cv.stride, dt)
         p = (hh + 2 * cv.pad - cv.k) // cv.stride + 1
         q = (ww + 2 * cv.pad - cv.k) // cv.stride + 1
         out = self._buf(n * p * q * cv.cout * 2)
-        ws = self._buf(int(lib.omCudaStemWorkspaceBytes(n, cv.cin, hh, ww, cv.pad)))
+        ws = self._buf(int(lib.omCudaStemWorkspaceBytes(n, cv.cin, hh, ww, cv.k, cv.k, cv.stride,
+                                                        cv.pad)))
         for x in self.inputs:
             self._need(x, n * cv.cin * hh * ww * 4)
         # The input pointer is the one op argument looked up when the op is issued: the slot

@@ -32,6 +32,11 @@ CASES = [
     (25, 64, 56, 64, 3, 1, 1, "bf16", False, "relu", False),      # BN=64, M = 78400
     (25, 64, 56, 128, 3, 1, 1, "bf16", True, "relu", False),      # BN=128 + residual
     (100, 128, 56, 128, 3, 2, 1, "f16", False, "relu", False),    # stride 2, fp16
+    # 16 stored channels: one 32-byte-swizzled im2col box per filter tap
+    (2, 16, 20, 96, 1, 1, 0, "f16", False, "relu6", False),       # 1x1: one tap per k-block
+    (2, 16, 15, 64, 3, 1, 1, "bf16", True, "relu", False),        # 9 taps: 4 + 4 + 1
+    (3, 12, 17, 32, 5, 2, 2, "bf16", False, "none", False),       # 12 -> 16 channels, stride 2
+    (40, 16, 56, 128, 3, 1, 1, "bf16", False, "relu", False),     # two sub-tiles, 16 epi warps
 ]
 
 
@@ -133,20 +138,23 @@ def test_conv_rejects_bad_shapes(gpu):
     assert lib.omCudaConv2dBnAct(18, 16, None, None, 16, 1, 8, 8, 64, 64, 3, 3, 1, 1, 0, 1, 1) == -2
 
 
-@pytest.mark.parametrize("n,h,k,ks,stride,pad,dt", [(2, 224, 64, 7, 2, 3, "bf16"),
-                                                    (3, 37, 64, 7, 2, 3, "bf16"),
-                                                    (2, 31, 32, 3, 2, 1, "f16"),
-                                                    (1, 300, 64, 7, 2, 3, "bf16"),  # 2 tiles/row
-                                                    (2, 20, 32, 7, 1, 3, "bf16")])  # stride 1
-def test_stem_conv_from_nchw_image(gpu, n, h, k, ks, stride, pad, dt):
+@pytest.mark.parametrize("n,c,h,k,ks,stride,pad,dt", [(2, 3, 224, 64, 7, 2, 3, "bf16"),
+                                                      (3, 3, 37, 64, 7, 2, 3, "bf16"),
+                                                      (2, 3, 31, 32, 3, 2, 1, "f16"),
+                                                      (1, 3, 300, 64, 7, 2, 3, "bf16"),
+                                                      (2, 3, 20, 32, 7, 1, 3, "bf16"),  # stride 1
+                                                      (2, 4, 33, 64, 5, 2, 2, "bf16"),  # 16 of 16
+                                                      (1, 16, 24, 32, 3, 1, 1, "f16"),
+                                                      (2, 1, 40, 8, 7, 2, 3, "bf16")])
+def test_stem_conv_from_nchw_image(gpu, n, c, h, k, ks, stride, pad, dt):
     """omCudaStemConvBnAct: the image stem straight from NCHW fp32 (ImageNet 7x7/2 and the
-    MobileNet 3x3/2 stem), checked like the other fused convs."""
+    MobileNet 3x3/2 stem, and other channel counts that fit one 16-channel space-to-depth
+    pixel), checked like the other fused convs."""
     import oracle as orc
     from omnimatchdeeplearningtool_b200 import _lib
     from omnimatchdeeplearningtool_b200._lib import call, lib
     from omnimatchdeeplearningtool_b200.backend import DeviceBuffer
     rng = np.random.Generator(np.random.PCG64(77 + h))
-    c = 3
     x = rng.standard_normal((n, c, h, h), dtype=np.float32)
     w = (rng.standard_normal((k, c, ks, ks)) * np.sqrt(2.0 / (c * ks * ks))).astype(np.float32)
     g = rng.uniform(0.5, 1.5, k).astype(np.float32)
@@ -156,12 +164,12 @@ def test_stem_conv_from_nchw_image(gpu, n, h, k, ks, stride, pad, dt):
     dtype = _lib.DTYPE_BF16 if dt == "bf16" else _lib.DTYPE_F16
     p = (h + 2 * pad - ks) // stride + 1
     keep = [DeviceBuffer.from_numpy(a) for a in (x, w, g, b, mu, var)]
-    packed = DeviceBuffer(int(lib.omCudaPackedStemWeightElems(k, c, ks)) * 2)
+    packed = DeviceBuffer(int(lib.omCudaPackedStemWeightElems(k, c, ks, ks, stride)) * 2)
     bias = DeviceBuffer(k * 4)
     call("omCudaPackStemWeight", keep[1].ptr, None, keep[2].ptr, keep[3].ptr, keep[4].ptr,
-         keep[5].ptr, 1e-5, packed.ptr, bias.ptr, k, c, ks, ks, dtype)
+         keep[5].ptr, 1e-5, packed.ptr, bias.ptr, k, c, ks, ks, stride, dtype)
     out = DeviceBuffer(n * p * p * k * 2)
-    ws = DeviceBuffer(int(lib.omCudaStemWorkspaceBytes(n, c, h, h, pad)))
+    ws = DeviceBuffer(int(lib.omCudaStemWorkspaceBytes(n, c, h, h, ks, ks, stride, pad)))
     keep.append(ws)
     call("omCudaStemConvBnAct", keep[0].ptr, ws.ptr, packed.ptr, bias.ptr, out.ptr, n, c, h, h, k,
          ks, ks, stride, pad, 1, dtype)
