@@ -80,18 +80,63 @@ def _max_over_ranks(dist, v: float) -> float:
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+    """SM clocks and clock-event (throttle) reasons sampled during the timed region: through NVML
+    in a background thread every 5 ms (so a timed region of a few tens of ms still gets
+    samples), else through `nvidia-smi -lms 200`. Only reads GPU state; changes nothing."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clock-event reason bits
+    REASONS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+               "hw_thermal_slowdown": 0x40}
 
     def __init__(self, device: int):
         self.device = device
-        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
         self.proc = None
+        self.file = None
+        self.thread = None
+        self.samples = []
+        self.mask = 0
+        self.max_mhz = None
+        self._stop = None
+
+    def _nvml_handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        try:
+            import torch
+            prop = torch.cuda.get_device_properties(self.device)
+            bus = "%08x:%02x:%02x.0" % (prop.pci_domain_id, prop.pci_bus_id, prop.pci_device_id)
+            return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.device)
 
     def start(self):
+        import threading
+        try:
+            nv, h = self._nvml_handle()
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+        except Exception:
+            self._start_smi()
+            return
+        self._stop = threading.Event()
+
+        def loop():
+            while True:
+                try:
+                    self.samples.append(float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)))
+                    self.mask |= int(nv.nvmlDeviceGetCurrentClocksEventReasons(h))
+                except Exception:
+                    pass
+                if self._stop.wait(0.005):
+                    break
+
+        self.thread = threading.Thread(target=loop, daemon=True)
+        self.thread.start()
+
+    def _start_smi(self):
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}",
@@ -101,8 +146,15 @@ class ClockSampler:
             self.proc = None
 
     def stop(self) -> dict:
+        if self.thread is not None:
+            self._stop.set()
+            self.thread.join(timeout=5)
+            reasons = sorted(n for n, bit in self.REASONS.items() if self.mask & bit)
+            return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                    "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                    "samples": len(self.samples), "source": "nvml, 5 ms"}
         if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["clock sampling unavailable"]}
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
@@ -126,7 +178,7 @@ class ClockSampler:
                     reasons.add(nm)
         os.unlink(self.file.name)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "source": "nvidia-smi, 200 ms"}
 
 
 def _host_threads() -> int:

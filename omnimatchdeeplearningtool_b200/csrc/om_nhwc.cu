@@ -126,8 +126,10 @@ __global__ void nhwc_to_nchw_kernel(const typename Half16<DT>::T* __restrict__ i
 // One block per output row (n, p); its threads walk the row's (q, 8-channel group) items, each
 // the max of up to k*k 16-byte vectors taken on packed 16-bit pairs (a max is one of its
 // operands, so no rounding is involved). Windows with no pixel inside the image give -1e30,
-// the reference's starting value (cpu_backend.ixx maxPool2d).
-template <int DT>
+// the reference's starting value (cpu_backend.ixx maxPool2d). KS > 0 fixes the window at
+// KS x KS: all its loads are issued before the max is taken (pixels outside the image count
+// as -1e30, which is where the reference starts every window too).
+template <int DT, int KS>
 __global__ void maxpool_nhwc_kernel(const uint4* __restrict__ in, uint4* __restrict__ out, int H,
                                     int W, int C8, int P, int Q, int k, int stride, int pad) {
     using H16 = Half16<DT>;
@@ -136,29 +138,60 @@ __global__ void maxpool_nhwc_kernel(const uint4* __restrict__ in, uint4* __restr
     const int n = row / P;
     const int p = row - n * P;
     const int h0 = p * stride - pad;
-    const int r0 = h0 < 0 ? -h0 : 0;
-    const int r1 = (H - h0) < k ? (H - h0) : k;
     const uint4* img = in + (size_t)n * H * W * C8;
     uint4* orow = out + (size_t)row * Q * C8;
     const T2 lowest = H16::pack(-1e30f, -1e30f);
-    for (int i = threadIdx.x; i < Q * C8; i += blockDim.x) {
-        const int q = i / C8;
-        const int c8 = i - q * C8;
-        const int w0 = q * stride - pad;
-        const int s0 = w0 < 0 ? -w0 : 0;
-        const int s1 = (W - w0) < k ? (W - w0) : k;
-        T2 m[4] = {lowest, lowest, lowest, lowest};
-        for (int r = r0; r < r1; ++r) {
-            // first in-image pixel of the window row; the pointer never leaves the image
-            const uint4* src = img + ((size_t)(h0 + r) * W + (w0 + s0)) * C8 + c8;
-            for (int s = s0; s < s1; ++s) {
-                uint4 v = __ldg(src + (size_t)(s - s0) * C8);
-                const T2* v2 = reinterpret_cast<const T2*>(&v);
+    if constexpr (KS > 0) {
+        uint4 low4;
+        {
+            T2* l2 = reinterpret_cast<T2*>(&low4);
+            l2[0] = l2[1] = l2[2] = l2[3] = lowest;
+        }
+        for (int i = threadIdx.x; i < Q * C8; i += blockDim.x) {
+            const int q = i / C8;
+            const int c8 = i - q * C8;
+            const int w0 = q * stride - pad;
+            uint4 v[KS * KS];
+#pragma unroll
+            for (int r = 0; r < KS; ++r) {
+#pragma unroll
+                for (int s = 0; s < KS; ++s) {
+                    const int hh = h0 + r, ww = w0 + s;
+                    const bool ok = hh >= 0 && hh < H && ww >= 0 && ww < W;
+                    v[r * KS + s] = ok ? __ldg(img + ((size_t)hh * W + ww) * C8 + c8) : low4;
+                }
+            }
+            T2 m[4] = {lowest, lowest, lowest, lowest};
+#pragma unroll
+            for (int t = 0; t < KS * KS; ++t) {
+                const T2* v2 = reinterpret_cast<const T2*>(&v[t]);
 #pragma unroll
                 for (int j = 0; j < 4; ++j) m[j] = __hmax2(m[j], v2[j]);
             }
+            orow[i] = *reinterpret_cast<const uint4*>(m);
         }
-        orow[i] = *reinterpret_cast<const uint4*>(m);
+    } else {
+        const int r0 = h0 < 0 ? -h0 : 0;
+        const int r1 = (H - h0) < k ? (H - h0) : k;
+        for (int i = threadIdx.x; i < Q * C8; i += blockDim.x) {
+            const int q = i / C8;
+            const int c8 = i - q * C8;
+            const int w0 = q * stride - pad;
+            const int s0 = w0 < 0 ? -w0 : 0;
+            const int s1 = (W - w0) < k ? (W - w0) : k;
+            T2 m[4] = {lowest, lowest, lowest, lowest};
+            for (int r = r0; r < r1; ++r) {
+                // first in-image pixel of the window row; the pointer never leaves the image
+                const uint4* src = img + ((size_t)(h0 + r) * W + (w0 + s0)) * C8 + c8;
+                for (int s = s0; s < s1; ++s) {
+                    uint4 v = __ldg(src + (size_t)(s - s0) * C8);
+                    const T2* v2 = reinterpret_cast<const T2*>(&v);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) m[j] = __hmax2(m[j], v2[j]);
+                }
+            }
+            orow[i] = *reinterpret_cast<const uint4*>(m);
+        }
     }
 }
 
@@ -388,14 +421,26 @@ extern "C" int omCudaMaxPool2dNhwc(const void* pIn, void* pOut, int nN, int nH, 
     const long long rows = (long long)nN * P;
     if (rows >= (1LL << 31) || (long long)Q * (nCs / 8) >= (1LL << 31)) return OM_ERR_UNSUPPORTED;
     const int threads = Q * (nCs / 8) >= 256 ? 256 : 128;
-    if (nDtype == OM_DTYPE_BF16)
-        maxpool_nhwc_kernel<OM_DTYPE_BF16><<<(unsigned)rows, threads, 0, c->compute>>>(
-            static_cast<const uint4*>(pIn), static_cast<uint4*>(pOut), nH, nW, nCs / 8, P, Q, nK, nStride, nPad);
-    else if (nDtype == OM_DTYPE_F16)
-        maxpool_nhwc_kernel<OM_DTYPE_F16><<<(unsigned)rows, threads, 0, c->compute>>>(
-            static_cast<const uint4*>(pIn), static_cast<uint4*>(pOut), nH, nW, nCs / 8, P, Q, nK, nStride, nPad);
-    else
+    const uint4* src = static_cast<const uint4*>(pIn);
+    uint4* dst = static_cast<uint4*>(pOut);
+    const int c8 = nCs / 8;
+    if (nDtype == OM_DTYPE_BF16) {
+        if (nK == 3)
+            maxpool_nhwc_kernel<OM_DTYPE_BF16, 3><<<(unsigned)rows, threads, 0, c->compute>>>(
+                src, dst, nH, nW, c8, P, Q, nK, nStride, nPad);
+        else
+            maxpool_nhwc_kernel<OM_DTYPE_BF16, 0><<<(unsigned)rows, threads, 0, c->compute>>>(
+                src, dst, nH, nW, c8, P, Q, nK, nStride, nPad);
+    } else if (nDtype == OM_DTYPE_F16) {
+        if (nK == 3)
+            maxpool_nhwc_kernel<OM_DTYPE_F16, 3><<<(unsigned)rows, threads, 0, c->compute>>>(
+                src, dst, nH, nW, c8, P, Q, nK, nStride, nPad);
+        else
+            maxpool_nhwc_kernel<OM_DTYPE_F16, 0><<<(unsigned)rows, threads, 0, c->compute>>>(
+                src, dst, nH, nW, c8, P, Q, nK, nStride, nPad);
+    } else {
         return OM_ERR_UNSUPPORTED;
+    }
     return after_launch(c);
 }
 
