@@ -28,6 +28,21 @@ struct DeviceCtx {
 // Context of the calling thread's current device, or nullptr before omCudaInit.
 DeviceCtx* ctx();
 
+namespace tc {
+// 3xTF32 tensor-core convolution of an NCHW fp32 source (om_conv_tc.cu): the source is copied
+// to NHWC [N, Hp, Wp, ceil32(Cin)] with out[n,hp,wp,c] = src[n,c,(hp-offh)/up,(wp-offw)/up]
+// (exact divisions inside the source, else 0), convolved (stride, pad) with W [Kw, Cw, R, S]
+// (flip = false: Kout = Kw output channels; flip = true: Kout = Cw, the filter transposed and
+// rotated by 180 degrees, for the backward-input pass) and written NCHW [N, Kout, P, Q] (+bias).
+int tf32_conv(DeviceCtx* c, const float* src, int N, int Cin, int Hin, int Win, int Hp, int Wp,
+              int offh, int offw, int up, const float* w, int Kout, int R, int S, bool flip,
+              int Cw, const float* bias, float* out, int stride, int pad);
+// 3xTF32 tensor-core weight gradient of a (stride, pad) convolution: dW [K, Cin, R, S] from
+// X [N, Cin, H, W] and dY [N, K, P, Q], all NCHW fp32 (om_conv_tc.cu).
+int tf32_wgrad(DeviceCtx* c, const float* x, const float* dy, float* dw, int N, int Cin, int H,
+               int W, int K, int R, int S, int stride, int pad);
+}  // namespace tc
+
 inline int status_of(cudaError_t e) { return e == cudaSuccess ? OM_OK : OM_ERR_CUDA; }
 
 // Called after every launch: records the launch and turns a launch error into a status.

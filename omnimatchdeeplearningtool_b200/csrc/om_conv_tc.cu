@@ -35,6 +35,13 @@
 //               32 B, written with the 32-byte swizzle (SBO = 256 B) and consumed by one K=16
 //               MMA. A k-block past the last tap loads and multiplies only the taps that exist.
 //               B is SW128 as above.
+//   MODE_TF32:  the fp32 path, 3xTF32. Operands are fp32 NHWC / K-major, each split into a
+//               TF32 "hi" part and the TF32 rounding of the remainder ("lo"): x = hi + lo to
+//               about 2^-22. A stage holds A_hi, A_lo (im2col boxes of 128 pixels x 32 fp32
+//               channels = 128 rows of 128 B, 128-byte swizzle) and B_hi, B_lo; each K=8 step
+//               issues hi*hi (kind::tf32) into a main fp32 accumulator and lo*hi + hi*lo into a
+//               correction accumulator beside it; the epilogue adds the two. Output fp32 NCHW,
+//               stored directly. The kernel's four maps are A_hi, B_hi, B_lo, A_lo.
 //   MODE_INTERLEAVE: Cs % 8 == 0 (the 32-channel MobileNet layers). A stage holds 8 im2col
 //               boxes of 128 pixels x 8 channels (2 KB each, no swizzle): core matrices of
 //               8 rows x 16 B, SBO = 128 B (next 8 rows), LBO = 2 KB (next 8 K-elements).
@@ -94,7 +101,7 @@ constexpr uint32_t STEM_TMEM_COLS = 512;
 constexpr int STEM_A_COLS = STEM_MAX_TAPS * 8;
 constexpr unsigned long long OMB_WAIT_NS = 2000000000ull;  // 2 s per wait
 
-enum { MODE_SW128 = 0, MODE_INTERLEAVE = 1, MODE_STEM = 2, MODE_SW32 = 3 };
+enum { MODE_SW128 = 0, MODE_INTERLEAVE = 1, MODE_STEM = 2, MODE_SW32 = 3, MODE_TF32 = 4 };
 constexpr int SW32_BOX_BYTES = BM * 16 * 2;            // MODE_SW32: one tap, 128 px x 16 ch
 
 struct Params {
@@ -186,6 +193,14 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void*
         "r"(smem_u32(src)), "r"(x), "r"(y)
         : "memory");
 }
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                            int x, int y, int z) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+        : "memory");
+}
 __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar,
                                             int x, int y, int z, int w) {
     asm volatile(
@@ -246,6 +261,15 @@ __device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
 }
+// the same with TF32 operands (fp32 containers, K = 8 per instruction)
+__device__ __forceinline__ void tc_mma_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                            uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
 // MMA with the A operand in tensor memory (lanes = rows, 16-bit K pairs per 32-bit column)
 __device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc,
                                           uint32_t idesc, uint32_t accumulate) {
@@ -301,10 +325,16 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint
     d |= (uint64_t)layout << 61;
     return d;
 }
-constexpr uint32_t LAYOUT_NONE = 0, LAYOUT_SW128 = 2, LAYOUT_SW32 = 6;
+constexpr uint32_t LAYOUT_NONE = 0, LAYOUT_SW128_BASE32B = 1, LAYOUT_SW128 = 2, LAYOUT_SW32 = 6;
 
 // Instruction descriptor for kind::f16: D fp32, A/B bf16 (1) or f16 (0), both K-major,
 // N>>3 at [17,23), M>>4 at [24,29).
+// kind::tf32: D fp32, A/B TF32 (2), both K-major
+template <int BN>
+__host__ __device__ constexpr uint32_t instr_desc_tf32() {
+    return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BN >> 3) << 17) |
+           ((uint32_t)(BM >> 4) << 24);
+}
 template <int BN, bool F16>
 __host__ __device__ constexpr uint32_t instr_desc() {
     return (1u << 4) | ((F16 ? 0u : 1u) << 7) | ((F16 ? 0u : 1u) << 10) |
@@ -321,24 +351,45 @@ __device__ __forceinline__ uint32_t sw64(int r, int j) {
 // stages and doubles the independent pipelines per SM; it is chosen for short-K, memory-bound
 // layers where one CTA cannot keep enough loads and stores in flight.
 // EXTRA = mode-specific shared memory after the epilogue buffers (the stem's patch buffers).
-template <int BN, int OCC, int EXTRA = 0, int MT = 1, int EW = 4>
+// AB = operand copies per stage (2 for MODE_TF32: hi and lo).
+template <int BN, int OCC, int EXTRA = 0, int MT = 1, int EW = 4, int AB = 1>
 struct Cfg {
     static constexpr int EPI_BYTES = epi_bytes<EW>();
-    static constexpr int A_BYTES = MT * A_STAGE_BYTES;   // A bytes per stage
-    static constexpr int B_STAGE_BYTES = BN * BK * 2;
+    static constexpr int A_BYTES = MT * A_STAGE_BYTES * AB;   // A bytes per stage
+    static constexpr int B_STAGE_BYTES = BN * BK * 2 * AB;
     static constexpr int STAGE_BYTES = A_BYTES + B_STAGE_BYTES;
     static constexpr int BAR_BYTES = 1024;
     static constexpr int BUDGET = OCC == 1 ? MAX_DYN_SMEM : (233472 - 2048) / 2 - 1024;
     static constexpr int STAGES_RAW =
         (BUDGET - 1024 - BAR_BYTES - EPI_BYTES - EXTRA) / STAGE_BYTES;
     static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
-    static constexpr int TMEM_COLS = 2 * MT * BN < 32 ? 32 : 2 * MT * BN;
+    // two accumulators (double buffer); MODE_TF32 (AB = 2) keeps a main and a correction
+    // accumulator in each
+    static constexpr int ACC_COLS = MT * BN * AB;
+    static constexpr int TMEM_COLS = 2 * ACC_COLS < 32 ? 32 : 2 * ACC_COLS;
     // operand stages + epilogue buffers + extra + barriers/flags + slack for 1024-byte alignment
     static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_BYTES + EXTRA + BAR_BYTES + 1024;
     static_assert(SMEM_BYTES <= BUDGET, "shared memory budget");
     static_assert(STAGES >= 2, "pipeline depth");
     static_assert(TMEM_COLS * OCC <= 512, "TMEM budget");
 };
+
+// fp32 NCHW output chunk (MODE_TF32): row m = pixel (img, pq), 32 channels from n0; for each
+// channel the warp's 32 lanes store consecutive pixels. + bias, activation.
+__device__ __forceinline__ void store_chunk_nchw(const Params& p, int m, int n0,
+                                                 const uint32_t (&v)[32]) {
+    const int PQ = p.P * p.Q;
+    const int img = m / PQ;
+    float* base = static_cast<float*>(p.out) + (size_t)img * p.K * PQ + (m - img * PQ);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        const int k = n0 + j;
+        if (k >= p.K) break;
+        float o = __uint_as_float(v[j]);
+        if (p.bias) o += __ldg(p.bias + k);
+        base[(size_t)k * PQ] = apply_act(o, p.act);
+    }
+}
 
 // fp32-output chunk (classifier logits): + bias, + fp32 residual, activation, direct store
 __device__ __forceinline__ void store_chunk_f32(const Params& p, int m, int n0,
@@ -384,7 +435,8 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
                   "MT = 2 tiles");
     static_assert(EW == 4 || (EW == 16 && OCC == 1 && MODE != MODE_STEM) ||
                       (EW == 8 && MODE == MODE_STEM), "epilogue warps");
-    using C = Cfg<BN, OCC, extra_bytes<BN, MODE, OCC, EW>(), MT, EW>;
+    static_assert(MODE != MODE_TF32 || (MT == 1 && EW == 4 && OCC == 1), "TF32 tiles");
+    using C = Cfg<BN, OCC, extra_bytes<BN, MODE, OCC, EW>(), MT, EW, MODE == MODE_TF32 ? 2 : 1>;
     constexpr int EPI_BUFS = epi_bufs<EW>();
     constexpr int TM = BM * MT;   // output pixels per tile
     using H16 = Half16<DT>;
@@ -517,6 +569,24 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
                                 ++fr;
                             }
                         }
+                    } else if (MODE == MODE_TF32) {
+                        // kk = kb * 32 = (fr * S + fs) * Cs + c0 with Cs % 32 == 0 (fp32)
+                        mbar_expect_tx(&full[stage], C::STAGE_BYTES);
+                        tma_load_im2col(a_dst, &tmA, &full[stage], c0, wb, hb, img, (uint16_t)fs,
+                                        (uint16_t)fr);
+                        tma_load_im2col(a_dst + A_STAGE_BYTES, &tmRes, &full[stage], c0, wb, hb,
+                                        img, (uint16_t)fs, (uint16_t)fr);
+                        tma_load_2d(b_dst, &tmB, &full[stage], kb * 32, n0);
+                        tma_load_2d(b_dst + C::B_STAGE_BYTES / 2, &tmOut, &full[stage], kb * 32,
+                                    n0);
+                        c0 += 32;
+                        if (c0 == p.Cs) {
+                            c0 = 0;
+                            if (++fs == p.S) {
+                                fs = 0;
+                                ++fr;
+                            }
+                        }
                     } else if (MODE == MODE_SW32) {
                         // kk = kb * 64 + j * 16 = (fr * S + fs) * 16: box j is filter tap
                         // kb * 4 + j; the k-block holds nt of them (fewer only in the last)
@@ -629,7 +699,7 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
                     break;
                 }
                 tc_fence_after();
-                const uint32_t d_tmem = tmem_base + (uint32_t)(acc * MT * BN);
+                const uint32_t d_tmem = tmem_base + (uint32_t)(acc * C::ACC_COLS);
                 for (int kb = 0; kb < p.num_kb; ++kb) {
                     if (!mbar_wait(&full[stage], phase, abort_flag)) {
                         ok = false;
@@ -638,7 +708,25 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
                     tc_fence_after();
                     const uint64_t ad = adesc0 + (uint64_t)(stage * (C::A_BYTES >> 4));
                     const uint64_t bd = bdesc0 + (uint64_t)(stage * (C::B_STAGE_BYTES >> 4));
-                    if (MODE == MODE_SW32) {
+                    if (MODE == MODE_TF32) {
+                        // 3xTF32 per K=8 step: hi*hi into the main accumulator, lo*hi + hi*lo
+                        // into the correction accumulator (BN columns further). The tensor
+                        // core's accumulation error grows with the additions into an
+                        // accumulator; keeping the small terms apart leaves the main one a
+                        // third of them, and the two are added once, in fp32, by the epilogue.
+                        constexpr uint32_t IDESC_TF = instr_desc_tf32<BN>();
+                        constexpr uint64_t A_LO = A_STAGE_BYTES >> 4;
+                        constexpr uint64_t B_LO = (C::B_STAGE_BYTES / 2) >> 4;
+                        const uint32_t d_corr = d_tmem + (uint32_t)BN;
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) {
+                            const uint64_t ah = ad + k * A_K_STEP, bh = bd + k * B_K_STEP;
+                            const uint32_t acc_in = (kb > 0 || k > 0) ? 1u : 0u;
+                            tc_mma_tf32(d_corr, ah + A_LO, bh, IDESC_TF, acc_in);
+                            tc_mma_tf32(d_corr, ah, bh + B_LO, IDESC_TF, 1u);
+                            tc_mma_tf32(d_tmem, ah, bh, IDESC_TF, acc_in);
+                        }
+                    } else if (MODE == MODE_SW32) {
                         const int nt = sw32_taps(p, kb);
                         for (int k = 0; k < nt; ++k)
 #pragma unroll
@@ -810,7 +898,7 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
             }
             tc_fence_after();
             const uint32_t t_quarter = tmem_base + ((uint32_t)(quarter * 32) << 16) +
-                                       (uint32_t)(acc * MT * BN);
+                                       (uint32_t)(acc * C::ACC_COLS);
             int j = 0;   // live chunk index within this tile
 #pragma unroll 1
             for (int k = 0; k < KMAX; ++k) {
@@ -850,6 +938,13 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
                 }
                 uint32_t v[32];
                 tmem_ld32(t_quarter + (uint32_t)(mt * BN + c * 32), v);
+                if (MODE == MODE_TF32) {
+                    uint32_t vc[32];
+                    tmem_ld32(t_quarter + (uint32_t)(BN + c * 32), vc);
+#pragma unroll
+                    for (int q = 0; q < 32; ++q)
+                        v[q] = __float_as_uint(__uint_as_float(v[q]) + __uint_as_float(vc[q]));
+                }
                 if (chain && j >= 1) {
                     // live chunk j-1 of the next tile into the sub-tile of chunk g-1, whose store
                     // was issued a chunk ago
@@ -870,7 +965,10 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
                     pre_next = j;
                 }
                 if (!use_tma) {
-                    if (mw + lane < p.M) store_chunk_f32(p, mw + lane, n0, v);
+                    if (mw + lane < p.M) {
+                        if (MODE == MODE_TF32) store_chunk_nchw(p, mw + lane, n0, v);
+                        else store_chunk_f32(p, mw + lane, n0, v);
+                    }
                     ++g;
                     ++j;
                     continue;
@@ -1144,7 +1242,7 @@ static int encode_epilogue_map(CUtensorMap* map, const void* base, int rows, int
 template <int BN, int MODE, int DT, int OCC, int MT = 1, int EW = 4>
 static int launch(DeviceCtx* c, const CUtensorMap& ta, const CUtensorMap& tb,
                   const CUtensorMap& to, const CUtensorMap& tr, const Params& p) {
-    using Cf = Cfg<BN, OCC, extra_bytes<BN, MODE, OCC, EW>(), MT, EW>;
+    using Cf = Cfg<BN, OCC, extra_bytes<BN, MODE, OCC, EW>(), MT, EW, MODE == MODE_TF32 ? 2 : 1>;
     auto kern = conv_tc_kernel<BN, MODE, DT, OCC, MT, EW>;
     static bool attr_set[64] = {false};
     if (!attr_set[c->device]) {
@@ -1575,3 +1673,533 @@ extern "C" int omCudaStemConvBnAct(const float* pInput, void* pWorkspace, const 
     if (r != CUDA_SUCCESS) return OM_ERR_DRIVER;
     return finish_and_launch<MODE_STEM>(c, bn, occ, mt, ew, nDtype, ta, tb, p);
 }
+
+// ---------------------------------------------------------------- fp32 path (3xTF32)
+namespace omb {
+namespace tc {
+
+// TF32 rounding (to nearest, ties away) of an fp32 value, kept as an fp32 bit pattern
+__device__ __forceinline__ float tf32_rna(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return __uint_as_float(r);
+}
+
+// NCHW fp32 [N, Cin, Hin, Win] -> NHWC [N, Hp, Wp, Cs] split into hi = tf32(x) and
+// lo = tf32(x - hi): out[n, hp, wp, c] = x[n, c, (hp - offh) / up, (wp - offw) / up] where both
+// divisions are exact and land inside the input, else 0 (channels c >= Cin are 0). With
+// up = 1 and offsets 0 it is a plain layout change; the backward-input pass uses up = stride
+// (zero insertion) and offsets R-1-pad, S-1-pad. A block moves 32 pixels x 32 channels
+// through shared memory so that both the reads (along w) and the writes (along c) coalesce.
+// blocked = 1 writes the channel-blocked layout [Cs / 32][N*Hp*Wp][32] instead (the weight
+// gradient's dY operand, whose 32-channel blocks are then one TMA box dimension).
+__global__ void split_nhwc_kernel(const float* __restrict__ x, float* __restrict__ hi,
+                                  float* __restrict__ lo, int N, int Cin, int Hin, int Win, int Hp,
+                                  int Wp, int Cs, int offh, int offw, int up, int blocked) {
+    __shared__ float tile[32][33];
+    const int tx = threadIdx.x, ty = threadIdx.y;
+    const int wt = (Wp + 31) / 32;                 // blockIdx.x = hp * wt + pixel tile
+    const int hp = blockIdx.x / wt;
+    const int wp0 = (blockIdx.x - hp * wt) * 32, c0 = blockIdx.y * 32;
+    const int n = blockIdx.z;
+    const int i = hp - offh;
+    const bool row_ok = i >= 0 && i % up == 0 && i / up < Hin;
+    const int hs = row_ok ? i / up : 0;
+    for (int cc = ty; cc < 32; cc += 8) {
+        const int c = c0 + cc, wp = wp0 + tx, j = wp - offw;
+        float v = 0.f;
+        if (row_ok && c < Cin && wp < Wp && j >= 0 && j % up == 0 && j / up < Win)
+            v = __ldg(x + (((size_t)n * Cin + c) * Hin + hs) * Win + j / up);
+        tile[cc][tx] = v;
+    }
+    __syncthreads();
+    for (int pp = ty; pp < 32; pp += 8) {
+        const int wp = wp0 + pp;
+        if (wp >= Wp) continue;
+        const float v = tile[tx][pp];
+        const float h = tf32_rna(v);
+        const size_t pix = ((size_t)n * Hp + hp) * Wp + wp;
+        const size_t o = blocked ? ((size_t)(c0 / 32) * N * Hp * Wp + pix) * 32 + tx
+                                 : pix * Cs + c0 + tx;
+        hi[o] = h;
+        lo[o] = tf32_rna(v - h);
+    }
+}
+
+// Packed K-major hi/lo weights [Kout, R*S*Cs], kk = (r*S + s)*Cs + ci, from W [Kw, Cw, R, S]:
+// forward (flip = 0): row o = output channel, ci = input channel, W[o, ci, r, s];
+// backward-input (flip = 1): row o = input channel c, ci = output channel k, the filter
+// rotated by 180 degrees: W[ci, o, R-1-r, S-1-s]. Entries with ci >= Cinner are 0.
+__global__ void pack_tf32_weight_kernel(const float* __restrict__ w, float* __restrict__ hi,
+                                        float* __restrict__ lo, int Kout, int Cinner, int R, int S,
+                                        int Cs, int flip, int Cw) {
+    const long long kpad = (long long)R * S * Cs;
+    const long long total = (long long)Kout * kpad;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int o = (int)(i / kpad);
+        const int kk = (int)(i - (long long)o * kpad);
+        const int rs = kk / Cs, ci = kk - rs * Cs;
+        const int r = rs / S, s = rs - r * S;
+        float v = 0.f;
+        if (ci < Cinner)
+            v = flip ? w[(((size_t)ci * Cw + o) * R + (R - 1 - r)) * S + (S - 1 - s)]
+                     : w[(((size_t)o * Cw + ci) * R + r) * S + s];
+        const float h = tf32_rna(v);
+        hi[i] = h;
+        lo[i] = tf32_rna(v - h);
+    }
+}
+
+// One 3xTF32 convolution: the NCHW source is split into an NHWC copy [N, Hp, Wp, Cs] (see
+// split_nhwc_kernel), convolved (stride, pad) with the packed filter on the tensor cores, and
+// the result written as NCHW fp32 [N, Kout, P, Q]. Scratch comes from the stream-ordered pool.
+int tf32_conv(DeviceCtx* c, const float* src, int N, int Cin, int Hin, int Win, int Hp, int Wp,
+              int offh, int offw, int up, const float* w, int Kout, int R, int S, bool flip,
+              int Cw, const float* bias, float* out, int stride, int pad) {
+    const int Cs = (Cin + 31) / 32 * 32;
+    const int P = (Hp + 2 * pad - R) / stride + 1, Q = (Wp + 2 * pad - S) / stride + 1;
+    if (P <= 0 || Q <= 0) return OM_ERR_INVALID;
+    const long long Mll = (long long)N * P * Q;
+    const long long kpad = (long long)R * S * Cs;
+    if (Mll >= (1LL << 31) || kpad >= (1LL << 31) || N > 65535 ||
+        (long long)Hp * ((Wp + 31) / 32) >= (1LL << 31))
+        return OM_ERR_UNSUPPORTED;
+    if (-pad < -128 || pad - (R - 1) < -128 || pad - (S - 1) < -128 || pad - (R - 1) > 127 ||
+        pad - (S - 1) > 127)
+        return OM_ERR_UNSUPPORTED;
+    if (!load_driver_entry_points()) return OM_ERR_DRIVER;
+    const size_t xe = (size_t)N * Hp * Wp * Cs, we = (size_t)Kout * kpad;
+    const size_t xb = (xe * 4 + 255) / 256 * 256, wb = (we * 4 + 255) / 256 * 256;
+    uint8_t* scratch = nullptr;
+    OMB_CHECK(cudaMallocAsync(&scratch, 2 * xb + 2 * wb, c->compute));
+    float* xhi = reinterpret_cast<float*>(scratch);
+    float* xlo = reinterpret_cast<float*>(scratch + xb);
+    float* whi = reinterpret_cast<float*>(scratch + 2 * xb);
+    float* wlo = reinterpret_cast<float*>(scratch + 2 * xb + wb);
+    int st = OM_OK;
+    {
+        dim3 grid((unsigned)(Hp * ((Wp + 31) / 32)), Cs / 32, (unsigned)N);
+        split_nhwc_kernel<<<grid, dim3(32, 8), 0, c->compute>>>(src, xhi, xlo, N, Cin, Hin, Win,
+                                                               Hp, Wp, Cs, offh, offw, up, 0);
+        st = after_launch(c);
+    }
+    if (st == OM_OK) {
+        pack_tf32_weight_kernel<<<ew_grid(c, (long long)we, 256), 256, 0, c->compute>>>(
+            w, whi, wlo, Kout, Cin, R, S, Cs, flip ? 1 : 0, Cw);
+        st = after_launch(c);
+    }
+    if (st == OM_OK) {
+        Params p;
+        p.N = N; p.H = Hp; p.W = Wp; p.Cs = Cs; p.K = Kout;
+        p.R = R; p.S = S; p.stride = stride; p.pad = pad;
+        p.P = P; p.Q = Q; p.M = (int)Mll;
+        p.num_kb = (int)(kpad / 32);
+        const int bn = Kout <= 32 ? 32 : (Kout <= 64 ? 64 : 128);
+        p.num_m_tiles = (int)((Mll + BM - 1) / BM);
+        p.num_n_tiles = (Kout + bn - 1) / bn;
+        p.QT = 1;
+        p.box_w = 0;
+        p.bias = bias;
+        p.residual = nullptr;
+        p.out = out;
+        p.act = OM_ACT_NONE;
+        p.out_f32 = 1;
+        p.err = c->err_word;
+        // A: im2col views of the hi and lo copies, dims innermost-first (Cs, Wp, Hp, N)
+        CUtensorMap ta_hi, ta_lo, tb_hi, tb_lo;
+        cuuint64_t a_dims[4] = {(cuuint64_t)Cs, (cuuint64_t)Wp, (cuuint64_t)Hp, (cuuint64_t)N};
+        cuuint64_t a_strides[3] = {(cuuint64_t)Cs * 4, (cuuint64_t)Wp * Cs * 4,
+                                   (cuuint64_t)Hp * Wp * Cs * 4};
+        int lo_c[2] = {-pad, -pad};
+        int hi_c[2] = {pad - (S - 1), pad - (R - 1)};
+        cuuint32_t a_estr[4] = {1, (cuuint32_t)stride, (cuuint32_t)stride, 1};
+        for (int k = 0; k < 2 && st == OM_OK; ++k) {
+            CUtensorMap* m = k ? &ta_lo : &ta_hi;
+            CUresult r = g_encode_im2col(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, k ? xlo : xhi,
+                                         a_dims, a_strides, lo_c, hi_c, 32, BM, a_estr,
+                                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+            if (r != CUDA_SUCCESS) st = OM_ERR_DRIVER;
+            // drivers up to 13.1 mis-handle this bit for im2col tensors under 128 KiB (as CUTLASS)
+            else if (g_driver_version <= 13010 && xe * 4 < 131072ull)
+                reinterpret_cast<uint64_t*>(m)[1] &= ~(1ull << 21);
+        }
+        cuuint64_t b_dims[2] = {(cuuint64_t)kpad, (cuuint64_t)Kout};
+        cuuint64_t b_strides[1] = {(cuuint64_t)kpad * 4};
+        cuuint32_t b_box[2] = {32u, (cuuint32_t)bn};
+        cuuint32_t b_estr[2] = {1, 1};
+        for (int k = 0; k < 2 && st == OM_OK; ++k) {
+            CUresult r = g_encode_tiled(k ? &tb_lo : &tb_hi, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
+                                        k ? wlo : whi, b_dims, b_strides, b_box, b_estr,
+                                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+            if (r != CUDA_SUCCESS) st = OM_ERR_DRIVER;
+        }
+        if (st == OM_OK) {
+            // maps: A_hi, B_hi, B_lo (output slot), A_lo (residual slot)
+            switch (bn) {
+                case 32: st = launch<32, MODE_TF32, OM_DTYPE_BF16, 1, 1, 4>(c, ta_hi, tb_hi, tb_lo, ta_lo, p); break;
+                case 64: st = launch<64, MODE_TF32, OM_DTYPE_BF16, 1, 1, 4>(c, ta_hi, tb_hi, tb_lo, ta_lo, p); break;
+                default: st = launch<128, MODE_TF32, OM_DTYPE_BF16, 1, 1, 4>(c, ta_hi, tb_hi, tb_lo, ta_lo, p); break;
+            }
+        }
+    }
+    cudaFreeAsync(scratch, c->compute);
+    return st;
+}
+
+}  // namespace tc
+}  // namespace omb
+
+// ---------------------------------------------------------------- fp32 weight gradient (3xTF32)
+// dW[k, c, r, s] = sum over output pixels j = (n, p, q) of dY[n, k, p, q] * X[n, c, p*st-pad+r,
+// q*st-pad+s]: a GEMM with M = output channels k, N = (tap, input channel) and the long
+// reduction over j. Both operands are MN-major in shared memory, in the one layout the
+// tensor cores take for MN-major 32-bit operands (128-byte swizzle of 32-byte granules):
+//   A: dY in the channel-blocked layout [K/32][j][32] (hi and lo copies), one 3-D TMA box of
+//      4 blocks x 32 pixels = 128 output channels (32-element MN blocks LBO = 4 KB apart);
+//   B: the input's NHWC hi/lo copies through an im2col map with 32 pixels per box, BN/32 boxes
+//      of 32 channels for the tile's tap.
+// A tile is 128 output channels x BN channels of one tap over one split of the reduction
+// (32-pixel k-blocks); per K=8 step hi*hi goes to the main accumulator, lo*hi + hi*lo to the
+// correction one. Each split writes its fp32 partial [split][K][R*S][Cs]; wgrad_reduce_kernel
+// sums the splits in order into the reference layout. One tile per CTA: warp 0 loads, warp 1
+// issues the MMAs, warps 2-5 read the accumulators.
+namespace omb {
+namespace tc {
+
+struct WgradParams {
+    int N, K, Cs, R, S, stride, pad, P, Q;
+    int num_kb;    // 32-pixel k-blocks of the reduction
+    int cb;        // BN-wide channel slices per tap
+    int splits;
+    float* ws;     // [splits][K][R*S][Cs]
+    unsigned int* err;
+};
+
+template <int BN>
+struct WgCfg {
+    static constexpr int A_BOX = 128 * 32 * 4;      // 128 output channels x 32 pixels
+    static constexpr int B_BOX = BN * 32 * 4;       // BN channels x 32 pixels
+    static constexpr int STAGE = 2 * A_BOX + 2 * B_BOX;
+    static constexpr int RAW = (MAX_DYN_SMEM - 2048) / STAGE;
+    static constexpr int STAGES = RAW > 6 ? 6 : RAW;
+    static constexpr int SMEM = STAGES * STAGE + 2048;
+    static constexpr uint32_t TMEM = 2 * BN;        // main + correction accumulators
+};
+
+template <int BN>
+__global__ void __launch_bounds__(192, 1)
+    wgrad_tf32_kernel(const __grid_constant__ CUtensorMap tmA_hi,
+                      const __grid_constant__ CUtensorMap tmA_lo,
+                      const __grid_constant__ CUtensorMap tmB_hi,
+                      const __grid_constant__ CUtensorMap tmB_lo, const WgradParams p) {
+    using C = WgCfg<BN>;
+    constexpr int STAGES = C::STAGES;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE);
+    uint64_t* empty = full + STAGES;
+    uint64_t* done = empty + STAGES;
+    uint64_t* drain = done + 1;
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    const int RS = p.R * p.S;
+    const int tap = blockIdx.x / p.cb, cslice = blockIdx.x - tap * p.cb;
+    const int fr = tap / p.S, fs = tap - fr * p.S;
+    const int m_tile = blockIdx.y, z = blockIdx.z;
+    const int kb0 = (int)((long long)z * p.num_kb / p.splits);
+    const int kb1 = (int)((long long)(z + 1) * p.num_kb / p.splits);
+    const int PQ = p.P * p.Q;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < STAGES; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 1);
+        }
+        mbar_init(done, 1);
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        fence_async_smem();
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(tmem_holder)),
+                     "r"(C::TMEM));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_holder;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ------------------------------------------------------------ TMA producer
+            bool ok = true;
+            int n = 0;
+            for (int kb = kb0; kb < kb1; ++kb, ++n) {
+                const int st = n % STAGES;
+                if (!mbar_wait(&empty[st], (uint32_t)(((n / STAGES) & 1) ^ 1), abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                uint8_t* sa = smem + st * C::STAGE;
+                uint8_t* sb = sa + 2 * C::A_BOX;
+                const int j0 = kb * 32;
+                const int img = j0 / PQ, rem = j0 - img * PQ;
+                const int pp = rem / p.Q, qq = rem - pp * p.Q;
+                const int wb = qq * p.stride - p.pad, hb = pp * p.stride - p.pad;
+                mbar_expect_tx(&full[st], (uint32_t)C::STAGE);
+                tma_load_3d(sa, &tmA_hi, &full[st], 0, j0, m_tile * 4);
+                tma_load_3d(sa + C::A_BOX, &tmA_lo, &full[st], 0, j0, m_tile * 4);
+#pragma unroll
+                for (int i = 0; i < BN / 32; ++i) {
+                    const int c0 = cslice * BN + i * 32;
+                    tma_load_im2col(sb + i * 4096, &tmB_hi, &full[st], c0, wb, hb, img,
+                                    (uint16_t)fs, (uint16_t)fr);
+                    tma_load_im2col(sb + C::B_BOX + i * 4096, &tmB_lo, &full[st], c0, wb, hb, img,
+                                    (uint16_t)fs, (uint16_t)fr);
+                }
+            }
+            if (!ok) {
+                atomicOr(p.err, ERRBIT_TC_PRODUCER);
+                *abort_flag = 1;
+            }
+            // no TMA write may land after the CTA exits
+            for (int j = n - STAGES; j < n; ++j) {
+                if (j < 0) continue;
+                if (!mbar_wait_drain(&full[j % STAGES], (uint32_t)((j / STAGES) & 1))) {
+                    atomicOr(p.err, ERRBIT_TC_DRAIN);
+                    break;
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ------------------------------------------------------------ MMA issuer
+            // kind::tf32, M = 128, N = BN, A and B MN-major (bits 15, 16)
+            constexpr uint32_t IDESC = instr_desc_tf32<BN>() | (1u << 15) | (1u << 16);
+            // MN-major 32-bit operands use the 128-byte swizzle with 32-byte granules: atoms of
+            // 4 rows x 128 B (SBO = 512 B between them along K), 32-element MN blocks 4 KB apart
+            const uint64_t adesc0 = smem_desc(smem_u32(smem), 4096, 512, LAYOUT_SW128_BASE32B);
+            const uint64_t bdesc0 =
+                smem_desc(smem_u32(smem + 2 * C::A_BOX), 4096, 512, LAYOUT_SW128_BASE32B);
+            bool ok = true;
+            int n = 0;
+            for (int kb = kb0; kb < kb1; ++kb, ++n) {
+                const int st = n % STAGES;
+                if (!mbar_wait(&full[st], (uint32_t)((n / STAGES) & 1), abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint64_t so = (uint64_t)((st * C::STAGE) >> 4);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    // K step k = pixels 8k .. 8k+7 = rows 8k.. of every box: +1024 B
+                    const uint64_t ah = adesc0 + so + (uint64_t)(k * 64);
+                    const uint64_t bh = bdesc0 + so + (uint64_t)(k * 64);
+                    const uint32_t acc_in = (n > 0 || k > 0) ? 1u : 0u;
+                    tc_mma_tf32(tmem_base + BN, ah + (C::A_BOX >> 4), bh, IDESC, acc_in);
+                    tc_mma_tf32(tmem_base + BN, ah, bh + (C::B_BOX >> 4), IDESC, 1u);
+                    tc_mma_tf32(tmem_base, ah, bh, IDESC, acc_in);
+                }
+                tc_commit(&empty[st]);
+            }
+            if (!ok) {
+                atomicOr(p.err, ERRBIT_TC_MMA);
+                *abort_flag = 1;
+            }
+            tc_commit(done);
+            tc_commit(drain);
+            if (!mbar_wait_drain(drain, 0)) atomicOr(p.err, ERRBIT_TC_DRAIN);
+        }
+    } else {
+        // ---------------------------------------------------------------- epilogue
+        const int quarter = warp & 3;
+        const bool ok = __all_sync(0xffffffffu, mbar_wait(done, 0, abort_flag));
+        if (ok) {
+            tc_fence_after();
+            const int k = m_tile * 128 + quarter * 32 + lane;   // output channel of this row
+            const uint32_t t = tmem_base + ((uint32_t)(quarter * 32) << 16);
+            float* dst = p.ws + (((size_t)z * p.K + k) * RS + tap) * p.Cs + cslice * BN;
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+                uint32_t v[32], vc[32];
+                tmem_ld32(t + (uint32_t)(c * 32), v);
+                tmem_ld32(t + (uint32_t)(BN + c * 32), vc);
+                if (k < p.K) {
+                    float4* d4 = reinterpret_cast<float4*>(dst + c * 32);
+#pragma unroll
+                    for (int q = 0; q < 8; ++q)
+                        d4[q] = make_float4(__uint_as_float(v[4 * q]) + __uint_as_float(vc[4 * q]),
+                                            __uint_as_float(v[4 * q + 1]) + __uint_as_float(vc[4 * q + 1]),
+                                            __uint_as_float(v[4 * q + 2]) + __uint_as_float(vc[4 * q + 2]),
+                                            __uint_as_float(v[4 * q + 3]) + __uint_as_float(vc[4 * q + 3]));
+                }
+            }
+        } else if (lane == 0) {
+            atomicOr(p.err, ERRBIT_TC_EPILOGUE);
+            *abort_flag = 1;
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) {
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                     "r"(C::TMEM));
+    }
+}
+
+// dW[k, c, r, s] = sum over splits (in order) of ws[split][k][r*S + s][c]
+__global__ void wgrad_reduce_kernel(const float* __restrict__ ws, float* __restrict__ dw, int K,
+                                    int C, int RS, int Cs, int splits) {
+    const long long total = (long long)K * C * RS;
+    const size_t split_elems = (size_t)K * RS * Cs;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int rs = (int)(i % RS);
+        const long long t = i / RS;
+        const int c = (int)(t % C), k = (int)(t / C);
+        const size_t o = ((size_t)k * RS + rs) * Cs + c;
+        float sum = 0.f;
+        for (int z = 0; z < splits; ++z) sum += ws[z * split_elems + o];
+        dw[i] = sum;
+    }
+}
+
+template <int BN>
+static int launch_wgrad(DeviceCtx* c, const CUtensorMap& a_hi, const CUtensorMap& a_lo,
+                        const CUtensorMap& b_hi, const CUtensorMap& b_lo, const WgradParams& p,
+                        dim3 grid) {
+    using Cf = WgCfg<BN>;
+    auto kern = wgrad_tf32_kernel<BN>;
+    static bool attr_set[64] = {false};
+    if (!attr_set[c->device]) {
+        OMB_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM));
+        attr_set[c->device] = true;
+    }
+    kern<<<grid, 192, Cf::SMEM, c->compute>>>(a_hi, a_lo, b_hi, b_lo, p);
+    return after_launch(c);
+}
+
+// The fp32 weight gradient of a (stride, pad) convolution, NCHW in and out, 3xTF32 on the
+// tensor cores. Scratch (the hi/lo copies of X and dY and the split partials) comes from the
+// stream-ordered pool.
+int tf32_wgrad(DeviceCtx* c, const float* x, const float* dy, float* dw, int N, int Cin, int H,
+               int W, int K, int R, int S, int stride, int pad) {
+    const int P = (H + 2 * pad - R) / stride + 1, Q = (W + 2 * pad - S) / stride + 1;
+    if (P <= 0 || Q <= 0) return OM_ERR_INVALID;
+    const int Cs = (Cin + 31) / 32 * 32, Ks = (K + 31) / 32 * 32;
+    const long long NPQ = (long long)N * P * Q;
+    if (NPQ >= (1LL << 31) - 64 || N > 65535 || (long long)H * ((W + 31) / 32) >= (1LL << 31) ||
+        (long long)P * ((Q + 31) / 32) >= (1LL << 31))
+        return OM_ERR_UNSUPPORTED;
+    if (-pad < -128 || pad - (R - 1) < -128 || pad - (S - 1) < -128 || pad - (R - 1) > 127 ||
+        pad - (S - 1) > 127)
+        return OM_ERR_UNSUPPORTED;
+    if (!load_driver_entry_points()) return OM_ERR_DRIVER;
+    // channel slice per tile: the widest of 128, 64, 32 that divides Cs (a multiple of 32)
+    const int bnc = Cs % 128 == 0 ? 128 : (Cs % 64 == 0 ? 64 : 32);
+    const int cb = Cs / bnc;
+    const int RS = R * S;
+    const int num_kb = (int)((NPQ + 31) / 32);
+    const int m_tiles = (K + 127) / 128;
+    const long long tiles = (long long)RS * cb * m_tiles;
+    long long want = (2LL * c->num_sms + tiles - 1) / tiles;
+    long long cap = num_kb < 256 ? num_kb : 256;
+    const int splits = (int)(want < 1 ? 1 : (want > cap ? cap : want));
+    if (tiles > 65535LL * 1024) return OM_ERR_UNSUPPORTED;
+
+    const size_t xe = (size_t)N * H * W * Cs, ye = (size_t)Ks * NPQ;
+    const size_t we = (size_t)splits * K * RS * Cs;
+    auto r256 = [](size_t b) { return (b + 255) / 256 * 256; };
+    const size_t xb = r256(xe * 4), yb = r256(ye * 4), wb = r256(we * 4);
+    uint8_t* scratch = nullptr;
+    OMB_CHECK(cudaMallocAsync(&scratch, 2 * xb + 2 * yb + wb, c->compute));
+    float* xhi = reinterpret_cast<float*>(scratch);
+    float* xlo = reinterpret_cast<float*>(scratch + xb);
+    float* yhi = reinterpret_cast<float*>(scratch + 2 * xb);
+    float* ylo = reinterpret_cast<float*>(scratch + 2 * xb + yb);
+    float* ws = reinterpret_cast<float*>(scratch + 2 * xb + 2 * yb);
+    int st = OM_OK;
+    {
+        dim3 gx((unsigned)(H * ((W + 31) / 32)), Cs / 32, (unsigned)N);
+        split_nhwc_kernel<<<gx, dim3(32, 8), 0, c->compute>>>(x, xhi, xlo, N, Cin, H, W, H, W, Cs,
+                                                             0, 0, 1, 0);
+        st = after_launch(c);
+    }
+    if (st == OM_OK) {
+        dim3 gy((unsigned)(P * ((Q + 31) / 32)), Ks / 32, (unsigned)N);
+        split_nhwc_kernel<<<gy, dim3(32, 8), 0, c->compute>>>(dy, yhi, ylo, N, K, P, Q, P, Q, Ks,
+                                                             0, 0, 1, 1);
+        st = after_launch(c);
+    }
+    CUtensorMap a_hi, a_lo, b_hi, b_lo;
+    if (st == OM_OK) {
+        // A: blocked dY as (32, NPQ, Ks/32), box (32, 32, 4)
+        cuuint64_t dims[3] = {32, (cuuint64_t)NPQ, (cuuint64_t)(Ks / 32)};
+        cuuint64_t strides[2] = {128, (cuuint64_t)NPQ * 128};
+        cuuint32_t box[3] = {32, 32, 4};
+        cuuint32_t estr[3] = {1, 1, 1};
+        for (int k = 0; k < 2 && st == OM_OK; ++k) {
+            CUresult r = g_encode_tiled(k ? &a_lo : &a_hi, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3,
+                                        k ? ylo : yhi, dims, strides, box, estr,
+                                        CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                        CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B,
+                                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+            if (r != CUDA_SUCCESS) st = OM_ERR_DRIVER;
+        }
+        // B: im2col of the NHWC input, 32 pixels x 32 channels per box
+        cuuint64_t bd[4] = {(cuuint64_t)Cs, (cuuint64_t)W, (cuuint64_t)H, (cuuint64_t)N};
+        cuuint64_t bs[3] = {(cuuint64_t)Cs * 4, (cuuint64_t)W * Cs * 4, (cuuint64_t)H * W * Cs * 4};
+        int lo_c[2] = {-pad, -pad};
+        int hi_c[2] = {pad - (S - 1), pad - (R - 1)};
+        cuuint32_t bestr[4] = {1, (cuuint32_t)stride, (cuuint32_t)stride, 1};
+        for (int k = 0; k < 2 && st == OM_OK; ++k) {
+            CUtensorMap* m = k ? &b_lo : &b_hi;
+            CUresult r = g_encode_im2col(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, k ? xlo : xhi, bd,
+                                         bs, lo_c, hi_c, 32, 32, bestr,
+                                         CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                         CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B,
+                                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+            if (r != CUDA_SUCCESS) st = OM_ERR_DRIVER;
+            else if (g_driver_version <= 13010 && xe * 4 < 131072ull)
+                reinterpret_cast<uint64_t*>(m)[1] &= ~(1ull << 21);
+        }
+    }
+    if (st == OM_OK) {
+        WgradParams p;
+        p.N = N; p.K = K; p.Cs = Cs; p.R = R; p.S = S; p.stride = stride; p.pad = pad;
+        p.P = P; p.Q = Q; p.num_kb = num_kb; p.cb = cb; p.splits = splits; p.ws = ws;
+        p.err = c->err_word;
+        dim3 grid((unsigned)(RS * cb), (unsigned)m_tiles, (unsigned)splits);
+        switch (bnc) {
+            case 32: st = launch_wgrad<32>(c, a_hi, a_lo, b_hi, b_lo, p, grid); break;
+            case 64: st = launch_wgrad<64>(c, a_hi, a_lo, b_hi, b_lo, p, grid); break;
+            default: st = launch_wgrad<128>(c, a_hi, a_lo, b_hi, b_lo, p, grid); break;
+        }
+    }
+    if (st == OM_OK) {
+        const long long total = (long long)K * Cin * RS;
+        wgrad_reduce_kernel<<<ew_grid(c, total, 256), 256, 0, c->compute>>>(ws, dw, K, Cin, RS, Cs,
+                                                                             splits);
+        st = after_launch(c);
+    }
+    cudaFreeAsync(scratch, c->compute);
+    return st;
+}
+
+}  // namespace tc
+}  // namespace omb

@@ -241,6 +241,10 @@ extern "C" int omCudaConv2d(const float* pInput, const float* pWeight, const flo
     if (!pInput || !pWeight || !pOutput || nStride <= 0) return OM_ERR_INVALID;
     int P = (nH + 2 * nPad - nKH) / nStride + 1, Q = (nW + 2 * nPad - nKW) / nStride + 1;
     if (P <= 0 || Q <= 0) return OM_ERR_INVALID;
+    // tensor cores (3xTF32) first; the SIMT kernel covers what they do not
+    int st = omb::tc::tf32_conv(c, pInput, nBatch, nCin, nH, nW, nH, nW, 0, 0, 1, pWeight, nCout,
+                                nKH, nKW, false, nCin, pBias, pOutput, nStride, nPad);
+    if (st != OM_ERR_UNSUPPORTED) return st;
     ConvFwdOp op{pInput, pWeight, pBias, pOutput, nCin, nH, nW, nKH, nKW, nStride, nPad, P, Q,
                  nCin * nKH * nKW, nCout};
     return run_gemm(c, op, nCout, nBatch * P * Q, nCin * nKH * nKW, 1);
@@ -271,6 +275,14 @@ extern "C" int omCudaConv2dBackwardInput(const float* pGradOutput, const float* 
     if (!pGradOutput || !pWeight || !pGradInput || nStride <= 0) return OM_ERR_INVALID;
     int P = (nH + 2 * nPad - nKH) / nStride + 1, Q = (nW + 2 * nPad - nKW) / nStride + 1;
     if (P <= 0 || Q <= 0) return OM_ERR_INVALID;
+    // dX = (zero-inserted, padded dY) convolved with the rotated, transposed filter, stride 1:
+    // dY[n,k,p,q] lands at (R-1-pad + p*stride, S-1-pad + q*stride) of an (H+R-1) x (W+S-1) grid
+    if (nPad <= nKH - 1 && nPad <= nKW - 1) {
+        int st = omb::tc::tf32_conv(c, pGradOutput, nBatch, nCout, P, Q, nH + nKH - 1, nW + nKW - 1,
+                                    nKH - 1 - nPad, nKW - 1 - nPad, nStride, pWeight, nCin, nKH,
+                                    nKW, true, nCin, nullptr, pGradInput, 1, 0);
+        if (st != OM_ERR_UNSUPPORTED) return st;
+    }
     ConvDgradOp op{pGradOutput, pWeight, pGradInput, nCin, nH, nW, nCout, nKH, nKW, nStride, nPad, P, Q};
     return run_gemm(c, op, nCin, nBatch * nH * nW, nCout * nKH * nKW, 1);
 }
@@ -286,6 +298,14 @@ extern "C" int omCudaConv2dBackwardWeight(const float* pInput, const float* pGra
     const int CRS = nCin * nKH * nKW;
     const long long red = (long long)nBatch * P * Q;
     if (red >= (1LL << 31)) return OM_ERR_UNSUPPORTED;
+    // tensor cores (3xTF32) first; the SIMT kernel covers what they do not
+    int tst = omb::tc::tf32_wgrad(c, pInput, pGradOutput, pGradWeight, nBatch, nCin, nH, nW, nCout,
+                                  nKH, nKW, nStride, nPad);
+    if (tst != OM_ERR_UNSUPPORTED) {
+        if (tst != OM_OK || !pGradBias) return tst;
+        bias_grad_nchw_kernel<<<nCout, 256, 0, c->compute>>>(pGradOutput, pGradBias, nBatch, nCout, P * Q);
+        return after_launch(c);
+    }
     // enough splits to give every SM a few blocks, each split at least 256 long
     long long tiles = (long long)((CRS + BN - 1) / BN) * ((nCout + BM - 1) / BM);
     long long want = (4LL * c->num_sms + tiles - 1) / tiles;

@@ -49,6 +49,20 @@ CONV = [  # n, c, h, k, r, stride, pad, bias
     (3, 32, 14, 24, 3, 2, 1, True),
     (2, 64, 8, 128, 1, 2, 0, False),
     (1, 8, 9, 8, 5, 1, 2, True),
+    # the tensor-core (3xTF32) path: several 32-channel k-blocks and 32..128-wide output tiles,
+    # partial tiles in both dimensions, stride-2 backward-input through zero insertion
+    (4, 64, 28, 128, 3, 1, 1, False),
+    (2, 128, 14, 256, 3, 2, 1, True),
+    (8, 96, 16, 40, 1, 1, 0, False),
+    (2, 256, 7, 512, 3, 1, 1, False),
+    # every conv shape of the batch-4, 64x64 ResNet-18 training test (down to 2x2 maps)
+    (4, 3, 64, 64, 7, 2, 3, False),
+    (4, 64, 16, 64, 3, 1, 1, False),
+    (4, 128, 8, 256, 3, 2, 1, False),
+    (4, 128, 8, 256, 1, 2, 0, False),
+    (4, 256, 4, 256, 3, 1, 1, False),
+    (4, 256, 4, 512, 3, 2, 1, False),
+    (4, 512, 2, 512, 3, 1, 1, False),
 ]
 
 

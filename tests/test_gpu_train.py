@@ -57,6 +57,8 @@ def test_resnet18_training_step_small(gpu):
     assert np.isfinite(loss)
     assert abs(loss - oloss) <= 1e-4 * abs(oloss), (loss, oloss)
     errs = {name: rel_err(grads[name], ograds[name]) for name, _ in net.params}
+    print(f"small: loss err {abs(loss - oloss) / abs(oloss):.2e}, gradient error median "
+          f"{np.median(list(errs.values())):.2e} max {max(errs.values()):.2e}")
     assert float(np.median(list(errs.values()))) <= 1e-4, sorted(errs.items(), key=lambda t: -t[1])[:5]
     assert max(errs.values()) <= 1e-2, sorted(errs.items(), key=lambda t: -t[1])[:5]
     assert rel_err(new_fc, ow["fc.weight"]) <= 1e-5
@@ -69,6 +71,9 @@ def test_resnet18_training_step_config3(gpu):
     assert abs(loss - oloss) <= 1e-4 * abs(oloss), (loss, oloss)
     errs = np.array([rel_err(grads[name], ograds[name]) for name, _ in net.params])
     ref = gold["train_r18_224_ref_grad_err"]
+    print(f"config3: loss err {abs(loss - oloss) / abs(oloss):.2e}, gradient error median "
+          f"{np.median(errs):.4f} max {errs.max():.4f} (reference fp32: {np.median(ref):.4f}, "
+          f"{ref.max():.4f})")
     assert np.median(errs) <= np.median(ref), (np.median(errs), np.median(ref))
     assert errs.max() <= ref.max(), (errs.max(), ref.max())
     assert rel_err(new_fc, ow["fc.weight"]) <= 1e-4
@@ -98,5 +103,6 @@ def test_config1_resnet18_fp32_inference(gpu):
         dx.free()
     assert gpu.kernel_error() == 0
     assert np.array_equal(got, again)
+    print(f"config1: logits max rel err {rel_err(got, want):.2e}")
     assert rel_err(got, want) <= 1e-4, rel_err(got, want)
     assert np.array_equal(got.argmax(1), want.argmax(1))
