@@ -1751,6 +1751,105 @@ __global__ void pack_tf32_weight_kernel(const float* __restrict__ w, float* __re
     }
 }
 
+// fp32 space-to-depth copy for stride-f convolutions with Cin * f * f <= 32 channels (the
+// weight gradient of the image stem):
+// NCHW [N, Cin, H, W] -> NHWC [N, Hs, Ws, 32] hi/lo with channel (c*f + py)*f + px holding
+// x[n, c, f*u + py - pad, f*v + px - pad] (0 outside the image and past Cin*f*f). One thread
+// per output element; the 32 channels of a pixel are written by consecutive threads.
+__global__ void s2d_split_kernel(const float* __restrict__ x, float* __restrict__ hi,
+                                 float* __restrict__ lo, int N, int Cin, int H, int W, int Hs,
+                                 int Ws, int f, int pad) {
+    const long long total = (long long)N * Hs * Ws * 32;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int ch = (int)(i & 31);
+        const long long pix = i >> 5;
+        const int v = (int)(pix % Ws);
+        const long long t = pix / Ws;
+        const int u = (int)(t % Hs), n = (int)(t / Hs);
+        float val = 0.f;
+        if (ch < Cin * f * f) {
+            const int c = ch / (f * f), py = (ch / f) % f, px = ch % f;
+            const int h = f * u + py - pad, w = f * v + px - pad;
+            if (h >= 0 && h < H && w >= 0 && w < W)
+                val = __ldg(x + (((size_t)n * Cin + c) * H + h) * W + w);
+        }
+        const float hv = tf32_rna(val);
+        hi[i] = hv;
+        lo[i] = tf32_rna(val - hv);
+    }
+}
+
+// A 3xTF32 convolution over prebuilt NHWC hi/lo copies [N, Hp, Wp, Cs] (Cs % 32 == 0) with a
+// packed hi/lo filter [Kout, R*S*Cs]: result NCHW fp32 [N, Kout, P, Q] (+bias).
+static int tf32_conv_run(DeviceCtx* c, float* xhi, float* xlo, int N, int Hp, int Wp, int Cs,
+                         float* whi, float* wlo, int Kout, int R, int S, const float* bias,
+                         float* out, int stride, int pad) {
+    const int P = (Hp + 2 * pad - R) / stride + 1, Q = (Wp + 2 * pad - S) / stride + 1;
+    const long long Mll = (long long)N * P * Q;
+    const long long kpad = (long long)R * S * Cs;
+    const size_t xe = (size_t)N * Hp * Wp * Cs;
+    Params p;
+    p.N = N; p.H = Hp; p.W = Wp; p.Cs = Cs; p.K = Kout;
+    p.R = R; p.S = S; p.stride = stride; p.pad = pad;
+    p.P = P; p.Q = Q; p.M = (int)Mll;
+    p.num_kb = (int)(kpad / 32);
+    const int bn = Kout <= 32 ? 32 : (Kout <= 64 ? 64 : 128);
+    p.num_m_tiles = (int)((Mll + BM - 1) / BM);
+    p.num_n_tiles = (Kout + bn - 1) / bn;
+    p.QT = 1;
+    p.box_w = 0;
+    p.bias = bias;
+    p.residual = nullptr;
+    p.out = out;
+    p.act = OM_ACT_NONE;
+    p.out_f32 = 1;
+    p.err = c->err_word;
+    // A: im2col views of the hi and lo copies, dims innermost-first (Cs, Wp, Hp, N)
+    CUtensorMap ta_hi, ta_lo, tb_hi, tb_lo;
+    cuuint64_t a_dims[4] = {(cuuint64_t)Cs, (cuuint64_t)Wp, (cuuint64_t)Hp, (cuuint64_t)N};
+    cuuint64_t a_strides[3] = {(cuuint64_t)Cs * 4, (cuuint64_t)Wp * Cs * 4,
+                               (cuuint64_t)Hp * Wp * Cs * 4};
+    int lo_c[2] = {-pad, -pad};
+    int hi_c[2] = {pad - (S - 1), pad - (R - 1)};
+    cuuint32_t a_estr[4] = {1, (cuuint32_t)stride, (cuuint32_t)stride, 1};
+    for (int k = 0; k < 2; ++k) {
+        CUtensorMap* m = k ? &ta_lo : &ta_hi;
+        CUresult r = g_encode_im2col(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, k ? xlo : xhi, a_dims,
+                                     a_strides, lo_c, hi_c, 32, BM, a_estr,
+                                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) return OM_ERR_DRIVER;
+        // drivers up to 13.1 mis-handle this bit for im2col tensors under 128 KiB (as CUTLASS)
+        if (g_driver_version <= 13010 && xe * 4 < 131072ull)
+            reinterpret_cast<uint64_t*>(m)[1] &= ~(1ull << 21);
+    }
+    cuuint64_t b_dims[2] = {(cuuint64_t)kpad, (cuuint64_t)Kout};
+    cuuint64_t b_strides[1] = {(cuuint64_t)kpad * 4};
+    cuuint32_t b_box[2] = {32u, (cuuint32_t)bn};
+    cuuint32_t b_estr[2] = {1, 1};
+    for (int k = 0; k < 2; ++k) {
+        CUresult r = g_encode_tiled(k ? &tb_lo : &tb_hi, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
+                                    k ? wlo : whi, b_dims, b_strides, b_box, b_estr,
+                                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) return OM_ERR_DRIVER;
+    }
+    // maps: A_hi, B_hi, B_lo (output slot), A_lo (residual slot)
+    switch (bn) {
+        case 32: return launch<32, MODE_TF32, OM_DTYPE_BF16, 1, 1, 4>(c, ta_hi, tb_hi, tb_lo, ta_lo, p);
+        case 64: return launch<64, MODE_TF32, OM_DTYPE_BF16, 1, 1, 4>(c, ta_hi, tb_hi, tb_lo, ta_lo, p);
+        default: return launch<128, MODE_TF32, OM_DTYPE_BF16, 1, 1, 4>(c, ta_hi, tb_hi, tb_lo, ta_lo, p);
+    }
+}
+
+static bool tf32_pad_ok(int R, int S, int pad) {
+    return -pad >= -128 && pad - (R - 1) >= -128 && pad - (S - 1) >= -128 &&
+           pad - (R - 1) <= 127 && pad - (S - 1) <= 127;
+}
+
 // One 3xTF32 convolution: the NCHW source is split into an NHWC copy [N, Hp, Wp, Cs] (see
 // split_nhwc_kernel), convolved (stride, pad) with the packed filter on the tensor cores, and
 // the result written as NCHW fp32 [N, Kout, P, Q]. Scratch comes from the stream-ordered pool.
@@ -1763,10 +1862,7 @@ int tf32_conv(DeviceCtx* c, const float* src, int N, int Cin, int Hin, int Win, 
     const long long Mll = (long long)N * P * Q;
     const long long kpad = (long long)R * S * Cs;
     if (Mll >= (1LL << 31) || kpad >= (1LL << 31) || N > 65535 ||
-        (long long)Hp * ((Wp + 31) / 32) >= (1LL << 31))
-        return OM_ERR_UNSUPPORTED;
-    if (-pad < -128 || pad - (R - 1) < -128 || pad - (S - 1) < -128 || pad - (R - 1) > 127 ||
-        pad - (S - 1) > 127)
+        (long long)Hp * ((Wp + 31) / 32) >= (1LL << 31) || !tf32_pad_ok(R, S, pad))
         return OM_ERR_UNSUPPORTED;
     if (!load_driver_entry_points()) return OM_ERR_DRIVER;
     const size_t xe = (size_t)N * Hp * Wp * Cs, we = (size_t)Kout * kpad;
@@ -1789,66 +1885,30 @@ int tf32_conv(DeviceCtx* c, const float* src, int N, int Cin, int Hin, int Win, 
             w, whi, wlo, Kout, Cin, R, S, Cs, flip ? 1 : 0, Cw);
         st = after_launch(c);
     }
-    if (st == OM_OK) {
-        Params p;
-        p.N = N; p.H = Hp; p.W = Wp; p.Cs = Cs; p.K = Kout;
-        p.R = R; p.S = S; p.stride = stride; p.pad = pad;
-        p.P = P; p.Q = Q; p.M = (int)Mll;
-        p.num_kb = (int)(kpad / 32);
-        const int bn = Kout <= 32 ? 32 : (Kout <= 64 ? 64 : 128);
-        p.num_m_tiles = (int)((Mll + BM - 1) / BM);
-        p.num_n_tiles = (Kout + bn - 1) / bn;
-        p.QT = 1;
-        p.box_w = 0;
-        p.bias = bias;
-        p.residual = nullptr;
-        p.out = out;
-        p.act = OM_ACT_NONE;
-        p.out_f32 = 1;
-        p.err = c->err_word;
-        // A: im2col views of the hi and lo copies, dims innermost-first (Cs, Wp, Hp, N)
-        CUtensorMap ta_hi, ta_lo, tb_hi, tb_lo;
-        cuuint64_t a_dims[4] = {(cuuint64_t)Cs, (cuuint64_t)Wp, (cuuint64_t)Hp, (cuuint64_t)N};
-        cuuint64_t a_strides[3] = {(cuuint64_t)Cs * 4, (cuuint64_t)Wp * Cs * 4,
-                                   (cuuint64_t)Hp * Wp * Cs * 4};
-        int lo_c[2] = {-pad, -pad};
-        int hi_c[2] = {pad - (S - 1), pad - (R - 1)};
-        cuuint32_t a_estr[4] = {1, (cuuint32_t)stride, (cuuint32_t)stride, 1};
-        for (int k = 0; k < 2 && st == OM_OK; ++k) {
-            CUtensorMap* m = k ? &ta_lo : &ta_hi;
-            CUresult r = g_encode_im2col(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, k ? xlo : xhi,
-                                         a_dims, a_strides, lo_c, hi_c, 32, BM, a_estr,
-                                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-            if (r != CUDA_SUCCESS) st = OM_ERR_DRIVER;
-            // drivers up to 13.1 mis-handle this bit for im2col tensors under 128 KiB (as CUTLASS)
-            else if (g_driver_version <= 13010 && xe * 4 < 131072ull)
-                reinterpret_cast<uint64_t*>(m)[1] &= ~(1ull << 21);
-        }
-        cuuint64_t b_dims[2] = {(cuuint64_t)kpad, (cuuint64_t)Kout};
-        cuuint64_t b_strides[1] = {(cuuint64_t)kpad * 4};
-        cuuint32_t b_box[2] = {32u, (cuuint32_t)bn};
-        cuuint32_t b_estr[2] = {1, 1};
-        for (int k = 0; k < 2 && st == OM_OK; ++k) {
-            CUresult r = g_encode_tiled(k ? &tb_lo : &tb_hi, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
-                                        k ? wlo : whi, b_dims, b_strides, b_box, b_estr,
-                                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-            if (r != CUDA_SUCCESS) st = OM_ERR_DRIVER;
-        }
-        if (st == OM_OK) {
-            // maps: A_hi, B_hi, B_lo (output slot), A_lo (residual slot)
-            switch (bn) {
-                case 32: st = launch<32, MODE_TF32, OM_DTYPE_BF16, 1, 1, 4>(c, ta_hi, tb_hi, tb_lo, ta_lo, p); break;
-                case 64: st = launch<64, MODE_TF32, OM_DTYPE_BF16, 1, 1, 4>(c, ta_hi, tb_hi, tb_lo, ta_lo, p); break;
-                default: st = launch<128, MODE_TF32, OM_DTYPE_BF16, 1, 1, 4>(c, ta_hi, tb_hi, tb_lo, ta_lo, p); break;
-            }
-        }
-    }
+    if (st == OM_OK)
+        st = tf32_conv_run(c, xhi, xlo, N, Hp, Wp, Cs, whi, wlo, Kout, R, S, bias, out, stride, pad);
     cudaFreeAsync(scratch, c->compute);
     return st;
+}
+
+// Geometry of the space-to-depth form of a stride-2 convolution (Cin * 4 <= 32): the 32-channel
+// copy is Hs x Ws and the filter th x tw, stride 1, no padding. Only the weight gradient uses
+// it. The forward keeps the plain form: in the batch-4 training parity case, the space-to-depth
+// form's different rounding (no larger) moved a residual sum of ~1e-6 across zero two blocks
+// later, and that one ReLU decision set a BatchNorm gradient several percent off the exact one.
+struct S2dGeom {
+    int P, Q, th, tw, Hs, Ws;
+};
+static bool s2d_geom(int Cin, int H, int W, int R, int S, int stride, int pad, S2dGeom* g) {
+    if (stride != 2 || Cin * 4 > 32 || pad < 0) return false;
+    g->P = (H + 2 * pad - R) / 2 + 1;
+    g->Q = (W + 2 * pad - S) / 2 + 1;
+    if (g->P <= 0 || g->Q <= 0) return false;
+    g->th = (R + 1) / 2;
+    g->tw = (S + 1) / 2;
+    g->Hs = g->P + g->th - 1;
+    g->Ws = g->Q + g->tw - 1;
+    return true;
 }
 
 }  // namespace tc
@@ -1874,7 +1934,9 @@ namespace tc {
 struct WgradParams {
     int N, K, Cs, R, S, stride, pad, P, Q;
     int num_kb;    // 32-pixel k-blocks of the reduction
-    int cb;        // BN-wide channel slices per tap
+    int tpt;       // taps per tile
+    int csl;       // channels per tap in a tile (tpt * csl = the tile's 128 columns)
+    int cb;        // channel slices per tap (Cs / csl)
     int splits;
     float* ws;     // [splits][K][R*S][Cs]
     unsigned int* err;
@@ -1911,8 +1973,8 @@ __global__ void __launch_bounds__(192, 1)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     const int RS = p.R * p.S;
-    const int tap = blockIdx.x / p.cb, cslice = blockIdx.x - tap * p.cb;
-    const int fr = tap / p.S, fs = tap - fr * p.S;
+    const int group = blockIdx.x / p.cb, cslice = blockIdx.x - group * p.cb;
+    const int bpt = p.csl / 32;              // 32-channel boxes per tap
     const int m_tile = blockIdx.y, z = blockIdx.z;
     const int kb0 = (int)((long long)z * p.num_kb / p.splits);
     const int kb1 = (int)((long long)(z + 1) * p.num_kb / p.splits);
@@ -1962,7 +2024,13 @@ __global__ void __launch_bounds__(192, 1)
                 tma_load_3d(sa + C::A_BOX, &tmA_lo, &full[st], 0, j0, m_tile * 4);
 #pragma unroll
                 for (int i = 0; i < BN / 32; ++i) {
-                    const int c0 = cslice * BN + i * 32;
+                    // box i: tap group * tpt + i / bpt (a tap past the last one reloads the
+                    // last; its columns are never stored), channels from (i % bpt) * 32
+                    const int ti = i / bpt;
+                    int tap = group * p.tpt + ti;
+                    if (tap >= RS) tap = RS - 1;
+                    const int fr = tap / p.S, fs = tap - fr * p.S;
+                    const int c0 = cslice * p.csl + (i - ti * bpt) * 32;
                     tma_load_im2col(sb + i * 4096, &tmB_hi, &full[st], c0, wb, hb, img,
                                     (uint16_t)fs, (uint16_t)fr);
                     tma_load_im2col(sb + C::B_BOX + i * 4096, &tmB_lo, &full[st], c0, wb, hb, img,
@@ -2030,14 +2098,17 @@ __global__ void __launch_bounds__(192, 1)
             tc_fence_after();
             const int k = m_tile * 128 + quarter * 32 + lane;   // output channel of this row
             const uint32_t t = tmem_base + ((uint32_t)(quarter * 32) << 16);
-            float* dst = p.ws + (((size_t)z * p.K + k) * RS + tap) * p.Cs + cslice * BN;
 #pragma unroll 1
             for (int c = 0; c < BN / 32; ++c) {
                 uint32_t v[32], vc[32];
                 tmem_ld32(t + (uint32_t)(c * 32), v);
                 tmem_ld32(t + (uint32_t)(BN + c * 32), vc);
-                if (k < p.K) {
-                    float4* d4 = reinterpret_cast<float4*>(dst + c * 32);
+                const int ti = c / bpt;
+                const int tap = group * p.tpt + ti;
+                if (k < p.K && tap < RS) {
+                    float4* d4 = reinterpret_cast<float4*>(
+                        p.ws + (((size_t)z * p.K + k) * RS + tap) * p.Cs + cslice * p.csl +
+                        (c - ti * bpt) * 32);
 #pragma unroll
                     for (int q = 0; q < 8; ++q)
                         d4[q] = make_float4(__uint_as_float(v[4 * q]) + __uint_as_float(vc[4 * q]),
@@ -2060,29 +2131,41 @@ __global__ void __launch_bounds__(192, 1)
     }
 }
 
-// dW[k, c, r, s] = sum over splits (in order) of ws[split][k][r*S + s][c]
+// dW[k, c, r, s] = sum over splits (in order) of the partial at (k, tap, ch): for a plain
+// convolution tap = r*S + s and ch = c; for the space-to-depth form (f = 2) tap =
+// (r/2)*tw + s/2 and ch = (c*2 + r%2)*2 + s%2 over the th x tw filter.
 __global__ void wgrad_reduce_kernel(const float* __restrict__ ws, float* __restrict__ dw, int K,
-                                    int C, int RS, int Cs, int splits) {
-    const long long total = (long long)K * C * RS;
-    const size_t split_elems = (size_t)K * RS * Cs;
+                                    int C, int R, int S, int RSg, int tw, int Cs, int splits,
+                                    int f) {
+    const long long total = (long long)K * C * R * S;
+    const size_t split_elems = (size_t)K * RSg * Cs;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
          i += (long long)gridDim.x * blockDim.x) {
-        const int rs = (int)(i % RS);
-        const long long t = i / RS;
+        const int sx = (int)(i % S);
+        long long t = i / S;
+        const int r = (int)(t % R);
+        t /= R;
         const int c = (int)(t % C), k = (int)(t / C);
-        const size_t o = ((size_t)k * RS + rs) * Cs + c;
+        int tap, ch;
+        if (f == 1) {
+            tap = r * S + sx;
+            ch = c;
+        } else {
+            tap = (r / f) * tw + sx / f;
+            ch = (c * f + r % f) * f + sx % f;
+        }
+        const size_t o = ((size_t)k * RSg + tap) * Cs + ch;
         float sum = 0.f;
         for (int z = 0; z < splits; ++z) sum += ws[z * split_elems + o];
         dw[i] = sum;
     }
 }
 
-template <int BN>
 static int launch_wgrad(DeviceCtx* c, const CUtensorMap& a_hi, const CUtensorMap& a_lo,
                         const CUtensorMap& b_hi, const CUtensorMap& b_lo, const WgradParams& p,
                         dim3 grid) {
-    using Cf = WgCfg<BN>;
-    auto kern = wgrad_tf32_kernel<BN>;
+    using Cf = WgCfg<128>;
+    auto kern = wgrad_tf32_kernel<128>;
     static bool attr_set[64] = {false};
     if (!attr_set[c->device]) {
         OMB_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM));
@@ -2093,35 +2176,41 @@ static int launch_wgrad(DeviceCtx* c, const CUtensorMap& a_hi, const CUtensorMap
 }
 
 // The fp32 weight gradient of a (stride, pad) convolution, NCHW in and out, 3xTF32 on the
-// tensor cores. Scratch (the hi/lo copies of X and dY and the split partials) comes from the
-// stream-ordered pool.
+// tensor cores. A stride-2 convolution with Cin * 4 <= 32 (the image stem) runs in its
+// space-to-depth form: 32-channel copy of X, th x tw taps, stride 1 (a quarter of the taps and
+// four times the channel use of the plain form). Scratch (the hi/lo copies of X and dY and the
+// split partials) comes from the stream-ordered pool.
 int tf32_wgrad(DeviceCtx* c, const float* x, const float* dy, float* dw, int N, int Cin, int H,
                int W, int K, int R, int S, int stride, int pad) {
     const int P = (H + 2 * pad - R) / stride + 1, Q = (W + 2 * pad - S) / stride + 1;
     if (P <= 0 || Q <= 0) return OM_ERR_INVALID;
-    const int Cs = (Cin + 31) / 32 * 32, Ks = (K + 31) / 32 * 32;
+    S2dGeom g;
+    const bool s2d = s2d_geom(Cin, H, W, R, S, stride, pad, &g);
+    // geometry of the convolution the kernel runs
+    const int Hk = s2d ? g.Hs : H, Wk = s2d ? g.Ws : W;
+    const int Rk = s2d ? g.th : R, Sk = s2d ? g.tw : S;
+    const int stk = s2d ? 1 : stride, padk = s2d ? 0 : pad;
+    const int Cs = s2d ? 32 : (Cin + 31) / 32 * 32, Ks = (K + 31) / 32 * 32;
     const long long NPQ = (long long)N * P * Q;
-    if (NPQ >= (1LL << 31) - 64 || N > 65535 || (long long)H * ((W + 31) / 32) >= (1LL << 31) ||
-        (long long)P * ((Q + 31) / 32) >= (1LL << 31))
-        return OM_ERR_UNSUPPORTED;
-    if (-pad < -128 || pad - (R - 1) < -128 || pad - (S - 1) < -128 || pad - (R - 1) > 127 ||
-        pad - (S - 1) > 127)
+    if (NPQ >= (1LL << 31) - 64 || N > 65535 || (long long)Hk * ((Wk + 31) / 32) >= (1LL << 31) ||
+        (long long)P * ((Q + 31) / 32) >= (1LL << 31) || !tf32_pad_ok(Rk, Sk, padk))
         return OM_ERR_UNSUPPORTED;
     if (!load_driver_entry_points()) return OM_ERR_DRIVER;
-    // channel slice per tile: the widest of 128, 64, 32 that divides Cs (a multiple of 32)
-    const int bnc = Cs % 128 == 0 ? 128 : (Cs % 64 == 0 ? 64 : 32);
-    const int cb = Cs / bnc;
-    const int RS = R * S;
+    // a tile is 128 columns: tpt taps x csl channels, csl the widest of 128, 64, 32 dividing Cs
+    const int csl = Cs % 128 == 0 ? 128 : (Cs % 64 == 0 ? 64 : 32);
+    const int tpt = 128 / csl;
+    const int cb = Cs / csl;
+    const int RSk = Rk * Sk;
     const int num_kb = (int)((NPQ + 31) / 32);
     const int m_tiles = (K + 127) / 128;
-    const long long tiles = (long long)RS * cb * m_tiles;
+    const long long tiles = (long long)((RSk + tpt - 1) / tpt) * cb * m_tiles;
     long long want = (2LL * c->num_sms + tiles - 1) / tiles;
     long long cap = num_kb < 256 ? num_kb : 256;
     const int splits = (int)(want < 1 ? 1 : (want > cap ? cap : want));
-    if (tiles > 65535LL * 1024) return OM_ERR_UNSUPPORTED;
+    if (tiles * splits >= (1LL << 31)) return OM_ERR_UNSUPPORTED;
 
-    const size_t xe = (size_t)N * H * W * Cs, ye = (size_t)Ks * NPQ;
-    const size_t we = (size_t)splits * K * RS * Cs;
+    const size_t xe = (size_t)N * Hk * Wk * Cs, ye = (size_t)Ks * NPQ;
+    const size_t we = (size_t)splits * K * RSk * Cs;
     auto r256 = [](size_t b) { return (b + 255) / 256 * 256; };
     const size_t xb = r256(xe * 4), yb = r256(ye * 4), wb = r256(we * 4);
     uint8_t* scratch = nullptr;
@@ -2132,12 +2221,15 @@ int tf32_wgrad(DeviceCtx* c, const float* x, const float* dy, float* dw, int N, 
     float* ylo = reinterpret_cast<float*>(scratch + 2 * xb + yb);
     float* ws = reinterpret_cast<float*>(scratch + 2 * xb + 2 * yb);
     int st = OM_OK;
-    {
+    if (s2d) {
+        s2d_split_kernel<<<ew_grid(c, (long long)xe, 256), 256, 0, c->compute>>>(
+            x, xhi, xlo, N, Cin, H, W, g.Hs, g.Ws, 2, pad);
+    } else {
         dim3 gx((unsigned)(H * ((W + 31) / 32)), Cs / 32, (unsigned)N);
         split_nhwc_kernel<<<gx, dim3(32, 8), 0, c->compute>>>(x, xhi, xlo, N, Cin, H, W, H, W, Cs,
                                                              0, 0, 1, 0);
-        st = after_launch(c);
     }
+    st = after_launch(c);
     if (st == OM_OK) {
         dim3 gy((unsigned)(P * ((Q + 31) / 32)), Ks / 32, (unsigned)N);
         split_nhwc_kernel<<<gy, dim3(32, 8), 0, c->compute>>>(dy, yhi, ylo, N, K, P, Q, P, Q, Ks,
@@ -2160,12 +2252,13 @@ int tf32_wgrad(DeviceCtx* c, const float* x, const float* dy, float* dw, int N, 
                                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
             if (r != CUDA_SUCCESS) st = OM_ERR_DRIVER;
         }
-        // B: im2col of the NHWC input, 32 pixels x 32 channels per box
-        cuuint64_t bd[4] = {(cuuint64_t)Cs, (cuuint64_t)W, (cuuint64_t)H, (cuuint64_t)N};
-        cuuint64_t bs[3] = {(cuuint64_t)Cs * 4, (cuuint64_t)W * Cs * 4, (cuuint64_t)H * W * Cs * 4};
-        int lo_c[2] = {-pad, -pad};
-        int hi_c[2] = {pad - (S - 1), pad - (R - 1)};
-        cuuint32_t bestr[4] = {1, (cuuint32_t)stride, (cuuint32_t)stride, 1};
+        // B: im2col of the NHWC input copy, 32 pixels x 32 channels per box
+        cuuint64_t bd[4] = {(cuuint64_t)Cs, (cuuint64_t)Wk, (cuuint64_t)Hk, (cuuint64_t)N};
+        cuuint64_t bs[3] = {(cuuint64_t)Cs * 4, (cuuint64_t)Wk * Cs * 4,
+                            (cuuint64_t)Hk * Wk * Cs * 4};
+        int lo_c[2] = {-padk, -padk};
+        int hi_c[2] = {padk - (Sk - 1), padk - (Rk - 1)};
+        cuuint32_t bestr[4] = {1, (cuuint32_t)stk, (cuuint32_t)stk, 1};
         for (int k = 0; k < 2 && st == OM_OK; ++k) {
             CUtensorMap* m = k ? &b_lo : &b_hi;
             CUresult r = g_encode_im2col(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, k ? xlo : xhi, bd,
@@ -2181,20 +2274,17 @@ int tf32_wgrad(DeviceCtx* c, const float* x, const float* dy, float* dw, int N, 
     }
     if (st == OM_OK) {
         WgradParams p;
-        p.N = N; p.K = K; p.Cs = Cs; p.R = R; p.S = S; p.stride = stride; p.pad = pad;
-        p.P = P; p.Q = Q; p.num_kb = num_kb; p.cb = cb; p.splits = splits; p.ws = ws;
+        p.N = N; p.K = K; p.Cs = Cs; p.R = Rk; p.S = Sk; p.stride = stk; p.pad = padk;
+        p.P = P; p.Q = Q; p.num_kb = num_kb; p.tpt = tpt; p.csl = csl; p.cb = cb;
+        p.splits = splits; p.ws = ws;
         p.err = c->err_word;
-        dim3 grid((unsigned)(RS * cb), (unsigned)m_tiles, (unsigned)splits);
-        switch (bnc) {
-            case 32: st = launch_wgrad<32>(c, a_hi, a_lo, b_hi, b_lo, p, grid); break;
-            case 64: st = launch_wgrad<64>(c, a_hi, a_lo, b_hi, b_lo, p, grid); break;
-            default: st = launch_wgrad<128>(c, a_hi, a_lo, b_hi, b_lo, p, grid); break;
-        }
+        dim3 grid((unsigned)(((RSk + tpt - 1) / tpt) * cb), (unsigned)m_tiles, (unsigned)splits);
+        st = launch_wgrad(c, a_hi, a_lo, b_hi, b_lo, p, grid);
     }
     if (st == OM_OK) {
-        const long long total = (long long)K * Cin * RS;
-        wgrad_reduce_kernel<<<ew_grid(c, total, 256), 256, 0, c->compute>>>(ws, dw, K, Cin, RS, Cs,
-                                                                             splits);
+        const long long total = (long long)K * Cin * R * S;
+        wgrad_reduce_kernel<<<ew_grid(c, total, 256), 256, 0, c->compute>>>(
+            ws, dw, K, Cin, R, S, RSk, Sk, Cs, splits, s2d ? 2 : 1);
         st = after_launch(c);
     }
     cudaFreeAsync(scratch, c->compute);

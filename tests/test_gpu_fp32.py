@@ -58,6 +58,8 @@ CONV = [  # n, c, h, k, r, stride, pad, bias
     # every conv shape of the batch-4, 64x64 ResNet-18 training test (down to 2x2 maps)
     (4, 3, 64, 64, 7, 2, 3, False),
     (4, 64, 16, 64, 3, 1, 1, False),
+    (4, 64, 16, 128, 3, 2, 1, False),
+    (4, 64, 16, 128, 1, 2, 0, False),
     (4, 128, 8, 256, 3, 2, 1, False),
     (4, 128, 8, 256, 1, 2, 0, False),
     (4, 256, 4, 256, 3, 1, 1, False),
