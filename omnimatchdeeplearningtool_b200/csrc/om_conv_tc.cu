@@ -1342,6 +1342,9 @@ static void choose_tile(int Cout, int num_kb, long long m_tiles, int num_sms, bo
         long long tiles2 = (m_tiles + 1) / 2 * ((Cout + *bn - 1) / *bn);
         if (tiles2 >= 2LL * num_sms) *mt = 2;
     }
+    // a long reduction over very few tiles (the classifier at batch 256: 16 tiles of 128) is
+    // bound by each SM's operand bandwidth from L2: narrower tiles spread it over more SMs
+    while (*mt == 1 && *bn > 32 && m_tiles * ((Cout + *bn - 1) / *bn) < num_sms / 2) *bn /= 2;
 }
 
 // Encodes the output and residual maps (16-bit outputs) and launches the kernel.
@@ -1642,8 +1645,13 @@ extern "C" int omCudaStemConvBnAct(const float* pInput, void* pWorkspace, const 
     p.QT = qt;
     p.box_w = BM - 1 + g.tw;
     int bn, occ, mt, ew;
-    choose_tile(nCout, 1 << 20, p.num_m_tiles, c->num_sms, false, &bn, &occ, &mt, &ew);  // 1 CTA/SM
-    p.num_n_tiles = (nCout + bn - 1) / bn;
+    // one CTA per SM and one N tile holding every output channel (the packed weight stays
+    // resident from column 0)
+    bn = nCout <= 32 ? 32 : (nCout <= 64 ? 64 : 128);
+    occ = 1;
+    mt = 1;
+    ew = 8;
+    p.num_n_tiles = 1;
     p.bias = pBias;
     p.residual = nullptr;
     p.out = pOutput;
