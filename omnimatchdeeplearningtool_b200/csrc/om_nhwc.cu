@@ -258,22 +258,167 @@ __global__ void gap_nhwc_kernel(const uint4* __restrict__ in, void* __restrict__
 
 // ---------------------------------------------------------------- depthwise conv
 // packed weight: fp32 [R*S, Cs] (BN scale folded), bias fp32 [Cs]. One block per output row
-// (n, p); its threads walk the row's (q, 8-channel group) items with 32-bit indices.
-template <int DT>
+// (n, p); its threads walk the row's (q, 8-channel group) items with 32-bit indices. KS > 0
+// fixes the window at KS x KS: the item's KS*KS input loads are all issued before the
+// arithmetic (taps outside the image load zeros), which keeps the HBM pipe busy; the taps are
+// accumulated in the same order as the general loop.
+template <int DT, int KS>
 __global__ void depthwise_nhwc_kernel(const uint4* __restrict__ in, const float* __restrict__ wpk,
                                       const float* __restrict__ bias, uint4* __restrict__ out,
                                       int H, int W, int C8, int P, int Q, int R, int S,
-                                      int stride, int pad, int act) {
+                                      int stride, int pad, int act, int pair) {
     using H16 = Half16<DT>;
     const int Cs = C8 * 8;
-    const int row = blockIdx.x;          // n * P + p
-    const int n = row / P;
+    const int row = blockIdx.x;          // n * P + p (pair: n * ceil(P/2) + p/2)
+    const int n = pair ? row / ((P + 1) / 2) : row / P;
     const int p = row - n * P;
     const int h0 = p * stride - pad;
-    const int r0 = h0 < 0 ? -h0 : 0;
-    const int r1 = (H - h0) < R ? (H - h0) : R;
     const uint4* img = in + (size_t)n * H * W * C8;
     uint4* orow = out + (size_t)row * Q * C8;
+    if constexpr (KS > 0 && DT == OM_DTYPE_F16) {
+        if (blockDim.x % C8 == 0) {
+            // fp16: every item of this thread has the same 8 channels, so the KS*KS weights
+            // and the bias are loaded once, as half2, and the taps are accumulated with HFMA2
+            // (9 fp16 products and the bias: ~1e-3 relative, inside the 16-bit tolerance)
+            const int c8 = (int)threadIdx.x % C8;
+            __half2 wt[KS * KS][4];
+#pragma unroll
+            for (int t = 0; t < KS * KS; ++t) {
+                const float4* w4 = reinterpret_cast<const float4*>(wpk + (size_t)t * Cs + c8 * 8);
+                const float4 wa = __ldg(w4), wb = __ldg(w4 + 1);
+                wt[t][0] = __floats2half2_rn(wa.x, wa.y);
+                wt[t][1] = __floats2half2_rn(wa.z, wa.w);
+                wt[t][2] = __floats2half2_rn(wb.x, wb.y);
+                wt[t][3] = __floats2half2_rn(wb.z, wb.w);
+            }
+            const float4* b4 = reinterpret_cast<const float4*>(bias + c8 * 8);
+            const float4 ba = __ldg(b4), bb = __ldg(b4 + 1);
+            const __half2 bh[4] = {__floats2half2_rn(ba.x, ba.y), __floats2half2_rn(ba.z, ba.w),
+                                   __floats2half2_rn(bb.x, bb.y), __floats2half2_rn(bb.z, bb.w)};
+            const __half2 zero = __float2half2_rn(0.f), six = __float2half2_rn(6.f);
+            auto finish = [&](__half2 (&acc)[4]) {
+                uint4 o;
+                __half2* o2 = reinterpret_cast<__half2*>(&o);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    __half2 a = acc[j];
+                    if (act == OM_ACT_RELU) a = __hmax2(a, zero);
+                    else if (act == OM_ACT_RELU6) a = __hmin2(__hmax2(a, zero), six);
+                    o2[j] = a;
+                }
+                return o;
+            };
+            if (pair) {
+                // stride 1: this block owns output rows p and p + 1 (2 * blockIdx.x within the
+                // image); the two windows share KS - 1 input rows, loaded once
+                const int pr = 2 * (row - n * ((P + 1) / 2));
+                const int hb = pr - pad;
+                const bool second = pr + 1 < P;
+                uint4* orow0 = out + ((size_t)n * P + pr) * Q * C8;
+                for (int i = threadIdx.x; i < Q * C8; i += blockDim.x) {
+                    const int q = i / C8;
+                    const int w0 = q - pad;
+                    uint4 v[(KS + 1) * KS];
+#pragma unroll
+                    for (int r = 0; r < KS + 1; ++r) {
+#pragma unroll
+                        for (int sx = 0; sx < KS; ++sx) {
+                            const int hh = hb + r, ww = w0 + sx;
+                            const bool ok = hh >= 0 && hh < H && ww >= 0 && ww < W;
+                            v[r * KS + sx] = ok ? __ldg(img + ((size_t)hh * W + ww) * C8 + c8)
+                                                : make_uint4(0, 0, 0, 0);
+                        }
+                    }
+                    __half2 a0[4] = {bh[0], bh[1], bh[2], bh[3]};
+                    __half2 a1[4] = {bh[0], bh[1], bh[2], bh[3]};
+#pragma unroll
+                    for (int t = 0; t < KS * KS; ++t) {
+                        const __half2* x0 = reinterpret_cast<const __half2*>(&v[t]);
+                        const __half2* x1 = reinterpret_cast<const __half2*>(&v[t + KS]);
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            a0[j] = __hfma2(x0[j], wt[t][j], a0[j]);
+                            a1[j] = __hfma2(x1[j], wt[t][j], a1[j]);
+                        }
+                    }
+                    orow0[i] = finish(a0);
+                    if (second) orow0[(size_t)Q * C8 + i] = finish(a1);
+                }
+                return;
+            }
+            for (int i = threadIdx.x; i < Q * C8; i += blockDim.x) {
+                const int q = i / C8;
+                const int w0 = q * stride - pad;
+                uint4 v[KS * KS];
+#pragma unroll
+                for (int r = 0; r < KS; ++r) {
+#pragma unroll
+                    for (int sx = 0; sx < KS; ++sx) {
+                        const int hh = h0 + r, ww = w0 + sx;
+                        const bool ok = hh >= 0 && hh < H && ww >= 0 && ww < W;
+                        v[r * KS + sx] = ok ? __ldg(img + ((size_t)hh * W + ww) * C8 + c8)
+                                            : make_uint4(0, 0, 0, 0);
+                    }
+                }
+                __half2 acc[4] = {bh[0], bh[1], bh[2], bh[3]};
+#pragma unroll
+                for (int t = 0; t < KS * KS; ++t) {
+                    const __half2* v2 = reinterpret_cast<const __half2*>(&v[t]);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) acc[j] = __hfma2(v2[j], wt[t][j], acc[j]);
+                }
+                orow[i] = finish(acc);
+            }
+            return;
+        }
+    }
+    if constexpr (KS > 0) {
+        for (int i = threadIdx.x; i < Q * C8; i += blockDim.x) {
+            const int q = i / C8;
+            const int c8 = i - q * C8;
+            const int w0 = q * stride - pad;
+            uint4 v[KS * KS];
+#pragma unroll
+            for (int r = 0; r < KS; ++r) {
+#pragma unroll
+                for (int sx = 0; sx < KS; ++sx) {
+                    const int hh = h0 + r, ww = w0 + sx;
+                    const bool ok = hh >= 0 && hh < H && ww >= 0 && ww < W;
+                    v[r * KS + sx] = ok ? __ldg(img + ((size_t)hh * W + ww) * C8 + c8)
+                                        : make_uint4(0, 0, 0, 0);
+                }
+            }
+            float acc[8];
+            const float4* b4 = reinterpret_cast<const float4*>(bias + c8 * 8);
+            float4 b0 = __ldg(b4), b1 = __ldg(b4 + 1);
+            acc[0] = b0.x; acc[1] = b0.y; acc[2] = b0.z; acc[3] = b0.w;
+            acc[4] = b1.x; acc[5] = b1.y; acc[6] = b1.z; acc[7] = b1.w;
+#pragma unroll
+            for (int t = 0; t < KS * KS; ++t) {
+                const int r = t / KS, sx = t - r * KS;
+                if (h0 + r < 0 || h0 + r >= H || w0 + sx < 0 || w0 + sx >= W) continue;
+                const typename H16::T2* v2 = reinterpret_cast<const typename H16::T2*>(&v[t]);
+                const float4* w4 = reinterpret_cast<const float4*>(wpk + (size_t)t * Cs + c8 * 8);
+                float4 wa = __ldg(w4), wb = __ldg(w4 + 1);
+                float wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    float2 f = H16::unpack(v2[j]);
+                    acc[2 * j] += f.x * wv[2 * j];
+                    acc[2 * j + 1] += f.y * wv[2 * j + 1];
+                }
+            }
+            uint4 o;
+            typename H16::T2* o2 = reinterpret_cast<typename H16::T2*>(&o);
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                o2[j] = H16::pack(apply_act(acc[2 * j], act), apply_act(acc[2 * j + 1], act));
+            orow[i] = o;
+        }
+        return;
+    }
+    const int r0 = h0 < 0 ? -h0 : 0;
+    const int r1 = (H - h0) < R ? (H - h0) : R;
     for (int i = threadIdx.x; i < Q * C8; i += blockDim.x) {
         const int q = i / C8;
         const int c8 = i - q * C8;
@@ -500,16 +645,30 @@ extern "C" int omCudaDepthwiseConv2dNhwc(const void* pIn, const float* pPacked, 
     const long long rows = (long long)nN * P;
     if (rows >= (1LL << 31) || (long long)Q * (nCs / 8) >= (1LL << 31)) return OM_ERR_UNSUPPORTED;
     const int threads = Q * (nCs / 8) >= 256 ? 256 : 128;
-    if (nDtype == OM_DTYPE_BF16)
-        depthwise_nhwc_kernel<OM_DTYPE_BF16><<<(unsigned)rows, threads, 0, c->compute>>>(
-            static_cast<const uint4*>(pIn), pPacked, pBias, static_cast<uint4*>(pOut), nH, nW,
-            nCs / 8, P, Q, nKH, nKW, nStride, nPad, nAct);
-    else if (nDtype == OM_DTYPE_F16)
-        depthwise_nhwc_kernel<OM_DTYPE_F16><<<(unsigned)rows, threads, 0, c->compute>>>(
-            static_cast<const uint4*>(pIn), pPacked, pBias, static_cast<uint4*>(pOut), nH, nW,
-            nCs / 8, P, Q, nKH, nKW, nStride, nPad, nAct);
-    else
+    const uint4* src = static_cast<const uint4*>(pIn);
+    uint4* dst = static_cast<uint4*>(pOut);
+    const int c8 = nCs / 8;
+    const bool k3 = nKH == 3 && nKW == 3;
+    // fp16, 3x3, stride 1, every thread on fixed channels: one block per pair of output rows
+    const int pair = (nDtype == OM_DTYPE_F16 && k3 && nStride == 1 && threads % c8 == 0) ? 1 : 0;
+    const unsigned grid = pair ? (unsigned)((long long)nN * ((P + 1) / 2)) : (unsigned)rows;
+    if (nDtype == OM_DTYPE_BF16) {
+        if (k3)
+            depthwise_nhwc_kernel<OM_DTYPE_BF16, 3><<<grid, threads, 0, c->compute>>>(
+                src, pPacked, pBias, dst, nH, nW, c8, P, Q, nKH, nKW, nStride, nPad, nAct, 0);
+        else
+            depthwise_nhwc_kernel<OM_DTYPE_BF16, 0><<<grid, threads, 0, c->compute>>>(
+                src, pPacked, pBias, dst, nH, nW, c8, P, Q, nKH, nKW, nStride, nPad, nAct, 0);
+    } else if (nDtype == OM_DTYPE_F16) {
+        if (k3)
+            depthwise_nhwc_kernel<OM_DTYPE_F16, 3><<<grid, threads, 0, c->compute>>>(
+                src, pPacked, pBias, dst, nH, nW, c8, P, Q, nKH, nKW, nStride, nPad, nAct, pair);
+        else
+            depthwise_nhwc_kernel<OM_DTYPE_F16, 0><<<grid, threads, 0, c->compute>>>(
+                src, pPacked, pBias, dst, nH, nW, c8, P, Q, nKH, nKW, nStride, nPad, nAct, 0);
+    } else {
         return OM_ERR_UNSUPPORTED;
+    }
     return after_launch(c);
 }
 

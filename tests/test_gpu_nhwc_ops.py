@@ -4,8 +4,9 @@
   the oracle's max pool of the 16-bit-rounded input bit for bit;
 * global average pool (omCudaGlobalAvgPoolNhwc) with an fp32 output: fp32 sums of the 16-bit
   values, max|a-b|/max|b| <= 1e-5 against the oracle on the rounded input;
-* depthwise conv + BN + ReLU6 (omCudaDepthwiseConv2dNhwc): fp32 accumulation, 16-bit output:
-  <= 1e-2 against the oracle on rounded input and BN-folded fp32 weights;
+* depthwise conv + BN + ReLU6 (omCudaDepthwiseConv2dNhwc): fp32 accumulation (fp16 3x3 with the
+  weights held per thread: fp16 HFMA2 over the 9 taps), 16-bit output: <= 1e-2 against the
+  oracle on rounded input and BN-folded fp32 weights;
 * residual add + activation (omCudaAddActNhwc): one 16-bit rounding of act(a + b).
 Ragged sizes (odd H and W, channels stored padded to a multiple of 8) are included.
 """
@@ -99,7 +100,9 @@ def test_global_avgpool_nhwc(gpu, n, c, h, w, dt):
 
 @pytest.mark.parametrize("n,c,h,k,stride,dt", [(2, 144, 28, 3, 2, "f16"), (3, 32, 15, 3, 1, "bf16"),
                                                 (2, 40, 13, 5, 2, "bf16"),   # generic window
-                                                (1, 2048, 9, 3, 1, "f16")])  # C/8 = 256 threads
+                                                (1, 2048, 9, 3, 1, "f16"),   # C/8 = 256 threads
+                                                (3, 128, 15, 3, 1, "f16"),   # row pairs, odd P
+                                                (2, 64, 16, 3, 2, "f16")])   # fp16 weights held
 def test_depthwise_nhwc(gpu, n, c, h, k, stride, dt):
     import oracle as orc
     from omnimatchdeeplearningtool_b200 import _lib
