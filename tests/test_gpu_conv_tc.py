@@ -40,6 +40,11 @@ CASES = [
     # long reductions over a partial last wave of tiles
     (4, 512, 7, 512, 3, 1, 1, "bf16", False, "relu", False),      # 72 k-blocks, 8 tiles
     (8, 128, 56, 128, 3, 1, 1, "f16", False, "relu6", False),     # 196 tiles on 148 SMs
+    # 3x3 stride 1 on 28- to 57-wide maps: ragged last tiles, several N tiles, Cout < BN
+    (4, 128, 28, 128, 3, 1, 1, "bf16", False, "relu", False),     # two 64-channel slices
+    (3, 64, 28, 192, 3, 1, 1, "f16", True, "relu", False),        # two N tiles + residual
+    (2, 64, 57, 64, 3, 1, 1, "bf16", True, "none", False),        # odd width, residual
+    (2, 192, 30, 96, 3, 1, 1, "bf16", False, "relu6", False),     # three slices, Cout < BN
 ]
 
 
