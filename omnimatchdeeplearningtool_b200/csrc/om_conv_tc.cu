@@ -419,7 +419,9 @@ __device__ __forceinline__ void store_chunk_f32(const Params& p, int m, int n0,
 // the epilogue-bound configurations (the stem, two CTAs per SM, or 16 epilogue warps), each
 // epilogue warp's copy of the tile's bias.
 template <int BN, int MODE, int OCC, int EW>
-__host__ __device__ constexpr bool bias_smem() { return MODE == MODE_STEM || OCC == 2 || EW > 4; }
+__host__ __device__ constexpr bool bias_smem() {
+    return MODE == MODE_STEM || OCC == 2 || EW == 16;
+}
 template <int BN, int MODE, int OCC, int EW>
 __host__ __device__ constexpr int extra_bytes() {
     return (MODE == MODE_STEM ? STEM_EXTRA_BYTES : 0) +
@@ -433,8 +435,8 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
                    const __grid_constant__ CUtensorMap tmRes, const Params p) {
     static_assert(MT == 1 || ((MODE == MODE_SW128 || MODE == MODE_SW32) && BN <= 128 && OCC == 1),
                   "MT = 2 tiles");
-    static_assert(EW == 4 || (EW == 16 && OCC == 1 && MODE != MODE_STEM) ||
-                      (EW == 8 && MODE == MODE_STEM), "epilogue warps");
+    static_assert(EW == 4 || (EW == 16 && OCC == 1 && MODE != MODE_STEM) || (EW == 8 && OCC == 1),
+                  "epilogue warps");
     static_assert(MODE != MODE_TF32 || (MT == 1 && EW == 4 && OCC == 1), "TF32 tiles");
     using C = Cfg<BN, OCC, extra_bytes<BN, MODE, OCC, EW>(), MT, EW, MODE == MODE_TF32 ? 2 : 1>;
     constexpr int EPI_BUFS = epi_bufs<EW>();
@@ -1271,6 +1273,22 @@ static int dispatch_bn(DeviceCtx* c, int bn, int occ, int mt, int ew, const CUte
             }
             return OM_ERR_UNSUPPORTED;
         }
+        if (ew == 8) {
+            if (mt == 2) {
+                switch (bn) {
+                    case 64: return launch<64, MODE, DT, 1, 2, 8>(c, ta, tb, to, tr, p);
+                    case 128: return launch<128, MODE, DT, 1, 2, 8>(c, ta, tb, to, tr, p);
+                }
+                return OM_ERR_UNSUPPORTED;
+            }
+            switch (bn) {
+                case 32: return launch<32, MODE, DT, 1, 1, 8>(c, ta, tb, to, tr, p);
+                case 64: return launch<64, MODE, DT, 1, 1, 8>(c, ta, tb, to, tr, p);
+                case 128: return launch<128, MODE, DT, 1, 1, 8>(c, ta, tb, to, tr, p);
+                case 256: return launch<256, MODE, DT, 1, 1, 8>(c, ta, tb, to, tr, p);
+            }
+            return OM_ERR_UNSUPPORTED;
+        }
         if (mt == 2) {
             switch (bn) {
                 case 64: return launch<64, MODE, DT, 1, 2>(c, ta, tb, to, tr, p);
@@ -1317,7 +1335,7 @@ static int dispatch_bn(DeviceCtx* c, int bn, int occ, int mt, int ew, const CUte
 //    leaves SMs idle; when they stay at 64 or 128 wide, mt = 2 is used if that still fills two
 //    waves.
 static void choose_tile(int Cout, int num_kb, long long m_tiles, int num_sms, bool allow_mt2,
-                        int* bn, int* occ, int* mt, int* ew) {
+                        bool has_res, int* bn, int* occ, int* mt, int* ew) {
     *occ = 1;
     *mt = 1;
     *ew = 4;
@@ -1345,6 +1363,11 @@ static void choose_tile(int Cout, int num_kb, long long m_tiles, int num_sms, bo
     // a long reduction over very few tiles (the classifier at batch 256: 16 tiles of 128) is
     // bound by each SM's operand bandwidth from L2: narrower tiles spread it over more SMs
     while (*mt == 1 && *bn > 32 && m_tiles * ((Cout + *bn - 1) / *bn) < num_sms / 2) *bn /= 2;
+    // two epilogue warps per TMEM lane quarter (the same staging memory as four warps, so the
+    // same pipeline depth): the epilogue of a 256-row or 256-wide tile keeps up with its MMAs.
+    // Their two staging sub-tiles per warp leave no room to prefetch residuals two chunks ahead,
+    // so layers with a residual keep one warp per quarter.
+    if (allow_mt2 && !has_res) *ew = 8;
 }
 
 // Encodes the output and residual maps (16-bit outputs) and launches the kernel.
@@ -1435,8 +1458,8 @@ extern "C" int omCudaConv2dBnAct(const void* pInput, const void* pPacked, const 
     p.num_kb = (int)(kpad / BK);
     p.num_m_tiles = (int)((Mll + BM - 1) / BM);
     int bn, occ, mt, ew;
-    choose_tile(nCout, p.num_kb, p.num_m_tiles, c->num_sms, mode != MODE_INTERLEAVE, &bn, &occ,
-                &mt, &ew);
+    choose_tile(nCout, p.num_kb, p.num_m_tiles, c->num_sms, mode != MODE_INTERLEAVE,
+                pResidual != nullptr, &bn, &occ, &mt, &ew);
     p.num_m_tiles = (int)((Mll + BM * mt - 1) / (BM * mt));
     p.num_n_tiles = (nCout + bn - 1) / bn;
     p.QT = 1;
