@@ -1757,6 +1757,83 @@ __global__ void split_nhwc_kernel(const float* __restrict__ x, float* __restrict
     }
 }
 
+// The same split with output pixels flattened over (n, hp, wp): a block takes 128 consecutive
+// output pixels and 32 channels, whatever the spatial size, so 7- and 14-wide maps waste no
+// lanes; each output pixel looks up its source pixel once (none: zero). Each thread keeps 16
+// loads in flight; each lane stores 4 channels of one pixel as 16 bytes. Both passes through
+// shared memory are free of bank conflicts (row pitch 129). N * Hp * Wp < 2^31.
+__global__ void __launch_bounds__(256) split_flat_kernel(const float* __restrict__ x,
+                                                         float* __restrict__ hi,
+                                                         float* __restrict__ lo, int N, int Cin,
+                                                         int Hin, int Win, int Hp, int Wp, int Cs,
+                                                         int offh, int offw, int up, int blocked) {
+    __shared__ float tile[32][129];
+    const int HWp = Hp * Wp, HWin = Hin * Win;
+    const int NP = N * HWp;
+    const int P0 = blockIdx.x * 128;
+    const int c0 = blockIdx.y * 32;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    long long off[4];   // element offset of the source of pixel P0 + lane + 32k in channel 0, or -1
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int P = P0 + lane + 32 * k;
+        off[k] = -1;
+        if (P < NP) {
+            const int n = P / HWp;
+            const int r = P - n * HWp;
+            const int hp = r / Wp;
+            const int i = hp - offh, j = r - hp * Wp - offw;
+            if (i >= 0 && j >= 0 && i % up == 0 && j % up == 0 && i / up < Hin && j / up < Win)
+                off[k] = (long long)n * Cin * HWin + (i / up) * Win + j / up;
+        }
+    }
+#pragma unroll
+    for (int cc = 0; cc < 4; ++cc) {
+        const int ch = warp * 4 + cc;
+        const int c = c0 + ch;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            float v = 0.f;
+            if (c < Cin && off[k] >= 0) v = __ldg(x + (size_t)off[k] + (size_t)c * HWin);
+            tile[ch][lane + 32 * k] = v;
+        }
+    }
+    __syncthreads();
+    const int cq = (lane & 7) * 4;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int pl = k * 32 + warp * 4 + (lane >> 3);
+        const int P = P0 + pl;
+        if (P >= NP) continue;
+        const float v0 = tile[cq][pl], v1 = tile[cq + 1][pl], v2 = tile[cq + 2][pl],
+                    v3 = tile[cq + 3][pl];
+        const float4 h = make_float4(tf32_rna(v0), tf32_rna(v1), tf32_rna(v2), tf32_rna(v3));
+        const float4 l = make_float4(tf32_rna(v0 - h.x), tf32_rna(v1 - h.y), tf32_rna(v2 - h.z),
+                                     tf32_rna(v3 - h.w));
+        const size_t o = blocked ? ((size_t)(c0 / 32) * NP + P) * 32 + cq
+                                 : (size_t)P * Cs + c0 + cq;
+        *reinterpret_cast<float4*>(hi + o) = h;
+        *reinterpret_cast<float4*>(lo + o) = l;
+    }
+}
+
+// Splits NCHW fp32 x into NHWC hi/lo copies: the flat kernel, or the tiled one for more than
+// 2^31 output pixels.
+static void launch_split(DeviceCtx* c, const float* x, float* hi, float* lo, int N, int Cin,
+                         int Hin, int Win, int Hp, int Wp, int Cs, int offh, int offw, int up,
+                         int blocked) {
+    const long long np = (long long)N * Hp * Wp;
+    if (np + 128 < (1LL << 31)) {
+        dim3 grid((unsigned)((np + 127) / 128), (unsigned)(Cs / 32));
+        split_flat_kernel<<<grid, 256, 0, c->compute>>>(x, hi, lo, N, Cin, Hin, Win, Hp, Wp, Cs,
+                                                        offh, offw, up, blocked);
+        return;
+    }
+    dim3 grid((unsigned)(Hp * ((Wp + 31) / 32)), (unsigned)(Cs / 32), (unsigned)N);
+    split_nhwc_kernel<<<grid, dim3(32, 8), 0, c->compute>>>(x, hi, lo, N, Cin, Hin, Win, Hp, Wp,
+                                                           Cs, offh, offw, up, blocked);
+}
+
 // Packed K-major hi/lo weights [Kout, R*S*Cs], kk = (r*S + s)*Cs + ci, from W [Kw, Cw, R, S]:
 // forward (flip = 0): row o = output channel, ci = input channel, W[o, ci, r, s];
 // backward-input (flip = 1): row o = input channel c, ci = output channel k, the filter
@@ -1905,12 +1982,8 @@ int tf32_conv(DeviceCtx* c, const float* src, int N, int Cin, int Hin, int Win, 
     float* whi = reinterpret_cast<float*>(scratch + 2 * xb);
     float* wlo = reinterpret_cast<float*>(scratch + 2 * xb + wb);
     int st = OM_OK;
-    {
-        dim3 grid((unsigned)(Hp * ((Wp + 31) / 32)), Cs / 32, (unsigned)N);
-        split_nhwc_kernel<<<grid, dim3(32, 8), 0, c->compute>>>(src, xhi, xlo, N, Cin, Hin, Win,
-                                                               Hp, Wp, Cs, offh, offw, up, 0);
-        st = after_launch(c);
-    }
+    launch_split(c, src, xhi, xlo, N, Cin, Hin, Win, Hp, Wp, Cs, offh, offw, up, 0);
+    st = after_launch(c);
     if (st == OM_OK) {
         pack_tf32_weight_kernel<<<ew_grid(c, (long long)we, 256), 256, 0, c->compute>>>(
             w, whi, wlo, Kout, Cin, R, S, Cs, flip ? 1 : 0, Cw);
@@ -2256,15 +2329,11 @@ int tf32_wgrad(DeviceCtx* c, const float* x, const float* dy, float* dw, int N, 
         s2d_split_kernel<<<ew_grid(c, (long long)xe, 256), 256, 0, c->compute>>>(
             x, xhi, xlo, N, Cin, H, W, g.Hs, g.Ws, 2, pad);
     } else {
-        dim3 gx((unsigned)(H * ((W + 31) / 32)), Cs / 32, (unsigned)N);
-        split_nhwc_kernel<<<gx, dim3(32, 8), 0, c->compute>>>(x, xhi, xlo, N, Cin, H, W, H, W, Cs,
-                                                             0, 0, 1, 0);
+        launch_split(c, x, xhi, xlo, N, Cin, H, W, H, W, Cs, 0, 0, 1, 0);
     }
     st = after_launch(c);
     if (st == OM_OK) {
-        dim3 gy((unsigned)(P * ((Q + 31) / 32)), Ks / 32, (unsigned)N);
-        split_nhwc_kernel<<<gy, dim3(32, 8), 0, c->compute>>>(dy, yhi, ylo, N, K, P, Q, P, Q, Ks,
-                                                             0, 0, 1, 1);
+        launch_split(c, dy, yhi, ylo, N, K, P, Q, P, Q, Ks, 0, 0, 1, 1);
         st = after_launch(c);
     }
     CUtensorMap a_hi, a_lo, b_hi, b_lo;

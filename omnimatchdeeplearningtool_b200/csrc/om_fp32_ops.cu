@@ -38,33 +38,54 @@ __device__ __forceinline__ float block_sum(float v) {
 }
 
 // ---------------------------------------------------------------- BatchNorm
-// element j of channel c's reduction domain (n-major, hw-minor)
-__device__ __forceinline__ long long bn_index(long long j, int c, int C, int HW) {
-    long long n = j / HW;
-    return (n * C + c) * HW + (j - n * HW);
+// Channel c's reduction domain is the N*HW elements j = n*HW + hw (n-major), element j at
+// (n*C + c)*HW + hw. A reduction block covers [z*chunk, (z+1)*chunk); thread t sums j = beg+t,
+// beg+t+256, ... in that order, so the result depends only on (C, HW, N, splits), never on
+// timing. n = j / HW comes from a 32-bit multiply-shift division by the invariant HW (the
+// round-up method of Granlund and Montgomery), valid for j < 2^31; the loop is unrolled so that
+// loads overlap while the additions keep their order.
+struct FastDiv {
+    uint32_t d, mul, shift;
+};
+static FastDiv make_fastdiv(uint32_t d) {
+    uint32_t shift = 0;
+    while (shift < 32 && (1ull << shift) < d) ++shift;
+    const uint64_t one = 1;
+    const uint64_t magic = ((one << 32) * ((one << shift) - d)) / d + 1;
+    return FastDiv{d, (uint32_t)magic, shift};
+}
+__device__ __forceinline__ uint32_t fdiv(uint32_t n, const FastDiv& f) {
+    return (__umulhi(n, f.mul) + n) >> f.shift;
+}
+__device__ __forceinline__ size_t bn_index(uint32_t j, int c, int C, const FastDiv& hw) {
+    const uint32_t n = fdiv(j, hw);
+    return ((size_t)n * C + c) * hw.d + (j - n * hw.d);
 }
 
-__global__ void bn_partial_sum_kernel(const float* __restrict__ x, float* __restrict__ part,
-                                      int C, int HW, long long cnt, long long chunk) {
+__global__ void bn_partial_sum_kernel(const float* __restrict__ x, float* __restrict__ part, int C,
+                                      FastDiv hw, long long cnt, long long chunk) {
     const int c = blockIdx.x, z = blockIdx.y;
-    long long beg = z * chunk, end = min(cnt, beg + chunk);
+    const long long beg = z * chunk, end = min(cnt, beg + chunk);
     float s = 0.f;
-    for (long long j = beg + threadIdx.x; j < end; j += blockDim.x) s += x[bn_index(j, c, C, HW)];
+#pragma unroll 8
+    for (long long j = beg + threadIdx.x; j < end; j += blockDim.x)
+        s += __ldg(x + bn_index((uint32_t)j, c, C, hw));
     s = block_sum(s);
     if (threadIdx.x == 0) part[(long long)c * gridDim.y + z] = s;
 }
 
 __global__ void bn_partial_m2_kernel(const float* __restrict__ x, const float* __restrict__ psum,
-                                     float* __restrict__ part, int C, int HW, long long cnt,
+                                     float* __restrict__ part, int C, FastDiv hw, long long cnt,
                                      long long chunk) {
     const int c = blockIdx.x, z = blockIdx.y, S = gridDim.y;
     float tot = 0.f;
     for (int i = 0; i < S; ++i) tot += psum[(long long)c * S + i];
     const float mean = tot / (float)cnt;
-    long long beg = z * chunk, end = min(cnt, beg + chunk);
+    const long long beg = z * chunk, end = min(cnt, beg + chunk);
     float s = 0.f;
+#pragma unroll 8
     for (long long j = beg + threadIdx.x; j < end; j += blockDim.x) {
-        float d = x[bn_index(j, c, C, HW)] - mean;
+        const float d = __ldg(x + bn_index((uint32_t)j, c, C, hw)) - mean;
         s += d * d;
     }
     s = block_sum(s);
@@ -97,29 +118,45 @@ __global__ void bn_finalize_kernel(const float* __restrict__ psum, const float* 
     saved_invstd[c] = 1.f / sqrtf(var + eps);
 }
 
+// Elementwise BN kernels over the NCHW tensor. V = 4: vectors of 4 floats that share a channel
+// (HW % 4 == 0), one 32-bit division per vector (total < 2^32); V = 1: any shape.
+template <int V>
 __global__ void bn_apply_kernel(const float* __restrict__ x, float* __restrict__ y,
                                 const float* __restrict__ gamma, const float* __restrict__ beta,
                                 const float* __restrict__ mean, const float* __restrict__ invstd,
                                 long long total, int C, int HW) {
-    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+    const long long nv = total / V;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < nv;
          i += (long long)gridDim.x * blockDim.x) {
-        int c = (int)((i / HW) % C);
-        y[i] = gamma[c] * (x[i] - mean[c]) * invstd[c] + beta[c];
+        int c;
+        if constexpr (V == 4) c = (int)(((unsigned)i * 4u / (unsigned)HW) % (unsigned)C);
+        else c = (int)((i / HW) % C);
+        if constexpr (V == 4) {
+            const float4 v = __ldg(reinterpret_cast<const float4*>(x) + i);
+            reinterpret_cast<float4*>(y)[i] = make_float4(
+                gamma[c] * (v.x - mean[c]) * invstd[c] + beta[c],
+                gamma[c] * (v.y - mean[c]) * invstd[c] + beta[c],
+                gamma[c] * (v.z - mean[c]) * invstd[c] + beta[c],
+                gamma[c] * (v.w - mean[c]) * invstd[c] + beta[c]);
+        } else {
+            y[i] = gamma[c] * (x[i] - mean[c]) * invstd[c] + beta[c];
+        }
     }
 }
 
 __global__ void bn_bwd_partial_kernel(const float* __restrict__ dy, const float* __restrict__ x,
                                       const float* __restrict__ mean, const float* __restrict__ invstd,
-                                      float* __restrict__ pg, float* __restrict__ pb, int C, int HW,
-                                      long long cnt, long long chunk) {
+                                      float* __restrict__ pg, float* __restrict__ pb, int C,
+                                      FastDiv hw, long long cnt, long long chunk) {
     const int c = blockIdx.x, z = blockIdx.y;
     const float mu = mean[c], is = invstd[c];
-    long long beg = z * chunk, end = min(cnt, beg + chunk);
+    const long long beg = z * chunk, end = min(cnt, beg + chunk);
     float sg = 0.f, sb = 0.f;
+#pragma unroll 8
     for (long long j = beg + threadIdx.x; j < end; j += blockDim.x) {
-        long long idx = bn_index(j, c, C, HW);
-        float g = dy[idx];
-        sg += g * (x[idx] - mu) * is;
+        const size_t idx = bn_index((uint32_t)j, c, C, hw);
+        const float g = __ldg(dy + idx);
+        sg += g * (__ldg(x + idx) - mu) * is;
         sb += g;
     }
     sg = block_sum(sg);
@@ -142,17 +179,32 @@ __global__ void bn_bwd_finalize_kernel(const float* __restrict__ pg, const float
 }
 
 // dx = gamma*invstd/M * (M*dy - dbeta - xhat*dgamma)   (cpu_backend.ixx:847-892)
+template <int V>
 __global__ void bn_bwd_apply_kernel(const float* __restrict__ dy, const float* __restrict__ x,
                                     const float* __restrict__ mean, const float* __restrict__ invstd,
                                     const float* __restrict__ gamma, const float* __restrict__ dgamma,
                                     const float* __restrict__ dbeta, float* __restrict__ dx,
                                     long long total, int C, int HW, float M) {
-    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+    const long long nv = total / V;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < nv;
          i += (long long)gridDim.x * blockDim.x) {
-        int c = (int)((i / HW) % C);
-        float is = invstd[c];
-        float xh = (x[i] - mean[c]) * is;
-        dx[i] = gamma[c] * is / M * (M * dy[i] - dbeta[c] - xh * dgamma[c]);
+        int c;
+        if constexpr (V == 4) c = (int)(((unsigned)i * 4u / (unsigned)HW) % (unsigned)C);
+        else c = (int)((i / HW) % C);
+        const float is = invstd[c], mu = mean[c], k = gamma[c] * is / M, db = dbeta[c],
+                    dg = dgamma[c];
+        if constexpr (V == 4) {
+            const float4 g = __ldg(reinterpret_cast<const float4*>(dy) + i);
+            const float4 v = __ldg(reinterpret_cast<const float4*>(x) + i);
+            reinterpret_cast<float4*>(dx)[i] =
+                make_float4(k * (M * g.x - db - (v.x - mu) * is * dg),
+                            k * (M * g.y - db - (v.y - mu) * is * dg),
+                            k * (M * g.z - db - (v.z - mu) * is * dg),
+                            k * (M * g.w - db - (v.w - mu) * is * dg));
+        } else {
+            const float xh = (x[i] - mu) * is;
+            dx[i] = k * (M * dy[i] - db - xh * dg);
+        }
     }
 }
 
@@ -344,6 +396,25 @@ __global__ void map_kernel(long long n, F f) {
         f(i);
 }
 
+// y[i] = f(a[i], b[i]) (b absent: f(a[i], a[i])) in vectors of 4 floats, then the n % 4 tail.
+// The pointers are 16-byte aligned; y may be a or b (in place), so no restrict or
+// read-only-cache loads.
+template <class F>
+__global__ void zip_kernel(const float* a, const float* b, float* y, long long n, F f) {
+    const long long n4 = n >> 2;
+    const float4* a4 = reinterpret_cast<const float4*>(a);
+    const float4* b4 = reinterpret_cast<const float4*>(b);
+    float4* y4 = reinterpret_cast<float4*>(y);
+    const long long stride = (long long)gridDim.x * blockDim.x;
+    const long long t = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    for (long long i = t; i < n4; i += stride) {
+        const float4 u = a4[i];
+        const float4 v = b ? b4[i] : u;
+        y4[i] = make_float4(f(u.x, v.x), f(u.y, v.y), f(u.z, v.z), f(u.w, v.w));
+    }
+    for (long long i = (n4 << 2) + t; i < n; i += stride) y[i] = f(a[i], b ? b[i] : a[i]);
+}
+
 __global__ void sum_kernel(const float* __restrict__ x, float* __restrict__ out, long long n) {
     float s = 0.f;
     for (long long i = threadIdx.x; i < n; i += blockDim.x) s += x[i];
@@ -381,21 +452,56 @@ __global__ void transpose_kernel(const float* __restrict__ in, float* __restrict
 }
 
 __global__ void bias_grad_kernel(const float* __restrict__ dy, float* __restrict__ db, int N, int C,
-                                 int HW) {
-    int c = blockIdx.x;
+                                 FastDiv hw) {
+    const int c = blockIdx.x;
+    const long long cnt = (long long)N * hw.d;
     float s = 0.f;
-    for (long long j = threadIdx.x; j < (long long)N * HW; j += blockDim.x) s += dy[bn_index(j, c, C, HW)];
+#pragma unroll 8
+    for (long long j = threadIdx.x; j < cnt; j += blockDim.x) s += __ldg(dy + bn_index((uint32_t)j, c, C, hw));
     s = block_sum(s);
     if (threadIdx.x == 0) db[c] = s;
 }
 
+// Reduction blocks per channel for the BN statistics: >= 4 blocks per SM overall, each split
+// covering at least 4096 elements, at most 64.
 static int bn_splits(DeviceCtx* c, int C, long long cnt) {
-    // aim for >= 4 blocks per SM overall, each split covering at least 4096 elements
     long long want = (4LL * c->num_sms + C - 1) / C;
     long long maxs = cnt / 4096 > 0 ? cnt / 4096 : 1;
     long long s = want < maxs ? want : maxs;
     if (s > 64) s = 64;
     return s < 1 ? 1 : (int)s;
+}
+static bool aligned16f(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+// 4-float vectors for the elementwise BN kernels: whole vectors share a channel, every pointer is
+// 16-byte aligned and the 32-bit vector index math holds
+static bool bn_vec_flat(int HW, long long total, const void* a, const void* b,
+                        const void* d = nullptr) {
+    return HW % 4 == 0 && aligned16f(a) && aligned16f(b) && (!d || aligned16f(d)) &&
+           total < (1LL << 32);
+}
+
+// The BN training statistics of x into part (sums) and part + C*S (centred squares).
+static int bn_stats(DeviceCtx* c, const float* x, float* part, int N, int C, int HW, int S) {
+    const long long cnt = (long long)N * HW;
+    const long long chunk = (cnt + S - 1) / S;
+    const FastDiv hw = make_fastdiv((uint32_t)HW);
+    const dim3 grid(C, S);
+    bn_partial_sum_kernel<<<grid, 256, 0, c->compute>>>(x, part, C, hw, cnt, chunk);
+    int st = after_launch(c);
+    if (st != OM_OK) return st;
+    bn_partial_m2_kernel<<<grid, 256, 0, c->compute>>>(x, part, part + (long long)C * S, C, hw, cnt,
+                                                       chunk);
+    return after_launch(c);
+}
+static int bn_apply(DeviceCtx* c, const float* x, float* y, const float* gamma, const float* beta,
+                    const float* mean, const float* invstd, long long total, int C, int HW) {
+    if (bn_vec_flat(HW, total, x, y))
+        bn_apply_kernel<4><<<ew_grid(c, total / 4, 256), 256, 0, c->compute>>>(
+            x, y, gamma, beta, mean, invstd, total, C, HW);
+    else
+        bn_apply_kernel<1><<<ew_grid(c, total, 256), 256, 0, c->compute>>>(
+            x, y, gamma, beta, mean, invstd, total, C, HW);
+    return after_launch(c);
 }
 
 }  // namespace ops
@@ -405,6 +511,19 @@ using namespace omb;
 using namespace omb::ops;
 
 #define OMB_EW(n) ew_grid(c, (n), 256), 256, 0, c->compute
+
+// Elementwise y = f(a, b) over n floats: float4 vectors when every pointer is 16-byte aligned,
+// else one float per thread.
+template <class F>
+static int zip(DeviceCtx* c, const float* a, const float* b, float* y, long long n, F f) {
+    const bool vec = ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) |
+                       reinterpret_cast<uintptr_t>(y)) & 15) == 0;
+    if (vec)
+        zip_kernel<<<ew_grid(c, (n + 3) / 4, 256), 256, 0, c->compute>>>(a, b, y, n, f);
+    else
+        map_kernel<<<OMB_EW(n)>>>(n, [=] __device__(long long i) { y[i] = f(a[i], b ? b[i] : a[i]); });
+    return after_launch(c);
+}
 
 extern "C" int omCudaBatchNorm2d(const float* pInput, float* pOutput, const float* pGamma,
                                  const float* pBeta, float* pRunMean, float* pRunVar,
@@ -416,19 +535,13 @@ extern "C" int omCudaBatchNorm2d(const float* pInput, float* pOutput, const floa
         return OM_ERR_INVALID;
     const int HW = nH * nW;
     const long long cnt = (long long)nBatch * HW;
+    if (cnt >= (1LL << 31)) return OM_ERR_UNSUPPORTED;
     int S = 1;
     float* scratch = nullptr;
     if (bTraining) {
         S = bn_splits(c, nChannels, cnt);
         OMB_CHECK(cudaMallocAsync(&scratch, sizeof(float) * 2 * nChannels * S, c->compute));
-        long long chunk = (cnt + S - 1) / S;
-        bn_partial_sum_kernel<<<dim3(nChannels, S), 256, 0, c->compute>>>(pInput, scratch, nChannels, HW, cnt, chunk);
-        int st = after_launch(c);
-        if (st == OM_OK) {
-            bn_partial_m2_kernel<<<dim3(nChannels, S), 256, 0, c->compute>>>(
-                pInput, scratch, scratch + (long long)nChannels * S, nChannels, HW, cnt, chunk);
-            st = after_launch(c);
-        }
+        const int st = bn_stats(c, pInput, scratch, nBatch, nChannels, HW, S);
         if (st != OM_OK) {
             cudaFreeAsync(scratch, c->compute);
             return st;
@@ -440,10 +553,8 @@ extern "C" int omCudaBatchNorm2d(const float* pInput, float* pOutput, const floa
     int st = after_launch(c);
     if (scratch) cudaFreeAsync(scratch, c->compute);
     if (st != OM_OK) return st;
-    const long long total = cnt * nChannels;
-    bn_apply_kernel<<<OMB_EW(total)>>>(pInput, pOutput, pGamma, pBeta, pSavedMean, pSavedInvStd,
-                                       total, nChannels, HW);
-    return after_launch(c);
+    return bn_apply(c, pInput, pOutput, pGamma, pBeta, pSavedMean, pSavedInvStd,
+                    cnt * nChannels, nChannels, HW);
 }
 
 extern "C" int omCudaBatchNorm2dBackward(const float* pGradOutput, const float* pInput,
@@ -458,13 +569,14 @@ extern "C" int omCudaBatchNorm2dBackward(const float* pGradOutput, const float* 
         return OM_ERR_INVALID;
     const int HW = nH * nW;
     const long long cnt = (long long)nBatch * HW;
+    if (cnt >= (1LL << 31)) return OM_ERR_UNSUPPORTED;
     const int S = bn_splits(c, nChannels, cnt);
     float* scratch = nullptr;
     OMB_CHECK(cudaMallocAsync(&scratch, sizeof(float) * 2 * nChannels * S, c->compute));
-    long long chunk = (cnt + S - 1) / S;
+    const long long chunk = (cnt + S - 1) / S;
     bn_bwd_partial_kernel<<<dim3(nChannels, S), 256, 0, c->compute>>>(
         pGradOutput, pInput, pMean, pInvStd, scratch, scratch + (long long)nChannels * S, nChannels,
-        HW, cnt, chunk);
+        make_fastdiv((uint32_t)HW), cnt, chunk);
     int st = after_launch(c);
     if (st == OM_OK) {
         bn_bwd_finalize_kernel<<<(nChannels + 127) / 128, 128, 0, c->compute>>>(
@@ -474,8 +586,14 @@ extern "C" int omCudaBatchNorm2dBackward(const float* pGradOutput, const float* 
     cudaFreeAsync(scratch, c->compute);
     if (st != OM_OK) return st;
     const long long total = cnt * nChannels;
-    bn_bwd_apply_kernel<<<OMB_EW(total)>>>(pGradOutput, pInput, pMean, pInvStd, pGamma, pGradGamma,
-                                           pGradBeta, pGradInput, total, nChannels, HW, (float)cnt);
+    if (bn_vec_flat(HW, total, pGradOutput, pInput, pGradInput))
+        bn_bwd_apply_kernel<4><<<ew_grid(c, total / 4, 256), 256, 0, c->compute>>>(
+            pGradOutput, pInput, pMean, pInvStd, pGamma, pGradGamma, pGradBeta, pGradInput, total,
+            nChannels, HW, (float)cnt);
+    else
+        bn_bwd_apply_kernel<1><<<OMB_EW(total)>>>(pGradOutput, pInput, pMean, pInvStd, pGamma,
+                                                  pGradGamma, pGradBeta, pGradInput, total,
+                                                  nChannels, HW, (float)cnt);
     return after_launch(c);
 }
 
@@ -559,7 +677,9 @@ extern "C" int omCudaAddBiasBackward(const float* pGradOut, float* pGradBias, in
                                      int nHW) {
     OMB_CTX_OR_FAIL(c);
     if (!pGradOut || !pGradBias) return OM_ERR_INVALID;
-    bias_grad_kernel<<<nC, 256, 0, c->compute>>>(pGradOut, pGradBias, nN, nC, nHW);
+    if ((long long)nN * nHW >= (1LL << 31)) return OM_ERR_UNSUPPORTED;
+    bias_grad_kernel<<<nC, 256, 0, c->compute>>>(pGradOut, pGradBias, nN, nC,
+                                                 make_fastdiv((uint32_t)nHW));
     return after_launch(c);
 }
 
@@ -602,46 +722,38 @@ extern "C" int omCudaSgdStep(float* pParam, const float* pGrad, float* pVelocity
 extern "C" int omCudaAdd(const float* pA, const float* pB, float* pC, int nCount) {
     OMB_CTX_OR_FAIL(c);
     if (!pA || !pB || !pC || nCount < 0) return OM_ERR_INVALID;
-    map_kernel<<<OMB_EW(nCount)>>>((long long)nCount, [=] __device__(long long i) { pC[i] = pA[i] + pB[i]; });
-    return after_launch(c);
+    return zip(c, pA, pB, pC, nCount, [] __device__(float a, float b) { return a + b; });
 }
 
 extern "C" int omCudaMulScalar(const float* pA, float fScalar, float* pC, int nCount) {
     OMB_CTX_OR_FAIL(c);
     if (!pA || !pC || nCount < 0) return OM_ERR_INVALID;
-    map_kernel<<<OMB_EW(nCount)>>>((long long)nCount, [=] __device__(long long i) { pC[i] = pA[i] * fScalar; });
-    return after_launch(c);
+    return zip(c, pA, nullptr, pC, nCount,
+               [=] __device__(float a, float) { return a * fScalar; });
 }
 
 extern "C" int omCudaReLU(const float* pIn, float* pOut, int nCount) {
     OMB_CTX_OR_FAIL(c);
     if (!pIn || !pOut || nCount < 0) return OM_ERR_INVALID;
-    map_kernel<<<OMB_EW(nCount)>>>((long long)nCount, [=] __device__(long long i) {
-        float v = pIn[i];
-        pOut[i] = v > 0.f ? v : 0.f;
-    });
-    return after_launch(c);
+    return zip(c, pIn, nullptr, pOut, nCount,
+               [] __device__(float v, float) { return v > 0.f ? v : 0.f; });
 }
 
 extern "C" int omCudaReLUBackward(const float* pIn, const float* pGradOut, float* pGradIn,
                                   int nCount) {
     OMB_CTX_OR_FAIL(c);
     if (!pIn || !pGradOut || !pGradIn || nCount < 0) return OM_ERR_INVALID;
-    map_kernel<<<OMB_EW(nCount)>>>((long long)nCount, [=] __device__(long long i) {
-        pGradIn[i] = pIn[i] > 0.f ? pGradOut[i] : 0.f;
-    });
-    return after_launch(c);
+    return zip(c, pIn, pGradOut, pGradIn, nCount,
+               [] __device__(float x, float g) { return x > 0.f ? g : 0.f; });
 }
 
 extern "C" int omCudaClip(const float* pIn, float* pOut, int nCount, float fMin, float fMax) {
     OMB_CTX_OR_FAIL(c);
     if (!pIn || !pOut || nCount < 0) return OM_ERR_INVALID;
-    map_kernel<<<OMB_EW(nCount)>>>((long long)nCount, [=] __device__(long long i) {
-        float v = pIn[i];
+    return zip(c, pIn, nullptr, pOut, nCount, [=] __device__(float v, float) {
         v = v < fMin ? fMin : v;
-        pOut[i] = v > fMax ? fMax : v;
+        return v > fMax ? fMax : v;
     });
-    return after_launch(c);
 }
 
 extern "C" int omCudaFillValue(float* pData, int nCount, float fValue) {
@@ -718,6 +830,7 @@ extern "C" int omCudaBatchNorm2dNoAlloc(const float* pInput, float* pOutput, con
     if (nChannels > kNoAllocMaxChannels) return OM_ERR_TOO_LARGE;
     const int HW = nH * nW;
     const long long cnt = (long long)nBatch * HW;
+    if (cnt >= (1LL << 31)) return OM_ERR_UNSUPPORTED;
     int S = 1;
     float* scratch = nullptr;
     if (bTraining) {
@@ -733,14 +846,7 @@ extern "C" int omCudaBatchNorm2dNoAlloc(const float* pInput, float* pOutput, con
         S = bn_splits(c, nChannels, cnt);
         if (S > kNoAllocMaxSplits) S = kNoAllocMaxSplits;
         // Nothing needs clearing: each call writes every partial-sum slot it later reads.
-        const long long chunk = (cnt + S - 1) / S;
-        bn_partial_sum_kernel<<<dim3(nChannels, S), 256, 0, c->compute>>>(pInput, scratch, nChannels,
-                                                                          HW, cnt, chunk);
-        int st = after_launch(c);
-        if (st != OM_OK) return st;
-        bn_partial_m2_kernel<<<dim3(nChannels, S), 256, 0, c->compute>>>(
-            pInput, scratch, scratch + (long long)nChannels * S, nChannels, HW, cnt, chunk);
-        st = after_launch(c);
+        const int st = bn_stats(c, pInput, scratch, nBatch, nChannels, HW, S);
         if (st != OM_OK) return st;
     }
     bn_finalize_kernel<<<(nChannels + 127) / 128, 128, 0, c->compute>>>(
@@ -748,8 +854,6 @@ extern "C" int omCudaBatchNorm2dNoAlloc(const float* pInput, float* pOutput, con
         pSavedMean, pSavedInvStd, fEps, fMomentum, bTraining, nChannels);
     int st = after_launch(c);
     if (st != OM_OK) return st;
-    const long long total = cnt * nChannels;
-    bn_apply_kernel<<<OMB_EW(total)>>>(pInput, pOutput, pGamma, pBeta, pSavedMean, pSavedInvStd,
-                                       total, nChannels, HW);
-    return after_launch(c);
+    return bn_apply(c, pInput, pOutput, pGamma, pBeta, pSavedMean, pSavedInvStd,
+                    cnt * nChannels, nChannels, HW);
 }

@@ -117,11 +117,14 @@ def test_grouped_depthwise_conv(gpu):
     assert rel_err_floor(y.to_numpy(want.shape), want) <= TOL
 
 
+# shapes: HW = 63 (scalar planes); HW = 256 (4-float vectors, several blocks per channel);
+# HW = 49 over 64 images (several short planes per pass of a block); HW = 4 (one vector per plane)
+@pytest.mark.parametrize("shape", [(4, 16, 9, 7), (8, 24, 16, 16), (64, 8, 7, 7), (32, 4, 2, 2)])
 @pytest.mark.parametrize("training", [0, 1])
-def test_batchnorm_fwd_bwd(gpu, training):
+def test_batchnorm_fwd_bwd(gpu, training, shape):
     import oracle as orc
     rng = _rng(11 + training)
-    n, c, h, w = 4, 16, 9, 7
+    n, c, h, w = shape
     x = (rng.standard_normal((n, c, h, w)) * 2 + 0.5).astype(np.float32)
     g = rng.uniform(0.5, 1.5, c).astype(np.float32)
     b = rng.standard_normal(c).astype(np.float32)
@@ -270,6 +273,13 @@ def test_elementwise_and_bias(gpu):
     assert np.array_equal(o.to_numpy((1003,)), np.where(x > 0, y, 0))
     B.clip(dX.ptr, o.ptr, 1003, 0.0, 0.5)
     assert np.array_equal(o.to_numpy((1003,)), np.clip(x, 0, 0.5))
+    # in place (output = first input), and a start 4 bytes past 16-byte alignment (scalar path)
+    z = _dev(x)
+    B.add(z.ptr, dY.ptr, z.ptr, 1003)
+    assert np.array_equal(z.to_numpy((1003,)), x + y)
+    o2 = _out((1003,))
+    B.relu(z.ptr + 4, o2.ptr + 4, 1002)
+    assert np.array_equal(o2.to_numpy((1003,))[1:], np.maximum(x + y, 0)[1:])
     n, c, hw = 3, 5, 7
     a = rng.standard_normal((n, c, hw)).astype(np.float32)
     bias = rng.standard_normal(c).astype(np.float32)
