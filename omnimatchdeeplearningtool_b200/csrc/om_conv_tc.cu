@@ -20,7 +20,6 @@
 //               sub-tile brought in by TMA one chunk ahead and the output sub-tile written by
 //               a TMA store from a 64-byte-swizzled staging buffer (fp32 outputs, i.e. the
 //               classifier, store directly)
-//   warps 6..13 MODE_STEM only: build the A tile from the NCHW fp32 image (see below)
 // Two TMEM accumulators (2*BN columns) let the epilogue of tile i overlap the MMAs of i+1.
 // MT = 2 (BN <= 128, one CTA per SM): a tile is two 128-row sub-tiles that share each B stage;
 // every k-block then issues 8 MMAs into two accumulators behind one barrier wait and commit,
@@ -45,14 +44,14 @@
 //   MODE_INTERLEAVE: Cs % 8 == 0 (the 32-channel MobileNet layers). A stage holds 8 im2col
 //               boxes of 128 pixels x 8 channels (2 KB each, no swizzle): core matrices of
 //               8 rows x 16 B, SBO = 128 B (next 8 rows), LBO = 2 KB (next 8 K-elements).
-//   MODE_STEM:  the image stem (few channels, KW <= 8, stride 1 or 2). A tile is one output
-//               row (n, p) and up to 128 output columns; K is ordered (c, r, s) with the taps s
-//               padded to 8, so one 16-byte chunk of an A row holds 8 horizontal taps of one
-//               image plane row. A pre-pass writes the image as 16-bit NCHW rows shifted right
-//               by `pad` columns; one or two TMA boxes per tile bring the tile's rows into
-//               shared memory, and the gather warps copy each A chunk from there (for stride 2,
-//               four aligned 32-bit words) to its 128-byte-swizzled position. B is SW128. The
-//               output is stored through a 3-D map (Cout, Q, N*P) so columns past Q are clipped.
+//   MODE_STEM:  the image stem as a stride-1 R x S convolution over a 16-channel
+//               space-to-depth copy Y (see the host side). A tile is one output row (n, p) and
+//               up to 128 output columns. One 4-D TMA box per tile brings the R rows of Y it
+//               reads (127 + S pixels of 32 bytes each, 32-byte swizzle) into a patch buffer; the
+//               A operand of tap (r, s) is patch rows r * (127 + S) + s .. +127, read by the MMA in
+//               place through a descriptor that starts there (one K=16 MMA per tap). B, the whole
+//               packed weight, stays resident. The output is stored through a 3-D map
+//               (Cout, Q, N*P) so columns past Q are clipped.
 //
 // Every mbarrier wait is bounded (OMB_WAIT_NS); a wait that gives up records a bit in the
 // device error word, raises a CTA-wide abort flag, and the CTA drains its in-flight TMA
@@ -71,19 +70,16 @@ namespace tc {
 constexpr int BM = 128;                 // output pixels per tile (TMEM lanes)
 constexpr int BK = 64;                  // K elements per pipeline stage
 constexpr int A_STAGE_BYTES = BM * BK * 2;
-constexpr int NUM_GATHER_WARPS = 8;     // MODE_STEM only
 constexpr int EPI_SUB_BYTES = 32 * 32 * 2;             // one 32x32 16-bit sub-tile
-// EW epilogue warps (4, 8 for the stem, or 16; EW / 4 per TMEM lane quarter), each with
-// epi_bufs<EW>() 2 KB
-// staging sub-tiles; every CTA also has a producer warp and an MMA warp (and, for the stem,
-// NUM_GATHER_WARPS gather warps after the epilogue warps).
+// EW epilogue warps (4, 8 or 16; EW / 4 per TMEM lane quarter), each with epi_bufs<EW>() 2 KB
+// staging sub-tiles; every CTA also has a producer warp and an MMA warp.
 template <int EW>
 __host__ __device__ constexpr int epi_bufs() { return EW == 4 ? 4 : 2; }
 template <int EW>
 __host__ __device__ constexpr int epi_bytes() { return EW * epi_bufs<EW>() * EPI_SUB_BYTES; }
 template <int MODE, int EW>
 __host__ __device__ constexpr int cta_threads() {
-    return 64 + 32 * EW + (MODE == 2 ? 32 * NUM_GATHER_WARPS : 0);
+    return 64 + 32 * EW;
 }
 constexpr int MAX_DYN_SMEM = 232448;                   // 227 KB per CTA on sm_100
 // MODE_STEM input patch: per tile (output row p, columns q0 .. q0+127), the R space-to-depth
@@ -95,10 +91,6 @@ static_assert(STEM_PATCH_BYTES >= STEM_MAX_R * (BM - 1 + STEM_MAX_S) * 32, "patc
 static_assert(STEM_PATCH_BYTES % 1024 == 0, "patch buffers stay 1024-byte aligned");
 constexpr int STEM_PATCH_BUFS = 3;                     // two tiles' loads in flight
 constexpr int STEM_EXTRA_BYTES = STEM_PATCH_BUFS * STEM_PATCH_BYTES;
-// MODE_STEM tensor memory: the two accumulators (2 * BN columns, BN <= 128), then two A
-// buffers of up to 16 taps (8 columns, i.e. 16 16-bit K elements, per tap) each.
-constexpr uint32_t STEM_TMEM_COLS = 512;
-constexpr int STEM_A_COLS = STEM_MAX_TAPS * 8;
 constexpr unsigned long long OMB_WAIT_NS = 2000000000ull;  // 2 s per wait
 
 enum { MODE_SW128 = 0, MODE_INTERLEAVE = 1, MODE_STEM = 2, MODE_SW32 = 3, MODE_TF32 = 4 };
@@ -270,33 +262,9 @@ __device__ __forceinline__ void tc_mma_tf32(uint32_t d_tmem, uint64_t adesc, uin
         "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
 }
-// MMA with the A operand in tensor memory (lanes = rows, 16-bit K pairs per 32-bit column)
-__device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc,
-                                          uint32_t idesc, uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
-        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate));
-}
-// 16 consecutive 32-bit columns of this thread's TMEM lane
 // The tcgen05 .sync.aligned instructions must be executed by the whole warp together: every
 // helper reconverges the warp first (callers reach them after per-lane spin waits and
 // lane-0-only TMA issue).
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
-    __syncwarp();
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
-        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
-        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
-        "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
-        "r"(v[15])
-        : "memory");
-}
-__device__ __forceinline__ void tmem_wait_st() {
-    __syncwarp();
-    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-}
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
     __syncwarp();
     asm volatile(
@@ -457,10 +425,8 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
     uint64_t* tempty = tfull + 2;
     uint64_t* drain = tempty + 2;
     uint64_t* resfull = drain + 1;  // [EW][EPI_BUFS]
-    uint64_t* patch_full = resfull + EPI_BUFS * EW;  // [STEM_PATCH_BUFS], MODE_STEM
-    uint64_t* a_full = patch_full + STEM_PATCH_BUFS;  // [2], MODE_STEM: A buffer written
-    uint64_t* a_empty = a_full + 2;                   // [2], MODE_STEM: A buffer consumed
-    uint64_t* patch_empty = a_empty + 2;              // [STEM_PATCH_BUFS], MODE_STEM: patch read
+    uint64_t* patch_full = resfull + EPI_BUFS * EW;  // [STEM_PATCH_BUFS], MODE_STEM: written
+    uint64_t* patch_empty = patch_full + STEM_PATCH_BUFS;  // [STEM_PATCH_BUFS]: read by the MMAs
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(patch_empty + STEM_PATCH_BUFS);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
@@ -479,19 +445,15 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
         for (int i = 0; i < EPI_BUFS * EW; ++i) mbar_init(&resfull[i], 1);
         for (int i = 0; i < STEM_PATCH_BUFS; ++i) {
             mbar_init(&patch_full[i], 1);
-            mbar_init(&patch_empty[i], NUM_GATHER_WARPS);
-        }
-        for (int i = 0; i < 2; ++i) {
-            mbar_init(&a_full[i], NUM_GATHER_WARPS);
-            mbar_init(&a_empty[i], 1);
+            mbar_init(&patch_empty[i], 1);
         }
         mbar_init(drain, 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         fence_async_smem();
     }
-    constexpr uint32_t TMEM_ALLOC = MODE == MODE_STEM ? STEM_TMEM_COLS : (uint32_t)C::TMEM_COLS;
-    static_assert(MODE != MODE_STEM || (BN <= 128 && OCC == 1), "stem TMEM layout");
+    constexpr uint32_t TMEM_ALLOC = (uint32_t)C::TMEM_COLS;
+    static_assert(MODE != MODE_STEM || (BN <= 128 && OCC == 1 && MT == 1), "stem tiles");
     static_assert(MODE != MODE_STEM || C::STAGES * BK >= STEM_MAX_TAPS * 16,
                   "the stem's whole packed weight stays resident in the B stages");
     if (warp == 1) {
@@ -514,14 +476,39 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
             int stage = 0;
             uint32_t phase = 0;
             long long issued = 0;
+            long long pissued = 0;   // MODE_STEM: patch loads issued
             bool ok = true;
             if (MODE == MODE_STEM) {
-                // the stem's packed weight (num_kb <= 3 k-blocks) stays resident in the first
+                // the stem's packed weight (num_kb <= 4 k-blocks) stays resident in the first
                 // B stages for the whole kernel: one load, one barrier
                 mbar_expect_tx(&full[0], (uint32_t)(p.num_kb * C::B_STAGE_BYTES));
                 for (int kb = 0; kb < p.num_kb; ++kb)
                     tma_load_2d(sB + kb * C::B_STAGE_BYTES, &tmB, &full[0], kb * BK, 0);
                 issued = 1;
+                // Tile i's patch (Y rows pp .. pp+R-1 at pixels q0 .. q0+126+S, zero-filled past
+                // the image) into buffer i % STEM_PATCH_BUFS, once the MMAs of tile
+                // i - STEM_PATCH_BUFS have read that buffer
+                const uint32_t box_bytes = (uint32_t)(p.R * p.box_w * 32);
+                int pb = 0;
+                uint32_t pph = 0;
+                for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+                    if (!mbar_wait(&patch_empty[pb], pph ^ 1, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    const int rowid = tile / p.QT;             // one N tile: tile = m-tile
+                    const int q0 = (tile - rowid * p.QT) * BM;
+                    const int img = rowid / p.P;
+                    const int pp = rowid - img * p.P;
+                    mbar_expect_tx(&patch_full[pb], box_bytes);
+                    tma_load_4d(sExtra + pb * STEM_PATCH_BYTES, &tmA, &patch_full[pb], 0, q0, pp,
+                                img);
+                    ++pissued;
+                    if (++pb == STEM_PATCH_BUFS) {
+                        pb = 0;
+                        pph ^= 1;
+                    }
+                }
             }
             for (int tile = blockIdx.x; tile < num_tiles && ok && MODE != MODE_STEM;
                  tile += gridDim.x) {
@@ -645,6 +632,15 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
                     break;
                 }
             }
+            // the same for the last STEM_PATCH_BUFS patch loads
+            for (long long j = pissued - STEM_PATCH_BUFS; j < pissued; ++j) {
+                if (j < 0) continue;
+                if (!mbar_wait_drain(&patch_full[(int)(j % STEM_PATCH_BUFS)],
+                                     (uint32_t)((j / STEM_PATCH_BUFS) & 1))) {
+                    atomicOr(p.err, ERRBIT_TC_DRAIN);
+                    break;
+                }
+            }
         }
     } else if (warp == 1) {
         if (lane == 0) {
@@ -668,28 +664,45 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
             bool ok = true;
             int local = 0;
             if (MODE == MODE_STEM) {
-                // A from tensor memory (written by the gather warps, two buffers), B resident
+                // Tap t = (r, s) of output column m reads patch pixel (r, m + s): its 128 x 16 A
+                // operand is the 128 consecutive 32-byte patch rows from r * box_w + s on, read in
+                // place (32-byte swizzle; the descriptor may start on any row, the swizzle follows
+                // the address bits). B k-block t / 4, K step t % 4, resident.
                 ok = mbar_wait(&full[0], 0, abort_flag);
+                const uint32_t patch0 = smem_u32(sExtra);
+                const int taps = p.R * p.S;
+                int pb = 0;
+                uint32_t pph = 0;
                 for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
                     const int acc = local & 1;
                     const uint32_t par = (uint32_t)((local >> 1) & 1);
                     if (!mbar_wait(&tempty[acc], par ^ 1, abort_flag) ||
-                        !mbar_wait(&a_full[acc], par, abort_flag)) {
+                        !mbar_wait(&patch_full[pb], pph, abort_flag)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
-                    const uint32_t a_tmem = tmem_base + (uint32_t)(2 * BN + acc * STEM_A_COLS);
-                    // tap t: A columns 8t .. 8t+7, B k-block t / 4, K step t % 4
-                    const int taps = p.R * p.S;
-                    for (int t = 0; t < taps; ++t)
-                        tc_mma_ts(d_tmem, a_tmem + (uint32_t)(t * 8),
-                                  bdesc0 + (uint64_t)((t >> 2) * (C::B_STAGE_BYTES >> 4)) +
-                                      (t & 3) * B_K_STEP,
-                                  IDESC, t > 0 ? 1u : 0u);
-                    tc_commit(&a_empty[acc]);
+                    const uint32_t d_tmem = tmem_base + (uint32_t)(acc * C::ACC_COLS);
+                    const uint32_t base = patch0 + (uint32_t)(pb * STEM_PATCH_BYTES);
+                    int r = 0, sx = 0;
+                    for (int t = 0; t < taps; ++t) {
+                        const uint64_t ad =
+                            smem_desc(base + (uint32_t)((r * p.box_w + sx) * 32), 16, 256, LAYOUT_SW32);
+                        tc_mma(d_tmem, ad,
+                               bdesc0 + (uint64_t)((t >> 2) * (C::B_STAGE_BYTES >> 4)) +
+                                   (t & 3) * B_K_STEP,
+                               IDESC, t > 0 ? 1u : 0u);
+                        if (++sx == p.S) {
+                            sx = 0;
+                            ++r;
+                        }
+                    }
+                    tc_commit(&patch_empty[pb]);
                     tc_commit(&tfull[acc]);
+                    if (++pb == STEM_PATCH_BUFS) {
+                        pb = 0;
+                        pph ^= 1;
+                    }
                 }
             }
             for (int tile = blockIdx.x; tile < num_tiles && ok && MODE != MODE_STEM;
@@ -793,6 +806,7 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
         uint32_t rph = 0;     // per sub-tile: parity of its next residual load
         uint32_t rpend = 0;   // per sub-tile: a residual load is in flight
         int pre_next = 0;     // live chunks of the next tile whose residual is already requested
+        int bias_nbase = -1;  // BIAS_SMEM: the column the warp's bias copy starts at
         bool ok = true;
         int local = 0;
         // lane 0 only: request the residual of chunk h (sub-tile h % EPI_BUFS)
@@ -883,10 +897,14 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
             // shuffle path: the bias of the first live chunk, loaded before the accumulator wait
             float bnext = 0.f;
             if (BIAS_SMEM) {
+                // reloaded only when the tile's columns change (never with one N tile)
+                if (nbase != bias_nbase) {
 #pragma unroll
-                for (int j = 0; j < NCH; ++j) {
-                    const int col = nbase + j * 32 + lane;
-                    sbias[j * 32 + lane] = (p.bias && col < p.K) ? __ldg(p.bias + col) : 0.f;
+                    for (int j = 0; j < NCH; ++j) {
+                        const int col = nbase + j * 32 + lane;
+                        sbias[j * 32 + lane] = (p.bias && col < p.K) ? __ldg(p.bias + col) : 0.f;
+                    }
+                    bias_nbase = nbase;
                 }
                 __syncwarp();
             } else if (lmask) {
@@ -1058,141 +1076,6 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
             }
         }
         __syncwarp();
-    } else if (MODE == MODE_STEM) {
-        // ---------------------------------------------------------------- gather (stem)
-        // Input: the space-to-depth image Y [N, H, W, 16] (16-bit); the stem is a stride-1 R x S
-        // convolution over it. Tile i = output row (img, pp), columns q0 .. q0+127. Its patch
-        // (buffer i % 3) holds Y rows pp .. pp+R-1 at pixels q0 + [0, box_w), written by one
-        // TMA box with the 32-byte swizzle (the two 16-byte halves of a pixel swap when bit 2
-        // of its index in the box is set), so that a warp's 16-byte reads of 32 consecutive
-        // pixels are free of bank conflicts. A row m, tap t = (r, s): the 32 bytes of patch pixel
-        // (r, m + s), i.e. K elements 16t .. 16t+15 = TMEM columns 8t .. 8t+7. Pixels past the
-        // image are zero-filled by TMA; rows m with q0 + m >= Q are computed but never stored.
-        // Two gather warps per TMEM lane quarter split the taps. Gather thread 0 loads each
-        // tile's patch two tiles ahead, into a buffer every gather warp has released
-        // (patch_empty); the warps otherwise run independently.
-        const int gw = warp - 2 - EW;
-        const int gt = gw * 32 + lane;
-        // a warp writes only its TMEM lane quarter (warp % 4): A row = that quarter's 32 rows
-        const int row = (warp & 3) * 32 + lane;  // A row this thread builds
-        const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
-        const int taps = p.R * p.S;
-        // taps per gather warp, even: a lone last tap is stored with a zero partner, which
-        // lands in columns no other warp writes
-        const int tpw = (((taps + 1) >> 1) + 1) & ~1;
-        const int t_begin = (gw >> 2) * tpw;
-        const int t_end = t_begin + tpw < taps ? t_begin + tpw : taps;
-        const uint32_t box_bytes = (uint32_t)(p.R * p.box_w * 32);
-        const int my_tiles =
-            (int)blockIdx.x < num_tiles ? (num_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-        auto tile_row = [&](int i, int& rowid, int& q0) {
-            const int mt = ((int)blockIdx.x + i * (int)gridDim.x) / p.num_n_tiles;
-            rowid = mt / p.QT;
-            q0 = (mt - rowid * p.QT) * BM;
-        };
-        auto issue = [&](int i) {
-            int rowid, q0;
-            tile_row(i, rowid, q0);
-            const int img = rowid / p.P;
-            const int pp = rowid - img * p.P;
-            uint8_t* dst = sExtra + (i % STEM_PATCH_BUFS) * STEM_PATCH_BYTES;
-            uint64_t* bar = &patch_full[i % STEM_PATCH_BUFS];
-            fence_async_smem();   // generic reads of this buffer (tile i-3) precede the TMA write
-            mbar_expect_tx(bar, box_bytes);
-            tma_load_4d(dst, &tmA, bar, 0, q0, pp, img);
-        };
-        // Tile i's A goes to TMEM buffer i % 2 (columns 2*BN + (i % 2) * STEM_A_COLS), once the
-        // MMAs of tile i-2 have consumed it.
-        auto build = [&](int i) -> bool {
-            const int buf = i & 1;
-            const bool got = mbar_wait(&a_empty[buf], (uint32_t)(((i >> 1) & 1) ^ 1), abort_flag);
-            if (!__all_sync(0xffffffffu, got)) return false;   // warp-uniform
-            tc_fence_after();
-            const uint8_t* pb = sExtra + (i % STEM_PATCH_BUFS) * STEM_PATCH_BYTES;
-            const uint32_t a_col = tmem_base + lane_base + (uint32_t)(2 * BN + buf * STEM_A_COLS);
-            int r = t_begin / p.S, sx = t_begin - r * p.S;
-            for (int t = t_begin; t < t_end; t += 2) {
-                uint32_t w16[16];
-#pragma unroll
-                for (int jj = 0; jj < 2; ++jj) {
-                    uint4 lo = make_uint4(0, 0, 0, 0), hi = lo;
-                    if (t + jj < t_end) {
-                        // flattened box index: the swizzle follows shared-memory address
-                        // bit 7 (buffers are 1024-byte aligned)
-                        const int idx = r * p.box_w + row + sx;
-                        const uint8_t* pix = pb + idx * 32;
-                        const int swap = (idx >> 2) & 1;
-                        lo = *reinterpret_cast<const uint4*>(pix + (swap << 4));
-                        hi = *reinterpret_cast<const uint4*>(pix + ((swap ^ 1) << 4));
-                        if (++sx == p.S) {
-                            sx = 0;
-                            ++r;
-                        }
-                    }
-                    w16[8 * jj + 0] = lo.x; w16[8 * jj + 1] = lo.y;
-                    w16[8 * jj + 2] = lo.z; w16[8 * jj + 3] = lo.w;
-                    w16[8 * jj + 4] = hi.x; w16[8 * jj + 5] = hi.y;
-                    w16[8 * jj + 6] = hi.z; w16[8 * jj + 7] = hi.w;
-                }
-                tmem_st16(a_col + (uint32_t)(t * 8), w16);
-            }
-            // the stores are complete before the MMA issuer may read them
-            tmem_wait_st();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&a_full[buf]);
-            return true;
-        };
-        bool failed = false;
-        int issued = 0, waited = 0;   // patch loads issued / waited for (thread gt == 0)
-        if (gt == 0) {
-            for (; issued < 2 && issued < my_tiles; ++issued) issue(issued);
-        }
-        // every stop decision is taken by the whole warp (__any_sync), so that the warp stays
-        // converged for the tcgen05 stores
-        for (int i = 0; i < my_tiles; ++i) {
-            bool bad = false;
-            if (gt == 0 && i + 2 < my_tiles) {
-                // buffer (i+2) % 3 held tile i-1's patch: wait until every gather warp read it
-                if (i >= 1 && !mbar_wait(&patch_empty[(i - 1) % STEM_PATCH_BUFS],
-                                         (uint32_t)(((i - 1) / STEM_PATCH_BUFS) & 1), abort_flag))
-                    bad = true;
-                else
-                    issue(issued++);
-            }
-            if (__any_sync(0xffffffffu, bad)) {
-                failed = true;
-                break;
-            }
-            bad = !mbar_wait(&patch_full[i % STEM_PATCH_BUFS], (uint32_t)((i / STEM_PATCH_BUFS) & 1),
-                             abort_flag);
-            if (__any_sync(0xffffffffu, bad)) {
-                failed = true;
-                break;
-            }
-            if (gt == 0) ++waited;
-            if (!build(i)) {
-                failed = true;
-                break;
-            }
-            // this warp is done reading tile i's patch
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&patch_empty[i % STEM_PATCH_BUFS]);
-        }
-        if (gt == 0) {
-            // no patch load may land after the CTA exits
-            for (int j = waited; j < issued; ++j) {
-                if (!mbar_wait_drain(&patch_full[j % STEM_PATCH_BUFS],
-                                     (uint32_t)((j / STEM_PATCH_BUFS) & 1))) {
-                    atomicOr(p.err, ERRBIT_TC_DRAIN);
-                    break;
-                }
-            }
-        }
-        if (failed && lane == 0) {
-            atomicOr(p.err, ERRBIT_TC_PRODUCER);
-            *abort_flag = 1;
-        }
     }
 
     tc_fence_before();
@@ -1297,7 +1180,7 @@ static int dispatch_bn(DeviceCtx* c, int bn, int occ, int mt, int ew, const CUte
             return OM_ERR_UNSUPPORTED;
         }
     }
-    if constexpr (MODE != MODE_STEM) {  // the stem's 14 warps run one CTA per SM
+    if constexpr (MODE != MODE_STEM) {  // the stem runs one CTA per SM
         if (occ == 2) {
             switch (bn) {
                 case 32: return launch<32, MODE, DT, 2>(c, ta, tb, to, tr, p);
@@ -1307,7 +1190,7 @@ static int dispatch_bn(DeviceCtx* c, int bn, int occ, int mt, int ew, const CUte
             return OM_ERR_UNSUPPORTED;
         }
     }
-    if constexpr (MODE == MODE_STEM) {  // 8 epilogue warps beside the 8 gather warps
+    if constexpr (MODE == MODE_STEM) {  // 8 epilogue warps
         switch (bn) {
             case 32: return launch<32, MODE, DT, 1, 1, 8>(c, ta, tb, to, tr, p);
             case 64: return launch<64, MODE, DT, 1, 1, 8>(c, ta, tb, to, tr, p);
@@ -1320,7 +1203,7 @@ static int dispatch_bn(DeviceCtx* c, int bn, int occ, int mt, int ew, const CUte
         case 64: return launch<64, MODE, DT, 1>(c, ta, tb, to, tr, p);
         case 128: return launch<128, MODE, DT, 1>(c, ta, tb, to, tr, p);
     }
-    if constexpr (MODE != MODE_STEM) {  // the stem keeps A in TMEM beside <= 128-wide tiles
+    if constexpr (MODE != MODE_STEM) {  // stem tiles are <= 128 wide
         if (bn == 256) return launch<256, MODE, DT, 1>(c, ta, tb, to, tr, p);
     }
     return OM_ERR_UNSUPPORTED;
