@@ -15,7 +15,7 @@ for f in "$REF"/src/hal/om.hal.simd.ixx "$REF"/src/hal/om.hal.cpu_backend.ixx \
          "$REF"/src/engine/om.engine.activations.ixx "$REF"/src/engine/om.engine.conv.ixx \
          "$REF"/src/engine/om.engine.resnet.ixx "$REF"/src/engine/om.engine.resnet50.ixx \
          "$REF"/src/engine/om.engine.mobilenet.ixx "$REF"/src/engine/om.engine.optimizer.ixx \
-         "$REF"/src/engine/om.engine.loss.ixx; do
+         "$REF"/src/engine/om.engine.loss.ixx "$REF"/src/engine/om.engine.serializer.ixx; do
   b=$(basename "$f" .ixx)
   { echo '#pragma once'; \
     sed -e 's/^module;.*$//' -e 's/^export module .*;.*$//' \

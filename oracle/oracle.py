@@ -93,6 +93,7 @@ def ref():
             "omref_model_set_buffer": [P, I, P], "omref_model_get_buffer": [P, I, P],
             "omref_model_forward": [P, P, I, I, I, P],
             "omref_model_train_step": [P, P, P, I, I, I, I, F, F, I, P],
+            "omref_model_save": [P, ctypes.c_char_p, ctypes.c_char_p],
         }
         for n, a in sigs.items():
             f = getattr(L, n)
@@ -105,7 +106,7 @@ def ref():
         L.omref_cross_entropy.restype = c_float
         L.omref_model_train_step.restype = c_float
         for n in ("omref_model_num_params", "omref_model_num_buffers", "omref_model_param_info",
-                  "omref_model_buffer_info"):
+                  "omref_model_buffer_info", "omref_model_save"):
             getattr(L, n).restype = c_int
         _REF = L
     return _REF

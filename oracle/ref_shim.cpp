@@ -27,6 +27,7 @@ namespace std { using ::sqrtf; }  // om.engine.tensor_ops.ixx:901 names std::sqr
 #include "om.engine.mobilenet.hpp"
 #include "om.engine.optimizer.hpp"
 #include "om.engine.loss.hpp"
+#include "om.engine.serializer.hpp"
 
 #include <cstring>
 #include <memory>
@@ -206,6 +207,24 @@ public:
     std::shared_ptr<om::Linear> fc;
 };
 
+// A few-hundred-parameter model (conv with bias, BN, FC) whose .omm files the golden fixtures
+// keep: small enough to commit, with every entry kind (4-D, 1-D and 2-D parameters, BN buffers).
+class TinyNet : public om::Module {
+public:
+    explicit TinyNet(int classes) {
+        conv = std::make_shared<om::Conv2d>(3, 4, 3, 1, 1, true);
+        bn = std::make_shared<om::BatchNorm2d>(4);
+        fc = std::make_shared<om::Linear>(4, classes, true);
+        registerModule("conv", conv);
+        registerModule("bn", bn);
+        registerModule("fc", fc);
+    }
+    Tensor forward(const Tensor& x) override { return x; }
+    std::shared_ptr<om::Conv2d> conv;
+    std::shared_ptr<om::BatchNorm2d> bn;
+    std::shared_ptr<om::Linear> fc;
+};
+
 struct RefModel {
     std::unique_ptr<om::Module> mod;
     std::vector<std::pair<std::string, Tensor*>> params, bufs;
@@ -216,7 +235,9 @@ struct RefModel {
 
 void* omref_model_create(int kind, int classes) {
     auto* m = new RefModel();
-    if (kind == 2)
+    if (kind == 3)
+        m->mod = std::make_unique<TinyNet>(classes);
+    else if (kind == 2)
         m->mod = std::make_unique<MobileStack>(classes);
     else
         m->mod = std::make_unique<ImageNetResNet>(kind, classes);
@@ -225,6 +246,26 @@ void* omref_model_create(int kind, int classes) {
     return m;
 }
 void omref_model_destroy(void* h) { delete static_cast<RefModel*>(h); }
+// The model's parameters and buffers written by the reference's own ModelSerializer::save
+// (format v5, om.engine.serializer.ixx:174), XOR-encrypted with `password` when it is not
+// empty. Returns 0, or -1 when save threw.
+int omref_model_save(void* h, const char* path, const char* password) {
+    try {
+        om::ModelEncryptConfig enc;
+        if (password && password[0]) {
+            enc.bEncrypt = true;
+            enc.strPassword = password;
+        }
+        om::ModelMeta meta;
+        meta.strModelType = "TinyNet";
+        meta.nModelTypeHash = om::ModelMeta::hashString(meta.strModelType);
+        meta.nNumClasses = 3;
+        om::ModelSerializer::save(*static_cast<RefModel*>(h)->mod, path, meta, enc);
+        return 0;
+    } catch (...) {
+        return -1;
+    }
+}
 int omref_model_num_params(void* h) { return (int)static_cast<RefModel*>(h)->params.size(); }
 int omref_model_num_buffers(void* h) { return (int)static_cast<RefModel*>(h)->bufs.size(); }
 
