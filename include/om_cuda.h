@@ -146,6 +146,22 @@ int omCudaBatchNorm2dBackward(const float* pGradOutput, const float* pInput, con
                               const float* pInvStd, const float* pGamma, float* pGradInput,
                               float* pGradGamma, float* pGradBeta, int nBatch, int nChannels,
                               int nH, int nW, float fEps);                       /* replaces :3130 */
+/* new: BatchNorm with the activation that follows it (nAct: OM_ACT_NONE or OM_ACT_RELU)
+ * applied in the same pass, for conv -> BN -> ReLU chains (the reference calls :1648 and then
+ * its ReLU kernel). Same arguments as omCudaBatchNorm2d plus nAct; pOutput receives the
+ * activated result, bit-identical to omCudaBatchNorm2d followed by omCudaReLU. */
+int omCudaBatchNorm2dAct(const float* pInput, float* pOutput, const float* pGamma,
+                         const float* pBeta, float* pRunMean, float* pRunVar, float* pSavedMean,
+                         float* pSavedInvStd, int nBatch, int nChannels, int nH, int nW,
+                         float fEps, float fMomentum, int bTraining, int nAct);
+/* new: the matching backward (the reference calls its ReLU backward, then :3130). pOutput is the
+ * forward's activated output: the incoming gradient is zeroed where pOutput <= 0 inside the BN
+ * backward passes. Bit-identical to omCudaReLUBackward followed by omCudaBatchNorm2dBackward. */
+int omCudaBatchNorm2dBackwardAct(const float* pGradOutput, const float* pInput,
+                                 const float* pMean, const float* pInvStd, const float* pGamma,
+                                 const float* pOutput, float* pGradInput, float* pGradGamma,
+                                 float* pGradBeta, int nBatch, int nChannels, int nH, int nW,
+                                 float fEps, int nAct);
 int omCudaMaxPool2d(const float* pIn, float* pOut, int* pIndices, int nN, int nC, int nH, int nW,
                     int nKH, int nKW, int nSH, int nSW, int nPH, int nPW);       /* replaces :2052 */
 /* accumulates into pGradIn (callers zero it first, as CUDABackend::maxPool2dBackward does) */

@@ -82,6 +82,8 @@ _SIGS = {
     # norm / pool / loss / optimiser
     "omCudaBatchNorm2d": [P, P, P, P, P, P, P, P, I, I, I, I, F, F, I],
     "omCudaBatchNorm2dBackward": [P, P, P, P, P, P, P, P, I, I, I, I, F],
+    "omCudaBatchNorm2dAct": [P, P, P, P, P, P, P, P, I, I, I, I, F, F, I, I],
+    "omCudaBatchNorm2dBackwardAct": [P, P, P, P, P, P, P, P, P, I, I, I, I, F, I],
     "omCudaBatchNorm2dNoAlloc": [P, P, P, P, P, P, P, P, I, I, I, I, F, F, I],
     "omCudaMaxPool2d": [P, P, P, I, I, I, I, I, I, I, I, I, I],
     "omCudaMaxPool2dBackward": [P, P, P, I, I, I, I, I, I],

@@ -120,11 +120,13 @@ __global__ void bn_finalize_kernel(const float* __restrict__ psum, const float* 
 
 // Elementwise BN kernels over the NCHW tensor. V = 4: vectors of 4 floats that share a channel
 // (HW % 4 == 0), one 32-bit division per vector (total < 2^32); V = 1: any shape.
+// relu = 1: the ReLU of the result, written with the reference's expression (v > 0 ? v : 0).
+__device__ __forceinline__ float bn_act(float v, int relu) { return relu ? (v > 0.f ? v : 0.f) : v; }
 template <int V>
 __global__ void bn_apply_kernel(const float* __restrict__ x, float* __restrict__ y,
                                 const float* __restrict__ gamma, const float* __restrict__ beta,
                                 const float* __restrict__ mean, const float* __restrict__ invstd,
-                                long long total, int C, int HW) {
+                                long long total, int C, int HW, int relu) {
     const long long nv = total / V;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < nv;
          i += (long long)gridDim.x * blockDim.x) {
@@ -134,20 +136,21 @@ __global__ void bn_apply_kernel(const float* __restrict__ x, float* __restrict__
         if constexpr (V == 4) {
             const float4 v = __ldg(reinterpret_cast<const float4*>(x) + i);
             reinterpret_cast<float4*>(y)[i] = make_float4(
-                gamma[c] * (v.x - mean[c]) * invstd[c] + beta[c],
-                gamma[c] * (v.y - mean[c]) * invstd[c] + beta[c],
-                gamma[c] * (v.z - mean[c]) * invstd[c] + beta[c],
-                gamma[c] * (v.w - mean[c]) * invstd[c] + beta[c]);
+                bn_act(gamma[c] * (v.x - mean[c]) * invstd[c] + beta[c], relu),
+                bn_act(gamma[c] * (v.y - mean[c]) * invstd[c] + beta[c], relu),
+                bn_act(gamma[c] * (v.z - mean[c]) * invstd[c] + beta[c], relu),
+                bn_act(gamma[c] * (v.w - mean[c]) * invstd[c] + beta[c], relu));
         } else {
-            y[i] = gamma[c] * (x[i] - mean[c]) * invstd[c] + beta[c];
+            y[i] = bn_act(gamma[c] * (x[i] - mean[c]) * invstd[c] + beta[c], relu);
         }
     }
 }
 
 __global__ void bn_bwd_partial_kernel(const float* __restrict__ dy, const float* __restrict__ x,
                                       const float* __restrict__ mean, const float* __restrict__ invstd,
-                                      float* __restrict__ pg, float* __restrict__ pb, int C,
-                                      FastDiv hw, long long cnt, long long chunk) {
+                                      const float* __restrict__ mask, float* __restrict__ pg,
+                                      float* __restrict__ pb, int C, FastDiv hw, long long cnt,
+                                      long long chunk) {
     const int c = blockIdx.x, z = blockIdx.y;
     const float mu = mean[c], is = invstd[c];
     const long long beg = z * chunk, end = min(cnt, beg + chunk);
@@ -155,7 +158,8 @@ __global__ void bn_bwd_partial_kernel(const float* __restrict__ dy, const float*
 #pragma unroll 8
     for (long long j = beg + threadIdx.x; j < end; j += blockDim.x) {
         const size_t idx = bn_index((uint32_t)j, c, C, hw);
-        const float g = __ldg(dy + idx);
+        float g = __ldg(dy + idx);
+        if (mask) g = __ldg(mask + idx) > 0.f ? g : 0.f;   // the ReLU backward, fused
         sg += g * (__ldg(x + idx) - mu) * is;
         sb += g;
     }
@@ -184,7 +188,8 @@ __global__ void bn_bwd_apply_kernel(const float* __restrict__ dy, const float* _
                                     const float* __restrict__ mean, const float* __restrict__ invstd,
                                     const float* __restrict__ gamma, const float* __restrict__ dgamma,
                                     const float* __restrict__ dbeta, float* __restrict__ dx,
-                                    long long total, int C, int HW, float M) {
+                                    long long total, int C, int HW, float M,
+                                    const float* __restrict__ mask) {
     const long long nv = total / V;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < nv;
          i += (long long)gridDim.x * blockDim.x) {
@@ -194,7 +199,12 @@ __global__ void bn_bwd_apply_kernel(const float* __restrict__ dy, const float* _
         const float is = invstd[c], mu = mean[c], k = gamma[c] * is / M, db = dbeta[c],
                     dg = dgamma[c];
         if constexpr (V == 4) {
-            const float4 g = __ldg(reinterpret_cast<const float4*>(dy) + i);
+            float4 g = __ldg(reinterpret_cast<const float4*>(dy) + i);
+            if (mask) {
+                const float4 m = __ldg(reinterpret_cast<const float4*>(mask) + i);
+                g.x = m.x > 0.f ? g.x : 0.f; g.y = m.y > 0.f ? g.y : 0.f;
+                g.z = m.z > 0.f ? g.z : 0.f; g.w = m.w > 0.f ? g.w : 0.f;
+            }
             const float4 v = __ldg(reinterpret_cast<const float4*>(x) + i);
             reinterpret_cast<float4*>(dx)[i] =
                 make_float4(k * (M * g.x - db - (v.x - mu) * is * dg),
@@ -203,7 +213,8 @@ __global__ void bn_bwd_apply_kernel(const float* __restrict__ dy, const float* _
                             k * (M * g.w - db - (v.w - mu) * is * dg));
         } else {
             const float xh = (x[i] - mu) * is;
-            dx[i] = k * (M * dy[i] - db - xh * dg);
+            const float g = mask ? (mask[i] > 0.f ? dy[i] : 0.f) : dy[i];
+            dx[i] = k * (M * g - db - xh * dg);
         }
     }
 }
@@ -494,13 +505,14 @@ static int bn_stats(DeviceCtx* c, const float* x, float* part, int N, int C, int
     return after_launch(c);
 }
 static int bn_apply(DeviceCtx* c, const float* x, float* y, const float* gamma, const float* beta,
-                    const float* mean, const float* invstd, long long total, int C, int HW) {
+                    const float* mean, const float* invstd, long long total, int C, int HW,
+                    int relu = 0) {
     if (bn_vec_flat(HW, total, x, y))
         bn_apply_kernel<4><<<ew_grid(c, total / 4, 256), 256, 0, c->compute>>>(
-            x, y, gamma, beta, mean, invstd, total, C, HW);
+            x, y, gamma, beta, mean, invstd, total, C, HW, relu);
     else
         bn_apply_kernel<1><<<ew_grid(c, total, 256), 256, 0, c->compute>>>(
-            x, y, gamma, beta, mean, invstd, total, C, HW);
+            x, y, gamma, beta, mean, invstd, total, C, HW, relu);
     return after_launch(c);
 }
 
@@ -525,10 +537,11 @@ static int zip(DeviceCtx* c, const float* a, const float* b, float* y, long long
     return after_launch(c);
 }
 
-extern "C" int omCudaBatchNorm2d(const float* pInput, float* pOutput, const float* pGamma,
-                                 const float* pBeta, float* pRunMean, float* pRunVar,
-                                 float* pSavedMean, float* pSavedInvStd, int nBatch, int nChannels,
-                                 int nH, int nW, float fEps, float fMomentum, int bTraining) {
+// BatchNorm forward, with the ReLU of the result applied in the same pass when relu = 1.
+static int bn_forward(const float* pInput, float* pOutput, const float* pGamma, const float* pBeta,
+                      float* pRunMean, float* pRunVar, float* pSavedMean, float* pSavedInvStd,
+                      int nBatch, int nChannels, int nH, int nW, float fEps, float fMomentum,
+                      int bTraining, int relu) {
     OMB_CTX_OR_FAIL(c);
     if (!pInput || !pOutput || !pGamma || !pBeta || !pRunMean || !pRunVar || !pSavedMean ||
         !pSavedInvStd || nBatch <= 0 || nChannels <= 0 || nH <= 0 || nW <= 0)
@@ -554,18 +567,18 @@ extern "C" int omCudaBatchNorm2d(const float* pInput, float* pOutput, const floa
     if (scratch) cudaFreeAsync(scratch, c->compute);
     if (st != OM_OK) return st;
     return bn_apply(c, pInput, pOutput, pGamma, pBeta, pSavedMean, pSavedInvStd,
-                    cnt * nChannels, nChannels, HW);
+                    cnt * nChannels, nChannels, HW, relu);
 }
 
-extern "C" int omCudaBatchNorm2dBackward(const float* pGradOutput, const float* pInput,
-                                         const float* pMean, const float* pInvStd,
-                                         const float* pGamma, float* pGradInput, float* pGradGamma,
-                                         float* pGradBeta, int nBatch, int nChannels, int nH,
-                                         int nW, float fEps) {
-    (void)fEps;
+// BatchNorm backward; with pMask (the ReLU output of a fused forward), the incoming gradient
+// first goes through the ReLU backward (zero where pMask <= 0), in the same passes.
+static int bn_backward(const float* pGradOutput, const float* pInput, const float* pMean,
+                       const float* pInvStd, const float* pGamma, const float* pMask,
+                       float* pGradInput, float* pGradGamma, float* pGradBeta, int nBatch,
+                       int nChannels, int nH, int nW) {
     OMB_CTX_OR_FAIL(c);
     if (!pGradOutput || !pInput || !pMean || !pInvStd || !pGamma || !pGradInput || !pGradGamma ||
-        !pGradBeta)
+        !pGradBeta || nBatch <= 0 || nChannels <= 0 || nH <= 0 || nW <= 0)
         return OM_ERR_INVALID;
     const int HW = nH * nW;
     const long long cnt = (long long)nBatch * HW;
@@ -575,8 +588,8 @@ extern "C" int omCudaBatchNorm2dBackward(const float* pGradOutput, const float* 
     OMB_CHECK(cudaMallocAsync(&scratch, sizeof(float) * 2 * nChannels * S, c->compute));
     const long long chunk = (cnt + S - 1) / S;
     bn_bwd_partial_kernel<<<dim3(nChannels, S), 256, 0, c->compute>>>(
-        pGradOutput, pInput, pMean, pInvStd, scratch, scratch + (long long)nChannels * S, nChannels,
-        make_fastdiv((uint32_t)HW), cnt, chunk);
+        pGradOutput, pInput, pMean, pInvStd, pMask, scratch, scratch + (long long)nChannels * S,
+        nChannels, make_fastdiv((uint32_t)HW), cnt, chunk);
     int st = after_launch(c);
     if (st == OM_OK) {
         bn_bwd_finalize_kernel<<<(nChannels + 127) / 128, 128, 0, c->compute>>>(
@@ -586,15 +599,58 @@ extern "C" int omCudaBatchNorm2dBackward(const float* pGradOutput, const float* 
     cudaFreeAsync(scratch, c->compute);
     if (st != OM_OK) return st;
     const long long total = cnt * nChannels;
-    if (bn_vec_flat(HW, total, pGradOutput, pInput, pGradInput))
+    if (bn_vec_flat(HW, total, pGradOutput, pInput, pGradInput) && (!pMask || aligned16f(pMask)))
         bn_bwd_apply_kernel<4><<<ew_grid(c, total / 4, 256), 256, 0, c->compute>>>(
             pGradOutput, pInput, pMean, pInvStd, pGamma, pGradGamma, pGradBeta, pGradInput, total,
-            nChannels, HW, (float)cnt);
+            nChannels, HW, (float)cnt, pMask);
     else
         bn_bwd_apply_kernel<1><<<OMB_EW(total)>>>(pGradOutput, pInput, pMean, pInvStd, pGamma,
                                                   pGradGamma, pGradBeta, pGradInput, total,
-                                                  nChannels, HW, (float)cnt);
+                                                  nChannels, HW, (float)cnt, pMask);
     return after_launch(c);
+}
+
+extern "C" int omCudaBatchNorm2d(const float* pInput, float* pOutput, const float* pGamma,
+                                 const float* pBeta, float* pRunMean, float* pRunVar,
+                                 float* pSavedMean, float* pSavedInvStd, int nBatch, int nChannels,
+                                 int nH, int nW, float fEps, float fMomentum, int bTraining) {
+    return bn_forward(pInput, pOutput, pGamma, pBeta, pRunMean, pRunVar, pSavedMean, pSavedInvStd,
+                      nBatch, nChannels, nH, nW, fEps, fMomentum, bTraining, 0);
+}
+
+extern "C" int omCudaBatchNorm2dBackward(const float* pGradOutput, const float* pInput,
+                                         const float* pMean, const float* pInvStd,
+                                         const float* pGamma, float* pGradInput, float* pGradGamma,
+                                         float* pGradBeta, int nBatch, int nChannels, int nH,
+                                         int nW, float fEps) {
+    (void)fEps;
+    return bn_backward(pGradOutput, pInput, pMean, pInvStd, pGamma, nullptr, pGradInput,
+                       pGradGamma, pGradBeta, nBatch, nChannels, nH, nW);
+}
+
+extern "C" int omCudaBatchNorm2dAct(const float* pInput, float* pOutput, const float* pGamma,
+                                    const float* pBeta, float* pRunMean, float* pRunVar,
+                                    float* pSavedMean, float* pSavedInvStd, int nBatch,
+                                    int nChannels, int nH, int nW, float fEps, float fMomentum,
+                                    int bTraining, int nAct) {
+    if (nAct != OM_ACT_NONE && nAct != OM_ACT_RELU) return OM_ERR_UNSUPPORTED;
+    return bn_forward(pInput, pOutput, pGamma, pBeta, pRunMean, pRunVar, pSavedMean, pSavedInvStd,
+                      nBatch, nChannels, nH, nW, fEps, fMomentum, bTraining,
+                      nAct == OM_ACT_RELU ? 1 : 0);
+}
+
+extern "C" int omCudaBatchNorm2dBackwardAct(const float* pGradOutput, const float* pInput,
+                                            const float* pMean, const float* pInvStd,
+                                            const float* pGamma, const float* pOutput,
+                                            float* pGradInput, float* pGradGamma,
+                                            float* pGradBeta, int nBatch, int nChannels, int nH,
+                                            int nW, float fEps, int nAct) {
+    (void)fEps;
+    if (nAct != OM_ACT_NONE && nAct != OM_ACT_RELU) return OM_ERR_UNSUPPORTED;
+    if (nAct == OM_ACT_RELU && !pOutput) return OM_ERR_INVALID;
+    return bn_backward(pGradOutput, pInput, pMean, pInvStd, pGamma,
+                       nAct == OM_ACT_RELU ? pOutput : nullptr, pGradInput, pGradGamma, pGradBeta,
+                       nBatch, nChannels, nH, nW);
 }
 
 extern "C" int omCudaMaxPool2d(const float* pIn, float* pOut, int* pIndices, int nN, int nC,

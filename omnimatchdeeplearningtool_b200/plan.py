@@ -360,9 +360,15 @@ class Fp32Net:
             self.keep.append(self._grad_buf)
             grad_ptr = self._grad_buf.ptr
         self.grad_flat = grad_ptr
-        for name, shape in net.params:
-            self.param[name] = self._dev(weights[name])
-            self.vel[name] = self._zeros(int(np.prod(shape)) * 4)
+        # parameters and momentum are flat too (views per tensor), so SGD is one launch
+        flat = np.empty(self.n_params, np.float32)
+        for name, (off, n, shape) in self.offsets.items():
+            flat[off:off + n] = np.asarray(weights[name], np.float32).reshape(-1)
+        self.param_flat = self._dev(flat)
+        self.vel_flat = self._zeros(self.grad_bytes)
+        for name, (off, n, shape) in self.offsets.items():
+            self.param[name] = _Ptr(self.param_flat.ptr + off * 4)
+            self.vel[name] = _Ptr(self.vel_flat.ptr + off * 4)
         self.buffers = {name: self._dev(weights[name]) for name, _ in net.buffers}
         self.acts = {}
 
@@ -399,17 +405,16 @@ class Fp32Net:
         z = self._buf(key + ".z", cnt * 4)
         B.conv2d(x.ptr, self.param[cv.name + ".weight"].ptr, None, z.ptr, n, c, hh, ww, cv.cout,
                  cv.k, cv.k, cv.pad, cv.pad, cv.stride, cv.stride)
+        # BN and the ReLU after it in one pass (omCudaBatchNorm2dAct): y is the activated
+        # output, and its sign is the ReLU mask the backward needs
         y = self._buf(key + ".y", cnt * 4)
         mean = self._buf(key + ".mean", cv.cout * 4)
         invstd = self._buf(key + ".invstd", cv.cout * 4)
-        B.batchNorm2d(z.ptr, self.param[cv.bn + ".gamma"].ptr, self.param[cv.bn + ".beta"].ptr,
-                      y.ptr, self.buffers[cv.bn + ".running_mean"].ptr,
-                      self.buffers[cv.bn + ".running_var"].ptr, mean.ptr, invstd.ptr, n, cv.cout,
-                      p * q, 1e-5, 0.1, train)
+        call("omCudaBatchNorm2dAct", z.ptr, y.ptr, self.param[cv.bn + ".gamma"].ptr,
+             self.param[cv.bn + ".beta"].ptr, self.buffers[cv.bn + ".running_mean"].ptr,
+             self.buffers[cv.bn + ".running_var"].ptr, mean.ptr, invstd.ptr, n, cv.cout, p, q,
+             1e-5, 0.1, int(train), _lib.ACT_RELU if relu else _lib.ACT_NONE)
         out = y
-        if relu:
-            out = self._buf(key + ".a", cnt * 4)
-            B.relu(y.ptr, out.ptr, cnt)
         rec = dict(cv=cv, x=x, z=z, y=y, mean=mean, invstd=invstd, relu=relu, n=n, c=c, h=hh,
                    w=ww, p=p, q=q)
         return out, p, q, rec
@@ -526,14 +531,11 @@ class Fp32Net:
     def _conv_bn_backward(self, key, rec, dout, need_dx: bool = True) -> Optional[DeviceBuffer]:
         cv, n = rec["cv"], rec["n"]
         cnt = n * cv.cout * rec["p"] * rec["q"]
-        if rec["relu"]:
-            dr = self._buf(key + ".dr", cnt * 4)
-            B.reluBackward(rec["y"].ptr, dout.ptr, dr.ptr, cnt)
-            dout = dr
         dz = self._buf(key + ".dz", cnt * 4)
-        B.batchNorm2dBackward(dout.ptr, rec["z"].ptr, rec["mean"].ptr, rec["invstd"].ptr,
-                              self.param[cv.bn + ".gamma"].ptr, dz.ptr, self.grad(cv.bn + ".gamma"),
-                              self.grad(cv.bn + ".beta"), n, cv.cout, rec["p"], rec["q"])
+        call("omCudaBatchNorm2dBackwardAct", dout.ptr, rec["z"].ptr, rec["mean"].ptr,
+             rec["invstd"].ptr, self.param[cv.bn + ".gamma"].ptr, rec["y"].ptr, dz.ptr,
+             self.grad(cv.bn + ".gamma"), self.grad(cv.bn + ".beta"), n, cv.cout, rec["p"],
+             rec["q"], 1e-5, _lib.ACT_RELU if rec["relu"] else _lib.ACT_NONE)
         dx = None
         if need_dx:  # the image itself needs no gradient
             dx = self._buf(key + ".dx", n * rec["c"] * rec["h"] * rec["w"] * 4)
@@ -550,10 +552,9 @@ class Fp32Net:
         all-reduce) is applied to the flat gradient first."""
         if grad_scale != 1.0:
             B.mulScalar(self.grad_flat, grad_scale, self.grad_flat, self.n_params)
-        for name, _ in self.net.params:
-            off, cnt, _ = self.offsets[name]
-            B.sgdStep(self.param[name].ptr, self.grad_flat + off * 4, self.vel[name].ptr, cnt, lr,
-                      momentum)
+        # one launch over the flat parameters (elementwise, so the same as one per tensor)
+        B.sgdStep(self.param_flat.ptr, self.grad_flat, self.vel_flat.ptr, self.n_params, lr,
+                  momentum)
 
     def read_grads(self) -> Dict[str, np.ndarray]:
         flat = np.empty(self.n_params, np.float32)
@@ -561,8 +562,10 @@ class Fp32Net:
         return {name: flat[off:off + n].reshape(shape) for name, (off, n, shape) in self.offsets.items()}
 
     def read_param(self, name: str) -> np.ndarray:
-        _, n, shape = self.offsets[name]
-        return self.param[name].to_numpy(shape)
+        off, n, shape = self.offsets[name]
+        out = np.empty(n, np.float32)
+        call("omCudaCopyD2H", out.ctypes.data, self.param_flat.ptr + off * 4, n * 4)
+        return out.reshape(shape)
 
     def close(self) -> None:
         for b in self.keep:

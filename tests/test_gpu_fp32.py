@@ -158,6 +158,44 @@ def test_batchnorm_fwd_bwd(gpu, training, shape):
     assert rel_err_floor(dx.to_numpy(x.shape), wdx) <= TOL
 
 
+@pytest.mark.parametrize("shape", [(8, 24, 16, 16), (4, 16, 9, 7)])
+def test_batchnorm_relu_fused_matches_separate(gpu, shape):
+    """omCudaBatchNorm2dAct / omCudaBatchNorm2dBackwardAct give the bits of omCudaBatchNorm2d +
+    omCudaReLU and omCudaReLUBackward + omCudaBatchNorm2dBackward (4-float and scalar paths)."""
+    from omnimatchdeeplearningtool_b200 import _lib
+    from omnimatchdeeplearningtool_b200._lib import call
+    rng = _rng(21)
+    n, c, h, w = shape
+    x = rng.standard_normal((n, c, h, w)).astype(np.float32)
+    g = rng.uniform(0.5, 1.5, c).astype(np.float32)
+    b = rng.standard_normal(c).astype(np.float32)
+    dy = rng.standard_normal(x.shape).astype(np.float32)
+    outs = []
+    for fused in (False, True):
+        dX, dG, dB = _dev(x), _dev(g), _dev(b)
+        rm, rv = _dev(np.zeros(c, np.float32)), _dev(np.ones(c, np.float32))
+        y, sm, si = _out(x.shape), _out((c,)), _out((c,))
+        dx, dg, db = _out(x.shape), _out((c,)), _out((c,))
+        if fused:
+            call("omCudaBatchNorm2dAct", dX.ptr, y.ptr, dG.ptr, dB.ptr, rm.ptr, rv.ptr, sm.ptr,
+                 si.ptr, n, c, h, w, 1e-5, 0.1, 1, _lib.ACT_RELU)
+            call("omCudaBatchNorm2dBackwardAct", _dev(dy).ptr, dX.ptr, sm.ptr, si.ptr, dG.ptr,
+                 y.ptr, dx.ptr, dg.ptr, db.ptr, n, c, h, w, 1e-5, _lib.ACT_RELU)
+        else:
+            pre = _out(x.shape)
+            call("omCudaBatchNorm2d", dX.ptr, pre.ptr, dG.ptr, dB.ptr, rm.ptr, rv.ptr, sm.ptr,
+                 si.ptr, n, c, h, w, 1e-5, 0.1, 1)
+            call("omCudaReLU", pre.ptr, y.ptr, x.size)
+            dr = _out(x.shape)
+            call("omCudaReLUBackward", pre.ptr, _dev(dy).ptr, dr.ptr, x.size)
+            call("omCudaBatchNorm2dBackward", dr.ptr, dX.ptr, sm.ptr, si.ptr, dG.ptr, dx.ptr,
+                 dg.ptr, db.ptr, n, c, h, w, 1e-5)
+        outs.append([a.to_numpy(s_) for a, s_ in ((y, x.shape), (dx, x.shape), (dg, (c,)),
+                                                   (db, (c,)), (rv, (c,)))])
+    for a, b_ in zip(*outs):
+        assert np.array_equal(a, b_)
+
+
 def test_pooling(gpu):
     import oracle as orc
     from omnimatchdeeplearningtool_b200.backend import CUDABackend as B
