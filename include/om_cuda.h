@@ -1,7 +1,7 @@
 /*
  * om_cuda.h — C ABI of the B200 (sm_100a) compute backend for the OmniMatch engine.
  *
- * Drop-in for the hot-path subset of the reference's src/cuda/cuda_kernels.cuh: every
+ * Drop-in for all 97 entry points of the reference's src/cuda/cuda_kernels.cuh: every
  * function below that carries a "replaces" line has the same name, argument order and
  * argument meaning as the reference entry point it names (cuda_kernels.cu:<line>), so the
  * reference's CUDABackend (src/hal/om.hal.cuda_backend.ixx) links against this library
@@ -103,6 +103,25 @@ int omCudaCopy(const float* pSrc, float* pDst, int nCount);                     
 int omCudaSum(const float* pData, float* pResult, int nCount);                   /* replaces :1473 */
 int omCudaArgmax(const float* pData, int* pOut, int nBatch, int nClasses);       /* replaces :2415 */
 int omCudaTranspose(const float* pIn, float* pOut, int nRows, int nCols);        /* replaces :707 */
+int omCudaSub(const float* pA, const float* pB, float* pC, int nCount);          /* replaces :493 */
+int omCudaMul(const float* pA, const float* pB, float* pC, int nCount);          /* replaces :518 */
+int omCudaDiv(const float* pA, const float* pB, float* pC, int nCount);          /* replaces :3743 */
+int omCudaAddScalar(const float* pA, float fScalar, float* pC, int nCount);      /* replaces :566 */
+/* *pResult (device) = sum / nCount */
+int omCudaMean(const float* pData, float* pResult, int nCount);                  /* replaces :1506 */
+/* activations and their backwards; the Sigmoid / Tanh backwards take the forward output,
+ * the GELU (tanh form) / SiLU / LeakyReLU backwards the forward input */
+int omCudaSigmoid(const float* pIn, float* pOut, int nCount);                    /* replaces :615 */
+int omCudaSigmoidBackward(const float* pGrad, const float* pOutput, float* pOut, int nCount); /* :1978 */
+int omCudaTanh(const float* pIn, float* pOut, int nCount);                       /* replaces :1889 */
+int omCudaTanhBackward(const float* pGrad, const float* pOutput, float* pOut, int nCount); /* :1910 */
+int omCudaGELU(const float* pIn, float* pOut, int nCount);                       /* replaces :635 */
+int omCudaGeluBackward(const float* pGrad, const float* pInput, float* pOut, int nCount); /* :1936 */
+int omCudaSiLU(const float* pIn, float* pOut, int nCount);                       /* replaces :653 */
+int omCudaSiluBackward(const float* pGrad, const float* pInput, float* pOut, int nCount); /* :1957 */
+int omCudaLeakyRelu(const float* pIn, float* pOut, int nCount, float fSlope);    /* replaces :1871 */
+int omCudaLeakyReluBackward(const float* pGrad, const float* pInput, float* pOut, int nCount,
+                            float fSlope);                                       /* replaces :1997 */
 
 /* ---------------- dense contractions (fp32, reference layouts) ---------------- */
 /* C[M,N] = A[M,K] . B[K,N], row-major */
@@ -190,6 +209,96 @@ int omCudaSoftmaxCrossEntropyBackward(const float* pSoftmax, const float* pTarge
 /* v = m*v + g; p -= lr*v (m == 0 or pVelocity == NULL: p -= lr*g) */
 int omCudaSgdStep(float* pParam, const float* pGrad, float* pVelocity, int nCount, float fLr,
                   float fMomentum);                                              /* replaces :2511 */
+/* Adam with bias correction (beta^step from nStep >= 1) */
+int omCudaAdamStep(float* pParam, const float* pGrad, float* pM, float* pV, int nCount,
+                   float fLr, float fBeta1, float fBeta2, float fEps, int nStep); /* :2468 */
+
+/* ---------------- off the hot path: the reference's remaining entry points ----------------
+ * Plain SIMT kernels with the reference's arithmetic, for the engine's segmentation and
+ * transformer models. Reductions run in a fixed order (deterministic); the reference's
+ * host round trips for loss values are replaced by device-side finishing. */
+/* C[b] = A[b][M,K] . B[b][K,N], batches contiguous */
+int omCudaBatchedMatmul(const float* pA, const float* pB, float* pC, int nBatch, int nM, int nK,
+                        int nN);                                                 /* replaces :843 */
+/* same as omCudaConv2d */
+int omCudaConv2dIm2col(const float* pInput, const float* pWeight, const float* pBias,
+                       float* pOutput, int nBatch, int nCin, int nH, int nW, int nCout, int nKH,
+                       int nKW, int nStride, int nPad);                          /* replaces :991 */
+/* weight [Cin, Cout, KH, KW]; output side (in-1)*stride - 2*pad + K; pBias may be NULL */
+int omCudaConvTranspose2d(const float* pInput, const float* pWeight, const float* pBias,
+                          float* pOutput, int nBatch, int nCin, int nHin, int nWin, int nCout,
+                          int nKH, int nKW, int nStride, int nPad);              /* replaces :4187 */
+/* dW and dB (pGradBias may be NULL) of a dilated convolution, overwritten */
+int omCudaDilatedConv2dBackwardWeight(const float* pInput, const float* pGradOutput,
+                                      float* pGradWeight, float* pGradBias, int nBatch,
+                                      int nCin, int nH, int nW, int nCout, int nKH, int nKW,
+                                      int nStride, int nPad, int nDilation);     /* :2911 */
+/* LayerNorm over the last nDim of nBatch rows, saving mean and 1/sqrt(var + eps) per row */
+int omCudaLayerNorm(const float* pInput, float* pOutput, const float* pGamma, const float* pBeta,
+                    float* pSavedMean, float* pSavedInvStd, int nBatch, int nDim,
+                    float fEps);                                                 /* replaces :1829 */
+int omCudaLayerNormBackward(const float* pGradOut, const float* pInput, const float* pMean,
+                            const float* pInvStd, const float* pGamma, float* pGradInput,
+                            float* pGradGamma, float* pGradBeta, int nBatch, int nDim); /* :4096 */
+/* GroupNorm of NCHW with nGroups channel groups; saves per (n, group) mean and invstd */
+int omCudaGroupNorm2d(const float* pInput, float* pOutput, const float* pGamma, const float* pBeta,
+                      float* pSavedMean, float* pSavedInvStd, int nBatch, int nChannels, int nH,
+                      int nW, int nGroups, float fEps);                          /* replaces :3299 */
+int omCudaGroupNorm2dBackward(const float* pGradOutput, const float* pInput, const float* pMean,
+                              const float* pInvStd, const float* pGamma, float* pGradInput,
+                              float* pGradGamma, float* pGradBeta, int nBatch, int nChannels,
+                              int nH, int nW, int nGroups, float fEps);          /* :3458 */
+/* dx = s * (dy - sum(dy * s)) per row */
+int omCudaSoftmaxLastDimBackward(const float* pGradOut, const float* pSoftmax, float* pGradIn,
+                                 int nOuter, int nLastDim);                      /* :4409 */
+/* bilinear resize (half-pixel centres, clamped edges); the backward zeroes pGradIn first */
+int omCudaUpsampleBilinear(const float* pIn, float* pOut, int nBatch, int nChannels, int nH,
+                           int nW, int nOutH, int nOutW);                        /* replaces :3825 */
+int omCudaUpsampleBilinearBackward(const float* pGradOut, float* pGradIn, int nBatch,
+                                   int nChannels, int nInH, int nInW, int nOutH, int nOutW); /* :3639 */
+int omCudaConcatChannels(const float* pA, const float* pB, float* pOut, int nBatch, int nC1,
+                         int nC2, int nHW);                                      /* replaces :3866 */
+int omCudaConcatChannelsBackward(const float* pGradOut, float* pGradA, float* pGradB, int nBatch,
+                                 int nCA, int nCB, int nHW);                     /* :3686 */
+int omCudaConcatLastDim(const float* pA, const float* pB, float* pOut, int nOuter, int nDimA,
+                        int nDimB);                                              /* replaces :4244 */
+int omCudaConcatLastDimBackward(const float* pGradOut, float* pGradA, float* pGradB, int nOuter,
+                                int nDimA, int nDimB);                           /* :4281 */
+/* columns [nStart, nStart + nLen) of each row; the backward writes only those columns */
+int omCudaSliceLastDim(const float* pIn, float* pOut, int nOuter, int nFullDim, int nStart,
+                       int nLen);                                                /* replaces :4315 */
+int omCudaSliceLastDimBackward(const float* pGradOut, float* pGradIn, int nOuter, int nFullDim,
+                               int nStart, int nLen);                            /* :4345 */
+/* [N, S, 3, H, Dh] -> Q (times fScale), K, V as [N, H, S, Dh]; and [N, H, S, Dh] -> [N, S, H*Dh] */
+int omCudaQkvSplitHeads(const float* pQkv, float* pQ, float* pK, float* pV, int nBatch,
+                        int nSeqLen, int nHeads, int nHeadDim, float fScale);    /* :4854 */
+int omCudaMergeHeads(const float* pIn, float* pOut, int nBatch, int nSeqLen, int nHeads,
+                     int nHeadDim);                                              /* replaces :4866 */
+/* *pResult (device) = sum of max(x,0) - x*y + log(1 + exp(-|x|)); grad (sigmoid(x) - y) * fInvN */
+int omCudaBCEWithLogits(const float* pLogits, const float* pTargets, float* pResult,
+                        int nCount);                                             /* replaces :3921 */
+int omCudaBCEWithLogitsBackward(const float* pLogits, const float* pTargets, float* pGradLogits,
+                                int nCount, float fInvN);                        /* :3717 */
+/* soft Dice on sigmoid(logits): pStats = (sum s*t, sum s, sum t), *pLoss = 1 - 2 I/(P+T+1e-6) */
+int omCudaDiceLossForward(const float* pLogits, const float* pTarget, float* pLoss,
+                          float* pSigmoidOut, float* pStats, int nCount);        /* :4541 */
+int omCudaDiceLossBackward(const float* pSigmoidOut, const float* pTarget, const float* pStats,
+                           const float* pGradOutput, float* pGradLogits, int nCount); /* :4575 */
+/* class-weighted focal (gamma 2) cross-entropy per pixel of [B, K, S] logits against class-id
+ * targets; pStats = (weighted loss sum, weight sum), *pLoss = their ratio */
+int omCudaWeightedPixelCEForward(const float* pLogits, const float* pTarget,
+                                 const float* pClassWeights, float* pSoftmax, float* pLoss,
+                                 float* pStats, int nPixels, int nClasses, int nSpatial); /* :4747 */
+int omCudaWeightedPixelCEBackward(const float* pSoftmax, const float* pTarget,
+                                  const float* pClassWeights, const float* pGradOutput,
+                                  const float* pStats, float* pGradLogits, int nPixels,
+                                  int nClasses, int nSpatial);                   /* :4778 */
+/* out = in * mask / (1 - p) when training with p > 0, else a copy */
+int omCudaDropout(const float* pIn, float* pOut, const float* pMask, int nCount, float fProb,
+                  int bTraining);                                                /* replaces :2279 */
+/* mask from the reference's per-index hash of nSeed: 1/keep with probability keep, else 0 */
+int omCudaDropoutForward(const float* pIn, float* pOut, float* pMask, int nCount,
+                         float fKeepProb, unsigned long long nSeed);             /* :2324 */
 
 /* ---------------- new: NHWC bf16/fp16 fused inference path ---------------- */
 /* Elements of the packed K-major weight [Cout, Kpad] that omCudaPackConvWeight writes, where

@@ -186,6 +186,183 @@ public:
         OM_CALL(omCudaSum(pData, pResult, nCount));
     }
 
+    // ---- the wrapper's remaining methods (cuda_backend.ixx:295-984), each forwarding its
+    // arguments unchanged to the C-ABI entry point of the same name
+    static void sub(const float* pA, const float* pB, float* pOut, size_t nCount) {
+        OM_CALL(omCudaSub(pA, pB, pOut, static_cast<int>(nCount)));
+    }
+    static void mul(const float* pA, const float* pB, float* pOut, size_t nCount) {
+        OM_CALL(omCudaMul(pA, pB, pOut, static_cast<int>(nCount)));
+    }
+    static void div(const float* pA, const float* pB, float* pOut, size_t nCount) {
+        OM_CALL(omCudaDiv(pA, pB, pOut, static_cast<int>(nCount)));
+    }
+    static void addScalar(const float* pA, float fScalar, float* pOut, size_t nCount) {
+        OM_CALL(omCudaAddScalar(pA, fScalar, pOut, static_cast<int>(nCount)));
+    }
+    static void batchedMatmul(const float* pA, const float* pB, float* pC, int nBatch, int nM,
+                              int nK, int nN) {
+        OM_CALL(omCudaBatchedMatmul(pA, pB, pC, nBatch, nM, nK, nN));
+    }
+    static void sigmoid(const float* pIn, float* pOut, size_t nCount) {
+        OM_CALL(omCudaSigmoid(pIn, pOut, static_cast<int>(nCount)));
+    }
+    static void sigmoidBackward(const float* pGrad, const float* pOutput, float* pOut,
+                                size_t nCount) {
+        OM_CALL(omCudaSigmoidBackward(pGrad, pOutput, pOut, static_cast<int>(nCount)));
+    }
+    static void gelu(const float* pIn, float* pOut, size_t nCount) {
+        OM_CALL(omCudaGELU(pIn, pOut, static_cast<int>(nCount)));
+    }
+    static void geluBackward(const float* pGrad, const float* pInput, float* pOut, size_t nCount) {
+        OM_CALL(omCudaGeluBackward(pGrad, pInput, pOut, static_cast<int>(nCount)));
+    }
+    static void silu(const float* pIn, float* pOut, size_t nCount) {
+        OM_CALL(omCudaSiLU(pIn, pOut, static_cast<int>(nCount)));
+    }
+    static void siluBackward(const float* pGrad, const float* pInput, float* pOut, size_t nCount) {
+        OM_CALL(omCudaSiluBackward(pGrad, pInput, pOut, static_cast<int>(nCount)));
+    }
+    static void leakyRelu(const float* pIn, float* pOut, size_t nCount, float fSlope = 0.01f) {
+        OM_CALL(omCudaLeakyRelu(pIn, pOut, static_cast<int>(nCount), fSlope));
+    }
+    static void leakyReluBackward(const float* pGrad, const float* pInput, float* pOut,
+                                  size_t nCount, float fSlope = 0.01f) {
+        OM_CALL(omCudaLeakyReluBackward(pGrad, pInput, pOut, static_cast<int>(nCount), fSlope));
+    }
+    static void tanhForward(const float* pIn, float* pOut, size_t nCount) {
+        OM_CALL(omCudaTanh(pIn, pOut, static_cast<int>(nCount)));
+    }
+    static void tanhBackward(const float* pGrad, const float* pOutput, float* pOut, size_t nCount) {
+        OM_CALL(omCudaTanhBackward(pGrad, pOutput, pOut, static_cast<int>(nCount)));
+    }
+    static void dilatedConv2dBackwardWeight(const float* pInput, const float* pGradOutput,
+                                            float* pGradWeight, float* pGradBias, int nBatch,
+                                            int nCin, int nH, int nW, int nCout, int nKH, int nKW,
+                                            int nStride, int nPad, int nDilation) {
+        OM_CALL(omCudaDilatedConv2dBackwardWeight(pInput, pGradOutput, pGradWeight, pGradBias,
+                                                  nBatch, nCin, nH, nW, nCout, nKH, nKW, nStride,
+                                                  nPad, nDilation));
+    }
+    static void groupNorm2d(const float* pInput, float* pOutput, const float* pGamma,
+                            const float* pBeta, float* pSavedMean, float* pSavedInvStd, int nBatch,
+                            int nChannels, int nH, int nW, int nGroups, float fEps) {
+        OM_CALL(omCudaGroupNorm2d(pInput, pOutput, pGamma, pBeta, pSavedMean, pSavedInvStd,
+                                  nBatch, nChannels, nH, nW, nGroups, fEps));
+    }
+    static void groupNorm2dBackward(const float* pGradOutput, const float* pInput,
+                                    const float* pMean, const float* pInvStd, const float* pGamma,
+                                    float* pGradInput, float* pGradGamma, float* pGradBeta,
+                                    int nBatch, int nChannels, int nH, int nW, int nGroups,
+                                    float fEps) {
+        OM_CALL(omCudaGroupNorm2dBackward(pGradOutput, pInput, pMean, pInvStd, pGamma, pGradInput,
+                                          pGradGamma, pGradBeta, nBatch, nChannels, nH, nW,
+                                          nGroups, fEps));
+    }
+    static void layerNorm(const float* pInput, float* pOutput, const float* pGamma,
+                          const float* pBeta, float* pSavedMean, float* pSavedInvStd, int nBatch,
+                          int nDim, float fEps) {
+        OM_CALL(omCudaLayerNorm(pInput, pOutput, pGamma, pBeta, pSavedMean, pSavedInvStd, nBatch,
+                                nDim, fEps));
+    }
+    static void layerNormBackward(const float* pGradOut, const float* pInput, const float* pMean,
+                                  const float* pInvStd, const float* pGamma, float* pGradInput,
+                                  float* pGradGamma, float* pGradBeta, int nBatch, int nDim) {
+        OM_CALL(omCudaLayerNormBackward(pGradOut, pInput, pMean, pInvStd, pGamma, pGradInput,
+                                        pGradGamma, pGradBeta, nBatch, nDim));
+    }
+    static void adamStep(float* pParam, const float* pGrad, float* pM, float* pV, int nCount,
+                         float fLr, float fBeta1, float fBeta2, float fEps, int nStep) {
+        OM_CALL(omCudaAdamStep(pParam, pGrad, pM, pV, nCount, fLr, fBeta1, fBeta2, fEps, nStep));
+    }
+    static void upsampleBilinear(const float* pIn, float* pOut, int nBatch, int nChannels, int nH,
+                                 int nW, int nOutH, int nOutW) {
+        OM_CALL(omCudaUpsampleBilinear(pIn, pOut, nBatch, nChannels, nH, nW, nOutH, nOutW));
+    }
+    static void upsampleBilinearBackward(const float* pGradOut, float* pGradIn, int nBatch,
+                                         int nChannels, int nInH, int nInW, int nOutH,
+                                         int nOutW) {
+        OM_CALL(omCudaUpsampleBilinearBackward(pGradOut, pGradIn, nBatch, nChannels, nInH, nInW,
+                                               nOutH, nOutW));
+    }
+    static void concatChannels(const float* pA, const float* pB, float* pOut, int nBatch, int nC1,
+                               int nC2, int nHW) {
+        OM_CALL(omCudaConcatChannels(pA, pB, pOut, nBatch, nC1, nC2, nHW));
+    }
+    static void concatChannelsBackward(const float* pGradOut, float* pGradA, float* pGradB,
+                                       int nBatch, int nCA, int nCB, int nHW) {
+        OM_CALL(omCudaConcatChannelsBackward(pGradOut, pGradA, pGradB, nBatch, nCA, nCB, nHW));
+    }
+    static void bceWithLogitsForward(const float* pLogits, const float* pTargets, float* pResult,
+                                     int nCount) {
+        OM_CALL(omCudaBCEWithLogits(pLogits, pTargets, pResult, nCount));
+    }
+    static void bceWithLogitsBackward(const float* pLogits, const float* pTargets,
+                                      float* pGradLogits, int nCount, float fInvN) {
+        OM_CALL(omCudaBCEWithLogitsBackward(pLogits, pTargets, pGradLogits, nCount, fInvN));
+    }
+    static void convTranspose2d(const float* pInput, const float* pWeight, const float* pBias,
+                                float* pOutput, int nBatch, int nCin, int nHin, int nWin,
+                                int nCout, int nKH, int nKW, int nStride, int nPad) {
+        OM_CALL(omCudaConvTranspose2d(pInput, pWeight, pBias, pOutput, nBatch, nCin, nHin, nWin,
+                                      nCout, nKH, nKW, nStride, nPad));
+    }
+    static void concatLastDim(const float* pA, const float* pB, float* pOut, int nOuter,
+                              int nDimA, int nDimB) {
+        OM_CALL(omCudaConcatLastDim(pA, pB, pOut, nOuter, nDimA, nDimB));
+    }
+    static void concatLastDimBackward(const float* pGradOut, float* pGradA, float* pGradB,
+                                      int nOuter, int nDimA, int nDimB) {
+        OM_CALL(omCudaConcatLastDimBackward(pGradOut, pGradA, pGradB, nOuter, nDimA, nDimB));
+    }
+    static void sliceLastDim(const float* pIn, float* pOut, int nOuter, int nFullDim, int nStart,
+                             int nLen) {
+        OM_CALL(omCudaSliceLastDim(pIn, pOut, nOuter, nFullDim, nStart, nLen));
+    }
+    static void sliceLastDimBackward(const float* pGradOut, float* pGradIn, int nOuter,
+                                     int nFullDim, int nStart, int nLen) {
+        OM_CALL(omCudaSliceLastDimBackward(pGradOut, pGradIn, nOuter, nFullDim, nStart, nLen));
+    }
+    static void softmaxLastDimBackward(const float* pGradOut, const float* pSoftmax,
+                                       float* pGradIn, int nOuter, int nLastDim) {
+        OM_CALL(omCudaSoftmaxLastDimBackward(pGradOut, pSoftmax, pGradIn, nOuter, nLastDim));
+    }
+    static void dropoutForward(const float* pIn, float* pOut, float* pMask, int nCount,
+                               float fKeepProb, unsigned long long nSeed) {
+        OM_CALL(omCudaDropoutForward(pIn, pOut, pMask, nCount, fKeepProb, nSeed));
+    }
+    static void diceLossForward(const float* pLogits, const float* pTarget, float* pLoss,
+                                float* pSigmoidOut, float* pStats, int nCount) {
+        OM_CALL(omCudaDiceLossForward(pLogits, pTarget, pLoss, pSigmoidOut, pStats, nCount));
+    }
+    static void diceLossBackward(const float* pSigmoidOut, const float* pTarget,
+                                 const float* pStats, const float* pGradOutput,
+                                 float* pGradLogits, int nCount) {
+        OM_CALL(omCudaDiceLossBackward(pSigmoidOut, pTarget, pStats, pGradOutput, pGradLogits,
+                                       nCount));
+    }
+    static void weightedPixelCEForward(const float* pLogits, const float* pTarget,
+                                       const float* pClassWeights, float* pSoftmax, float* pLoss,
+                                       float* pStats, int nPixels, int nClasses, int nSpatial) {
+        OM_CALL(omCudaWeightedPixelCEForward(pLogits, pTarget, pClassWeights, pSoftmax, pLoss,
+                                             pStats, nPixels, nClasses, nSpatial));
+    }
+    static void weightedPixelCEBackward(const float* pSoftmax, const float* pTarget,
+                                        const float* pClassWeights, const float* pGradOutput,
+                                        const float* pStats, float* pGradLogits, int nPixels,
+                                        int nClasses, int nSpatial) {
+        OM_CALL(omCudaWeightedPixelCEBackward(pSoftmax, pTarget, pClassWeights, pGradOutput,
+                                              pStats, pGradLogits, nPixels, nClasses, nSpatial));
+    }
+    static void qkvSplitHeads(const float* pQkv, float* pQ, float* pK, float* pV, int nBatch,
+                              int nSeqLen, int nHeads, int nHeadDim, float fScale) {
+        OM_CALL(omCudaQkvSplitHeads(pQkv, pQ, pK, pV, nBatch, nSeqLen, nHeads, nHeadDim, fScale));
+    }
+    static void mergeHeads(const float* pIn, float* pOut, int nBatch, int nSeqLen, int nHeads,
+                           int nHeadDim) {
+        OM_CALL(omCudaMergeHeads(pIn, pOut, nBatch, nSeqLen, nHeads, nHeadDim));
+    }
+
 private:
     static void symmetric(int kh, int kw, int ph, int pw, int sh, int sw, const char* fn) {
         if (kh != kw || ph != pw || sh != sw) throw CudaBackendError(fn, OM_ERR_UNSUPPORTED);

@@ -95,6 +95,39 @@ _SIGS = {
     "omCudaSoftmax": [P, P, I, I], "omCudaCrossEntropy": [P, P, P, I, I],
     "omCudaSoftmaxCrossEntropyBackward": [P, P, P, I, I],
     "omCudaSgdStep": [P, P, P, I, F, F],
+    "omCudaAdamStep": [P, P, P, P, I, F, F, F, F, I],
+    # further elementwise ops and activations
+    "omCudaSub": [P, P, P, I], "omCudaMul": [P, P, P, I], "omCudaDiv": [P, P, P, I],
+    "omCudaAddScalar": [P, F, P, I], "omCudaMean": [P, P, I],
+    "omCudaSigmoid": [P, P, I], "omCudaSigmoidBackward": [P, P, P, I],
+    "omCudaTanh": [P, P, I], "omCudaTanhBackward": [P, P, P, I],
+    "omCudaGELU": [P, P, I], "omCudaGeluBackward": [P, P, P, I],
+    "omCudaSiLU": [P, P, I], "omCudaSiluBackward": [P, P, P, I],
+    "omCudaLeakyRelu": [P, P, I, F], "omCudaLeakyReluBackward": [P, P, P, I, F],
+    # off the hot path: the remaining reference entry points
+    "omCudaBatchedMatmul": [P, P, P, I, I, I, I],
+    "omCudaConv2dIm2col": [P, P, P, P, I, I, I, I, I, I, I, I, I],
+    "omCudaConvTranspose2d": [P, P, P, P, I, I, I, I, I, I, I, I, I],
+    "omCudaDilatedConv2dBackwardWeight": [P, P, P, P, I, I, I, I, I, I, I, I, I, I],
+    "omCudaLayerNorm": [P, P, P, P, P, P, I, I, F],
+    "omCudaLayerNormBackward": [P, P, P, P, P, P, P, P, I, I],
+    "omCudaGroupNorm2d": [P, P, P, P, P, P, I, I, I, I, I, F],
+    "omCudaGroupNorm2dBackward": [P, P, P, P, P, P, P, P, I, I, I, I, I, F],
+    "omCudaSoftmaxLastDimBackward": [P, P, P, I, I],
+    "omCudaUpsampleBilinear": [P, P, I, I, I, I, I, I],
+    "omCudaUpsampleBilinearBackward": [P, P, I, I, I, I, I, I],
+    "omCudaConcatChannels": [P, P, P, I, I, I, I],
+    "omCudaConcatChannelsBackward": [P, P, P, I, I, I, I],
+    "omCudaConcatLastDim": [P, P, P, I, I, I], "omCudaConcatLastDimBackward": [P, P, P, I, I, I],
+    "omCudaSliceLastDim": [P, P, I, I, I, I], "omCudaSliceLastDimBackward": [P, P, I, I, I, I],
+    "omCudaQkvSplitHeads": [P, P, P, P, I, I, I, I, F],
+    "omCudaMergeHeads": [P, P, I, I, I, I],
+    "omCudaBCEWithLogits": [P, P, P, I], "omCudaBCEWithLogitsBackward": [P, P, P, I, F],
+    "omCudaDiceLossForward": [P, P, P, P, P, I], "omCudaDiceLossBackward": [P, P, P, P, P, I],
+    "omCudaWeightedPixelCEForward": [P, P, P, P, P, P, I, I, I],
+    "omCudaWeightedPixelCEBackward": [P, P, P, P, P, P, I, I, I],
+    "omCudaDropout": [P, P, P, I, F, I],
+    "omCudaDropoutForward": [P, P, P, I, F, c_ulonglong],
     # NHWC fused path
     "omCudaPackConvWeight": [P, P, P, P, P, P, F, P, P, I, I, I, I, I, I],
     "omCudaConv2dBnAct": [P, P, P, P, P, I, I, I, I, I, I, I, I, I, I, I, I],

@@ -227,3 +227,169 @@ class CUDABackend:
     @staticmethod
     def sum(data, result, n):
         call("omCudaSum", data, result, n)
+
+    # ---- the reference wrapper's remaining methods (same names and argument orders; all
+    # forward their arguments unchanged to the C-ABI entry point of the same name)
+    @staticmethod
+    def sub(a, b, out, n):  # :295
+        call("omCudaSub", a, b, out, n)
+
+    @staticmethod
+    def mul(a, b, out, n):  # :302
+        call("omCudaMul", a, b, out, n)
+
+    @staticmethod
+    def addScalar(a, s, out, n):  # :309
+        call("omCudaAddScalar", a, s, out, n)
+
+    @staticmethod
+    def div(a, b, out, n):  # :782
+        call("omCudaDiv", a, b, out, n)
+
+    @staticmethod
+    def batchedMatmul(a, b, c, batch, m, k, n):  # :332
+        call("omCudaBatchedMatmul", a, b, c, batch, m, k, n)
+
+    @staticmethod
+    def sigmoid(inp, out, n):  # :363
+        call("omCudaSigmoid", inp, out, n)
+
+    @staticmethod
+    def sigmoidBackward(grad, output, out, n):  # :370
+        call("omCudaSigmoidBackward", grad, output, out, n)
+
+    @staticmethod
+    def gelu(inp, out, n):  # :377
+        call("omCudaGELU", inp, out, n)
+
+    @staticmethod
+    def geluBackward(grad, inp, out, n):  # :384
+        call("omCudaGeluBackward", grad, inp, out, n)
+
+    @staticmethod
+    def silu(inp, out, n):  # :391
+        call("omCudaSiLU", inp, out, n)
+
+    @staticmethod
+    def siluBackward(grad, inp, out, n):  # :398
+        call("omCudaSiluBackward", grad, inp, out, n)
+
+    @staticmethod
+    def leakyRelu(inp, out, n, slope=0.01):  # :405
+        call("omCudaLeakyRelu", inp, out, n, slope)
+
+    @staticmethod
+    def leakyReluBackward(grad, inp, out, n, slope=0.01):  # :412
+        call("omCudaLeakyReluBackward", grad, inp, out, n, slope)
+
+    @staticmethod
+    def tanhForward(inp, out, n):  # :420
+        call("omCudaTanh", inp, out, n)
+
+    @staticmethod
+    def tanhBackward(grad, output, out, n):  # :427
+        call("omCudaTanhBackward", grad, output, out, n)
+
+    @staticmethod
+    def dilatedConv2dBackwardWeight(x, dy, dw, db, N, Cin, H, W, Cout, KH, KW, stride, pad,
+                                    dil):  # :467
+        call("omCudaDilatedConv2dBackwardWeight", x, dy, dw, db, N, Cin, H, W, Cout, KH, KW,
+             stride, pad, dil)
+
+    @staticmethod
+    def groupNorm2d(inp, out, gamma, beta, mean, invstd, N, C, H, W, groups, eps):  # :607
+        call("omCudaGroupNorm2d", inp, out, gamma, beta, mean, invstd, N, C, H, W, groups, eps)
+
+    @staticmethod
+    def groupNorm2dBackward(dy, x, mean, invstd, gamma, dx, dgamma, dbeta, N, C, H, W, groups,
+                            eps):  # :624
+        call("omCudaGroupNorm2dBackward", dy, x, mean, invstd, gamma, dx, dgamma, dbeta, N, C, H,
+             W, groups, eps)
+
+    @staticmethod
+    def layerNorm(inp, out, gamma, beta, mean, invstd, batch, dim, eps):  # :639
+        call("omCudaLayerNorm", inp, out, gamma, beta, mean, invstd, batch, dim, eps)
+
+    @staticmethod
+    def layerNormBackward(dy, x, mean, invstd, gamma, dx, dgamma, dbeta, batch, dim):  # :833
+        call("omCudaLayerNormBackward", dy, x, mean, invstd, gamma, dx, dgamma, dbeta, batch, dim)
+
+    @staticmethod
+    def adamStep(param, grad, m, v, n, lr, b1, b2, eps, step):  # :670
+        call("omCudaAdamStep", param, grad, m, v, n, lr, b1, b2, eps, step)
+
+    @staticmethod
+    def upsampleBilinear(inp, out, N, C, H, W, OH, OW):  # :796
+        call("omCudaUpsampleBilinear", inp, out, N, C, H, W, OH, OW)
+
+    @staticmethod
+    def upsampleBilinearBackward(dy, dx, N, C, IH, IW, OH, OW):  # :755
+        call("omCudaUpsampleBilinearBackward", dy, dx, N, C, IH, IW, OH, OW)
+
+    @staticmethod
+    def concatChannels(a, b, out, N, C1, C2, HW):  # :804
+        call("omCudaConcatChannels", a, b, out, N, C1, C2, HW)
+
+    @staticmethod
+    def concatChannelsBackward(dy, da, db, N, CA, CB, HW):  # :763
+        call("omCudaConcatChannelsBackward", dy, da, db, N, CA, CB, HW)
+
+    @staticmethod
+    def bceWithLogitsForward(logits, targets, result, n):  # :813
+        call("omCudaBCEWithLogits", logits, targets, result, n)
+
+    @staticmethod
+    def bceWithLogitsBackward(logits, targets, grad, n, inv_n):  # :772
+        call("omCudaBCEWithLogitsBackward", logits, targets, grad, n, inv_n)
+
+    @staticmethod
+    def convTranspose2d(inp, w, b, out, N, Cin, H, W, Cout, KH, KW, stride, pad):  # :846
+        call("omCudaConvTranspose2d", inp, w, b, out, N, Cin, H, W, Cout, KH, KW, stride, pad)
+
+    @staticmethod
+    def concatLastDim(a, b, out, outer, da, db):  # :857
+        call("omCudaConcatLastDim", a, b, out, outer, da, db)
+
+    @staticmethod
+    def concatLastDimBackward(dy, ga, gb, outer, da, db):  # :865
+        call("omCudaConcatLastDimBackward", dy, ga, gb, outer, da, db)
+
+    @staticmethod
+    def sliceLastDim(inp, out, outer, full, start, length):  # :874
+        call("omCudaSliceLastDim", inp, out, outer, full, start, length)
+
+    @staticmethod
+    def sliceLastDimBackward(dy, dx, outer, full, start, length):  # :882
+        call("omCudaSliceLastDimBackward", dy, dx, outer, full, start, length)
+
+    @staticmethod
+    def softmaxLastDimBackward(dy, s, dx, outer, last):  # :894
+        call("omCudaSoftmaxLastDimBackward", dy, s, dx, outer, last)
+
+    @staticmethod
+    def dropoutForward(inp, out, mask, n, keep, seed):  # :905
+        call("omCudaDropoutForward", inp, out, mask, n, keep, seed)
+
+    @staticmethod
+    def diceLossForward(logits, target, loss, sig, stats, n):  # :916
+        call("omCudaDiceLossForward", logits, target, loss, sig, stats, n)
+
+    @staticmethod
+    def diceLossBackward(sig, target, stats, gout, grad, n):  # :927
+        call("omCudaDiceLossBackward", sig, target, stats, gout, grad, n)
+
+    @staticmethod
+    def weightedPixelCEForward(logits, target, cw, soft, loss, stats, P, K, S):  # :938
+        call("omCudaWeightedPixelCEForward", logits, target, cw, soft, loss, stats, P, K, S)
+
+    @staticmethod
+    def weightedPixelCEBackward(soft, target, cw, gout, stats, grad, P, K, S):  # :951
+        call("omCudaWeightedPixelCEBackward", soft, target, cw, gout, stats, grad, P, K, S)
+
+    @staticmethod
+    def qkvSplitHeads(qkv, q, k, v, N, S, H, D, scale):  # :967
+        call("omCudaQkvSplitHeads", qkv, q, k, v, N, S, H, D, scale)
+
+    @staticmethod
+    def mergeHeads(inp, out, N, S, H, D):  # :977
+        call("omCudaMergeHeads", inp, out, N, S, H, D)

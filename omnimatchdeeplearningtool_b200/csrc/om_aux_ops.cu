@@ -1,0 +1,769 @@
+// The rest of the reference's C ABI (src/cuda/cuda_kernels.cuh): ops off the hot path that the
+// engine still links against (losses and norms of its segmentation and transformer models,
+// channel / last-dimension concat and slice, attention head reshapes, bilinear upsampling,
+// transposed and dilated convolutions, Adam, dropout). Each follows the reference's arithmetic
+// (file:line of its definition at each entry point) as plain SIMT kernels; where the reference
+// reduces with atomics in any order, these reduce in a fixed order, and where it copies
+// statistics to the host to finish a loss, the loss is finished on the device.
+#include <cmath>
+
+#include "om_common.cuh"
+
+namespace omb {
+namespace aux {
+
+constexpr int kThreads = 256;
+
+template <class F>
+__global__ void each_kernel(long long n, F f) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+         i += (long long)gridDim.x * blockDim.x)
+        f(i);
+}
+template <class F>
+static int each(DeviceCtx* c, long long n, F f) {
+    if (n <= 0) return OM_OK;
+    each_kernel<<<ew_grid(c, n, kThreads), kThreads, 0, c->compute>>>(n, f);
+    return after_launch(c);
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+    for (int o = 16; o; o >>= 1) v += __shfl_down_sync(0xffffffffu, v, o);
+    return v;
+}
+// block-wide sum (blockDim a multiple of 32, <= 1024), valid in thread 0
+__device__ __forceinline__ float block_sum(float v) {
+    __shared__ float sh[32];
+    v = warp_sum(v);
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = v;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        v = threadIdx.x < (blockDim.x >> 5) ? sh[threadIdx.x] : 0.f;
+        v = warp_sum(v);
+    }
+    return v;
+}
+
+// ---- reductions of a whole array in one block (fixed order)
+template <class F>
+__global__ void sum1_kernel(long long n, float* out, float scale, F f) {
+    float s = 0.f;
+    for (long long i = threadIdx.x; i < n; i += blockDim.x) s += f(i);
+    s = block_sum(s);
+    if (threadIdx.x == 0) *out = s * scale;
+}
+
+// ---- LayerNorm: one block per row (cuda_kernels.cu:1782-1855, backward :3990-4130)
+__global__ void ln_stats_kernel(const float* x, float* mean, float* invstd, int D, float eps) {
+    const float* r = x + (size_t)blockIdx.x * D;
+    __shared__ float m;
+    float s = 0.f;
+    for (int d = threadIdx.x; d < D; d += blockDim.x) s += r[d];
+    s = block_sum(s);
+    if (threadIdx.x == 0) m = s / D;
+    __syncthreads();
+    const float mu = m;
+    float v = 0.f;
+    for (int d = threadIdx.x; d < D; d += blockDim.x) {
+        const float t = r[d] - mu;
+        v += t * t;
+    }
+    v = block_sum(v);
+    if (threadIdx.x == 0) {
+        mean[blockIdx.x] = mu;
+        invstd[blockIdx.x] = rsqrtf(v / D + eps);
+    }
+}
+// one block per row: the means over d of gamma*dy and of gamma*dy*xhat, then that row's dx
+__global__ void ln_bwd_row_kernel(const float* dy, const float* x, const float* mean,
+                                  const float* invstd, const float* gamma, float* dx, int D) {
+    const int b = blockIdx.x;
+    const size_t off = (size_t)b * D;
+    const float mu = mean[b], is = invstd[b];
+    __shared__ float m1, m2;
+    float s1 = 0.f, s2 = 0.f;
+    for (int d = threadIdx.x; d < D; d += blockDim.x) {
+        const float gg = gamma[d] * dy[off + d];
+        s1 += gg;
+        s2 += gg * ((x[off + d] - mu) * is);
+    }
+    s1 = block_sum(s1);
+    __syncthreads();
+    s2 = block_sum(s2);
+    if (threadIdx.x == 0) {
+        m1 = s1 * (1.0f / (float)D);
+        m2 = s2 * (1.0f / (float)D);
+    }
+    __syncthreads();
+    const float mgo = m1, mgx = m2;
+    for (int d = threadIdx.x; d < D; d += blockDim.x) {
+        const float xh = (x[off + d] - mu) * is;
+        dx[off + d] = is * (gamma[d] * dy[off + d] - mgo - xh * mgx);
+    }
+}
+
+// ---- GroupNorm: one block per (sample, group) (cuda_kernels.cu:3180-3300, backward :3330-3460)
+__global__ void gn_stats_kernel(const float* x, float* mean, float* invstd, int C, int HW, int G,
+                                float eps) {
+    const int ng = blockIdx.x, n = ng / G, g = ng - n * G;
+    const int cpg = C / G;
+    const long long size = (long long)cpg * HW;
+    const float* base = x + ((size_t)n * C + (size_t)g * cpg) * HW;
+    float s = 0.f, q = 0.f;
+    for (long long i = threadIdx.x; i < size; i += blockDim.x) {
+        const float v = base[i];
+        s += v;
+        q += v * v;
+    }
+    s = block_sum(s);
+    __syncthreads();
+    q = block_sum(q);
+    if (threadIdx.x == 0) {
+        // E[x^2] - mean^2, as the reference computes it
+        const float mu = s / (float)size;
+        const float var = q / (float)size - mu * mu;
+        mean[ng] = mu;
+        invstd[ng] = 1.0f / sqrtf(var + eps);
+    }
+}
+// per channel over every sample: sum dy * xhat and sum dy
+__global__ void gn_bwd_param_kernel(const float* dy, const float* x, const float* mean,
+                                    const float* invstd, float* dgamma, float* dbeta, int N,
+                                    int C, int HW, int G) {
+    const int c = blockIdx.x, g = c / (C / G);
+    float sg = 0.f, sb = 0.f;
+    for (int n = 0; n < N; ++n) {
+        const float mu = mean[n * G + g], is = invstd[n * G + g];
+        const size_t off = ((size_t)n * C + c) * HW;
+        for (int i = threadIdx.x; i < HW; i += blockDim.x) {
+            const float d = dy[off + i];
+            sg += d * ((x[off + i] - mu) * is);
+            sb += d;
+        }
+    }
+    sg = block_sum(sg);
+    __syncthreads();
+    sb = block_sum(sb);
+    if (threadIdx.x == 0) {
+        dgamma[c] = sg;
+        dbeta[c] = sb;
+    }
+}
+
+// ---- row softmax backward: dx = s * (dy - sum(dy * s)) (cuda_kernels.cu:4375-4420)
+__global__ void softmax_last_bwd_kernel(const float* dy, const float* s, float* dx, int D) {
+    const size_t off = (size_t)blockIdx.x * D;
+    __shared__ float dot;
+    float t = 0.f;
+    for (int j = threadIdx.x; j < D; j += blockDim.x) t += dy[off + j] * s[off + j];
+    t = block_sum(t);
+    if (threadIdx.x == 0) dot = t;
+    __syncthreads();
+    const float d0 = dot;
+    for (int j = threadIdx.x; j < D; j += blockDim.x) dx[off + j] = s[off + j] * (dy[off + j] - d0);
+}
+
+// ---- loss statistics in one block, finished on the device
+__global__ void dice_fwd_kernel(const float* logits, const float* target, float* sig_out,
+                                float* stats, float* loss, long long n) {
+    float si = 0.f, sp = 0.f, st = 0.f;
+    for (long long i = threadIdx.x; i < n; i += blockDim.x) {
+        const float s = 1.0f / (1.0f + expf(-logits[i]));
+        sig_out[i] = s;
+        si += s * target[i];
+        sp += s;
+        st += target[i];
+    }
+    si = block_sum(si);
+    __syncthreads();
+    sp = block_sum(sp);
+    __syncthreads();
+    st = block_sum(st);
+    if (threadIdx.x == 0) {
+        stats[0] = si;
+        stats[1] = sp;
+        stats[2] = st;
+        *loss = 1.0f - 2.0f * si / (sp + st + 1e-6f);
+    }
+}
+__global__ void wpce_fwd_kernel(const float* logits, const float* target, const float* cw,
+                                float* soft, float* stats, float* loss, int P, int K, int S) {
+    float sl = 0.f, sw = 0.f;
+    for (int p = threadIdx.x; p < P; p += blockDim.x) {
+        const int b = p / S, px = p - b * S;
+        const size_t base = (size_t)b * K * S + px;
+        float mx = -1e30f;
+        for (int k = 0; k < K; ++k) mx = fmaxf(mx, logits[base + (size_t)k * S]);
+        float es = 0.f;
+        for (int k = 0; k < K; ++k) {
+            const float e = expf(logits[base + (size_t)k * S] - mx);
+            soft[base + (size_t)k * S] = e;
+            es += e;
+        }
+        const float inv = 1.0f / es;
+        for (int k = 0; k < K; ++k) soft[base + (size_t)k * S] *= inv;
+        const int t = __float2int_rn(target[p]);
+        if (t >= 0 && t < K) {
+            const float w = cw[t], pt = soft[base + (size_t)t * S];
+            const float focal = (1.0f - pt) * (1.0f - pt);
+            sl -= w * focal * logf(pt + 1e-7f);
+            sw += w;
+        }
+    }
+    sl = block_sum(sl);
+    __syncthreads();
+    sw = block_sum(sw);
+    if (threadIdx.x == 0) {
+        stats[0] = sl;
+        stats[1] = sw;
+        *loss = sl / fmaxf(sw, 1e-7f);
+    }
+}
+
+// ---- the reference's dropout hash (cuda_kernels.cu:2300-2320): a uniform in [0, 1) per index
+__device__ __forceinline__ float dropout_uniform(unsigned long long seed, long long i) {
+    unsigned long long s = seed + (unsigned long long)i * 6364136223846793005ULL +
+                           1442695040888963407ULL;
+    s ^= s >> 33;
+    s *= 0xff51afd7ed558ccdULL;
+    s ^= s >> 33;
+    return (float)(s & 0xFFFFFF) / 16777216.0f;
+}
+
+}  // namespace aux
+}  // namespace omb
+
+using namespace omb;
+using namespace omb::aux;
+
+#define AUX_CTX(c) OMB_CTX_OR_FAIL(c)
+
+// cuda_kernels.cu:1506 — the mean of nCount floats into pResult[0]
+extern "C" int omCudaMean(const float* pData, float* pResult, int nCount) {
+    AUX_CTX(c);
+    if (!pData || !pResult || nCount <= 0) return OM_ERR_INVALID;
+    const float inv = 1.0f / static_cast<float>(nCount);
+    sum1_kernel<<<1, 1024, 0, c->compute>>>((long long)nCount, pResult, inv,
+                                            [=] __device__(long long i) { return pData[i]; });
+    return after_launch(c);
+}
+
+// cuda_kernels.cu:843 — C[b] = A[b] [M, K] x B[b] [K, N], row-major, batch-contiguous
+extern "C" int omCudaBatchedMatmul(const float* pA, const float* pB, float* pC, int nBatch,
+                                   int nM, int nK, int nN) {
+    if (!pA || !pB || !pC || nBatch < 0 || nM <= 0 || nK <= 0 || nN <= 0) return OM_ERR_INVALID;
+    for (int b = 0; b < nBatch; ++b) {
+        const int st = omCudaMatmul(pA + (size_t)b * nM * nK, pB + (size_t)b * nK * nN,
+                                    pC + (size_t)b * nM * nN, nM, nK, nN);
+        if (st != OM_OK) return st;
+    }
+    return OM_OK;
+}
+
+// cuda_kernels.cu:3866 / :3686 — concatenation along channels of NCHW tensors, and its backward
+extern "C" int omCudaConcatChannels(const float* pA, const float* pB, float* pOut, int nBatch,
+                                    int nC1, int nC2, int nHW) {
+    AUX_CTX(c);
+    if (!pA || !pB || !pOut) return OM_ERR_INVALID;
+    const int Ct = nC1 + nC2;
+    return each(c, (long long)nBatch * Ct * nHW, [=] __device__(long long i) {
+        const long long hw = i % nHW, t = i / nHW;
+        const int ch = (int)(t % Ct);
+        const long long b = t / Ct;
+        pOut[i] = ch < nC1 ? pA[(b * nC1 + ch) * nHW + hw] : pB[(b * nC2 + (ch - nC1)) * nHW + hw];
+    });
+}
+extern "C" int omCudaConcatChannelsBackward(const float* pGradOut, float* pGradA, float* pGradB,
+                                            int nBatch, int nCA, int nCB, int nHW) {
+    AUX_CTX(c);
+    if (!pGradOut || !pGradA || !pGradB) return OM_ERR_INVALID;
+    const int Ct = nCA + nCB;
+    return each(c, (long long)nBatch * Ct * nHW, [=] __device__(long long i) {
+        const long long hw = i % nHW, t = i / nHW;
+        const int ch = (int)(t % Ct);
+        const long long b = t / Ct;
+        if (ch < nCA) pGradA[(b * nCA + ch) * nHW + hw] = pGradOut[i];
+        else pGradB[(b * nCB + (ch - nCA)) * nHW + hw] = pGradOut[i];
+    });
+}
+// cuda_kernels.cu:4244 / :4281 — concatenation along the last dimension, and its backward
+extern "C" int omCudaConcatLastDim(const float* pA, const float* pB, float* pOut, int nOuter,
+                                   int nDimA, int nDimB) {
+    AUX_CTX(c);
+    if (!pA || !pB || !pOut) return OM_ERR_INVALID;
+    const int D = nDimA + nDimB;
+    return each(c, (long long)nOuter * D, [=] __device__(long long i) {
+        const long long r = i / D;
+        const int col = (int)(i - r * D);
+        pOut[i] = col < nDimA ? pA[r * nDimA + col] : pB[r * nDimB + (col - nDimA)];
+    });
+}
+extern "C" int omCudaConcatLastDimBackward(const float* pGradOut, float* pGradA, float* pGradB,
+                                           int nOuter, int nDimA, int nDimB) {
+    AUX_CTX(c);
+    if (!pGradOut || !pGradA || !pGradB) return OM_ERR_INVALID;
+    const int D = nDimA + nDimB;
+    return each(c, (long long)nOuter * D, [=] __device__(long long i) {
+        const long long r = i / D;
+        const int col = (int)(i - r * D);
+        if (col < nDimA) pGradA[r * nDimA + col] = pGradOut[i];
+        else pGradB[r * nDimB + (col - nDimA)] = pGradOut[i];
+    });
+}
+// cuda_kernels.cu:4315 / :4345 — columns [nStart, nStart + nLen) of each row, and the backward,
+// which writes those columns of pGradIn only (the caller zeroes the rest, as the reference's
+// callers do)
+extern "C" int omCudaSliceLastDim(const float* pIn, float* pOut, int nOuter, int nFullDim,
+                                  int nStart, int nLen) {
+    AUX_CTX(c);
+    if (!pIn || !pOut || nStart < 0 || nLen < 0 || nStart + nLen > nFullDim) return OM_ERR_INVALID;
+    return each(c, (long long)nOuter * nLen, [=] __device__(long long i) {
+        const long long r = i / nLen;
+        pOut[i] = pIn[r * nFullDim + nStart + (i - r * nLen)];
+    });
+}
+extern "C" int omCudaSliceLastDimBackward(const float* pGradOut, float* pGradIn, int nOuter,
+                                          int nFullDim, int nStart, int nLen) {
+    AUX_CTX(c);
+    if (!pGradOut || !pGradIn || nStart < 0 || nLen < 0 || nStart + nLen > nFullDim)
+        return OM_ERR_INVALID;
+    return each(c, (long long)nOuter * nLen, [=] __device__(long long i) {
+        const long long r = i / nLen;
+        pGradIn[r * nFullDim + nStart + (i - r * nLen)] = pGradOut[i];
+    });
+}
+// cuda_kernels.cu:4854 — [N, S, 3, H, Dh] rows into Q (scaled), K, V as [N, H, S, Dh]
+extern "C" int omCudaQkvSplitHeads(const float* pQkv, float* pQ, float* pK, float* pV, int nBatch,
+                                   int nSeqLen, int nHeads, int nHeadDim, float fScale) {
+    AUX_CTX(c);
+    if (!pQkv || !pQ || !pK || !pV) return OM_ERR_INVALID;
+    const int D = nHeads * nHeadDim;
+    return each(c, (long long)nBatch * nSeqLen * D, [=] __device__(long long i) {
+        const int d = (int)(i % nHeadDim);
+        long long t = i / nHeadDim;
+        const int h = (int)(t % nHeads);
+        t /= nHeads;
+        const int s = (int)(t % nSeqLen);
+        const long long n = t / nSeqLen;
+        const long long row = (n * nSeqLen + s) * 3 * D + h * nHeadDim + d;
+        const long long o = ((n * nHeads + h) * nSeqLen + s) * nHeadDim + d;
+        pQ[o] = pQkv[row] * fScale;
+        pK[o] = pQkv[row + D];
+        pV[o] = pQkv[row + 2 * D];
+    });
+}
+// cuda_kernels.cu:4866 — [N, H, S, Dh] back to [N, S, H * Dh]
+extern "C" int omCudaMergeHeads(const float* pIn, float* pOut, int nBatch, int nSeqLen,
+                                int nHeads, int nHeadDim) {
+    AUX_CTX(c);
+    if (!pIn || !pOut) return OM_ERR_INVALID;
+    const int D = nHeads * nHeadDim;
+    return each(c, (long long)nBatch * nSeqLen * D, [=] __device__(long long i) {
+        const int d = (int)(i % nHeadDim);
+        long long t = i / nHeadDim;
+        const int h = (int)(t % nHeads);
+        t /= nHeads;
+        const int s = (int)(t % nSeqLen);
+        const long long n = t / nSeqLen;
+        pOut[(n * nSeqLen + s) * D + h * nHeadDim + d] =
+            pIn[((n * nHeads + h) * nSeqLen + s) * nHeadDim + d];
+    });
+}
+// cuda_kernels.cu:4409 — softmax backward along the last dimension
+extern "C" int omCudaSoftmaxLastDimBackward(const float* pGradOut, const float* pSoftmax,
+                                            float* pGradIn, int nOuter, int nLastDim) {
+    AUX_CTX(c);
+    if (!pGradOut || !pSoftmax || !pGradIn || nOuter < 0 || nLastDim <= 0) return OM_ERR_INVALID;
+    if (nOuter == 0) return OM_OK;
+    softmax_last_bwd_kernel<<<nOuter, kThreads, 0, c->compute>>>(pGradOut, pSoftmax, pGradIn,
+                                                                 nLastDim);
+    return after_launch(c);
+}
+
+// cuda_kernels.cu:1829 — LayerNorm over the last nDim of nBatch rows; saves mean and invstd
+extern "C" int omCudaLayerNorm(const float* pInput, float* pOutput, const float* pGamma,
+                               const float* pBeta, float* pSavedMean, float* pSavedInvStd,
+                               int nBatch, int nDim, float fEps) {
+    AUX_CTX(c);
+    if (!pInput || !pOutput || !pGamma || !pBeta || !pSavedMean || !pSavedInvStd || nBatch <= 0 ||
+        nDim <= 0)
+        return OM_ERR_INVALID;
+    ln_stats_kernel<<<nBatch, kThreads, 0, c->compute>>>(pInput, pSavedMean, pSavedInvStd, nDim,
+                                                         fEps);
+    int st = after_launch(c);
+    if (st != OM_OK) return st;
+    return each(c, (long long)nBatch * nDim, [=] __device__(long long i) {
+        const long long b = i / nDim;
+        const int d = (int)(i - b * nDim);
+        pOutput[i] = pGamma[d] * ((pInput[i] - pSavedMean[b]) * pSavedInvStd[b]) + pBeta[d];
+    });
+}
+// cuda_kernels.cu:4096 — dx = invstd * (gamma*dy - mean_d(gamma*dy) - xhat * mean_d(gamma*dy*xhat)),
+// dgamma = sum_b dy*xhat, dbeta = sum_b dy (both overwritten)
+extern "C" int omCudaLayerNormBackward(const float* pGradOut, const float* pInput,
+                                       const float* pMean, const float* pInvStd,
+                                       const float* pGamma, float* pGradInput, float* pGradGamma,
+                                       float* pGradBeta, int nBatch, int nDim) {
+    AUX_CTX(c);
+    if (!pGradOut || !pInput || !pMean || !pInvStd || !pGamma || !pGradInput || !pGradGamma ||
+        !pGradBeta || nBatch <= 0 || nDim <= 0)
+        return OM_ERR_INVALID;
+    ln_bwd_row_kernel<<<nBatch, kThreads, 0, c->compute>>>(pGradOut, pInput, pMean, pInvStd,
+                                                           pGamma, pGradInput, nDim);
+    const int st = after_launch(c);
+    if (st != OM_OK) return st;
+    return each(c, nDim, [=] __device__(long long d) {
+        float sg = 0.f, sb = 0.f;
+        for (int b = 0; b < nBatch; ++b) {
+            const size_t i = (size_t)b * nDim + d;
+            sg += pGradOut[i] * ((pInput[i] - pMean[b]) * pInvStd[b]);
+            sb += pGradOut[i];
+        }
+        pGradGamma[d] = sg;
+        pGradBeta[d] = sb;
+    });
+}
+
+// cuda_kernels.cu:3299 — GroupNorm of NCHW [N, C, H, W] in nGroups groups of channels
+extern "C" int omCudaGroupNorm2d(const float* pInput, float* pOutput, const float* pGamma,
+                                 const float* pBeta, float* pSavedMean, float* pSavedInvStd,
+                                 int nBatch, int nChannels, int nH, int nW, int nGroups,
+                                 float fEps) {
+    AUX_CTX(c);
+    if (!pInput || !pOutput || !pGamma || !pBeta || !pSavedMean || !pSavedInvStd || nBatch <= 0 ||
+        nChannels <= 0 || nGroups <= 0 || nChannels % nGroups != 0 || nH <= 0 || nW <= 0)
+        return OM_ERR_INVALID;
+    const int HW = nH * nW, G = nGroups, cpg = nChannels / nGroups;
+    gn_stats_kernel<<<nBatch * G, kThreads, 0, c->compute>>>(pInput, pSavedMean, pSavedInvStd,
+                                                             nChannels, HW, G, fEps);
+    int st = after_launch(c);
+    if (st != OM_OK) return st;
+    return each(c, (long long)nBatch * nChannels * HW, [=] __device__(long long i) {
+        const long long t = i / HW;
+        const int ch = (int)(t % nChannels);
+        const long long n = t / nChannels;
+        const long long sidx = n * G + ch / cpg;
+        pOutput[i] = pGamma[ch] * ((pInput[i] - pSavedMean[sidx]) * pSavedInvStd[sidx]) + pBeta[ch];
+    });
+}
+// cuda_kernels.cu:3458 (the same formula as the reference's CPU path, autograd.ixx:784-890):
+// dgamma[c] = sum over samples and pixels of dy*xhat, dbeta[c] = sum of dy, and
+// dx = gamma[c] * invstd * (dy - GB/M - xhat*GG/M), with GB and GG the sums of dbeta and dgamma
+// over the channels of c's group and M = channels per group * H*W. The reference uses these
+// batch totals in each sample's dx; this keeps its results.
+extern "C" int omCudaGroupNorm2dBackward(const float* pGradOutput, const float* pInput,
+                                         const float* pMean, const float* pInvStd,
+                                         const float* pGamma, float* pGradInput,
+                                         float* pGradGamma, float* pGradBeta, int nBatch,
+                                         int nChannels, int nH, int nW, int nGroups, float fEps) {
+    (void)fEps;
+    AUX_CTX(c);
+    if (!pGradOutput || !pInput || !pMean || !pInvStd || !pGamma || !pGradInput || !pGradGamma ||
+        !pGradBeta || nBatch <= 0 || nChannels <= 0 || nGroups <= 0 ||
+        nChannels % nGroups != 0 || nH <= 0 || nW <= 0)
+        return OM_ERR_INVALID;
+    const int HW = nH * nW, G = nGroups, cpg = nChannels / nGroups;
+    gn_bwd_param_kernel<<<nChannels, kThreads, 0, c->compute>>>(
+        pGradOutput, pInput, pMean, pInvStd, pGradGamma, pGradBeta, nBatch, nChannels, HW, G);
+    int st = after_launch(c);
+    if (st != OM_OK) return st;
+    const float invM = 1.0f / static_cast<float>(cpg * HW);
+    return each(c, (long long)nBatch * nChannels * HW, [=] __device__(long long i) {
+        const long long t = i / HW;
+        const int ch = (int)(t % nChannels);
+        const long long n = t / nChannels;
+        const int g = ch / cpg;
+        float gg = 0.f, gb = 0.f;
+        for (int ci = g * cpg; ci < (g + 1) * cpg; ++ci) {
+            gg += pGradGamma[ci];
+            gb += pGradBeta[ci];
+        }
+        const float is = pInvStd[n * G + g];
+        const float xh = (pInput[i] - pMean[n * G + g]) * is;
+        pGradInput[i] = pGamma[ch] * is * (pGradOutput[i] - gb * invM - xh * gg * invM);
+    });
+}
+
+// cuda_kernels.cu:3825 — bilinear resize of NCHW maps, half-pixel centres, edges clamped
+extern "C" int omCudaUpsampleBilinear(const float* pIn, float* pOut, int nBatch, int nChannels,
+                                      int nH, int nW, int nOutH, int nOutW) {
+    AUX_CTX(c);
+    if (!pIn || !pOut || nH <= 0 || nW <= 0 || nOutH <= 0 || nOutW <= 0) return OM_ERR_INVALID;
+    const float sh = (float)nH / (float)nOutH, sw = (float)nW / (float)nOutW;
+    return each(c, (long long)nBatch * nChannels * nOutH * nOutW, [=] __device__(long long i) {
+        const int ow = (int)(i % nOutW);
+        long long t = i / nOutW;
+        const int oh = (int)(t % nOutH);
+        const long long nc = t / nOutH;
+        const float fh = ((float)oh + 0.5f) * sh - 0.5f, fw = ((float)ow + 0.5f) * sw - 0.5f;
+        int h0 = (int)floorf(fh), w0 = (int)floorf(fw);
+        const float lh = fh - (float)h0, lw = fw - (float)w0;
+        int h1 = h0 + 1, w1 = w0 + 1;
+        h0 = max(0, min(h0, nH - 1)); h1 = max(0, min(h1, nH - 1));
+        w0 = max(0, min(w0, nW - 1)); w1 = max(0, min(w1, nW - 1));
+        const float* p = pIn + nc * nH * nW;
+        pOut[i] = (1.0f - lh) * ((1.0f - lw) * p[h0 * nW + w0] + lw * p[h0 * nW + w1]) +
+                  lh * ((1.0f - lw) * p[h1 * nW + w0] + lw * p[h1 * nW + w1]);
+    });
+}
+// cuda_kernels.cu:3639 — its backward into a zeroed pGradIn (atomic adds, as the reference)
+extern "C" int omCudaUpsampleBilinearBackward(const float* pGradOut, float* pGradIn, int nBatch,
+                                              int nChannels, int nInH, int nInW, int nOutH,
+                                              int nOutW) {
+    AUX_CTX(c);
+    if (!pGradOut || !pGradIn || nInH <= 0 || nInW <= 0 || nOutH <= 0 || nOutW <= 0)
+        return OM_ERR_INVALID;
+    OMB_CHECK(cudaMemsetAsync(pGradIn, 0, sizeof(float) * (size_t)nBatch * nChannels * nInH * nInW,
+                              c->compute));
+    const float sh = (float)nInH / (float)nOutH, sw = (float)nInW / (float)nOutW;
+    return each(c, (long long)nBatch * nChannels * nOutH * nOutW, [=] __device__(long long i) {
+        const int ow = (int)(i % nOutW);
+        long long t = i / nOutW;
+        const int oh = (int)(t % nOutH);
+        const long long nc = t / nOutH;
+        const float fh = ((float)oh + 0.5f) * sh - 0.5f, fw = ((float)ow + 0.5f) * sw - 0.5f;
+        int h0 = (int)floorf(fh), w0 = (int)floorf(fw);
+        const float lh = fh - (float)h0, lw = fw - (float)w0;
+        int h1 = h0 + 1, w1 = w0 + 1;
+        h0 = max(0, min(h0, nInH - 1)); h1 = max(0, min(h1, nInH - 1));
+        w0 = max(0, min(w0, nInW - 1)); w1 = max(0, min(w1, nInW - 1));
+        float* p = pGradIn + nc * nInH * nInW;
+        const float g = pGradOut[i];
+        atomicAdd(p + h0 * nInW + w0, g * (1.0f - lh) * (1.0f - lw));
+        atomicAdd(p + h0 * nInW + w1, g * (1.0f - lh) * lw);
+        atomicAdd(p + h1 * nInW + w0, g * lh * (1.0f - lw));
+        atomicAdd(p + h1 * nInW + w1, g * lh * lw);
+    });
+}
+
+// cuda_kernels.cu:4187 (CPU: cpu_backend.ixx:1031) — transposed convolution, weight
+// [Cin, Cout, KH, KW], output (Hin-1)*stride - 2*pad + KH per side; each output element
+// gathers its contributions (the reference scatters with atomic adds)
+extern "C" int omCudaConvTranspose2d(const float* pInput, const float* pWeight, const float* pBias,
+                                     float* pOutput, int nBatch, int nCin, int nHin, int nWin,
+                                     int nCout, int nKH, int nKW, int nStride, int nPad) {
+    AUX_CTX(c);
+    if (!pInput || !pWeight || !pOutput || nStride <= 0 || nPad < 0) return OM_ERR_INVALID;
+    const int Ho = (nHin - 1) * nStride - 2 * nPad + nKH;
+    const int Wo = (nWin - 1) * nStride - 2 * nPad + nKW;
+    if (Ho <= 0 || Wo <= 0) return OM_ERR_INVALID;
+    return each(c, (long long)nBatch * nCout * Ho * Wo, [=] __device__(long long i) {
+        const int ow = (int)(i % Wo);
+        long long t = i / Wo;
+        const int oh = (int)(t % Ho);
+        t /= Ho;
+        const int co = (int)(t % nCout);
+        const long long n = t / nCout;
+        float acc = 0.f;
+        for (int ci = 0; ci < nCin; ++ci) {
+            const float* x = pInput + (n * nCin + ci) * nHin * nWin;
+            const float* w = pWeight + ((size_t)ci * nCout + co) * nKH * nKW;
+            for (int kh = 0; kh < nKH; ++kh) {
+                const int th = oh + nPad - kh;
+                if (th < 0 || th % nStride) continue;
+                const int ih = th / nStride;
+                if (ih >= nHin) continue;
+                for (int kw = 0; kw < nKW; ++kw) {
+                    const int tw = ow + nPad - kw;
+                    if (tw < 0 || tw % nStride) continue;
+                    const int iw = tw / nStride;
+                    if (iw >= nWin) continue;
+                    acc += x[ih * nWin + iw] * w[kh * nKW + kw];
+                }
+            }
+        }
+        pOutput[i] = pBias ? acc + pBias[co] : acc;
+    });
+}
+
+// cuda_kernels.cu:2911 — weight (and bias) gradient of a dilated convolution, overwritten:
+// dW[co, ci, kh, kw] = sum over n, p, q of dY[n, co, p, q] * X[n, ci, p*s - pad + kh*d,
+// q*s - pad + kw*d] (zero outside), dBias[co] = sum of dY[., co, ., .]
+extern "C" int omCudaDilatedConv2dBackwardWeight(const float* pInput, const float* pGradOutput,
+                                                 float* pGradWeight, float* pGradBias, int nBatch,
+                                                 int nCin, int nH, int nW, int nCout, int nKH,
+                                                 int nKW, int nStride, int nPad, int nDilation) {
+    AUX_CTX(c);
+    if (!pInput || !pGradOutput || !pGradWeight || nStride <= 0 || nDilation <= 0 || nPad < 0)
+        return OM_ERR_INVALID;
+    const int ekh = nKH + (nKH - 1) * (nDilation - 1), ekw = nKW + (nKW - 1) * (nDilation - 1);
+    const int P = (nH + 2 * nPad - ekh) / nStride + 1, Q = (nW + 2 * nPad - ekw) / nStride + 1;
+    if (P <= 0 || Q <= 0) return OM_ERR_INVALID;
+    int st = each(c, (long long)nCout * nCin * nKH * nKW, [=] __device__(long long i) {
+        const int kw = (int)(i % nKW);
+        long long t = i / nKW;
+        const int kh = (int)(t % nKH);
+        t /= nKH;
+        const int ci = (int)(t % nCin);
+        const int co = (int)(t / nCin);
+        float acc = 0.f;
+        for (int n = 0; n < nBatch; ++n) {
+            const float* x = pInput + ((size_t)n * nCin + ci) * nH * nW;
+            const float* g = pGradOutput + ((size_t)n * nCout + co) * P * Q;
+            for (int p = 0; p < P; ++p) {
+                const int h = p * nStride - nPad + kh * nDilation;
+                if (h < 0 || h >= nH) continue;
+                for (int q = 0; q < Q; ++q) {
+                    const int w = q * nStride - nPad + kw * nDilation;
+                    if (w >= 0 && w < nW) acc += g[p * Q + q] * x[h * nW + w];
+                }
+            }
+        }
+        pGradWeight[i] = acc;
+    });
+    if (st != OM_OK || !pGradBias) return st;
+    return each(c, nCout, [=] __device__(long long co) {
+        float acc = 0.f;
+        for (int n = 0; n < nBatch; ++n) {
+            const float* g = pGradOutput + ((size_t)n * nCout + co) * P * Q;
+            for (int k = 0; k < P * Q; ++k) acc += g[k];
+        }
+        pGradBias[co] = acc;
+    });
+}
+
+// cuda_kernels.cu:991 — the reference's im2col convolution computes what omCudaConv2d does
+extern "C" int omCudaConv2dIm2col(const float* pInput, const float* pWeight, const float* pBias,
+                                  float* pOutput, int nBatch, int nCin, int nH, int nW, int nCout,
+                                  int nKH, int nKW, int nStride, int nPad) {
+    return omCudaConv2d(pInput, pWeight, pBias, pOutput, nBatch, nCin, nH, nW, nCout, nKH, nKW,
+                        nStride, nPad);
+}
+
+// cuda_kernels.cu:3921 / :3717 — sum over elements of the stable BCE-with-logits loss
+// max(x, 0) - x*y + log(1 + exp(-|x|)) into pResult[0]; gradient (sigmoid(x) - y) * fInvN
+extern "C" int omCudaBCEWithLogits(const float* pLogits, const float* pTargets, float* pResult,
+                                   int nCount) {
+    AUX_CTX(c);
+    if (!pLogits || !pTargets || !pResult || nCount < 0) return OM_ERR_INVALID;
+    sum1_kernel<<<1, 1024, 0, c->compute>>>((long long)nCount, pResult, 1.0f,
+                                            [=] __device__(long long i) {
+                                                const float x = pLogits[i], y = pTargets[i];
+                                                return fmaxf(x, 0.0f) - x * y +
+                                                       logf(1.0f + expf(-fabsf(x)));
+                                            });
+    return after_launch(c);
+}
+extern "C" int omCudaBCEWithLogitsBackward(const float* pLogits, const float* pTargets,
+                                           float* pGradLogits, int nCount, float fInvN) {
+    AUX_CTX(c);
+    if (!pLogits || !pTargets || !pGradLogits || nCount < 0) return OM_ERR_INVALID;
+    return each(c, nCount, [=] __device__(long long i) {
+        pGradLogits[i] = (1.0f / (1.0f + expf(-pLogits[i])) - pTargets[i]) * fInvN;
+    });
+}
+
+// cuda_kernels.cu:4541 / :4575 — soft Dice loss on sigmoid(logits): stats = (sum s*t, sum s,
+// sum t), loss = 1 - 2*stats[0] / (stats[1] + stats[2] + 1e-6); the backward scales by
+// pGradOutput[0]
+extern "C" int omCudaDiceLossForward(const float* pLogits, const float* pTarget, float* pLoss,
+                                     float* pSigmoidOut, float* pStats, int nCount) {
+    AUX_CTX(c);
+    if (!pLogits || !pTarget || !pLoss || !pSigmoidOut || !pStats || nCount < 0)
+        return OM_ERR_INVALID;
+    dice_fwd_kernel<<<1, 1024, 0, c->compute>>>(pLogits, pTarget, pSigmoidOut, pStats, pLoss,
+                                                nCount);
+    return after_launch(c);
+}
+extern "C" int omCudaDiceLossBackward(const float* pSigmoidOut, const float* pTarget,
+                                      const float* pStats, const float* pGradOutput,
+                                      float* pGradLogits, int nCount) {
+    AUX_CTX(c);
+    if (!pSigmoidOut || !pTarget || !pStats || !pGradOutput || !pGradLogits || nCount < 0)
+        return OM_ERR_INVALID;
+    return each(c, nCount, [=] __device__(long long i) {
+        const float D = pStats[1] + pStats[2] + 1e-6f;
+        const float s = pSigmoidOut[i];
+        const float dd = 2.0f * (pTarget[i] * D - pStats[0]) * (1.0f / (D * D));
+        pGradLogits[i] = -pGradOutput[0] * dd * (s * (1.0f - s));
+    });
+}
+
+// cuda_kernels.cu:4747 / :4778 — class-weighted focal cross-entropy per pixel of [B, K, S]
+// logits against class-index targets [B*S]: stats = (sum w*(1-p)^2*(-log(p+1e-7)), sum w) over
+// valid pixels, loss = stats[0] / max(stats[1], 1e-7); softmax kept for the backward
+extern "C" int omCudaWeightedPixelCEForward(const float* pLogits, const float* pTarget,
+                                            const float* pClassWeights, float* pSoftmax,
+                                            float* pLoss, float* pStats, int nPixels,
+                                            int nClasses, int nSpatial) {
+    AUX_CTX(c);
+    if (!pLogits || !pTarget || !pClassWeights || !pSoftmax || !pLoss || !pStats ||
+        nClasses <= 0 || nSpatial <= 0 || nPixels < 0)
+        return OM_ERR_INVALID;
+    wpce_fwd_kernel<<<1, 1024, 0, c->compute>>>(pLogits, pTarget, pClassWeights, pSoftmax, pStats,
+                                                pLoss, nPixels, nClasses, nSpatial);
+    return after_launch(c);
+}
+extern "C" int omCudaWeightedPixelCEBackward(const float* pSoftmax, const float* pTarget,
+                                             const float* pClassWeights, const float* pGradOutput,
+                                             const float* pStats, float* pGradLogits,
+                                             int nPixels, int nClasses, int nSpatial) {
+    AUX_CTX(c);
+    if (!pSoftmax || !pTarget || !pClassWeights || !pGradOutput || !pStats || !pGradLogits ||
+        nClasses <= 0 || nSpatial <= 0 || nPixels < 0)
+        return OM_ERR_INVALID;
+    return each(c, nPixels, [=] __device__(long long p) {
+        const float scale0 = pGradOutput[0] / fmaxf(pStats[1], 1e-7f);
+        const long long b = p / nSpatial, px = p - b * nSpatial;
+        const long long base = b * nClasses * nSpatial + px;
+        const int t = __float2int_rn(pTarget[p]);
+        const bool valid = t >= 0 && t < nClasses;
+        const float w = valid ? pClassWeights[t] : 0.0f;
+        const float pt = valid ? pSoftmax[base + (long long)t * nSpatial] : 1.0f;
+        const float focal = (1.0f - pt) * (1.0f - pt);
+        const float lpt = logf(pt + 1e-7f);
+        for (int k = 0; k < nClasses; ++k) {
+            const float sm = pSoftmax[base + (long long)k * nSpatial];
+            const float gce = focal * (sm - (k == t ? 1.0f : 0.0f));
+            const float gf = (k == t) ? (-2.0f * (1.0f - pt) * lpt * sm) : 0.0f;
+            pGradLogits[base + (long long)k * nSpatial] = (w * scale0) * (gce + gf);
+        }
+    });
+}
+
+// cuda_kernels.cu:2279 — out = in * mask / (1 - p) in training with p > 0, else a copy
+extern "C" int omCudaDropout(const float* pIn, float* pOut, const float* pMask, int nCount,
+                             float fProb, int bTraining) {
+    AUX_CTX(c);
+    if (!pIn || !pOut || nCount < 0) return OM_ERR_INVALID;
+    if (!bTraining || fProb <= 0.0f) {
+        if (pIn != pOut)
+            OMB_CHECK(cudaMemcpyAsync(pOut, pIn, sizeof(float) * (size_t)nCount,
+                                      cudaMemcpyDeviceToDevice, c->compute));
+        return OM_OK;
+    }
+    if (!pMask) return OM_ERR_INVALID;
+    const float scale = 1.0f / (1.0f - fProb);
+    return each(c, nCount, [=] __device__(long long i) { pOut[i] = pIn[i] * pMask[i] * scale; });
+}
+// cuda_kernels.cu:2324 — draws the mask from the reference's per-index hash of nSeed:
+// mask = 1/keep where the uniform is below keep, else 0; out = in * mask
+extern "C" int omCudaDropoutForward(const float* pIn, float* pOut, float* pMask, int nCount,
+                                    float fKeepProb, unsigned long long nSeed) {
+    AUX_CTX(c);
+    if (!pIn || !pOut || !pMask || nCount < 0 || !(fKeepProb > 0.0f)) return OM_ERR_INVALID;
+    return each(c, nCount, [=] __device__(long long i) {
+        const float m = dropout_uniform(nSeed, i) < fKeepProb ? 1.0f / fKeepProb : 0.0f;
+        pMask[i] = m;
+        pOut[i] = pIn[i] * m;
+    });
+}
+
+// cuda_kernels.cu:2468 — Adam with bias correction; beta^step computed on the host as there
+extern "C" int omCudaAdamStep(float* pParam, const float* pGrad, float* pM, float* pV, int nCount,
+                              float fLr, float fBeta1, float fBeta2, float fEps, int nStep) {
+    AUX_CTX(c);
+    if (!pParam || !pGrad || !pM || !pV || nCount < 0 || nStep < 1) return OM_ERR_INVALID;
+    const float b1p = std::pow(fBeta1, static_cast<float>(nStep));
+    const float b2p = std::pow(fBeta2, static_cast<float>(nStep));
+    return each(c, nCount, [=] __device__(long long i) {
+        const float g = pGrad[i];
+        const float m = fBeta1 * pM[i] + (1.0f - fBeta1) * g;
+        const float v = fBeta2 * pV[i] + (1.0f - fBeta2) * g * g;
+        pM[i] = m;
+        pV[i] = v;
+        const float mh = m / (1.0f - b1p), vh = v / (1.0f - b2p);
+        pParam[i] -= fLr * mh / (sqrtf(vh) + fEps);
+    });
+}

@@ -812,6 +812,82 @@ extern "C" int omCudaClip(const float* pIn, float* pOut, int nCount, float fMin,
     });
 }
 
+// ---------------------------------------------------------------- more elementwise ops
+// The reference's remaining elementwise entry points (cuda_kernels.cu:477-660, 1871-2005,
+// 3735), with its formulas; the math functions are CUDA's own expf / tanhf.
+#define OMB_ZIP_ENTRY(NAME, A, B, FN)                                              \
+    extern "C" int NAME {                                                          \
+        OMB_CTX_OR_FAIL(c);                                                        \
+        if (!(A) || !pOut || nCount < 0) return OM_ERR_INVALID;                    \
+        return zip(c, A, B, pOut, nCount, FN);                                     \
+    }
+extern "C" int omCudaSub(const float* pA, const float* pB, float* pC, int nCount) {
+    OMB_CTX_OR_FAIL(c);
+    if (!pA || !pB || !pC || nCount < 0) return OM_ERR_INVALID;
+    return zip(c, pA, pB, pC, nCount, [] __device__(float a, float b) { return a - b; });
+}
+extern "C" int omCudaMul(const float* pA, const float* pB, float* pC, int nCount) {
+    OMB_CTX_OR_FAIL(c);
+    if (!pA || !pB || !pC || nCount < 0) return OM_ERR_INVALID;
+    return zip(c, pA, pB, pC, nCount, [] __device__(float a, float b) { return a * b; });
+}
+extern "C" int omCudaDiv(const float* pA, const float* pB, float* pC, int nCount) {
+    OMB_CTX_OR_FAIL(c);
+    if (!pA || !pB || !pC || nCount < 0) return OM_ERR_INVALID;
+    return zip(c, pA, pB, pC, nCount, [] __device__(float a, float b) { return a / b; });
+}
+extern "C" int omCudaAddScalar(const float* pA, float fScalar, float* pC, int nCount) {
+    OMB_CTX_OR_FAIL(c);
+    if (!pA || !pC || nCount < 0) return OM_ERR_INVALID;
+    return zip(c, pA, nullptr, pC, nCount, [=] __device__(float a, float) { return a + fScalar; });
+}
+// sigmoid(x) = 1 / (1 + exp(-x)); its backward from the output o: g * o * (1 - o)
+OMB_ZIP_ENTRY(omCudaSigmoid(const float* pIn, float* pOut, int nCount), pIn, nullptr,
+              [] __device__(float x, float) { return 1.0f / (1.0f + expf(-x)); })
+OMB_ZIP_ENTRY(omCudaSigmoidBackward(const float* pGrad, const float* pOutput, float* pOut,
+                                    int nCount), pGrad, pOutput,
+              [] __device__(float g, float o) { return g * o * (1.0f - o); })
+OMB_ZIP_ENTRY(omCudaTanh(const float* pIn, float* pOut, int nCount), pIn, nullptr,
+              [] __device__(float x, float) { return tanhf(x); })
+OMB_ZIP_ENTRY(omCudaTanhBackward(const float* pGrad, const float* pOutput, float* pOut,
+                                 int nCount), pGrad, pOutput,
+              [] __device__(float g, float o) { return g * (1.0f - o * o); })
+// GELU, tanh form: 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))
+OMB_ZIP_ENTRY(omCudaGELU(const float* pIn, float* pOut, int nCount), pIn, nullptr,
+              [] __device__(float x, float) {
+                  const float u = 0.7978845608f * (x + 0.044715f * x * x * x);
+                  return 0.5f * x * (1.0f + tanhf(u));
+              })
+OMB_ZIP_ENTRY(omCudaGeluBackward(const float* pGrad, const float* pInput, float* pOut,
+                                 int nCount), pGrad, pInput,
+              [] __device__(float g, float x) {
+                  const float t = tanhf(0.7978845608f * (x + 0.044715f * x * x * x));
+                  const float du = 0.7978845608f * (1.0f + 3.0f * 0.044715f * x * x);
+                  return g * (0.5f * (1.0f + t) + 0.5f * x * (1.0f - t * t) * du);
+              })
+OMB_ZIP_ENTRY(omCudaSiLU(const float* pIn, float* pOut, int nCount), pIn, nullptr,
+              [] __device__(float x, float) { return x * (1.0f / (1.0f + expf(-x))); })
+OMB_ZIP_ENTRY(omCudaSiluBackward(const float* pGrad, const float* pInput, float* pOut,
+                                 int nCount), pGrad, pInput,
+              [] __device__(float g, float x) {
+                  const float s = 1.0f / (1.0f + expf(-x));
+                  return g * s * (1.0f + x * (1.0f - s));
+              })
+extern "C" int omCudaLeakyRelu(const float* pIn, float* pOut, int nCount, float fSlope) {
+    OMB_CTX_OR_FAIL(c);
+    if (!pIn || !pOut || nCount < 0) return OM_ERR_INVALID;
+    return zip(c, pIn, nullptr, pOut, nCount,
+               [=] __device__(float x, float) { return x > 0.0f ? x : fSlope * x; });
+}
+extern "C" int omCudaLeakyReluBackward(const float* pGrad, const float* pInput, float* pOut,
+                                       int nCount, float fSlope) {
+    OMB_CTX_OR_FAIL(c);
+    if (!pGrad || !pInput || !pOut || nCount < 0) return OM_ERR_INVALID;
+    return zip(c, pGrad, pInput, pOut, nCount,
+               [=] __device__(float g, float x) { return x > 0.0f ? g : fSlope * g; });
+}
+#undef OMB_ZIP_ENTRY
+
 extern "C" int omCudaFillValue(float* pData, int nCount, float fValue) {
     OMB_CTX_OR_FAIL(c);
     if (!pData || nCount < 0) return OM_ERR_INVALID;

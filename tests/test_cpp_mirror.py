@@ -16,3 +16,15 @@ def test_cpp_mirror_compiles_links_and_throws(tmp_path):
     r = subprocess.run([str(exe)], capture_output=True, text=True)
     assert r.returncode == 0, r.stdout + r.stderr
     assert "threw -4" in r.stdout
+
+
+def test_python_mirror_has_every_reference_method():
+    """The Python CUDABackend carries the same method names as the C++ mirror's list of the
+    reference wrapper's methods (tests/cpp/backend_mirror.cpp)."""
+    import re
+    from omnimatchdeeplearningtool_b200.backend import CUDABackend
+    src = open(os.path.join(ROOT, "tests", "cpp", "backend_mirror.cpp")).read()
+    names = re.findall(r"OMB_HAS\((\w+)\)", src.split("reference_methods_exist() {")[1])
+    assert len(names) == 71
+    missing = [n for n in names if not callable(getattr(CUDABackend, n, None))]
+    assert not missing, missing
