@@ -209,6 +209,17 @@ int omCudaSoftmaxCrossEntropyBackward(const float* pSoftmax, const float* pTarge
 /* v = m*v + g; p -= lr*v (m == 0 or pVelocity == NULL: p -= lr*g) */
 int omCudaSgdStep(float* pParam, const float* pGrad, float* pVelocity, int nCount, float fLr,
                   float fMomentum);                                              /* replaces :2511 */
+/* new: the training loop's gradient guard (EngineBridge.cpp:1885-1925) on the device, in place of
+ * its per-step host copy of every gradient. pStatus (device, 3 floats) receives the L2 norm (NaN
+ * when an element is not finite), the verdict (1 = step, 0 = skip: a NaN/Inf element) and the
+ * clip coefficient. When the step goes ahead, pGrad is multiplied by fMaxNorm / norm if the norm
+ * exceeds fMaxNorm (fMaxNorm <= 0: no clipping), then by fAccumScale (1 = none); when it is
+ * skipped, pGrad is left unchanged. The reduction order is fixed (deterministic). */
+int omCudaGradNormClip(float* pGrad, int nCount, float fMaxNorm, float fAccumScale, float* pStatus);
+/* new: omCudaSgdStep that does nothing when the guard's verdict pStatus[1] is 0, so a skipped
+ * step needs no host round trip */
+int omCudaSgdStepGuarded(float* pParam, const float* pGrad, float* pVelocity, int nCount,
+                         float fLr, float fMomentum, const float* pStatus);
 /* Adam with bias correction (beta^step from nStep >= 1) */
 int omCudaAdamStep(float* pParam, const float* pGrad, float* pM, float* pV, int nCount,
                    float fLr, float fBeta1, float fBeta2, float fEps, int nStep); /* :2468 */

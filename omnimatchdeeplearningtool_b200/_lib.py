@@ -96,6 +96,7 @@ _SIGS = {
     "omCudaSoftmaxCrossEntropyBackward": [P, P, P, I, I],
     "omCudaSgdStep": [P, P, P, I, F, F],
     "omCudaAdamStep": [P, P, P, P, I, F, F, F, F, I],
+    "omCudaGradNormClip": [P, I, F, F, P], "omCudaSgdStepGuarded": [P, P, P, I, F, F, P],
     # further elementwise ops and activations
     "omCudaSub": [P, P, P, I], "omCudaMul": [P, P, P, I], "omCudaDiv": [P, P, P, I],
     "omCudaAddScalar": [P, F, P, I], "omCudaMean": [P, P, I],

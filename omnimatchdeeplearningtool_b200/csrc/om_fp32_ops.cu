@@ -14,6 +14,8 @@
 // the result is deterministic and large feature maps still fill all SMs.
 #include <mutex>
 
+#include <algorithm>
+
 #include "om_common.cuh"
 
 namespace omb {
@@ -386,8 +388,10 @@ __global__ void ce_softmax_bwd_kernel(const float* __restrict__ p, const float* 
 }
 
 // ---------------------------------------------------------------- optimiser, elementwise
+// status (nullable): the gradient guard's verdict; status[1] == 0 skips the step
 __global__ void sgd_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ v,
-                           long long n, float lr, float mom) {
+                           long long n, float lr, float mom, const float* __restrict__ status) {
+    if (status && status[1] == 0.f) return;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
          i += (long long)gridDim.x * blockDim.x) {
         if (v) {
@@ -771,7 +775,98 @@ extern "C" int omCudaSgdStep(float* pParam, const float* pGrad, float* pVelocity
     if (!pParam || !pGrad || nCount < 0) return OM_ERR_INVALID;
     float* v = fMomentum > 0.f ? pVelocity : nullptr;
     if (fMomentum > 0.f && !pVelocity) return OM_ERR_INVALID;
-    sgd_kernel<<<OMB_EW(nCount)>>>(pParam, pGrad, v, nCount, fLr, fMomentum);
+    sgd_kernel<<<OMB_EW(nCount)>>>(pParam, pGrad, v, nCount, fLr, fMomentum, nullptr);
+    return after_launch(c);
+}
+
+// ---------------------------------------------------------------- gradient guard
+// The training loop's check before each optimiser step (EngineBridge.cpp:1885-1925), on the
+// device instead of through a host copy of every gradient: a non-finite gradient skips the
+// step; otherwise the gradient is scaled by maxNorm / ||g|| when its L2 norm exceeds maxNorm,
+// then by the accumulation scale. One pass reduces (each block's partial, then the last block
+// to finish sums the partials in block order, so the result is deterministic) and one scales.
+namespace gradguard {
+constexpr int kMaxBlocks = 1024;
+__device__ float g_partial[kMaxBlocks];
+__device__ int g_bad[kMaxBlocks];
+__device__ unsigned int g_ticket;  // zero between calls: the last block resets it
+
+__global__ void reduce_kernel(const float* __restrict__ g, long long n, float max_norm,
+                              float* __restrict__ status) {
+    __shared__ float sh[32];
+    __shared__ bool last;
+    float s = 0.f;
+    int bad = 0;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+         i += (long long)gridDim.x * blockDim.x) {
+        const float x = g[i];
+        bad |= !isfinite(x);
+        s += x * x;
+    }
+    bad = __syncthreads_or(bad);
+    for (int o = 16; o; o >>= 1) s += __shfl_down_sync(0xffffffffu, s, o);
+    if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float t = 0.f;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += sh[w];
+        g_partial[blockIdx.x] = t;
+        g_bad[blockIdx.x] = bad;
+        __threadfence();
+        last = atomicAdd(&g_ticket, 1u) == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (last && threadIdx.x == 0) {
+        __threadfence();
+        float t = 0.f;
+        int any_bad = 0;
+        for (int b = 0; b < (int)gridDim.x; ++b) {
+            t += __ldcg(&g_partial[b]);
+            any_bad |= __ldcg(&g_bad[b]);
+        }
+        const float norm = sqrtf(t);
+        status[0] = any_bad ? __int_as_float(0x7fc00000) : norm;
+        status[1] = any_bad ? 0.f : 1.f;
+        status[2] = (!any_bad && max_norm > 0.f && norm > max_norm) ? max_norm / norm : 1.f;
+        g_ticket = 0;
+    }
+}
+
+__global__ void scale_kernel(float* __restrict__ g, long long n, float accum_scale,
+                             const float* __restrict__ status) {
+    if (status[1] == 0.f) return;  // the step is skipped; the gradient stays as it was
+    const float clip = status[2];
+    if (clip == 1.f && accum_scale == 1.f) return;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+         i += (long long)gridDim.x * blockDim.x) {
+        float x = g[i];
+        if (clip != 1.f) x *= clip;
+        if (accum_scale != 1.f) x *= accum_scale;
+        g[i] = x;
+    }
+}
+}  // namespace gradguard
+
+extern "C" int omCudaGradNormClip(float* pGrad, int nCount, float fMaxNorm, float fAccumScale,
+                                  float* pStatus) {
+    OMB_CTX_OR_FAIL(c);
+    if (!pGrad || !pStatus || nCount <= 0) return OM_ERR_INVALID;
+    const int blocks = (int)std::min<long long>(2LL * c->num_sms, gradguard::kMaxBlocks);
+    gradguard::reduce_kernel<<<blocks, 512, 0, c->compute>>>(pGrad, nCount, fMaxNorm, pStatus);
+    int st = after_launch(c);
+    if (st != OM_OK) return st;
+    gradguard::scale_kernel<<<OMB_EW(nCount)>>>(pGrad, nCount, fAccumScale, pStatus);
+    return after_launch(c);
+}
+
+extern "C" int omCudaSgdStepGuarded(float* pParam, const float* pGrad, float* pVelocity,
+                                    int nCount, float fLr, float fMomentum,
+                                    const float* pStatus) {
+    OMB_CTX_OR_FAIL(c);
+    if (!pParam || !pGrad || !pStatus || nCount < 0) return OM_ERR_INVALID;
+    float* v = fMomentum > 0.f ? pVelocity : nullptr;
+    if (fMomentum > 0.f && !pVelocity) return OM_ERR_INVALID;
+    sgd_kernel<<<OMB_EW(nCount)>>>(pParam, pGrad, v, nCount, fLr, fMomentum, pStatus);
     return after_launch(c);
 }
 

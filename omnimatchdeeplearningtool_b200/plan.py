@@ -23,7 +23,7 @@ training step (forward, CE loss, backward, SGD momentum) of the reference engine
 from __future__ import annotations
 
 import ctypes
-from typing import Dict, List, Optional, Sequence
+from typing import Dict, List, Optional, Sequence, Tuple
 
 import numpy as np
 
@@ -345,6 +345,7 @@ class Fp32Net:
                  w: int = 224, grad_ptr: Optional[int] = None):
         self.net, self.batch, self.h, self.w = net, batch, h, w
         self.keep: List[DeviceBuffer] = []
+        self._guard: Optional[DeviceBuffer] = None  # the gradient guard's status (device)
         self.param = {}
         self.vel = {}
         self.offsets = {}
@@ -547,14 +548,34 @@ class Fp32Net:
                                cv.stride, cv.stride)
         return dx
 
-    def step(self, lr: float = 0.01, momentum: float = 0.9, grad_scale: float = 1.0) -> None:
+    def step(self, lr: float = 0.01, momentum: float = 0.9, grad_scale: float = 1.0,
+             max_grad_norm: Optional[float] = None, accum_scale: float = 1.0) -> None:
         """SGD with momentum on every parameter; grad_scale (1/world after a summing
-        all-reduce) is applied to the flat gradient first."""
+        all-reduce) is applied to the flat gradient first.
+
+        With max_grad_norm set, the training loop's gradient guard (EngineBridge.cpp:1885-1925,
+        which uses 5.0) runs first, on the device: a NaN/Inf gradient skips the step, a norm
+        above max_grad_norm scales the gradient down to it, then accum_scale (1/accumulation
+        steps) applies. :meth:`guard_status` reads the verdict back."""
         if grad_scale != 1.0:
             B.mulScalar(self.grad_flat, grad_scale, self.grad_flat, self.n_params)
-        # one launch over the flat parameters (elementwise, so the same as one per tensor)
-        B.sgdStep(self.param_flat.ptr, self.grad_flat, self.vel_flat.ptr, self.n_params, lr,
-                  momentum)
+        if max_grad_norm is None:
+            # one launch over the flat parameters (elementwise, so the same as one per tensor)
+            B.sgdStep(self.param_flat.ptr, self.grad_flat, self.vel_flat.ptr, self.n_params, lr,
+                      momentum)
+            return
+        if self._guard is None:
+            self._guard = DeviceBuffer.zeros(16)
+            self.keep.append(self._guard)
+        call("omCudaGradNormClip", self.grad_flat, self.n_params, max_grad_norm, accum_scale,
+             self._guard.ptr)
+        call("omCudaSgdStepGuarded", self.param_flat.ptr, self.grad_flat, self.vel_flat.ptr,
+             self.n_params, lr, momentum, self._guard.ptr)
+
+    def guard_status(self) -> Tuple[float, bool, float]:
+        """(gradient norm, whether the last guarded step ran, clip coefficient)."""
+        v = self._guard.to_numpy((4,))
+        return float(v[0]), bool(v[1] != 0), float(v[2])
 
     def read_grads(self) -> Dict[str, np.ndarray]:
         flat = np.empty(self.n_params, np.float32)

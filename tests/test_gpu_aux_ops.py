@@ -490,3 +490,53 @@ def test_adam_step(gpu):
     assert rel_err(dv.to_numpy((n,)), v64) < TOL
     assert rel_err(dp.to_numpy((n,)) - p, p64 - p) < 1e-3  # the update itself, within 0.1%
     assert gpu.kernel_error() == 0
+
+
+@pytest.mark.parametrize("n", [5, 100003, 3 * 2 ** 20 + 7])
+def test_gradient_guard_clip_and_skip(gpu, n):
+    """omCudaGradNormClip + omCudaSgdStepGuarded: the training loop's NaN/Inf skip, norm clip
+    to max_norm and accumulation scale (EngineBridge.cpp:1885-1925), on the device."""
+    from omnimatchdeeplearningtool_b200._lib import call
+    rng = _rng(17)
+    g = rng.standard_normal(n).astype(np.float32)
+    g64 = g.astype(np.float64)
+    norm = float(np.sqrt((g64 ** 2).sum()))
+    st = _out((4,))
+    # below the limit: the gradient is untouched, the step goes ahead
+    dg = _dev(g)
+    call("omCudaGradNormClip", dg.ptr, n, norm * 2, 1.0, st.ptr)
+    s = st.to_numpy((4,))
+    assert abs(s[0] - norm) / norm < 1e-5 and s[1] == 1.0 and s[2] == 1.0
+    assert np.array_equal(dg.to_numpy((n,)), g)
+    # above the limit, then the accumulation scale, as two multiplies in that order
+    for _ in range(3):  # repeated calls: the cross-block ticket resets itself
+        dg = _dev(g)
+        call("omCudaGradNormClip", dg.ptr, n, norm / 4, 0.5, st.ptr)
+        s = st.to_numpy((4,))
+        assert s[1] == 1.0 and abs(s[2] - 0.25) < 1e-5
+        want = (g * np.float32(s[2])) * np.float32(0.5)
+        assert np.array_equal(dg.to_numpy((n,)), want)
+    first = s.copy()
+    call("omCudaGradNormClip", _dev(g).ptr, n, norm / 4, 0.5, st.ptr)
+    assert np.array_equal(st.to_numpy((4,)), first)  # deterministic
+    # guarded SGD after a passing guard equals the plain step
+    p = rng.standard_normal(n).astype(np.float32)
+    v = rng.standard_normal(n).astype(np.float32)
+    dp, dv = _dev(p), _dev(v)
+    call("omCudaSgdStepGuarded", dp.ptr, dg.ptr, dv.ptr, n, 0.01, 0.9, st.ptr)
+    dp2, dv2 = _dev(p), _dev(v)
+    call("omCudaSgdStep", dp2.ptr, dg.ptr, dv2.ptr, n, 0.01, 0.9)
+    assert np.array_equal(dp.to_numpy((n,)), dp2.to_numpy((n,)))
+    assert np.array_equal(dv.to_numpy((n,)), dv2.to_numpy((n,)))
+    # a non-finite element: verdict 0, gradient, parameters and velocity all unchanged
+    bad = g.copy()
+    bad[n // 2] = np.nan if n % 2 else np.inf
+    dg = _dev(bad)
+    call("omCudaGradNormClip", dg.ptr, n, 1.0, 0.5, st.ptr)
+    s = st.to_numpy((4,))
+    assert np.isnan(s[0]) and s[1] == 0.0
+    assert np.array_equal(dg.to_numpy((n,)), bad, equal_nan=True)
+    call("omCudaSgdStepGuarded", dp.ptr, dg.ptr, dv.ptr, n, 0.01, 0.9, st.ptr)
+    assert np.array_equal(dp.to_numpy((n,)), dp2.to_numpy((n,)))
+    assert np.array_equal(dv.to_numpy((n,)), dv2.to_numpy((n,)))
+    assert gpu.kernel_error() == 0

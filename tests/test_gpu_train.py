@@ -106,3 +106,29 @@ def test_config1_resnet18_fp32_inference(gpu):
     print(f"config1: logits max rel err {rel_err(got, want):.2e}")
     assert rel_err(got, want) <= 1e-4, rel_err(got, want)
     assert np.array_equal(got.argmax(1), want.argmax(1))
+
+
+def test_guarded_step_clips_like_the_training_loop(gpu):
+    """Fp32Net.step(max_grad_norm=...) after a real backward: the parameters move as if the
+    flat gradient had been scaled by max_norm / ||g|| (the training loop's clip,
+    EngineBridge.cpp:1885-1925), and a limit above the norm leaves the plain step."""
+    from omnimatchdeeplearningtool_b200 import synth
+    from omnimatchdeeplearningtool_b200.backend import DeviceBuffer
+    from omnimatchdeeplearningtool_b200.plan import Fp32Net
+    net = synth.resnet_spec(18, 10)
+    w = synth.make_weights(net)
+    x = synth.normal_input(2, 3, 32, 32, seed=5)
+    y = synth.onehot_labels(2, 10, seed=6)
+    fnet = Fp32Net(net, w, 2, 32, 32)
+    dx, dy, dloss = DeviceBuffer.from_numpy(x), DeviceBuffer.from_numpy(y), DeviceBuffer.zeros(4)
+    fnet.forward_backward(dx.ptr, dy.ptr, dloss.ptr)
+    g = np.concatenate([v.ravel() for v in fnet.read_grads().values()]).astype(np.float64)
+    norm = float(np.sqrt((g ** 2).sum()))
+    w0 = fnet.read_param("fc.weight").astype(np.float64)
+    g_fc = fnet.read_grads()["fc.weight"].astype(np.float64)
+    fnet.step(0.01, 0.0, max_grad_norm=norm / 2)
+    got_norm, ran, clip = fnet.guard_status()
+    assert ran and abs(got_norm - norm) / norm < 1e-5 and abs(clip - 0.5) < 1e-5
+    assert rel_err(fnet.read_param("fc.weight") - w0, -0.01 * 0.5 * g_fc) < 1e-5
+    fnet.close()
+    assert gpu.kernel_error() == 0
