@@ -1,0 +1,153 @@
+"""Multi-device batch classification (omnimatchdeeplearningtool_b200/serving.py), the form of the
+reference's EngineBridge::inferBatch that uses every GPU.
+
+CPU tests replace the per-device plan with a fake that records what it was given, to check the
+dealing of chunks, the zero padding of the ragged end, the order of the results and error
+reporting. classify_logits is checked against a restatement of the reference's per-image loop
+(EngineBridge.cpp:3691-3717). The GPU test compares the classifier's logits with one plan's on
+the same images, on every visible device."""
+import math
+import threading
+
+import numpy as np
+import pytest
+
+from omnimatchdeeplearningtool_b200 import serving
+
+
+class _FakePlan:
+    """Logit row = [device, first pixel of the image, count of calls so far on this plan]."""
+
+    def __init__(self, device, log):
+        self.device, self.log, self.calls = device, log, 0
+
+    def run(self, x):
+        self.log.append((self.device, threading.current_thread().name, x.shape[0],
+                         float(x[-1].sum())))
+        self.calls += 1
+        return np.stack([np.array([self.device, img.flat[0], self.calls], np.float32)
+                         for img in x])
+
+    def close(self):
+        self.log.append((self.device, "closed"))
+
+
+def _classifier(devices, batch, log, init_log=None):
+    def init(d):
+        if init_log is not None:
+            init_log.append((d, threading.current_thread().name))
+    return serving.MultiDeviceClassifier(None, {}, devices, batch, h=2, w=2,
+                                         make_plan=lambda d: _FakePlan(d, log), init_device=init)
+
+
+def test_chunks_are_dealt_round_robin_padded_and_reassembled():
+    log, inits = [], []
+    clf = _classifier([3, 5, 7], 4, log, inits)
+    n = 4 * 7 + 2  # seven full chunks and a ragged one of 2
+    x = np.zeros((n, 3, 2, 2), np.float32)
+    x[:, 0, 0, 0] = np.arange(n) + 1
+    out = clf.infer_logits(x)
+    assert out.shape == (n, 3)
+    assert np.array_equal(out[:, 1], np.arange(n) + 1)  # input order kept
+    chunk_dev = [out[i * 4, 0] for i in range(math.ceil(n / 4))]
+    assert chunk_dev == [3, 5, 7, 3, 5, 7, 3, 5]  # chunk i on device i mod 3
+    runs = [e for e in log if len(e) == 4]
+    assert all(e[2] == 4 for e in runs)  # every call sees a full batch
+    assert any(e[3] == 0.0 for e in runs)  # the padded rows of the last chunk are zeros
+    # each device is initialised and driven by its own thread
+    names = {d: t for d, t in inits}
+    assert sorted(names) == [3, 5, 7] and len(set(names.values())) == 3
+    assert all(names[e[0]] == e[1] for e in runs)
+    clf.close()
+    assert sorted(e[0] for e in log if e[1] == "closed") == [3, 5, 7]
+
+
+def test_arguments_and_failures_are_reported():
+    log = []
+    with pytest.raises(ValueError):
+        _classifier([0, 0], 2, log)
+    with pytest.raises(ValueError):
+        _classifier([], 2, log)
+    clf = _classifier([0], 2, log)
+    with pytest.raises(ValueError):
+        clf.infer_logits(np.zeros((2, 3, 4, 4), np.float32))  # wrong image size
+    clf.close()
+
+    def bad_init(d):
+        raise RuntimeError("no such device")
+    with pytest.raises(RuntimeError, match="setup failed"):
+        serving.MultiDeviceClassifier(None, {}, [0, 1], 2, h=2, w=2,
+                                      make_plan=lambda d: _FakePlan(d, log), init_device=bad_init)
+
+    class Failing(_FakePlan):
+        def run(self, x):
+            raise RuntimeError("kernel failed")
+    clf = serving.MultiDeviceClassifier(None, {}, [0], 2, h=2, w=2,
+                                        make_plan=lambda d: Failing(d, log),
+                                        init_device=lambda d: None)
+    with pytest.raises(RuntimeError, match="chunk 0 failed"):
+        clf.infer_logits(np.zeros((2, 3, 2, 2), np.float32))
+    clf.close()
+
+
+def _reference_result(row, threshold):
+    """The reference's per-image loop, element by element in float32."""
+    m = max(row)
+    probs = [np.float32(math.exp(np.float32(v) - m)) for v in row]
+    s = np.float32(0)
+    for p in probs:
+        s = np.float32(s + p)
+    best, best_p = 0, 0.0
+    out = []
+    for c, p in enumerate(probs):
+        q = np.float32(p / max(s, np.float32(1e-8)))
+        out.append(q)
+        if q > best_p:
+            best, best_p = c, q
+    return (best if best_p >= threshold else -1), best_p, np.array(out, np.float32)
+
+
+def test_classify_logits_follows_the_reference():
+    rng = np.random.Generator(np.random.PCG64(3))
+    z = (rng.standard_normal((50, 7)) * 3).astype(np.float32)
+    z[0] = 0.0  # uniform: confidence 1/7, below the threshold -> class -1
+    res = serving.classify_logits(z, 0.5)
+    for row, r in zip(z, res):
+        cls, conf, probs = _reference_result(row.tolist(), 0.5)
+        assert r.predicted_class == cls
+        assert abs(r.confidence - conf) <= 1e-6
+        assert np.allclose(r.probs, probs, rtol=1e-6, atol=1e-7)
+    assert res[0].predicted_class == -1
+
+
+@pytest.mark.gpu
+def test_multi_device_logits_match_one_plan(gpu):
+    """Every visible device (one thread each) against a single plan on device 0: identical
+    logits for the same images, including a ragged last chunk."""
+    from omnimatchdeeplearningtool_b200 import _lib, synth
+    from omnimatchdeeplearningtool_b200.plan import InferencePlan
+    ndev = _lib.lib.omCudaGetDeviceCount()
+    devices = list(range(min(ndev, 8)))
+    net = synth.resnet_spec(18)
+    w = synth.make_weights(net)
+    b = 8
+    n = b * len(devices) + 3
+    x = synth.imagenet_input(n)
+    clf = serving.MultiDeviceClassifier(net, w, devices, b)
+    try:
+        got = clf.infer_logits(x)
+        results = clf.infer_batch(x)
+    finally:
+        clf.close()
+    plan = InferencePlan(net, w, batch=b)
+    want = []
+    for s in range(0, n, b):
+        part = x[s:s + b]
+        pad = np.zeros((b - part.shape[0],) + part.shape[1:], np.float32)
+        want.append(plan.run(np.concatenate([part, pad]))[:part.shape[0]])
+    plan.close()
+    want = np.concatenate(want)
+    assert np.array_equal(got, want)
+    ref = serving.classify_logits(want)
+    assert [r.predicted_class for r in results] == [r.predicted_class for r in ref]
+    assert gpu.kernel_error() == 0
