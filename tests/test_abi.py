@@ -60,3 +60,43 @@ def test_missing_library_fails_loudly(tmp_path, monkeypatch):
     monkeypatch.setattr(L, "LIB_PATH", str(tmp_path / "nope.so"))
     with pytest.raises(ImportError):
         L._load()
+
+
+# every extern "C" entry point of the reference's src/cuda/cuda_kernels.cuh (97 functions)
+REFERENCE_ENTRY_POINTS = [
+    "omCudaAdamStep", "omCudaAdaptiveAvgPool2d", "omCudaAdaptiveAvgPool2dBackward", "omCudaAdd",
+    "omCudaAddBias", "omCudaAddBiasBackward", "omCudaAddScalar", "omCudaArgmax",
+    "omCudaAsyncCopyD2H", "omCudaAsyncCopyH2D", "omCudaAvgPool2d", "omCudaAvgPool2dBackward",
+    "omCudaBCEWithLogits", "omCudaBCEWithLogitsBackward", "omCudaBatchNorm2d",
+    "omCudaBatchNorm2dBackward", "omCudaBatchedMatmul", "omCudaCleanup", "omCudaClip",
+    "omCudaConcatChannels", "omCudaConcatChannelsBackward", "omCudaConcatLastDim",
+    "omCudaConcatLastDimBackward", "omCudaConv2d", "omCudaConv2dBackwardInput",
+    "omCudaConv2dBackwardWeight", "omCudaConv2dIm2col", "omCudaConvTranspose2d", "omCudaCopy",
+    "omCudaCopyD2D", "omCudaCopyD2H", "omCudaCopyH2D", "omCudaCrossEntropy",
+    "omCudaDiceLossBackward", "omCudaDiceLossForward", "omCudaDilatedConv2d",
+    "omCudaDilatedConv2dBackwardWeight", "omCudaDiv", "omCudaDropout", "omCudaDropoutForward",
+    "omCudaFillOnes", "omCudaFillValue", "omCudaFillZeros", "omCudaFree", "omCudaFreeHost",
+    "omCudaGELU", "omCudaGeluBackward", "omCudaGetComputeCapability", "omCudaGetDeviceCount",
+    "omCudaGetDeviceName", "omCudaGetMemInfo", "omCudaGraphBeginCapture", "omCudaGraphDestroy",
+    "omCudaGraphEndCapture", "omCudaGraphLaunch", "omCudaGroupNorm2d",
+    "omCudaGroupNorm2dBackward", "omCudaInit", "omCudaLayerNorm", "omCudaLayerNormBackward",
+    "omCudaLeakyRelu", "omCudaLeakyReluBackward", "omCudaMalloc", "omCudaMallocHost",
+    "omCudaMatmul", "omCudaMaxPool2d", "omCudaMaxPool2dBackward", "omCudaMean", "omCudaMemset",
+    "omCudaMergeHeads", "omCudaMul", "omCudaMulScalar", "omCudaQkvSplitHeads", "omCudaReLU",
+    "omCudaReLUBackward", "omCudaSgdStep", "omCudaSiLU", "omCudaSigmoid",
+    "omCudaSigmoidBackward", "omCudaSiluBackward", "omCudaSliceLastDim",
+    "omCudaSliceLastDimBackward", "omCudaSoftmax", "omCudaSoftmaxCrossEntropyBackward",
+    "omCudaSoftmaxLastDimBackward", "omCudaSub", "omCudaSum", "omCudaSyncComputeStream",
+    "omCudaSyncTransferStream", "omCudaSynchronize", "omCudaTanh", "omCudaTanhBackward",
+    "omCudaTranspose", "omCudaUpsampleBilinear", "omCudaUpsampleBilinearBackward",
+    "omCudaWeightedPixelCEBackward", "omCudaWeightedPixelCEForward",
+]
+
+
+def test_header_and_library_cover_every_reference_entry_point():
+    from omnimatchdeeplearningtool_b200 import _lib
+    assert len(REFERENCE_ENTRY_POINTS) == 97
+    declared = set(_declared())
+    assert not [n for n in REFERENCE_ENTRY_POINTS if n not in declared]
+    lib = ctypes.CDLL(_lib.LIB_PATH)
+    assert not [n for n in REFERENCE_ENTRY_POINTS if not hasattr(lib, n)]
