@@ -250,6 +250,17 @@ extern "C" int omCudaConv2d(const float* pInput, const float* pWeight, const flo
     return run_gemm(c, op, nCout, nBatch * P * Q, nCin * nKH * nKW, 1);
 }
 
+// [F, KH, KW] filters -> [F, eR, eS] with the taps d apart and zeros between them
+__global__ void dilate_filter_kernel(const float* __restrict__ w, float* __restrict__ wd,
+                                     long long n, int KH, int KW, int d, int eR, int eS) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
+         i += (long long)gridDim.x * blockDim.x) {
+        const long long f = i / (eR * eS);
+        const int rs = (int)(i - f * eR * eS), r = rs / eS, sx = rs - r * eS;
+        wd[i] = (r % d == 0 && sx % d == 0) ? w[f * KH * KW + (r / d) * KW + sx / d] : 0.f;
+    }
+}
+
 extern "C" int omCudaDilatedConv2d(const float* pInput, const float* pWeight, const float* pBias,
                                    float* pOutput, int nBatch, int nCin, int nH, int nW, int nCout,
                                    int nKH, int nKW, int nStride, int nPad, int nDilation,
@@ -261,6 +272,27 @@ extern "C" int omCudaDilatedConv2d(const float* pInput, const float* pWeight, co
     int eR = nKH + (nKH - 1) * (nDilation - 1), eS = nKW + (nKW - 1) * (nDilation - 1);
     int P = (nH + 2 * nPad - eR) / nStride + 1, Q = (nW + 2 * nPad - eS) / nStride + 1;
     if (P <= 0 || Q <= 0) return OM_ERR_INVALID;
+    if (nGroups == 1) {
+        // dense: the tensor-core path of omCudaConv2d. A dilated filter is the eR x eS filter
+        // with zeros between the taps; it goes there too while that is at most 3x the taps
+        // (dilation 2 of a 3x3), and larger dilations stay on the direct kernel below
+        if (nDilation == 1)
+            return omCudaConv2d(pInput, pWeight, pBias, pOutput, nBatch, nCin, nH, nW, nCout,
+                                nKH, nKW, nStride, nPad);
+        if ((long long)eR * eS <= 3LL * nKH * nKW) {
+            const long long kc = (long long)nCout * nCin, n = kc * eR * eS;
+            float* wd = nullptr;
+            OMB_CHECK(cudaMallocAsync(&wd, sizeof(float) * (size_t)n, c->compute));
+            dilate_filter_kernel<<<ew_grid(c, n, 256), 256, 0, c->compute>>>(
+                pWeight, wd, n, nKH, nKW, nDilation, eR, eS);
+            int st = after_launch(c);
+            if (st == OM_OK)
+                st = omCudaConv2d(pInput, wd, pBias, pOutput, nBatch, nCin, nH, nW, nCout, eR, eS,
+                                  nStride, nPad);
+            cudaFreeAsync(wd, c->compute);
+            return st;
+        }
+    }
     long long total = (long long)nBatch * nCout * P * Q;
     grouped_conv_kernel<<<ew_grid(c, total, 256), 256, 0, c->compute>>>(
         pInput, pWeight, pBias, pOutput, nBatch, nCin, nH, nW, nCout, nKH, nKW, nStride, nPad,

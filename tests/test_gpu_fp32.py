@@ -117,6 +117,33 @@ def test_grouped_depthwise_conv(gpu):
     assert rel_err_floor(y.to_numpy(want.shape), want) <= TOL
 
 
+@pytest.mark.parametrize("c,k,h,stride,pad,dil,groups", [
+    (32, 48, 20, 1, 1, 1, 1),   # dense, dilation 1: omCudaConv2d's tensor-core path
+    (32, 40, 21, 1, 2, 2, 1),   # dilation 2: the zero-inserted 5x5 filter on the same path
+    (16, 24, 19, 2, 2, 2, 1),   # dilation 2, stride 2
+    (8, 16, 23, 1, 3, 3, 1),    # dilation 3: the direct kernel
+    (12, 18, 17, 1, 2, 2, 3)])  # grouped and dilated: the direct kernel
+def test_dilated_conv_routes(gpu, c, k, h, stride, pad, dil, groups):
+    """omCudaDilatedConv2d (cuda_kernels.cu:1201) against the oracle's convolution with the
+    filter dilated by zero insertion; bias included."""
+    import oracle as orc
+    from omnimatchdeeplearningtool_b200.backend import CUDABackend as B
+    rng = _rng(70 + dil + groups)
+    n, r = 2, 3
+    x = rng.standard_normal((n, c, h, h), dtype=np.float32)
+    w = rng.standard_normal((k, c // groups, r, r), dtype=np.float32)
+    b = rng.standard_normal(k).astype(np.float32)
+    er = r + (r - 1) * (dil - 1)
+    wd = np.zeros((k, c // groups, er, er), np.float32)
+    wd[:, :, ::dil, ::dil] = w
+    want = orc.conv2d(x, wd, b, stride, pad, groups=groups)
+    y = _out(want.shape)
+    B.dilatedConv2d(_dev(x).ptr, _dev(w).ptr, _dev(b).ptr, y.ptr, n, c, h, h, k, r, r, stride,
+                    pad, dil, groups)
+    assert rel_err_floor(y.to_numpy(want.shape), want) <= TOL
+    assert gpu.kernel_error() == 0
+
+
 # shapes: HW = 63 (scalar planes); HW = 256 (4-float vectors, several blocks per channel);
 # HW = 49 over 64 images (several short planes per pass of a block); HW = 4 (one vector per plane)
 @pytest.mark.parametrize("shape", [(4, 16, 9, 7), (8, 24, 16, 16), (64, 8, 7, 7), (32, 4, 2, 2)])
