@@ -121,7 +121,9 @@ def test_grouped_depthwise_conv(gpu):
     (32, 48, 20, 1, 1, 1, 1),   # dense, dilation 1: omCudaConv2d's tensor-core path
     (32, 40, 21, 1, 2, 2, 1),   # dilation 2: the zero-inserted 5x5 filter on the same path
     (16, 24, 19, 2, 2, 2, 1),   # dilation 2, stride 2
-    (8, 16, 23, 1, 3, 3, 1),    # dilation 3: the direct kernel
+    (8, 16, 23, 1, 3, 3, 1),    # dilation 3: the zero-inserted 7x7 filter
+    (4, 8, 24, 1, 9, 9, 1),     # dilation 9: the zero-inserted 19x19 filter
+    (4, 8, 24, 1, 13, 13, 1),   # dilation 13 (27x27, over 64x the taps): the direct kernel
     (12, 18, 17, 1, 2, 2, 3)])  # grouped and dilated: the direct kernel
 def test_dilated_conv_routes(gpu, c, k, h, stride, pad, dil, groups):
     """omCudaDilatedConv2d (cuda_kernels.cu:1201) against the oracle's convolution with the
