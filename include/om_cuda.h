@@ -65,6 +65,9 @@ int omCudaAsyncCopyD2H(void* pDst, const void* pSrc, size_t nBytes);   /* replac
 int omCudaSyncTransferStream(void);                                    /* replaces :404 */
 int omCudaSyncComputeStream(void);                                     /* replaces :412 */
 int omCudaCleanup(void);                                               /* replaces :420 */
+/* replaces :429 (declared by the engine at EngineBridge.cpp:143, called at :4047): wait for the
+ * device, clear the last error, release cached pool blocks; no cudaDeviceReset */
+int omCudaForceReset(void);
 int omCudaMallocHost(void** ppPtr, size_t nBytes);                     /* replaces :4887 */
 int omCudaFreeHost(void* pPtr);                                        /* replaces :4895 */
 int omCudaGraphBeginCapture(void);                                     /* replaces :4909 */
@@ -214,7 +217,9 @@ int omCudaSgdStep(float* pParam, const float* pGrad, float* pVelocity, int nCoun
  * when an element is not finite), the verdict (1 = step, 0 = skip: a NaN/Inf element) and the
  * clip coefficient. When the step goes ahead, pGrad is multiplied by fMaxNorm / norm if the norm
  * exceeds fMaxNorm (fMaxNorm <= 0: no clipping), then by fAccumScale (1 = none); when it is
- * skipped, pGrad is left unchanged. The reduction order is fixed (deterministic). */
+ * skipped, pGrad is left unchanged. The reduction order is fixed (deterministic). Its partial
+ * sums and last-block ticket live in a per-device array that every call shares: two calls on
+ * one device must not overlap (for example from graphs replayed on different streams). */
 int omCudaGradNormClip(float* pGrad, int nCount, float fMaxNorm, float fAccumScale, float* pStatus);
 /* new: omCudaSgdStep that does nothing when the guard's verdict pStatus[1] is 0, so a skipped
  * step needs no host round trip */
@@ -334,6 +339,11 @@ int omCudaConv2dBnAct(const void* pInput, const void* pPacked, const float* pBia
                       const void* pResidual, void* pOutput, int nBatch, int nH, int nW, int nCs,
                       int nCout, int nKH, int nKW, int nStride, int nPad, int nAct, int nDtype,
                       int nOutDtype);
+/* new: the tile plan omCudaConv2dBnAct picks on the current device for these arguments (no
+ * launch): pPlan[0] = tile width BN (32/64/128/256 output channels), [1] = CTAs per SM,
+ * [2] = 128-row sub-tiles per tile, [3] = epilogue warps. For tests that must cover a variant. */
+int omCudaConvTilePlan(int nBatch, int nH, int nW, int nCs, int nCout, int nKH, int nKW,
+                       int nStride, int nPad, int bResidual, int* pPlan);
 /* new: the image stem (stride 1 or 2, Cin * stride^2 <= 16, Cout % 8 == 0) from the NCHW fp32
  * image: out[n,p,q,k] = act(sum_{c,r,s} x[n,c,p*st-pad+r,q*st-pad+s] * W[k,c,r,s] * scale[k]
  * + bias[k]), NHWC 16-bit output, BN folded as in omCudaPackConvWeight. A first launch writes a

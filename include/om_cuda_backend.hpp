@@ -6,8 +6,9 @@
 // unchanged against this header. Two deliberate differences:
 //   * every call checks the C-ABI status and throws om::CudaBackendError on failure (the
 //     reference discards it, e.g. cuda_backend.ixx:325-329, :438-452);
-//   * conv2d/conv2dBackward* reject asymmetric kernel/pad/stride instead of silently using
-//     the H values for both dimensions as the reference does (cuda_backend.ixx:446-449).
+//   * conv2d/conv2dBackward* reject asymmetric pad or stride instead of silently using the H
+//     values for both dimensions as the reference does (cuda_backend.ixx:446-449); rectangular
+//     filters (KH != KW) pass through, as the C ABI takes both.
 #pragma once
 
 #include <cstddef>
@@ -61,7 +62,7 @@ public:
     static void conv2d(const float* pInput, const float* pWeight, const float* pBias,
                        float* pOutput, int nBatch, int nCin, int nH, int nW, int nCout, int nKH,
                        int nKW, int nPadH, int nPadW, int nStrH, int nStrW) {
-        symmetric(nKH, nKW, nPadH, nPadW, nStrH, nStrW, "conv2d");
+        symmetric(nPadH, nPadW, nStrH, nStrW, "conv2d");
         OM_CALL(omCudaConv2d(pInput, pWeight, pBias, pOutput, nBatch, nCin, nH, nW, nCout, nKH,
                              nKW, nStrH, nPadH));
     }
@@ -76,7 +77,7 @@ public:
                                     float* pGradInput, int nBatch, int nCin, int nH, int nW,
                                     int nCout, int nKH, int nKW, int nPadH, int nPadW, int nStrH,
                                     int nStrW) {
-        symmetric(nKH, nKW, nPadH, nPadW, nStrH, nStrW, "conv2dBackwardInput");
+        symmetric(nPadH, nPadW, nStrH, nStrW, "conv2dBackwardInput");
         OM_CALL(omCudaConv2dBackwardInput(pGradOutput, pWeight, pGradInput, nBatch, nCin, nH, nW,
                                           nCout, nKH, nKW, nStrH, nPadH));
     }
@@ -84,7 +85,7 @@ public:
                                      float* pGradWeight, float* pGradBias, int nBatch, int nCin,
                                      int nH, int nW, int nCout, int nKH, int nKW, int nPadH,
                                      int nPadW, int nStrH, int nStrW) {
-        symmetric(nKH, nKW, nPadH, nPadW, nStrH, nStrW, "conv2dBackwardWeight");
+        symmetric(nPadH, nPadW, nStrH, nStrW, "conv2dBackwardWeight");
         OM_CALL(omCudaConv2dBackwardWeight(pInput, pGradOutput, pGradWeight, pGradBias, nBatch,
                                            nCin, nH, nW, nCout, nKH, nKW, nStrH, nPadH));
     }
@@ -364,8 +365,10 @@ public:
     }
 
 private:
-    static void symmetric(int kh, int kw, int ph, int pw, int sh, int sw, const char* fn) {
-        if (kh != kw || ph != pw || sh != sw) throw CudaBackendError(fn, OM_ERR_UNSUPPORTED);
+    // The C ABI takes one padding and one stride for both dimensions (the reference wrapper
+    // passes the H values, cuda_backend.ixx:447-448); a rectangular filter is fine.
+    static void symmetric(int ph, int pw, int sh, int sw, const char* fn) {
+        if (ph != pw || sh != sw) throw CudaBackendError(fn, OM_ERR_UNSUPPORTED);
     }
 };
 

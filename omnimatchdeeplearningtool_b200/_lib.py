@@ -60,7 +60,7 @@ _SIGS = {
     "omCudaCopyD2D": [P, P, c_size_t], "omCudaMemset": [P, I, c_size_t],
     "omCudaSynchronize": [], "omCudaAsyncCopyH2D": [P, P, c_size_t],
     "omCudaAsyncCopyD2H": [P, P, c_size_t], "omCudaSyncTransferStream": [],
-    "omCudaSyncComputeStream": [], "omCudaCleanup": [],
+    "omCudaSyncComputeStream": [], "omCudaCleanup": [], "omCudaForceReset": [],
     "omCudaTransferH2D": [P, P, c_size_t], "omCudaTransferD2H": [P, P, c_size_t],
     "omCudaComputeWaitTransfer": [], "omCudaTransferWaitCompute": [],
     "omCudaMallocHost": [POINTER(c_void_p), c_size_t], "omCudaFreeHost": [P],
@@ -132,6 +132,7 @@ _SIGS = {
     # NHWC fused path
     "omCudaPackConvWeight": [P, P, P, P, P, P, F, P, P, I, I, I, I, I, I],
     "omCudaConv2dBnAct": [P, P, P, P, P, I, I, I, I, I, I, I, I, I, I, I, I],
+    "omCudaConvTilePlan": [I, I, I, I, I, I, I, I, I, I, POINTER(c_int)],
     "omCudaPackStemWeight": [P, P, P, P, P, P, F, P, P, I, I, I, I, I, I],
     "omCudaStemConvBnAct": [P, P, P, P, P, I, I, I, I, I, I, I, I, I, I, I],
     "omCudaNchwToNhwc": [P, P, I, I, I, I, I, I], "omCudaNhwcToNchw": [P, P, I, I, I, I, I, I],

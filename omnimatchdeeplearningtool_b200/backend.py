@@ -121,8 +121,8 @@ class CUDABackend:
 
     @staticmethod
     def conv2d(inp, w, b, out, N, Cin, H, W, Cout, KH, KW, padH, padW, strH, strW):  # :438
-        if KH != KW or padH != padW or strH != strW:
-            raise OmCudaError("conv2d (asymmetric kernel/pad/stride)", -3)
+        if padH != padW or strH != strW:
+            raise OmCudaError("conv2d (asymmetric pad/stride)", -3)
         call("omCudaConv2d", inp, w, b, out, N, Cin, H, W, Cout, KH, KW, strH, padH)
 
     @staticmethod

@@ -100,6 +100,7 @@ struct Params {
     int N, H, W, Cs;
     int K;
     int R, S, stride, pad;
+    int dil;              // MODE_TF32: filter dilation (tap (r, s) reads offset (r*dil, s*dil))
     int P, Q, M;
     int num_kb;
     int num_m_tiles, num_n_tiles;
@@ -561,10 +562,10 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
                     } else if (MODE == MODE_TF32) {
                         // kk = kb * 32 = (fr * S + fs) * Cs + c0 with Cs % 32 == 0 (fp32)
                         mbar_expect_tx(&full[stage], C::STAGE_BYTES);
-                        tma_load_im2col(a_dst, &tmA, &full[stage], c0, wb, hb, img, (uint16_t)fs,
-                                        (uint16_t)fr);
+                        const uint16_t os = (uint16_t)(fs * p.dil), orr = (uint16_t)(fr * p.dil);
+                        tma_load_im2col(a_dst, &tmA, &full[stage], c0, wb, hb, img, os, orr);
                         tma_load_im2col(a_dst + A_STAGE_BYTES, &tmRes, &full[stage], c0, wb, hb,
-                                        img, (uint16_t)fs, (uint16_t)fr);
+                                        img, os, orr);
                         tma_load_2d(b_dst, &tmB, &full[stage], kb * 32, n0);
                         tma_load_2d(b_dst + C::B_STAGE_BYTES / 2, &tmOut, &full[stage], kb * 32,
                                     n0);
@@ -1300,6 +1301,24 @@ extern "C" int omCudaStoredChannels(int nC) {
     return (nC + 7) / 8 * 8;
 }
 
+extern "C" int omCudaConvTilePlan(int nBatch, int nH, int nW, int nCs, int nCout, int nKH,
+                                  int nKW, int nStride, int nPad, int bResidual, int* pPlan) {
+    OMB_CTX_OR_FAIL(c);
+    using namespace omb::tc;
+    if (!pPlan || nBatch <= 0 || nH <= 0 || nW <= 0 || nCs <= 0 || nCout <= 0 || nKH <= 0 ||
+        nKW <= 0 || nStride <= 0 || nPad < 0)
+        return OM_ERR_INVALID;
+    const int P = (nH + 2 * nPad - nKH) / nStride + 1;
+    const int Q = (nW + 2 * nPad - nKW) / nStride + 1;
+    if (P <= 0 || Q <= 0) return OM_ERR_INVALID;
+    const int mode = (nCs % 64 == 0) ? MODE_SW128 : (nCs == 16 ? MODE_SW32 : MODE_INTERLEAVE);
+    const long long kpad = ((long long)nKH * nKW * nCs + BK - 1) / BK * BK;
+    const long long m_tiles = ((long long)nBatch * P * Q + BM - 1) / BM;
+    choose_tile(nCout, (int)(kpad / BK), m_tiles, c->num_sms, mode != MODE_INTERLEAVE,
+                bResidual != 0, &pPlan[0], &pPlan[1], &pPlan[2], &pPlan[3]);
+    return OM_OK;
+}
+
 extern "C" int omCudaConv2dBnAct(const void* pInput, const void* pPacked, const float* pBias,
                                  const void* pResidual, void* pOutput, int nBatch, int nH, int nW,
                                  int nCs, int nCout, int nKH, int nKW, int nStride, int nPad,
@@ -1336,7 +1355,7 @@ extern "C" int omCudaConv2dBnAct(const void* pInput, const void* pPacked, const 
 
     Params p;
     p.N = nBatch; p.H = nH; p.W = nW; p.Cs = nCs; p.K = nCout;
-    p.R = nKH; p.S = nKW; p.stride = nStride; p.pad = nPad;
+    p.R = nKH; p.S = nKW; p.stride = nStride; p.pad = nPad; p.dil = 1;
     p.P = P; p.Q = Q; p.M = (int)Mll;
     p.num_kb = (int)(kpad / BK);
     p.num_m_tiles = (int)((Mll + BM - 1) / BM);
@@ -1544,7 +1563,7 @@ extern "C" int omCudaStemConvBnAct(const float* pInput, void* pWorkspace, const 
 
     Params p;
     p.N = nBatch; p.H = g.Hs; p.W = g.Ws; p.Cs = 16; p.K = nCout;
-    p.R = g.th; p.S = g.tw; p.stride = 1; p.pad = 0;
+    p.R = g.th; p.S = g.tw; p.stride = 1; p.pad = 0; p.dil = 1;
     p.P = g.P; p.Q = g.Q; p.M = (int)Mll;
     p.num_kb = (int)(kpad / BK);
     p.num_m_tiles = (int)m_tiles;
@@ -1775,14 +1794,15 @@ __global__ void s2d_split_kernel(const float* __restrict__ x, float* __restrict_
 // packed hi/lo filter [Kout, R*S*Cs]: result NCHW fp32 [N, Kout, P, Q] (+bias).
 static int tf32_conv_run(DeviceCtx* c, float* xhi, float* xlo, int N, int Hp, int Wp, int Cs,
                          float* whi, float* wlo, int Kout, int R, int S, const float* bias,
-                         float* out, int stride, int pad) {
-    const int P = (Hp + 2 * pad - R) / stride + 1, Q = (Wp + 2 * pad - S) / stride + 1;
+                         float* out, int stride, int pad, int dil) {
+    const int eR = (R - 1) * dil + 1, eS = (S - 1) * dil + 1;   // dilated filter extent
+    const int P = (Hp + 2 * pad - eR) / stride + 1, Q = (Wp + 2 * pad - eS) / stride + 1;
     const long long Mll = (long long)N * P * Q;
     const long long kpad = (long long)R * S * Cs;
     const size_t xe = (size_t)N * Hp * Wp * Cs;
     Params p;
     p.N = N; p.H = Hp; p.W = Wp; p.Cs = Cs; p.K = Kout;
-    p.R = R; p.S = S; p.stride = stride; p.pad = pad;
+    p.R = R; p.S = S; p.stride = stride; p.pad = pad; p.dil = dil;
     p.P = P; p.Q = Q; p.M = (int)Mll;
     p.num_kb = (int)(kpad / 32);
     const int bn = Kout <= 32 ? 32 : (Kout <= 64 ? 64 : 128);
@@ -1802,7 +1822,7 @@ static int tf32_conv_run(DeviceCtx* c, float* xhi, float* xlo, int N, int Hp, in
     cuuint64_t a_strides[3] = {(cuuint64_t)Cs * 4, (cuuint64_t)Wp * Cs * 4,
                                (cuuint64_t)Hp * Wp * Cs * 4};
     int lo_c[2] = {-pad, -pad};
-    int hi_c[2] = {pad - (S - 1), pad - (R - 1)};
+    int hi_c[2] = {pad - (eS - 1), pad - (eR - 1)};
     cuuint32_t a_estr[4] = {1, (cuuint32_t)stride, (cuuint32_t)stride, 1};
     for (int k = 0; k < 2; ++k) {
         CUtensorMap* m = k ? &ta_lo : &ta_hi;
@@ -1836,6 +1856,7 @@ static int tf32_conv_run(DeviceCtx* c, float* xhi, float* xlo, int N, int Hp, in
     }
 }
 
+// im2col corners are signed 8-bit per spatial dim; R and S are the (dilated) filter extents
 static bool tf32_pad_ok(int R, int S, int pad) {
     return -pad >= -128 && pad - (R - 1) >= -128 && pad - (S - 1) >= -128 &&
            pad - (R - 1) <= 127 && pad - (S - 1) <= 127;
@@ -1846,20 +1867,28 @@ static bool tf32_pad_ok(int R, int S, int pad) {
 // the result written as NCHW fp32 [N, Kout, P, Q]. Scratch comes from the stream-ordered pool.
 int tf32_conv(DeviceCtx* c, const float* src, int N, int Cin, int Hin, int Win, int Hp, int Wp,
               int offh, int offw, int up, const float* w, int Kout, int R, int S, bool flip,
-              int Cw, const float* bias, float* out, int stride, int pad) {
+              int Cw, const float* bias, float* out, int stride, int pad, int dil) {
     const int Cs = (Cin + 31) / 32 * 32;
-    const int P = (Hp + 2 * pad - R) / stride + 1, Q = (Wp + 2 * pad - S) / stride + 1;
+    if (dil < 1 || (long long)(R - 1) * dil + 1 > 256 || (long long)(S - 1) * dil + 1 > 256)
+        return OM_ERR_UNSUPPORTED;
+    const int eR = (R - 1) * dil + 1, eS = (S - 1) * dil + 1;
+    const int P = (Hp + 2 * pad - eR) / stride + 1, Q = (Wp + 2 * pad - eS) / stride + 1;
     if (P <= 0 || Q <= 0) return OM_ERR_INVALID;
     const long long Mll = (long long)N * P * Q;
     const long long kpad = (long long)R * S * Cs;
     if (Mll >= (1LL << 31) || kpad >= (1LL << 31) || N > 65535 ||
-        (long long)Hp * ((Wp + 31) / 32) >= (1LL << 31) || !tf32_pad_ok(R, S, pad))
+        (long long)Hp * ((Wp + 31) / 32) >= (1LL << 31) || !tf32_pad_ok(eR, eS, pad))
         return OM_ERR_UNSUPPORTED;
     if (!load_driver_entry_points()) return OM_ERR_DRIVER;
     const size_t xe = (size_t)N * Hp * Wp * Cs, we = (size_t)Kout * kpad;
     const size_t xb = (xe * 4 + 255) / 256 * 256, wb = (we * 4 + 255) / 256 * 256;
     uint8_t* scratch = nullptr;
-    OMB_CHECK(cudaMallocAsync(&scratch, 2 * xb + 2 * wb, c->compute));
+    cudaError_t ae = cudaMallocAsync(&scratch, 2 * xb + 2 * wb, c->compute);
+    if (ae == cudaErrorMemoryAllocation) {
+        cudaGetLastError();
+        return OM_ERR_OOM;
+    }
+    if (ae != cudaSuccess) return OM_ERR_CUDA;
     float* xhi = reinterpret_cast<float*>(scratch);
     float* xlo = reinterpret_cast<float*>(scratch + xb);
     float* whi = reinterpret_cast<float*>(scratch + 2 * xb);
@@ -1873,7 +1902,8 @@ int tf32_conv(DeviceCtx* c, const float* src, int N, int Cin, int Hin, int Win, 
         st = after_launch(c);
     }
     if (st == OM_OK)
-        st = tf32_conv_run(c, xhi, xlo, N, Hp, Wp, Cs, whi, wlo, Kout, R, S, bias, out, stride, pad);
+        st = tf32_conv_run(c, xhi, xlo, N, Hp, Wp, Cs, whi, wlo, Kout, R, S, bias, out, stride, pad,
+                           dil);
     cudaFreeAsync(scratch, c->compute);
     return st;
 }

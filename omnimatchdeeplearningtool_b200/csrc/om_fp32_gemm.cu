@@ -241,24 +241,14 @@ extern "C" int omCudaConv2d(const float* pInput, const float* pWeight, const flo
     if (!pInput || !pWeight || !pOutput || nStride <= 0) return OM_ERR_INVALID;
     int P = (nH + 2 * nPad - nKH) / nStride + 1, Q = (nW + 2 * nPad - nKW) / nStride + 1;
     if (P <= 0 || Q <= 0) return OM_ERR_INVALID;
-    // tensor cores (3xTF32) first; the SIMT kernel covers what they do not
+    // tensor cores (3xTF32) first; the SIMT kernel, which needs no scratch, covers the shapes
+    // they do not take and the case where their operand copies do not fit in device memory
     int st = omb::tc::tf32_conv(c, pInput, nBatch, nCin, nH, nW, nH, nW, 0, 0, 1, pWeight, nCout,
                                 nKH, nKW, false, nCin, pBias, pOutput, nStride, nPad);
-    if (st != OM_ERR_UNSUPPORTED) return st;
+    if (st != OM_ERR_UNSUPPORTED && st != OM_ERR_OOM) return st;
     ConvFwdOp op{pInput, pWeight, pBias, pOutput, nCin, nH, nW, nKH, nKW, nStride, nPad, P, Q,
                  nCin * nKH * nKW, nCout};
     return run_gemm(c, op, nCout, nBatch * P * Q, nCin * nKH * nKW, 1);
-}
-
-// [F, KH, KW] filters -> [F, eR, eS] with the taps d apart and zeros between them
-__global__ void dilate_filter_kernel(const float* __restrict__ w, float* __restrict__ wd,
-                                     long long n, int KH, int KW, int d, int eR, int eS) {
-    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
-         i += (long long)gridDim.x * blockDim.x) {
-        const long long f = i / (eR * eS);
-        const int rs = (int)(i - f * eR * eS), r = rs / eS, sx = rs - r * eS;
-        wd[i] = (r % d == 0 && sx % d == 0) ? w[f * KH * KW + (r / d) * KW + sx / d] : 0.f;
-    }
 }
 
 extern "C" int omCudaDilatedConv2d(const float* pInput, const float* pWeight, const float* pBias,
@@ -273,27 +263,14 @@ extern "C" int omCudaDilatedConv2d(const float* pInput, const float* pWeight, co
     int P = (nH + 2 * nPad - eR) / nStride + 1, Q = (nW + 2 * nPad - eS) / nStride + 1;
     if (P <= 0 || Q <= 0) return OM_ERR_INVALID;
     if (nGroups == 1) {
-        // dense: the tensor-core path of omCudaConv2d. A dilated filter is the eR x eS filter
-        // with zeros between the taps; it goes there too while that is at most 64x the taps
-        // (dilation 11 of a 3x3). Measured for 128 -> 128 channels at 56x56 on a B200, the
-        // direct kernel below takes ~95x the time of the dense 3x3 on that path, and the
-        // dilation-3 filter (5.4x the taps) ~3.7x.
-        if (nDilation == 1)
-            return omCudaConv2d(pInput, pWeight, pBias, pOutput, nBatch, nCin, nH, nW, nCout,
-                                nKH, nKW, nStride, nPad);
-        if ((long long)eR * eS <= 64LL * nKH * nKW) {
-            const long long kc = (long long)nCout * nCin, n = kc * eR * eS;
-            float* wd = nullptr;
-            OMB_CHECK(cudaMallocAsync(&wd, sizeof(float) * (size_t)n, c->compute));
-            dilate_filter_kernel<<<ew_grid(c, n, 256), 256, 0, c->compute>>>(
-                pWeight, wd, n, nKH, nKW, nDilation, eR, eS);
-            int st = after_launch(c);
-            if (st == OM_OK)
-                st = omCudaConv2d(pInput, wd, pBias, pOutput, nBatch, nCin, nH, nW, nCout, eR, eS,
-                                  nStride, nPad);
-            cudaFreeAsync(wd, c->compute);
-            return st;
-        }
+        // dense: the 3xTF32 tensor-core conv walks the dilated taps directly (tap (r, s) reads
+        // input offset (r*d, s*d)), so no zero-inserted filter and no extra arithmetic. Shapes
+        // that path does not take, or whose operand copies do not fit in device memory, run on
+        // the direct kernel below, which needs no scratch.
+        int st = omb::tc::tf32_conv(c, pInput, nBatch, nCin, nH, nW, nH, nW, 0, 0, 1, pWeight,
+                                    nCout, nKH, nKW, false, nCin, pBias, pOutput, nStride, nPad,
+                                    nDilation);
+        if (st != OM_ERR_UNSUPPORTED && st != OM_ERR_OOM) return st;
     }
     long long total = (long long)nBatch * nCout * P * Q;
     grouped_conv_kernel<<<ew_grid(c, total, 256), 256, 0, c->compute>>>(
@@ -315,7 +292,7 @@ extern "C" int omCudaConv2dBackwardInput(const float* pGradOutput, const float* 
         int st = omb::tc::tf32_conv(c, pGradOutput, nBatch, nCout, P, Q, nH + nKH - 1, nW + nKW - 1,
                                     nKH - 1 - nPad, nKW - 1 - nPad, nStride, pWeight, nCin, nKH,
                                     nKW, true, nCin, nullptr, pGradInput, 1, 0);
-        if (st != OM_ERR_UNSUPPORTED) return st;
+        if (st != OM_ERR_UNSUPPORTED && st != OM_ERR_OOM) return st;
     }
     ConvDgradOp op{pGradOutput, pWeight, pGradInput, nCin, nH, nW, nCout, nKH, nKW, nStride, nPad, P, Q};
     return run_gemm(c, op, nCin, nBatch * nH * nW, nCout * nKH * nKW, 1);

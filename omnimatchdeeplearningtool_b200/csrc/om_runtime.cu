@@ -218,6 +218,21 @@ int omCudaCleanup(void) {
     return omb::status_of(cudaMemPoolTrimTo(pool, 0));
 }
 
+// Recovery after an engine-level failure (the reference's cuda_kernels.cu:429-437, called by
+// EngineBridge.cpp:4047): wait for all work on the device, clear a sticky-free last error and
+// release the cached pool blocks. Like the reference it does not call cudaDeviceReset, so device
+// pointers that tensors still hold stay valid. The context's streams are kept (the reference
+// destroys and lazily re-creates its global streams; here every entry point uses them).
+int omCudaForceReset(void) {
+    OMB_CTX_OR_FAIL(c);
+    cudaError_t e = cudaDeviceSynchronize();
+    cudaGetLastError();
+    if (e != cudaSuccess) return OM_ERR_CUDA;
+    cudaMemPool_t pool;
+    OMB_CHECK(cudaDeviceGetDefaultMemPool(&pool, c->device));
+    return omb::status_of(cudaMemPoolTrimTo(pool, 0));
+}
+
 int omCudaMallocHost(void** ppPtr, size_t nBytes) {
     return omb::status_of(cudaMallocHost(ppPtr, nBytes));
 }

@@ -68,8 +68,10 @@ def _reference(x, w, bn, res, stride, pad, act):
     return y
 
 
-@pytest.mark.parametrize("case", CASES, ids=[f"c{i}" for i in range(len(CASES))])
-def test_conv_bn_act(gpu, case):
+def _check_case(gpu, case, images=None):
+    """Run one case through omCudaConv2dBnAct and check it against the oracle. With `images`,
+    the kernel runs on the whole batch and the oracle only on those images (the CPU cost of a
+    full batch-256 oracle would be minutes); the comparison covers every output of them."""
     from omnimatchdeeplearningtool_b200 import _lib
     from omnimatchdeeplearningtool_b200.backend import DeviceBuffer
     from omnimatchdeeplearningtool_b200._lib import call, lib
@@ -92,6 +94,7 @@ def test_conv_bn_act(gpu, case):
     dx32 = DeviceBuffer.from_numpy(x)
     dx = DeviceBuffer(n * h * h * cs * 2)
     call("omCudaNchwToNhwc", dx32.ptr, dx.ptr, n, c, h, h, cs, dtype)
+    dx32.free()
     dw = DeviceBuffer.from_numpy(w)
     bufs = [DeviceBuffer.from_numpy(a) for a in (gamma, beta, mean, var)]
     packed = DeviceBuffer(int(lib.omCudaPackedConvWeightElems(k, ks, ks, cs)) * 2)
@@ -100,12 +103,13 @@ def test_conv_bn_act(gpu, case):
          k, c, ks, ks, cs, dtype)
     dres = None
     if use_res:
-        r32 = DeviceBuffer.from_numpy(res)
         if out_f32:
             dres = DeviceBuffer.from_numpy(np.ascontiguousarray(res.transpose(0, 2, 3, 1)))
         else:
+            r32 = DeviceBuffer.from_numpy(res)
             dres = DeviceBuffer(n * p * p * k * 2)
             call("omCudaNchwToNhwc", r32.ptr, dres.ptr, n, k, p, p, k, dtype)
+            r32.free()
     out = DeviceBuffer(n * p * p * k * (4 if out_f32 else 2))
     out2 = DeviceBuffer(n * p * p * k * (4 if out_f32 else 2))
     for o in (out, out2):
@@ -120,11 +124,18 @@ def test_conv_bn_act(gpu, case):
         o32 = DeviceBuffer(n * k * p * p * 4)
         call("omCudaNhwcToNchw", out.ptr, o32.ptr, n, k, p, p, k, dtype)
         got = o32.to_numpy((n, k, p, p))
+        o32.free()
     assert gpu.kernel_error() == 0
+    for b in [dx, dw, packed, bias, out, out2] + bufs + ([dres] if dres else []):
+        b.free()
+    assert np.isfinite(got).all()
+    if images is not None:
+        got = got[images]
+        x = np.ascontiguousarray(x[images])
+        res = None if res is None else np.ascontiguousarray(res[images])
 
     # fp32 reference on the original data
     want = _reference(x, w, (gamma, beta, mean, var), res, stride, pad, act)
-    assert np.isfinite(got).all()
     e32 = rel_err(got, want)
     # reference on 16-bit-rounded operands with the BN scale folded as the kernel does
     scale = gamma / np.sqrt(var + 1e-5)
@@ -140,6 +151,51 @@ def test_conv_bn_act(gpu, case):
     e16 = rel_err(got, y)
     assert e16 <= 1e-2, f"vs rounded-operand oracle: {e16}"
     assert e32 <= 2e-2, f"vs fp32 oracle: {e32}"
+
+
+@pytest.mark.parametrize("case", CASES, ids=[f"c{i}" for i in range(len(CASES))])
+def test_conv_bn_act(gpu, case):
+    _check_case(gpu, case)
+
+
+def tile_plan(n, h, cs, k, ks, stride, pad, residual):
+    """(BN, CTAs per SM, sub-tiles per tile, epilogue warps) that omCudaConv2dBnAct picks."""
+    import ctypes
+    from omnimatchdeeplearningtool_b200._lib import call
+    plan = (ctypes.c_int * 4)()
+    call("omCudaConvTilePlan", n, h, h, cs, k, ks, ks, stride, pad, int(residual), plan)
+    return tuple(plan)
+
+
+# ResNet-50's batch-256 layers whose tile variant only a full batch reaches: 256-wide tiles for
+# long reductions (the layer-3/4 3x3 and 1x1 convs), and the sub-tile pairs of the 64- and
+# 128-wide 3x3 layers. Each case names the plan it must get, so a retune that stops covering a
+# variant fails here instead of leaving it untested. (n, c, h, k, ks, stride, pad, dtype,
+# residual, act, out_f32), expected (BN, OCC, MT, EW)
+FULL_BATCH_CASES = [
+    ((256, 256, 14, 256, 3, 1, 1, "bf16", False, "relu", False), (256, 1, 1, 8)),   # layer-3 3x3
+    ((256, 512, 7, 512, 3, 1, 1, "bf16", False, "relu", False), (256, 1, 1, 8)),    # layer-4 3x3
+    ((256, 1024, 14, 256, 1, 1, 0, "bf16", False, "relu", False), (256, 1, 1, 8)),  # layer-3 1x1 in
+    ((256, 2048, 7, 512, 1, 1, 0, "bf16", False, "relu", False), (256, 1, 1, 8)),   # layer-4 1x1 in
+    ((256, 2048, 7, 512, 1, 1, 0, "bf16", True, "relu", False), (256, 1, 1, 4)),    # + residual
+    ((256, 1024, 14, 256, 1, 1, 0, "f16", True, "relu", False), (256, 1, 1, 4)),    # + residual
+    ((256, 64, 56, 64, 3, 1, 1, "bf16", False, "relu", False), (64, 1, 2, 8)),      # layer-1 3x3
+    ((256, 128, 28, 128, 3, 1, 1, "bf16", False, "relu", False), (128, 1, 2, 8)),   # layer-2 3x3
+]
+FULL_BATCH_IMAGES = [0, 1, 2, 3, 252, 253, 254, 255]
+
+
+@pytest.mark.parametrize("case,plan", FULL_BATCH_CASES,
+                         ids=[f"b256_{c[1]}x{c[2]}_{c[3]}k{c[4]}{'_res' if c[8] else ''}"
+                              for c, _ in FULL_BATCH_CASES])
+def test_conv_bn_act_full_batch(gpu, case, plan):
+    """The tile variants of the benchmarked batch-256 ResNet-50 forward, launched at batch 256
+    and compared on its first four and last four images."""
+    from omnimatchdeeplearningtool_b200._lib import lib
+    n, c, h, k, ks, stride, pad, _, res = case[:9]
+    cs = int(lib.omCudaStoredChannels(c))
+    assert tile_plan(n, h, cs, k, ks, stride, pad, res) == plan
+    _check_case(gpu, case, images=FULL_BATCH_IMAGES)
 
 
 def test_conv_rejects_bad_shapes(gpu):

@@ -117,30 +117,32 @@ def test_grouped_depthwise_conv(gpu):
     assert rel_err_floor(y.to_numpy(want.shape), want) <= TOL
 
 
-@pytest.mark.parametrize("c,k,h,stride,pad,dil,groups", [
-    (32, 48, 20, 1, 1, 1, 1),   # dense, dilation 1: omCudaConv2d's tensor-core path
-    (32, 40, 21, 1, 2, 2, 1),   # dilation 2: the zero-inserted 5x5 filter on the same path
-    (16, 24, 19, 2, 2, 2, 1),   # dilation 2, stride 2
-    (8, 16, 23, 1, 3, 3, 1),    # dilation 3: the zero-inserted 7x7 filter
-    (4, 8, 24, 1, 9, 9, 1),     # dilation 9: the zero-inserted 19x19 filter
-    (4, 8, 24, 1, 13, 13, 1),   # dilation 13 (27x27, over 64x the taps): the direct kernel
-    (12, 18, 17, 1, 2, 2, 3)])  # grouped and dilated: the direct kernel
-def test_dilated_conv_routes(gpu, c, k, h, stride, pad, dil, groups):
+@pytest.mark.parametrize("n,c,k,h,stride,pad,dil,groups,kh,kw", [
+    (2, 32, 48, 20, 1, 1, 1, 1, 3, 3),    # dense, dilation 1: omCudaConv2d's tensor-core path
+    (2, 32, 40, 21, 1, 2, 2, 1, 3, 3),    # dilation 2: dilated taps on the tensor-core path
+    (2, 16, 24, 19, 2, 2, 2, 1, 3, 3),    # dilation 2, stride 2
+    (2, 8, 16, 23, 1, 3, 3, 1, 3, 3),     # dilation 3
+    (2, 4, 8, 24, 1, 9, 9, 1, 3, 3),      # dilation 9 (19x19 extent)
+    (2, 4, 8, 24, 1, 13, 13, 1, 3, 3),    # dilation 13 (27x27 extent)
+    (2, 20, 24, 30, 1, 4, 4, 1, 3, 1),    # non-square 3x1 filter, dilation 4
+    (2, 37, 45, 26, 1, 6, 6, 1, 3, 3),    # channels not a multiple of 32 or 8, dilation 6
+    (1, 2, 4, 40, 1, 130, 130, 1, 3, 3),  # 261x261 extent: tensor path refuses, direct kernel
+    (2, 12, 18, 17, 1, 2, 2, 3, 3, 3)])   # grouped and dilated: the direct kernel
+def test_dilated_conv_routes(gpu, n, c, k, h, stride, pad, dil, groups, kh, kw):
     """omCudaDilatedConv2d (cuda_kernels.cu:1201) against the oracle's convolution with the
     filter dilated by zero insertion; bias included."""
     import oracle as orc
     from omnimatchdeeplearningtool_b200.backend import CUDABackend as B
     rng = _rng(70 + dil + groups)
-    n, r = 2, 3
     x = rng.standard_normal((n, c, h, h), dtype=np.float32)
-    w = rng.standard_normal((k, c // groups, r, r), dtype=np.float32)
+    w = rng.standard_normal((k, c // groups, kh, kw), dtype=np.float32)
     b = rng.standard_normal(k).astype(np.float32)
-    er = r + (r - 1) * (dil - 1)
-    wd = np.zeros((k, c // groups, er, er), np.float32)
+    er, es = kh + (kh - 1) * (dil - 1), kw + (kw - 1) * (dil - 1)
+    wd = np.zeros((k, c // groups, er, es), np.float32)
     wd[:, :, ::dil, ::dil] = w
     want = orc.conv2d(x, wd, b, stride, pad, groups=groups)
     y = _out(want.shape)
-    B.dilatedConv2d(_dev(x).ptr, _dev(w).ptr, _dev(b).ptr, y.ptr, n, c, h, h, k, r, r, stride,
+    B.dilatedConv2d(_dev(x).ptr, _dev(w).ptr, _dev(b).ptr, y.ptr, n, c, h, h, k, kh, kw, stride,
                     pad, dil, groups)
     assert rel_err_floor(y.to_numpy(want.shape), want) <= TOL
     assert gpu.kernel_error() == 0

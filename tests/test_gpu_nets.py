@@ -36,6 +36,39 @@ def test_inference_plan_matches_oracle(gpu, name, dtype):
     assert np.array_equal(got.argmax(1), want.argmax(1))
 
 
+def test_resnet50_bf16_batch256_matches_oracle_on_subset(gpu):
+    """The benchmarked configuration itself: the ResNet-50 bf16 plan at batch 256 (whose long
+    reductions run on 256-wide tiles and whose 64/128-wide 3x3 layers on sub-tile pairs, tile
+    variants that small batches never reach), compared with the fp32 oracle on the first four
+    and the last four images of the batch: <= 2e-2 and identical top-1."""
+    import oracle as orc
+    from omnimatchdeeplearningtool_b200 import _lib, synth
+    from omnimatchdeeplearningtool_b200._lib import lib
+    from omnimatchdeeplearningtool_b200.plan import InferencePlan
+    from test_gpu_conv_tc import tile_plan
+    # the layer-3/4 3x3 convs of this batch take 256-wide tiles, layer 1's 3x3 sub-tile pairs
+    assert tile_plan(256, 14, 256, 256, 3, 1, 1, False)[0] == 256
+    assert tile_plan(256, 7, 512, 512, 3, 1, 1, False)[0] == 256
+    assert tile_plan(256, 56, 64, 64, 3, 1, 1, False)[2] == 2
+    assert int(lib.omCudaStoredChannels(64)) == 64
+    net = synth.resnet_spec(50)
+    w = synth.make_weights(net)
+    x = synth.normal_input(256)
+    plan = InferencePlan(net, w, batch=256, dtype=_lib.DTYPE_BF16)
+    try:
+        plan.capture()
+        got = plan.run(x)
+    finally:
+        plan.close()
+    assert np.isfinite(got).all()
+    idx = [0, 1, 2, 3, 252, 253, 254, 255]
+    want = orc.forward(net, w, np.ascontiguousarray(x[idx]))
+    e = rel_err(got[idx], want)
+    print(f"resnet50 bf16 batch 256, images {idx}: max rel err {e:.2e}")
+    assert e <= 2e-2, e
+    assert np.array_equal(got[idx].argmax(1), want.argmax(1))
+
+
 @pytest.mark.parametrize("slots", [1, 2])
 def test_serve_pipeline_matches_run(gpu, slots):
     """InferencePlan.serve (copies on the transfer stream, two input slots, one graph each)

@@ -7,10 +7,12 @@ owns the device. For them, omCudaBatchNorm2dNoAlloc computes exactly what omCuda
 computes, but keeps its training-mode partial sums in a fixed per-device array inside the
 library instead of pool memory.
 
-This file is named so that pytest collects it last. It checks, through the C ABI, that two
-calls in a row match the pool-backed entry point within the fp32 tolerance (1e-4, max-
-normalised), and that a channel count beyond the fixed maximum is refused without a launch.
-It runs the same alone in a fresh process and after the other tests.
+This file is named so that pytest collects it last. It checks, through the C ABI, that calls
+in a row give bit for bit what the pool-backed entry point gives (both run the same kernels
+with the same number of partial-sum splits), including a call whose channel and split counts
+differ from the one before, so that slots left over in the shared array would show, and that
+a channel count beyond the fixed maximum is refused without a launch. It runs the same alone
+in a fresh process and after the other tests.
 """
 import numpy as np
 import pytest
@@ -18,7 +20,6 @@ import pytest
 from conftest import rel_err
 
 pytestmark = pytest.mark.gpu
-TOL = 1e-4
 
 
 def _bn(lib_fn, x, g, b, rm, rv, n, c, h, w, training):
@@ -35,25 +36,31 @@ def _bn(lib_fn, x, g, b, rm, rv, n, c, h, w, training):
 def test_no_alloc_batchnorm_matches_pool_backed_entry_point(gpu):
     from omnimatchdeeplearningtool_b200._lib import lib
     rng = np.random.Generator(np.random.PCG64(21))
-    n, c, h, w = 8, 64, 64, 64   # 32768 values per channel: several partial-sum splits
-    g = rng.uniform(0.5, 1.5, c).astype(np.float32)
-    b = rng.standard_normal(c).astype(np.float32)
-    rm_a = (rng.standard_normal(c) * 0.1).astype(np.float32)
-    rv_a = rng.uniform(0.5, 1.5, c).astype(np.float32)
-    rm_b, rv_b = rm_a.copy(), rv_a.copy()
-    for call_no in range(2):   # two calls in a row; the shared array keeps the first's contents
+    # 64 channels of 32768 values (several partial-sum splits), then 24 channels of 6400 values
+    # (another split count), then the first shape again
+    shapes = [(8, 64, 64, 64), (4, 24, 40, 40), (8, 64, 64, 64)]
+    state = {}
+    for call_no, (n, c, h, w) in enumerate(shapes):
+        if c not in state:
+            g = rng.uniform(0.5, 1.5, c).astype(np.float32)
+            b = rng.standard_normal(c).astype(np.float32)
+            rm = (rng.standard_normal(c) * 0.1).astype(np.float32)
+            rv = rng.uniform(0.5, 1.5, c).astype(np.float32)
+            state[c] = [g, b, rm, rv, rm.copy(), rv.copy()]
+        g, b, rm_a, rv_a, rm_b, rv_b = state[c]
         x = (rng.standard_normal((n, c, h, w)) * (1 + call_no) + 0.3).astype(np.float32)
         ref = _bn(lib.omCudaBatchNorm2d, x, g, b, rm_a, rv_a, n, c, h, w, 1)
         got = _bn(lib.omCudaBatchNorm2dNoAlloc, x, g, b, rm_b, rv_b, n, c, h, w, 1)
+        # output, saved mean, saved inverse std, running mean, running variance
         for a, e in zip(got, ref):
-            assert rel_err(a, e) <= TOL, (call_no, rel_err(a, e))
-        rm_a, rv_a = ref[3], ref[4]
-        rm_b, rv_b = got[3], got[4]
+            assert np.array_equal(a, e), (call_no, rel_err(a, e))
+        state[c] = [g, b, ref[3], ref[4], got[3], got[4]]
     # eval mode reads the running statistics only
-    x = rng.standard_normal((2, c, 5, 5)).astype(np.float32)
-    ref = _bn(lib.omCudaBatchNorm2d, x, g, b, rm_a, rv_a, 2, c, 5, 5, 0)
-    got = _bn(lib.omCudaBatchNorm2dNoAlloc, x, g, b, rm_b, rv_b, 2, c, 5, 5, 0)
-    assert rel_err(got[0], ref[0]) <= TOL
+    g, b, rm_a, rv_a, rm_b, rv_b = state[64]
+    x = rng.standard_normal((2, 64, 5, 5)).astype(np.float32)
+    ref = _bn(lib.omCudaBatchNorm2d, x, g, b, rm_a, rv_a, 2, 64, 5, 5, 0)
+    got = _bn(lib.omCudaBatchNorm2dNoAlloc, x, g, b, rm_b, rv_b, 2, 64, 5, 5, 0)
+    assert np.array_equal(got[0], ref[0])
 
 
 def test_no_alloc_batchnorm_refuses_too_many_channels(gpu):
