@@ -87,6 +87,14 @@ int omCudaTransferWaitCompute(void);
 int omCudaSetDevice(int nDeviceId);
 /* new: the compute stream of the calling thread's device, as a cudaStream_t */
 void* omCudaGetStream(void);
+/* new: the calling thread's current device (set by omCudaInit / omCudaSetDevice), -1 if none */
+int omCudaGetCurrentDevice(void);
+/* new: device-side gather of a strided fp32 view into a contiguous buffer (Tensor::contiguous
+ * without the host round trip of om.engine.tensor.ixx:390-391):
+ * dst[i] = src[nOffset + sum_d coord_d(i) * pStrides[d]], with coord(i) the row-major coordinates
+ * of i in pShape. pShape / pStrides are host arrays of nDims <= 8 entries (elements, >= 0). */
+int omCudaStridedCopy(const float* pSrc, float* pDst, const int* pShape, const int* pStrides,
+                      int nDims, long long nOffset);
 /* new: read and clear the device error word that bounded in-kernel waits set; *pCode is 0
  * when no kernel gave up since the last call. Synchronises the compute stream. */
 int omCudaGetKernelError(unsigned int* pCode);

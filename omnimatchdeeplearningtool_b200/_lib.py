@@ -67,6 +67,8 @@ _SIGS = {
     "omCudaGraphBeginCapture": [], "omCudaGraphEndCapture": [POINTER(c_void_p)],
     "omCudaGraphLaunch": [P], "omCudaGraphDestroy": [P],
     "omCudaGetKernelError": [POINTER(c_uint)], "omCudaGetLaunchCount": [POINTER(c_ulonglong)],
+    "omCudaGetCurrentDevice": [],
+    "omCudaStridedCopy": [P, P, POINTER(c_int), POINTER(c_int), I, c_longlong],
     # elementwise
     "omCudaAdd": [P, P, P, I], "omCudaMulScalar": [P, F, P, I], "omCudaReLU": [P, P, I],
     "omCudaReLUBackward": [P, P, P, I], "omCudaClip": [P, P, I, F, F],

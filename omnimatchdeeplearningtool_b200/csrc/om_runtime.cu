@@ -70,6 +70,11 @@ int omCudaSetDevice(int nDeviceId) {
     return OM_OK;
 }
 
+int omCudaGetCurrentDevice(void) {
+    DeviceCtx* c = omb::ctx();
+    return c ? c->device : -1;
+}
+
 void* omCudaGetStream(void) {
     DeviceCtx* c = omb::ctx();
     return c ? (void*)c->compute : nullptr;

@@ -4,8 +4,11 @@
 # The transform is purely mechanical and the output goes to a scratch directory given
 # as $2; nothing generated here is committed or shipped.
 #   $1 = reference root (the read-only checkout), $2 = output directory
+#   $3 = "backend" (optional): the engine's TensorStorage and CUDABackend modules become
+#        forwarding headers to this repository's replacements (include/om_tensor_storage.hpp,
+#        include/om_cuda_backend.hpp), for a build of the engine on the B200 backend
 set -e
-REF="$1"; OUT="$2"
+REF="$1"; OUT="$2"; MODE="$3"
 mkdir -p "$OUT"
 for f in "$REF"/src/hal/om.hal.simd.ixx "$REF"/src/hal/om.hal.cpu_backend.ixx \
          "$REF"/src/hal/om.hal.cuda_backend.ixx \
@@ -22,3 +25,7 @@ for f in "$REF"/src/hal/om.hal.simd.ixx "$REF"/src/hal/om.hal.cpu_backend.ixx \
         -e 's/^import \(om\.[a-z_.0-9]*\);.*$/#include "\1.hpp"/' \
         -e 's/^export namespace/namespace/' -e 's/^export //' "$f"; } > "$OUT/$b.hpp"
 done
+if [ "$MODE" = "backend" ]; then
+  printf '#pragma once\n#include "om_tensor_storage.hpp"\n' > "$OUT/om.engine.tensor_storage.hpp"
+  printf '#pragma once\n#include "om_cuda_backend.hpp"\n' > "$OUT/om.hal.cuda_backend.hpp"
+fi
