@@ -129,11 +129,19 @@ int omeng_model_param_is_cuda(void* h, int i) {
     return params_of(static_cast<EngineModel*>(h))[i].second->isCuda() ? 1 : 0;
 }
 
-// Every parameter and buffer replaced by its device copy (EngineBridge.cpp:915-931).
+// Every parameter and buffer replaced by its device copy (EngineBridge.cpp:915-931). The
+// reference's Tensor::to() does not carry the leaf's GradAccumulator over (om.engine.tensor.ixx:
+// 264), and every op takes its tensors by value, so a parameter moved exactly as EngineBridge
+// moves it would record no gradient: backward would accumulate into an accumulator created on a
+// temporary copy (tensor_ops.ixx:81-98). The shim re-arms each moved parameter the way
+// Module::registerParameter arms it at construction (module.ixx:39, tensorSetRequiresGrad).
 int omeng_model_to_cuda(void* h) {
     auto* m = static_cast<EngineModel*>(h);
     return guarded([&] {
-        for (auto& p : params_of(m)) *p.second = p.second->cuda();
+        for (auto& p : params_of(m)) {
+            *p.second = p.second->cuda();
+            om::tensorSetRequiresGrad(*p.second, true);
+        }
         for (auto& b : buffers_of(m)) *b.second = b.second->cuda();
         m->on_cuda = true;
     });
