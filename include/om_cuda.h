@@ -36,6 +36,7 @@ extern "C" {
 #define OM_ERR_KERNEL_TIMEOUT (-6)/* a bounded in-kernel wait gave up (see omCudaGetKernelError) */
 #define OM_ERR_DRIVER (-7)        /* a driver entry point (tensor-map encode) was unavailable */
 #define OM_ERR_TOO_LARGE (-8)     /* request exceeds the fixed capacity of an allocation-free entry point */
+#define OM_ERR_COMM (-9)          /* a collective failed or timed out; the communicator was aborted */
 
 /* element types for the NHWC entry points */
 #define OM_DTYPE_F32 0
@@ -220,6 +221,9 @@ int omCudaSoftmaxCrossEntropyBackward(const float* pSoftmax, const float* pTarge
 /* v = m*v + g; p -= lr*v (m == 0 or pVelocity == NULL: p -= lr*g) */
 int omCudaSgdStep(float* pParam, const float* pGrad, float* pVelocity, int nCount, float fLr,
                   float fMomentum);                                              /* replaces :2511 */
+/* new: omCudaSgdStep on fGradScale * grad (1/world after a summing all-reduce), one pass */
+int omCudaSgdStepScaled(float* pParam, const float* pGrad, float* pVelocity, int nCount,
+                        float fLr, float fMomentum, float fGradScale);
 /* new: the training loop's gradient guard (EngineBridge.cpp:1885-1925) on the device, in place of
  * its per-step host copy of every gradient. pStatus (device, 3 floats) receives the L2 norm (NaN
  * when an element is not finite), the verdict (1 = step, 0 = skip: a NaN/Inf element) and the
@@ -323,6 +327,37 @@ int omCudaDropout(const float* pIn, float* pOut, const float* pMask, int nCount,
 /* mask from the reference's per-index hash of nSeed: 1/keep with probability keep, else 0 */
 int omCudaDropoutForward(const float* pIn, float* pOut, float* pMask, int nCount,
                          float fKeepProb, unsigned long long nSeed);             /* :2324 */
+
+/* ---------------- new: data-parallel gradient exchange over NCCL ----------------
+ * Replaces the stub DataParallel::synchronizeGradients (om.engine.distributed.ixx:132-161),
+ * which names ncclAllReduce but does nothing. One communicator per device, joined by the
+ * thread that drives the device; its collectives run on a communication stream of their own.
+ * Every failure (an NCCL error, a time limit passed) aborts the communicator: later calls on it
+ * return OM_ERR_COMM instead of waiting for a peer that is gone. */
+#define OM_NCCL_ID_BYTES 128
+#define OM_REDUCE_SUM 0
+#define OM_REDUCE_MAX 1
+/* rank 0 creates the communicator's id (OM_NCCL_ID_BYTES opaque bytes) and hands it to all ranks */
+int omNcclGetUniqueId(void* pId);
+/* the calling thread's device joins as nRank of nWorld; initialisation is non-blocking and
+ * polled for at most nTimeoutMs (a rank that never joins makes every rank return OM_ERR_COMM) */
+int omNcclInit(int nRank, int nWorld, const void* pId, int nTimeoutMs);
+/* in-place all-reduce (sum or max) of nCount floats that starts once the compute work issued
+ * so far has finished and overlaps the compute work issued after it */
+int omCudaAllreduceAsync(float* pData, long long nCount, int nOp);
+/* later compute work waits for every all-reduce issued so far (stream-ordered, no host wait) */
+int omCudaAllreduceJoin(void);
+/* omCudaAllreduceAsync + omCudaAllreduceJoin */
+int omCudaAllreduce(float* pData, long long nCount, int nOp);
+/* host: wait up to nTimeoutMs for the issued all-reduces, polling the communicator's error
+ * state; an error or the time limit aborts the communicator and returns OM_ERR_COMM */
+int omNcclPoll(int nTimeoutMs);
+/* rank and world size of the device's communicator */
+int omNcclRankInfo(int* pRank, int* pWorld);
+/* abort the communicator (pending collectives are cancelled) and release it */
+int omNcclAbort(void);
+/* finalise and release the communicator after its work has finished */
+int omNcclDestroy(void);
 
 /* ---------------- new: NHWC bf16/fp16 fused inference path ---------------- */
 /* Elements of the packed K-major weight [Cout, Kpad] that omCudaPackConvWeight writes, where

@@ -23,6 +23,7 @@ STATUS_NAMES = {
     -6: "OM_ERR_KERNEL_TIMEOUT",
     -7: "OM_ERR_DRIVER",
     -8: "OM_ERR_TOO_LARGE",
+    -9: "OM_ERR_COMM",
 }
 DTYPE_F32, DTYPE_BF16, DTYPE_F16 = 0, 1, 2
 ACT_NONE, ACT_RELU, ACT_RELU6 = 0, 1, 2
@@ -68,6 +69,11 @@ _SIGS = {
     "omCudaGraphLaunch": [P], "omCudaGraphDestroy": [P],
     "omCudaGetKernelError": [POINTER(c_uint)], "omCudaGetLaunchCount": [POINTER(c_ulonglong)],
     "omCudaGetCurrentDevice": [],
+    # data-parallel gradient exchange
+    "omNcclGetUniqueId": [P], "omNcclInit": [I, I, P, I],
+    "omCudaAllreduceAsync": [P, c_longlong, I], "omCudaAllreduceJoin": [],
+    "omCudaAllreduce": [P, c_longlong, I], "omNcclPoll": [I],
+    "omNcclRankInfo": [POINTER(c_int), POINTER(c_int)], "omNcclAbort": [], "omNcclDestroy": [],
     "omCudaStridedCopy": [P, P, POINTER(c_int), POINTER(c_int), I, c_longlong],
     # elementwise
     "omCudaAdd": [P, P, P, I], "omCudaMulScalar": [P, F, P, I], "omCudaReLU": [P, P, I],
@@ -96,7 +102,7 @@ _SIGS = {
     "omCudaAddBias": [P, P, P, I, I, I], "omCudaAddBiasBackward": [P, P, I, I, I],
     "omCudaSoftmax": [P, P, I, I], "omCudaCrossEntropy": [P, P, P, I, I],
     "omCudaSoftmaxCrossEntropyBackward": [P, P, P, I, I],
-    "omCudaSgdStep": [P, P, P, I, F, F],
+    "omCudaSgdStepScaled": [P, P, P, I, F, F, F], "omCudaSgdStep": [P, P, P, I, F, F],
     "omCudaAdamStep": [P, P, P, P, I, F, F, F, F, I],
     "omCudaGradNormClip": [P, I, F, F, P], "omCudaSgdStepGuarded": [P, P, P, I, F, F, P],
     # further elementwise ops and activations

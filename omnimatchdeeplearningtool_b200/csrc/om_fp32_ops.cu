@@ -389,17 +389,20 @@ __global__ void ce_softmax_bwd_kernel(const float* __restrict__ p, const float* 
 
 // ---------------------------------------------------------------- optimiser, elementwise
 // status (nullable): the gradient guard's verdict; status[1] == 0 skips the step
+// gs scales the gradient first (1/world after a summing all-reduce; exactly 1 otherwise)
 __global__ void sgd_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ v,
-                           long long n, float lr, float mom, const float* __restrict__ status) {
+                           long long n, float lr, float mom, const float* __restrict__ status,
+                           float gs = 1.f) {
     if (status && status[1] == 0.f) return;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n;
          i += (long long)gridDim.x * blockDim.x) {
+        const float gi = gs == 1.f ? g[i] : gs * g[i];
         if (v) {
-            float nv = mom * v[i] + g[i];
+            float nv = mom * v[i] + gi;
             v[i] = nv;
             p[i] -= lr * nv;
         } else {
-            p[i] -= lr * g[i];
+            p[i] -= lr * gi;
         }
     }
 }
@@ -776,6 +779,18 @@ extern "C" int omCudaSgdStep(float* pParam, const float* pGrad, float* pVelocity
     float* v = fMomentum > 0.f ? pVelocity : nullptr;
     if (fMomentum > 0.f && !pVelocity) return OM_ERR_INVALID;
     sgd_kernel<<<OMB_EW(nCount)>>>(pParam, pGrad, v, nCount, fLr, fMomentum, nullptr);
+    return after_launch(c);
+}
+
+// Data-parallel SGD: the summed gradient of `world` ranks scaled by fGradScale (1/world) inside
+// the update, so the scale costs no extra pass over the gradient.
+extern "C" int omCudaSgdStepScaled(float* pParam, const float* pGrad, float* pVelocity,
+                                   int nCount, float fLr, float fMomentum, float fGradScale) {
+    OMB_CTX_OR_FAIL(c);
+    if (!pParam || !pGrad || nCount < 0) return OM_ERR_INVALID;
+    float* v = fMomentum > 0.f ? pVelocity : nullptr;
+    if (fMomentum > 0.f && !pVelocity) return OM_ERR_INVALID;
+    sgd_kernel<<<OMB_EW(nCount)>>>(pParam, pGrad, v, nCount, fLr, fMomentum, nullptr, fGradScale);
     return after_launch(c);
 }
 

@@ -23,7 +23,7 @@ training step (forward, CE loss, backward, SGD momentum) of the reference engine
 from __future__ import annotations
 
 import ctypes
-from typing import Dict, List, Optional, Sequence, Tuple
+from typing import Callable, Dict, List, Optional, Sequence, Tuple
 
 import numpy as np
 
@@ -372,6 +372,14 @@ class Fp32Net:
             self.vel[name] = _Ptr(self.vel_flat.ptr + off * 4)
         self.buffers = {name: self._dev(weights[name]) for name, _ in net.buffers}
         self.acts = {}
+        # called with a parameter's name once the backward pass has issued the last kernel
+        # that writes its gradient (a data-parallel wrapper starts bucket all-reduces from it)
+        self.grad_hook: Optional[Callable[[str], None]] = None
+
+    def _grad_done(self, *names: str) -> None:
+        if self.grad_hook is not None:
+            for n in names:
+                self.grad_hook(n)
 
     # ------------------------------------------------------------------ memory helpers
     def _dev(self, a: np.ndarray) -> DeviceBuffer:
@@ -501,6 +509,7 @@ class Fp32Net:
         B.transpose(feat.ptr, featT.ptr, n, c)
         B.matmul(featT.ptr, dlog.ptr, self.grad("fc.weight"), c, n, K)
         B.addBiasBackward(dlog.ptr, self.grad("fc.bias"), n, K, 1)
+        self._grad_done("fc.weight", "fc.bias")
         WT = self._buf("fcWT", c * K * 4)
         B.transpose(self.param["fc.weight"].ptr, WT.ptr, c, K)
         dfeat = self._buf("dfeat", n * c * 4)
@@ -537,6 +546,7 @@ class Fp32Net:
              rec["invstd"].ptr, self.param[cv.bn + ".gamma"].ptr, rec["y"].ptr, dz.ptr,
              self.grad(cv.bn + ".gamma"), self.grad(cv.bn + ".beta"), n, cv.cout, rec["p"],
              rec["q"], 1e-5, _lib.ACT_RELU if rec["relu"] else _lib.ACT_NONE)
+        self._grad_done(cv.bn + ".gamma", cv.bn + ".beta")
         dx = None
         if need_dx:  # the image itself needs no gradient
             dx = self._buf(key + ".dx", n * rec["c"] * rec["h"] * rec["w"] * 4)
@@ -546,6 +556,7 @@ class Fp32Net:
         B.conv2dBackwardWeight(rec["x"].ptr, dz.ptr, self.grad(cv.name + ".weight"), None, n,
                                rec["c"], rec["h"], rec["w"], cv.cout, cv.k, cv.k, cv.pad, cv.pad,
                                cv.stride, cv.stride)
+        self._grad_done(cv.name + ".weight")
         return dx
 
     def step(self, lr: float = 0.01, momentum: float = 0.9, grad_scale: float = 1.0,
@@ -557,13 +568,18 @@ class Fp32Net:
         which uses 5.0) runs first, on the device: a NaN/Inf gradient skips the step, a norm
         above max_grad_norm scales the gradient down to it, then accum_scale (1/accumulation
         steps) applies. :meth:`guard_status` reads the verdict back."""
+        if max_grad_norm is None:
+            # one launch over the flat parameters (elementwise, so the same as one per tensor),
+            # with the data-parallel 1/world scale applied inside the update
+            if grad_scale != 1.0:
+                call("omCudaSgdStepScaled", self.param_flat.ptr, self.grad_flat,
+                     self.vel_flat.ptr, self.n_params, lr, momentum, grad_scale)
+            else:
+                B.sgdStep(self.param_flat.ptr, self.grad_flat, self.vel_flat.ptr, self.n_params,
+                          lr, momentum)
+            return
         if grad_scale != 1.0:
             B.mulScalar(self.grad_flat, grad_scale, self.grad_flat, self.n_params)
-        if max_grad_norm is None:
-            # one launch over the flat parameters (elementwise, so the same as one per tensor)
-            B.sgdStep(self.param_flat.ptr, self.grad_flat, self.vel_flat.ptr, self.n_params, lr,
-                      momentum)
-            return
         if self._guard is None:
             self._guard = DeviceBuffer.zeros(16)
             self.keep.append(self._guard)

@@ -13,7 +13,7 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 def _declared():
     src = open(os.path.join(ROOT, "include", "om_cuda.h")).read()
     src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
-    return sorted(set(re.findall(r"\b(omCuda\w+)\s*\(", src)))
+    return sorted(set(re.findall(r"\b(om(?:Cuda|Nccl)\w+)\s*\(", src)))
 
 
 def test_header_declares_reference_hot_path():
