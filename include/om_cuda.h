@@ -387,6 +387,15 @@ int omCudaConv2dBnAct(const void* pInput, const void* pPacked, const float* pBia
  * [2] = 128-row sub-tiles per tile, [3] = epilogue warps. For tests that must cover a variant. */
 int omCudaConvTilePlan(int nBatch, int nH, int nW, int nCs, int nCout, int nKH, int nKW,
                        int nStride, int nPad, int bResidual, int* pPlan);
+/* new: launch-duration stamps for measurement. With pStamps (device, 2 * nCapacity u64) set,
+ * every tcgen05 conv launch on the calling thread's device (omCudaConv2dBnAct, the stem, the
+ * fp32 3xTF32 convs) takes one pair per CTA, in launch order: %globaltimer (ns) at the CTA's
+ * start and at its end; a launch that no longer fits records nothing. NULL switches it off.
+ * Each call resets the launch list. A launch captured into a CUDA graph keeps its slots. */
+int omCudaConvStamps(unsigned long long* pStamps, int nCapacity);
+/* the launches recorded since omCudaConvStamps: first pair index and CTA count of each (up to
+ * nMax of them); *pCount = number recorded */
+int omCudaConvStampLaunches(int* pFirst, int* pCtas, int nMax, int* pCount);
 /* new: the image stem (stride 1 or 2, Cin * stride^2 <= 16, Cout % 8 == 0) from the NCHW fp32
  * image: out[n,p,q,k] = act(sum_{c,r,s} x[n,c,p*st-pad+r,q*st-pad+s] * W[k,c,r,s] * scale[k]
  * + bias[k]), NHWC 16-bit output, BN folded as in omCudaPackConvWeight. A first launch writes a
@@ -404,6 +413,13 @@ int omCudaPackStemWeight(const float* pWeight, const float* pConvBias, const flo
 int omCudaStemConvBnAct(const float* pInput, void* pWorkspace, const void* pPacked,
                         const float* pBias, void* pOutput, int nBatch, int nCin, int nH, int nW,
                         int nCout, int nKH, int nKW, int nStride, int nPad, int nAct, int nDtype);
+/* new: omCudaStemConvBnAct from an NCHW image in nInDtype: OM_DTYPE_F32, or the conv's own
+ * 16-bit nDtype (half the bytes to move to the device; a 16-bit image gives the same output as
+ * its fp32 form, since the stem rounds its input to nDtype anyway) */
+int omCudaStemConvBnActIn(const void* pInput, int nInDtype, void* pWorkspace, const void* pPacked,
+                          const float* pBias, void* pOutput, int nBatch, int nCin, int nH, int nW,
+                          int nCout, int nKH, int nKW, int nStride, int nPad, int nAct,
+                          int nDtype);
 /* NCHW fp32 -> NHWC (nDtype) with channels zero-padded to nCs */
 int omCudaNchwToNhwc(const float* pIn, void* pOut, int nN, int nC, int nH, int nW, int nCs,
                      int nDtype);

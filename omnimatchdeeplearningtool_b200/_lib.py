@@ -141,8 +141,11 @@ _SIGS = {
     "omCudaPackConvWeight": [P, P, P, P, P, P, F, P, P, I, I, I, I, I, I],
     "omCudaConv2dBnAct": [P, P, P, P, P, I, I, I, I, I, I, I, I, I, I, I, I],
     "omCudaConvTilePlan": [I, I, I, I, I, I, I, I, I, I, POINTER(c_int)],
+    "omCudaConvStamps": [P, I],
+    "omCudaConvStampLaunches": [POINTER(c_int), POINTER(c_int), I, POINTER(c_int)],
     "omCudaPackStemWeight": [P, P, P, P, P, P, F, P, P, I, I, I, I, I, I],
     "omCudaStemConvBnAct": [P, P, P, P, P, I, I, I, I, I, I, I, I, I, I, I],
+    "omCudaStemConvBnActIn": [P, I, P, P, P, P, I, I, I, I, I, I, I, I, I, I, I],
     "omCudaNchwToNhwc": [P, P, I, I, I, I, I, I], "omCudaNhwcToNchw": [P, P, I, I, I, I, I, I],
     "omCudaMaxPool2dNhwc": [P, P, I, I, I, I, I, I, I, I],
     "omCudaGlobalAvgPoolNhwc": [P, P, I, I, I, I, I],

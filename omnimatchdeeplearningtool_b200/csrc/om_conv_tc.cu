@@ -62,6 +62,8 @@
 #include <mutex>
 #include <type_traits>
 
+#include <vector>
+
 #include "om_common.cuh"
 
 namespace omb {
@@ -112,6 +114,8 @@ struct Params {
     int act;
     int out_f32;          // 1: fp32 output stored directly (classifier logits)
     unsigned int* err;
+    // optional (nullptr: off): %globaltimer at each CTA's start and end, stamps[2*cta + 0/1]
+    unsigned long long* stamps;
 };
 
 // MODE_SW32: filter taps in k-block kb (4, or what is left of the R*S taps in the last one)
@@ -435,6 +439,7 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
     const int lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
+        if (p.stamps) p.stamps[2 * blockIdx.x] = gtimer();
         for (int i = 0; i < STAGES; ++i) {
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], 1);
@@ -1086,9 +1091,31 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
                      "r"(TMEM_ALLOC));
     }
+    if (threadIdx.x == 0 && p.stamps) p.stamps[2 * blockIdx.x + 1] = gtimer();
 }
 
 // ---------------------------------------------------------------- host side
+// Launch-duration stamps (omCudaConvStamps): while a device has a stamp buffer, every
+// conv_tc_kernel launch on it takes one start/end pair per CTA from the buffer, in launch
+// order, and the host keeps each launch's (first pair, CTA count). A launch captured into a CUDA
+// graph keeps its slots, so every replay rewrites them.
+struct StampState {
+    unsigned long long* buf = nullptr;
+    int capacity = 0;  // CTA pairs
+    int cursor = 0;
+    std::vector<std::pair<int, int>> launches;
+};
+static StampState g_stamps[64];
+
+static unsigned long long* take_stamps(int dev, int ctas) {
+    StampState& s = g_stamps[dev];
+    if (!s.buf || s.cursor + ctas > s.capacity) return nullptr;
+    unsigned long long* out = s.buf + 2 * (size_t)s.cursor;
+    s.launches.emplace_back(s.cursor, ctas);
+    s.cursor += ctas;
+    return out;
+}
+
 static PFN_cuTensorMapEncodeTiled_v12000 g_encode_tiled = nullptr;
 static PFN_cuTensorMapEncodeIm2col_v12000 g_encode_im2col = nullptr;
 static int g_driver_version = 0;
@@ -1139,7 +1166,9 @@ static int launch(DeviceCtx* c, const CUtensorMap& ta, const CUtensorMap& tb,
     const int tiles = p.num_m_tiles * p.num_n_tiles;
     const int slots = OCC * c->num_sms;
     const int grid = tiles < slots ? tiles : slots;
-    kern<<<grid, cta_threads<MODE, EW>(), Cf::SMEM_BYTES, c->compute>>>(ta, tb, to, tr, p);
+    Params q = p;
+    q.stamps = take_stamps(c->device, grid);
+    kern<<<grid, cta_threads<MODE, EW>(), Cf::SMEM_BYTES, c->compute>>>(ta, tb, to, tr, q);
     return after_launch(c);
 }
 
@@ -1319,6 +1348,29 @@ extern "C" int omCudaConvTilePlan(int nBatch, int nH, int nW, int nCs, int nCout
     return OM_OK;
 }
 
+extern "C" int omCudaConvStamps(unsigned long long* pStamps, int nCapacity) {
+    OMB_CTX_OR_FAIL(c);
+    if (pStamps && nCapacity <= 0) return OM_ERR_INVALID;
+    omb::tc::StampState& s = omb::tc::g_stamps[c->device];
+    s.buf = pStamps;
+    s.capacity = pStamps ? nCapacity : 0;
+    s.cursor = 0;
+    s.launches.clear();
+    return OM_OK;
+}
+
+extern "C" int omCudaConvStampLaunches(int* pFirst, int* pCtas, int nMax, int* pCount) {
+    OMB_CTX_OR_FAIL(c);
+    if (!pCount || nMax < 0 || (nMax > 0 && (!pFirst || !pCtas))) return OM_ERR_INVALID;
+    const auto& l = omb::tc::g_stamps[c->device].launches;
+    *pCount = (int)l.size();
+    for (int i = 0; i < nMax && i < (int)l.size(); ++i) {
+        pFirst[i] = l[i].first;
+        pCtas[i] = l[i].second;
+    }
+    return OM_OK;
+}
+
 extern "C" int omCudaConv2dBnAct(const void* pInput, const void* pPacked, const float* pBias,
                                  const void* pResidual, void* pOutput, int nBatch, int nH, int nW,
                                  int nCs, int nCout, int nKH, int nKW, int nStride, int nPad,
@@ -1445,8 +1497,14 @@ static bool stem_geom(int nCin, int nH, int nW, int nKH, int nKW, int nStride, i
 
 // One thread per space-to-depth pixel (n, u, v): 16 channels, two 16-byte stores. F (the
 // stride) is a template parameter so the channel decomposition is resolved at compile time.
-template <typename T, int F>
-__global__ void stem_s2d_kernel(const float* __restrict__ x, T* __restrict__ out, int N, int C,
+// The source image is NCHW fp32, or NCHW in the conv's own 16-bit type (S = T: the copy then
+// moves the values unchanged, so a 16-bit image gives the same bits as its fp32 form).
+__device__ __forceinline__ float stem_src_f(float v) { return v; }
+__device__ __forceinline__ float stem_src_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ float stem_src_f(__half v) { return __half2float(v); }
+
+template <typename T, int F, typename S = float>
+__global__ void stem_s2d_kernel(const S* __restrict__ x, T* __restrict__ out, int N, int C,
                                 int H, int W, int Hs, int Ws, int pad) {
     using H16 = Half16<std::is_same<T, __half>::value ? OM_DTYPE_F16 : OM_DTYPE_BF16>;
     constexpr int CMAX = 16 / (F * F);
@@ -1465,12 +1523,12 @@ __global__ void stem_s2d_kernel(const float* __restrict__ x, T* __restrict__ out
             for (int py = 0; py < F; ++py) {
                 const int yy = F * u + py - pad;
                 const bool row_ok = c < C && yy >= 0 && yy < H;
-                const float* src = x + (((long long)n * C + (row_ok ? c : 0)) * H + (row_ok ? yy : 0)) * W;
+                const S* src = x + (((long long)n * C + (row_ok ? c : 0)) * H + (row_ok ? yy : 0)) * W;
 #pragma unroll
                 for (int px = 0; px < F; ++px) {
                     const int xx = F * v + px - pad;
                     vals[(c * F + py) * F + px] =
-                        (row_ok && xx >= 0 && xx < W) ? __ldg(src + xx) : 0.f;
+                        (row_ok && xx >= 0 && xx < W) ? stem_src_f(__ldg(src + xx)) : 0.f;
                 }
             }
         }
@@ -1505,10 +1563,30 @@ extern "C" long long omCudaStemWorkspaceBytes(int nBatch, int nCin, int nH, int 
     return (long long)nBatch * g.Hs * g.Ws * 16 * 2;
 }
 
+static int stem_conv(const void* pInput, int nInDtype, void* pWorkspace, const void* pPacked,
+                     const float* pBias, void* pOutput, int nBatch, int nCin, int nH, int nW,
+                     int nCout, int nKH, int nKW, int nStride, int nPad, int nAct, int nDtype);
+
 extern "C" int omCudaStemConvBnAct(const float* pInput, void* pWorkspace, const void* pPacked,
                                    const float* pBias, void* pOutput, int nBatch, int nCin, int nH,
                                    int nW, int nCout, int nKH, int nKW, int nStride, int nPad,
                                    int nAct, int nDtype) {
+    return stem_conv(pInput, OM_DTYPE_F32, pWorkspace, pPacked, pBias, pOutput, nBatch, nCin, nH,
+                     nW, nCout, nKH, nKW, nStride, nPad, nAct, nDtype);
+}
+
+extern "C" int omCudaStemConvBnActIn(const void* pInput, int nInDtype, void* pWorkspace,
+                                     const void* pPacked, const float* pBias, void* pOutput,
+                                     int nBatch, int nCin, int nH, int nW, int nCout, int nKH,
+                                     int nKW, int nStride, int nPad, int nAct, int nDtype) {
+    if (nInDtype != OM_DTYPE_F32 && nInDtype != nDtype) return OM_ERR_UNSUPPORTED;
+    return stem_conv(pInput, nInDtype, pWorkspace, pPacked, pBias, pOutput, nBatch, nCin, nH, nW,
+                     nCout, nKH, nKW, nStride, nPad, nAct, nDtype);
+}
+
+static int stem_conv(const void* pInput, int nInDtype, void* pWorkspace, const void* pPacked,
+                     const float* pBias, void* pOutput, int nBatch, int nCin, int nH, int nW,
+                     int nCout, int nKH, int nKW, int nStride, int nPad, int nAct, int nDtype) {
     OMB_CTX_OR_FAIL(c);
     using namespace omb::tc;
     if (!pInput || !pWorkspace || !pPacked || !pOutput) return OM_ERR_INVALID;
@@ -1532,8 +1610,14 @@ extern "C" int omCudaStemConvBnAct(const float* pInput, void* pWorkspace, const 
         const int grid = (int)(blocks < 8LL * c->num_sms ? blocks : 8LL * c->num_sms);
         auto launch_s2d = [&](auto tag, auto f) {
             using T = decltype(tag);
-            stem_s2d_kernel<T, decltype(f)::value><<<grid, 256, 0, c->compute>>>(
-                pInput, static_cast<T*>(pWorkspace), nBatch, nCin, nH, nW, g.Hs, g.Ws, nPad);
+            if (nInDtype == OM_DTYPE_F32)
+                stem_s2d_kernel<T, decltype(f)::value, float><<<grid, 256, 0, c->compute>>>(
+                    static_cast<const float*>(pInput), static_cast<T*>(pWorkspace), nBatch, nCin,
+                    nH, nW, g.Hs, g.Ws, nPad);
+            else
+                stem_s2d_kernel<T, decltype(f)::value, T><<<grid, 256, 0, c->compute>>>(
+                    static_cast<const T*>(pInput), static_cast<T*>(pWorkspace), nBatch, nCin, nH,
+                    nW, g.Hs, g.Ws, nPad);
         };
         using F1 = std::integral_constant<int, 1>;
         using F2 = std::integral_constant<int, 2>;

@@ -40,15 +40,29 @@ def stored_channels(c: int) -> int:
     return int(lib.omCudaStoredChannels(c))
 
 
+def to_bf16_bits(x: np.ndarray) -> np.ndarray:
+    """fp32 -> bf16 (round to nearest even, as __float2bfloat16_rn), as uint16 bit patterns;
+    NaN is not expected in images."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32)
+    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+
+
 class InferencePlan:
     """Fused NHWC inference of a :class:`NetSpec` at a fixed batch size."""
 
     def __init__(self, net: NetSpec, weights: Dict[str, np.ndarray], batch: int,
-                 dtype: int = DTYPE_BF16, h: int = 224, w: int = 224, input_slots: int = 2):
+                 dtype: int = DTYPE_BF16, h: int = 224, w: int = 224, input_slots: int = 2,
+                 input_dtype: int = DTYPE_F32):
+        """input_dtype: element type of the NCHW image the plan takes, fp32 (the engine's
+        tensors) or the plan's own 16-bit dtype (half the bytes per image to copy to the
+        device; the stem rounds its input to that type anyway, so the logits are the same)."""
         assert dtype in (DTYPE_BF16, DTYPE_F16)
         if input_slots not in (1, 2):
             raise ValueError("input_slots must be 1 or 2")
+        if input_dtype not in (DTYPE_F32, dtype):
+            raise ValueError("input_dtype must be fp32 or the plan's dtype")
         self.net, self.batch, self.dtype, self.h, self.w = net, batch, dtype, h, w
+        self.input_dtype = input_dtype
         self.ops: List = []           # callables, each issuing one C-ABI launch
         self.keep: List[DeviceBuffer] = []
         self.graphs: List[int] = []   # one captured graph per input slot
@@ -59,7 +73,7 @@ class InferencePlan:
         self.meta: List[dict] = []         # one descriptor per op (kind, buffers, shape)
         # input staging: NCHW fp32 as the engine hands it over. With two slots the next batch's
         # host->device copy lands in one slot while the forward reads the other (serve()).
-        self.in_bytes = batch * 3 * h * w * 4
+        self.in_bytes = batch * 3 * h * w * (4 if input_dtype == DTYPE_F32 else 2)
         self.inputs = [self._buf(self.in_bytes) for _ in range(input_slots)]
         self.in_f32 = self.inputs[0]
         self._slot = 0                # the slot the stem reads when ops are issued
@@ -69,6 +83,8 @@ class InferencePlan:
         for i, cv in enumerate(net.stem):
             if i == 0 and cv.k <= 8 and cv.groups == 1:
                 cur, hh, ww, c = self._stem(cv, weights, hh, ww, act0)
+            elif i == 0 and input_dtype != DTYPE_F32:
+                raise ValueError("a 16-bit input needs the image-stem kernel")
             else:
                 cur, hh, ww, c = self._conv(cv, weights, cur, hh, ww, c, act0)
         if net.maxpool:
@@ -179,13 +195,15 @@ class InferencePlan:
         out = self._buf(n * p * q * cv.cout * 2)
         ws = self._buf(int(lib.omCudaStemWorkspaceBytes(n, cv.cin, hh, ww, cv.k, cv.k, cv.stride,
                                                         cv.pad)))
+        esize = 4 if self.input_dtype == DTYPE_F32 else 2
         for x in self.inputs:
-            self._need(x, n * cv.cin * hh * ww * 4)
+            self._need(x, n * cv.cin * hh * ww * esize)
         # The input pointer is the one op argument looked up when the op is issued: the slot
         # being captured or launched (every other argument is bound here).
+        idt = self.input_dtype
         self._op(lambda out=out, ws=ws: call(
-            "omCudaStemConvBnAct", self.inputs[self._slot].ptr, ws.ptr, packed.ptr, bias.ptr,
-            out.ptr, n, cv.cin, hh, ww, cv.cout, cv.k, cv.k, cv.stride, cv.pad, act, dt),
+            "omCudaStemConvBnActIn", self.inputs[self._slot].ptr, idt, ws.ptr, packed.ptr,
+            bias.ptr, out.ptr, n, cv.cin, hh, ww, cv.cout, cv.k, cv.k, cv.stride, cv.pad, act, dt),
             dict(kind="stem", inp=self.in_f32, out=out, w=weights[cv.name + ".weight"],
                  bn=self._bn_params(weights, cv.bn), c=cv.cin, k=cv.cout, ks=cv.k,
                  stride=cv.stride, pad=cv.pad, act=act, h=hh, wd=ww, p=p, q=q))
@@ -279,9 +297,18 @@ class InferencePlan:
             self.graphs.append(g.value)
         self._slot = 0
 
-    def set_input(self, x: np.ndarray, slot: int = 0) -> None:
+    def host_input(self, x: np.ndarray) -> np.ndarray:
+        """The NCHW image in the plan's input_dtype, as bytes to copy to the device."""
         assert x.shape == (self.batch, 3, self.h, self.w)
-        self.inputs[slot].upload(np.ascontiguousarray(x, dtype=np.float32))
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        if self.input_dtype == DTYPE_F32:
+            return x
+        if self.input_dtype == DTYPE_F16:
+            return x.astype(np.float16)
+        return to_bf16_bits(x)
+
+    def set_input(self, x: np.ndarray, slot: int = 0) -> None:
+        self.inputs[slot].upload(self.host_input(x))
 
     def run(self, x: np.ndarray) -> np.ndarray:
         """Host NCHW fp32 input -> host fp32 logits [N, classes]."""

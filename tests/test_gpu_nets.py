@@ -69,6 +69,48 @@ def test_resnet50_bf16_batch256_matches_oracle_on_subset(gpu):
     assert np.array_equal(got[idx].argmax(1), want.argmax(1))
 
 
+@pytest.mark.parametrize("name,dtype", [("resnet50", "bf16"), ("mobilenet", "f16")])
+def test_16bit_input_gives_the_same_logits(gpu, name, dtype):
+    """A plan that takes its NCHW image in its own 16-bit type (input_dtype; half the bytes to
+    copy to the device) gives bit for bit the logits of the fp32-input plan on the same image
+    rounded to that type: the stem rounds its fp32 input to the 16-bit type anyway. Also
+    checked through serve() (the copies on the transfer stream)."""
+    import ctypes
+    from omnimatchdeeplearningtool_b200 import _lib, synth
+    from omnimatchdeeplearningtool_b200._lib import call
+    from omnimatchdeeplearningtool_b200.plan import InferencePlan
+    net = synth.mobilenet_spec() if name == "mobilenet" else synth.resnet_spec(50)
+    w = synth.make_weights(net)
+    dt = _lib.DTYPE_BF16 if dtype == "bf16" else _lib.DTYPE_F16
+    x = synth.normal_input(4, seed=9)
+    p32 = InferencePlan(net, w, batch=4, dtype=dt)
+    p16 = InferencePlan(net, w, batch=4, dtype=dt, input_dtype=dt)
+    hin = hout = None
+    try:
+        assert p16.in_bytes * 2 == p32.in_bytes
+        want = p32.run(x)
+        got = p16.run(x)
+        assert np.array_equal(got, want)
+        p16.capture()
+        h = ctypes.c_void_p()
+        call("omCudaMallocHost", ctypes.byref(h), p16.in_bytes)
+        hin = h.value
+        ctypes.memmove(hin, p16.host_input(x).ctypes.data, p16.in_bytes)
+        o = ctypes.c_void_p()
+        call("omCudaMallocHost", ctypes.byref(o), want.nbytes)
+        hout = o.value
+        p16.serve([hin], [hout])
+        call("omCudaSynchronize")
+        served = np.frombuffer(ctypes.string_at(hout, want.nbytes), np.float32).reshape(want.shape)
+        assert np.array_equal(served, want)
+    finally:
+        p32.close()
+        p16.close()
+        for ptr in (hin, hout):
+            if ptr:
+                call("omCudaFreeHost", ptr)
+
+
 @pytest.mark.parametrize("slots", [1, 2])
 def test_serve_pipeline_matches_run(gpu, slots):
     """InferencePlan.serve (copies on the transfer stream, two input slots, one graph each)
