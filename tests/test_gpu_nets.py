@@ -95,7 +95,8 @@ def test_16bit_input_gives_the_same_logits(gpu, name, dtype):
         h = ctypes.c_void_p()
         call("omCudaMallocHost", ctypes.byref(h), p16.in_bytes)
         hin = h.value
-        ctypes.memmove(hin, p16.host_input(x).ctypes.data, p16.in_bytes)
+        src = p16.host_input(x)   # kept alive while it is copied
+        ctypes.memmove(hin, src.ctypes.data, p16.in_bytes)
         o = ctypes.c_void_p()
         call("omCudaMallocHost", ctypes.byref(o), want.nbytes)
         hout = o.value
