@@ -218,6 +218,13 @@ int omCudaCrossEntropy(const float* pSoftmax, const float* pTarget, float* pResu
                        int nClasses);                                            /* replaces :3973 */
 int omCudaSoftmaxCrossEntropyBackward(const float* pSoftmax, const float* pTarget,
                                       float* pGradLogits, int nBatch, int nClasses); /* :2539 */
+/* new: softmax (:1387), cross-entropy (:3934) and its gradient (:2539) in one pass over the
+ * logits, with the CPU backend's semantics: pSoftmax (may be NULL) = softmax(logits), *pLoss
+ * (device) = -sum over targets > 0.5 of log(max(p, 1e-7)) / nBatch, pGradLogits = (p - t) /
+ * nBatch. The loss is summed in a fixed order (deterministic) through a per-device array that
+ * every call shares: two calls on one device must not overlap. nBatch <= 65536. */
+int omCudaSoftmaxCrossEntropyFused(const float* pLogits, const float* pTarget, float* pSoftmax,
+                                   float* pGradLogits, float* pLoss, int nBatch, int nClasses);
 /* v = m*v + g; p -= lr*v (m == 0 or pVelocity == NULL: p -= lr*g) */
 int omCudaSgdStep(float* pParam, const float* pGrad, float* pVelocity, int nCount, float fLr,
                   float fMomentum);                                              /* replaces :2511 */

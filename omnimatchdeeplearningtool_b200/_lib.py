@@ -102,7 +102,8 @@ _SIGS = {
     "omCudaAddBias": [P, P, P, I, I, I], "omCudaAddBiasBackward": [P, P, I, I, I],
     "omCudaSoftmax": [P, P, I, I], "omCudaCrossEntropy": [P, P, P, I, I],
     "omCudaSoftmaxCrossEntropyBackward": [P, P, P, I, I],
-    "omCudaSgdStepScaled": [P, P, P, I, F, F, F], "omCudaSgdStep": [P, P, P, I, F, F],
+    "omCudaSgdStepScaled": [P, P, P, I, F, F, F],
+    "omCudaSoftmaxCrossEntropyFused": [P, P, P, P, P, I, I], "omCudaSgdStep": [P, P, P, I, F, F],
     "omCudaAdamStep": [P, P, P, P, I, F, F, F, F, I],
     "omCudaGradNormClip": [P, I, F, F, P], "omCudaSgdStepGuarded": [P, P, P, I, F, F, P],
     # further elementwise ops and activations

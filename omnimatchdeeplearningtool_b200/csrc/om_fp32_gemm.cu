@@ -230,6 +230,15 @@ extern "C" int omCudaMatmul(const float* pA, const float* pB, float* pC, int nM,
     OMB_CTX_OR_FAIL(c);
     if (!pA || !pB || !pC || nM < 0 || nK < 0 || nN < 0) return OM_ERR_INVALID;
     if (nK == 0) return omb::status_of(cudaMemsetAsync(pC, 0, sizeof(float) * (size_t)nM * nN, c->compute));
+    // Tensor cores (3xTF32) first: C = A . B is the 1x1 convolution of the NCHW "image" A
+    // [M, K, 1, 1] with the filter B^T, which the pack step takes transposed from B [K, N] (its
+    // flip mode, a 180-degree turn of a 1x1 filter being the identity); the result is NCHW
+    // [M, N, 1, 1] = C. The SIMT kernel covers what that path does not take.
+    if (nM > 0 && nN > 0) {
+        int st = omb::tc::tf32_conv(c, pA, nM, nK, 1, 1, 1, 1, 0, 0, 1, pB, nN, 1, 1, true, nN,
+                                    nullptr, pC, 1, 0);
+        if (st != OM_ERR_UNSUPPORTED && st != OM_ERR_OOM) return st;
+    }
     MatmulOp op{pA, pB, pC, nK, nN};
     return run_gemm(c, op, nM, nN, nK, 1);
 }

@@ -387,6 +387,67 @@ __global__ void ce_softmax_bwd_kernel(const float* __restrict__ p, const float* 
         g[i] = (p[i] - t[i]) * scale;
 }
 
+// Softmax, cross-entropy and its gradient in one pass over the logits (the three reference
+// kernels cuda_kernels.cu:1387, :3934 and :2539 with the CPU backend's semantics: divide by the
+// sum, loss = -sum over targets > 0.5 of log(max(p, 1e-7)) / N, grad = (p - t) / N). One warp
+// per row, 8 rows per block; each block adds its rows' losses in row order into a per-block
+// partial, and the last block to finish adds the partials in block order (deterministic).
+namespace sce {
+constexpr int kRows = 8;
+constexpr int kMaxBlocks = 8192;   // 65536 rows
+__device__ float g_part[kMaxBlocks];
+__device__ unsigned int g_ticket;  // zero between calls: the last block resets it
+}  // namespace sce
+
+__global__ void __launch_bounds__(256) softmax_ce_fused_kernel(
+    const float* __restrict__ x, const float* __restrict__ t, float* __restrict__ prob,
+    float* __restrict__ grad, float* __restrict__ loss, int N, int C, float invN) {
+    __shared__ float rowloss[sce::kRows];
+    __shared__ int is_last;
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const long long row = (long long)blockIdx.x * sce::kRows + w;
+    float rl = 0.f;
+    if (row < N) {
+        const float* xr = x + row * C;
+        const float* tr = t + row * C;
+        float m = -INFINITY;
+        for (int j = lane; j < C; j += 32) m = fmaxf(m, xr[j]);
+        for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        float s = 0.f;
+        for (int j = lane; j < C; j += 32) s += expf(xr[j] - m);
+        for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        const float inv = 1.f / s;
+        for (int j = lane; j < C; j += 32) {
+            const float p = expf(xr[j] - m) * inv;
+            const float tj = tr[j];
+            if (prob) prob[row * C + j] = p;
+            grad[row * C + j] = (p - tj) * invN;
+            if (tj > 0.5f) rl -= logf(fmaxf(p, 1e-7f));
+        }
+        for (int o = 16; o; o >>= 1) rl += __shfl_xor_sync(0xffffffffu, rl, o);
+    }
+    if (lane == 0) rowloss[w] = rl;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float b = 0.f;
+        for (int i = 0; i < sce::kRows; ++i) b += rowloss[i];
+        sce::g_part[blockIdx.x] = b;
+        __threadfence();
+        is_last = atomicAdd(&sce::g_ticket, 1u) == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (is_last && w == 0) {
+        __threadfence();
+        float v = 0.f;
+        for (int b = lane; b < (int)gridDim.x; b += 32) v += __ldcg(&sce::g_part[b]);
+        for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (lane == 0) {
+            *loss = v * invN;
+            sce::g_ticket = 0;
+        }
+    }
+}
+
 // ---------------------------------------------------------------- optimiser, elementwise
 // status (nullable): the gradient guard's verdict; status[1] == 0 skips the step
 // gs scales the gradient first (1/world after a summing all-reduce; exactly 1 otherwise)
@@ -760,6 +821,19 @@ extern "C" int omCudaCrossEntropy(const float* pSoftmax, const float* pTarget, f
     if (!pSoftmax || !pTarget || !pResult || nBatch <= 0) return OM_ERR_INVALID;
     cross_entropy_kernel<<<1, 1024, 0, c->compute>>>(pSoftmax, pTarget, pResult,
                                                      (long long)nBatch * nClasses, nBatch);
+    return after_launch(c);
+}
+
+extern "C" int omCudaSoftmaxCrossEntropyFused(const float* pLogits, const float* pTarget,
+                                              float* pSoftmax, float* pGradLogits, float* pLoss,
+                                              int nBatch, int nClasses) {
+    OMB_CTX_OR_FAIL(c);
+    if (!pLogits || !pTarget || !pGradLogits || !pLoss || nBatch <= 0 || nClasses <= 0)
+        return OM_ERR_INVALID;
+    const long long blocks = ((long long)nBatch + sce::kRows - 1) / sce::kRows;
+    if (blocks > sce::kMaxBlocks) return OM_ERR_UNSUPPORTED;
+    softmax_ce_fused_kernel<<<(int)blocks, 32 * sce::kRows, 0, c->compute>>>(
+        pLogits, pTarget, pSoftmax, pGradLogits, pLoss, nBatch, nClasses, 1.f / (float)nBatch);
     return after_launch(c);
 }
 

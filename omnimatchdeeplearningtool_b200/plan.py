@@ -525,13 +525,13 @@ class Fp32Net:
         recs, blocks, feat, c, hh, ww = (st[k] for k in ("recs", "blocks", "feat", "c", "hh", "ww"))
         pc, ph, pw, P, idx = st["pool"]
         logits_b = self.logits
-        prob = self._buf("prob", n * K * 4)
-        B.softmax(logits_b.ptr, prob.ptr, n, K)
-        B.crossEntropyForward(prob.ptr, onehot_ptr, loss_ptr, n, K)
+        # softmax, loss and the logits' gradient in one pass (omCudaSoftmaxCrossEntropyFused:
+        # the reference's softmax, crossEntropy and crossEntropySoftmaxBackward)
+        dlog = self._buf("dlogits", n * K * 4)
+        call("omCudaSoftmaxCrossEntropyFused", logits_b.ptr, onehot_ptr, None, dlog.ptr,
+             loss_ptr, n, K)
 
         # ---------------------------------------------------------------- backward
-        dlog = self._buf("dlogits", n * K * 4)
-        B.crossEntropySoftmaxBackward(prob.ptr, onehot_ptr, dlog.ptr, n, K)
         featT = self._buf("featT", n * c * 4)
         B.transpose(feat.ptr, featT.ptr, n, c)
         B.matmul(featT.ptr, dlog.ptr, self.grad("fc.weight"), c, n, K)

@@ -365,3 +365,57 @@ def test_elementwise_and_bias(gpu):
     t = _out((1003,))
     B.transpose(_dev(x[:1000].reshape(20, 50)).ptr, t.ptr, 20, 50)
     assert np.array_equal(t.to_numpy((50, 20)), x[:1000].reshape(20, 50).T)
+
+
+@pytest.mark.parametrize("n,k", [(8, 1000), (130, 1000), (1, 10), (4, 37)])
+def test_softmax_ce_fused(gpu, n, k):
+    """omCudaSoftmaxCrossEntropyFused against the three reference-named kernels it replaces
+    (the softmax and the gradient bit for bit, the loss to summation order) and against the
+    oracle (1e-4); two calls in a row, so the last-block ticket is seen to reset."""
+    import oracle as orc
+    from omnimatchdeeplearningtool_b200._lib import call
+    from omnimatchdeeplearningtool_b200.backend import CUDABackend as B
+    rng = _rng(31 + n)
+    for rep in range(2):
+        logits = (rng.standard_normal((n, k)) * 3).astype(np.float32)
+        oh = np.zeros((n, k), np.float32)
+        oh[np.arange(n), rng.integers(0, k, n)] = 1
+        dL, dT = _dev(logits), _dev(oh)
+        p, g, loss = _out((n, k)), _out((n, k)), _out((1,))
+        call("omCudaSoftmaxCrossEntropyFused", dL.ptr, dT.ptr, p.ptr, g.ptr, loss.ptr, n, k)
+        p2, g2, loss2 = _out((n, k)), _out((n, k)), _out((1,))
+        B.softmax(dL.ptr, p2.ptr, n, k)
+        B.crossEntropyForward(p2.ptr, dT.ptr, loss2.ptr, n, k)
+        B.crossEntropySoftmaxBackward(p2.ptr, dT.ptr, g2.ptr, n, k)
+        assert np.array_equal(p.to_numpy((n, k)), p2.to_numpy((n, k)))
+        assert np.array_equal(g.to_numpy((n, k)), g2.to_numpy((n, k)))
+        lv, lv2 = float(loss.to_numpy((1,))[0]), float(loss2.to_numpy((1,))[0])
+        assert abs(lv - lv2) <= 1e-6 * abs(lv2)
+        wp = np.empty_like(logits)
+        orc.O.oracle_softmax(logits.ctypes.data, wp.ctypes.data, n, k)
+        wl = orc.O.oracle_cross_entropy(wp.ctypes.data, oh.ctypes.data, n, k)
+        assert abs(lv - wl) <= TOL * abs(wl)
+        # without the softmax output
+        g3, loss3 = _out((n, k)), _out((1,))
+        call("omCudaSoftmaxCrossEntropyFused", dL.ptr, dT.ptr, None, g3.ptr, loss3.ptr, n, k)
+        assert np.array_equal(g3.to_numpy((n, k)), g2.to_numpy((n, k)))
+        assert float(loss3.to_numpy((1,))[0]) == lv
+
+
+@pytest.mark.parametrize("m,kk,n", [(128, 512, 1000), (512, 128, 1000), (128, 1000, 512),
+                                    (8, 2048, 1000), (1, 3, 1), (33, 7, 65), (70000, 8, 16)])
+def test_matmul_shapes(gpu, m, kk, n):
+    """omCudaMatmul (cuda_kernels.cu:768) on the training path's FC shapes (forward, weight and
+    input gradients of 512 -> 1000 at batch 128) through the 3xTF32 tensor-core path, tiny and
+    ragged shapes, and M > 65535 (the SIMT kernel), against the oracle's matmul (1e-4)."""
+    import oracle as orc
+    from omnimatchdeeplearningtool_b200.backend import CUDABackend as B
+    rng = _rng(m + kk + n)
+    a = rng.standard_normal((m, kk)).astype(np.float32)
+    bm = rng.standard_normal((kk, n)).astype(np.float32)
+    c = _out((m, n))
+    B.matmul(_dev(a).ptr, _dev(bm).ptr, c.ptr, m, kk, n)
+    wc = np.empty((m, n), np.float32)
+    orc.O.oracle_matmul(a.ctypes.data, bm.ctypes.data, wc.ctypes.data, m, kk, n)
+    assert rel_err_floor(c.to_numpy((m, n)), wc) <= TOL
+    assert gpu.kernel_error() == 0
