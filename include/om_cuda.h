@@ -99,6 +99,14 @@ int omCudaStridedCopy(const float* pSrc, float* pDst, const int* pShape, const i
 /* new: read and clear the device error word that bounded in-kernel waits set; *pCode is 0
  * when no kernel gave up since the last call. Synchronises the compute stream. */
 int omCudaGetKernelError(unsigned int* pCode);
+/* new: wait for the compute stream, then OM_ERR_KERNEL_TIMEOUT if a bounded in-kernel wait gave
+ * up since the last check (the error word is read and cleared), else OM_OK */
+int omCudaSynchronizeChecked(void);
+/* new, for tests of the bounded waits: the next tensor-core conv launch on the calling thread's
+ * device gets role waits limited to nWaitNs (1 ms .. 2 s) and a producer that stops issuing
+ * loads after nLoadsBeforeStall of them, so the MMA issuer waits for a load that never comes
+ * and gives up; every load issued has landed before the kernel exits. One launch only. */
+int omCudaTestStallNextConv(long long nLoadsBeforeStall, unsigned long long nWaitNs);
 /* new: number of kernels this library has launched on the calling thread's device */
 int omCudaGetLaunchCount(unsigned long long* pCount);
 

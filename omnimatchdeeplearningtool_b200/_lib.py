@@ -69,6 +69,7 @@ _SIGS = {
     "omCudaGraphLaunch": [P], "omCudaGraphDestroy": [P],
     "omCudaGetKernelError": [POINTER(c_uint)], "omCudaGetLaunchCount": [POINTER(c_ulonglong)],
     "omCudaGetCurrentDevice": [],
+    "omCudaSynchronizeChecked": [], "omCudaTestStallNextConv": [c_longlong, c_ulonglong],
     # data-parallel gradient exchange
     "omNcclGetUniqueId": [P], "omNcclInit": [I, I, P, I],
     "omCudaAllreduceAsync": [P, c_longlong, I], "omCudaAllreduceJoin": [],

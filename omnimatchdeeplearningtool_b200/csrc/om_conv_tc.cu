@@ -116,6 +116,11 @@ struct Params {
     unsigned int* err;
     // optional (nullptr: off): %globaltimer at each CTA's start and end, stamps[2*cta + 0/1]
     unsigned long long* stamps;
+    // limit of the role waits (OMB_WAIT_NS unless a test shortens it), and the test-only stall:
+    // the producer stops issuing loads after `stall_after` of them (-1: never), which leaves
+    // the MMA issuer waiting for a load that nothing will bring (omCudaTestStallNextConv)
+    unsigned long long wait_ns;
+    long long stall_after;
 };
 
 // MODE_SW32: filter taps in k-block kb (4, or what is left of the R*S taps in the last one)
@@ -158,13 +163,14 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Bounded wait for the phase with the given parity to complete. Returns false when it gave
 // up, either on its own timeout or because another role raised the abort flag.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
-                                          volatile int* abort_flag) {
+                                          volatile int* abort_flag,
+                                          unsigned long long limit_ns = OMB_WAIT_NS) {
     if (mbar_try_wait(bar, parity)) return true;
     unsigned long long t0 = gtimer();
     while (true) {
         if (mbar_try_wait(bar, parity)) return true;
         if (*abort_flag) return false;
-        if (gtimer() - t0 > OMB_WAIT_NS) return false;
+        if (gtimer() - t0 > limit_ns) return false;
     }
 }
 // Bounded wait used on exit paths (no abort flag: it must not give up early).
@@ -498,7 +504,7 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
                 int pb = 0;
                 uint32_t pph = 0;
                 for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-                    if (!mbar_wait(&patch_empty[pb], pph ^ 1, abort_flag)) {
+                    if (!mbar_wait(&patch_empty[pb], pph ^ 1, abort_flag, p.wait_ns)) {
                         ok = false;
                         break;
                     }
@@ -516,7 +522,8 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
                     }
                 }
             }
-            for (int tile = blockIdx.x; tile < num_tiles && ok && MODE != MODE_STEM;
+            bool stalled = false;
+            for (int tile = blockIdx.x; tile < num_tiles && ok && !stalled && MODE != MODE_STEM;
                  tile += gridDim.x) {
                 const int m_tile = tile / p.num_n_tiles;
                 const int n_tile = tile - m_tile * p.num_n_tiles;
@@ -541,7 +548,11 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
                 }
                 int c0 = 0, fs = 0, fr = 0;   // MODE_SW128: channel slice and filter tap of kb
                 for (int kb = 0; kb < p.num_kb; ++kb) {
-                    if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag)) {
+                    if (issued == p.stall_after) {  // test-only: stop with every load landed
+                        stalled = true;
+                        break;
+                    }
+                    if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.wait_ns)) {
                         ok = false;
                         break;
                     }
@@ -674,7 +685,7 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
                 // operand is the 128 consecutive 32-byte patch rows from r * box_w + s on, read in
                 // place (32-byte swizzle; the descriptor may start on any row, the swizzle follows
                 // the address bits). B k-block t / 4, K step t % 4, resident.
-                ok = mbar_wait(&full[0], 0, abort_flag);
+                ok = mbar_wait(&full[0], 0, abort_flag, p.wait_ns);
                 const uint32_t patch0 = smem_u32(sExtra);
                 const int taps = p.R * p.S;
                 int pb = 0;
@@ -682,8 +693,8 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
                 for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
                     const int acc = local & 1;
                     const uint32_t par = (uint32_t)((local >> 1) & 1);
-                    if (!mbar_wait(&tempty[acc], par ^ 1, abort_flag) ||
-                        !mbar_wait(&patch_full[pb], pph, abort_flag)) {
+                    if (!mbar_wait(&tempty[acc], par ^ 1, abort_flag, p.wait_ns) ||
+                        !mbar_wait(&patch_full[pb], pph, abort_flag, p.wait_ns)) {
                         ok = false;
                         break;
                     }
@@ -715,14 +726,14 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
                  tile += gridDim.x, ++local) {
                 const int acc = local & 1;
                 const uint32_t acc_phase = (uint32_t)((local >> 1) & 1);
-                if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag)) {
+                if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, p.wait_ns)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + (uint32_t)(acc * C::ACC_COLS);
                 for (int kb = 0; kb < p.num_kb; ++kb) {
-                    if (!mbar_wait(&full[stage], phase, abort_flag)) {
+                    if (!mbar_wait(&full[stage], phase, abort_flag, p.wait_ns)) {
                         ok = false;
                         break;
                     }
@@ -918,7 +929,7 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
                 const int col = nbase + (u0 % NCH) * 32 + lane;
                 bnext = (p.bias && col < p.K) ? __ldg(p.bias + col) : 0.f;
             }
-            if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) {
+            if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.wait_ns)) {
                 ok = false;
                 break;
             }
@@ -1017,7 +1028,7 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
                 }
                 uint8_t* sb = ebuf + ub * EPI_SUB_BYTES;
                 if (has_res) {
-                    if (!mbar_wait(&rbar[ub], (rph >> ub) & 1u, abort_flag)) {
+                    if (!mbar_wait(&rbar[ub], (rph >> ub) & 1u, abort_flag, p.wait_ns)) {
                         ok = false;
                         break;
                     }
@@ -1116,6 +1127,22 @@ static unsigned long long* take_stamps(int dev, int ctas) {
     return out;
 }
 
+// Test-only, one launch: the next conv_tc_kernel launch on a device gets a shortened wait
+// limit and a producer that stops after a given number of loads (omCudaTestStallNextConv).
+struct TestStall {
+    bool armed = false;
+    long long after = -1;
+    unsigned long long wait_ns = OMB_WAIT_NS;
+};
+static TestStall g_test_stall[64];
+
+static void take_test_stall(int dev, unsigned long long* wait_ns, long long* stall_after) {
+    TestStall& t = g_test_stall[dev];
+    *wait_ns = t.armed ? t.wait_ns : OMB_WAIT_NS;
+    *stall_after = t.armed ? t.after : -1;
+    t = TestStall();
+}
+
 static PFN_cuTensorMapEncodeTiled_v12000 g_encode_tiled = nullptr;
 static PFN_cuTensorMapEncodeIm2col_v12000 g_encode_im2col = nullptr;
 static int g_driver_version = 0;
@@ -1168,6 +1195,7 @@ static int launch(DeviceCtx* c, const CUtensorMap& ta, const CUtensorMap& tb,
     const int grid = tiles < slots ? tiles : slots;
     Params q = p;
     q.stamps = take_stamps(c->device, grid);
+    take_test_stall(c->device, &q.wait_ns, &q.stall_after);
     kern<<<grid, cta_threads<MODE, EW>(), Cf::SMEM_BYTES, c->compute>>>(ta, tb, to, tr, q);
     return after_launch(c);
 }
@@ -1345,6 +1373,17 @@ extern "C" int omCudaConvTilePlan(int nBatch, int nH, int nW, int nCs, int nCout
     const long long m_tiles = ((long long)nBatch * P * Q + BM - 1) / BM;
     choose_tile(nCout, (int)(kpad / BK), m_tiles, c->num_sms, mode != MODE_INTERLEAVE,
                 bResidual != 0, &pPlan[0], &pPlan[1], &pPlan[2], &pPlan[3]);
+    return OM_OK;
+}
+
+extern "C" int omCudaTestStallNextConv(long long nLoadsBeforeStall, unsigned long long nWaitNs) {
+    OMB_CTX_OR_FAIL(c);
+    if (nLoadsBeforeStall < 0 || nWaitNs < 1000000ull || nWaitNs > omb::tc::OMB_WAIT_NS)
+        return OM_ERR_INVALID;
+    omb::tc::TestStall& t = omb::tc::g_test_stall[c->device];
+    t.armed = true;
+    t.after = nLoadsBeforeStall;
+    t.wait_ns = nWaitNs;
     return OM_OK;
 }
 

@@ -282,6 +282,13 @@ int omCudaGetKernelError(unsigned int* pCode) {
     return OM_OK;
 }
 
+int omCudaSynchronizeChecked(void) {
+    unsigned int code = 0;
+    int st = omCudaGetKernelError(&code);
+    if (st != OM_OK) return st;
+    return code ? OM_ERR_KERNEL_TIMEOUT : OM_OK;
+}
+
 int omCudaGetLaunchCount(unsigned long long* pCount) {
     OMB_CTX_OR_FAIL(c);
     if (!pCount) return OM_ERR_INVALID;
