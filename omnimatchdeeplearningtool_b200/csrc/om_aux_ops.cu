@@ -548,6 +548,17 @@ extern "C" int omCudaConvTranspose2d(const float* pInput, const float* pWeight, 
     const int Ho = (nHin - 1) * nStride - 2 * nPad + nKH;
     const int Wo = (nWin - 1) * nStride - 2 * nPad + nKW;
     if (Ho <= 0 || Wo <= 0) return OM_ERR_INVALID;
+    // A transposed convolution is the input gradient of the forward convolution whose weight
+    // [K = Cin, C = Cout, KH, KW] it shares: the 3xTF32 tensor-core conv runs it as it runs
+    // omCudaConv2dBackwardInput (input zero-inserted by the stride and offset by K-1-pad, the
+    // filter transposed and turned by 180 degrees, stride 1), bias added in its epilogue. The
+    // direct kernel below covers pad > K-1 and what that path does not take.
+    if (nPad <= nKH - 1 && nPad <= nKW - 1) {
+        int st = omb::tc::tf32_conv(c, pInput, nBatch, nCin, nHin, nWin, Ho + nKH - 1,
+                                    Wo + nKW - 1, nKH - 1 - nPad, nKW - 1 - nPad, nStride, pWeight,
+                                    nCout, nKH, nKW, true, nCout, pBias, pOutput, 1, 0);
+        if (st != OM_ERR_UNSUPPORTED && st != OM_ERR_OOM) return st;
+    }
     return each(c, (long long)nBatch * nCout * Ho * Wo, [=] __device__(long long i) {
         const int ow = (int)(i % Wo);
         long long t = i / Wo;

@@ -300,8 +300,13 @@ def test_upsample_bilinear(gpu, h, w, oh, ow):
 
 @pytest.mark.parametrize("cin,h,cout,k,stride,pad,bias",
                          [(3, 5, 4, 4, 2, 1, True), (8, 7, 6, 3, 1, 1, False),
-                          (4, 6, 5, 2, 2, 0, True)])
+                          (4, 6, 5, 2, 2, 0, True),
+                          (64, 14, 32, 2, 2, 0, True),    # UNet-style 2x upsampling
+                          (48, 9, 40, 4, 2, 1, False),    # 4x4 / 2 with padding
+                          (6, 5, 7, 3, 2, 3, True)])      # pad > K-1: the direct kernel
 def test_conv_transpose2d(gpu, cin, h, cout, k, stride, pad, bias):
+    """omCudaConvTranspose2d (cuda_kernels.cu:4187) against a float64 scatter; pad <= K-1 runs
+    on the 3xTF32 tensor-core conv (the input gradient of the matching convolution)."""
     from omnimatchdeeplearningtool_b200.backend import CUDABackend as B
     rng = _rng(9 + cin)
     n, w_ = 2, h + 1

@@ -123,7 +123,8 @@ def test_classify_logits_follows_the_reference():
 @pytest.mark.gpu
 def test_multi_device_logits_match_one_plan(gpu):
     """Every visible device (one thread each) against a single plan on device 0: identical
-    logits for the same images, including a ragged last chunk."""
+    logits for the same images, including a ragged last chunk; and the images each device
+    processed against the fp32 oracle (<= 2e-2, identical top-1)."""
     from omnimatchdeeplearningtool_b200 import _lib, synth
     from omnimatchdeeplearningtool_b200.plan import InferencePlan
     ndev = _lib.lib.omCudaGetDeviceCount()
@@ -151,3 +152,10 @@ def test_multi_device_logits_match_one_plan(gpu):
     ref = serving.classify_logits(want)
     assert [r.predicted_class for r in results] == [r.predicted_class for r in ref]
     assert gpu.kernel_error() == 0
+    # and against the fp32 oracle: the first image of every device's chunks and the ragged tail
+    import oracle as orc
+    from conftest import rel_err
+    idx = sorted({i * b for i in range(len(devices))} | {n - 1})
+    want_o = orc.forward(net, w, np.ascontiguousarray(x[idx]))
+    assert rel_err(got[idx], want_o) <= 2e-2
+    assert np.array_equal(got[idx].argmax(1), want_o.argmax(1))
