@@ -590,8 +590,8 @@ def conv_stamp_profile(plan, reps: int):
 
 
 def conv_groups(plan):
-    """Label of each tensor-core op: stem, fc, 256-wide (long reductions on 256-wide tiles),
-    3x3 or 1x1 (the rest, by filter size)."""
+    """Label of each tensor-core op: stem, fc, a fused 3x3 + 1x1 pair, 256-wide (long reductions
+    on 256-wide tiles), 3x3 or 1x1 (the rest, by filter size)."""
     import ctypes
     from omnimatchdeeplearningtool_b200._lib import call
     labels = []
@@ -599,6 +599,9 @@ def conv_groups(plan):
         m = plan.meta[i]
         if m.get("kind") == "stem":
             labels.append("stem")
+            continue
+        if m.get("kind") == "pair":
+            labels.append("3x3+1x1 pair")
             continue
         if m.get("out_dtype") == 0:  # fp32 logits: the classifier
             labels.append("fc")
@@ -614,7 +617,8 @@ def conv_op_flops(plan):
     out = []
     for i in plan.tc_op_index:
         m = plan.meta[i]
-        out.append(2 * plan.batch * m["p"] * m["q"] * m["k"] * m["c"] * m["ks"] * m["ks"])
+        out.append(m["flops"] if "flops" in m else
+                   2 * plan.batch * m["p"] * m["q"] * m["k"] * m["c"] * m["ks"] * m["ks"])
     return out
 
 

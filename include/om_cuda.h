@@ -411,6 +411,20 @@ int omCudaConvStamps(unsigned long long* pStamps, int nCapacity);
 /* the launches recorded since omCudaConvStamps: first pair index and CTA count of each (up to
  * nMax of them); *pCount = number recorded */
 int omCudaConvStampLaunches(int* pFirst, int* pCtas, int nMax, int* pCount);
+/* new: a conv and the 1x1 conv after it in one kernel (a bottleneck's 3x3 and its expansion):
+ *   mid = act1(conv(in, W1') + bias1)             [N, P, Q, nMid], kept on chip in nDtype
+ *   out = act2(mid . W2' + bias2 + residual)      [N, P, Q, nCout] (residual may be NULL)
+ * in: NHWC [N, H, W, nCs]; W1' from omCudaPackConvWeight (nCs inputs, nKH x nKW), W2' from it as
+ * a 1x1 conv with nMid inputs. The intermediate map never reaches device memory; the results
+ * are those of omCudaConv2dBnAct twice (the same roundings and summation order). nCs % 64 == 0,
+ * nMid 64 or 128, nCout a multiple of 128 up to 512 (omCudaConvPairSupported). */
+int omCudaConvPairBnAct(const void* pInput, const void* pPacked1, const float* pBias1,
+                        const void* pPacked2, const float* pBias2, const void* pResidual,
+                        void* pOutput, int nBatch, int nH, int nW, int nCs, int nMid, int nCout,
+                        int nKH, int nKW, int nStride, int nPad, int nAct1, int nAct2,
+                        int nDtype);
+/* 1 when omCudaConvPairBnAct takes these channel counts and dtype, else 0 */
+int omCudaConvPairSupported(int nCs, int nMid, int nCout, int nDtype);
 /* new: the image stem (stride 1 or 2, Cin * stride^2 <= 16, Cout % 8 == 0) from the NCHW fp32
  * image: out[n,p,q,k] = act(sum_{c,r,s} x[n,c,p*st-pad+r,q*st-pad+s] * W[k,c,r,s] * scale[k]
  * + bias[k]), NHWC 16-bit output, BN folded as in omCudaPackConvWeight. A first launch writes a

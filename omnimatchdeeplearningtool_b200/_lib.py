@@ -143,6 +143,8 @@ _SIGS = {
     "omCudaPackConvWeight": [P, P, P, P, P, P, F, P, P, I, I, I, I, I, I],
     "omCudaConv2dBnAct": [P, P, P, P, P, I, I, I, I, I, I, I, I, I, I, I, I],
     "omCudaConvTilePlan": [I, I, I, I, I, I, I, I, I, I, POINTER(c_int)],
+    "omCudaConvPairBnAct": [P, P, P, P, P, P, P] + [I] * 13,
+    "omCudaConvPairSupported": [I, I, I, I],
     "omCudaConvStamps": [P, I],
     "omCudaConvStampLaunches": [POINTER(c_int), POINTER(c_int), I, POINTER(c_int)],
     "omCudaPackStemWeight": [P, P, P, P, P, P, F, P, P, I, I, I, I, I, I],

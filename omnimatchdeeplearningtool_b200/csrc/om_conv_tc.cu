@@ -1730,6 +1730,608 @@ static int stem_conv(const void* pInput, int nInDtype, void* pWorkspace, const v
     return finish_and_launch<MODE_STEM>(c, bn, occ, mt, ew, nDtype, ta, tb, p);
 }
 
+// ---------------------------------------------------------------- conv pair
+namespace omb {
+namespace tc {
+
+// A bottleneck's R x S conv (conv 1: Cs -> C1 channels, BN folded, act1) and the 1x1 expansion
+// after it (conv 2: C1 -> K2 channels, BN folded, + residual, act2) in one kernel: conv 1's
+// output tile never leaves the SM. Per 128-pixel tile:
+//   S1  conv 1's mainloop (im2col A, packed W1 B) into accumulator D1 (C1 TMEM columns, two
+//       buffers);
+//   E1  the epilogue warps read D1, add the bias, apply act1, round to 16 bits and write the
+//       tile into shared memory as conv 2's A operand (K-major, 128-byte swizzle, the layout TMA
+//       would have written), then signal the MMA warp;
+//   S2  conv 2 in 128-column chunks: A from that shared tile, B (packed W2) streamed through
+//       the same pipeline stages, into accumulator D2 (two 128-column buffers);
+//   E2  per chunk: + bias, + residual (TMA-loaded into the chunk's staging buffer ahead of
+//       time), act2, 16-bit, TMA store from the same buffer.
+// The MMA warp issues S1(t+1) before S2(t), so the tensor cores compute the next tile's conv 1
+// while the epilogue finishes this one; the epilogue runs E1(t), E2(t), E1(t+1), ... so the
+// shared A tile is rewritten only after S2(t) has completed (its last chunk's D2 is drained).
+// Only the output (and the residual) cross HBM: the intermediate C1-channel map is never
+// written, and the expansion's memory traffic overlaps conv 1's tensor-core work.
+constexpr int PAIR_BN2 = 128;                        // conv-2 columns per chunk
+constexpr int PAIR_EW = 4;                           // epilogue warps, one per TMEM lane quarter
+constexpr int PAIR_CHUNK_BYTES = BM * PAIR_BN2 * 2;  // a chunk's residual / output staging
+constexpr int PAIR_MAX_K2 = 512;
+
+struct PairParams {
+    int N, H, W, Cs;
+    int C1, K2;
+    int R, S, stride, pad;
+    int P, Q, M;
+    int num_kb1, num_tiles;
+    const float* bias1;
+    const float* bias2;
+    const void* residual;
+    int act1, act2;
+    unsigned int* err;
+    unsigned long long* stamps;
+    unsigned long long wait_ns;
+};
+
+template <int C1>
+struct PairCfg {
+    // a stage: conv-1 A (128 px x 64 ch) + a B slot of 128 rows x 64 K (conv 1 uses C1 rows)
+    static constexpr int B_SLOT = PAIR_BN2 * BK * 2;
+    static constexpr int STAGE_BYTES = A_STAGE_BYTES + B_SLOT;
+    static constexpr int A2_BYTES = BM * C1 * 2;      // conv 2's A: C1 / 64 blocks of 16 KB
+    static constexpr int RES_BUFS = 2;
+    static constexpr int RES_BYTES = RES_BUFS * PAIR_CHUNK_BYTES;
+    static constexpr int BIAS_BYTES = (C1 + PAIR_MAX_K2) * 4;
+    static constexpr int BAR_BYTES = 1024;
+    static constexpr int FIXED = A2_BYTES + RES_BYTES + BIAS_BYTES + BAR_BYTES + 1024;
+    static constexpr int STAGES_RAW = (MAX_DYN_SMEM - FIXED) / STAGE_BYTES;
+    static constexpr int STAGES = STAGES_RAW > 6 ? 6 : STAGES_RAW;
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + FIXED;
+    static constexpr int D2_BASE = 2 * C1;           // two D1 buffers, then two D2 buffers
+    static constexpr int TMEM_COLS = 512;
+    static_assert(STAGES >= 3, "pipeline depth");
+    static_assert(SMEM_BYTES <= MAX_DYN_SMEM, "shared memory budget");
+    static_assert(2 * C1 + 2 * PAIR_BN2 <= TMEM_COLS, "TMEM budget");
+    static_assert(BIAS_BYTES % 8 == 0, "barriers stay 8-byte aligned");
+};
+
+template <int C1, int DT>
+__global__ void __launch_bounds__(64 + 32 * PAIR_EW, 1)
+    conv_pair_kernel(const __grid_constant__ CUtensorMap tmA,
+                     const __grid_constant__ CUtensorMap tmB1,
+                     const __grid_constant__ CUtensorMap tmB2,
+                     const __grid_constant__ CUtensorMap tmOut,
+                     const __grid_constant__ CUtensorMap tmRes, const PairParams p) {
+    using C = PairCfg<C1>;
+    using H16 = Half16<DT>;
+    constexpr int STAGES = C::STAGES;
+    constexpr bool F16 = (DT == OM_DTYPE_F16);
+    constexpr int KB2 = C1 / BK;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint8_t* sStage = smem;
+    uint8_t* sA2 = sStage + STAGES * C::STAGE_BYTES;
+    uint8_t* sRes = sA2 + C::A2_BYTES;
+    float* sBias1 = reinterpret_cast<float*>(sRes + C::RES_BYTES);
+    float* sBias2 = sBias1 + C1;
+    uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(sBias1) + C::BIAS_BYTES);
+    uint64_t* empty = full + STAGES;
+    uint64_t* d1full = empty + STAGES;     // [2]
+    uint64_t* d1empty = d1full + 2;        // [2]
+    uint64_t* a2full = d1empty + 2;        // [1]
+    uint64_t* d2full = a2full + 1;         // [2]
+    uint64_t* d2empty = d2full + 2;        // [2]
+    uint64_t* resbar = d2empty + 2;        // [RES_BUFS][PAIR_EW]
+    uint64_t* drain = resbar + C::RES_BUFS * PAIR_EW;
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int nch2 = p.K2 / PAIR_BN2;
+
+    if (threadIdx.x == 0) {
+        if (p.stamps) p.stamps[2 * blockIdx.x] = gtimer();
+        for (int i = 0; i < STAGES; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&d1full[i], 1);
+            mbar_init(&d1empty[i], PAIR_EW);
+            mbar_init(&d2full[i], 1);
+            mbar_init(&d2empty[i], PAIR_EW);
+        }
+        mbar_init(a2full, PAIR_EW);
+        for (int i = 0; i < C::RES_BUFS * PAIR_EW; ++i) mbar_init(&resbar[i], 1);
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        fence_async_smem();
+    }
+    if (warp >= 2) {
+        for (int i = threadIdx.x - 64; i < C1 + p.K2; i += 32 * PAIR_EW) {
+            if (i < C1) sBias1[i] = p.bias1 ? __ldg(p.bias1 + i) : 0.f;
+            else sBias2[i - C1] = p.bias2 ? __ldg(p.bias2 + i - C1) : 0.f;
+        }
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(tmem_holder)),
+                     "r"((uint32_t)C::TMEM_COLS));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_holder;
+    const int PQ = p.P * p.Q;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ------------------------------------------------------------ TMA producer
+            int stage = 0;
+            uint32_t phase = 0;
+            long long issued = 0;
+            bool ok = true;
+            auto next = [&]() {
+                ++issued;
+                if (++stage == STAGES) {
+                    stage = 0;
+                    phase ^= 1;
+                }
+            };
+            auto produce1 = [&](int tile) -> bool {
+                const int m0 = tile * BM;
+                const int img = m0 / PQ;
+                const int rem = m0 - img * PQ;
+                const int pp = rem / p.Q;
+                const int qq = rem - pp * p.Q;
+                const int wb = qq * p.stride - p.pad;
+                const int hb = pp * p.stride - p.pad;
+                int c0 = 0, fs = 0, fr = 0;
+                for (int kb = 0; kb < p.num_kb1; ++kb) {
+                    if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.wait_ns)) return false;
+                    uint8_t* a_dst = sStage + stage * C::STAGE_BYTES;
+                    mbar_expect_tx(&full[stage], (uint32_t)(A_STAGE_BYTES + C1 * BK * 2));
+                    tma_load_im2col(a_dst, &tmA, &full[stage], c0, wb, hb, img, (uint16_t)fs,
+                                    (uint16_t)fr);
+                    tma_load_2d(a_dst + A_STAGE_BYTES, &tmB1, &full[stage], kb * BK, 0);
+                    c0 += BK;
+                    if (c0 == p.Cs) {
+                        c0 = 0;
+                        if (++fs == p.S) {
+                            fs = 0;
+                            ++fr;
+                        }
+                    }
+                    next();
+                }
+                return true;
+            };
+            auto produce2 = [&]() -> bool {
+                for (int j = 0; j < nch2; ++j)
+                    for (int kb = 0; kb < KB2; ++kb) {
+                        if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.wait_ns)) return false;
+                        uint8_t* b_dst = sStage + stage * C::STAGE_BYTES + A_STAGE_BYTES;
+                        mbar_expect_tx(&full[stage], (uint32_t)C::B_SLOT);
+                        tma_load_2d(b_dst, &tmB2, &full[stage], kb * BK, j * PAIR_BN2);
+                        next();
+                    }
+                return true;
+            };
+            int n = 0;
+            for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, ++n) {
+                ok = produce1(tile);
+                if (ok && n > 0) ok = produce2();
+            }
+            if (ok && n > 0) ok = produce2();
+            if (!ok) {
+                atomicOr(p.err, ERRBIT_TC_PRODUCER);
+                *abort_flag = 1;
+            }
+            // never leave with a TMA write in flight: the last STAGES loads (bounded waits)
+            for (long long j = issued - STAGES; j < issued; ++j) {
+                if (j < 0) continue;
+                if (!mbar_wait_drain(&full[(int)(j % STAGES)], (uint32_t)((j / STAGES) & 1))) {
+                    atomicOr(p.err, ERRBIT_TC_DRAIN);
+                    break;
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ------------------------------------------------------------ MMA issuer
+            constexpr uint32_t IDESC1 = instr_desc<C1, F16>();
+            constexpr uint32_t IDESC2 = instr_desc<PAIR_BN2, F16>();
+            const uint64_t adesc0 = smem_desc(smem_u32(sStage), 16, 1024, LAYOUT_SW128);
+            const uint64_t bdesc0 = smem_desc(smem_u32(sStage + A_STAGE_BYTES), 16, 1024, LAYOUT_SW128);
+            const uint64_t a2desc0 = smem_desc(smem_u32(sA2), 16, 1024, LAYOUT_SW128);
+            constexpr uint64_t STAGE_STEP = C::STAGE_BYTES >> 4;
+            constexpr uint64_t K_STEP = 32 >> 4;
+            int stage = 0;
+            uint32_t phase = 0;
+            int gq = 0;  // conv-2 chunks issued (D2 buffer gq & 1)
+            auto next = [&]() {
+                if (++stage == STAGES) {
+                    stage = 0;
+                    phase ^= 1;
+                }
+            };
+            auto mma1 = [&](int n) -> bool {
+                const int b = n & 1;
+                if (!mbar_wait(&d1empty[b], (uint32_t)(((n >> 1) & 1) ^ 1), abort_flag, p.wait_ns))
+                    return false;
+                tc_fence_after();
+                const uint32_t d = tmem_base + (uint32_t)(b * C1);
+                for (int kb = 0; kb < p.num_kb1; ++kb) {
+                    if (!mbar_wait(&full[stage], phase, abort_flag, p.wait_ns)) return false;
+                    tc_fence_after();
+                    const uint64_t ad = adesc0 + (uint64_t)stage * STAGE_STEP;
+                    const uint64_t bd = bdesc0 + (uint64_t)stage * STAGE_STEP;
+#pragma unroll
+                    for (int k = 0; k < BK / 16; ++k)
+                        tc_mma(d, ad + k * K_STEP, bd + k * K_STEP, IDESC1, (kb > 0 || k > 0) ? 1u : 0u);
+                    tc_commit(&empty[stage]);
+                    next();
+                }
+                tc_commit(&d1full[b]);
+                return true;
+            };
+            auto mma2 = [&](int n) -> bool {
+                if (!mbar_wait(a2full, (uint32_t)(n & 1), abort_flag, p.wait_ns)) return false;
+                tc_fence_after();
+                for (int j = 0; j < nch2; ++j, ++gq) {
+                    const int b = gq & 1;
+                    if (!mbar_wait(&d2empty[b], (uint32_t)(((gq >> 1) & 1) ^ 1), abort_flag,
+                                   p.wait_ns))
+                        return false;
+                    tc_fence_after();
+                    const uint32_t d = tmem_base + (uint32_t)(C::D2_BASE + b * PAIR_BN2);
+                    for (int kb = 0; kb < KB2; ++kb) {
+                        if (!mbar_wait(&full[stage], phase, abort_flag, p.wait_ns)) return false;
+                        tc_fence_after();
+                        const uint64_t ad = a2desc0 + (uint64_t)kb * (A_STAGE_BYTES >> 4);
+                        const uint64_t bd = bdesc0 + (uint64_t)stage * STAGE_STEP;
+#pragma unroll
+                        for (int k = 0; k < BK / 16; ++k)
+                            tc_mma(d, ad + k * K_STEP, bd + k * K_STEP, IDESC2,
+                                   (kb > 0 || k > 0) ? 1u : 0u);
+                        tc_commit(&empty[stage]);
+                        next();
+                    }
+                    tc_commit(&d2full[b]);
+                }
+                return true;
+            };
+            bool ok = true;
+            int n = 0;
+            for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x, ++n) {
+                ok = mma1(n);
+                if (ok && n > 0) ok = mma2(n - 1);
+            }
+            if (ok && n > 0) ok = mma2(n - 1);
+            if (!ok) {
+                atomicOr(p.err, ERRBIT_TC_MMA);
+                *abort_flag = 1;
+            }
+            tc_commit(drain);
+            if (!mbar_wait_drain(drain, 0)) atomicOr(p.err, ERRBIT_TC_DRAIN);
+        }
+    } else {
+        // ---------------------------------------------------------------- epilogue
+        const int ew = warp - 2;
+        const int quarter = warp & 3;   // TMEM lane quarter this warp may access
+        const int r = quarter * 32 + lane;   // the tile row (output pixel) of this lane
+        const bool has_res = p.residual != nullptr;
+        const float hi1 = p.act1 == OM_ACT_RELU6 ? 6.f : INFINITY;
+        const float hi2 = p.act2 == OM_ACT_RELU6 ? 6.f : INFINITY;
+        const bool clamp1 = p.act1 != OM_ACT_NONE, clamp2 = p.act2 != OM_ACT_NONE;
+        const uint32_t t_lane = tmem_base + ((uint32_t)(quarter * 32) << 16);
+        // this warp's 32 rows x 128 columns of a staging buffer: four 32 x 32 sub-tiles
+        auto sub = [&](int bb, int s) {
+            return sRes + bb * PAIR_CHUNK_BYTES + (quarter * 4 + s) * EPI_SUB_BYTES;
+        };
+        uint32_t rph = 0;    // per buffer: parity of its next residual load
+        uint32_t rpend = 0;  // per buffer: a residual load is in flight
+        int gq = 0;          // conv-2 chunks processed (D2 buffer gq & 1)
+        int gc = 0;          // chunks staged (staging buffer gc & 1)
+        bool ok = true;
+        // lane 0: the residual of chunk j of the tile whose first row is m0, into buffer bb
+        auto issue_res = [&](int bb, int j, int row0) {
+            bulk_wait_read<0>();   // the buffer's previous stores have read it
+            fence_async_smem();
+            mbar_expect_tx(&resbar[bb * PAIR_EW + ew], 4 * EPI_SUB_BYTES);
+#pragma unroll
+            for (int s = 0; s < 4; ++s)
+                tma_load_2d(sub(bb, s), &tmRes, &resbar[bb * PAIR_EW + ew], j * PAIR_BN2 + s * 32,
+                            row0);
+        };
+        for (int tile = blockIdx.x, n = 0; tile < p.num_tiles; tile += gridDim.x, ++n) {
+            const int row0 = tile * BM + quarter * 32;
+            const bool live = row0 < p.M;
+            // residuals of the tile's first two chunks, before conv 1's accumulator is ready
+            if (has_res && live) {
+                for (int j = 0; j < 2 && j < nch2; ++j) {
+                    const int bb = (gc + j) & 1;
+                    if (lane == 0) issue_res(bb, j, row0);
+                    rpend |= 1u << bb;
+                }
+            }
+            __syncwarp();
+            // E1: conv 1's tile -> conv 2's A operand in shared memory
+            const int b1 = n & 1;
+            if (!mbar_wait(&d1full[b1], (uint32_t)((n >> 1) & 1), abort_flag, p.wait_ns)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+#pragma unroll 1
+            for (int c = 0; c < C1 / 32; ++c) {
+                uint32_t v[32];
+                tmem_ld32(t_lane + (uint32_t)(b1 * C1 + c * 32), v);
+                const float4* b4 = reinterpret_cast<const float4*>(sBias1 + c * 32);
+                uint4 packed[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const float4 ba = b4[2 * q], bb = b4[2 * q + 1];
+                    float f[8] = {__uint_as_float(v[8 * q]) + ba.x, __uint_as_float(v[8 * q + 1]) + ba.y,
+                                  __uint_as_float(v[8 * q + 2]) + ba.z, __uint_as_float(v[8 * q + 3]) + ba.w,
+                                  __uint_as_float(v[8 * q + 4]) + bb.x, __uint_as_float(v[8 * q + 5]) + bb.y,
+                                  __uint_as_float(v[8 * q + 6]) + bb.z, __uint_as_float(v[8 * q + 7]) + bb.w};
+                    if (clamp1) {
+#pragma unroll
+                        for (int t = 0; t < 8; ++t) f[t] = fminf(fmaxf(f[t], 0.f), hi1);
+                    }
+                    typename H16::T2* o2 = reinterpret_cast<typename H16::T2*>(&packed[q]);
+#pragma unroll
+                    for (int t = 0; t < 4; ++t) o2[t] = H16::pack(f[2 * t], f[2 * t + 1]);
+                }
+                // row r of k-block c / 2, 16-byte chunks (c & 1) * 4 .. +3, 128-byte swizzle
+                uint8_t* dst = sA2 + (c >> 1) * A_STAGE_BYTES + r * 128;
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                    *reinterpret_cast<uint4*>(dst + ((((c & 1) * 4 + q) ^ (r & 7)) << 4)) = packed[q];
+            }
+            fence_async_smem();   // the tensor cores read what the threads wrote
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&d1empty[b1]);
+                mbar_arrive(a2full);
+            }
+            // E2: conv 2's chunks
+#pragma unroll 1
+            for (int j = 0; j < nch2; ++j, ++gq) {
+                const int bb = (gc + j) & 1;
+                const int b2 = gq & 1;
+                if (!has_res && lane == 0) bulk_wait_read<0>();   // staging free for outputs
+                __syncwarp();
+                if (!mbar_wait(&d2full[b2], (uint32_t)((gq >> 1) & 1), abort_flag, p.wait_ns)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                if (has_res && live) {
+                    if (!mbar_wait(&resbar[bb * PAIR_EW + ew], (rph >> bb) & 1u, abort_flag,
+                                   p.wait_ns)) {
+                        ok = false;
+                        break;
+                    }
+                    rph ^= 1u << bb;
+                    rpend &= ~(1u << bb);
+                }
+                // a quarter wholly past M loads and stores nothing, and leaves its staging
+                // buffer alone (an earlier tile's stores may still read it)
+#pragma unroll 1
+                for (int s = 0; s < 4 && live; ++s) {
+                    uint32_t v[32];
+                    tmem_ld32(t_lane + (uint32_t)(C::D2_BASE + b2 * PAIR_BN2 + s * 32), v);
+                    const float4* b4 = reinterpret_cast<const float4*>(sBias2 + j * PAIR_BN2 + s * 32);
+                    uint8_t* sb = sub(bb, s);
+                    float f[32];
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) {
+                        const float4 bq = b4[q];
+                        f[4 * q] = __uint_as_float(v[4 * q]) + bq.x;
+                        f[4 * q + 1] = __uint_as_float(v[4 * q + 1]) + bq.y;
+                        f[4 * q + 2] = __uint_as_float(v[4 * q + 2]) + bq.z;
+                        f[4 * q + 3] = __uint_as_float(v[4 * q + 3]) + bq.w;
+                    }
+                    if (has_res) {
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            uint4 rv = *reinterpret_cast<const uint4*>(sb + sw64(lane, q));
+                            const typename H16::T2* r2 = reinterpret_cast<const typename H16::T2*>(&rv);
+#pragma unroll
+                            for (int t = 0; t < 4; ++t) {
+                                float2 rr = H16::unpack(r2[t]);
+                                f[8 * q + 2 * t] += rr.x;
+                                f[8 * q + 2 * t + 1] += rr.y;
+                            }
+                        }
+                    }
+                    if (clamp2) {
+#pragma unroll
+                        for (int q = 0; q < 32; ++q) f[q] = fminf(fmaxf(f[q], 0.f), hi2);
+                    }
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        uint4 ov;
+                        typename H16::T2* o2 = reinterpret_cast<typename H16::T2*>(&ov);
+#pragma unroll
+                        for (int t = 0; t < 4; ++t) o2[t] = H16::pack(f[8 * q + 2 * t], f[8 * q + 2 * t + 1]);
+                        *reinterpret_cast<uint4*>(sb + sw64(lane, q)) = ov;
+                    }
+                }
+                fence_async_smem();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&d2empty[b2]);
+                    if (live) {
+#pragma unroll
+                        for (int s = 0; s < 4; ++s)
+                            tma_store_2d(&tmOut, sub(bb, s), j * PAIR_BN2 + s * 32, row0);
+                        bulk_commit();
+                    }
+                }
+                // the residual two chunks ahead goes into the buffer just stored from
+                if (has_res && live && j + 2 < nch2) {
+                    if (lane == 0) issue_res(bb, j + 2, row0);
+                    rpend |= 1u << bb;
+                }
+                __syncwarp();
+            }
+            if (!ok) break;
+            gc += nch2;
+        }
+        if (!ok && lane == 0) {
+            atomicOr(p.err, ERRBIT_TC_EPILOGUE);
+            *abort_flag = 1;
+        }
+        if (lane == 0) {
+            bulk_wait_all();
+            for (int bb = 0; bb < C::RES_BUFS; ++bb) {
+                if (((rpend >> bb) & 1u) &&
+                    !mbar_wait_drain(&resbar[bb * PAIR_EW + ew], (rph >> bb) & 1u)) {
+                    atomicOr(p.err, ERRBIT_TC_DRAIN);
+                    break;
+                }
+            }
+        }
+        __syncwarp();
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) {
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                     "r"((uint32_t)C::TMEM_COLS));
+    }
+    if (threadIdx.x == 0 && p.stamps) p.stamps[2 * blockIdx.x + 1] = gtimer();
+}
+
+template <int C1, int DT>
+static int launch_pair(DeviceCtx* c, const CUtensorMap& ta, const CUtensorMap& tb1,
+                       const CUtensorMap& tb2, const CUtensorMap& to, const CUtensorMap& tr,
+                       const PairParams& p) {
+    using Cf = PairCfg<C1>;
+    auto kern = conv_pair_kernel<C1, DT>;
+    static bool attr_set[64] = {false};
+    if (!attr_set[c->device]) {
+        OMB_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       Cf::SMEM_BYTES));
+        attr_set[c->device] = true;
+    }
+    const int grid = p.num_tiles < c->num_sms ? p.num_tiles : c->num_sms;
+    PairParams q = p;
+    q.stamps = take_stamps(c->device, grid);
+    kern<<<grid, 64 + 32 * PAIR_EW, Cf::SMEM_BYTES, c->compute>>>(ta, tb1, tb2, to, tr, q);
+    return after_launch(c);
+}
+
+}  // namespace tc
+}  // namespace omb
+
+extern "C" int omCudaConvPairSupported(int nCs, int nMid, int nCout, int nDtype) {
+    return (nDtype == OM_DTYPE_BF16 || nDtype == OM_DTYPE_F16) && nCs > 0 && nCs % 64 == 0 &&
+           (nMid == 64 || nMid == 128) && nCout > 0 && nCout % omb::tc::PAIR_BN2 == 0 &&
+           nCout <= omb::tc::PAIR_MAX_K2;
+}
+
+extern "C" int omCudaConvPairBnAct(const void* pInput, const void* pPacked1, const float* pBias1,
+                                   const void* pPacked2, const float* pBias2,
+                                   const void* pResidual, void* pOutput, int nBatch, int nH,
+                                   int nW, int nCs, int nMid, int nCout, int nKH, int nKW,
+                                   int nStride, int nPad, int nAct1, int nAct2, int nDtype) {
+    OMB_CTX_OR_FAIL(c);
+    using namespace omb::tc;
+    if (!pInput || !pPacked1 || !pPacked2 || !pOutput) return OM_ERR_INVALID;
+    if (nBatch <= 0 || nH <= 0 || nW <= 0 || nKH <= 0 || nKW <= 0 || nStride <= 0 || nPad < 0)
+        return OM_ERR_INVALID;
+    if (!omCudaConvPairSupported(nCs, nMid, nCout, nDtype)) return OM_ERR_UNSUPPORTED;
+    if ((reinterpret_cast<uintptr_t>(pInput) | reinterpret_cast<uintptr_t>(pPacked1) |
+         reinterpret_cast<uintptr_t>(pPacked2) | reinterpret_cast<uintptr_t>(pOutput) |
+         reinterpret_cast<uintptr_t>(pResidual) | reinterpret_cast<uintptr_t>(pBias1) |
+         reinterpret_cast<uintptr_t>(pBias2)) & 15)
+        return OM_ERR_INVALID;
+    const int P = (nH + 2 * nPad - nKH) / nStride + 1;
+    const int Q = (nW + 2 * nPad - nKW) / nStride + 1;
+    if (P <= 0 || Q <= 0) return OM_ERR_INVALID;
+    const int lower = -nPad, upper = nPad - (nKH - 1), upper_w = nPad - (nKW - 1);
+    if (lower < -128 || upper < -128 || upper > 127 || upper_w < -128 || upper_w > 127)
+        return OM_ERR_UNSUPPORTED;
+    const long long Mll = (long long)nBatch * P * Q;
+    if (Mll >= (1LL << 31)) return OM_ERR_UNSUPPORTED;
+    if (!load_driver_entry_points()) return OM_ERR_DRIVER;
+    const long long kpad1 = (long long)nKH * nKW * nCs;   // Cs % 64 == 0: no padding
+
+    PairParams p;
+    p.N = nBatch; p.H = nH; p.W = nW; p.Cs = nCs;
+    p.C1 = nMid; p.K2 = nCout;
+    p.R = nKH; p.S = nKW; p.stride = nStride; p.pad = nPad;
+    p.P = P; p.Q = Q; p.M = (int)Mll;
+    p.num_kb1 = (int)(kpad1 / BK);
+    p.num_tiles = (int)((Mll + BM - 1) / BM);
+    p.bias1 = pBias1;
+    p.bias2 = pBias2;
+    p.residual = pResidual;
+    p.act1 = nAct1;
+    p.act2 = nAct2;
+    p.err = c->err_word;
+    p.stamps = nullptr;
+    p.wait_ns = OMB_WAIT_NS;
+
+    const CUtensorMapDataType dt =
+        nDtype == OM_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    CUtensorMap ta, tb1, tb2, to, tr;
+    cuuint64_t a_dims[4] = {(cuuint64_t)nCs, (cuuint64_t)nW, (cuuint64_t)nH, (cuuint64_t)nBatch};
+    cuuint64_t a_strides[3] = {(cuuint64_t)nCs * 2, (cuuint64_t)nW * nCs * 2,
+                               (cuuint64_t)nH * nW * nCs * 2};
+    int lo[2] = {-nPad, -nPad};
+    int hi[2] = {nPad - (nKW - 1), nPad - (nKH - 1)};
+    cuuint32_t a_estr[4] = {1, (cuuint32_t)nStride, (cuuint32_t)nStride, 1};
+    CUresult r = g_encode_im2col(&ta, dt, 4, const_cast<void*>(pInput), a_dims, a_strides, lo, hi,
+                                 64, BM, a_estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                 CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return OM_ERR_DRIVER;
+    if (g_driver_version <= 13010 && (unsigned long long)nBatch * nH * nW * nCs * 2 < 131072ull)
+        reinterpret_cast<uint64_t*>(&ta)[1] &= ~(1ull << 21);
+    cuuint32_t b_estr[2] = {1, 1};
+    {
+        cuuint64_t dims[2] = {(cuuint64_t)kpad1, (cuuint64_t)nMid};
+        cuuint64_t strides[1] = {(cuuint64_t)kpad1 * 2};
+        cuuint32_t box[2] = {64u, (cuuint32_t)nMid};
+        r = g_encode_tiled(&tb1, dt, 2, const_cast<void*>(pPacked1), dims, strides, box, b_estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) return OM_ERR_DRIVER;
+    }
+    {
+        cuuint64_t dims[2] = {(cuuint64_t)nMid, (cuuint64_t)nCout};
+        cuuint64_t strides[1] = {(cuuint64_t)nMid * 2};
+        cuuint32_t box[2] = {64u, (cuuint32_t)PAIR_BN2};
+        r = g_encode_tiled(&tb2, dt, 2, const_cast<void*>(pPacked2), dims, strides, box, b_estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) return OM_ERR_DRIVER;
+    }
+    int st = encode_epilogue_map(&to, pOutput, p.M, nCout, dt);
+    if (st != OM_OK) return st;
+    tr = to;
+    if (pResidual) {
+        st = encode_epilogue_map(&tr, pResidual, p.M, nCout, dt);
+        if (st != OM_OK) return st;
+    }
+    if (nDtype == OM_DTYPE_BF16)
+        return nMid == 64 ? launch_pair<64, OM_DTYPE_BF16>(c, ta, tb1, tb2, to, tr, p)
+                          : launch_pair<128, OM_DTYPE_BF16>(c, ta, tb1, tb2, to, tr, p);
+    return nMid == 64 ? launch_pair<64, OM_DTYPE_F16>(c, ta, tb1, tb2, to, tr, p)
+                      : launch_pair<128, OM_DTYPE_F16>(c, ta, tb1, tb2, to, tr, p);
+}
+
 // ---------------------------------------------------------------- fp32 path (3xTF32)
 namespace omb {
 namespace tc {

@@ -52,7 +52,7 @@ class InferencePlan:
 
     def __init__(self, net: NetSpec, weights: Dict[str, np.ndarray], batch: int,
                  dtype: int = DTYPE_BF16, h: int = 224, w: int = 224, input_slots: int = 2,
-                 input_dtype: int = DTYPE_F32):
+                 input_dtype: int = DTYPE_F32, fuse_pairs: bool = True):
         """input_dtype: element type of the NCHW image the plan takes, fp32 (the engine's
         tensors) or the plan's own 16-bit dtype (half the bytes per image to copy to the
         device; the stem rounds its input to that type anyway, so the logits are the same)."""
@@ -63,6 +63,9 @@ class InferencePlan:
             raise ValueError("input_dtype must be fp32 or the plan's dtype")
         self.net, self.batch, self.dtype, self.h, self.w = net, batch, dtype, h, w
         self.input_dtype = input_dtype
+        # a bottleneck's 3x3 conv and the 1x1 expansion after it run as one kernel where it
+        # takes the shapes (omCudaConvPairBnAct: the 3x3 output never reaches device memory)
+        self.fuse_pairs = fuse_pairs
         self.ops: List = []           # callables, each issuing one C-ABI launch
         self.keep: List[DeviceBuffer] = []
         self.graphs: List[int] = []   # one captured graph per input slot
@@ -246,16 +249,65 @@ class InferencePlan:
                  pad=cv.pad, act=act, h=hh, wd=ww, p=p, q=q))
         return out, p, q, c
 
+    def _pair_ok(self, a: ConvSpec, b: ConvSpec) -> bool:
+        return (self.fuse_pairs and a.groups == 1 and b.groups == 1 and b.k == 1 and
+                b.stride == 1 and b.pad == 0 and b.cin == a.cout and
+                bool(lib.omCudaConvPairSupported(stored_channels(a.cin), a.cout, b.cout,
+                                                 self.dtype)))
+
+    def _conv_pair(self, a: ConvSpec, b: ConvSpec, weights, x, hh, ww, act1, act2, residual):
+        """Record conv `a` (BN, act1) and the 1x1 conv `b` after it (BN, + residual, act2) as one
+        fused launch (omCudaConvPairBnAct)."""
+        n, dt = self.batch, self.dtype
+        cs_in = stored_channels(a.cin)
+        packs = []
+        for cv, cin_s in ((a, cs_in), (b, a.cout)):
+            wbuf = self._upload(weights[cv.name + ".weight"])
+            g, b_, m, v = (self._upload(t) for t in self._bn_params(weights, cv.bn))
+            packed = self._buf(int(lib.omCudaPackedConvWeightElems(cv.cout, cv.k, cv.k, cin_s)) * 2)
+            bias = self._buf(cv.cout * 4)
+            call("omCudaPackConvWeight", wbuf.ptr, None, g.ptr, b_.ptr, m.ptr, v.ptr, 1e-5,
+                 packed.ptr, bias.ptr, cv.cout, cv.cin, cv.k, cv.k, cin_s, dt)
+            packs.append((packed, bias))
+        p = (hh + 2 * a.pad - a.k) // a.stride + 1
+        q = (ww + 2 * a.pad - a.k) // a.stride + 1
+        obytes = n * p * q * b.cout * 2
+        out = self._buf(obytes)
+        self._need(x, n * hh * ww * cs_in * 2)
+        if residual is not None:
+            self._need(residual, obytes)
+        (p1, b1), (p2, b2) = packs
+        res = residual
+        self._op(lambda x=x, out=out, res=res: call(
+            "omCudaConvPairBnAct", x.ptr, p1.ptr, b1.ptr, p2.ptr, b2.ptr,
+            res.ptr if res is not None else None, out.ptr, n, hh, ww, cs_in, a.cout, b.cout, a.k,
+            a.k, a.stride, a.pad, act1, act2, dt),
+            dict(kind="pair", inp=x, out=out, res=residual, c=a.cin, cs=cs_in, mid=a.cout,
+                 k=b.cout, ks=a.k, stride=a.stride, pad=a.pad, h=hh, wd=ww, p=p, q=q,
+                 flops=2 * n * p * q * (a.cout * a.cin * a.k * a.k + b.cout * b.cin)))
+        self.n_tc_launches += 1
+        self.tc_op_index.append(len(self.ops) - 1)
+        self.conv_flops += 2 * n * p * q * (a.cout * a.cin * a.k * a.k + b.cout * b.cin)
+        return out, p, q, b.cout
+
     def _block(self, blk, weights, x, hh, ww, c):
         if blk.kind in ("basic", "bottleneck"):
             shortcut = x
             if blk.downsample is not None:
                 shortcut, _, _, _ = self._conv(blk.downsample, weights, x, hh, ww, c, ACT_NONE)
             cur, h2, w2, c2 = x, hh, ww, c
-            for i, cv in enumerate(blk.convs):
-                last = i == len(blk.convs) - 1
+            convs = list(blk.convs)
+            i = 0
+            while i < len(convs):
+                cv = convs[i]
+                if (blk.kind == "bottleneck" and i == len(convs) - 2 and
+                        self._pair_ok(cv, convs[i + 1])):
+                    return self._conv_pair(cv, convs[i + 1], weights, cur, h2, w2, ACT_RELU,
+                                           ACT_RELU, shortcut)
+                last = i == len(convs) - 1
                 cur, h2, w2, c2 = self._conv(cv, weights, cur, h2, w2, c2, ACT_RELU,
                                              residual=shortcut if last else None)
+                i += 1
             return cur, h2, w2, c2
         # inverted residual: expand (ReLU6) -> depthwise (ReLU6) -> project (linear) [+ x]
         e, d, pj = blk.convs
