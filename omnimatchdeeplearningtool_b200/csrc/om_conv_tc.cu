@@ -1752,7 +1752,8 @@ namespace tc {
 // Only the output (and the residual) cross HBM: the intermediate C1-channel map is never
 // written, and the expansion's memory traffic overlaps conv 1's tensor-core work.
 constexpr int PAIR_BN2 = 128;                        // conv-2 columns per chunk
-constexpr int PAIR_EW = 4;                           // epilogue warps, one per TMEM lane quarter
+constexpr int PAIR_EW = 16;                          // epilogue warps, four per TMEM lane quarter
+constexpr int PAIR_SLOTS = PAIR_EW / 4;              // warps sharing a quarter
 constexpr int PAIR_CHUNK_BYTES = BM * PAIR_BN2 * 2;  // a chunk's residual / output staging
 constexpr int PAIR_MAX_K2 = 512;
 
@@ -2019,18 +2020,24 @@ __global__ void __launch_bounds__(64 + 32 * PAIR_EW, 1)
         }
     } else {
         // ---------------------------------------------------------------- epilogue
+        // Warp `warp` may read TMEM lane quarter warp % 4; the PAIR_SLOTS warps of a quarter
+        // split conv 1's 32-column groups (E1) and each takes one 32-column sub-tile of every
+        // conv-2 chunk (E2).
         const int ew = warp - 2;
         const int quarter = warp & 3;   // TMEM lane quarter this warp may access
+        const int slot = ew >> 2;
         const int r = quarter * 32 + lane;   // the tile row (output pixel) of this lane
         const bool has_res = p.residual != nullptr;
         const float hi1 = p.act1 == OM_ACT_RELU6 ? 6.f : INFINITY;
         const float hi2 = p.act2 == OM_ACT_RELU6 ? 6.f : INFINITY;
         const bool clamp1 = p.act1 != OM_ACT_NONE, clamp2 = p.act2 != OM_ACT_NONE;
         const uint32_t t_lane = tmem_base + ((uint32_t)(quarter * 32) << 16);
-        // this warp's 32 rows x 128 columns of a staging buffer: four 32 x 32 sub-tiles
-        auto sub = [&](int bb, int s) {
-            return sRes + bb * PAIR_CHUNK_BYTES + (quarter * 4 + s) * EPI_SUB_BYTES;
-        };
+        // this warp's 32 x 32 sub-tile of a chunk's staging buffer (rows of its quarter,
+        // columns slot * 32 of the chunk)
+        static_assert(PAIR_SLOTS * 32 == PAIR_BN2, "one sub-tile per warp and chunk");
+        uint8_t* const subs[C::RES_BUFS] = {
+            sRes + (quarter * PAIR_SLOTS + slot) * EPI_SUB_BYTES,
+            sRes + PAIR_CHUNK_BYTES + (quarter * PAIR_SLOTS + slot) * EPI_SUB_BYTES};
         uint32_t rph = 0;    // per buffer: parity of its next residual load
         uint32_t rpend = 0;  // per buffer: a residual load is in flight
         int gq = 0;          // conv-2 chunks processed (D2 buffer gq & 1)
@@ -2038,13 +2045,11 @@ __global__ void __launch_bounds__(64 + 32 * PAIR_EW, 1)
         bool ok = true;
         // lane 0: the residual of chunk j of the tile whose first row is m0, into buffer bb
         auto issue_res = [&](int bb, int j, int row0) {
-            bulk_wait_read<0>();   // the buffer's previous stores have read it
+            bulk_wait_read<0>();   // the buffer's previous store has read it
             fence_async_smem();
-            mbar_expect_tx(&resbar[bb * PAIR_EW + ew], 4 * EPI_SUB_BYTES);
-#pragma unroll
-            for (int s = 0; s < 4; ++s)
-                tma_load_2d(sub(bb, s), &tmRes, &resbar[bb * PAIR_EW + ew], j * PAIR_BN2 + s * 32,
-                            row0);
+            mbar_expect_tx(&resbar[bb * PAIR_EW + ew], EPI_SUB_BYTES);
+            tma_load_2d(subs[bb], &tmRes, &resbar[bb * PAIR_EW + ew], j * PAIR_BN2 + slot * 32,
+                        row0);
         };
         for (int tile = blockIdx.x, n = 0; tile < p.num_tiles; tile += gridDim.x, ++n) {
             const int row0 = tile * BM + quarter * 32;
@@ -2066,7 +2071,7 @@ __global__ void __launch_bounds__(64 + 32 * PAIR_EW, 1)
             }
             tc_fence_after();
 #pragma unroll 1
-            for (int c = 0; c < C1 / 32; ++c) {
+            for (int c = slot; c < C1 / 32; c += PAIR_SLOTS) {
                 uint32_t v[32];
                 tmem_ld32(t_lane + (uint32_t)(b1 * C1 + c * 32), v);
                 const float4* b4 = reinterpret_cast<const float4*>(sBias1 + c * 32);
@@ -2121,13 +2126,13 @@ __global__ void __launch_bounds__(64 + 32 * PAIR_EW, 1)
                     rpend &= ~(1u << bb);
                 }
                 // a quarter wholly past M loads and stores nothing, and leaves its staging
-                // buffer alone (an earlier tile's stores may still read it)
-#pragma unroll 1
-                for (int s = 0; s < 4 && live; ++s) {
+                // buffer alone (an earlier tile's store may still read it)
+                if (live) {
+                    const int s = slot;
                     uint32_t v[32];
                     tmem_ld32(t_lane + (uint32_t)(C::D2_BASE + b2 * PAIR_BN2 + s * 32), v);
                     const float4* b4 = reinterpret_cast<const float4*>(sBias2 + j * PAIR_BN2 + s * 32);
-                    uint8_t* sb = sub(bb, s);
+                    uint8_t* sb = subs[bb];
                     float f[32];
 #pragma unroll
                     for (int q = 0; q < 8; ++q) {
@@ -2169,9 +2174,7 @@ __global__ void __launch_bounds__(64 + 32 * PAIR_EW, 1)
                 if (lane == 0) {
                     mbar_arrive(&d2empty[b2]);
                     if (live) {
-#pragma unroll
-                        for (int s = 0; s < 4; ++s)
-                            tma_store_2d(&tmOut, sub(bb, s), j * PAIR_BN2 + s * 32, row0);
+                        tma_store_2d(&tmOut, subs[bb], j * PAIR_BN2 + slot * 32, row0);
                         bulk_commit();
                     }
                 }
