@@ -262,6 +262,17 @@ __global__ void gap_nhwc_kernel(const uint4* __restrict__ in, void* __restrict__
 // fixes the window at KS x KS: the item's KS*KS input loads are all issued before the
 // arithmetic (taps outside the image load zeros), which keeps the HBM pipe busy; the taps are
 // accumulated in the same order as the general loop.
+// One window tap: the 8 channels at (hh, ww), or zeros outside the image. The load itself is
+// unconditional (from the clamped, always valid pixel) and the zeros are selected afterwards,
+// so that a thread's taps are all in flight at once instead of each waiting behind a branch.
+__device__ __forceinline__ uint4 tap_load(const uint4* __restrict__ img, int hh, int ww, int H,
+                                          int W, int C8, int c8) {
+    const bool ok = hh >= 0 && hh < H && ww >= 0 && ww < W;
+    const int hc = min(max(hh, 0), H - 1), wc = min(max(ww, 0), W - 1);
+    const uint4 t = __ldg(img + ((size_t)hc * W + wc) * C8 + c8);
+    return ok ? t : make_uint4(0, 0, 0, 0);
+}
+
 template <int DT, int KS>
 __global__ void depthwise_nhwc_kernel(const uint4* __restrict__ in, const float* __restrict__ wpk,
                                       const float* __restrict__ bias, uint4* __restrict__ out,
@@ -324,9 +335,7 @@ __global__ void depthwise_nhwc_kernel(const uint4* __restrict__ in, const float*
 #pragma unroll
                         for (int sx = 0; sx < KS; ++sx) {
                             const int hh = hb + r, ww = w0 + sx;
-                            const bool ok = hh >= 0 && hh < H && ww >= 0 && ww < W;
-                            v[r * KS + sx] = ok ? __ldg(img + ((size_t)hh * W + ww) * C8 + c8)
-                                                : make_uint4(0, 0, 0, 0);
+                            v[r * KS + sx] = tap_load(img, hh, ww, H, W, C8, c8);
                         }
                     }
                     __half2 a0[4] = {bh[0], bh[1], bh[2], bh[3]};
@@ -355,9 +364,7 @@ __global__ void depthwise_nhwc_kernel(const uint4* __restrict__ in, const float*
 #pragma unroll
                     for (int sx = 0; sx < KS; ++sx) {
                         const int hh = h0 + r, ww = w0 + sx;
-                        const bool ok = hh >= 0 && hh < H && ww >= 0 && ww < W;
-                        v[r * KS + sx] = ok ? __ldg(img + ((size_t)hh * W + ww) * C8 + c8)
-                                            : make_uint4(0, 0, 0, 0);
+                        v[r * KS + sx] = tap_load(img, hh, ww, H, W, C8, c8);
                     }
                 }
                 __half2 acc[4] = {bh[0], bh[1], bh[2], bh[3]};
@@ -383,9 +390,7 @@ __global__ void depthwise_nhwc_kernel(const uint4* __restrict__ in, const float*
 #pragma unroll
                 for (int sx = 0; sx < KS; ++sx) {
                     const int hh = h0 + r, ww = w0 + sx;
-                    const bool ok = hh >= 0 && hh < H && ww >= 0 && ww < W;
-                    v[r * KS + sx] = ok ? __ldg(img + ((size_t)hh * W + ww) * C8 + c8)
-                                        : make_uint4(0, 0, 0, 0);
+                    v[r * KS + sx] = tap_load(img, hh, ww, H, W, C8, c8);
                 }
             }
             float acc[8];
