@@ -162,22 +162,28 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 // Bounded wait for the phase with the given parity to complete. Returns false when it gave
 // up, either on its own timeout or because another role raised the abort flag.
+// try_wait suspends the thread for a while in hardware before it reports "not yet", so the
+// loop spins slowly; the abort flag and the clock are looked at only every OMB_CHECK_EVERY
+// rounds, because many warps spin at once and each clock read is an instruction they all issue.
+constexpr uint32_t OMB_CHECK_EVERY = 32;
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
                                           volatile int* abort_flag,
                                           unsigned long long limit_ns = OMB_WAIT_NS) {
     if (mbar_try_wait(bar, parity)) return true;
     unsigned long long t0 = gtimer();
-    while (true) {
+    for (uint32_t spin = 1;; ++spin) {
         if (mbar_try_wait(bar, parity)) return true;
-        if (*abort_flag) return false;
-        if (gtimer() - t0 > limit_ns) return false;
+        if (spin % OMB_CHECK_EVERY == 0) {
+            if (*abort_flag) return false;
+            if (gtimer() - t0 > limit_ns) return false;
+        }
     }
 }
 // Bounded wait used on exit paths (no abort flag: it must not give up early).
 __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity) {
     unsigned long long t0 = gtimer();
-    while (!mbar_try_wait(bar, parity)) {
-        if (gtimer() - t0 > OMB_WAIT_NS) return false;
+    for (uint32_t spin = 1; !mbar_try_wait(bar, parity); ++spin) {
+        if (spin % OMB_CHECK_EVERY == 0 && gtimer() - t0 > OMB_WAIT_NS) return false;
     }
     return true;
 }
