@@ -598,7 +598,7 @@ def conv_groups(plan):
     for i in plan.tc_op_index:
         m = plan.meta[i]
         if m.get("kind") == "stem":
-            labels.append("stem")
+            labels.append("stem + max pool" if m.get("pool") else "stem")
             continue
         if m.get("kind") == "pair":
             labels.append("3x3+1x1 pair")

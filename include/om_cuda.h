@@ -449,6 +449,20 @@ int omCudaStemConvBnActIn(const void* pInput, int nInDtype, void* pWorkspace, co
                           const float* pBias, void* pOutput, int nBatch, int nCin, int nH, int nW,
                           int nCout, int nKH, int nKW, int nStride, int nPad, int nAct,
                           int nDtype);
+/* new: the stem followed by its 3x3 / stride 2 / pad 1 max pool in one kernel (the stem output
+ * never reaches device memory). pPooled: NHWC [nBatch, P2, Q2, nCout] with P2 = (P - 1) / 2 + 1,
+ * Q2 likewise, P x Q the stem's output. Bit-identical to omCudaStemConvBnActIn followed by
+ * omCudaMaxPool2dNhwc(..., 3, 2, 1, ...). Shapes omCudaStemPoolSupported rejects return
+ * OM_ERR_UNSUPPORTED (nothing launched). Fuses the reference ResNet's stem sequence
+ * conv1 -> bn1 -> relu -> maxpool(3, 2, 1) (om.engine.resnet.ixx:236-241). */
+int omCudaStemConvBnActPoolIn(const void* pInput, int nInDtype, void* pWorkspace,
+                              const void* pPacked, const float* pBias, void* pPooled, int nBatch,
+                              int nCin, int nH, int nW, int nCout, int nKH, int nKW, int nStride,
+                              int nPad, int nAct, int nDtype);
+/* 1 when omCudaStemConvBnActPoolIn takes these shapes: the stem kernel's tap limits, output
+ * width <= 128, nCout 32, 64 or 128, a 16-bit dtype; else 0 */
+int omCudaStemPoolSupported(int nBatch, int nCin, int nH, int nW, int nCout, int nKH, int nKW,
+                            int nStride, int nPad, int nDtype);
 /* NCHW fp32 -> NHWC (nDtype) with channels zero-padded to nCs */
 int omCudaNchwToNhwc(const float* pIn, void* pOut, int nN, int nC, int nH, int nW, int nCs,
                      int nDtype);

@@ -150,6 +150,8 @@ _SIGS = {
     "omCudaPackStemWeight": [P, P, P, P, P, P, F, P, P, I, I, I, I, I, I],
     "omCudaStemConvBnAct": [P, P, P, P, P, I, I, I, I, I, I, I, I, I, I, I],
     "omCudaStemConvBnActIn": [P, I, P, P, P, P, I, I, I, I, I, I, I, I, I, I, I],
+    "omCudaStemConvBnActPoolIn": [P, I, P, P, P, P, I, I, I, I, I, I, I, I, I, I, I],
+    "omCudaStemPoolSupported": [I, I, I, I, I, I, I, I, I, I],
     "omCudaNchwToNhwc": [P, P, I, I, I, I, I, I], "omCudaNhwcToNchw": [P, P, I, I, I, I, I, I],
     "omCudaMaxPool2dNhwc": [P, P, I, I, I, I, I, I, I, I],
     "omCudaGlobalAvgPoolNhwc": [P, P, I, I, I, I, I],

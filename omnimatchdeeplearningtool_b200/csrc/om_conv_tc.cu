@@ -1592,6 +1592,348 @@ __global__ void stem_s2d_kernel(const S* __restrict__ x, T* __restrict__ out, in
 }  // namespace tc
 }  // namespace omb
 
+// ---------------------------------------------------------------- stem + max pool
+namespace omb {
+namespace tc {
+
+// The image stem and the 3x3/2/1 max pool after it in one kernel (omCudaStemConvBnActPoolIn).
+// Unfused, the stem writes its full-resolution output (411 MB for a batch of 256 ResNet-50
+// images) and the pool reads it back; here a stem row never leaves the SM:
+//   - CTA c owns a contiguous range of pooled rows (n, y2) and computes the stem rows they need
+//     in order, rows 2*y2-1 .. 2*y2+1, each once (the row before its range start again, as a
+//     halo: one row in about 100);
+//   - producer, MMA issuer and the stem's patch loads are those of MODE_STEM: one TMA box of
+//     the space-to-depth rows per stem row, the packed weight resident, one K=16 MMA per tap;
+//   - the 8 epilogue warps turn a stem row's accumulator into 16-bit values (bias, act) in a
+//     three-row ring in shared memory; after the last row a pooled row needs, they compute it
+//     with the pool kernel's comparisons in its order (window row, then column; positions
+//     outside the map take the lowest value) and store it.
+// Results are bit-identical to omCudaStemConvBnActIn followed by omCudaMaxPool2dNhwc.
+struct StemPoolParams {
+    int P, Q, P2, Q2, K;      // stem output P x Q x K, pooled P2 x Q2 x K
+    int R, S, box_w, num_kb;
+    int rows2;                // N * P2 pooled rows
+    const float* bias;
+    int act;
+    void* out;
+    unsigned int* err;
+    unsigned long long* stamps;
+    unsigned long long wait_ns;
+};
+
+template <int BN>
+struct StemPoolCfg {
+    static constexpr int KB_BYTES = BN * BK * 2;           // one resident weight k-block
+    static constexpr int W_BYTES = 4 * KB_BYTES;           // <= 4 k-blocks (16 taps x 16 ch)
+    static constexpr int PATCH_BYTES = STEM_PATCH_BUFS * STEM_PATCH_BYTES;
+    static constexpr int CH = BN / 8;                      // 16-byte chunks per pixel
+    static constexpr int ROW_BYTES = BM * BN * 2;          // one stem row, <= 128 pixels
+    static constexpr int RING_BYTES = 3 * ROW_BYTES;
+    static constexpr int BIAS_BYTES = BN * 4;
+    static constexpr int BAR_BYTES = 256;
+    static constexpr int SMEM_BYTES =
+        W_BYTES + PATCH_BYTES + RING_BYTES + BIAS_BYTES + BAR_BYTES + 1024;
+    static constexpr int TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
+    static constexpr int EW = 8;
+    static_assert(SMEM_BYTES <= MAX_DYN_SMEM, "shared memory budget");
+    static_assert(BN == 32 || BN == 64 || BN == 128, "stem widths");
+};
+
+// 16-byte chunk j of pixel q in a ring row: chunks are XOR-swizzled by the pixel so that a
+// warp's 32 pixels (one per lane) hit different banks
+template <int BN>
+__device__ __forceinline__ uint32_t ring_off(int q, int j) {
+    constexpr int CH = BN / 8;
+    constexpr int SW = CH < 8 ? CH - 1 : 7;
+    return (uint32_t)(q * (BN * 2) + ((j ^ (q & SW)) << 4));
+}
+
+// pooled rows [g0, g1) of CTA `cta` out of `ctas`
+__device__ __forceinline__ void stem_pool_range(int rows2, int& g0, int& g1) {
+    g0 = (int)((long long)rows2 * blockIdx.x / gridDim.x);
+    g1 = (int)((long long)rows2 * (blockIdx.x + 1) / gridDim.x);
+}
+// the stem rows pooled row g (image n, row y2) needs and this CTA has not computed yet
+__device__ __forceinline__ void stem_pool_rows(const StemPoolParams& p, int g, int g0, int& n,
+                                               int& y2, int& r_first, int& r_last) {
+    n = g / p.P2;
+    y2 = g - n * p.P2;
+    const int lo = 2 * y2 - 1 < 0 ? 0 : 2 * y2 - 1;
+    r_last = 2 * y2 + 1 < p.P ? 2 * y2 + 1 : p.P - 1;
+    r_first = (g == g0 || y2 == 0) ? lo : 2 * y2;
+}
+
+template <int BN, int DT>
+__global__ void __launch_bounds__(64 + 32 * 8, 1)
+    stem_pool_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const StemPoolParams p) {
+    using C = StemPoolCfg<BN>;
+    using H16 = Half16<DT>;
+    using T2 = typename H16::T2;
+    constexpr bool F16 = (DT == OM_DTYPE_F16);
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint8_t* sW = smem;
+    uint8_t* sPatch = sW + C::W_BYTES;
+    uint8_t* sRing = sPatch + C::PATCH_BYTES;
+    float* sBias = reinterpret_cast<float*>(sRing + C::RING_BYTES);
+    uint64_t* wfull = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(sBias) + C::BIAS_BYTES);
+    uint64_t* patch_full = wfull + 1;                    // [STEM_PATCH_BUFS]
+    uint64_t* patch_empty = patch_full + STEM_PATCH_BUFS;  // [STEM_PATCH_BUFS]
+    uint64_t* tfull = patch_empty + STEM_PATCH_BUFS;     // [2]
+    uint64_t* tempty = tfull + 2;                        // [2]
+    uint64_t* drain = tempty + 2;
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+    static_assert((2 * STEM_PATCH_BUFS + 6) * 8 + 8 <= C::BAR_BYTES, "barrier block");
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        if (p.stamps) p.stamps[2 * blockIdx.x] = gtimer();
+        mbar_init(wfull, 1);
+        for (int i = 0; i < STEM_PATCH_BUFS; ++i) {
+            mbar_init(&patch_full[i], 1);
+            mbar_init(&patch_empty[i], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&tfull[i], 1);
+            mbar_init(&tempty[i], C::EW);
+        }
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        fence_async_smem();
+    }
+    if (warp >= 2)
+        for (int i = threadIdx.x - 64; i < BN; i += 32 * C::EW)
+            sBias[i] = (p.bias && i < p.K) ? __ldg(p.bias + i) : 0.f;
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(tmem_holder)),
+                     "r"((uint32_t)C::TMEM_COLS));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_holder;
+    int g0, g1;
+    stem_pool_range(p.rows2, g0, g1);
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ------------------------------------------------------------ TMA producer
+            mbar_expect_tx(wfull, (uint32_t)(p.num_kb * C::KB_BYTES));
+            for (int kb = 0; kb < p.num_kb; ++kb)
+                tma_load_2d(sW + kb * C::KB_BYTES, &tmB, wfull, kb * BK, 0);
+            const uint32_t box_bytes = (uint32_t)(p.R * p.box_w * 32);
+            int pb = 0;
+            uint32_t pph = 0;
+            long long issued = 0;
+            bool ok = true;
+            for (int g = g0; g < g1 && ok; ++g) {
+                int n, y2, rf, rl;
+                stem_pool_rows(p, g, g0, n, y2, rf, rl);
+                for (int r = rf; r <= rl; ++r) {
+                    if (!mbar_wait(&patch_empty[pb], pph ^ 1, abort_flag, p.wait_ns)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_expect_tx(&patch_full[pb], box_bytes);
+                    tma_load_4d(sPatch + pb * STEM_PATCH_BYTES, &tmA, &patch_full[pb], 0, 0, r, n);
+                    ++issued;
+                    if (++pb == STEM_PATCH_BUFS) {
+                        pb = 0;
+                        pph ^= 1;
+                    }
+                }
+            }
+            if (!ok) {
+                atomicOr(p.err, ERRBIT_TC_PRODUCER);
+                *abort_flag = 1;
+            }
+            // never leave with a TMA write in flight (bounded waits)
+            for (long long j = issued - STEM_PATCH_BUFS; j < issued; ++j) {
+                if (j < 0) continue;
+                if (!mbar_wait_drain(&patch_full[(int)(j % STEM_PATCH_BUFS)],
+                                     (uint32_t)((j / STEM_PATCH_BUFS) & 1))) {
+                    atomicOr(p.err, ERRBIT_TC_DRAIN);
+                    break;
+                }
+            }
+            if (!mbar_wait_drain(wfull, 0)) atomicOr(p.err, ERRBIT_TC_DRAIN);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ------------------------------------------------------------ MMA issuer
+            constexpr uint32_t IDESC = instr_desc<BN, F16>();
+            const uint64_t bdesc0 = smem_desc(smem_u32(sW), 16, 1024, LAYOUT_SW128);
+            const uint32_t patch0 = smem_u32(sPatch);
+            const int taps = p.R * p.S;
+            bool ok = mbar_wait(wfull, 0, abort_flag, p.wait_ns);
+            int pb = 0, local = 0;
+            uint32_t pph = 0;
+            for (int g = g0; g < g1 && ok; ++g) {
+                int n, y2, rf, rl;
+                stem_pool_rows(p, g, g0, n, y2, rf, rl);
+                for (int r = rf; r <= rl; ++r, ++local) {
+                    const int acc = local & 1;
+                    if (!mbar_wait(&tempty[acc], (uint32_t)(((local >> 1) & 1) ^ 1), abort_flag,
+                                   p.wait_ns) ||
+                        !mbar_wait(&patch_full[pb], pph, abort_flag, p.wait_ns)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t d = tmem_base + (uint32_t)(acc * BN);
+                    const uint32_t base = patch0 + (uint32_t)(pb * STEM_PATCH_BYTES);
+                    int rr = 0, ss = 0;
+                    for (int t = 0; t < taps; ++t) {
+                        // tap (rr, ss): A = patch rows rr * box_w + ss .. +127 (32-byte swizzle,
+                        // read in place); B = k-block t / 4, K step t % 4
+                        const uint64_t ad =
+                            smem_desc(base + (uint32_t)((rr * p.box_w + ss) * 32), 16, 256, LAYOUT_SW32);
+                        tc_mma(d, ad, bdesc0 + (uint64_t)((t >> 2) * (C::KB_BYTES >> 4)) + (t & 3) * 2,
+                               IDESC, t > 0 ? 1u : 0u);
+                        if (++ss == p.S) {
+                            ss = 0;
+                            ++rr;
+                        }
+                    }
+                    tc_commit(&patch_empty[pb]);
+                    tc_commit(&tfull[acc]);
+                    if (++pb == STEM_PATCH_BUFS) {
+                        pb = 0;
+                        pph ^= 1;
+                    }
+                }
+            }
+            if (!ok) {
+                atomicOr(p.err, ERRBIT_TC_MMA);
+                *abort_flag = 1;
+            }
+            tc_commit(drain);
+            if (!mbar_wait_drain(drain, 0)) atomicOr(p.err, ERRBIT_TC_DRAIN);
+        }
+    } else {
+        // ---------------------------------------------------------------- epilogue
+        // Warp `warp` reads TMEM lane quarter warp % 4 (pixels q = 32 * quarter + lane); the two
+        // warps of a quarter take alternate 32-column chunks. The loop has the same trip count
+        // in every epilogue warp whatever happens (a failed wait only skips work), because the
+        // warps meet at named barriers around each pooled row.
+        const int ew = warp - 2;
+        const int quarter = warp & 3;
+        const int half = ew >> 2;
+        const int q = quarter * 32 + lane;
+        const bool clamp = p.act != OM_ACT_NONE;
+        const float act_hi = p.act == OM_ACT_RELU6 ? 6.f : INFINITY;
+        const uint32_t t_quarter = tmem_base + ((uint32_t)(quarter * 32) << 16);
+        const T2 lowest = H16::pack(-1e30f, -1e30f);
+        uint4 low4;
+        {
+            T2* l2 = reinterpret_cast<T2*>(&low4);
+            l2[0] = l2[1] = l2[2] = l2[3] = lowest;
+        }
+        bool ok = true;
+        int local = 0;
+        for (int g = g0; g < g1; ++g) {
+            int n, y2, rf, rl;
+            stem_pool_rows(p, g, g0, n, y2, rf, rl);
+            for (int r = rf; r <= rl; ++r, ++local) {
+                const int acc = local & 1;
+                if (ok && !mbar_wait(&tfull[acc], (uint32_t)((local >> 1) & 1), abort_flag, p.wait_ns))
+                    ok = false;
+                if (ok) {
+                    tc_fence_after();
+                    uint8_t* row = sRing + (r % 3) * C::ROW_BYTES;
+#pragma unroll 1
+                    for (int c = half; c < BN / 32; c += 2) {
+                        uint32_t v[32];
+                        tmem_ld32(t_quarter + (uint32_t)(acc * BN + c * 32), v);
+                        float f[32];
+                        const float4* b4 = reinterpret_cast<const float4*>(sBias + c * 32);
+#pragma unroll
+                        for (int k = 0; k < 8; ++k) {
+                            const float4 bb = b4[k];
+                            f[4 * k] = __uint_as_float(v[4 * k]) + bb.x;
+                            f[4 * k + 1] = __uint_as_float(v[4 * k + 1]) + bb.y;
+                            f[4 * k + 2] = __uint_as_float(v[4 * k + 2]) + bb.z;
+                            f[4 * k + 3] = __uint_as_float(v[4 * k + 3]) + bb.w;
+                        }
+                        if (clamp) {
+#pragma unroll
+                            for (int k = 0; k < 32; ++k) f[k] = fminf(fmaxf(f[k], 0.f), act_hi);
+                        }
+                        if (q < p.Q) {
+#pragma unroll
+                            for (int k = 0; k < 4; ++k) {
+                                uint4 ov;
+                                T2* o2 = reinterpret_cast<T2*>(&ov);
+#pragma unroll
+                                for (int t = 0; t < 4; ++t)
+                                    o2[t] = H16::pack(f[8 * k + 2 * t], f[8 * k + 2 * t + 1]);
+                                *reinterpret_cast<uint4*>(row + ring_off<BN>(q, c * 4 + k)) = ov;
+                            }
+                        }
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tempty[acc]);
+            }
+            // pooled row (n, y2) from the ring: every epilogue warp's rows are written
+            asm volatile("bar.sync 1, %0;" ::"r"(32 * C::EW) : "memory");
+            if (ok && !*abort_flag) {
+                const int tid = threadIdx.x - 64;
+                typename H16::T* out = static_cast<typename H16::T*>(p.out) +
+                                       ((size_t)n * p.P2 + y2) * p.Q2 * BN;
+                for (int i = tid; i < p.Q2 * C::CH; i += 32 * C::EW) {
+                    const int x2 = i / C::CH;
+                    const int j = i - x2 * C::CH;
+                    T2 m[4] = {lowest, lowest, lowest, lowest};
+#pragma unroll
+                    for (int wr = 0; wr < 3; ++wr) {
+                        const int hh = 2 * y2 - 1 + wr;
+                        const uint8_t* row = sRing + (hh < 0 ? 0 : hh % 3) * C::ROW_BYTES;
+#pragma unroll
+                        for (int wc = 0; wc < 3; ++wc) {
+                            const int ww = 2 * x2 - 1 + wc;
+                            const bool in = hh >= 0 && hh < p.P && ww >= 0 && ww < p.Q;
+                            const uint4 v = in ? *reinterpret_cast<const uint4*>(row + ring_off<BN>(ww, j))
+                                               : low4;
+                            const T2* v2 = reinterpret_cast<const T2*>(&v);
+#pragma unroll
+                            for (int t = 0; t < 4; ++t) m[t] = __hmax2(m[t], v2[t]);
+                        }
+                    }
+                    *reinterpret_cast<uint4*>(out + (size_t)x2 * BN + j * 8) =
+                        *reinterpret_cast<const uint4*>(m);
+                }
+            }
+            // the ring rows read above are rewritten only after every warp is done with them
+            asm volatile("bar.sync 1, %0;" ::"r"(32 * C::EW) : "memory");
+        }
+        if (!ok && lane == 0) {
+            atomicOr(p.err, ERRBIT_TC_EPILOGUE);
+            *abort_flag = 1;
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) {
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                     "r"((uint32_t)C::TMEM_COLS));
+    }
+    if (threadIdx.x == 0 && p.stamps) p.stamps[2 * blockIdx.x + 1] = gtimer();
+}
+
+}  // namespace tc
+}  // namespace omb
+
 // K layout of the stem's packed weight: kk = (tr * ceil(KW / f) + ts) * 16 + ch over the
 // space-to-depth channels ch (see above), padded to a multiple of 64.
 extern "C" long long omCudaPackedStemWeightElems(int nCout, int nCin, int nKH, int nKW,
@@ -1610,7 +1952,8 @@ extern "C" long long omCudaStemWorkspaceBytes(int nBatch, int nCin, int nH, int 
 
 static int stem_conv(const void* pInput, int nInDtype, void* pWorkspace, const void* pPacked,
                      const float* pBias, void* pOutput, int nBatch, int nCin, int nH, int nW,
-                     int nCout, int nKH, int nKW, int nStride, int nPad, int nAct, int nDtype);
+                     int nCout, int nKH, int nKW, int nStride, int nPad, int nAct, int nDtype,
+                     bool pool = false);
 
 extern "C" int omCudaStemConvBnAct(const float* pInput, void* pWorkspace, const void* pPacked,
                                    const float* pBias, void* pOutput, int nBatch, int nCin, int nH,
@@ -1629,9 +1972,58 @@ extern "C" int omCudaStemConvBnActIn(const void* pInput, int nInDtype, void* pWo
                      nCout, nKH, nKW, nStride, nPad, nAct, nDtype);
 }
 
+extern "C" int omCudaStemPoolSupported(int nBatch, int nCin, int nH, int nW, int nCout, int nKH,
+                                       int nKW, int nStride, int nPad, int nDtype) {
+    using namespace omb::tc;
+    StemGeom g;
+    if (nBatch <= 0 || !stem_geom(nCin, nH, nW, nKH, nKW, nStride, nPad, &g)) return 0;
+    return (nDtype == OM_DTYPE_BF16 || nDtype == OM_DTYPE_F16) && g.th <= STEM_MAX_R &&
+           g.tw <= STEM_MAX_S && g.th * g.tw <= STEM_MAX_TAPS && g.Q <= BM &&
+           (nCout == 32 || nCout == 64 || nCout == 128) &&
+           (long long)nBatch * ((g.P - 1) / 2 + 1) < (1LL << 31);
+}
+
+extern "C" int omCudaStemConvBnActPoolIn(const void* pInput, int nInDtype, void* pWorkspace,
+                                         const void* pPacked, const float* pBias, void* pPooled,
+                                         int nBatch, int nCin, int nH, int nW, int nCout, int nKH,
+                                         int nKW, int nStride, int nPad, int nAct, int nDtype) {
+    if (nInDtype != OM_DTYPE_F32 && nInDtype != nDtype) return OM_ERR_UNSUPPORTED;
+    if (!omCudaStemPoolSupported(nBatch, nCin, nH, nW, nCout, nKH, nKW, nStride, nPad, nDtype))
+        return OM_ERR_UNSUPPORTED;
+    return stem_conv(pInput, nInDtype, pWorkspace, pPacked, pBias, pPooled, nBatch, nCin, nH, nW,
+                     nCout, nKH, nKW, nStride, nPad, nAct, nDtype, true);
+}
+
+namespace omb {
+namespace tc {
+template <int BN, int DT>
+static int launch_stem_pool(DeviceCtx* c, const CUtensorMap& ta, const CUtensorMap& tb,
+                            const StemPoolParams& p) {
+    using Cf = StemPoolCfg<BN>;
+    auto kern = stem_pool_kernel<BN, DT>;
+    static bool attr_set[64] = {false};
+    if (!attr_set[c->device]) {
+        OMB_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       Cf::SMEM_BYTES));
+        attr_set[c->device] = true;
+    }
+    const int grid = p.rows2 < c->num_sms ? p.rows2 : c->num_sms;
+    StemPoolParams q = p;
+    q.stamps = take_stamps(c->device, grid);
+    unsigned long long wait_ns;
+    long long stall_after;
+    take_test_stall(c->device, &wait_ns, &stall_after);
+    q.wait_ns = wait_ns;
+    kern<<<grid, 64 + 32 * Cf::EW, Cf::SMEM_BYTES, c->compute>>>(ta, tb, q);
+    return after_launch(c);
+}
+}  // namespace tc
+}  // namespace omb
+
 static int stem_conv(const void* pInput, int nInDtype, void* pWorkspace, const void* pPacked,
                      const float* pBias, void* pOutput, int nBatch, int nCin, int nH, int nW,
-                     int nCout, int nKH, int nKW, int nStride, int nPad, int nAct, int nDtype) {
+                     int nCout, int nKH, int nKW, int nStride, int nPad, int nAct, int nDtype,
+                     bool pool) {
     OMB_CTX_OR_FAIL(c);
     using namespace omb::tc;
     if (!pInput || !pWorkspace || !pPacked || !pOutput) return OM_ERR_INVALID;
@@ -1678,6 +2070,9 @@ static int stem_conv(const void* pInput, int nInDtype, void* pWorkspace, const v
     }
     // Stems with at most 16 taps of at most 4 x 8 and at most 128 output channels keep A in
     // tensor memory (MODE_STEM); any other runs through the generic 16-channel path.
+    if (pool && ((reinterpret_cast<uintptr_t>(pPacked) | reinterpret_cast<uintptr_t>(pOutput) |
+                  reinterpret_cast<uintptr_t>(pBias)) & 15))
+        return OM_ERR_INVALID;
     if (g.th > STEM_MAX_R || g.tw > STEM_MAX_S || g.th * g.tw > STEM_MAX_TAPS || nCout > 128 ||
         (reinterpret_cast<uintptr_t>(pPacked) | reinterpret_cast<uintptr_t>(pOutput) |
          reinterpret_cast<uintptr_t>(pBias)) & 15)
@@ -1733,6 +2128,27 @@ static int stem_conv(const void* pInput, int nInDtype, void* pWorkspace, const v
                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return OM_ERR_DRIVER;
+    if (pool) {
+        StemPoolParams sp;
+        sp.P = g.P; sp.Q = g.Q;
+        sp.P2 = (g.P - 1) / 2 + 1;   // 3x3 window, stride 2, padding 1
+        sp.Q2 = (g.Q - 1) / 2 + 1;
+        sp.K = nCout;
+        sp.R = g.th; sp.S = g.tw; sp.box_w = p.box_w; sp.num_kb = p.num_kb;
+        sp.rows2 = nBatch * sp.P2;
+        sp.bias = pBias; sp.act = nAct; sp.out = pOutput; sp.err = c->err_word;
+        sp.stamps = nullptr; sp.wait_ns = OMB_WAIT_NS;
+        const bool b16 = nDtype == OM_DTYPE_BF16;
+        switch (nCout) {
+            case 32: return b16 ? launch_stem_pool<32, OM_DTYPE_BF16>(c, ta, tb, sp)
+                                : launch_stem_pool<32, OM_DTYPE_F16>(c, ta, tb, sp);
+            case 64: return b16 ? launch_stem_pool<64, OM_DTYPE_BF16>(c, ta, tb, sp)
+                                : launch_stem_pool<64, OM_DTYPE_F16>(c, ta, tb, sp);
+            case 128: return b16 ? launch_stem_pool<128, OM_DTYPE_BF16>(c, ta, tb, sp)
+                                 : launch_stem_pool<128, OM_DTYPE_F16>(c, ta, tb, sp);
+        }
+        return OM_ERR_UNSUPPORTED;
+    }
     return finish_and_launch<MODE_STEM>(c, bn, occ, mt, ew, nDtype, ta, tb, p);
 }
 

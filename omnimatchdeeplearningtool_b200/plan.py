@@ -52,7 +52,8 @@ class InferencePlan:
 
     def __init__(self, net: NetSpec, weights: Dict[str, np.ndarray], batch: int,
                  dtype: int = DTYPE_BF16, h: int = 224, w: int = 224, input_slots: int = 2,
-                 input_dtype: int = DTYPE_F32, fuse_pairs: bool = True):
+                 input_dtype: int = DTYPE_F32, fuse_pairs: bool = True,
+                 fuse_stem_pool: bool = True):
         """input_dtype: element type of the NCHW image the plan takes, fp32 (the engine's
         tensors) or the plan's own 16-bit dtype (half the bytes per image to copy to the
         device; the stem rounds its input to that type anyway, so the logits are the same)."""
@@ -66,6 +67,9 @@ class InferencePlan:
         # a bottleneck's 3x3 conv and the 1x1 expansion after it run as one kernel where it
         # takes the shapes (omCudaConvPairBnAct: the 3x3 output never reaches device memory)
         self.fuse_pairs = fuse_pairs
+        # the image stem and the 3x3/2 max pool after it run as one kernel where it takes the
+        # shapes (omCudaStemConvBnActPoolIn: the stem output never reaches device memory)
+        self.fuse_stem_pool = fuse_stem_pool
         self.ops: List = []           # callables, each issuing one C-ABI launch
         self.keep: List[DeviceBuffer] = []
         self.graphs: List[int] = []   # one captured graph per input slot
@@ -83,14 +87,16 @@ class InferencePlan:
         # the image stem reads the NCHW fp32 input directly (tcgen05 kernel, gathered A tile)
         cur, hh, ww, c = self.in_f32, h, w, 3
         act0 = _ACT[net.stem_act]
+        pooled = False
         for i, cv in enumerate(net.stem):
             if i == 0 and cv.k <= 8 and cv.groups == 1:
-                cur, hh, ww, c = self._stem(cv, weights, hh, ww, act0)
+                pool = net.maxpool and len(net.stem) == 1 and self.fuse_stem_pool
+                cur, hh, ww, c, pooled = self._stem(cv, weights, hh, ww, act0, pool)
             elif i == 0 and input_dtype != DTYPE_F32:
                 raise ValueError("a 16-bit input needs the image-stem kernel")
             else:
                 cur, hh, ww, c = self._conv(cv, weights, cur, hh, ww, c, act0)
-        if net.maxpool:
+        if net.maxpool and not pooled:
             p, q = (hh + 2 - 3) // 2 + 1, (ww + 2 - 3) // 2 + 1
             cs = stored_channels(c)
             y = self._buf(batch * p * q * cs * 2)
@@ -183,8 +189,10 @@ class InferencePlan:
         self.conv_flops += 2 * n * p * q * cout * cin * k * k
         return out, p, q, cout
 
-    def _stem(self, cv: ConvSpec, weights, hh, ww, act):
-        """First conv on the NCHW fp32 image with its BN folded (omCudaStemConvBnAct)."""
+    def _stem(self, cv: ConvSpec, weights, hh, ww, act, pool: bool = False):
+        """First conv on the NCHW image with its BN folded (omCudaStemConvBnActIn), or, with
+        `pool` and shapes the fused kernel takes, that conv and the 3x3/2/1 max pool after it in
+        one launch (omCudaStemConvBnActPoolIn). Returns (out, h, w, c, pooled)."""
         n, dt = self.batch, self.dtype
         wbuf = self._upload(weights[cv.name + ".weight"])
         g, b_, m, v = (self._upload(a) for a in self._bn_params(weights, cv.bn))
@@ -195,7 +203,10 @@ class InferencePlan:
              bias.ptr, cv.cout, cv.cin, cv.k, cv.k, cv.stride, dt)
         p = (hh + 2 * cv.pad - cv.k) // cv.stride + 1
         q = (ww + 2 * cv.pad - cv.k) // cv.stride + 1
-        out = self._buf(n * p * q * cv.cout * 2)
+        pool = pool and bool(lib.omCudaStemPoolSupported(n, cv.cin, hh, ww, cv.cout, cv.k, cv.k,
+                                                         cv.stride, cv.pad, dt))
+        p2, q2 = ((p - 1) // 2 + 1, (q - 1) // 2 + 1) if pool else (p, q)
+        out = self._buf(n * p2 * q2 * cv.cout * 2)
         ws = self._buf(int(lib.omCudaStemWorkspaceBytes(n, cv.cin, hh, ww, cv.k, cv.k, cv.stride,
                                                         cv.pad)))
         esize = 4 if self.input_dtype == DTYPE_F32 else 2
@@ -204,16 +215,17 @@ class InferencePlan:
         # The input pointer is the one op argument looked up when the op is issued: the slot
         # being captured or launched (every other argument is bound here).
         idt = self.input_dtype
+        fn = "omCudaStemConvBnActPoolIn" if pool else "omCudaStemConvBnActIn"
         self._op(lambda out=out, ws=ws: call(
-            "omCudaStemConvBnActIn", self.inputs[self._slot].ptr, idt, ws.ptr, packed.ptr,
+            fn, self.inputs[self._slot].ptr, idt, ws.ptr, packed.ptr,
             bias.ptr, out.ptr, n, cv.cin, hh, ww, cv.cout, cv.k, cv.k, cv.stride, cv.pad, act, dt),
-            dict(kind="stem", inp=self.in_f32, out=out, w=weights[cv.name + ".weight"],
+            dict(kind="stem", pool=pool, inp=self.in_f32, out=out, w=weights[cv.name + ".weight"],
                  bn=self._bn_params(weights, cv.bn), c=cv.cin, k=cv.cout, ks=cv.k,
-                 stride=cv.stride, pad=cv.pad, act=act, h=hh, wd=ww, p=p, q=q))
+                 stride=cv.stride, pad=cv.pad, act=act, h=hh, wd=ww, p=p, q=q, p2=p2, q2=q2))
         self.n_tc_launches += 1
         self.tc_op_index.append(len(self.ops) - 1)
         self.conv_flops += 2 * n * p * q * cv.cout * cv.cin * cv.k * cv.k
-        return out, p, q, cv.cout
+        return out, p2, q2, cv.cout, pool
 
     def _bn_params(self, weights, bn: str):
         return (weights[bn + ".gamma"], weights[bn + ".beta"], weights[bn + ".running_mean"],
