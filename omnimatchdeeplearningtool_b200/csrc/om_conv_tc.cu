@@ -1056,9 +1056,14 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
                     if (lane == 0) bulk_wait_read<EPI_BUFS - 1>();
                     __syncwarp();
                 }
+                // ReLU: one max per value; ReLU6 clamps above as well
                 if (clamp) {
 #pragma unroll
-                    for (int q = 0; q < 32; ++q) f[q] = fminf(fmaxf(f[q], 0.f), act_hi);
+                    for (int q = 0; q < 32; ++q) f[q] = fmaxf(f[q], 0.f);
+                    if (act_hi < INFINITY) {
+#pragma unroll
+                        for (int q = 0; q < 32; ++q) f[q] = fminf(f[q], act_hi);
+                    }
                 }
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
@@ -1864,7 +1869,11 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
                         }
                         if (clamp) {
 #pragma unroll
-                            for (int k = 0; k < 32; ++k) f[k] = fminf(fmaxf(f[k], 0.f), act_hi);
+                            for (int k = 0; k < 32; ++k) f[k] = fmaxf(f[k], 0.f);
+                            if (act_hi < INFINITY) {
+#pragma unroll
+                                for (int k = 0; k < 32; ++k) f[k] = fminf(f[k], act_hi);
+                            }
                         }
                         if (q < p.Q) {
 #pragma unroll
@@ -2507,7 +2516,11 @@ __global__ void __launch_bounds__(64 + 32 * PAIR_EW, 1)
                                   __uint_as_float(v[8 * q + 6]) + bb.z, __uint_as_float(v[8 * q + 7]) + bb.w};
                     if (clamp1) {
 #pragma unroll
-                        for (int t = 0; t < 8; ++t) f[t] = fminf(fmaxf(f[t], 0.f), hi1);
+                        for (int t = 0; t < 8; ++t) f[t] = fmaxf(f[t], 0.f);
+                        if (hi1 < INFINITY) {
+#pragma unroll
+                            for (int t = 0; t < 8; ++t) f[t] = fminf(f[t], hi1);
+                        }
                     }
                     typename H16::T2* o2 = reinterpret_cast<typename H16::T2*>(&packed[q]);
 #pragma unroll
@@ -2579,7 +2592,11 @@ __global__ void __launch_bounds__(64 + 32 * PAIR_EW, 1)
                     }
                     if (clamp2) {
 #pragma unroll
-                        for (int q = 0; q < 32; ++q) f[q] = fminf(fmaxf(f[q], 0.f), hi2);
+                        for (int q = 0; q < 32; ++q) f[q] = fmaxf(f[q], 0.f);
+                        if (hi2 < INFINITY) {
+#pragma unroll
+                            for (int q = 0; q < 32; ++q) f[q] = fminf(f[q], hi2);
+                        }
                     }
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
