@@ -459,8 +459,9 @@ int omCudaStemConvBnActPoolIn(const void* pInput, int nInDtype, void* pWorkspace
                               const void* pPacked, const float* pBias, void* pPooled, int nBatch,
                               int nCin, int nH, int nW, int nCout, int nKH, int nKW, int nStride,
                               int nPad, int nAct, int nDtype);
-/* 1 when omCudaStemConvBnActPoolIn takes these shapes: the stem kernel's tap limits, output
- * width <= 128, nCout 32, 64 or 128, a 16-bit dtype; else 0 */
+/* 1 when omCudaStemConvBnActPoolIn takes these shapes: nCout 64, a filter whose space-to-depth
+ * form has 4 tap columns and at most 4 tap rows (the 7x7 / stride 2 ImageNet stem), output
+ * width <= 128, a 16-bit dtype; else 0 */
 int omCudaStemPoolSupported(int nBatch, int nCin, int nH, int nW, int nCout, int nKH, int nKW,
                             int nStride, int nPad, int nDtype);
 /* NCHW fp32 -> NHWC (nDtype) with channels zero-padded to nCs */

@@ -1604,19 +1604,26 @@ namespace tc {
 // The image stem and the 3x3/2/1 max pool after it in one kernel (omCudaStemConvBnActPoolIn).
 // Unfused, the stem writes its full-resolution output (411 MB for a batch of 256 ResNet-50
 // images) and the pool reads it back; here a stem row never leaves the SM:
-//   - CTA c owns a contiguous range of pooled rows (n, y2) and computes the stem rows they need
-//     in order, rows 2*y2-1 .. 2*y2+1, each once (the row before its range start again, as a
-//     halo: one row in about 100);
-//   - producer, MMA issuer and the stem's patch loads are those of MODE_STEM: one TMA box of
-//     the space-to-depth rows per stem row, the packed weight resident, one K=16 MMA per tap;
-//   - the 8 epilogue warps turn a stem row's accumulator into 16-bit values (bias, act) in a
-//     three-row ring in shared memory; after the last row a pooled row needs, they compute it
-//     with the pool kernel's comparisons in its order (window row, then column; positions
-//     outside the map take the lowest value) and store it.
+//   - CTA c owns a contiguous range of pooled rows (n, y2). Pooled row y2 needs stem rows
+//     2 y2 - 1 .. 2 y2 + 1: a tile is the stem row pair (2 y2, 2 y2 + 1), and row 2 y2 - 1 is
+//     the previous tile's (at the start of a range a halo tile computes the pair before);
+//   - a tile is one GEMM with N = 128: column dy * 64 + c is channel c of stem row y0 + dy.
+//     Its K runs over the R + 1 space-to-depth rows r' the two rows read (tap row r' - dy of
+//     row y0 + dy, zero where that tap row does not exist), so the pair takes 5 x 4 MMAs of
+//     N = 128 where two single rows take 2 x 16 of N = 64, and an N = 128 MMA costs the tensor
+//     core what an N = 64 one does;
+//   - one TMA box of the R + 1 space-to-depth rows per tile (32-byte swizzle); tap (r', s) of
+//     output column m is patch pixel (r', m + s), read in place by the MMA as with MODE_STEM.
+//     The B operand, k-block r' = [packed tap row r' for dy = 0; tap row r' - 1 for dy = 1], is
+//     loaded once per CTA from the packed stem weight (tap rows outside it read as zeros);
+//   - the 8 epilogue warps turn the accumulator into 16-bit values (bias, act) in a three-row
+//     ring in shared memory; after each tile they compute pooled row y2 with the pool kernel's
+//     comparisons in its order (window row, then column; positions outside the map take the
+//     lowest value) and store it.
 // Results are bit-identical to omCudaStemConvBnActIn followed by omCudaMaxPool2dNhwc.
 struct StemPoolParams {
     int P, Q, P2, Q2, K;      // stem output P x Q x K, pooled P2 x Q2 x K
-    int R, S, box_w, num_kb;
+    int R, S, box_w;          // tap rows and columns of the space-to-depth conv, patch width
     int rows2;                // N * P2 pooled rows
     const float* bias;
     int act;
@@ -1626,53 +1633,57 @@ struct StemPoolParams {
     unsigned long long wait_ns;
 };
 
-template <int BN>
+constexpr int SP_BN = 64;                 // stem channels
+constexpr int SP_N = 2 * SP_BN;           // MMA N: two stem rows
+constexpr int SP_KB = STEM_MAX_R + 1;     // k-blocks: space-to-depth rows of a row pair
+constexpr int SP_PATCH_BYTES = 22528;     // >= 5 * (127 + 4) * 32, 1 KB multiple
+static_assert(SP_PATCH_BYTES >= SP_KB * (BM - 1 + 4) * 32, "patch size");
+static_assert(SP_PATCH_BYTES % 1024 == 0, "patch buffers stay 1024-byte aligned");
+
 struct StemPoolCfg {
-    static constexpr int KB_BYTES = BN * BK * 2;           // one resident weight k-block
-    static constexpr int W_BYTES = 4 * KB_BYTES;           // <= 4 k-blocks (16 taps x 16 ch)
-    static constexpr int PATCH_BYTES = STEM_PATCH_BUFS * STEM_PATCH_BYTES;
-    static constexpr int CH = BN / 8;                      // 16-byte chunks per pixel
-    static constexpr int ROW_BYTES = BM * BN * 2;          // one stem row, <= 128 pixels
+    static constexpr int KB_BYTES = SP_N * BK * 2;          // one resident k-block, 128 rows
+    static constexpr int W_BYTES = SP_KB * KB_BYTES;
+    static constexpr int PATCH_BYTES = STEM_PATCH_BUFS * SP_PATCH_BYTES;
+    static constexpr int CH = SP_BN / 8;                    // 16-byte chunks per pixel
+    static constexpr int ROW_BYTES = BM * SP_BN * 2;        // one stem row, <= 128 pixels
     static constexpr int RING_BYTES = 3 * ROW_BYTES;
-    static constexpr int BIAS_BYTES = BN * 4;
+    static constexpr int BIAS_BYTES = SP_BN * 4;
     static constexpr int BAR_BYTES = 256;
     static constexpr int SMEM_BYTES =
         W_BYTES + PATCH_BYTES + RING_BYTES + BIAS_BYTES + BAR_BYTES + 1024;
-    static constexpr int TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
+    static constexpr int TMEM_COLS = 2 * SP_N;
     static constexpr int EW = 8;
     static_assert(SMEM_BYTES <= MAX_DYN_SMEM, "shared memory budget");
-    static_assert(BN == 32 || BN == 64 || BN == 128, "stem widths");
 };
 
 // 16-byte chunk j of pixel q in a ring row: chunks are XOR-swizzled by the pixel so that a
 // warp's 32 pixels (one per lane) hit different banks
-template <int BN>
 __device__ __forceinline__ uint32_t ring_off(int q, int j) {
-    constexpr int CH = BN / 8;
-    constexpr int SW = CH < 8 ? CH - 1 : 7;
-    return (uint32_t)(q * (BN * 2) + ((j ^ (q & SW)) << 4));
+    return (uint32_t)(q * (SP_BN * 2) + ((j ^ (q & 7)) << 4));
 }
 
-// pooled rows [g0, g1) of CTA `cta` out of `ctas`
+// pooled rows [g0, g1) of this CTA
 __device__ __forceinline__ void stem_pool_range(int rows2, int& g0, int& g1) {
     g0 = (int)((long long)rows2 * blockIdx.x / gridDim.x);
     g1 = (int)((long long)rows2 * (blockIdx.x + 1) / gridDim.x);
 }
-// the stem rows pooled row g (image n, row y2) needs and this CTA has not computed yet
-__device__ __forceinline__ void stem_pool_rows(const StemPoolParams& p, int g, int g0, int& n,
-                                               int& y2, int& r_first, int& r_last) {
+// Tiles of pooled row g (image n, row y2): the halo pair (2 y2 - 2, 2 y2 - 1) when the range
+// starts there, then the pair (2 y2, 2 y2 + 1). Returns the number of tiles, first_y0 the
+// first tile's first stem row.
+__device__ __forceinline__ int stem_pool_tiles(const StemPoolParams& p, int g, int g0, int& n,
+                                               int& y2, int& first_y0) {
     n = g / p.P2;
     y2 = g - n * p.P2;
-    const int lo = 2 * y2 - 1 < 0 ? 0 : 2 * y2 - 1;
-    r_last = 2 * y2 + 1 < p.P ? 2 * y2 + 1 : p.P - 1;
-    r_first = (g == g0 || y2 == 0) ? lo : 2 * y2;
+    const bool halo = g == g0 && y2 > 0;
+    first_y0 = halo ? 2 * y2 - 2 : 2 * y2;
+    return halo ? 2 : 1;
 }
 
-template <int BN, int DT>
+template <int DT>
 __global__ void __launch_bounds__(64 + 32 * 8, 1)
     stem_pool_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const StemPoolParams p) {
-    using C = StemPoolCfg<BN>;
+    using C = StemPoolCfg;
     using H16 = Half16<DT>;
     using T2 = typename H16::T2;
     constexpr bool F16 = (DT == OM_DTYPE_F16);
@@ -1712,8 +1723,8 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
         fence_async_smem();
     }
     if (warp >= 2)
-        for (int i = threadIdx.x - 64; i < BN; i += 32 * C::EW)
-            sBias[i] = (p.bias && i < p.K) ? __ldg(p.bias + i) : 0.f;
+        for (int i = threadIdx.x - 64; i < SP_BN; i += 32 * C::EW)
+            sBias[i] = p.bias ? __ldg(p.bias + i) : 0.f;
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                          smem_u32(tmem_holder)),
@@ -1726,28 +1737,33 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
     const uint32_t tmem_base = *tmem_holder;
     int g0, g1;
     stem_pool_range(p.rows2, g0, g1);
+    const int kbs = p.R + 1;   // k-blocks of a row pair
 
     if (warp == 0) {
         if (lane == 0) {
             // ------------------------------------------------------------ TMA producer
-            mbar_expect_tx(wfull, (uint32_t)(p.num_kb * C::KB_BYTES));
-            for (int kb = 0; kb < p.num_kb; ++kb)
+            // B k-block r': rows 0..63 = packed tap row r' (the stem's k-block r'), rows
+            // 64..127 = packed tap row r' - 1; r' = R and r' - 1 = -1 lie outside: zeros
+            mbar_expect_tx(wfull, (uint32_t)(kbs * C::KB_BYTES));
+            for (int kb = 0; kb < kbs; ++kb) {
                 tma_load_2d(sW + kb * C::KB_BYTES, &tmB, wfull, kb * BK, 0);
-            const uint32_t box_bytes = (uint32_t)(p.R * p.box_w * 32);
+                tma_load_2d(sW + kb * C::KB_BYTES + SP_BN * BK * 2, &tmB, wfull, (kb - 1) * BK, 0);
+            }
+            const uint32_t box_bytes = (uint32_t)(kbs * p.box_w * 32);
             int pb = 0;
             uint32_t pph = 0;
             long long issued = 0;
             bool ok = true;
             for (int g = g0; g < g1 && ok; ++g) {
-                int n, y2, rf, rl;
-                stem_pool_rows(p, g, g0, n, y2, rf, rl);
-                for (int r = rf; r <= rl; ++r) {
+                int n, y2, y0;
+                const int nt = stem_pool_tiles(p, g, g0, n, y2, y0);
+                for (int t = 0; t < nt; ++t, y0 += 2) {
                     if (!mbar_wait(&patch_empty[pb], pph ^ 1, abort_flag, p.wait_ns)) {
                         ok = false;
                         break;
                     }
                     mbar_expect_tx(&patch_full[pb], box_bytes);
-                    tma_load_4d(sPatch + pb * STEM_PATCH_BYTES, &tmA, &patch_full[pb], 0, 0, r, n);
+                    tma_load_4d(sPatch + pb * SP_PATCH_BYTES, &tmA, &patch_full[pb], 0, 0, y0, n);
                     ++issued;
                     if (++pb == STEM_PATCH_BUFS) {
                         pb = 0;
@@ -1773,17 +1789,16 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
     } else if (warp == 1) {
         if (lane == 0) {
             // ------------------------------------------------------------ MMA issuer
-            constexpr uint32_t IDESC = instr_desc<BN, F16>();
+            constexpr uint32_t IDESC = instr_desc<SP_N, F16>();
             const uint64_t bdesc0 = smem_desc(smem_u32(sW), 16, 1024, LAYOUT_SW128);
             const uint32_t patch0 = smem_u32(sPatch);
-            const int taps = p.R * p.S;
             bool ok = mbar_wait(wfull, 0, abort_flag, p.wait_ns);
             int pb = 0, local = 0;
             uint32_t pph = 0;
             for (int g = g0; g < g1 && ok; ++g) {
-                int n, y2, rf, rl;
-                stem_pool_rows(p, g, g0, n, y2, rf, rl);
-                for (int r = rf; r <= rl; ++r, ++local) {
+                int n, y2, y0;
+                const int nt = stem_pool_tiles(p, g, g0, n, y2, y0);
+                for (int t = 0; t < nt; ++t, ++local) {
                     const int acc = local & 1;
                     if (!mbar_wait(&tempty[acc], (uint32_t)(((local >> 1) & 1) ^ 1), abort_flag,
                                    p.wait_ns) ||
@@ -1792,19 +1807,17 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t d = tmem_base + (uint32_t)(acc * BN);
-                    const uint32_t base = patch0 + (uint32_t)(pb * STEM_PATCH_BYTES);
-                    int rr = 0, ss = 0;
-                    for (int t = 0; t < taps; ++t) {
-                        // tap (rr, ss): A = patch rows rr * box_w + ss .. +127 (32-byte swizzle,
-                        // read in place); B = k-block t / 4, K step t % 4
-                        const uint64_t ad =
-                            smem_desc(base + (uint32_t)((rr * p.box_w + ss) * 32), 16, 256, LAYOUT_SW32);
-                        tc_mma(d, ad, bdesc0 + (uint64_t)((t >> 2) * (C::KB_BYTES >> 4)) + (t & 3) * 2,
-                               IDESC, t > 0 ? 1u : 0u);
-                        if (++ss == p.S) {
-                            ss = 0;
-                            ++rr;
+                    const uint32_t d = tmem_base + (uint32_t)(acc * SP_N);
+                    const uint32_t base = patch0 + (uint32_t)(pb * SP_PATCH_BYTES);
+                    for (int rr = 0; rr < kbs; ++rr) {
+#pragma unroll
+                        for (int ss = 0; ss < 4; ++ss) {
+                            // tap (rr, ss): A = patch rows rr * box_w + ss .. +127 (32-byte
+                            // swizzle, read in place); B = k-block rr, K step ss
+                            const uint64_t ad = smem_desc(base + (uint32_t)((rr * p.box_w + ss) * 32),
+                                                          16, 256, LAYOUT_SW32);
+                            tc_mma(d, ad, bdesc0 + (uint64_t)(rr * (C::KB_BYTES >> 4)) + ss * 2,
+                                   IDESC, (rr > 0 || ss > 0) ? 1u : 0u);
                         }
                     }
                     tc_commit(&patch_empty[pb]);
@@ -1825,9 +1838,10 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
     } else {
         // ---------------------------------------------------------------- epilogue
         // Warp `warp` reads TMEM lane quarter warp % 4 (pixels q = 32 * quarter + lane); the two
-        // warps of a quarter take alternate 32-column chunks. The loop has the same trip count
-        // in every epilogue warp whatever happens (a failed wait only skips work), because the
-        // warps meet at named barriers around each pooled row.
+        // warps of a quarter take alternate 32-column chunks (chunk c: stem row y0 + c / 2,
+        // channels (c % 2) * 32 ..). The loop has the same trip count in every epilogue warp
+        // whatever happens (a failed wait only skips work), because the warps meet at named
+        // barriers around each pooled row.
         const int ew = warp - 2;
         const int quarter = warp & 3;
         const int half = ew >> 2;
@@ -1844,21 +1858,21 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
         bool ok = true;
         int local = 0;
         for (int g = g0; g < g1; ++g) {
-            int n, y2, rf, rl;
-            stem_pool_rows(p, g, g0, n, y2, rf, rl);
-            for (int r = rf; r <= rl; ++r, ++local) {
+            int n, y2, y0;
+            const int nt = stem_pool_tiles(p, g, g0, n, y2, y0);
+            for (int t = 0; t < nt; ++t, ++local, y0 += 2) {
                 const int acc = local & 1;
                 if (ok && !mbar_wait(&tfull[acc], (uint32_t)((local >> 1) & 1), abort_flag, p.wait_ns))
                     ok = false;
                 if (ok) {
                     tc_fence_after();
-                    uint8_t* row = sRing + (r % 3) * C::ROW_BYTES;
 #pragma unroll 1
-                    for (int c = half; c < BN / 32; c += 2) {
+                    for (int c = half; c < SP_N / 32; c += 2) {
                         uint32_t v[32];
-                        tmem_ld32(t_quarter + (uint32_t)(acc * BN + c * 32), v);
+                        tmem_ld32(t_quarter + (uint32_t)(acc * SP_N + c * 32), v);
+                        const int col = (c & 1) * 32;
                         float f[32];
-                        const float4* b4 = reinterpret_cast<const float4*>(sBias + c * 32);
+                        const float4* b4 = reinterpret_cast<const float4*>(sBias + col);
 #pragma unroll
                         for (int k = 0; k < 8; ++k) {
                             const float4 bb = b4[k];
@@ -1875,15 +1889,17 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
                                 for (int k = 0; k < 32; ++k) f[k] = fminf(f[k], act_hi);
                             }
                         }
-                        if (q < p.Q) {
+                        const int r = y0 + (c >> 1);
+                        if (q < p.Q && r < p.P) {
+                            uint8_t* row = sRing + (r % 3) * C::ROW_BYTES;
 #pragma unroll
                             for (int k = 0; k < 4; ++k) {
                                 uint4 ov;
                                 T2* o2 = reinterpret_cast<T2*>(&ov);
 #pragma unroll
-                                for (int t = 0; t < 4; ++t)
-                                    o2[t] = H16::pack(f[8 * k + 2 * t], f[8 * k + 2 * t + 1]);
-                                *reinterpret_cast<uint4*>(row + ring_off<BN>(q, c * 4 + k)) = ov;
+                                for (int tt = 0; tt < 4; ++tt)
+                                    o2[tt] = H16::pack(f[8 * k + 2 * tt], f[8 * k + 2 * tt + 1]);
+                                *reinterpret_cast<uint4*>(row + ring_off(q, col / 8 + k)) = ov;
                             }
                         }
                     }
@@ -1897,7 +1913,7 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
             if (ok && !*abort_flag) {
                 const int tid = threadIdx.x - 64;
                 typename H16::T* out = static_cast<typename H16::T*>(p.out) +
-                                       ((size_t)n * p.P2 + y2) * p.Q2 * BN;
+                                       ((size_t)n * p.P2 + y2) * p.Q2 * SP_BN;
                 for (int i = tid; i < p.Q2 * C::CH; i += 32 * C::EW) {
                     const int x2 = i / C::CH;
                     const int j = i - x2 * C::CH;
@@ -1910,14 +1926,14 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
                         for (int wc = 0; wc < 3; ++wc) {
                             const int ww = 2 * x2 - 1 + wc;
                             const bool in = hh >= 0 && hh < p.P && ww >= 0 && ww < p.Q;
-                            const uint4 v = in ? *reinterpret_cast<const uint4*>(row + ring_off<BN>(ww, j))
+                            const uint4 v = in ? *reinterpret_cast<const uint4*>(row + ring_off(ww, j))
                                                : low4;
                             const T2* v2 = reinterpret_cast<const T2*>(&v);
 #pragma unroll
                             for (int t = 0; t < 4; ++t) m[t] = __hmax2(m[t], v2[t]);
                         }
                     }
-                    *reinterpret_cast<uint4*>(out + (size_t)x2 * BN + j * 8) =
+                    *reinterpret_cast<uint4*>(out + (size_t)x2 * SP_BN + j * 8) =
                         *reinterpret_cast<const uint4*>(m);
                 }
             }
@@ -1986,9 +2002,9 @@ extern "C" int omCudaStemPoolSupported(int nBatch, int nCin, int nH, int nW, int
     using namespace omb::tc;
     StemGeom g;
     if (nBatch <= 0 || !stem_geom(nCin, nH, nW, nKH, nKW, nStride, nPad, &g)) return 0;
+    // the pair GEMM reads a packed k-block as one tap row: four taps of 16 channels
     return (nDtype == OM_DTYPE_BF16 || nDtype == OM_DTYPE_F16) && g.th <= STEM_MAX_R &&
-           g.tw <= STEM_MAX_S && g.th * g.tw <= STEM_MAX_TAPS && g.Q <= BM &&
-           (nCout == 32 || nCout == 64 || nCout == 128) &&
+           g.tw == 4 && g.Q <= BM && nCout == SP_BN &&
            (long long)nBatch * ((g.P - 1) / 2 + 1) < (1LL << 31);
 }
 
@@ -2005,11 +2021,11 @@ extern "C" int omCudaStemConvBnActPoolIn(const void* pInput, int nInDtype, void*
 
 namespace omb {
 namespace tc {
-template <int BN, int DT>
+template <int DT>
 static int launch_stem_pool(DeviceCtx* c, const CUtensorMap& ta, const CUtensorMap& tb,
                             const StemPoolParams& p) {
-    using Cf = StemPoolCfg<BN>;
-    auto kern = stem_pool_kernel<BN, DT>;
+    using Cf = StemPoolCfg;
+    auto kern = stem_pool_kernel<DT>;
     static bool attr_set[64] = {false};
     if (!attr_set[c->device]) {
         OMB_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -2143,20 +2159,18 @@ static int stem_conv(const void* pInput, int nInDtype, void* pWorkspace, const v
         sp.P2 = (g.P - 1) / 2 + 1;   // 3x3 window, stride 2, padding 1
         sp.Q2 = (g.Q - 1) / 2 + 1;
         sp.K = nCout;
-        sp.R = g.th; sp.S = g.tw; sp.box_w = p.box_w; sp.num_kb = p.num_kb;
+        sp.R = g.th; sp.S = g.tw; sp.box_w = p.box_w;
         sp.rows2 = nBatch * sp.P2;
         sp.bias = pBias; sp.act = nAct; sp.out = pOutput; sp.err = c->err_word;
         sp.stamps = nullptr; sp.wait_ns = OMB_WAIT_NS;
-        const bool b16 = nDtype == OM_DTYPE_BF16;
-        switch (nCout) {
-            case 32: return b16 ? launch_stem_pool<32, OM_DTYPE_BF16>(c, ta, tb, sp)
-                                : launch_stem_pool<32, OM_DTYPE_F16>(c, ta, tb, sp);
-            case 64: return b16 ? launch_stem_pool<64, OM_DTYPE_BF16>(c, ta, tb, sp)
-                                : launch_stem_pool<64, OM_DTYPE_F16>(c, ta, tb, sp);
-            case 128: return b16 ? launch_stem_pool<128, OM_DTYPE_BF16>(c, ta, tb, sp)
-                                 : launch_stem_pool<128, OM_DTYPE_F16>(c, ta, tb, sp);
-        }
-        return OM_ERR_UNSUPPORTED;
+        // the patch of a stem row pair: R + 1 space-to-depth rows (past the map: zeros)
+        cuuint32_t a_box5[4] = {16, (cuuint32_t)p.box_w, (cuuint32_t)(g.th + 1), 1};
+        r = g_encode_tiled(&ta, dt, 4, pWorkspace, a_dims, a_strides, a_box5, a_estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_32B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) return OM_ERR_DRIVER;
+        return nDtype == OM_DTYPE_BF16 ? launch_stem_pool<OM_DTYPE_BF16>(c, ta, tb, sp)
+                                       : launch_stem_pool<OM_DTYPE_F16>(c, ta, tb, sp);
     }
     return finish_and_launch<MODE_STEM>(c, bn, occ, mt, ew, nDtype, ta, tb, p);
 }

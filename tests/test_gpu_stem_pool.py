@@ -15,14 +15,15 @@ from conftest import rel_err
 pytestmark = pytest.mark.gpu
 
 # n, h, w, cout, act, dtype, input dtype. Odd sizes give an odd stem output (the last pooled
-# row and column have a two-wide window); batch 3 and 37 make CTA ranges cross image boundaries.
+# row and column have a two-wide window, the last stem row pair has one row); batch 3 and 37
+# make CTA ranges cross image boundaries and start at halo pairs.
 CASES = [
     (2, 224, 224, 64, "relu", "bf16", "f32"),     # the ResNet-50 stem
     (2, 224, 224, 64, "relu", "bf16", "bf16"),    # the same from a bf16 image
     (3, 221, 221, 64, "relu", "f16", "f32"),      # 111 x 111 stem output
     (37, 64, 48, 64, "none", "bf16", "f32"),      # negative values, 32 x 24 stem output, 37 images
-    (2, 100, 90, 32, "relu6", "bf16", "f32"),     # 32 channels
-    (2, 90, 100, 128, "relu", "f16", "f16"),      # 128 channels
+    (2, 100, 90, 64, "relu6", "bf16", "f32"),     # ReLU6, 50 x 45 stem output
+    (2, 90, 100, 64, "relu", "f16", "f16"),       # fp16 image, 45 x 50 stem output
     (256, 224, 224, 64, "relu", "bf16", "bf16"),  # the benchmarked batch
 ]
 ACT = {"none": 0, "relu": 1, "relu6": 2}
@@ -95,8 +96,11 @@ def test_stem_pool_rejects_unsupported_shapes(gpu):
     from omnimatchdeeplearningtool_b200 import _lib
     from omnimatchdeeplearningtool_b200._lib import lib
     bf = _lib.DTYPE_BF16
-    # 96 output channels, a stem output wider than 128, fp32: not taken, nothing launched
-    assert lib.omCudaStemPoolSupported(2, 3, 224, 224, 96, 7, 7, 2, 3, bf) == 0
+    # 32, 96 or 128 output channels, a stem output wider than 128, a 3x3 stem (two tap
+    # columns after space-to-depth), fp32: not taken, nothing launched
+    for k in (32, 96, 128):
+        assert lib.omCudaStemPoolSupported(2, 3, 224, 224, k, 7, 7, 2, 3, bf) == 0
+    assert lib.omCudaStemPoolSupported(2, 3, 224, 224, 64, 3, 3, 2, 1, bf) == 0
     assert lib.omCudaStemPoolSupported(2, 3, 224, 300, 64, 7, 7, 2, 3, bf) == 0
     assert lib.omCudaStemPoolSupported(2, 3, 224, 224, 64, 7, 7, 2, 3, _lib.DTYPE_F32) == 0
     assert lib.omCudaStemConvBnActPoolIn(16, 0, 16, 16, 16, 16, 2, 3, 224, 224, 96, 7, 7, 2, 3,
