@@ -1616,10 +1616,11 @@ namespace tc {
 //     output column m is patch pixel (r', m + s), read in place by the MMA as with MODE_STEM.
 //     The B operand, k-block r' = [packed tap row r' for dy = 0; tap row r' - 1 for dy = 1], is
 //     loaded once per CTA from the packed stem weight (tap rows outside it read as zeros);
-//   - the 8 epilogue warps turn the accumulator into 16-bit values (bias, act) in a three-row
+//   - the 16 epilogue warps turn the accumulator into 16-bit values (bias, act) in a five-row
 //     ring in shared memory; after each tile they compute pooled row y2 with the pool kernel's
 //     comparisons in its order (window row, then column; positions outside the map take the
-//     lowest value) and store it.
+//     lowest value) and store it. Five rows let the next pair be written while the pool reads
+//     the last three, so the warps meet once per pooled row.
 // Results are bit-identical to omCudaStemConvBnActIn followed by omCudaMaxPool2dNhwc.
 struct StemPoolParams {
     int P, Q, P2, Q2, K;      // stem output P x Q x K, pooled P2 x Q2 x K
@@ -1636,7 +1637,8 @@ struct StemPoolParams {
 constexpr int SP_BN = 64;                 // stem channels
 constexpr int SP_N = 2 * SP_BN;           // MMA N: two stem rows
 constexpr int SP_KB = STEM_MAX_R + 1;     // k-blocks: space-to-depth rows of a row pair
-constexpr int SP_PATCH_BYTES = 22528;     // >= 5 * (127 + 4) * 32, 1 KB multiple
+constexpr int SP_PATCH_BYTES = 21504;     // >= 5 * (127 + 4) * 32, 1 KB multiple
+constexpr int SP_RING = 5;                // stem rows kept: a pooled row's three and the next pair
 static_assert(SP_PATCH_BYTES >= SP_KB * (BM - 1 + 4) * 32, "patch size");
 static_assert(SP_PATCH_BYTES % 1024 == 0, "patch buffers stay 1024-byte aligned");
 
@@ -1646,13 +1648,13 @@ struct StemPoolCfg {
     static constexpr int PATCH_BYTES = STEM_PATCH_BUFS * SP_PATCH_BYTES;
     static constexpr int CH = SP_BN / 8;                    // 16-byte chunks per pixel
     static constexpr int ROW_BYTES = BM * SP_BN * 2;        // one stem row, <= 128 pixels
-    static constexpr int RING_BYTES = 3 * ROW_BYTES;
+    static constexpr int RING_BYTES = SP_RING * ROW_BYTES;
     static constexpr int BIAS_BYTES = SP_BN * 4;
     static constexpr int BAR_BYTES = 256;
     static constexpr int SMEM_BYTES =
         W_BYTES + PATCH_BYTES + RING_BYTES + BIAS_BYTES + BAR_BYTES + 1024;
     static constexpr int TMEM_COLS = 2 * SP_N;
-    static constexpr int EW = 8;
+    static constexpr int EW = 16;          // epilogue warps, four per TMEM lane quarter
     static_assert(SMEM_BYTES <= MAX_DYN_SMEM, "shared memory budget");
 };
 
@@ -1680,7 +1682,7 @@ __device__ __forceinline__ int stem_pool_tiles(const StemPoolParams& p, int g, i
 }
 
 template <int DT>
-__global__ void __launch_bounds__(64 + 32 * 8, 1)
+__global__ void __launch_bounds__(64 + 32 * StemPoolCfg::EW, 1)
     stem_pool_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const StemPoolParams p) {
     using C = StemPoolCfg;
@@ -1837,14 +1839,14 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
         }
     } else {
         // ---------------------------------------------------------------- epilogue
-        // Warp `warp` reads TMEM lane quarter warp % 4 (pixels q = 32 * quarter + lane); the two
-        // warps of a quarter take alternate 32-column chunks (chunk c: stem row y0 + c / 2,
-        // channels (c % 2) * 32 ..). The loop has the same trip count in every epilogue warp
-        // whatever happens (a failed wait only skips work), because the warps meet at named
-        // barriers around each pooled row.
+        // Warp `warp` reads TMEM lane quarter warp % 4 (pixels q = 32 * quarter + lane); the
+        // EW / 4 warps of a quarter take the 32-column chunks round-robin (chunk c: stem row
+        // y0 + c / 2, channels (c % 2) * 32 ..). The loop has the same trip count in every epilogue warp
+        // whatever happens (a failed wait only skips work), because the warps meet at a named
+        // barrier before each pooled row.
         const int ew = warp - 2;
         const int quarter = warp & 3;
-        const int half = ew >> 2;
+        const int slot = ew >> 2;
         const int q = quarter * 32 + lane;
         const bool clamp = p.act != OM_ACT_NONE;
         const float act_hi = p.act == OM_ACT_RELU6 ? 6.f : INFINITY;
@@ -1867,7 +1869,7 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
                 if (ok) {
                     tc_fence_after();
 #pragma unroll 1
-                    for (int c = half; c < SP_N / 32; c += 2) {
+                    for (int c = slot; c < SP_N / 32; c += C::EW / 4) {
                         uint32_t v[32];
                         tmem_ld32(t_quarter + (uint32_t)(acc * SP_N + c * 32), v);
                         const int col = (c & 1) * 32;
@@ -1889,9 +1891,11 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
                                 for (int k = 0; k < 32; ++k) f[k] = fminf(f[k], act_hi);
                             }
                         }
+                        // ring rows go by this CTA's running pair count, not by the row
+                        // number, which restarts at every image
                         const int r = y0 + (c >> 1);
                         if (q < p.Q && r < p.P) {
-                            uint8_t* row = sRing + (r % 3) * C::ROW_BYTES;
+                            uint8_t* row = sRing + ((2 * local + (c >> 1)) % SP_RING) * C::ROW_BYTES;
 #pragma unroll
                             for (int k = 0; k < 4; ++k) {
                                 uint4 ov;
@@ -1912,6 +1916,7 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
             asm volatile("bar.sync 1, %0;" ::"r"(32 * C::EW) : "memory");
             if (ok && !*abort_flag) {
                 const int tid = threadIdx.x - 64;
+                const int lm = local - 1;   // the pair just written: rows 2 y2, 2 y2 + 1
                 typename H16::T* out = static_cast<typename H16::T*>(p.out) +
                                        ((size_t)n * p.P2 + y2) * p.Q2 * SP_BN;
                 for (int i = tid; i < p.Q2 * C::CH; i += 32 * C::EW) {
@@ -1921,7 +1926,9 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
 #pragma unroll
                     for (int wr = 0; wr < 3; ++wr) {
                         const int hh = 2 * y2 - 1 + wr;
-                        const uint8_t* row = sRing + (hh < 0 ? 0 : hh % 3) * C::ROW_BYTES;
+                        // row 2 y2 - 1 + wr is ring row 2 lm - 1 + wr (row 2 y2 - 1: the previous
+                        // pair's second row)
+                        const uint8_t* row = sRing + ((2 * lm - 1 + wr + SP_RING) % SP_RING) * C::ROW_BYTES;
 #pragma unroll
                         for (int wc = 0; wc < 3; ++wc) {
                             const int ww = 2 * x2 - 1 + wc;
@@ -1937,8 +1944,9 @@ __global__ void __launch_bounds__(64 + 32 * 8, 1)
                         *reinterpret_cast<const uint4*>(m);
                 }
             }
-            // the ring rows read above are rewritten only after every warp is done with them
-            asm volatile("bar.sync 1, %0;" ::"r"(32 * C::EW) : "memory");
+            // The next pair goes to the two ring rows this pool did not read. The pair after
+            // it rewrites rows read here only once every warp has passed the next pool's
+            // barrier, i.e. finished this pool.
         }
         if (!ok && lane == 0) {
             atomicOr(p.err, ERRBIT_TC_EPILOGUE);
