@@ -79,6 +79,14 @@ def _max_over_ranks(dist, v: float) -> float:
     return float(t.item())
 
 
+def _wait_gil_free(event) -> None:
+    """Wait for the compute stream through the backend (a ctypes call, which releases the GIL,
+    so the clock sampler thread keeps sampling during the wait), then for `event`."""
+    from omnimatchdeeplearningtool_b200._lib import call
+    call("omCudaSynchronize")
+    event.synchronize()
+
+
 class ClockSampler:
     """SM clocks and clock-event (throttle) reasons sampled during the timed region: through NVML
     in a background thread every 5 ms (so a timed region of a few tens of ms still gets
@@ -267,7 +275,7 @@ def run_train(args, world, rank, local, dist):
         one_step()
     with torch.cuda.stream(stream):
         e1.record()
-    e1.synchronize()
+    _wait_gil_free(e1)
     dp.check()
     torch.cuda.synchronize()
     launches = backend.launch_count() - l0
@@ -403,7 +411,7 @@ def run_mobilenet(args, world, rank, local, dist):
         for _ in range(args.steps):
             plan.launch()
         e1.record()
-    e1.synchronize()
+    _wait_gil_free(e1)
     _barrier(dist)
     clk = clocks.stop()
     t = _max_over_ranks(dist, e0.elapsed_time(e1) / 1e3)
@@ -707,7 +715,7 @@ def run_ours(args, world, rank, local, dist):
         for _ in range(args.steps):
             plan.launch()
         e1.record()
-    e1.synchronize()
+    _wait_gil_free(e1)
     torch.cuda.synchronize()
     _barrier(dist)
     clk = clocks.stop()
@@ -806,7 +814,7 @@ def run_ours(args, world, rank, local, dist):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="r50-infer",
