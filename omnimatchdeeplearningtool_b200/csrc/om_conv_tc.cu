@@ -138,6 +138,15 @@ __device__ __forceinline__ unsigned long long gtimer() {
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
+// Programmatic dependent launch: the conv kernels are launched so that their prologue (barrier
+// set-up, TMEM allocation) may run on SMs the previous kernel has left while its last CTAs
+// finish. pdl_wait() returns once the previous kernel has completed and its writes are visible;
+// nothing before it touches memory another kernel writes or reads. pdl_launch_dependents()
+// lets the next kernel's CTAs start their own prologue as SMs free up.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
 }
@@ -451,7 +460,6 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
     const int lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
-        if (p.stamps) p.stamps[2 * blockIdx.x] = gtimer();
         for (int i = 0; i < STAGES; ++i) {
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], 1);
@@ -484,6 +492,9 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_holder;
+    pdl_wait();
+    if (threadIdx.x == 0 && p.stamps) p.stamps[2 * blockIdx.x] = gtimer();
+    pdl_launch_dependents();
 
     const int num_tiles = p.num_m_tiles * p.num_n_tiles;
     const int PQ = p.P * p.Q;
@@ -1190,6 +1201,25 @@ static int encode_epilogue_map(CUtensorMap* map, const void* base, int rows, int
     return r == CUDA_SUCCESS ? OM_OK : OM_ERR_DRIVER;
 }
 
+// Launch with programmatic stream serialization: the kernel may start (and run its prologue up
+// to pdl_wait) while the previous kernel on the stream finishes; inside a CUDA graph capture it
+// becomes a programmatic dependency edge.
+template <typename Kern, typename... Args>
+static cudaError_t launch_pdl(Kern kern, int grid, int block, int smem, cudaStream_t st,
+                              const Args&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3((unsigned)block);
+    cfg.dynamicSmemBytes = (size_t)smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 template <int BN, int MODE, int DT, int OCC, int MT = 1, int EW = 4>
 static int launch(DeviceCtx* c, const CUtensorMap& ta, const CUtensorMap& tb,
                   const CUtensorMap& to, const CUtensorMap& tr, const Params& p) {
@@ -1207,7 +1237,8 @@ static int launch(DeviceCtx* c, const CUtensorMap& ta, const CUtensorMap& tb,
     Params q = p;
     q.stamps = take_stamps(c->device, grid);
     take_test_stall(c->device, &q.wait_ns, &q.stall_after);
-    kern<<<grid, cta_threads<MODE, EW>(), Cf::SMEM_BYTES, c->compute>>>(ta, tb, to, tr, q);
+    OMB_CHECK(launch_pdl(kern, grid, cta_threads<MODE, EW>(), Cf::SMEM_BYTES, c->compute, ta, tb,
+                         to, tr, q));
     return after_launch(c);
 }
 
@@ -1709,7 +1740,6 @@ __global__ void __launch_bounds__(64 + 32 * StemPoolCfg::EW, 1)
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
-        if (p.stamps) p.stamps[2 * blockIdx.x] = gtimer();
         mbar_init(wfull, 1);
         for (int i = 0; i < STEM_PATCH_BUFS; ++i) {
             mbar_init(&patch_full[i], 1);
@@ -1737,6 +1767,9 @@ __global__ void __launch_bounds__(64 + 32 * StemPoolCfg::EW, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_holder;
+    pdl_wait();
+    if (threadIdx.x == 0 && p.stamps) p.stamps[2 * blockIdx.x] = gtimer();
+    pdl_launch_dependents();
     int g0, g1;
     stem_pool_range(p.rows2, g0, g1);
     const int kbs = p.R + 1;   // k-blocks of a row pair
@@ -2047,7 +2080,7 @@ static int launch_stem_pool(DeviceCtx* c, const CUtensorMap& ta, const CUtensorM
     long long stall_after;
     take_test_stall(c->device, &wait_ns, &stall_after);
     q.wait_ns = wait_ns;
-    kern<<<grid, 64 + 32 * Cf::EW, Cf::SMEM_BYTES, c->compute>>>(ta, tb, q);
+    OMB_CHECK(launch_pdl(kern, grid, 64 + 32 * Cf::EW, Cf::SMEM_BYTES, c->compute, ta, tb, q));
     return after_launch(c);
 }
 }  // namespace tc
@@ -2284,7 +2317,6 @@ __global__ void __launch_bounds__(64 + 32 * PAIR_EW, 1)
     const int nch2 = p.K2 / PAIR_BN2;
 
     if (threadIdx.x == 0) {
-        if (p.stamps) p.stamps[2 * blockIdx.x] = gtimer();
         for (int i = 0; i < STAGES; ++i) {
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], 1);
@@ -2318,6 +2350,9 @@ __global__ void __launch_bounds__(64 + 32 * PAIR_EW, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_holder;
+    pdl_wait();
+    if (threadIdx.x == 0 && p.stamps) p.stamps[2 * blockIdx.x] = gtimer();
+    pdl_launch_dependents();
     const int PQ = p.P * p.Q;
 
     if (warp == 0) {
@@ -2691,7 +2726,8 @@ static int launch_pair(DeviceCtx* c, const CUtensorMap& ta, const CUtensorMap& t
     const int grid = p.num_tiles < c->num_sms ? p.num_tiles : c->num_sms;
     PairParams q = p;
     q.stamps = take_stamps(c->device, grid);
-    kern<<<grid, 64 + 32 * PAIR_EW, Cf::SMEM_BYTES, c->compute>>>(ta, tb1, tb2, to, tr, q);
+    OMB_CHECK(launch_pdl(kern, grid, 64 + 32 * PAIR_EW, Cf::SMEM_BYTES, c->compute, ta, tb1, tb2,
+                         to, tr, q));
     return after_launch(c);
 }
 
