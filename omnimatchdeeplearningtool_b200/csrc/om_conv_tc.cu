@@ -34,6 +34,10 @@
 //               32 B, written with the 32-byte swizzle (SBO = 256 B) and consumed by one K=16
 //               MMA. A k-block past the last tap loads and multiplies only the taps that exist.
 //               B is SW128 as above.
+//   MODE_SW64:  Cs == 32 (the 32-channel MobileNet layers). As MODE_SW32 with 64-byte rows: a
+//               k-block is two taps, each one im2col box of 128 pixels x 32 channels written
+//               with the 64-byte swizzle (SBO = 512 B) and consumed by two K=16 MMAs (the second
+//               32 B further into the swizzled row).
 //   MODE_TF32:  the fp32 path, 3xTF32. Operands are fp32 NHWC / K-major, each split into a
 //               TF32 "hi" part and the TF32 rounding of the remainder ("lo"): x = hi + lo to
 //               about 2^-22. A stage holds A_hi, A_lo (im2col boxes of 128 pixels x 32 fp32
@@ -41,7 +45,7 @@
 //               issues hi*hi (kind::tf32) into a main fp32 accumulator and lo*hi + hi*lo into a
 //               correction accumulator beside it; the epilogue adds the two. Output fp32 NCHW,
 //               stored directly. The kernel's four maps are A_hi, B_hi, B_lo, A_lo.
-//   MODE_INTERLEAVE: Cs % 8 == 0 (the 32-channel MobileNet layers). A stage holds 8 im2col
+//   MODE_INTERLEAVE: Cs % 8 == 0, other channel counts. A stage holds 8 im2col
 //               boxes of 128 pixels x 8 channels (2 KB each, no swizzle): core matrices of
 //               8 rows x 16 B, SBO = 128 B (next 8 rows), LBO = 2 KB (next 8 K-elements).
 //   MODE_STEM:  the image stem as a stride-1 R x S convolution over a 16-channel
@@ -95,8 +99,11 @@ constexpr int STEM_PATCH_BUFS = 3;                     // two tiles' loads in fl
 constexpr int STEM_EXTRA_BYTES = STEM_PATCH_BUFS * STEM_PATCH_BYTES;
 constexpr unsigned long long OMB_WAIT_NS = 2000000000ull;  // 2 s per wait
 
-enum { MODE_SW128 = 0, MODE_INTERLEAVE = 1, MODE_STEM = 2, MODE_SW32 = 3, MODE_TF32 = 4 };
-constexpr int SW32_BOX_BYTES = BM * 16 * 2;            // MODE_SW32: one tap, 128 px x 16 ch
+enum { MODE_SW128 = 0, MODE_INTERLEAVE = 1, MODE_STEM = 2, MODE_SW32 = 3, MODE_TF32 = 4,
+       MODE_SW64 = 5 };
+// MODE_SW32 / MODE_SW64: channels per tap, taps per k-block, bytes of one tap's im2col box
+template <int MODE> __host__ __device__ constexpr int tap_ch() { return MODE == MODE_SW64 ? 32 : 16; }
+template <int MODE> __host__ __device__ constexpr int tap_box_bytes() { return BM * tap_ch<MODE>() * 2; }
 
 struct Params {
     int N, H, W, Cs;
@@ -123,10 +130,12 @@ struct Params {
     long long stall_after;
 };
 
-// MODE_SW32: filter taps in k-block kb (4, or what is left of the R*S taps in the last one)
+// MODE_SW32 / MODE_SW64: filter taps in k-block kb (BK / Cs of them, or what is left of the
+// R*S taps in the last one)
 __device__ __forceinline__ int sw32_taps(const Params& p, int kb) {
-    const int left = p.R * p.S - kb * (BK / 16);
-    return left < BK / 16 ? left : BK / 16;
+    const int per = BK / p.Cs;
+    const int left = p.R * p.S - kb * per;
+    return left < per ? left : per;
 }
 
 // ---------------------------------------------------------------- PTX wrappers
@@ -319,7 +328,8 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint
     d |= (uint64_t)layout << 61;
     return d;
 }
-constexpr uint32_t LAYOUT_NONE = 0, LAYOUT_SW128_BASE32B = 1, LAYOUT_SW128 = 2, LAYOUT_SW32 = 6;
+constexpr uint32_t LAYOUT_NONE = 0, LAYOUT_SW128_BASE32B = 1, LAYOUT_SW128 = 2, LAYOUT_SW64 = 4,
+                   LAYOUT_SW32 = 6;
 
 // Instruction descriptor for kind::f16: D fp32, A/B bf16 (1) or f16 (0), both K-major,
 // N>>3 at [17,23), M>>4 at [24,29).
@@ -427,7 +437,8 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
     conv_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmOut,
                    const __grid_constant__ CUtensorMap tmRes, const Params p) {
-    static_assert(MT == 1 || ((MODE == MODE_SW128 || MODE == MODE_SW32) && BN <= 128 && OCC == 1),
+    static_assert(MT == 1 || ((MODE == MODE_SW128 || MODE == MODE_SW32 || MODE == MODE_SW64) &&
+                              BN <= 128 && OCC == 1),
                   "MT = 2 tiles");
     static_assert(EW == 4 || (EW == 16 && OCC == 1 && MODE != MODE_STEM) || (EW == 8 && OCC == 1),
                   "epilogue warps");
@@ -610,19 +621,18 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
                                 ++fr;
                             }
                         }
-                    } else if (MODE == MODE_SW32) {
-                        // kk = kb * 64 + j * 16 = (fr * S + fs) * 16: box j is filter tap
-                        // kb * 4 + j; the k-block holds nt of them (fewer only in the last)
+                    } else if (MODE == MODE_SW32 || MODE == MODE_SW64) {
+                        // kk = kb * 64 + j * Cs = (fr * S + fs) * Cs: box j is filter tap
+                        // kb * (64 / Cs) + j; the k-block holds nt of them (fewer only in the last)
+                        constexpr int TB = tap_box_bytes<MODE>();
                         const int nt = sw32_taps(p, kb);
-                        mbar_expect_tx(&full[stage],
-                                       (uint32_t)(MT * nt * SW32_BOX_BYTES + C::B_STAGE_BYTES));
+                        mbar_expect_tx(&full[stage], (uint32_t)(MT * nt * TB + C::B_STAGE_BYTES));
                         for (int j = 0; j < nt; ++j) {
-                            tma_load_im2col(a_dst + j * SW32_BOX_BYTES, &tmA, &full[stage], 0, wb,
-                                            hb, img, (uint16_t)fs, (uint16_t)fr);
+                            tma_load_im2col(a_dst + j * TB, &tmA, &full[stage], 0, wb, hb, img,
+                                            (uint16_t)fs, (uint16_t)fr);
                             if (MT == 2)
-                                tma_load_im2col(a_dst + A_STAGE_BYTES + j * SW32_BOX_BYTES, &tmA,
-                                                &full[stage], 0, wb1, hb1, img1, (uint16_t)fs,
-                                                (uint16_t)fr);
+                                tma_load_im2col(a_dst + A_STAGE_BYTES + j * TB, &tmA, &full[stage],
+                                                0, wb1, hb1, img1, (uint16_t)fs, (uint16_t)fr);
                             if (++fs == p.S) {
                                 fs = 0;
                                 ++fr;
@@ -685,12 +695,14 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
             const uint64_t adesc0 =
                 MODE == MODE_INTERLEAVE ? smem_desc(smem_u32(sA), BM * 16, 128, LAYOUT_NONE)
                 : MODE == MODE_SW32     ? smem_desc(smem_u32(sA), 16, 256, LAYOUT_SW32)
+                : MODE == MODE_SW64     ? smem_desc(smem_u32(sA), 16, 512, LAYOUT_SW64)
                                         : smem_desc(smem_u32(sA), 16, 1024, LAYOUT_SW128);
             const uint64_t bdesc0 = MODE != MODE_INTERLEAVE
                                         ? smem_desc(smem_u32(sB), 16, 1024, LAYOUT_SW128)
                                         : smem_desc(smem_u32(sB), BN * 16, 128, LAYOUT_NONE);
             constexpr uint32_t A_K_STEP = MODE == MODE_INTERLEAVE ? (2 * BM * 16) >> 4
-                                          : MODE == MODE_SW32     ? SW32_BOX_BYTES >> 4
+                                          : (MODE == MODE_SW32 || MODE == MODE_SW64)
+                                              ? tap_box_bytes<MODE>() >> 4
                                                                   : 32 >> 4;
             constexpr uint32_t B_K_STEP = MODE != MODE_INTERLEAVE ? 32 >> 4 : (2 * BN * 16) >> 4;
             int stage = 0;
@@ -775,14 +787,20 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
                             tc_mma_tf32(d_corr, ah, bh + B_LO, IDESC_TF, 1u);
                             tc_mma_tf32(d_tmem, ah, bh, IDESC_TF, acc_in);
                         }
-                    } else if (MODE == MODE_SW32) {
+                    } else if (MODE == MODE_SW32 || MODE == MODE_SW64) {
+                        // tap k: Cs / 16 MMAs, the h-th 32 B into the tap's swizzled rows
+                        constexpr int HPT = tap_ch<MODE>() / 16;
                         const int nt = sw32_taps(p, kb);
                         for (int k = 0; k < nt; ++k)
 #pragma unroll
-                            for (int mt = 0; mt < MT; ++mt)
-                                tc_mma(d_tmem + (uint32_t)(mt * BN),
-                                       ad + (uint64_t)(mt * (A_STAGE_BYTES >> 4)) + k * A_K_STEP,
-                                       bd + k * B_K_STEP, IDESC, (kb > 0 || k > 0) ? 1u : 0u);
+                            for (int h = 0; h < HPT; ++h)
+#pragma unroll
+                                for (int mt = 0; mt < MT; ++mt)
+                                    tc_mma(d_tmem + (uint32_t)(mt * BN),
+                                           ad + (uint64_t)(mt * (A_STAGE_BYTES >> 4)) + k * A_K_STEP +
+                                               h * (32 >> 4),
+                                           bd + (k * HPT + h) * B_K_STEP, IDESC,
+                                           (kb > 0 || k > 0 || h > 0) ? 1u : 0u);
                     } else {
 #pragma unroll
                         for (int k = 0; k < BK / 16; ++k)
@@ -1246,7 +1264,7 @@ template <int MODE, int DT>
 static int dispatch_bn(DeviceCtx* c, int bn, int occ, int mt, int ew, const CUtensorMap& ta,
                        const CUtensorMap& tb, const CUtensorMap& to, const CUtensorMap& tr,
                        const Params& p) {
-    if constexpr (MODE == MODE_SW128 || MODE == MODE_SW32) {
+    if constexpr (MODE == MODE_SW128 || MODE == MODE_SW32 || MODE == MODE_SW64) {
         if (ew == 16) {
             if (mt != 2) return OM_ERR_UNSUPPORTED;
             switch (bn) {
@@ -1410,7 +1428,10 @@ extern "C" int omCudaConvTilePlan(int nBatch, int nH, int nW, int nCs, int nCout
     const int P = (nH + 2 * nPad - nKH) / nStride + 1;
     const int Q = (nW + 2 * nPad - nKW) / nStride + 1;
     if (P <= 0 || Q <= 0) return OM_ERR_INVALID;
-    const int mode = (nCs % 64 == 0) ? MODE_SW128 : (nCs == 16 ? MODE_SW32 : MODE_INTERLEAVE);
+    const int mode = (nCs % 64 == 0) ? MODE_SW128
+                     : nCs == 16     ? MODE_SW32
+                     : nCs == 32     ? MODE_SW64
+                                     : MODE_INTERLEAVE;
     const long long kpad = ((long long)nKH * nKW * nCs + BK - 1) / BK * BK;
     const long long m_tiles = ((long long)nBatch * P * Q + BM - 1) / BM;
     choose_tile(nCout, (int)(kpad / BK), m_tiles, c->num_sms, mode != MODE_INTERLEAVE,
@@ -1481,7 +1502,10 @@ extern "C" int omCudaConv2dBnAct(const void* pInput, const void* pPacked, const 
     if (Mll >= (1LL << 31)) return OM_ERR_UNSUPPORTED;
     if (!load_driver_entry_points()) return OM_ERR_DRIVER;
 
-    const int mode = (nCs % 64 == 0) ? MODE_SW128 : (nCs == 16 ? MODE_SW32 : MODE_INTERLEAVE);
+    const int mode = (nCs % 64 == 0) ? MODE_SW128
+                     : nCs == 16     ? MODE_SW32
+                     : nCs == 32     ? MODE_SW64
+                                     : MODE_INTERLEAVE;
     const long long kk_total = (long long)nKH * nKW * nCs;
     const long long kpad = (kk_total + BK - 1) / BK * BK;
     const bool sw128 = mode == MODE_SW128;
@@ -1519,9 +1543,12 @@ extern "C" int omCudaConv2dBnAct(const void* pInput, const void* pPacked, const 
     cuuint32_t a_estr[4] = {1, (cuuint32_t)nStride, (cuuint32_t)nStride, 1};
     CUresult r = g_encode_im2col(
         &ta, dt, 4, const_cast<void*>(pInput), a_dims, a_strides, lo, hi,
-        sw128 ? 64 : (mode == MODE_SW32 ? 16 : 8), BM, a_estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-        sw128 ? CU_TENSOR_MAP_SWIZZLE_128B
-              : (mode == MODE_SW32 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_NONE),
+        sw128 ? 64 : (mode == MODE_SW32 ? 16 : (mode == MODE_SW64 ? 32 : 8)), BM, a_estr,
+        CU_TENSOR_MAP_INTERLEAVE_NONE,
+        sw128                ? CU_TENSOR_MAP_SWIZZLE_128B
+        : mode == MODE_SW32  ? CU_TENSOR_MAP_SWIZZLE_32B
+        : mode == MODE_SW64  ? CU_TENSOR_MAP_SWIZZLE_64B
+                             : CU_TENSOR_MAP_SWIZZLE_NONE,
         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return OM_ERR_DRIVER;
     // Drivers up to 13.1 mis-handle this descriptor bit for im2col tensors under 128 KiB;
@@ -1543,6 +1570,7 @@ extern "C" int omCudaConv2dBnAct(const void* pInput, const void* pPacked, const 
 
     if (mode == MODE_SW128) return finish_and_launch<MODE_SW128>(c, bn, occ, mt, ew, nDtype, ta, tb, p);
     if (mode == MODE_SW32) return finish_and_launch<MODE_SW32>(c, bn, occ, mt, ew, nDtype, ta, tb, p);
+    if (mode == MODE_SW64) return finish_and_launch<MODE_SW64>(c, bn, occ, mt, ew, nDtype, ta, tb, p);
     return finish_and_launch<MODE_INTERLEAVE>(c, bn, occ, mt, ew, nDtype, ta, tb, p);
 }
 

@@ -21,7 +21,11 @@ CASES = [
     (3, 64, 15, 128, 3, 2, 1, "bf16", False, "relu", False),      # stride 2, ragged M
     (2, 64, 14, 256, 1, 2, 0, "bf16", False, "none", False),      # strided 1x1 downsample
     (2, 3, 32, 64, 7, 2, 3, "bf16", False, "relu", False),        # ImageNet stem, Cs=8
-    (2, 32, 16, 128, 1, 1, 0, "f16", False, "relu6", False),      # C=32 interleaved
+    (2, 32, 16, 128, 1, 1, 0, "f16", False, "relu6", False),      # C=32: 64-byte swizzle
+    (2, 32, 15, 64, 3, 1, 1, "bf16", True, "relu", False),        # C=32, 9 taps: 2+2+2+2+1
+    (3, 32, 17, 96, 3, 2, 1, "f16", False, "relu6", False),       # C=32, stride 2
+    (8, 32, 112, 128, 1, 1, 0, "bf16", False, "relu6", False),    # MobileNet expand, large M
+    (2, 40, 12, 64, 1, 1, 0, "bf16", False, "relu", False),       # C=40: interleaved boxes
     (2, 128, 8, 32, 1, 1, 0, "f16", True, "none", False),         # BN=32 + residual
     (2, 64, 14, 64, 3, 1, 1, "f16", True, "relu", False),         # fp16 + residual
     (16, 64, 56, 256, 1, 1, 0, "bf16", True, "relu", False),      # BN=256 tiles
