@@ -1656,6 +1656,324 @@ __global__ void stem_s2d_kernel(const S* __restrict__ x, T* __restrict__ out, in
 }  // namespace tc
 }  // namespace omb
 
+// ---------------------------------------------------------------- depthwise 3x3 (TMA row ring)
+namespace omb {
+namespace tc {
+
+// fp16 3x3 depthwise conv + bias + act (omCudaDepthwiseConv2dNhwc), stride 1 or 2, padding 1,
+// on a ring of input rows in shared memory. The work is the list of output rows (n, channel
+// tile, p), p fastest; each CTA takes an equal contiguous range of it, which falls into one or a
+// few runs of rows of one (image, channel tile). A producer warp walks the input rows those runs
+// read, one TMA box per row (columns -1 .. the last one a window reaches, one channel tile;
+// padding rows and columns arrive as TMA zero fill), into the next free ring slot. Fifteen
+// compute warps wait for the rows an output row (stride 1: an output row pair) reads, compute
+// it from shared memory and free the rows the next one no longer reads. One CTA per SM holds a
+// ring of up to 200 KB, so a dozen rows are in flight while the current ones are computed. Every input row is
+// loaded once per run, and the loads of the next rows overlap the arithmetic on the current
+// ones. An item is one (output column, 8-channel group); a thread's channel group is fixed, so
+// its weights (BN scale folded) and bias are held as fp16 pairs, and the taps are accumulated
+// with HFMA2 in the order of the direct kernel: the results are the same bits.
+constexpr int DW_COMPUTE_WARPS = 15;
+constexpr int DW_THREADS = 32 * (DW_COMPUTE_WARPS + 1);  // + the producer warp
+constexpr int DW_MAX_SLOTS = 32;
+constexpr int DW_RING_BYTES = 200 * 1024;               // one CTA per SM
+constexpr int DW_MAX_SLOT_BYTES = 16 * 1024;
+
+struct DwParams {
+    int N, H, W, Cs, P, Q, stride;
+    int CW;              // channels per tile (64, 128 or 256)
+    int CT;              // channel tiles, Cs / CW
+    int rows;            // output rows in the work list, N * CT * P
+    int slots;           // ring slots
+    int wbox;            // input columns per slot
+    int slot_bytes;      // wbox * CW * 2, rounded up to 128
+    const float* wpk;    // [9][Cs] fp32
+    const float* bias;   // [Cs] fp32
+    __half* out;
+    int act;
+    unsigned int* err;
+};
+
+// A run: output rows p0 .. p1-1 of image n, channel tile ct. It reads input rows
+// p0*stride - 1 .. (p1-1)*stride + 1: runs of stride 1 read p1 - p0 + 2 rows, of stride 2
+// 2 (p1 - p0) + 1.
+struct DwRun {
+    int n, ct, p0, p1, nrows;
+};
+__device__ __forceinline__ int dw_range_start(const DwParams& p, int b) {
+    return (int)((long long)p.rows * b / gridDim.x);
+}
+__device__ __forceinline__ DwRun dw_run(const DwParams& p, int cur, int end) {
+    const int img = cur / p.P;                    // n * CT + ct
+    DwRun r;
+    r.p0 = cur - img * p.P;
+    const int stop = min(end, (img + 1) * p.P);
+    r.p1 = stop - img * p.P;
+    r.n = img / p.CT;
+    r.ct = img - r.n * p.CT;
+    r.nrows = p.stride == 1 ? r.p1 - r.p0 + 2 : 2 * (r.p1 - r.p0) + 1;
+    return r;
+}
+
+__global__ void __launch_bounds__(DW_THREADS, 1)
+    depthwise_ring_kernel(const __grid_constant__ CUtensorMap tmIn, const DwParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* ring = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint64_t* full = reinterpret_cast<uint64_t*>(ring + (size_t)p.slots * p.slot_bytes);
+    uint64_t* empty = full + p.slots;
+    __shared__ int s_abort;
+    const int S = p.slots;
+    if (threadIdx.x == 0) {
+        s_abort = 0;
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], DW_COMPUTE_WARPS);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        fence_async_smem();
+    }
+    __syncthreads();
+    const int start = dw_range_start(p, blockIdx.x);
+    const int end = dw_range_start(p, blockIdx.x + 1);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    if (warp == 0) {
+        // ---- producer: one TMA box per input row, in the order the compute warps read them
+        if (lane != 0) return;
+        const uint32_t load_bytes = (uint32_t)(p.wbox * p.CW * 2);
+        int slot = 0;
+        uint32_t ph = 0, issued = 0;
+        bool ok = true;
+        for (int cur = start; ok && cur < end;) {
+            const DwRun r = dw_run(p, cur, end);
+            const int h0 = r.p0 * p.stride - 1;
+            for (int j = 0; j < r.nrows; ++j) {
+                if (!mbar_wait(&empty[slot], ph ^ 1, &s_abort, OMB_WAIT_NS)) {
+                    atomicOr(p.err, ERRBIT_TC_PRODUCER);
+                    s_abort = 1;
+                    ok = false;
+                    break;
+                }
+                mbar_expect_tx(&full[slot], load_bytes);
+                tma_load_4d(ring + (size_t)slot * p.slot_bytes, &tmIn, &full[slot], r.ct * p.CW,
+                            -1, h0 + j, r.n);
+                ++issued;
+                if (++slot == S) { slot = 0; ph ^= 1; }
+            }
+            cur += r.p1 - r.p0;
+        }
+        // the compute warps may leave early (a wait that gave up): wait (bounded) until the
+        // loads still in flight have landed, so that no TMA write outlives the CTA. Older rows'
+        // slots were reused, which needed the compute warps to have seen those rows land.
+        const uint32_t first = issued > (uint32_t)S ? issued - S : 0;
+        for (uint32_t g = first; g < issued; ++g)
+            if (!mbar_wait_drain(&full[g % S], (g / S) & 1)) atomicOr(p.err, ERRBIT_TC_DRAIN);
+        return;
+    }
+
+    // ---- compute warps
+    const int ctid = threadIdx.x - 32;
+    const int CW8 = p.CW >> 3;
+    const int cg = ctid & (CW8 - 1);            // this thread's 8-channel group in the tile
+    const int items = p.Q * CW8;
+    const int C8 = p.Cs >> 3;
+    const __half2 zero = __float2half2_rn(0.f), six = __float2half2_rn(6.f);
+    auto finish = [&](const __half2 (&acc)[4]) {
+        uint4 o;
+        __half2* o2 = reinterpret_cast<__half2*>(&o);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            __half2 a = acc[j];
+            if (p.act == OM_ACT_RELU) a = __hmax2(a, zero);
+            else if (p.act == OM_ACT_RELU6) a = __hmin2(__hmax2(a, zero), six);
+            o2[j] = a;
+        }
+        return o;
+    };
+    // cursors over the ring: the next row to wait for, and the oldest row still held
+    int wslot = 0, rslot = 0;
+    uint32_t wph = 0;
+    int loaded_ct = -1;
+    __half2 wt[9][4], bh[4];
+    const uint8_t* cgbase = ring + (size_t)cg * 16;
+    for (int cur = start; cur < end;) {
+        const DwRun r = dw_run(p, cur, end);
+        cur += r.p1 - r.p0;
+        if (r.ct != loaded_ct) {
+            const int c = r.ct * p.CW + cg * 8;
+#pragma unroll
+            for (int t = 0; t < 9; ++t) {
+                const float4* w4 = reinterpret_cast<const float4*>(p.wpk + (size_t)t * p.Cs + c);
+                const float4 wa = __ldg(w4), wb = __ldg(w4 + 1);
+                wt[t][0] = __floats2half2_rn(wa.x, wa.y);
+                wt[t][1] = __floats2half2_rn(wa.z, wa.w);
+                wt[t][2] = __floats2half2_rn(wb.x, wb.y);
+                wt[t][3] = __floats2half2_rn(wb.z, wb.w);
+            }
+            const float4* b4 = reinterpret_cast<const float4*>(p.bias + c);
+            const float4 ba = __ldg(b4), bb = __ldg(b4 + 1);
+            bh[0] = __floats2half2_rn(ba.x, ba.y);
+            bh[1] = __floats2half2_rn(ba.z, ba.w);
+            bh[2] = __floats2half2_rn(bb.x, bb.y);
+            bh[3] = __floats2half2_rn(bb.z, bb.w);
+            loaded_ct = r.ct;
+        }
+        uint4* obase = reinterpret_cast<uint4*>(p.out) +
+                       (((size_t)r.n * p.P) * p.Q * C8 + (size_t)r.ct * (p.CW >> 3) + cg);
+        int waited = 0, held = 0;   // rows of this run waited for / released so far
+        const int step = p.stride == 1 ? 2 : 1;
+        for (int pp = r.p0; pp < r.p1; pp += step) {
+            const bool two = p.stride == 1 && pp + 1 < r.p1;
+            const int need = p.stride == 1 ? (pp - r.p0) + (two ? 4 : 3) : 2 * (pp - r.p0) + 3;
+            while (waited < need) {
+                // the warp leaves together if any lane gave up
+                if (!__all_sync(0xffffffffu, mbar_wait(&full[wslot], wph, &s_abort, OMB_WAIT_NS))) {
+                    if (lane == 0) atomicOr(p.err, ERRBIT_TC_EPILOGUE);
+                    s_abort = 1;
+                    return;
+                }
+                ++waited;
+                if (++wslot == S) { wslot = 0; wph ^= 1; }
+            }
+            // ring rows held: rslot, rslot + 1, ... (the window's first input row first)
+            const uint8_t* rows[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int s = rslot + k < S ? rslot + k : rslot + k - S;
+                rows[k] = cgbase + (size_t)s * p.slot_bytes;
+            }
+            uint4* orow = obase + ((size_t)pp * p.Q) * C8;
+            if (p.stride == 1) {
+                for (int i = ctid; i < items; i += DW_COMPUTE_WARPS * 32) {
+                    const int q = i / CW8;   // its window: ring columns q .. q + 2
+                    const size_t off = (size_t)q * p.CW * 2;
+                    // input row rr is window row rr of the first output row and window row
+                    // rr - 1 of the second: both accumulate their taps in the order t = 0 .. 8
+                    __half2 a0[4] = {bh[0], bh[1], bh[2], bh[3]};
+                    __half2 a1[4] = {bh[0], bh[1], bh[2], bh[3]};
+#pragma unroll
+                    for (int rr = 0; rr < 4; ++rr) {
+                        if (rr == 3 && !two) break;
+                        uint4 v[3];
+#pragma unroll
+                        for (int sx = 0; sx < 3; ++sx)
+                            v[sx] = *reinterpret_cast<const uint4*>(rows[rr] + off +
+                                                                    (size_t)sx * p.CW * 2);
+#pragma unroll
+                        for (int sx = 0; sx < 3; ++sx) {
+                            const __half2* x = reinterpret_cast<const __half2*>(&v[sx]);
+                            if (rr < 3) {
+#pragma unroll
+                                for (int j = 0; j < 4; ++j)
+                                    a0[j] = __hfma2(x[j], wt[rr * 3 + sx][j], a0[j]);
+                            }
+                            if (rr > 0) {
+#pragma unroll
+                                for (int j = 0; j < 4; ++j)
+                                    a1[j] = __hfma2(x[j], wt[(rr - 1) * 3 + sx][j], a1[j]);
+                            }
+                        }
+                    }
+                    orow[(size_t)q * C8] = finish(a0);
+                    if (two) orow[((size_t)p.Q + q) * C8] = finish(a1);
+                }
+            } else {
+                for (int i = ctid; i < items; i += DW_COMPUTE_WARPS * 32) {
+                    const int q = i / CW8;   // its window: ring columns 2q .. 2q + 2
+                    const size_t off = (size_t)(2 * q) * p.CW * 2;
+                    __half2 a0[4] = {bh[0], bh[1], bh[2], bh[3]};
+#pragma unroll
+                    for (int rr = 0; rr < 3; ++rr) {
+                        uint4 v[3];
+#pragma unroll
+                        for (int sx = 0; sx < 3; ++sx)
+                            v[sx] = *reinterpret_cast<const uint4*>(rows[rr] + off +
+                                                                    (size_t)sx * p.CW * 2);
+#pragma unroll
+                        for (int sx = 0; sx < 3; ++sx) {
+                            const __half2* x = reinterpret_cast<const __half2*>(&v[sx]);
+#pragma unroll
+                            for (int j = 0; j < 4; ++j)
+                                a0[j] = __hfma2(x[j], wt[rr * 3 + sx][j], a0[j]);
+                        }
+                    }
+                    orow[(size_t)q * C8] = finish(a0);
+                }
+            }
+            // the next output row (pair) starts two input rows further down: free two rows
+            __syncwarp();
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+                if (lane == 0) mbar_arrive(&empty[rslot]);
+                if (++rslot == S) rslot = 0;
+            }
+            held += 2;
+        }
+        // the run's last rows
+        for (; held < r.nrows; ++held) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[rslot]);
+            if (++rslot == S) rslot = 0;
+        }
+    }
+}
+
+}  // namespace tc
+}  // namespace omb
+
+// Internal entry for omCudaDepthwiseConv2dNhwc (fp16, 3x3, padding 1, stride 1 or 2): returns
+// OM_ERR_UNSUPPORTED, with nothing launched, for shapes the ring kernel does not take (the
+// caller then runs the direct kernel).
+extern "C" __attribute__((visibility("hidden"))) int omb_depthwise_ring(
+    DeviceCtx* c, const void* pIn, const float* pPacked, const float* pBias, void* pOut, int nN,
+    int nH, int nW, int nCs, int nStride, int nAct) {
+    using namespace omb::tc;
+    if (nN <= 0 || nH <= 0 || nW <= 0 || (nStride != 1 && nStride != 2)) return OM_ERR_UNSUPPORTED;
+    const int P = (nH - 1) / nStride + 1, Q = (nW - 1) / nStride + 1;
+    const int wbox = nStride == 1 ? Q + 2 : 2 * Q + 1;   // input columns -1 .. the last read
+    if (wbox > 256) return OM_ERR_UNSUPPORTED;
+    // the widest channel tile whose row fits a slot
+    int CW = 0;
+    for (int cw = 256; cw >= 64; cw >>= 1)
+        if (nCs % cw == 0 && wbox * cw * 2 <= DW_MAX_SLOT_BYTES) { CW = cw; break; }
+    if (CW == 0) return OM_ERR_UNSUPPORTED;
+    if (!load_driver_entry_points()) return OM_ERR_UNSUPPORTED;
+    const long long rows = (long long)nN * (nCs / CW) * P;
+    if (rows >= (1LL << 31)) return OM_ERR_UNSUPPORTED;
+    DwParams p;
+    p.N = nN; p.H = nH; p.W = nW; p.Cs = nCs; p.P = P; p.Q = Q; p.stride = nStride;
+    p.CW = CW; p.CT = nCs / CW; p.rows = (int)rows; p.wbox = wbox;
+    p.slot_bytes = (wbox * CW * 2 + 127) & ~127;
+    p.slots = DW_RING_BYTES / p.slot_bytes;
+    if (p.slots > DW_MAX_SLOTS) p.slots = DW_MAX_SLOTS;
+    p.wpk = pPacked; p.bias = pBias; p.out = static_cast<__half*>(pOut); p.act = nAct;
+    p.err = c->err_word;
+    CUtensorMap tm;
+    cuuint64_t dims[4] = {(cuuint64_t)nCs, (cuuint64_t)nW, (cuuint64_t)nH, (cuuint64_t)nN};
+    cuuint64_t strides[3] = {(cuuint64_t)nCs * 2, (cuuint64_t)nW * nCs * 2,
+                             (cuuint64_t)nH * nW * nCs * 2};
+    cuuint32_t box[4] = {(cuuint32_t)CW, (cuuint32_t)wbox, 1, 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    if (g_encode_tiled(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(pIn), dims,
+                       strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                       CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return OM_ERR_UNSUPPORTED;
+    const int smem = 1024 + p.slots * p.slot_bytes + 2 * p.slots * 8;
+    static int attr_smem[64] = {0};
+    if (c->device < 0 || c->device >= 64) return OM_ERR_UNSUPPORTED;
+    if (smem > attr_smem[c->device]) {
+        OMB_CHECK(cudaFuncSetAttribute(depthwise_ring_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        attr_smem[c->device] = smem;
+    }
+    long long grid = c->num_sms;
+    if (grid > rows) grid = rows;
+    depthwise_ring_kernel<<<(unsigned)grid, DW_THREADS, smem, c->compute>>>(tm, p);
+    return after_launch(c);
+}
+
 // ---------------------------------------------------------------- stem + max pool
 namespace omb {
 namespace tc {

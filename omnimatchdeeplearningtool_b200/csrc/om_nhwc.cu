@@ -638,6 +638,11 @@ extern "C" int omCudaPackDepthwiseWeight(const float* pWeight, const float* pGam
     return st;
 }
 
+// the ring kernel for fp16 3x3 layers with padding 1 and stride 1 or 2 (om_conv_tc.cu)
+extern "C" __attribute__((visibility("hidden"))) int omb_depthwise_ring(
+    DeviceCtx* c, const void* pIn, const float* pPacked, const float* pBias, void* pOut, int nN,
+    int nH, int nW, int nCs, int nStride, int nAct);
+
 extern "C" int omCudaDepthwiseConv2dNhwc(const void* pIn, const float* pPacked, const float* pBias,
                                          void* pOut, int nN, int nH, int nW, int nCs, int nKH,
                                          int nKW, int nStride, int nPad, int nAct, int nDtype) {
@@ -654,6 +659,11 @@ extern "C" int omCudaDepthwiseConv2dNhwc(const void* pIn, const float* pPacked, 
     uint4* dst = static_cast<uint4*>(pOut);
     const int c8 = nCs / 8;
     const bool k3 = nKH == 3 && nKW == 3;
+    if (nDtype == OM_DTYPE_F16 && k3 && nPad == 1) {
+        const int st = omb_depthwise_ring(c, pIn, pPacked, pBias, pOut, nN, nH, nW, nCs, nStride,
+                                          nAct);
+        if (st != OM_ERR_UNSUPPORTED) return st;
+    }
     // fp16, 3x3, stride 1, every thread on fixed channels: one block per pair of output rows
     const int pair = (nDtype == OM_DTYPE_F16 && k3 && nStride == 1 && threads % c8 == 0) ? 1 : 0;
     const unsigned grid = pair ? (unsigned)((long long)nN * ((P + 1) / 2)) : (unsigned)rows;

@@ -6,7 +6,10 @@
   values, max|a-b|/max|b| <= 1e-5 against the oracle on the rounded input;
 * depthwise conv + BN + ReLU6 (omCudaDepthwiseConv2dNhwc): fp32 accumulation (fp16 3x3 with the
   weights held per thread: fp16 HFMA2 over the 9 taps), 16-bit output: <= 1e-2 against the
-  oracle on rounded input and BN-folded fp32 weights;
+  oracle on rounded input and BN-folded fp32 weights. The fp16 3x3 paths (the TMA row-ring
+  kernel and the direct kernel) are also checked bit for bit against an exact emulation of
+  their arithmetic: the bias and the taps' products accumulated by fused multiply-adds, each
+  rounded once to fp16, in tap order;
 * residual add + activation (omCudaAddActNhwc): one 16-bit rounding of act(a + b).
 Ragged sizes (odd H and W, channels stored padded to a multiple of 8) are included.
 """
@@ -102,7 +105,10 @@ def test_global_avgpool_nhwc(gpu, n, c, h, w, dt):
                                                 (2, 40, 13, 5, 2, "bf16"),   # generic window
                                                 (1, 2048, 9, 3, 1, "f16"),   # C/8 = 256 threads
                                                 (3, 128, 15, 3, 1, "f16"),   # row pairs, odd P
-                                                (2, 64, 16, 3, 2, "f16")])   # fp16 weights held
+                                                (2, 64, 16, 3, 2, "f16"),    # fp16 weights held
+                                                (4, 128, 112, 3, 1, "f16"),  # row ring, MobileNet size
+                                                (2, 192, 7, 3, 1, "f16"),    # ring: 3 channel tiles
+                                                (3, 256, 56, 3, 2, "f16")])  # ring, stride 2
 def test_depthwise_nhwc(gpu, n, c, h, k, stride, dt):
     import oracle as orc
     from omnimatchdeeplearningtool_b200 import _lib
@@ -151,3 +157,63 @@ def test_add_act_nhwc(gpu):
     want = _round16(np.maximum(_round16(a, "bf16") + _round16(bb, "bf16"), 0), "bf16")
     assert gpu.kernel_error() == 0
     assert np.array_equal(got, want)
+
+
+def _hfma_depthwise(x16, w16, b16, stride, act6=True):
+    """Exact model of the fp16 3x3 depthwise kernels' arithmetic on NHWC fp16 input x16
+    [N, H, W, C]: acc = bias; for the taps t = 0..8 (row-major) acc = fp16(x * w + acc), one
+    rounding per fused multiply-add; then ReLU6. The products of two fp16 values and their sum
+    with an fp16 accumulator of these magnitudes are exact in fp64, so rounding that sum to
+    fp16 once is the fused operation's rounding."""
+    n, h, w, c = x16.shape
+    p, q = (h - 1) // stride + 1, (w - 1) // stride + 1
+    xp = np.zeros((n, h + 2, w + 2, c), np.float16)
+    xp[:, 1:h + 1, 1:w + 1] = x16
+    acc = np.broadcast_to(b16, (n, p, q, c)).astype(np.float16)
+    for t in range(9):
+        r, sx = divmod(t, 3)
+        tap = xp[:, r:r + stride * (p - 1) + 1:stride, sx:sx + stride * (q - 1) + 1:stride]
+        acc = (tap.astype(np.float64) * w16[t].astype(np.float64)
+               + acc.astype(np.float64)).astype(np.float16)
+    if act6:
+        acc = np.minimum(np.maximum(acc, np.float16(0)), np.float16(6))
+    return acc
+
+
+@pytest.mark.parametrize("n,c,h,w,stride", [
+    (4, 128, 112, 112, 1),   # ring kernel: MobileNet stage-1 size, 2 channel tiles of 64
+    (3, 256, 56, 56, 2),     # ring kernel, stride 2, 128-channel tiles
+    (2, 1024, 14, 14, 1),    # ring kernel, 256-channel tiles
+    (5, 192, 9, 11, 1),      # ring kernel, ragged, runs that cross images, odd P
+    (3, 64, 15, 13, 2),      # ring kernel, stride 2, odd sizes
+    (2, 32, 20, 18, 1),      # direct kernel (32 channels), row pairs
+    (1, 64, 9, 300, 2),      # direct kernel (row wider than a ring slot)
+])
+def test_depthwise_f16_bit_exact(gpu, n, c, h, w, stride):
+    from omnimatchdeeplearningtool_b200 import _lib
+    from omnimatchdeeplearningtool_b200._lib import call
+    from omnimatchdeeplearningtool_b200.backend import DeviceBuffer
+    rng = np.random.Generator(np.random.PCG64(300 + c + h))
+    x16 = rng.standard_normal((n, h, w, c)).astype(np.float16)
+    wt = (rng.standard_normal((c, 1, 3, 3)) * 0.5).astype(np.float32)
+    g = rng.uniform(0.5, 1.5, c).astype(np.float32)
+    b = (rng.standard_normal(c) * 0.1).astype(np.float32)
+    mu = (rng.standard_normal(c) * 0.1).astype(np.float32)
+    var = rng.uniform(0.5, 1.5, c).astype(np.float32)
+    din = DeviceBuffer.from_numpy(x16)
+    bufs = [DeviceBuffer.from_numpy(a) for a in (wt, g, b, mu, var)]
+    packed, bias = DeviceBuffer(9 * c * 4), DeviceBuffer(c * 4)
+    _KEEP.extend(bufs + [din, packed, bias])
+    call("omCudaPackDepthwiseWeight", *[t.ptr for t in bufs], 1e-5, packed.ptr, bias.ptr, c, 3, 3, c)
+    p, q = (h - 1) // stride + 1, (w - 1) // stride + 1
+    out = DeviceBuffer(n * p * q * c * 2)
+    _KEEP.append(out)
+    call("omCudaDepthwiseConv2dNhwc", din.ptr, packed.ptr, bias.ptr, out.ptr, n, h, w, c, 3, 3,
+         stride, 1, 2, _lib.DTYPE_F16)
+    got = out.to_numpy((n, p, q, c), np.float16)
+    w16 = packed.to_numpy((9, c)).astype(np.float16)
+    b16 = bias.to_numpy((c,)).astype(np.float16)
+    want = _hfma_depthwise(x16, w16, b16, stride)
+    assert gpu.kernel_error() == 0
+    bad = np.flatnonzero(got.view(np.uint16) != want.view(np.uint16))
+    assert bad.size == 0, (bad.size, bad[:5], got.ravel()[bad[:5]], want.ravel()[bad[:5]])
