@@ -236,6 +236,15 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, u
         "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "r"(w)
         : "memory");
 }
+__device__ __forceinline__ void tma_load_5d(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                            int x, int y, int z, int w, int v) {
+    asm volatile(
+        "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "r"(w),
+        "r"(v)
+        : "memory");
+}
 __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int x, int y,
                                              int z) {
     asm volatile(
@@ -1677,11 +1686,12 @@ constexpr int DW_COMPUTE_WARPS = 15;
 constexpr int DW_THREADS = 32 * (DW_COMPUTE_WARPS + 1);  // + the producer warp
 constexpr int DW_MAX_SLOTS = 32;
 constexpr int DW_RING_BYTES = 200 * 1024;               // one CTA per SM
-constexpr int DW_MAX_SLOT_BYTES = 16 * 1024;
+constexpr int DW_MAX_SLOT_BYTES = 32 * 1024;
 
 struct DwParams {
     int N, H, W, Cs, P, Q, stride;
-    int CW;              // channels per tile (64, 128 or 256)
+    int CW;              // channels per tile (64 .. 1024)
+    int CB;              // 256-channel blocks per tile (1 when CW <= 256)
     int CT;              // channel tiles, Cs / CW
     int rows;            // output rows in the work list, N * CT * P
     int slots;           // ring slots
@@ -1756,8 +1766,8 @@ __global__ void __launch_bounds__(DW_THREADS, 1)
                     break;
                 }
                 mbar_expect_tx(&full[slot], load_bytes);
-                tma_load_4d(ring + (size_t)slot * p.slot_bytes, &tmIn, &full[slot], r.ct * p.CW,
-                            -1, h0 + j, r.n);
+                tma_load_5d(ring + (size_t)slot * p.slot_bytes, &tmIn, &full[slot], 0,
+                            r.ct * p.CB, -1, h0 + j, r.n);
                 ++issued;
                 if (++slot == S) { slot = 0; ph ^= 1; }
             }
@@ -1777,6 +1787,10 @@ __global__ void __launch_bounds__(DW_THREADS, 1)
     const int CW8 = p.CW >> 3;
     const int cg = ctid & (CW8 - 1);            // this thread's 8-channel group in the tile
     const int items = p.Q * CW8;
+    // threads that take items: the largest multiple of CW8 (so every item of a thread has its
+    // channel group); the others only keep the ring's bookkeeping
+    const int active = (DW_COMPUTE_WARPS * 32 / CW8) * CW8;
+    const int first_item = ctid < active ? ctid : items;
     const int C8 = p.Cs >> 3;
     const __half2 zero = __float2half2_rn(0.f), six = __float2half2_rn(6.f);
     auto finish = [&](const __half2 (&acc)[4]) {
@@ -1845,7 +1859,7 @@ __global__ void __launch_bounds__(DW_THREADS, 1)
             }
             uint4* orow = obase + ((size_t)pp * p.Q) * C8;
             if (p.stride == 1) {
-                for (int i = ctid; i < items; i += DW_COMPUTE_WARPS * 32) {
+                for (int i = first_item; i < items; i += active) {
                     const int q = i / CW8;   // its window: ring columns q .. q + 2
                     const size_t off = (size_t)q * p.CW * 2;
                     // input row rr is window row rr of the first output row and window row
@@ -1879,7 +1893,7 @@ __global__ void __launch_bounds__(DW_THREADS, 1)
                     if (two) orow[((size_t)p.Q + q) * C8] = finish(a1);
                 }
             } else {
-                for (int i = ctid; i < items; i += DW_COMPUTE_WARPS * 32) {
+                for (int i = first_item; i < items; i += active) {
                     const int q = i / CW8;   // its window: ring columns 2q .. 2q + 2
                     const size_t off = (size_t)(2 * q) * p.CW * 2;
                     __half2 a0[4] = {bh[0], bh[1], bh[2], bh[3]};
@@ -1933,29 +1947,34 @@ extern "C" __attribute__((visibility("hidden"))) int omb_depthwise_ring(
     const int P = (nH - 1) / nStride + 1, Q = (nW - 1) / nStride + 1;
     const int wbox = nStride == 1 ? Q + 2 : 2 * Q + 1;   // input columns -1 .. the last read
     if (wbox > 256) return OM_ERR_UNSUPPORTED;
-    // the widest channel tile whose row fits a slot
+    // the widest channel tile whose row fits a slot (whole pixels where they fit: each row is
+    // then one contiguous read)
     int CW = 0;
-    for (int cw = 256; cw >= 64; cw >>= 1)
+    for (int cw = 1024; cw >= 64; cw >>= 1)
         if (nCs % cw == 0 && wbox * cw * 2 <= DW_MAX_SLOT_BYTES) { CW = cw; break; }
     if (CW == 0) return OM_ERR_UNSUPPORTED;
+    const int CWi = CW < 256 ? CW : 256;        // a TMA box dimension holds at most 256
     if (!load_driver_entry_points()) return OM_ERR_UNSUPPORTED;
     const long long rows = (long long)nN * (nCs / CW) * P;
     if (rows >= (1LL << 31)) return OM_ERR_UNSUPPORTED;
     DwParams p;
     p.N = nN; p.H = nH; p.W = nW; p.Cs = nCs; p.P = P; p.Q = Q; p.stride = nStride;
-    p.CW = CW; p.CT = nCs / CW; p.rows = (int)rows; p.wbox = wbox;
+    p.CW = CW; p.CB = CW / CWi; p.CT = nCs / CW; p.rows = (int)rows; p.wbox = wbox;
     p.slot_bytes = (wbox * CW * 2 + 127) & ~127;
     p.slots = DW_RING_BYTES / p.slot_bytes;
     if (p.slots > DW_MAX_SLOTS) p.slots = DW_MAX_SLOTS;
     p.wpk = pPacked; p.bias = pBias; p.out = static_cast<__half*>(pOut); p.act = nAct;
     p.err = c->err_word;
+    // 5-D view [N][H][W][Cs / CWi][CWi]: a box of CB blocks of CWi channels lands in shared
+    // memory as [wbox][CW], the layout of a tile of CW channels
     CUtensorMap tm;
-    cuuint64_t dims[4] = {(cuuint64_t)nCs, (cuuint64_t)nW, (cuuint64_t)nH, (cuuint64_t)nN};
-    cuuint64_t strides[3] = {(cuuint64_t)nCs * 2, (cuuint64_t)nW * nCs * 2,
+    cuuint64_t dims[5] = {(cuuint64_t)CWi, (cuuint64_t)(nCs / CWi), (cuuint64_t)nW, (cuuint64_t)nH,
+                          (cuuint64_t)nN};
+    cuuint64_t strides[4] = {(cuuint64_t)CWi * 2, (cuuint64_t)nCs * 2, (cuuint64_t)nW * nCs * 2,
                              (cuuint64_t)nH * nW * nCs * 2};
-    cuuint32_t box[4] = {(cuuint32_t)CW, (cuuint32_t)wbox, 1, 1};
-    cuuint32_t estr[4] = {1, 1, 1, 1};
-    if (g_encode_tiled(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(pIn), dims,
+    cuuint32_t box[5] = {(cuuint32_t)CWi, (cuuint32_t)(CW / CWi), (cuuint32_t)wbox, 1, 1};
+    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    if (g_encode_tiled(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5, const_cast<void*>(pIn), dims,
                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                        CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)

@@ -181,10 +181,13 @@ def _hfma_depthwise(x16, w16, b16, stride, act6=True):
 
 
 @pytest.mark.parametrize("n,c,h,w,stride", [
-    (4, 128, 112, 112, 1),   # ring kernel: MobileNet stage-1 size, 2 channel tiles of 64
-    (3, 256, 56, 56, 2),     # ring kernel, stride 2, 128-channel tiles
-    (2, 1024, 14, 14, 1),    # ring kernel, 256-channel tiles
-    (5, 192, 9, 11, 1),      # ring kernel, ragged, runs that cross images, odd P
+    (4, 128, 112, 112, 1),   # ring kernel: MobileNet stage-1 size, whole 128-channel pixels
+    (3, 256, 56, 56, 2),     # ring kernel, stride 2, whole 256-channel pixels
+    (2, 1024, 14, 14, 1),    # ring kernel, 1024-channel pixels as four 256-channel boxes
+    (3, 512, 27, 27, 1),     # ring kernel, 512-channel tiles, odd P
+    (2, 512, 28, 28, 2),     # ring kernel, stride 2, 512-channel tiles
+    (2, 256, 112, 112, 1),   # ring kernel, two 128-channel tiles per pixel
+    (5, 192, 9, 11, 1),      # ring kernel, 64-channel tiles, runs that cross images
     (3, 64, 15, 13, 2),      # ring kernel, stride 2, odd sizes
     (2, 32, 20, 18, 1),      # direct kernel (32 channels), row pairs
     (1, 64, 9, 300, 2),      # direct kernel (row wider than a ring slot)
