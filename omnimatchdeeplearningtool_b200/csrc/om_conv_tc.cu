@@ -120,6 +120,7 @@ struct Params {
     void* out;
     int act;
     int out_f32;          // 1: fp32 output stored directly (classifier logits)
+    int out_ktot;         // MODE_TF32: channels per output image (0: K; a group writes K of them)
     unsigned int* err;
     // optional (nullptr: off): %globaltimer at each CTA's start and end, stamps[2*cta + 0/1]
     unsigned long long* stamps;
@@ -393,7 +394,8 @@ __device__ __forceinline__ void store_chunk_nchw(const Params& p, int m, int n0,
                                                  const uint32_t (&v)[32]) {
     const int PQ = p.P * p.Q;
     const int img = m / PQ;
-    float* base = static_cast<float*>(p.out) + (size_t)img * p.K * PQ + (m - img * PQ);
+    const int ktot = p.out_ktot ? p.out_ktot : p.K;
+    float* base = static_cast<float*>(p.out) + (size_t)img * ktot * PQ + (m - img * PQ);
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
         const int k = n0 + j;
@@ -1537,6 +1539,7 @@ extern "C" int omCudaConv2dBnAct(const void* pInput, const void* pPacked, const 
     p.out = pOutput;
     p.act = nAct;
     p.out_f32 = (nOutDtype == OM_DTYPE_F32);
+    p.out_ktot = 0;
     p.err = c->err_word;
 
     const CUtensorMapDataType dt =
@@ -2537,6 +2540,7 @@ static int stem_conv(const void* pInput, int nInDtype, void* pWorkspace, const v
     p.out = pOutput;
     p.act = nAct;
     p.out_f32 = 0;
+    p.out_ktot = 0;
     p.err = c->err_word;
 
     const CUtensorMapDataType dt =
@@ -3218,7 +3222,8 @@ __device__ __forceinline__ float tf32_rna(float x) {
 // gradient's dY operand, whose 32-channel blocks are then one TMA box dimension).
 __global__ void split_nhwc_kernel(const float* __restrict__ x, float* __restrict__ hi,
                                   float* __restrict__ lo, int N, int Cin, int Hin, int Win, int Hp,
-                                  int Wp, int Cs, int offh, int offw, int up, int blocked) {
+                                  int Wp, int Cs, int offh, int offw, int up, int blocked,
+                                  int Csrc) {
     __shared__ float tile[32][33];
     const int tx = threadIdx.x, ty = threadIdx.y;
     const int wt = (Wp + 31) / 32;                 // blockIdx.x = hp * wt + pixel tile
@@ -3232,7 +3237,7 @@ __global__ void split_nhwc_kernel(const float* __restrict__ x, float* __restrict
         const int c = c0 + cc, wp = wp0 + tx, j = wp - offw;
         float v = 0.f;
         if (row_ok && c < Cin && wp < Wp && j >= 0 && j % up == 0 && j / up < Win)
-            v = __ldg(x + (((size_t)n * Cin + c) * Hin + hs) * Win + j / up);
+            v = __ldg(x + (((size_t)n * Csrc + c) * Hin + hs) * Win + j / up);
         tile[cc][tx] = v;
     }
     __syncthreads();
@@ -3258,7 +3263,8 @@ __global__ void __launch_bounds__(256) split_flat_kernel(const float* __restrict
                                                          float* __restrict__ hi,
                                                          float* __restrict__ lo, int N, int Cin,
                                                          int Hin, int Win, int Hp, int Wp, int Cs,
-                                                         int offh, int offw, int up, int blocked) {
+                                                         int offh, int offw, int up, int blocked,
+                                                         int Csrc) {
     __shared__ float tile[32][129];
     const int HWp = Hp * Wp, HWin = Hin * Win;
     const int NP = N * HWp;
@@ -3276,7 +3282,7 @@ __global__ void __launch_bounds__(256) split_flat_kernel(const float* __restrict
             const int hp = r / Wp;
             const int i = hp - offh, j = r - hp * Wp - offw;
             if (i >= 0 && j >= 0 && i % up == 0 && j % up == 0 && i / up < Hin && j / up < Win)
-                off[k] = (long long)n * Cin * HWin + (i / up) * Win + j / up;
+                off[k] = (long long)n * Csrc * HWin + (i / up) * Win + j / up;
         }
     }
 #pragma unroll
@@ -3313,17 +3319,18 @@ __global__ void __launch_bounds__(256) split_flat_kernel(const float* __restrict
 // 2^31 output pixels.
 static void launch_split(DeviceCtx* c, const float* x, float* hi, float* lo, int N, int Cin,
                          int Hin, int Win, int Hp, int Wp, int Cs, int offh, int offw, int up,
-                         int blocked) {
+                         int blocked, int Csrc = 0) {
+    if (Csrc == 0) Csrc = Cin;   // channels per source image (a group reads Cin of them)
     const long long np = (long long)N * Hp * Wp;
     if (np + 128 < (1LL << 31)) {
         dim3 grid((unsigned)((np + 127) / 128), (unsigned)(Cs / 32));
         split_flat_kernel<<<grid, 256, 0, c->compute>>>(x, hi, lo, N, Cin, Hin, Win, Hp, Wp, Cs,
-                                                        offh, offw, up, blocked);
+                                                        offh, offw, up, blocked, Csrc);
         return;
     }
     dim3 grid((unsigned)(Hp * ((Wp + 31) / 32)), (unsigned)(Cs / 32), (unsigned)N);
     split_nhwc_kernel<<<grid, dim3(32, 8), 0, c->compute>>>(x, hi, lo, N, Cin, Hin, Win, Hp, Wp,
-                                                           Cs, offh, offw, up, blocked);
+                                                           Cs, offh, offw, up, blocked, Csrc);
 }
 
 // Packed K-major hi/lo weights [Kout, R*S*Cs], kk = (r*S + s)*Cs + ci, from W [Kw, Cw, R, S]:
@@ -3384,7 +3391,7 @@ __global__ void s2d_split_kernel(const float* __restrict__ x, float* __restrict_
 // packed hi/lo filter [Kout, R*S*Cs]: result NCHW fp32 [N, Kout, P, Q] (+bias).
 static int tf32_conv_run(DeviceCtx* c, float* xhi, float* xlo, int N, int Hp, int Wp, int Cs,
                          float* whi, float* wlo, int Kout, int R, int S, const float* bias,
-                         float* out, int stride, int pad, int dil) {
+                         float* out, int stride, int pad, int dil, int out_ktot = 0) {
     const int eR = (R - 1) * dil + 1, eS = (S - 1) * dil + 1;   // dilated filter extent
     const int P = (Hp + 2 * pad - eR) / stride + 1, Q = (Wp + 2 * pad - eS) / stride + 1;
     const long long Mll = (long long)N * P * Q;
@@ -3405,6 +3412,7 @@ static int tf32_conv_run(DeviceCtx* c, float* xhi, float* xlo, int N, int Hp, in
     p.out = out;
     p.act = OM_ACT_NONE;
     p.out_f32 = 1;
+    p.out_ktot = out_ktot;
     p.err = c->err_word;
     // A: im2col views of the hi and lo copies, dims innermost-first (Cs, Wp, Hp, N)
     CUtensorMap ta_hi, ta_lo, tb_hi, tb_lo;
@@ -3457,7 +3465,8 @@ static bool tf32_pad_ok(int R, int S, int pad) {
 // the result written as NCHW fp32 [N, Kout, P, Q]. Scratch comes from the stream-ordered pool.
 int tf32_conv(DeviceCtx* c, const float* src, int N, int Cin, int Hin, int Win, int Hp, int Wp,
               int offh, int offw, int up, const float* w, int Kout, int R, int S, bool flip,
-              int Cw, const float* bias, float* out, int stride, int pad, int dil) {
+              int Cw, const float* bias, float* out, int stride, int pad, int dil, int src_ctot,
+              int out_ktot) {
     const int Cs = (Cin + 31) / 32 * 32;
     if (dil < 1 || (long long)(R - 1) * dil + 1 > 256 || (long long)(S - 1) * dil + 1 > 256)
         return OM_ERR_UNSUPPORTED;
@@ -3484,7 +3493,7 @@ int tf32_conv(DeviceCtx* c, const float* src, int N, int Cin, int Hin, int Win, 
     float* whi = reinterpret_cast<float*>(scratch + 2 * xb);
     float* wlo = reinterpret_cast<float*>(scratch + 2 * xb + wb);
     int st = OM_OK;
-    launch_split(c, src, xhi, xlo, N, Cin, Hin, Win, Hp, Wp, Cs, offh, offw, up, 0);
+    launch_split(c, src, xhi, xlo, N, Cin, Hin, Win, Hp, Wp, Cs, offh, offw, up, 0, src_ctot);
     st = after_launch(c);
     if (st == OM_OK) {
         pack_tf32_weight_kernel<<<ew_grid(c, (long long)we, 256), 256, 0, c->compute>>>(
@@ -3493,7 +3502,7 @@ int tf32_conv(DeviceCtx* c, const float* src, int N, int Cin, int Hin, int Win, 
     }
     if (st == OM_OK)
         st = tf32_conv_run(c, xhi, xlo, N, Hp, Wp, Cs, whi, wlo, Kout, R, S, bias, out, stride, pad,
-                           dil);
+                           dil, out_ktot);
     cudaFreeAsync(scratch, c->compute);
     return st;
 }

@@ -280,6 +280,22 @@ extern "C" int omCudaDilatedConv2d(const float* pInput, const float* pWeight, co
                                     nCout, nKH, nKW, false, nCin, pBias, pOutput, nStride, nPad,
                                     nDilation);
         if (st != OM_ERR_UNSUPPORTED && st != OM_ERR_OOM) return st;
+    } else if (nCin / nGroups >= 16 && nCout / nGroups >= 16 && nGroups <= 64) {
+        // grouped, with enough channels per group for a GEMM: one 3xTF32 tensor-core conv per
+        // group, reading its Cin/g channels of every input image and writing its Cout/g
+        // channels of every output image in place (weights [Cout, Cin/g, R, S] are grouped by
+        // output channel already). Depthwise and other thin groups stay on the direct kernel.
+        const int cg = nCin / nGroups, kg = nCout / nGroups;
+        int st = OM_OK;
+        for (int g = 0; g < nGroups && st == OM_OK; ++g)
+            st = omb::tc::tf32_conv(c, pInput + (size_t)g * cg * nH * nW, nBatch, cg, nH, nW, nH,
+                                    nW, 0, 0, 1, pWeight + (size_t)g * kg * cg * nKH * nKW, kg,
+                                    nKH, nKW, false, cg, pBias ? pBias + (size_t)g * kg : nullptr,
+                                    pOutput + (size_t)g * kg * P * Q, nStride, nPad, nDilation,
+                                    nCin, nCout);
+        // a refusal comes at the first group (every group has the same shape); the direct
+        // kernel then writes the whole output
+        if (st != OM_ERR_UNSUPPORTED && st != OM_ERR_OOM) return st;
     }
     long long total = (long long)nBatch * nCout * P * Q;
     grouped_conv_kernel<<<ew_grid(c, total, 256), 256, 0, c->compute>>>(

@@ -127,7 +127,11 @@ def test_grouped_depthwise_conv(gpu):
     (2, 20, 24, 30, 1, 4, 4, 1, 3, 1),    # non-square 3x1 filter, dilation 4
     (2, 37, 45, 26, 1, 6, 6, 1, 3, 3),    # channels not a multiple of 32 or 8, dilation 6
     (1, 2, 4, 40, 1, 130, 130, 1, 3, 3),  # 261x261 extent: tensor path refuses, direct kernel
-    (2, 12, 18, 17, 1, 2, 2, 3, 3, 3)])   # grouped and dilated: the direct kernel
+    (2, 12, 18, 17, 1, 2, 2, 3, 3, 3),    # grouped, 4 channels per group: the direct kernel
+    (2, 64, 96, 18, 1, 1, 1, 2, 3, 3),    # 2 groups of 32 -> 48: one tensor-core conv per group
+    (2, 128, 128, 15, 2, 1, 1, 4, 3, 3),  # 4 groups, stride 2, tensor cores
+    (2, 96, 64, 17, 1, 2, 2, 4, 3, 3),    # 4 groups of 24 -> 16, dilation 2, tensor cores
+    (3, 64, 64, 9, 1, 0, 1, 2, 1, 1)])    # grouped 1x1, tensor cores
 def test_dilated_conv_routes(gpu, n, c, k, h, stride, pad, dil, groups, kh, kw):
     """omCudaDilatedConv2d (cuda_kernels.cu:1201) against the oracle's convolution with the
     filter dilated by zero insertion; bias included."""
