@@ -193,6 +193,21 @@ int omCudaBatchNorm2dAct(const float* pInput, float* pOutput, const float* pGamm
                          const float* pBeta, float* pRunMean, float* pRunVar, float* pSavedMean,
                          float* pSavedInvStd, int nBatch, int nChannels, int nH, int nW,
                          float fEps, float fMomentum, int bTraining, int nAct);
+/* new: train-mode conv -> BatchNorm (-> ReLU) with the BatchNorm statistics taken in the
+ * convolution's epilogue (the reference calls :1076, then :1648 and its ReLU kernel). The conv
+ * (arguments as omCudaConv2d, square stride and padding) writes pConvOut [N, Cout, P, Q]; the
+ * BatchNorm (arguments as omCudaBatchNorm2d, always training: batch statistics with the biased
+ * variance, running statistics updated with fMomentum) writes pOutput with nAct (OM_ACT_NONE or
+ * OM_ACT_RELU) applied, and the saved mean and 1/sqrt(var + eps) its backward needs. The
+ * statistics are combined in a fixed order, so the result is deterministic; they agree with
+ * omCudaBatchNorm2d's two-pass statistics to fp32 rounding. pConvOut is written once and read
+ * once. */
+int omCudaConv2dBatchNorm2dAct(const float* pInput, const float* pWeight, const float* pBias,
+                               float* pConvOut, float* pOutput, const float* pGamma,
+                               const float* pBeta, float* pRunMean, float* pRunVar,
+                               float* pSavedMean, float* pSavedInvStd, int nBatch, int nCin,
+                               int nH, int nW, int nCout, int nKH, int nKW, int nStride, int nPad,
+                               float fEps, float fMomentum, int nAct);
 /* new: the matching backward (the reference calls its ReLU backward, then :3130). pOutput is the
  * forward's activated output: the incoming gradient is zeroed where pOutput <= 0 inside the BN
  * backward passes. Bit-identical to omCudaReLUBackward followed by omCudaBatchNorm2dBackward. */

@@ -92,6 +92,8 @@ _SIGS = {
     "omCudaBatchNorm2d": [P, P, P, P, P, P, P, P, I, I, I, I, F, F, I],
     "omCudaBatchNorm2dBackward": [P, P, P, P, P, P, P, P, I, I, I, I, F],
     "omCudaBatchNorm2dAct": [P, P, P, P, P, P, P, P, I, I, I, I, F, F, I, I],
+    "omCudaConv2dBatchNorm2dAct": [P, P, P, P, P, P, P, P, P, P, P, I, I, I, I, I, I, I, I, I,
+                                   F, F, I],
     "omCudaBatchNorm2dBackwardAct": [P, P, P, P, P, P, P, P, P, I, I, I, I, F, I],
     "omCudaBatchNorm2dNoAlloc": [P, P, P, P, P, P, P, P, I, I, I, I, F, F, I],
     "omCudaMaxPool2d": [P, P, P, I, I, I, I, I, I, I, I, I, I],

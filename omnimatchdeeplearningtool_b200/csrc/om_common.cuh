@@ -37,13 +37,16 @@ namespace tc {
 // With dil > 1 the filter is dilated: tap (r, s) reads input offset (r*dil, s*dil), so P and Q
 // follow the dilated extent (R-1)*dil+1. One group of a grouped convolution reads Cin of the
 // source's src_ctot channels per image (src points at its first) and writes Kout of the
-// output's out_ktot channels per image (0: Cin and Kout, the whole tensors). Returns
-// OM_ERR_UNSUPPORTED for shapes the tensor path does not take and OM_ERR_OOM when its operand
-// copies do not fit; nothing is launched then.
+// output's out_ktot channels per image (0: Cin and Kout, the whole tensors). With bn_part the
+// epilogue also writes BatchNorm statistics of the output per 32-pixel group g = m / 32 of the
+// N*P*Q output pixels m (G = ceil(N*P*Q / 32) groups) and channel k: the group's mean at
+// bn_part[k*G + g], its sum of squared deviations from that mean at bn_part[(Kout + k)*G + g].
+// Returns OM_ERR_UNSUPPORTED for shapes the tensor path does not take and OM_ERR_OOM when its
+// operand copies do not fit; nothing is launched then.
 int tf32_conv(DeviceCtx* c, const float* src, int N, int Cin, int Hin, int Win, int Hp, int Wp,
               int offh, int offw, int up, const float* w, int Kout, int R, int S, bool flip,
               int Cw, const float* bias, float* out, int stride, int pad, int dil = 1,
-              int src_ctot = 0, int out_ktot = 0);
+              int src_ctot = 0, int out_ktot = 0, float* bn_part = nullptr);
 // 3xTF32 tensor-core weight gradient of a (stride, pad) convolution: dW [K, Cin, R, S] from
 // X [N, Cin, H, W] and dY [N, K, P, Q], all NCHW fp32 (om_conv_tc.cu).
 int tf32_wgrad(DeviceCtx* c, const float* x, const float* dy, float* dw, int N, int Cin, int H,

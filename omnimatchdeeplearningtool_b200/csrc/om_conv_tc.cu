@@ -121,6 +121,11 @@ struct Params {
     int act;
     int out_f32;          // 1: fp32 output stored directly (classifier logits)
     int out_ktot;         // MODE_TF32: channels per output image (0: K; a group writes K of them)
+    // MODE_TF32, optional (nullptr: off): BatchNorm statistics of the output, per 32-pixel group
+    // g and channel k: the group's mean at bn_part[k * bn_groups + g] and its sum of squared
+    // deviations from that mean at bn_part[(K + k) * bn_groups + g]
+    float* bn_part;
+    int bn_groups;
     unsigned int* err;
     // optional (nullptr: off): %globaltimer at each CTA's start and end, stamps[2*cta + 0/1]
     unsigned long long* stamps;
@@ -403,6 +408,56 @@ __device__ __forceinline__ void store_chunk_nchw(const Params& p, int m, int n0,
         float o = __uint_as_float(v[j]);
         if (p.bias) o += __ldg(p.bias + k);
         base[(size_t)k * PQ] = apply_act(o, p.act);
+    }
+}
+
+// Sums over the warp's 32 lanes of 32 values each: afterwards lane l's x[0] is the sum of x[l]
+// over all lanes (31 shuffles: each round keeps half of the values and adds the partner's half).
+__device__ __forceinline__ void warp_transpose_sum(float (&x)[32]) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+        const bool upper = (lane & off) != 0;
+#pragma unroll
+        for (int i = 0; i < off; ++i) {
+            const float send = upper ? x[i] : x[i + off];
+            const float keep = upper ? x[i + off] : x[i];
+            x[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+        }
+    }
+}
+
+// BatchNorm statistics of an fp32 NCHW output chunk (MODE_TF32 with p.bn_part): rows mw ..
+// mw+31 (the valid ones), 32 channels from n0. Per channel, the chunk's mean and the sum of
+// squared deviations from it (two passes over the registers), written for a fixed-order
+// combination later (Chan et al.'s pairwise update). Called by the whole warp.
+__device__ __forceinline__ void chunk_bn_stats(const Params& p, int mw, int n0,
+                                               const uint32_t (&v)[32]) {
+    const int lane = threadIdx.x & 31;
+    const int cnt = min(32, p.M - mw);
+    const bool valid = lane < cnt;
+    float x[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        float o = __uint_as_float(v[j]);
+        if (p.bias && n0 + j < p.K) o += __ldg(p.bias + n0 + j);
+        x[j] = valid ? o : 0.f;
+    }
+    warp_transpose_sum(x);
+    const float mean = x[0] / (float)cnt;   // of channel n0 + lane
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        float o = __uint_as_float(v[j]);
+        if (p.bias && n0 + j < p.K) o += __ldg(p.bias + n0 + j);
+        const float d = o - __shfl_sync(0xffffffffu, mean, j);
+        x[j] = valid ? d * d : 0.f;
+    }
+    warp_transpose_sum(x);
+    const int k = n0 + lane;
+    if (k < p.K) {
+        const size_t gi = (size_t)k * p.bn_groups + (mw >> 5);
+        p.bn_part[gi] = mean;
+        p.bn_part[(size_t)p.K * p.bn_groups + gi] = x[0];
     }
 }
 
@@ -1052,6 +1107,7 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
                         if (MODE == MODE_TF32) store_chunk_nchw(p, mw + lane, n0, v);
                         else store_chunk_f32(p, mw + lane, n0, v);
                     }
+                    if (MODE == MODE_TF32 && p.bn_part && mw < p.M) chunk_bn_stats(p, mw, n0, v);
                     ++g;
                     ++j;
                     continue;
@@ -1540,6 +1596,8 @@ extern "C" int omCudaConv2dBnAct(const void* pInput, const void* pPacked, const 
     p.act = nAct;
     p.out_f32 = (nOutDtype == OM_DTYPE_F32);
     p.out_ktot = 0;
+    p.bn_part = nullptr;
+    p.bn_groups = 0;
     p.err = c->err_word;
 
     const CUtensorMapDataType dt =
@@ -2541,6 +2599,8 @@ static int stem_conv(const void* pInput, int nInDtype, void* pWorkspace, const v
     p.act = nAct;
     p.out_f32 = 0;
     p.out_ktot = 0;
+    p.bn_part = nullptr;
+    p.bn_groups = 0;
     p.err = c->err_word;
 
     const CUtensorMapDataType dt =
@@ -3391,7 +3451,8 @@ __global__ void s2d_split_kernel(const float* __restrict__ x, float* __restrict_
 // packed hi/lo filter [Kout, R*S*Cs]: result NCHW fp32 [N, Kout, P, Q] (+bias).
 static int tf32_conv_run(DeviceCtx* c, float* xhi, float* xlo, int N, int Hp, int Wp, int Cs,
                          float* whi, float* wlo, int Kout, int R, int S, const float* bias,
-                         float* out, int stride, int pad, int dil, int out_ktot = 0) {
+                         float* out, int stride, int pad, int dil, int out_ktot = 0,
+                         float* bn_part = nullptr) {
     const int eR = (R - 1) * dil + 1, eS = (S - 1) * dil + 1;   // dilated filter extent
     const int P = (Hp + 2 * pad - eR) / stride + 1, Q = (Wp + 2 * pad - eS) / stride + 1;
     const long long Mll = (long long)N * P * Q;
@@ -3413,6 +3474,8 @@ static int tf32_conv_run(DeviceCtx* c, float* xhi, float* xlo, int N, int Hp, in
     p.act = OM_ACT_NONE;
     p.out_f32 = 1;
     p.out_ktot = out_ktot;
+    p.bn_part = bn_part;
+    p.bn_groups = (int)((Mll + 31) / 32);
     p.err = c->err_word;
     // A: im2col views of the hi and lo copies, dims innermost-first (Cs, Wp, Hp, N)
     CUtensorMap ta_hi, ta_lo, tb_hi, tb_lo;
@@ -3466,7 +3529,7 @@ static bool tf32_pad_ok(int R, int S, int pad) {
 int tf32_conv(DeviceCtx* c, const float* src, int N, int Cin, int Hin, int Win, int Hp, int Wp,
               int offh, int offw, int up, const float* w, int Kout, int R, int S, bool flip,
               int Cw, const float* bias, float* out, int stride, int pad, int dil, int src_ctot,
-              int out_ktot) {
+              int out_ktot, float* bn_part) {
     const int Cs = (Cin + 31) / 32 * 32;
     if (dil < 1 || (long long)(R - 1) * dil + 1 > 256 || (long long)(S - 1) * dil + 1 > 256)
         return OM_ERR_UNSUPPORTED;
@@ -3502,7 +3565,7 @@ int tf32_conv(DeviceCtx* c, const float* src, int N, int Cin, int Hin, int Win, 
     }
     if (st == OM_OK)
         st = tf32_conv_run(c, xhi, xlo, N, Hp, Wp, Cs, whi, wlo, Kout, R, S, bias, out, stride, pad,
-                           dil, out_ktot);
+                           dil, out_ktot, bn_part);
     cudaFreeAsync(scratch, c->compute);
     return st;
 }

@@ -584,6 +584,55 @@ static int bn_apply(DeviceCtx* c, const float* x, float* y, const float* gamma, 
     return after_launch(c);
 }
 
+// BatchNorm statistics from a convolution's per-group partials (the 3xTF32 conv epilogue with
+// bn_part): for channel c, G groups of 32 output pixels (the last one holds cnt - 32 (G - 1)),
+// each with its mean and sum of squared deviations. They are combined with Chan et al.'s
+// pairwise update (n = na + nb, d = mb - ma, m = ma + d nb / n, M2 = M2a + M2b + d^2 na nb / n)
+// in a fixed order: thread t takes groups t, t + 256, ... one after another, then the 256
+// partials are combined pairwise down a tree. Then, as bn_finalize_kernel: biased variance,
+// running statistics with momentum, saved mean and 1/sqrt(var + eps). One block per channel.
+__device__ __forceinline__ void chan_combine(float& na, float& ma, float& m2a, float nb, float mb,
+                                             float m2b) {
+    const float n = na + nb;
+    if (nb == 0.f) return;
+    const float d = mb - ma;
+    const float f = nb / n;
+    ma += d * f;
+    m2a += m2b + d * d * na * f;
+    na = n;
+}
+__global__ void __launch_bounds__(256) bn_chan_finalize_kernel(
+    const float* __restrict__ part, int G, long long cnt, int C, float* run_mean, float* run_var,
+    float* saved_mean, float* saved_invstd, float eps, float momentum) {
+    const int c = blockIdx.x;
+    const float* pm = part + (size_t)c * G;
+    const float* pq = part + ((size_t)C + c) * G;
+    float n = 0.f, m = 0.f, m2 = 0.f;
+    for (int g = threadIdx.x; g < G; g += 256) {
+        const long long left = cnt - 32LL * g;
+        chan_combine(n, m, m2, (float)(left < 32 ? left : 32), pm[g], pq[g]);
+    }
+    __shared__ float sn[256], sm[256], sq[256];
+    sn[threadIdx.x] = n; sm[threadIdx.x] = m; sq[threadIdx.x] = m2;
+    __syncthreads();
+    for (int h = 128; h >= 1; h >>= 1) {
+        if ((int)threadIdx.x < h) {
+            float a = sn[threadIdx.x], b = sm[threadIdx.x], q = sq[threadIdx.x];
+            chan_combine(a, b, q, sn[threadIdx.x + h], sm[threadIdx.x + h], sq[threadIdx.x + h]);
+            sn[threadIdx.x] = a; sm[threadIdx.x] = b; sq[threadIdx.x] = q;
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        const float mean = sm[0];
+        const float var = sq[0] / (float)cnt;
+        run_mean[c] = (1.f - momentum) * run_mean[c] + momentum * mean;
+        run_var[c] = (1.f - momentum) * run_var[c] + momentum * var;
+        saved_mean[c] = mean;
+        saved_invstd[c] = 1.f / sqrtf(var + eps);
+    }
+}
+
 }  // namespace ops
 }  // namespace omb
 
@@ -705,6 +754,53 @@ extern "C" int omCudaBatchNorm2dAct(const float* pInput, float* pOutput, const f
     return bn_forward(pInput, pOutput, pGamma, pBeta, pRunMean, pRunVar, pSavedMean, pSavedInvStd,
                       nBatch, nChannels, nH, nW, fEps, fMomentum, bTraining,
                       nAct == OM_ACT_RELU ? 1 : 0);
+}
+
+// Train-mode conv -> BatchNorm (-> ReLU) with the statistics taken in the conv's epilogue: the
+// conv output is written once and read once (by the normalisation), instead of three times
+// (two statistics passes and the normalisation).
+extern "C" int omCudaConv2dBatchNorm2dAct(const float* pInput, const float* pWeight,
+                                          const float* pBias, float* pConvOut, float* pOutput,
+                                          const float* pGamma, const float* pBeta,
+                                          float* pRunMean, float* pRunVar, float* pSavedMean,
+                                          float* pSavedInvStd, int nBatch, int nCin, int nH,
+                                          int nW, int nCout, int nKH, int nKW, int nStride,
+                                          int nPad, float fEps, float fMomentum, int nAct) {
+    OMB_CTX_OR_FAIL(c);
+    if (!pInput || !pWeight || !pConvOut || !pOutput || !pGamma || !pBeta || !pRunMean ||
+        !pRunVar || !pSavedMean || !pSavedInvStd || nBatch <= 0 || nCin <= 0 || nCout <= 0 ||
+        nStride <= 0 || nPad < 0)
+        return OM_ERR_INVALID;
+    if (nAct != OM_ACT_NONE && nAct != OM_ACT_RELU) return OM_ERR_UNSUPPORTED;
+    const int P = (nH + 2 * nPad - nKH) / nStride + 1, Q = (nW + 2 * nPad - nKW) / nStride + 1;
+    if (P <= 0 || Q <= 0) return OM_ERR_INVALID;
+    const long long cnt = (long long)nBatch * P * Q;
+    if (cnt >= (1LL << 31)) return OM_ERR_UNSUPPORTED;
+    const long long G = (cnt + 31) / 32;
+    float* part = nullptr;
+    OMB_CHECK(cudaMallocAsync(&part, sizeof(float) * 2 * (size_t)nCout * G, c->compute));
+    int st = omb::tc::tf32_conv(c, pInput, nBatch, nCin, nH, nW, nH, nW, 0, 0, 1, pWeight, nCout,
+                                nKH, nKW, false, nCin, pBias, pConvOut, nStride, nPad, 1, 0, 0,
+                                part);
+    if (st == OM_OK) {
+        bn_chan_finalize_kernel<<<nCout, 256, 0, c->compute>>>(part, (int)G, cnt, nCout,
+                                                               pRunMean, pRunVar, pSavedMean,
+                                                               pSavedInvStd, fEps, fMomentum);
+        st = after_launch(c);
+    }
+    cudaFreeAsync(part, c->compute);
+    if (st == OM_ERR_UNSUPPORTED || st == OM_ERR_OOM) {
+        // the tensor path did not take the shape: the conv and the BatchNorm separately
+        st = omCudaConv2d(pInput, pWeight, pBias, pConvOut, nBatch, nCin, nH, nW, nCout, nKH, nKW,
+                          nStride, nPad);
+        if (st != OM_OK) return st;
+        return omCudaBatchNorm2dAct(pConvOut, pOutput, pGamma, pBeta, pRunMean, pRunVar,
+                                    pSavedMean, pSavedInvStd, nBatch, nCout, P, Q, fEps, fMomentum,
+                                    1, nAct);
+    }
+    if (st != OM_OK) return st;
+    return bn_apply(c, pConvOut, pOutput, pGamma, pBeta, pSavedMean, pSavedInvStd,
+                    cnt * nCout, nCout, P * Q, nAct == OM_ACT_RELU ? 1 : 0);
 }
 
 extern "C" int omCudaBatchNorm2dBackwardAct(const float* pGradOutput, const float* pInput,

@@ -433,8 +433,11 @@ class Fp32Net:
     """
 
     def __init__(self, net: NetSpec, weights: Dict[str, np.ndarray], batch: int, h: int = 224,
-                 w: int = 224, grad_ptr: Optional[int] = None):
+                 w: int = 224, grad_ptr: Optional[int] = None, fused_bn_stats: bool = False):
         self.net, self.batch, self.h, self.w = net, batch, h, w
+        # train-mode BatchNorm statistics from the conv epilogue (omCudaConv2dBatchNorm2dAct);
+        # False: the reference's order of calls, conv then omCudaBatchNorm2dAct
+        self.fused_bn_stats = fused_bn_stats
         self.keep: List[DeviceBuffer] = []
         self._guard: Optional[DeviceBuffer] = None  # the gradient guard's status (device)
         self.param = {}
@@ -503,17 +506,26 @@ class Fp32Net:
         q = (ww + 2 * cv.pad - cv.k) // cv.stride + 1
         cnt = n * cv.cout * p * q
         z = self._buf(key + ".z", cnt * 4)
-        B.conv2d(x.ptr, self.param[cv.name + ".weight"].ptr, None, z.ptr, n, c, hh, ww, cv.cout,
-                 cv.k, cv.k, cv.pad, cv.pad, cv.stride, cv.stride)
-        # BN and the ReLU after it in one pass (omCudaBatchNorm2dAct): y is the activated
-        # output, and its sign is the ReLU mask the backward needs
+        # BN and the ReLU after it in one pass: y is the activated output, and its sign is the
+        # ReLU mask the backward needs
         y = self._buf(key + ".y", cnt * 4)
         mean = self._buf(key + ".mean", cv.cout * 4)
         invstd = self._buf(key + ".invstd", cv.cout * 4)
-        call("omCudaBatchNorm2dAct", z.ptr, y.ptr, self.param[cv.bn + ".gamma"].ptr,
-             self.param[cv.bn + ".beta"].ptr, self.buffers[cv.bn + ".running_mean"].ptr,
-             self.buffers[cv.bn + ".running_var"].ptr, mean.ptr, invstd.ptr, n, cv.cout, p, q,
-             1e-5, 0.1, int(train), _lib.ACT_RELU if relu else _lib.ACT_NONE)
+        act = _lib.ACT_RELU if relu else _lib.ACT_NONE
+        gamma, beta = self.param[cv.bn + ".gamma"].ptr, self.param[cv.bn + ".beta"].ptr
+        rmean = self.buffers[cv.bn + ".running_mean"].ptr
+        rvar = self.buffers[cv.bn + ".running_var"].ptr
+        if train and self.fused_bn_stats:
+            # batch statistics from the conv's epilogue (omCudaConv2dBatchNorm2dAct): z is
+            # written once and read once
+            call("omCudaConv2dBatchNorm2dAct", x.ptr, self.param[cv.name + ".weight"].ptr, None,
+                 z.ptr, y.ptr, gamma, beta, rmean, rvar, mean.ptr, invstd.ptr, n, c, hh, ww,
+                 cv.cout, cv.k, cv.k, cv.stride, cv.pad, 1e-5, 0.1, act)
+        else:
+            B.conv2d(x.ptr, self.param[cv.name + ".weight"].ptr, None, z.ptr, n, c, hh, ww,
+                     cv.cout, cv.k, cv.k, cv.pad, cv.pad, cv.stride, cv.stride)
+            call("omCudaBatchNorm2dAct", z.ptr, y.ptr, gamma, beta, rmean, rvar, mean.ptr,
+                 invstd.ptr, n, cv.cout, p, q, 1e-5, 0.1, int(train), act)
         out = y
         rec = dict(cv=cv, x=x, z=z, y=y, mean=mean, invstd=invstd, relu=relu, n=n, c=c, h=hh,
                    w=ww, p=p, q=q)

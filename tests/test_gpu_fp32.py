@@ -193,6 +193,61 @@ def test_batchnorm_fwd_bwd(gpu, training, shape):
     assert rel_err_floor(dx.to_numpy(x.shape), wdx) <= TOL
 
 
+@pytest.mark.parametrize("n,c,h,k,r,stride,pad,act", [
+    (4, 16, 15, 24, 3, 1, 1, 1),     # 900 pixels: a partial 32-pixel group at the end
+    (2, 32, 28, 160, 3, 2, 1, 1),    # several 128-wide output tiles, stride 2
+    (8, 64, 14, 64, 1, 1, 0, 0),     # 1x1, no activation
+    (2, 3, 64, 64, 7, 2, 3, 1),      # the ImageNet stem shape (3 input channels)
+    (4, 64, 56, 64, 3, 1, 1, 1)])    # a ResNet-18 layer-1 conv at batch 4 (392 groups/channel)
+def test_conv_batchnorm_stats_in_epilogue(gpu, n, c, h, k, r, stride, pad, act):
+    """omCudaConv2dBatchNorm2dAct (BatchNorm statistics from the conv epilogue, combined in a
+    fixed order) against omCudaConv2d + omCudaBatchNorm2dAct (two-pass statistics): the conv
+    output bit-identical, everything else within the fp32 tolerance; and against the oracle's
+    train-mode BatchNorm of the oracle's conv."""
+    import oracle as orc
+    from omnimatchdeeplearningtool_b200._lib import call
+    rng = _rng(500 + c + k)
+    x = rng.standard_normal((n, c, h, h), dtype=np.float32)
+    w = (rng.standard_normal((k, c, r, r)) * np.sqrt(2.0 / (c * r * r))).astype(np.float32)
+    g = rng.uniform(0.5, 1.5, k).astype(np.float32)
+    b = rng.standard_normal(k).astype(np.float32)
+    rm = (rng.standard_normal(k) * 0.1).astype(np.float32)
+    rv = rng.uniform(0.5, 1.5, k).astype(np.float32)
+    p = (h + 2 * pad - r) // stride + 1
+    dx, dw, dg, db = _dev(x), _dev(w), _dev(g), _dev(b)
+    res = []
+    for fused in (True, False):
+        z, y, sm, si = _out((n, k, p, p)), _out((n, k, p, p)), _out((k,)), _out((k,))
+        drm, drv = _dev(rm), _dev(rv)
+        if fused:
+            call("omCudaConv2dBatchNorm2dAct", dx.ptr, dw.ptr, None, z.ptr, y.ptr, dg.ptr, db.ptr,
+                 drm.ptr, drv.ptr, sm.ptr, si.ptr, n, c, h, h, k, r, r, stride, pad, 1e-5, 0.1, act)
+        else:
+            call("omCudaConv2d", dx.ptr, dw.ptr, None, z.ptr, n, c, h, h, k, r, r, stride, pad)
+            call("omCudaBatchNorm2dAct", z.ptr, y.ptr, dg.ptr, db.ptr, drm.ptr, drv.ptr, sm.ptr,
+                 si.ptr, n, k, p, p, 1e-5, 0.1, 1, act)
+        res.append([t.to_numpy(s) for t, s in ((z, (n, k, p, p)), (y, (n, k, p, p)), (sm, (k,)),
+                                                (si, (k,)), (drm, (k,)), (drv, (k,)))])
+    fz, fy, fsm, fsi, frm, frv = res[0]
+    assert np.array_equal(fz, res[1][0])
+    for a, e in zip(res[0][1:], res[1][1:]):
+        assert rel_err_floor(a, e) <= 1e-5
+    # the oracle: its conv, then its train-mode BatchNorm (+ ReLU)
+    zo = orc.conv2d(x, w, None, stride, pad)
+    wy, wrm, wrv = np.empty_like(zo), rm.copy(), rv.copy()
+    wsm, wsi = np.empty(k, np.float32), np.empty(k, np.float32)
+    orc.O.oracle_batchnorm2d(zo.ctypes.data, wy.ctypes.data, g.ctypes.data, b.ctypes.data,
+                             wrm.ctypes.data, wrv.ctypes.data, wsm.ctypes.data, wsi.ctypes.data,
+                             n, k, p, p, 1e-5, 0.1, 1)
+    if act:
+        wy = np.maximum(wy, 0)
+    assert rel_err_floor(fy, wy) <= TOL
+    assert rel_err_floor(fsi, wsi) <= TOL
+    assert rel_err_floor(frm, wrm) <= TOL
+    assert rel_err_floor(frv, wrv) <= TOL
+    assert gpu.kernel_error() == 0
+
+
 @pytest.mark.parametrize("shape", [(8, 24, 16, 16), (4, 16, 9, 7)])
 def test_batchnorm_relu_fused_matches_separate(gpu, shape):
     """omCudaBatchNorm2dAct / omCudaBatchNorm2dBackwardAct give the bits of omCudaBatchNorm2d +

@@ -25,7 +25,7 @@ from conftest import rel_err
 pytestmark = pytest.mark.gpu
 
 
-def _run(batch, hw, classes, seed):
+def _run(batch, hw, classes, seed, fused_bn_stats=False):
     import oracle as orc
     from omnimatchdeeplearningtool_b200 import synth
     from omnimatchdeeplearningtool_b200._lib import call
@@ -35,7 +35,7 @@ def _run(batch, hw, classes, seed):
     w = synth.make_weights(net)
     x = synth.normal_input(batch, 3, hw, hw, seed=seed)
     y = synth.onehot_labels(batch, classes, seed=seed + 1)
-    fnet = Fp32Net(net, w, batch, hw, hw)
+    fnet = Fp32Net(net, w, batch, hw, hw, fused_bn_stats=fused_bn_stats)
     dx, dy = DeviceBuffer.from_numpy(x), DeviceBuffer.from_numpy(y)
     dloss = DeviceBuffer.zeros(4)
     fnet.forward_backward(dx.ptr, dy.ptr, dloss.ptr)
@@ -65,13 +65,16 @@ def test_resnet18_training_step_small(gpu):
     assert rel_err(new_conv1, ow["conv1.weight"]) <= 1e-5
 
 
-def test_resnet18_training_step_config3(gpu):
+@pytest.mark.parametrize("fused_bn_stats", [False, True])
+def test_resnet18_training_step_config3(gpu, fused_bn_stats):
     gold = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "golden.npz"))
-    net, loss, grads, new_fc, new_conv1, oloss, ograds, ow = _run(8, 224, 1000, 11)
+    net, loss, grads, new_fc, new_conv1, oloss, ograds, ow = _run(8, 224, 1000, 11,
+                                                                  fused_bn_stats)
     assert abs(loss - oloss) <= 1e-4 * abs(oloss), (loss, oloss)
     errs = np.array([rel_err(grads[name], ograds[name]) for name, _ in net.params])
     ref = gold["train_r18_224_ref_grad_err"]
-    print(f"config3: loss err {abs(loss - oloss) / abs(oloss):.2e}, gradient error median "
+    print(f"config3 (fused BN statistics: {fused_bn_stats}): loss err "
+          f"{abs(loss - oloss) / abs(oloss):.2e}, gradient error median "
           f"{np.median(errs):.4f} max {errs.max():.4f} (reference fp32: {np.median(ref):.4f}, "
           f"{ref.max():.4f})")
     assert np.median(errs) <= np.median(ref), (np.median(errs), np.median(ref))
