@@ -8,12 +8,15 @@ only cross-rank traffic is the host-side barrier and the max-over-ranks of the t
 Printed JSON line (rank 0):
   value   images/s of the whole job, device-resident inputs, graph replay, max over ranks
   e2e     images/s through InferencePlan.serve with host buffers: per step the pinned
-          host->device copy of the step's NCHW fp32 input (on the transfer stream, overlapping
-          the previous step's forward), the forward, and the device->host copy of the logits,
-          all inside the timed region
-  roofline  the dominant kernel (conv_tc_kernel): algorithmic conv+FC FLOPs of one step
-          divided by the summed duration of its launches, from CUDA events around each
-          launch in an instrumented eager pass of the same steps
+          host->device copy of the step's NCHW input (a bf16 image; e2e.fp32_input is the same
+          loop with the fp32 image), on the transfer stream overlapping the previous step's
+          forward, the forward, and the device->host copy of the logits, all inside the timed
+          region
+  roofline  the dominant kernels (the tensor-core convs): algorithmic conv+FC FLOPs of one
+          step divided by their time per step, measured by the kernels' own per-CTA
+          %globaltimer stamps in a graph replay of the same forward
+  configs   (N = 1) short runs of the other configs: the conv sweep, ResNet-18 training and
+          the MobileNet-style stack
   cpu_baseline  the reference engine's own CPU ResNet-50 forward (oracle/_ref/libomref.so,
           AVX2 + OpenMP on every host core) on a bounded sample, rank 0 at N=1 only
 
