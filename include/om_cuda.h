@@ -479,6 +479,19 @@ int omCudaStemConvBnActPoolIn(const void* pInput, int nInDtype, void* pWorkspace
  * width <= 128, a 16-bit dtype; else 0 */
 int omCudaStemPoolSupported(int nBatch, int nCin, int nH, int nW, int nCout, int nKH, int nKW,
                             int nStride, int nPad, int nDtype);
+/* new: the stem (bPool = 0: omCudaStemConvBnActIn; 1: omCudaStemConvBnActPoolIn) on an image
+ * that is not normalised yet: channel c of the image becomes (x - pNormMean[c]) * pNormInvStd[c]
+ * in fp32, subtract then multiply, before the rounding to 16 bits; padding stays 0. That is the
+ * reference's ImageNet normalisation of inferBatch (EngineBridge.cpp:3580-3594, normalizeImage
+ * om.engine.data_pipeline.ixx:744-803, invstd = 1.0f / std), done inside the stem's pre-pass
+ * instead of on the host: with an fp32 image the result is bit-identical to normalising on the
+ * host and calling the plain entry point. pNormMean and pNormInvStd are HOST arrays of nCin
+ * floats (nCin <= 16). */
+int omCudaStemConvBnActNormIn(const void* pInput, int nInDtype, const float* pNormMean,
+                              const float* pNormInvStd, void* pWorkspace, const void* pPacked,
+                              const float* pBias, void* pOutput, int nBatch, int nCin, int nH,
+                              int nW, int nCout, int nKH, int nKW, int nStride, int nPad,
+                              int nAct, int nDtype, int bPool);
 /* NCHW fp32 -> NHWC (nDtype) with channels zero-padded to nCs */
 int omCudaNchwToNhwc(const float* pIn, void* pOut, int nN, int nC, int nH, int nW, int nCs,
                      int nDtype);

@@ -153,6 +153,7 @@ _SIGS = {
     "omCudaStemConvBnAct": [P, P, P, P, P, I, I, I, I, I, I, I, I, I, I, I],
     "omCudaStemConvBnActIn": [P, I, P, P, P, P, I, I, I, I, I, I, I, I, I, I, I],
     "omCudaStemConvBnActPoolIn": [P, I, P, P, P, P, I, I, I, I, I, I, I, I, I, I, I],
+    "omCudaStemConvBnActNormIn": [P, I, P, P, P, P, P, P, I, I, I, I, I, I, I, I, I, I, I, I],
     "omCudaStemPoolSupported": [I, I, I, I, I, I, I, I, I, I],
     "omCudaNchwToNhwc": [P, P, I, I, I, I, I, I], "omCudaNhwcToNchw": [P, P, I, I, I, I, I, I],
     "omCudaMaxPool2dNhwc": [P, P, I, I, I, I, I, I, I, I],

@@ -1682,9 +1682,18 @@ __device__ __forceinline__ float stem_src_f(float v) { return v; }
 __device__ __forceinline__ float stem_src_f(__nv_bfloat16 v) { return __bfloat162float(v); }
 __device__ __forceinline__ float stem_src_f(__half v) { return __half2float(v); }
 
+// Per-channel normalisation of the image inside the pre-pass, (x - mean[c]) * invstd[c] in fp32
+// (the reference's normalizeImage, om.engine.data_pipeline.ixx:744-803), before the rounding to
+// 16 bits; padding stays 0, as when a normalised image is zero-padded. on = 0: the image as is.
+struct StemNorm {
+    float mean[16];
+    float invstd[16];
+    int on;
+};
+
 template <typename T, int F, typename S = float>
 __global__ void stem_s2d_kernel(const S* __restrict__ x, T* __restrict__ out, int N, int C,
-                                int H, int W, int Hs, int Ws, int pad) {
+                                int H, int W, int Hs, int Ws, int pad, const StemNorm norm) {
     using H16 = Half16<std::is_same<T, __half>::value ? OM_DTYPE_F16 : OM_DTYPE_BF16>;
     constexpr int CMAX = 16 / (F * F);
     const long long total = (long long)N * Hs * Ws;   // < 2^31, checked by the caller
@@ -1706,8 +1715,13 @@ __global__ void stem_s2d_kernel(const S* __restrict__ x, T* __restrict__ out, in
 #pragma unroll
                 for (int px = 0; px < F; ++px) {
                     const int xx = F * v + px - pad;
-                    vals[(c * F + py) * F + px] =
-                        (row_ok && xx >= 0 && xx < W) ? stem_src_f(__ldg(src + xx)) : 0.f;
+                    float val = 0.f;
+                    if (row_ok && xx >= 0 && xx < W) {
+                        val = stem_src_f(__ldg(src + xx));
+                        // subtract, then multiply: two roundings, as the reference computes it
+                        if (norm.on) val = __fmul_rn(__fsub_rn(val, norm.mean[c]), norm.invstd[c]);
+                    }
+                    vals[(c * F + py) * F + px] = val;
                 }
             }
         }
@@ -2445,7 +2459,8 @@ extern "C" long long omCudaStemWorkspaceBytes(int nBatch, int nCin, int nH, int 
 static int stem_conv(const void* pInput, int nInDtype, void* pWorkspace, const void* pPacked,
                      const float* pBias, void* pOutput, int nBatch, int nCin, int nH, int nW,
                      int nCout, int nKH, int nKW, int nStride, int nPad, int nAct, int nDtype,
-                     bool pool = false);
+                     bool pool = false, const float* pNormMean = nullptr,
+                     const float* pNormInvStd = nullptr);
 
 extern "C" int omCudaStemConvBnAct(const float* pInput, void* pWorkspace, const void* pPacked,
                                    const float* pBias, void* pOutput, int nBatch, int nCin, int nH,
@@ -2486,6 +2501,22 @@ extern "C" int omCudaStemConvBnActPoolIn(const void* pInput, int nInDtype, void*
                      nCout, nKH, nKW, nStride, nPad, nAct, nDtype, true);
 }
 
+extern "C" int omCudaStemConvBnActNormIn(const void* pInput, int nInDtype,
+                                         const float* pNormMean, const float* pNormInvStd,
+                                         void* pWorkspace, const void* pPacked, const float* pBias,
+                                         void* pOutput, int nBatch, int nCin, int nH, int nW,
+                                         int nCout, int nKH, int nKW, int nStride, int nPad,
+                                         int nAct, int nDtype, int bPool) {
+    if (nInDtype != OM_DTYPE_F32 && nInDtype != nDtype) return OM_ERR_UNSUPPORTED;
+    if (!pNormMean || !pNormInvStd) return OM_ERR_INVALID;
+    if (bPool &&
+        !omCudaStemPoolSupported(nBatch, nCin, nH, nW, nCout, nKH, nKW, nStride, nPad, nDtype))
+        return OM_ERR_UNSUPPORTED;
+    return stem_conv(pInput, nInDtype, pWorkspace, pPacked, pBias, pOutput, nBatch, nCin, nH, nW,
+                     nCout, nKH, nKW, nStride, nPad, nAct, nDtype, bPool != 0, pNormMean,
+                     pNormInvStd);
+}
+
 namespace omb {
 namespace tc {
 template <int DT>
@@ -2515,7 +2546,7 @@ static int launch_stem_pool(DeviceCtx* c, const CUtensorMap& ta, const CUtensorM
 static int stem_conv(const void* pInput, int nInDtype, void* pWorkspace, const void* pPacked,
                      const float* pBias, void* pOutput, int nBatch, int nCin, int nH, int nW,
                      int nCout, int nKH, int nKW, int nStride, int nPad, int nAct, int nDtype,
-                     bool pool) {
+                     bool pool, const float* pNormMean, const float* pNormInvStd) {
     OMB_CTX_OR_FAIL(c);
     using namespace omb::tc;
     if (!pInput || !pWorkspace || !pPacked || !pOutput) return OM_ERR_INVALID;
@@ -2534,6 +2565,15 @@ static int stem_conv(const void* pInput, int nInDtype, void* pWorkspace, const v
     const long long pixels = (long long)nBatch * g.Hs * g.Ws;
     if (pixels >= (1LL << 31) || (long long)nBatch * nCin * nH * nW >= (1LL << 40))
         return OM_ERR_UNSUPPORTED;
+    StemNorm norm{};
+    if (pNormMean || pNormInvStd) {
+        if (!pNormMean || !pNormInvStd || nCin > 16) return OM_ERR_INVALID;
+        for (int ch = 0; ch < nCin; ++ch) {
+            norm.mean[ch] = pNormMean[ch];
+            norm.invstd[ch] = pNormInvStd[ch];
+        }
+        norm.on = 1;
+    }
     {
         const long long blocks = (pixels + 255) / 256;
         const int grid = (int)(blocks < 8LL * c->num_sms ? blocks : 8LL * c->num_sms);
@@ -2542,11 +2582,11 @@ static int stem_conv(const void* pInput, int nInDtype, void* pWorkspace, const v
             if (nInDtype == OM_DTYPE_F32)
                 stem_s2d_kernel<T, decltype(f)::value, float><<<grid, 256, 0, c->compute>>>(
                     static_cast<const float*>(pInput), static_cast<T*>(pWorkspace), nBatch, nCin,
-                    nH, nW, g.Hs, g.Ws, nPad);
+                    nH, nW, g.Hs, g.Ws, nPad, norm);
             else
                 stem_s2d_kernel<T, decltype(f)::value, T><<<grid, 256, 0, c->compute>>>(
                     static_cast<const T*>(pInput), static_cast<T*>(pWorkspace), nBatch, nCin, nH,
-                    nW, g.Hs, g.Ws, nPad);
+                    nW, g.Hs, g.Ws, nPad, norm);
         };
         using F1 = std::integral_constant<int, 1>;
         using F2 = std::integral_constant<int, 2>;

@@ -35,6 +35,21 @@ from .synth import ConvSpec, NetSpec
 
 _ACT = {"relu": ACT_RELU, "relu6": ACT_RELU6, "none": ACT_NONE}
 
+# the reference's ImageNet preset (om.engine.data_pipeline.ixx:767-771): (mean, std), RGB
+IMAGENET_NORM = ((0.485, 0.456, 0.406), (0.229, 0.224, 0.225))
+
+
+def _norm_arrays(mean: Sequence[float], std: Sequence[float], channels: int):
+    """Per-channel mean and 1/std as ctypes float arrays, as the reference's normalizeImage
+    derives them: channel c uses entry min(c, 2) when the image has 3 or more channels, entry 0
+    otherwise; std below 1e-7 becomes 1e-7; 1/std is computed in fp32."""
+    m = np.asarray(mean, np.float32)
+    s = np.maximum(np.asarray(std, np.float32), np.float32(1e-7))
+    idx = [min(ch, 2) if channels >= 3 else 0 for ch in range(channels)]
+    inv = (np.float32(1.0) / s).astype(np.float32)
+    arr = ctypes.c_float * channels
+    return arr(*[float(m[i]) for i in idx]), arr(*[float(inv[i]) for i in idx])
+
 
 def stored_channels(c: int) -> int:
     return int(lib.omCudaStoredChannels(c))
@@ -53,10 +68,17 @@ class InferencePlan:
     def __init__(self, net: NetSpec, weights: Dict[str, np.ndarray], batch: int,
                  dtype: int = DTYPE_BF16, h: int = 224, w: int = 224, input_slots: int = 2,
                  input_dtype: int = DTYPE_F32, fuse_pairs: bool = True,
-                 fuse_stem_pool: bool = True):
+                 fuse_stem_pool: bool = True,
+                 input_norm: Optional[Tuple[Sequence[float], Sequence[float]]] = None):
         """input_dtype: element type of the NCHW image the plan takes, fp32 (the engine's
         tensors) or the plan's own 16-bit dtype (half the bytes per image to copy to the
-        device; the stem rounds its input to that type anyway, so the logits are the same)."""
+        device; the stem rounds its input to that type anyway, so the logits are the same).
+
+        input_norm: (mean, std) per channel, e.g. IMAGENET_NORM: the plan takes images that are
+        not normalised yet and normalises them inside the stem's pre-pass as the reference's
+        inferBatch does on the host (normalizeImage: (x - mean) * (1 / std) in fp32; images
+        with more than 3 channels reuse the third channel's values, 1- and 2-channel images the
+        first's). None: the images come normalised."""
         assert dtype in (DTYPE_BF16, DTYPE_F16)
         if input_slots not in (1, 2):
             raise ValueError("input_slots must be 1 or 2")
@@ -64,6 +86,10 @@ class InferencePlan:
             raise ValueError("input_dtype must be fp32 or the plan's dtype")
         self.net, self.batch, self.dtype, self.h, self.w = net, batch, dtype, h, w
         self.input_dtype = input_dtype
+        self.input_norm = None
+        if input_norm is not None:
+            mean, std = input_norm
+            self.input_norm = _norm_arrays(mean, std, 3)
         # a bottleneck's 3x3 conv and the 1x1 expansion after it run as one kernel where it
         # takes the shapes (omCudaConvPairBnAct: the 3x3 output never reaches device memory)
         self.fuse_pairs = fuse_pairs
@@ -92,8 +118,8 @@ class InferencePlan:
             if i == 0 and cv.k <= 8 and cv.groups == 1:
                 pool = net.maxpool and len(net.stem) == 1 and self.fuse_stem_pool
                 cur, hh, ww, c, pooled = self._stem(cv, weights, hh, ww, act0, pool)
-            elif i == 0 and input_dtype != DTYPE_F32:
-                raise ValueError("a 16-bit input needs the image-stem kernel")
+            elif i == 0 and (input_dtype != DTYPE_F32 or input_norm is not None):
+                raise ValueError("a 16-bit or unnormalised input needs the image-stem kernel")
             else:
                 cur, hh, ww, c = self._conv(cv, weights, cur, hh, ww, c, act0)
         if net.maxpool and not pooled:
@@ -215,10 +241,19 @@ class InferencePlan:
         # The input pointer is the one op argument looked up when the op is issued: the slot
         # being captured or launched (every other argument is bound here).
         idt = self.input_dtype
-        fn = "omCudaStemConvBnActPoolIn" if pool else "omCudaStemConvBnActIn"
-        self._op(lambda out=out, ws=ws: call(
-            fn, self.inputs[self._slot].ptr, idt, ws.ptr, packed.ptr,
-            bias.ptr, out.ptr, n, cv.cin, hh, ww, cv.cout, cv.k, cv.k, cv.stride, cv.pad, act, dt),
+        if self.input_norm is not None:
+            # normalisation inside the stem's pre-pass (host arrays, copied at each launch)
+            nm, ni = self.input_norm
+            issue = lambda out=out, ws=ws: call(
+                "omCudaStemConvBnActNormIn", self.inputs[self._slot].ptr, idt, nm, ni, ws.ptr,
+                packed.ptr, bias.ptr, out.ptr, n, cv.cin, hh, ww, cv.cout, cv.k, cv.k, cv.stride,
+                cv.pad, act, dt, int(pool))
+        else:
+            fn = "omCudaStemConvBnActPoolIn" if pool else "omCudaStemConvBnActIn"
+            issue = lambda out=out, ws=ws: call(
+                fn, self.inputs[self._slot].ptr, idt, ws.ptr, packed.ptr, bias.ptr, out.ptr, n,
+                cv.cin, hh, ww, cv.cout, cv.k, cv.k, cv.stride, cv.pad, act, dt)
+        self._op(issue,
             dict(kind="stem", pool=pool, inp=self.in_f32, out=out, w=weights[cv.name + ".weight"],
                  bn=self._bn_params(weights, cv.bn), c=cv.cin, k=cv.cout, ks=cv.k,
                  stride=cv.stride, pad=cv.pad, act=act, h=hh, wd=ww, p=p, q=q, p2=p2, q2=q2))

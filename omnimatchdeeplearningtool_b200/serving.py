@@ -12,9 +12,13 @@ BatchNorm keeps the images independent) and its padding rows are dropped.
 :func:`classify_logits` turns logits into the reference's per-image result
 (EngineBridge.cpp:3691-3717): softmax with the maximum subtracted and the sum floored at 1e-8,
 the most probable class and its probability, and class -1 when that probability is below the
-confidence threshold (``BridgeInferParams::fConfThreshold``, default 0.5). Images are expected
-already normalised: the reference's ImageNet normalisation step (EngineBridge.cpp:3580-3594) is
-the caller's.
+confidence threshold (``BridgeInferParams::fConfThreshold``, default 0.5).
+
+The reference normalises each image on the host before its forward (EngineBridge.cpp:3580-3594:
+the ImageNet preset for ResNet/MobileNet models). With ``normalize=IMAGENET_NORM`` (or any
+(mean, std) pair) the classifier takes the images as the reference's inferBatch does, in [0, 1],
+and each plan normalises them inside its stem's pre-pass on the GPU, with the reference's
+arithmetic; with ``normalize=None`` the images come normalised.
 """
 from __future__ import annotations
 
@@ -103,7 +107,8 @@ class MultiDeviceClassifier:
     def __init__(self, net, weights: Dict[str, np.ndarray], devices: Sequence[int],
                  batch_per_device: int, dtype: int = DTYPE_BF16, h: int = 224, w: int = 224,
                  make_plan: Optional[Callable[[int], object]] = None,
-                 init_device: Optional[Callable[[int], None]] = None):
+                 init_device: Optional[Callable[[int], None]] = None,
+                 normalize=None):
         if not devices:
             raise ValueError("MultiDeviceClassifier needs at least one device")
         if len(set(devices)) != len(devices):
@@ -114,7 +119,8 @@ class MultiDeviceClassifier:
             from .plan import InferencePlan
 
             def make_plan(_device):
-                return InferencePlan(net, weights, batch=batch_per_device, dtype=dtype, h=h, w=w)
+                return InferencePlan(net, weights, batch=batch_per_device, dtype=dtype, h=h, w=w,
+                                     input_norm=normalize)
         if init_device is None:
             from . import backend
             init_device = backend.init

@@ -159,3 +159,44 @@ def test_multi_device_logits_match_one_plan(gpu):
     want_o = orc.forward(net, w, np.ascontiguousarray(x[idx]))
     assert rel_err(got[idx], want_o) <= 2e-2
     assert np.array_equal(got[idx].argmax(1), want_o.argmax(1))
+
+
+def _host_normalise(raw, mean, std):
+    """The reference's normalizeImage on the host: (x - mean) * (1 / std) in fp32."""
+    m = np.asarray(mean, np.float32).reshape(1, -1, 1, 1)
+    inv = (np.float32(1.0) / np.asarray(std, np.float32)).reshape(1, -1, 1, 1)
+    return ((raw - m) * inv).astype(np.float32)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("arch", ["resnet18", "mobilenet"])
+def test_normalisation_on_the_device_matches_the_host(gpu, arch):
+    """Images in [0, 1] normalised inside the stem's pre-pass (InferencePlan input_norm,
+    omCudaStemConvBnActNormIn; ResNet: the stem fused with its max pool, MobileNet: the plain
+    stem) give the logits of host-normalised images, bit for bit; so does the multi-device
+    classifier with normalize=IMAGENET_NORM on every visible device."""
+    from omnimatchdeeplearningtool_b200 import _lib, synth
+    from omnimatchdeeplearningtool_b200.plan import IMAGENET_NORM, InferencePlan
+    net = synth.resnet_spec(18) if arch == "resnet18" else synth.mobilenet_spec()
+    w = synth.make_weights(net)
+    b = 4
+    rng = np.random.Generator(np.random.PCG64(77))
+    raw = rng.random((b, 3, 224, 224), dtype=np.float32)
+    dt = _lib.DTYPE_BF16 if arch == "resnet18" else _lib.DTYPE_F16
+    plain = InferencePlan(net, w, batch=b, dtype=dt)
+    want = plain.run(_host_normalise(raw, *IMAGENET_NORM))
+    plain.close()
+    normed = InferencePlan(net, w, batch=b, dtype=dt, input_norm=IMAGENET_NORM)
+    got = normed.run(raw)
+    normed.close()
+    assert np.array_equal(got, want)
+    assert gpu.kernel_error() == 0
+    if arch == "resnet18":
+        devices = list(range(min(_lib.lib.omCudaGetDeviceCount(), 8)))
+        clf = serving.MultiDeviceClassifier(net, w, devices, b, dtype=dt,
+                                            normalize=IMAGENET_NORM)
+        try:
+            got2 = clf.infer_logits(np.concatenate([raw] * len(devices)))
+        finally:
+            clf.close()
+        assert np.array_equal(got2, np.concatenate([want] * len(devices)))
