@@ -744,6 +744,27 @@ def run_ours(args, world, rank, local, dist):
     plan16.close()
     e2e32, in32, _, logits32, copy32 = _serve_e2e(plan, x, args, world, dist, stream)
     finite = bool(np.isfinite(logits32).all() and np.array_equal(logits16, logits32))
+    # 8-bit images as a camera or decoder delivers them, normalised on the GPU inside the stem's
+    # pre-pass (the reference's ImageNet normalisation of inferBatch): a quarter of the fp32
+    # bytes. Checked against the fp32 image sample / 255 normalised on the host.
+    from omnimatchdeeplearningtool_b200.plan import IMAGENET_NORM
+    x8 = np.random.Generator(np.random.PCG64(1000 + rank)).integers(
+        0, 256, (BATCH, 3, 224, 224), dtype=np.uint8)
+    plan8 = InferencePlan(net, weights, batch=BATCH, dtype=_lib.DTYPE_BF16,
+                          input_dtype=_lib.DTYPE_U8, input_norm=IMAGENET_NORM)
+    plan8.set_input(x8)
+    plan8.launch()
+    call("omCudaSynchronize")
+    plan8.capture()
+    e2e8, in8, _, logits8, copy8 = _serve_e2e(plan8, x8, args, world, dist, stream)
+    plan8.close()
+    mean = np.asarray(IMAGENET_NORM[0], np.float32).reshape(1, 3, 1, 1)
+    inv = (np.float32(1.0) / np.asarray(IMAGENET_NORM[1], np.float32)).reshape(1, 3, 1, 1)
+    x8f = ((x8.astype(np.float32) / np.float32(255.0) - mean) * inv).astype(np.float32)
+    plan.set_input(x8f)
+    plan.launch()
+    ref8 = plan.logits.to_numpy((BATCH, net.classes)).reshape(-1)
+    u8_identical = bool(np.array_equal(logits8, ref8))
 
     # ---------------------------------------------------------------- conv kernel roofline
     durs, replay_s = conv_stamp_profile(plan, max(3, min(args.steps, 10)))
@@ -783,7 +804,12 @@ def run_ours(args, world, rank, local, dist):
                     "input": "bf16 NCHW image (InferencePlan input_dtype; logits bit-identical "
                              "to the fp32-image plan)",
                     "fp32_input": {"value": e2e32, "h2d_bytes_per_step": in32},
-                    "h2d_copy_only_gbs": {"bf16_input": copy16, "fp32_input": copy32}},
+                    "u8_input": {"value": e2e8, "h2d_bytes_per_step": in8,
+                                 "input": "uint8 NCHW image, / 255 and ImageNet-normalised on "
+                                          "the GPU in the stem's pre-pass",
+                                 "logits_identical_to_host_normalised_fp32": u8_identical},
+                    "h2d_copy_only_gbs": {"bf16_input": copy16, "fp32_input": copy32,
+                                          "u8_input": copy8}},
             "roofline": {"bound": "tensor", "kernel": "conv_tc_kernel (tcgen05 implicit GEMM)",
                          "achieved": achieved, "peak": peak_burst, "unit": "TFLOP/s",
                          "frac": achieved / peak_burst,

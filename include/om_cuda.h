@@ -42,6 +42,8 @@ extern "C" {
 #define OM_DTYPE_F32 0
 #define OM_DTYPE_BF16 1
 #define OM_DTYPE_F16 2
+/* 8-bit image samples (value = sample / 255): only as the image input of the stem entry points */
+#define OM_DTYPE_U8 3
 
 /* fused epilogue activations */
 #define OM_ACT_NONE 0
@@ -457,9 +459,12 @@ int omCudaPackStemWeight(const float* pWeight, const float* pConvBias, const flo
 int omCudaStemConvBnAct(const float* pInput, void* pWorkspace, const void* pPacked,
                         const float* pBias, void* pOutput, int nBatch, int nCin, int nH, int nW,
                         int nCout, int nKH, int nKW, int nStride, int nPad, int nAct, int nDtype);
-/* new: omCudaStemConvBnAct from an NCHW image in nInDtype: OM_DTYPE_F32, or the conv's own
+/* new: omCudaStemConvBnAct from an NCHW image in nInDtype: OM_DTYPE_F32, the conv's own
  * 16-bit nDtype (half the bytes to move to the device; a 16-bit image gives the same output as
- * its fp32 form, since the stem rounds its input to nDtype anyway) */
+ * its fp32 form, since the stem rounds its input to nDtype anyway), or OM_DTYPE_U8, 8-bit
+ * samples read as sample / 255 in fp32 (a quarter of the bytes; the same output as the fp32
+ * image sample / 255.0f). The same input dtypes apply to omCudaStemConvBnActPoolIn and
+ * omCudaStemConvBnActNormIn. */
 int omCudaStemConvBnActIn(const void* pInput, int nInDtype, void* pWorkspace, const void* pPacked,
                           const float* pBias, void* pOutput, int nBatch, int nCin, int nH, int nW,
                           int nCout, int nKH, int nKW, int nStride, int nPad, int nAct,

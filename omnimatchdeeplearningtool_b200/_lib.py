@@ -26,6 +26,7 @@ STATUS_NAMES = {
     -9: "OM_ERR_COMM",
 }
 DTYPE_F32, DTYPE_BF16, DTYPE_F16 = 0, 1, 2
+DTYPE_U8 = 3   # 8-bit image samples (value / 255), an input dtype of the stem entry points
 ACT_NONE, ACT_RELU, ACT_RELU6 = 0, 1, 2
 
 

@@ -1681,6 +1681,9 @@ static bool stem_geom(int nCin, int nH, int nW, int nKH, int nKW, int nStride, i
 __device__ __forceinline__ float stem_src_f(float v) { return v; }
 __device__ __forceinline__ float stem_src_f(__nv_bfloat16 v) { return __bfloat162float(v); }
 __device__ __forceinline__ float stem_src_f(__half v) { return __half2float(v); }
+// an 8-bit sample is the image value times 255: v / 255 in fp32, correctly rounded, as the host
+// turns 8-bit images into the engine's [0, 1] floats
+__device__ __forceinline__ float stem_src_f(uint8_t v) { return __fdiv_rn((float)v, 255.f); }
 
 // Per-channel normalisation of the image inside the pre-pass, (x - mean[c]) * invstd[c] in fp32
 // (the reference's normalizeImage, om.engine.data_pipeline.ixx:744-803), before the rounding to
@@ -2474,7 +2477,8 @@ extern "C" int omCudaStemConvBnActIn(const void* pInput, int nInDtype, void* pWo
                                      const void* pPacked, const float* pBias, void* pOutput,
                                      int nBatch, int nCin, int nH, int nW, int nCout, int nKH,
                                      int nKW, int nStride, int nPad, int nAct, int nDtype) {
-    if (nInDtype != OM_DTYPE_F32 && nInDtype != nDtype) return OM_ERR_UNSUPPORTED;
+    if (nInDtype != OM_DTYPE_F32 && nInDtype != OM_DTYPE_U8 && nInDtype != nDtype)
+        return OM_ERR_UNSUPPORTED;
     return stem_conv(pInput, nInDtype, pWorkspace, pPacked, pBias, pOutput, nBatch, nCin, nH, nW,
                      nCout, nKH, nKW, nStride, nPad, nAct, nDtype);
 }
@@ -2494,7 +2498,8 @@ extern "C" int omCudaStemConvBnActPoolIn(const void* pInput, int nInDtype, void*
                                          const void* pPacked, const float* pBias, void* pPooled,
                                          int nBatch, int nCin, int nH, int nW, int nCout, int nKH,
                                          int nKW, int nStride, int nPad, int nAct, int nDtype) {
-    if (nInDtype != OM_DTYPE_F32 && nInDtype != nDtype) return OM_ERR_UNSUPPORTED;
+    if (nInDtype != OM_DTYPE_F32 && nInDtype != OM_DTYPE_U8 && nInDtype != nDtype)
+        return OM_ERR_UNSUPPORTED;
     if (!omCudaStemPoolSupported(nBatch, nCin, nH, nW, nCout, nKH, nKW, nStride, nPad, nDtype))
         return OM_ERR_UNSUPPORTED;
     return stem_conv(pInput, nInDtype, pWorkspace, pPacked, pBias, pPooled, nBatch, nCin, nH, nW,
@@ -2507,7 +2512,8 @@ extern "C" int omCudaStemConvBnActNormIn(const void* pInput, int nInDtype,
                                          void* pOutput, int nBatch, int nCin, int nH, int nW,
                                          int nCout, int nKH, int nKW, int nStride, int nPad,
                                          int nAct, int nDtype, int bPool) {
-    if (nInDtype != OM_DTYPE_F32 && nInDtype != nDtype) return OM_ERR_UNSUPPORTED;
+    if (nInDtype != OM_DTYPE_F32 && nInDtype != OM_DTYPE_U8 && nInDtype != nDtype)
+        return OM_ERR_UNSUPPORTED;
     if (!pNormMean || !pNormInvStd) return OM_ERR_INVALID;
     if (bPool &&
         !omCudaStemPoolSupported(nBatch, nCin, nH, nW, nCout, nKH, nKW, nStride, nPad, nDtype))
@@ -2583,6 +2589,10 @@ static int stem_conv(const void* pInput, int nInDtype, void* pWorkspace, const v
                 stem_s2d_kernel<T, decltype(f)::value, float><<<grid, 256, 0, c->compute>>>(
                     static_cast<const float*>(pInput), static_cast<T*>(pWorkspace), nBatch, nCin,
                     nH, nW, g.Hs, g.Ws, nPad, norm);
+            else if (nInDtype == OM_DTYPE_U8)
+                stem_s2d_kernel<T, decltype(f)::value, uint8_t><<<grid, 256, 0, c->compute>>>(
+                    static_cast<const uint8_t*>(pInput), static_cast<T*>(pWorkspace), nBatch,
+                    nCin, nH, nW, g.Hs, g.Ws, nPad, norm);
             else
                 stem_s2d_kernel<T, decltype(f)::value, T><<<grid, 256, 0, c->compute>>>(
                     static_cast<const T*>(pInput), static_cast<T*>(pWorkspace), nBatch, nCin, nH,

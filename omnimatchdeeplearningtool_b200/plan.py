@@ -28,12 +28,16 @@ from typing import Callable, Dict, List, Optional, Sequence, Tuple
 import numpy as np
 
 from . import _lib
-from ._lib import ACT_NONE, ACT_RELU, ACT_RELU6, DTYPE_BF16, DTYPE_F16, DTYPE_F32, call, lib
+from ._lib import (ACT_NONE, ACT_RELU, ACT_RELU6, DTYPE_BF16, DTYPE_F16, DTYPE_F32, DTYPE_U8,
+                   call, lib)
 from .backend import CUDABackend as B
 from .backend import DeviceBuffer
 from .synth import ConvSpec, NetSpec
 
 _ACT = {"relu": ACT_RELU, "relu6": ACT_RELU6, "none": ACT_NONE}
+
+# bytes per image sample of each input dtype
+_INPUT_SIZE = {DTYPE_F32: 4, DTYPE_BF16: 2, DTYPE_F16: 2, DTYPE_U8: 1}
 
 # the reference's ImageNet preset (om.engine.data_pipeline.ixx:767-771): (mean, std), RGB
 IMAGENET_NORM = ((0.485, 0.456, 0.406), (0.229, 0.224, 0.225))
@@ -71,8 +75,10 @@ class InferencePlan:
                  fuse_stem_pool: bool = True,
                  input_norm: Optional[Tuple[Sequence[float], Sequence[float]]] = None):
         """input_dtype: element type of the NCHW image the plan takes, fp32 (the engine's
-        tensors) or the plan's own 16-bit dtype (half the bytes per image to copy to the
-        device; the stem rounds its input to that type anyway, so the logits are the same).
+        tensors), the plan's own 16-bit dtype (half the bytes per image to copy to the
+        device; the stem rounds its input to that type anyway, so the logits are the same), or
+        DTYPE_U8: 8-bit samples, read as sample / 255 in fp32 on the device (a quarter of the
+        bytes; the logits of the fp32 image sample / 255), usually with input_norm.
 
         input_norm: (mean, std) per channel, e.g. IMAGENET_NORM: the plan takes images that are
         not normalised yet and normalises them inside the stem's pre-pass as the reference's
@@ -82,8 +88,8 @@ class InferencePlan:
         assert dtype in (DTYPE_BF16, DTYPE_F16)
         if input_slots not in (1, 2):
             raise ValueError("input_slots must be 1 or 2")
-        if input_dtype not in (DTYPE_F32, dtype):
-            raise ValueError("input_dtype must be fp32 or the plan's dtype")
+        if input_dtype not in (DTYPE_F32, dtype, DTYPE_U8):
+            raise ValueError("input_dtype must be fp32, the plan's dtype or DTYPE_U8")
         self.net, self.batch, self.dtype, self.h, self.w = net, batch, dtype, h, w
         self.input_dtype = input_dtype
         self.input_norm = None
@@ -106,7 +112,7 @@ class InferencePlan:
         self.meta: List[dict] = []         # one descriptor per op (kind, buffers, shape)
         # input staging: NCHW fp32 as the engine hands it over. With two slots the next batch's
         # host->device copy lands in one slot while the forward reads the other (serve()).
-        self.in_bytes = batch * 3 * h * w * (4 if input_dtype == DTYPE_F32 else 2)
+        self.in_bytes = batch * 3 * h * w * _INPUT_SIZE[input_dtype]
         self.inputs = [self._buf(self.in_bytes) for _ in range(input_slots)]
         self.in_f32 = self.inputs[0]
         self._slot = 0                # the slot the stem reads when ops are issued
@@ -235,7 +241,7 @@ class InferencePlan:
         out = self._buf(n * p2 * q2 * cv.cout * 2)
         ws = self._buf(int(lib.omCudaStemWorkspaceBytes(n, cv.cin, hh, ww, cv.k, cv.k, cv.stride,
                                                         cv.pad)))
-        esize = 4 if self.input_dtype == DTYPE_F32 else 2
+        esize = _INPUT_SIZE[self.input_dtype]
         for x in self.inputs:
             self._need(x, n * cv.cin * hh * ww * esize)
         # The input pointer is the one op argument looked up when the op is issued: the slot
@@ -397,8 +403,13 @@ class InferencePlan:
         self._slot = 0
 
     def host_input(self, x: np.ndarray) -> np.ndarray:
-        """The NCHW image in the plan's input_dtype, as bytes to copy to the device."""
+        """The NCHW image in the plan's input_dtype, as bytes to copy to the device (DTYPE_U8:
+        the caller's uint8 samples as they are)."""
         assert x.shape == (self.batch, 3, self.h, self.w)
+        if self.input_dtype == DTYPE_U8:
+            if x.dtype != np.uint8:
+                raise TypeError("an 8-bit plan takes uint8 images")
+            return np.ascontiguousarray(x)
         x = np.ascontiguousarray(x, dtype=np.float32)
         if self.input_dtype == DTYPE_F32:
             return x

@@ -28,7 +28,7 @@ from typing import Callable, Dict, List, NamedTuple, Optional, Sequence
 
 import numpy as np
 
-from ._lib import DTYPE_BF16
+from ._lib import DTYPE_BF16, DTYPE_F32, DTYPE_U8
 
 
 class InferResult(NamedTuple):
@@ -108,7 +108,7 @@ class MultiDeviceClassifier:
                  batch_per_device: int, dtype: int = DTYPE_BF16, h: int = 224, w: int = 224,
                  make_plan: Optional[Callable[[int], object]] = None,
                  init_device: Optional[Callable[[int], None]] = None,
-                 normalize=None):
+                 normalize=None, input_dtype: int = DTYPE_F32):
         if not devices:
             raise ValueError("MultiDeviceClassifier needs at least one device")
         if len(set(devices)) != len(devices):
@@ -120,11 +120,13 @@ class MultiDeviceClassifier:
 
             def make_plan(_device):
                 return InferencePlan(net, weights, batch=batch_per_device, dtype=dtype, h=h, w=w,
-                                     input_norm=normalize)
+                                     input_norm=normalize, input_dtype=input_dtype)
         if init_device is None:
             from . import backend
             init_device = backend.init
         self.batch = batch_per_device
+        # DTYPE_U8: the images are uint8 samples (value / 255), a quarter of the bytes to copy
+        self.u8 = input_dtype == DTYPE_U8
         self.shape = (3, h, w) if net is None else (net.stem[0].cin, h, w)
         self.workers = [_Worker(d, (lambda d=d: make_plan(d)), init_device) for d in devices]
         try:
@@ -135,8 +137,11 @@ class MultiDeviceClassifier:
             raise
 
     def infer_logits(self, images: np.ndarray) -> np.ndarray:
-        """[n, C, H, W] fp32 host images -> [n, classes] fp32 logits, in input order."""
-        x = np.ascontiguousarray(images, np.float32)
+        """[n, C, H, W] fp32 host images (uint8 with input_dtype=DTYPE_U8) -> [n, classes] fp32
+        logits, in input order."""
+        if self.u8 and np.asarray(images).dtype != np.uint8:
+            raise TypeError("an 8-bit classifier takes uint8 images")
+        x = np.ascontiguousarray(images, np.uint8 if self.u8 else np.float32)
         if x.ndim != 4 or x.shape[1:] != self.shape:
             raise ValueError(f"images must be [n, {self.shape[0]}, {self.shape[1]}, "
                              f"{self.shape[2]}], got {x.shape}")
@@ -150,7 +155,7 @@ class MultiDeviceClassifier:
             part = x[s:e]
             if e - s < self.batch:  # the ragged end: zero rows, dropped again below
                 part = np.concatenate([part, np.zeros((self.batch - (e - s),) + self.shape,
-                                                      np.float32)])
+                                                      x.dtype)])
             self.workers[i % len(self.workers)].jobs.put((part, results, i, done))
         for _ in chunks:
             done.acquire()

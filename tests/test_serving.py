@@ -200,3 +200,38 @@ def test_normalisation_on_the_device_matches_the_host(gpu, arch):
         finally:
             clf.close()
         assert np.array_equal(got2, np.concatenate([want] * len(devices)))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("pool", [True, False])
+def test_u8_images_match_their_float_form(gpu, pool):
+    """8-bit images (input_dtype DTYPE_U8, sample / 255 on the device) normalised on the device
+    give the logits of the fp32 images sample / 255.0f normalised on the host, bit for bit;
+    with the stem fused with its max pool and without (omCudaStemConvBnActNormIn bPool 1 / 0);
+    and through the multi-device classifier."""
+    from omnimatchdeeplearningtool_b200 import _lib, synth
+    from omnimatchdeeplearningtool_b200.plan import IMAGENET_NORM, InferencePlan
+    net = synth.resnet_spec(18)
+    w = synth.make_weights(net)
+    b = 4
+    rng = np.random.Generator(np.random.PCG64(78))
+    u8 = rng.integers(0, 256, (b, 3, 224, 224), dtype=np.uint8)
+    as_float = (u8.astype(np.float32) / np.float32(255.0)).astype(np.float32)
+    plain = InferencePlan(net, w, batch=b, fuse_stem_pool=pool)
+    want = plain.run(_host_normalise(as_float, *IMAGENET_NORM))
+    plain.close()
+    p8 = InferencePlan(net, w, batch=b, fuse_stem_pool=pool, input_dtype=_lib.DTYPE_U8,
+                       input_norm=IMAGENET_NORM)
+    assert p8.in_bytes == b * 3 * 224 * 224
+    got = p8.run(u8)
+    p8.close()
+    assert np.array_equal(got, want)
+    assert gpu.kernel_error() == 0
+    if pool:
+        clf = serving.MultiDeviceClassifier(net, w, [0], b, normalize=IMAGENET_NORM,
+                                            input_dtype=_lib.DTYPE_U8)
+        try:
+            got2 = clf.infer_logits(u8[:3])
+        finally:
+            clf.close()
+        assert np.array_equal(got2, want[:3])
