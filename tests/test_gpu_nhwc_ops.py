@@ -189,6 +189,9 @@ def _hfma_depthwise(x16, w16, b16, stride, act6=True):
     (2, 256, 112, 112, 1),   # ring kernel, two 128-channel tiles per pixel
     (5, 192, 9, 11, 1),      # ring kernel, 64-channel tiles, runs that cross images
     (3, 64, 15, 13, 2),      # ring kernel, stride 2, odd sizes
+    (1, 64, 3, 254, 1),      # ring kernel, the widest row a slot takes (256 columns)
+    (2, 64, 1, 1, 1),        # ring kernel, 1x1 images
+    (1, 128, 2, 3, 2),       # ring kernel, stride 2 on a 2x3 image
     (2, 32, 20, 18, 1),      # direct kernel (32 channels), row pairs
     (1, 64, 9, 300, 2),      # direct kernel (row wider than a ring slot)
 ])
