@@ -69,6 +69,32 @@ def test_resnet50_bf16_batch256_matches_oracle_on_subset(gpu):
     assert np.array_equal(got[idx].argmax(1), want.argmax(1))
 
 
+def test_mobilenet_f16_batch256_matches_oracle_on_subset(gpu):
+    """The benchmarked MobileNet-style configuration: the fp16 plan at batch 256, whose
+    depthwise layers run on the TMA row-ring kernel with whole-pixel channel tiles and CTA
+    ranges that cross images (shapes batch 2 does not reach), compared with the fp32 oracle on
+    the first two and the last two images: <= 2e-2 and identical top-1."""
+    import oracle as orc
+    from omnimatchdeeplearningtool_b200 import _lib, synth
+    from omnimatchdeeplearningtool_b200.plan import InferencePlan
+    net = synth.mobilenet_spec()
+    w = synth.make_weights(net)
+    x = synth.normal_input(256, seed=5)
+    plan = InferencePlan(net, w, batch=256, dtype=_lib.DTYPE_F16)
+    try:
+        plan.capture()
+        got = plan.run(x)
+    finally:
+        plan.close()
+    assert np.isfinite(got).all()
+    idx = [0, 1, 254, 255]
+    want = orc.forward(net, w, np.ascontiguousarray(x[idx]))
+    e = rel_err(got[idx], want)
+    print(f"mobilenet f16 batch 256, images {idx}: max rel err {e:.2e}")
+    assert e <= 2e-2, e
+    assert np.array_equal(got[idx].argmax(1), want.argmax(1))
+
+
 @pytest.mark.parametrize("name,dtype", [("resnet50", "bf16"), ("mobilenet", "f16")])
 def test_16bit_input_gives_the_same_logits(gpu, name, dtype):
     """A plan that takes its NCHW image in its own 16-bit type (input_dtype; half the bytes to
