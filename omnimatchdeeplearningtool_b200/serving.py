@@ -171,6 +171,15 @@ class MultiDeviceClassifier:
         """The reference's ``inferBatch`` result for each image."""
         return classify_logits(self.infer_logits(images), conf_threshold)
 
+    def infer(self, image: np.ndarray, conf_threshold: float = 0.5) -> InferResult:
+        """The reference's single-image ``infer`` (EngineBridge.cpp:3100-3200) for a
+        classifier: one [C, H, W] image, on the first device's plan (build the classifier with
+        ``batch_per_device=1`` for the lowest latency; a larger plan pads the image)."""
+        x = np.asarray(image)
+        if x.shape != self.shape:
+            raise ValueError(f"image must be {list(self.shape)}, got {list(x.shape)}")
+        return self.infer_batch(x[None], conf_threshold)[0]
+
     def close(self) -> None:
         for wk in self.workers:
             wk.stop()

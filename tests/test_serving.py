@@ -62,6 +62,23 @@ def test_chunks_are_dealt_round_robin_padded_and_reassembled():
     assert sorted(e[0] for e in log if e[1] == "closed") == [3, 5, 7]
 
 
+def test_single_image_infer():
+    """infer(image): one [C, H, W] image through the first device, the reference's single-image
+    result; a wrongly shaped image is refused."""
+    log = []
+    clf = _classifier([2, 4], 1, log)
+    x = np.zeros((3, 2, 2), np.float32)
+    x[0, 0, 0] = 9.0
+    r = clf.infer(x)
+    assert isinstance(r, serving.InferResult)
+    assert r.probs.shape == (3,)
+    runs = [e for e in log if len(e) == 4]
+    assert [e[0] for e in runs] == [2]
+    with pytest.raises(ValueError):
+        clf.infer(np.zeros((1, 3, 2, 2), np.float32))
+    clf.close()
+
+
 def test_arguments_and_failures_are_reported():
     log = []
     with pytest.raises(ValueError):
