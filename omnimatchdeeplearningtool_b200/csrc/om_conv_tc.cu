@@ -430,7 +430,7 @@ __device__ __forceinline__ void warp_transpose_sum(float (&x)[32]) {
 // BatchNorm statistics of an fp32 NCHW output chunk (MODE_TF32 with p.bn_part): rows mw ..
 // mw+31 (the valid ones), 32 channels from n0. Per channel, the chunk's mean and the sum of
 // squared deviations from it (two passes over the registers), written for a fixed-order
-// combination later (Chan et al.'s pairwise update). Called by the whole warp.
+// combination later (the parallel form of the two-pass variance). Called by the whole warp.
 __device__ __forceinline__ void chunk_bn_stats(const Params& p, int mw, int n0,
                                                const uint32_t (&v)[32]) {
     const int lane = threadIdx.x & 31;

@@ -586,20 +586,22 @@ static int bn_apply(DeviceCtx* c, const float* x, float* y, const float* gamma, 
 
 // BatchNorm statistics from a convolution's per-group partials (the 3xTF32 conv epilogue with
 // bn_part): for channel c, G groups of 32 output pixels (the last one holds cnt - 32 (G - 1)),
-// each with its mean and sum of squared deviations. They are combined with Chan et al.'s
-// pairwise update (n = na + nb, d = mb - ma, m = ma + d nb / n, M2 = M2a + M2b + d^2 na nb / n)
-// in a fixed order: thread t takes groups t, t + 256, ... one after another, then the 256
-// partials are combined pairwise down a tree. Then, as bn_finalize_kernel: biased variance,
-// running statistics with momentum, saved mean and 1/sqrt(var + eps). One block per channel.
-__device__ __forceinline__ void chan_combine(float& na, float& ma, float& m2a, float nb, float mb,
-                                             float m2b) {
-    const float n = na + nb;
-    if (nb == 0.f) return;
-    const float d = mb - ma;
-    const float f = nb / n;
-    ma += d * f;
-    m2a += m2b + d * d * na * f;
-    na = n;
+// each with its mean m_g and sum of squared deviations q_g. The channel's mean is
+// sum n_g m_g / cnt and its sum of squared deviations sum (q_g + n_g (m_g - mean)^2) (the
+// parallel form of the two-pass variance, exact in real arithmetic), each summed in a fixed
+// order: thread t takes groups t, t + 256, ..., then the 256 partial sums are added pairwise
+// down a tree. Then, as bn_finalize_kernel: biased variance, running statistics with momentum,
+// saved mean and 1/sqrt(var + eps). One block per channel.
+__device__ __forceinline__ float bn_tree_sum(float v, float* sh) {
+    sh[threadIdx.x] = v;
+    __syncthreads();
+    for (int h = 128; h >= 1; h >>= 1) {
+        if ((int)threadIdx.x < h) sh[threadIdx.x] += sh[threadIdx.x + h];
+        __syncthreads();
+    }
+    const float r = sh[0];
+    __syncthreads();
+    return r;
 }
 __global__ void __launch_bounds__(256) bn_chan_finalize_kernel(
     const float* __restrict__ part, int G, long long cnt, int C, float* run_mean, float* run_var,
@@ -607,25 +609,20 @@ __global__ void __launch_bounds__(256) bn_chan_finalize_kernel(
     const int c = blockIdx.x;
     const float* pm = part + (size_t)c * G;
     const float* pq = part + ((size_t)C + c) * G;
-    float n = 0.f, m = 0.f, m2 = 0.f;
+    __shared__ float sh[256];
+    // every group holds 32 pixels except possibly the last
+    const float n_last = (float)(cnt - 32LL * (G - 1));
+    float s = 0.f;
+    for (int g = threadIdx.x; g < G; g += 256) s += (g == G - 1 ? n_last : 32.f) * pm[g];
+    const float mean = bn_tree_sum(s, sh) / (float)cnt;
+    float q = 0.f;
     for (int g = threadIdx.x; g < G; g += 256) {
-        const long long left = cnt - 32LL * g;
-        chan_combine(n, m, m2, (float)(left < 32 ? left : 32), pm[g], pq[g]);
+        const float d = pm[g] - mean;
+        q += pq[g] + (g == G - 1 ? n_last : 32.f) * d * d;
     }
-    __shared__ float sn[256], sm[256], sq[256];
-    sn[threadIdx.x] = n; sm[threadIdx.x] = m; sq[threadIdx.x] = m2;
-    __syncthreads();
-    for (int h = 128; h >= 1; h >>= 1) {
-        if ((int)threadIdx.x < h) {
-            float a = sn[threadIdx.x], b = sm[threadIdx.x], q = sq[threadIdx.x];
-            chan_combine(a, b, q, sn[threadIdx.x + h], sm[threadIdx.x + h], sq[threadIdx.x + h]);
-            sn[threadIdx.x] = a; sm[threadIdx.x] = b; sq[threadIdx.x] = q;
-        }
-        __syncthreads();
-    }
+    const float m2 = bn_tree_sum(q, sh);
     if (threadIdx.x == 0) {
-        const float mean = sm[0];
-        const float var = sq[0] / (float)cnt;
+        const float var = m2 / (float)cnt;
         run_mean[c] = (1.f - momentum) * run_mean[c] + momentum * mean;
         run_var[c] = (1.f - momentum) * run_var[c] + momentum * var;
         saved_mean[c] = mean;
