@@ -203,13 +203,29 @@ int omCudaBatchNorm2dAct(const float* pInput, float* pOutput, const float* pGamm
  * OM_ACT_RELU) applied, and the saved mean and 1/sqrt(var + eps) its backward needs. The
  * statistics are combined in a fixed order, so the result is deterministic; they agree with
  * omCudaBatchNorm2d's two-pass statistics to fp32 rounding. pConvOut is written once and read
- * once. */
+ * once. pInputSplit (may be NULL): a device buffer of omCudaConvInputSplitBytes(nBatch, nCin,
+ * nH, nW, nStride) bytes (when that is not 0) that receives the convolution's tensor-core copy
+ * of pInput and keeps it for omCudaConv2dBackwardWeightSplit, which then does not make it
+ * again. */
 int omCudaConv2dBatchNorm2dAct(const float* pInput, const float* pWeight, const float* pBias,
                                float* pConvOut, float* pOutput, const float* pGamma,
                                const float* pBeta, float* pRunMean, float* pRunVar,
                                float* pSavedMean, float* pSavedInvStd, int nBatch, int nCin,
                                int nH, int nW, int nCout, int nKH, int nKW, int nStride, int nPad,
-                               float fEps, float fMomentum, int nAct);
+                               float fEps, float fMomentum, int nAct, void* pInputSplit);
+/* new: bytes of the kept input copy that omCudaConv2dBatchNorm2dAct writes and
+ * omCudaConv2dBackwardWeightSplit reads (the hi and lo fp32 parts of the NHWC input with the
+ * channels padded to 32); 0 when the weight gradient of this shape makes its own copy (stride-2
+ * convs of at most 8 input channels) or the arguments are invalid */
+long long omCudaConvInputSplitBytes(int nBatch, int nCin, int nH, int nW, int nStride);
+/* new: omCudaConv2dBackwardWeight reading the input's kept copy (pInputSplit, written by the
+ * forward omCudaConv2dBatchNorm2dAct of the same pInput and shape, unchanged since) instead of
+ * copying pInput again; pInput is still read where the tensor path does not take the shape.
+ * Bit-identical to omCudaConv2dBackwardWeight. */
+int omCudaConv2dBackwardWeightSplit(const float* pInput, const void* pInputSplit,
+                                    const float* pGradOutput, float* pGradWeight,
+                                    float* pGradBias, int nBatch, int nCin, int nH, int nW,
+                                    int nCout, int nKH, int nKW, int nStride, int nPad);
 /* new: the matching backward (the reference calls its ReLU backward, then :3130). pOutput is the
  * forward's activated output: the incoming gradient is zeroed where pOutput <= 0 inside the BN
  * backward passes. Bit-identical to omCudaReLUBackward followed by omCudaBatchNorm2dBackward. */

@@ -94,7 +94,8 @@ _SIGS = {
     "omCudaBatchNorm2dBackward": [P, P, P, P, P, P, P, P, I, I, I, I, F],
     "omCudaBatchNorm2dAct": [P, P, P, P, P, P, P, P, I, I, I, I, F, F, I, I],
     "omCudaConv2dBatchNorm2dAct": [P, P, P, P, P, P, P, P, P, P, P, I, I, I, I, I, I, I, I, I,
-                                   F, F, I],
+                                   F, F, I, P],
+    "omCudaConv2dBackwardWeightSplit": [P, P, P, P, P, I, I, I, I, I, I, I, I, I],
     "omCudaBatchNorm2dBackwardAct": [P, P, P, P, P, P, P, P, P, I, I, I, I, F, I],
     "omCudaBatchNorm2dNoAlloc": [P, P, P, P, P, P, P, P, I, I, I, I, F, F, I],
     "omCudaMaxPool2d": [P, P, P, I, I, I, I, I, I, I, I, I, I],
@@ -177,10 +178,12 @@ lib.omCudaStemWorkspaceBytes.argtypes = [I, I, I, I, I, I, I, I]
 lib.omCudaStemWorkspaceBytes.restype = c_longlong
 lib.omCudaStoredChannels.argtypes = [I]
 lib.omCudaStoredChannels.restype = c_int
+lib.omCudaConvInputSplitBytes.argtypes = [I, I, I, I, I]
+lib.omCudaConvInputSplitBytes.restype = c_longlong
 
 EXPORTED = sorted(list(_SIGS) + ["omCudaGetStream", "omCudaPackedConvWeightElems",
                                  "omCudaPackedStemWeightElems", "omCudaStemWorkspaceBytes",
-                                 "omCudaStoredChannels"])
+                                 "omCudaStoredChannels", "omCudaConvInputSplitBytes"])
 
 
 def check(status: int, fn: str = "omCuda") -> None:

@@ -41,16 +41,29 @@ namespace tc {
 // epilogue also writes BatchNorm statistics of the output per 32-pixel group g = m / 32 of the
 // N*P*Q output pixels m (G = ceil(N*P*Q / 32) groups) and channel k: the group's mean at
 // bn_part[k*G + g], its sum of squared deviations from that mean at bn_part[(Kout + k)*G + g].
-// Returns OM_ERR_UNSUPPORTED for shapes the tensor path does not take and OM_ERR_OOM when its
-// operand copies do not fit; nothing is launched then.
+// With keep_split the NHWC hi/lo copy of the source is written to that caller buffer (hi at
+// byte 0, lo at byte conv_split_half_bytes(N, Hp, Wp, Cin)) instead of scratch, and stays
+// there for the weight gradient. Returns OM_ERR_UNSUPPORTED for shapes the tensor path does
+// not take and OM_ERR_OOM when its operand copies do not fit; nothing is launched then.
 int tf32_conv(DeviceCtx* c, const float* src, int N, int Cin, int Hin, int Win, int Hp, int Wp,
               int offh, int offw, int up, const float* w, int Kout, int R, int S, bool flip,
               int Cw, const float* bias, float* out, int stride, int pad, int dil = 1,
-              int src_ctot = 0, int out_ktot = 0, float* bn_part = nullptr);
+              int src_ctot = 0, int out_ktot = 0, float* bn_part = nullptr,
+              float* keep_split = nullptr);
+// Bytes of one half (hi or lo) of a kept input copy: N*H*W*ceil32(C) floats, rounded up to 256.
+inline size_t conv_split_half_bytes(long long N, long long H, long long W, long long C) {
+    return ((size_t)(N * H * W * ((C + 31) / 32 * 32)) * 4 + 255) / 256 * 256;
+}
+// The kept input copy of tf32_conv's keep_split written on its own (for a forward that did not
+// take the tensor path).
+int tf32_split_input(DeviceCtx* c, const float* x, int N, int C, int H, int W, float* keep_split);
+// Whether tf32_wgrad reads a kept input copy for this shape (it takes the space-to-depth form,
+// with its own copy, for stride-2 convs of at most 8 input channels).
+inline bool wgrad_reads_kept_split(int Cin, int stride) { return !(stride == 2 && Cin * 4 <= 32); }
 // 3xTF32 tensor-core weight gradient of a (stride, pad) convolution: dW [K, Cin, R, S] from
 // X [N, Cin, H, W] and dY [N, K, P, Q], all NCHW fp32 (om_conv_tc.cu).
 int tf32_wgrad(DeviceCtx* c, const float* x, const float* dy, float* dw, int N, int Cin, int H,
-               int W, int K, int R, int S, int stride, int pad);
+               int W, int K, int R, int S, int stride, int pad, const float* given_split = nullptr);
 }  // namespace tc
 
 inline int status_of(cudaError_t e) { return e == cudaSuccess ? OM_OK : OM_ERR_CUDA; }

@@ -3579,7 +3579,7 @@ static bool tf32_pad_ok(int R, int S, int pad) {
 int tf32_conv(DeviceCtx* c, const float* src, int N, int Cin, int Hin, int Win, int Hp, int Wp,
               int offh, int offw, int up, const float* w, int Kout, int R, int S, bool flip,
               int Cw, const float* bias, float* out, int stride, int pad, int dil, int src_ctot,
-              int out_ktot, float* bn_part) {
+              int out_ktot, float* bn_part, float* keep_split) {
     const int Cs = (Cin + 31) / 32 * 32;
     if (dil < 1 || (long long)(R - 1) * dil + 1 > 256 || (long long)(S - 1) * dil + 1 > 256)
         return OM_ERR_UNSUPPORTED;
@@ -3594,17 +3594,20 @@ int tf32_conv(DeviceCtx* c, const float* src, int N, int Cin, int Hin, int Win, 
     if (!load_driver_entry_points()) return OM_ERR_DRIVER;
     const size_t xe = (size_t)N * Hp * Wp * Cs, we = (size_t)Kout * kpad;
     const size_t xb = (xe * 4 + 255) / 256 * 256, wb = (we * 4 + 255) / 256 * 256;
+    // the source's hi/lo copies go to the caller's keep_split (hi at 0, lo at xb) when given
+    const size_t xs = keep_split ? 0 : 2 * xb;
     uint8_t* scratch = nullptr;
-    cudaError_t ae = cudaMallocAsync(&scratch, 2 * xb + 2 * wb, c->compute);
+    cudaError_t ae = cudaMallocAsync(&scratch, xs + 2 * wb, c->compute);
     if (ae == cudaErrorMemoryAllocation) {
         cudaGetLastError();
         return OM_ERR_OOM;
     }
     if (ae != cudaSuccess) return OM_ERR_CUDA;
-    float* xhi = reinterpret_cast<float*>(scratch);
-    float* xlo = reinterpret_cast<float*>(scratch + xb);
-    float* whi = reinterpret_cast<float*>(scratch + 2 * xb);
-    float* wlo = reinterpret_cast<float*>(scratch + 2 * xb + wb);
+    uint8_t* xbase = keep_split ? reinterpret_cast<uint8_t*>(keep_split) : scratch;
+    float* xhi = reinterpret_cast<float*>(xbase);
+    float* xlo = reinterpret_cast<float*>(xbase + xb);
+    float* whi = reinterpret_cast<float*>(scratch + xs);
+    float* wlo = reinterpret_cast<float*>(scratch + xs + wb);
     int st = OM_OK;
     launch_split(c, src, xhi, xlo, N, Cin, Hin, Win, Hp, Wp, Cs, offh, offw, up, 0, src_ctot);
     st = after_launch(c);
@@ -3618,6 +3621,15 @@ int tf32_conv(DeviceCtx* c, const float* src, int N, int Cin, int Hin, int Win, 
                            dil, out_ktot, bn_part);
     cudaFreeAsync(scratch, c->compute);
     return st;
+}
+
+int tf32_split_input(DeviceCtx* c, const float* x, int N, int C, int H, int W, float* keep_split) {
+    if ((long long)N * H * ((W + 31) / 32) >= (1LL << 31) || N > 65535) return OM_ERR_UNSUPPORTED;
+    const int Cs = (C + 31) / 32 * 32;
+    const size_t xb = conv_split_half_bytes(N, H, W, C);
+    launch_split(c, x, keep_split, reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(keep_split) + xb),
+                 N, C, H, W, H, W, Cs, 0, 0, 1, 0);
+    return after_launch(c);
 }
 
 // Geometry of the space-to-depth form of a stride-2 convolution (Cin * 4 <= 32): the 32-channel
@@ -3910,7 +3922,7 @@ static int launch_wgrad(DeviceCtx* c, const CUtensorMap& a_hi, const CUtensorMap
 // four times the channel use of the plain form). Scratch (the hi/lo copies of X and dY and the
 // split partials) comes from the stream-ordered pool.
 int tf32_wgrad(DeviceCtx* c, const float* x, const float* dy, float* dw, int N, int Cin, int H,
-               int W, int K, int R, int S, int stride, int pad) {
+               int W, int K, int R, int S, int stride, int pad, const float* given_split) {
     const int P = (H + 2 * pad - R) / stride + 1, Q = (W + 2 * pad - S) / stride + 1;
     if (P <= 0 || Q <= 0) return OM_ERR_INVALID;
     S2dGeom g;
@@ -3942,21 +3954,29 @@ int tf32_wgrad(DeviceCtx* c, const float* x, const float* dy, float* dw, int N, 
     const size_t we = (size_t)splits * K * RSk * Cs;
     auto r256 = [](size_t b) { return (b + 255) / 256 * 256; };
     const size_t xb = r256(xe * 4), yb = r256(ye * 4), wb = r256(we * 4);
+    // a kept copy of x from its forward conv (tf32_conv keep_split: the same NHWC hi/lo layout)
+    // replaces the split of x; the space-to-depth form makes its own
+    const bool reuse = given_split != nullptr && !s2d;
+    const size_t xs = reuse ? 0 : 2 * xb;
     uint8_t* scratch = nullptr;
-    OMB_CHECK(cudaMallocAsync(&scratch, 2 * xb + 2 * yb + wb, c->compute));
-    float* xhi = reinterpret_cast<float*>(scratch);
-    float* xlo = reinterpret_cast<float*>(scratch + xb);
-    float* yhi = reinterpret_cast<float*>(scratch + 2 * xb);
-    float* ylo = reinterpret_cast<float*>(scratch + 2 * xb + yb);
-    float* ws = reinterpret_cast<float*>(scratch + 2 * xb + 2 * yb);
+    OMB_CHECK(cudaMallocAsync(&scratch, xs + 2 * yb + wb, c->compute));
+    const float* xhi = reuse ? given_split : reinterpret_cast<float*>(scratch);
+    const float* xlo = reuse ? given_split + xb / 4 : reinterpret_cast<float*>(scratch + xb);
+    float* yhi = reinterpret_cast<float*>(scratch + xs);
+    float* ylo = reinterpret_cast<float*>(scratch + xs + yb);
+    float* ws = reinterpret_cast<float*>(scratch + xs + 2 * yb);
     int st = OM_OK;
-    if (s2d) {
+    if (reuse) {
+        // nothing to prepare for x
+    } else if (s2d) {
         s2d_split_kernel<<<ew_grid(c, (long long)xe, 256), 256, 0, c->compute>>>(
-            x, xhi, xlo, N, Cin, H, W, g.Hs, g.Ws, 2, pad);
+            x, const_cast<float*>(xhi), const_cast<float*>(xlo), N, Cin, H, W, g.Hs, g.Ws, 2,
+            pad);
     } else {
-        launch_split(c, x, xhi, xlo, N, Cin, H, W, H, W, Cs, 0, 0, 1, 0);
+        launch_split(c, x, const_cast<float*>(xhi), const_cast<float*>(xlo), N, Cin, H, W, H, W,
+                     Cs, 0, 0, 1, 0);
     }
-    st = after_launch(c);
+    if (!reuse) st = after_launch(c);
     if (st == OM_OK) {
         launch_split(c, dy, yhi, ylo, N, K, P, Q, P, Q, Ks, 0, 0, 1, 1);
         st = after_launch(c);
@@ -3986,7 +4006,8 @@ int tf32_wgrad(DeviceCtx* c, const float* x, const float* dy, float* dw, int N, 
         cuuint32_t bestr[4] = {1, (cuuint32_t)stk, (cuuint32_t)stk, 1};
         for (int k = 0; k < 2 && st == OM_OK; ++k) {
             CUtensorMap* m = k ? &b_lo : &b_hi;
-            CUresult r = g_encode_im2col(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, k ? xlo : xhi, bd,
+            CUresult r = g_encode_im2col(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4,
+                                         const_cast<float*>(k ? xlo : xhi), bd,
                                          bs, lo_c, hi_c, 32, 32, bestr,
                                          CU_TENSOR_MAP_INTERLEAVE_NONE,
                                          CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B,

@@ -323,10 +323,11 @@ extern "C" int omCudaConv2dBackwardInput(const float* pGradOutput, const float* 
     return run_gemm(c, op, nCin, nBatch * nH * nW, nCout * nKH * nKW, 1);
 }
 
-extern "C" int omCudaConv2dBackwardWeight(const float* pInput, const float* pGradOutput,
-                                          float* pGradWeight, float* pGradBias, int nBatch,
-                                          int nCin, int nH, int nW, int nCout, int nKH, int nKW,
-                                          int nStride, int nPad) {
+// The weight gradient; pInputSplit (optional): the forward's kept tensor-core copy of pInput
+// (omCudaConv2dBatchNorm2dAct), which the tensor path then reads instead of splitting pInput.
+static int conv_wgrad(const float* pInput, const void* pInputSplit, const float* pGradOutput,
+                      float* pGradWeight, float* pGradBias, int nBatch, int nCin, int nH, int nW,
+                      int nCout, int nKH, int nKW, int nStride, int nPad) {
     OMB_CTX_OR_FAIL(c);
     if (!pInput || !pGradOutput || !pGradWeight || nStride <= 0) return OM_ERR_INVALID;
     int P = (nH + 2 * nPad - nKH) / nStride + 1, Q = (nW + 2 * nPad - nKW) / nStride + 1;
@@ -336,7 +337,8 @@ extern "C" int omCudaConv2dBackwardWeight(const float* pInput, const float* pGra
     if (red >= (1LL << 31)) return OM_ERR_UNSUPPORTED;
     // tensor cores (3xTF32) first; the SIMT kernel covers what they do not
     int tst = omb::tc::tf32_wgrad(c, pInput, pGradOutput, pGradWeight, nBatch, nCin, nH, nW, nCout,
-                                  nKH, nKW, nStride, nPad);
+                                  nKH, nKW, nStride, nPad,
+                                  static_cast<const float*>(pInputSplit));
     if (tst != OM_ERR_UNSUPPORTED) {
         if (tst != OM_OK || !pGradBias) return tst;
         bias_grad_nchw_kernel<<<nCout, 256, 0, c->compute>>>(pGradOutput, pGradBias, nBatch, nCout, P * Q);
@@ -373,4 +375,29 @@ extern "C" int omCudaConv2dBackwardWeight(const float* pInput, const float* pGra
         st = after_launch(c);
     }
     return st;
+}
+
+extern "C" int omCudaConv2dBackwardWeight(const float* pInput, const float* pGradOutput,
+                                          float* pGradWeight, float* pGradBias, int nBatch,
+                                          int nCin, int nH, int nW, int nCout, int nKH, int nKW,
+                                          int nStride, int nPad) {
+    return conv_wgrad(pInput, nullptr, pGradOutput, pGradWeight, pGradBias, nBatch, nCin, nH, nW,
+                      nCout, nKH, nKW, nStride, nPad);
+}
+
+extern "C" int omCudaConv2dBackwardWeightSplit(const float* pInput, const void* pInputSplit,
+                                               const float* pGradOutput, float* pGradWeight,
+                                               float* pGradBias, int nBatch, int nCin, int nH,
+                                               int nW, int nCout, int nKH, int nKW, int nStride,
+                                               int nPad) {
+    if (!pInputSplit) return OM_ERR_INVALID;
+    return conv_wgrad(pInput, pInputSplit, pGradOutput, pGradWeight, pGradBias, nBatch, nCin, nH,
+                      nW, nCout, nKH, nKW, nStride, nPad);
+}
+
+extern "C" long long omCudaConvInputSplitBytes(int nBatch, int nCin, int nH, int nW,
+                                               int nStride) {
+    if (nBatch <= 0 || nCin <= 0 || nH <= 0 || nW <= 0 || nStride <= 0) return 0;
+    if (!omb::tc::wgrad_reads_kept_split(nCin, nStride)) return 0;
+    return 2LL * (long long)omb::tc::conv_split_half_bytes(nBatch, nH, nW, nCin);
 }

@@ -762,7 +762,8 @@ extern "C" int omCudaConv2dBatchNorm2dAct(const float* pInput, const float* pWei
                                           float* pRunMean, float* pRunVar, float* pSavedMean,
                                           float* pSavedInvStd, int nBatch, int nCin, int nH,
                                           int nW, int nCout, int nKH, int nKW, int nStride,
-                                          int nPad, float fEps, float fMomentum, int nAct) {
+                                          int nPad, float fEps, float fMomentum, int nAct,
+                                          void* pInputSplit) {
     OMB_CTX_OR_FAIL(c);
     if (!pInput || !pWeight || !pConvOut || !pOutput || !pGamma || !pBeta || !pRunMean ||
         !pRunVar || !pSavedMean || !pSavedInvStd || nBatch <= 0 || nCin <= 0 || nCout <= 0 ||
@@ -776,9 +777,13 @@ extern "C" int omCudaConv2dBatchNorm2dAct(const float* pInput, const float* pWei
     const long long G = (cnt + 31) / 32;
     float* part = nullptr;
     OMB_CHECK(cudaMallocAsync(&part, sizeof(float) * 2 * (size_t)nCout * G, c->compute));
+    // the input's tensor-core copy is kept in pInputSplit for the weight gradient when the
+    // caller gave one (omCudaConvInputSplitBytes says whether the weight gradient reads it)
+    float* keep = static_cast<float*>(pInputSplit);
+    if (keep && !omb::tc::wgrad_reads_kept_split(nCin, nStride)) keep = nullptr;
     int st = omb::tc::tf32_conv(c, pInput, nBatch, nCin, nH, nW, nH, nW, 0, 0, 1, pWeight, nCout,
                                 nKH, nKW, false, nCin, pBias, pConvOut, nStride, nPad, 1, 0, 0,
-                                part);
+                                part, keep);
     if (st == OM_OK) {
         bn_chan_finalize_kernel<<<nCout, 256, 0, c->compute>>>(part, (int)G, cnt, nCout,
                                                                pRunMean, pRunVar, pSavedMean,
@@ -787,10 +792,15 @@ extern "C" int omCudaConv2dBatchNorm2dAct(const float* pInput, const float* pWei
     }
     cudaFreeAsync(part, c->compute);
     if (st == OM_ERR_UNSUPPORTED || st == OM_ERR_OOM) {
-        // the tensor path did not take the shape: the conv and the BatchNorm separately
+        // the tensor path did not take the shape: the conv and the BatchNorm separately, and the
+        // kept copy written on its own
         st = omCudaConv2d(pInput, pWeight, pBias, pConvOut, nBatch, nCin, nH, nW, nCout, nKH, nKW,
                           nStride, nPad);
         if (st != OM_OK) return st;
+        if (keep) {
+            st = omb::tc::tf32_split_input(c, pInput, nBatch, nCin, nH, nW, keep);
+            if (st != OM_OK) return st;
+        }
         return omCudaBatchNorm2dAct(pConvOut, pOutput, pGamma, pBeta, pRunMean, pRunVar,
                                     pSavedMean, pSavedInvStd, nBatch, nCout, P, Q, fEps, fMomentum,
                                     1, nAct);

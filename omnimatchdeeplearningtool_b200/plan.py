@@ -561,12 +561,17 @@ class Fp32Net:
         gamma, beta = self.param[cv.bn + ".gamma"].ptr, self.param[cv.bn + ".beta"].ptr
         rmean = self.buffers[cv.bn + ".running_mean"].ptr
         rvar = self.buffers[cv.bn + ".running_var"].ptr
+        xs = None
         if train and self.fused_bn_stats:
             # batch statistics from the conv's epilogue (omCudaConv2dBatchNorm2dAct): z is
-            # written once and read once
+            # written once and read once; the conv's tensor-core copy of x is kept for the
+            # weight gradient (xs), which then does not make it again
+            nxs = int(lib.omCudaConvInputSplitBytes(n, c, hh, ww, cv.stride))
+            xs = self._buf(key + ".xs", nxs) if nxs > 0 else None
             call("omCudaConv2dBatchNorm2dAct", x.ptr, self.param[cv.name + ".weight"].ptr, None,
                  z.ptr, y.ptr, gamma, beta, rmean, rvar, mean.ptr, invstd.ptr, n, c, hh, ww,
-                 cv.cout, cv.k, cv.k, cv.stride, cv.pad, 1e-5, 0.1, act)
+                 cv.cout, cv.k, cv.k, cv.stride, cv.pad, 1e-5, 0.1, act,
+                 xs.ptr if xs is not None else None)
         else:
             B.conv2d(x.ptr, self.param[cv.name + ".weight"].ptr, None, z.ptr, n, c, hh, ww,
                      cv.cout, cv.k, cv.k, cv.pad, cv.pad, cv.stride, cv.stride)
@@ -574,7 +579,7 @@ class Fp32Net:
                  invstd.ptr, n, cv.cout, p, q, 1e-5, 0.1, int(train), act)
         out = y
         rec = dict(cv=cv, x=x, z=z, y=y, mean=mean, invstd=invstd, relu=relu, n=n, c=c, h=hh,
-                   w=ww, p=p, q=q)
+                   w=ww, p=p, q=q, xs=xs)
         return out, p, q, rec
 
     def forward_eval(self, x_ptr: int) -> np.ndarray:
@@ -702,9 +707,15 @@ class Fp32Net:
             B.conv2dBackwardInput(dz.ptr, self.param[cv.name + ".weight"].ptr, dx.ptr, n, rec["c"],
                                   rec["h"], rec["w"], cv.cout, cv.k, cv.k, cv.pad, cv.pad, cv.stride,
                                   cv.stride)
-        B.conv2dBackwardWeight(rec["x"].ptr, dz.ptr, self.grad(cv.name + ".weight"), None, n,
-                               rec["c"], rec["h"], rec["w"], cv.cout, cv.k, cv.k, cv.pad, cv.pad,
-                               cv.stride, cv.stride)
+        if rec.get("xs") is not None:
+            # the forward kept the tensor-core copy of x
+            call("omCudaConv2dBackwardWeightSplit", rec["x"].ptr, rec["xs"].ptr, dz.ptr,
+                 self.grad(cv.name + ".weight"), None, n, rec["c"], rec["h"], rec["w"], cv.cout,
+                 cv.k, cv.k, cv.stride, cv.pad)
+        else:
+            B.conv2dBackwardWeight(rec["x"].ptr, dz.ptr, self.grad(cv.name + ".weight"), None,
+                                   n, rec["c"], rec["h"], rec["w"], cv.cout, cv.k, cv.k, cv.pad,
+                                   cv.pad, cv.stride, cv.stride)
         self._grad_done(cv.name + ".weight")
         return dx
 

@@ -203,7 +203,9 @@ def test_conv_batchnorm_stats_in_epilogue(gpu, n, c, h, k, r, stride, pad, act):
     """omCudaConv2dBatchNorm2dAct (BatchNorm statistics from the conv epilogue, combined in a
     fixed order) against omCudaConv2d + omCudaBatchNorm2dAct (two-pass statistics): the conv
     output bit-identical, everything else within the fp32 tolerance; and against the oracle's
-    train-mode BatchNorm of the oracle's conv."""
+    train-mode BatchNorm of the oracle's conv. The input copy it keeps (pInputSplit) gives
+    omCudaConv2dBackwardWeightSplit the bits of omCudaConv2dBackwardWeight."""
+    from omnimatchdeeplearningtool_b200._lib import lib
     import oracle as orc
     from omnimatchdeeplearningtool_b200._lib import call
     rng = _rng(500 + c + k)
@@ -216,12 +218,15 @@ def test_conv_batchnorm_stats_in_epilogue(gpu, n, c, h, k, r, stride, pad, act):
     p = (h + 2 * pad - r) // stride + 1
     dx, dw, dg, db = _dev(x), _dev(w), _dev(g), _dev(b)
     res = []
+    nxs = int(lib.omCudaConvInputSplitBytes(n, c, h, h, stride))
+    xs = _out((max(nxs, 4) // 4,)) if nxs > 0 else None
     for fused in (True, False):
         z, y, sm, si = _out((n, k, p, p)), _out((n, k, p, p)), _out((k,)), _out((k,))
         drm, drv = _dev(rm), _dev(rv)
         if fused:
             call("omCudaConv2dBatchNorm2dAct", dx.ptr, dw.ptr, None, z.ptr, y.ptr, dg.ptr, db.ptr,
-                 drm.ptr, drv.ptr, sm.ptr, si.ptr, n, c, h, h, k, r, r, stride, pad, 1e-5, 0.1, act)
+                 drm.ptr, drv.ptr, sm.ptr, si.ptr, n, c, h, h, k, r, r, stride, pad, 1e-5, 0.1, act,
+                 xs.ptr if xs is not None else None)
         else:
             call("omCudaConv2d", dx.ptr, dw.ptr, None, z.ptr, n, c, h, h, k, r, r, stride, pad)
             call("omCudaBatchNorm2dAct", z.ptr, y.ptr, dg.ptr, db.ptr, drm.ptr, drv.ptr, sm.ptr,
@@ -245,6 +250,16 @@ def test_conv_batchnorm_stats_in_epilogue(gpu, n, c, h, k, r, stride, pad, act):
     assert rel_err_floor(fsi, wsi) <= TOL
     assert rel_err_floor(frm, wrm) <= TOL
     assert rel_err_floor(frv, wrv) <= TOL
+    # the weight gradient from the kept input copy
+    assert (nxs > 0) == (not (stride == 2 and c * 4 <= 32))
+    if xs is not None:
+        ddy = _dev(rng.standard_normal((n, k, p, p), dtype=np.float32))
+        g1, g2 = _out(w.shape), _out(w.shape)
+        call("omCudaConv2dBackwardWeight", dx.ptr, ddy.ptr, g1.ptr, None, n, c, h, h, k, r, r,
+             stride, pad)
+        call("omCudaConv2dBackwardWeightSplit", dx.ptr, xs.ptr, ddy.ptr, g2.ptr, None, n, c, h, h,
+             k, r, r, stride, pad)
+        assert np.array_equal(g1.to_numpy(w.shape), g2.to_numpy(w.shape))
     assert gpu.kernel_error() == 0
 
 
