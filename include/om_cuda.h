@@ -239,6 +239,14 @@ int omCudaMaxPool2d(const float* pIn, float* pOut, int* pIndices, int nN, int nC
 /* accumulates into pGradIn (callers zero it first, as CUDABackend::maxPool2dBackward does) */
 int omCudaMaxPool2dBackward(const float* pGradOut, const int* pIndices, float* pGradIn, int nN,
                             int nC, int nH, int nW, int nHout, int nWout);       /* replaces :2083 */
+/* new: the max-pool backward with the window geometry (as omCudaMaxPool2d), as a gather: each
+ * element of pGradIn is written (not accumulated; no zeroing needed) with the sum of the output
+ * gradients whose argmax picked it, added in increasing output order. That is the reference CPU
+ * backend's loop (cpu_backend.ixx:937-953) sum for sum: deterministic, unlike the scatter with
+ * atomics of omCudaMaxPool2dBackward where windows overlap. */
+int omCudaMaxPool2dBackwardGather(const float* pGradOut, const int* pIndices, float* pGradIn,
+                                  int nN, int nC, int nH, int nW, int nKH, int nKW, int nSH,
+                                  int nSW, int nPH, int nPW);
 int omCudaAvgPool2d(const float* pIn, float* pOut, int nN, int nC, int nH, int nW, int nKH,
                     int nKW, int nSH, int nSW, int nPH, int nPW);                /* replaces :2127 */
 /* accumulates into pGradIn (callers zero it first) */

@@ -262,6 +262,35 @@ __global__ void maxpool_bwd_kernel(const float* __restrict__ dy, const int* __re
     }
 }
 
+// Max-pool backward as a gather: each input element adds the gradients of the output windows
+// that picked it (argmax index == its flat index), in increasing output order, from 0. These
+// are the sums of the reference CPU backend's sequential scatter loop (cpu_backend.ixx:937-953)
+// in its order, so the result is deterministic and the same bits; no atomics, no zeroing.
+__global__ void maxpool_bwd_gather_kernel(const float* __restrict__ dy, const int* __restrict__ idx,
+                                          float* __restrict__ dx, int N, int C, int H, int W,
+                                          int kh, int kw, int sh, int sw, int ph, int pw, int P,
+                                          int Q) {
+    const long long total = (long long)N * C * H * W;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int w = (int)(i % W);
+        const long long t = i / W;
+        const int h = (int)(t % H);
+        const long long nc = t / H;
+        // windows p with p*sh - ph <= h <= p*sh - ph + kh - 1, likewise q
+        const int a = h + ph - kh + 1, b = w + pw - kw + 1;
+        const int p0 = a <= 0 ? 0 : (a + sh - 1) / sh, p1 = min(P - 1, (h + ph) / sh);
+        const int q0 = b <= 0 ? 0 : (b + sw - 1) / sw, q1 = min(Q - 1, (w + pw) / sw);
+        float acc = 0.f;
+        for (int p = p0; p <= p1; ++p)
+            for (int q = q0; q <= q1; ++q) {
+                const long long o = (nc * P + p) * Q + q;
+                if (idx[o] == (int)i) acc += dy[o];
+            }
+        dx[i] = acc;
+    }
+}
+
 __global__ void avgpool_kernel(const float* __restrict__ in, float* __restrict__ out, int N, int C,
                                int H, int W, int kh, int kw, int sh, int sw, int ph, int pw, int P,
                                int Q) {
@@ -844,6 +873,22 @@ extern "C" int omCudaMaxPool2dBackward(const float* pGradOut, const int* pIndice
     if (!pGradOut || !pIndices || !pGradIn) return OM_ERR_INVALID;
     long long n = (long long)nN * nC * nHout * nWout;
     maxpool_bwd_kernel<<<OMB_EW(n)>>>(pGradOut, pIndices, pGradIn, n);
+    return after_launch(c);
+}
+
+extern "C" int omCudaMaxPool2dBackwardGather(const float* pGradOut, const int* pIndices,
+                                             float* pGradIn, int nN, int nC, int nH, int nW,
+                                             int nKH, int nKW, int nSH, int nSW, int nPH,
+                                             int nPW) {
+    OMB_CTX_OR_FAIL(c);
+    if (!pGradOut || !pIndices || !pGradIn || nSH <= 0 || nSW <= 0 || nKH <= 0 || nKW <= 0)
+        return OM_ERR_INVALID;
+    const int P = (nH + 2 * nPH - nKH) / nSH + 1, Q = (nW + 2 * nPW - nKW) / nSW + 1;
+    if (P <= 0 || Q <= 0) return OM_ERR_INVALID;
+    const long long total = (long long)nN * nC * nH * nW;
+    if (total >= (1LL << 31)) return OM_ERR_UNSUPPORTED;   // int32 indices
+    maxpool_bwd_gather_kernel<<<OMB_EW(total)>>>(pGradOut, pIndices, pGradIn, nN, nC, nH, nW, nKH,
+                                                 nKW, nSH, nSW, nPH, nPW, P, Q);
     return after_launch(c);
 }
 

@@ -515,6 +515,7 @@ class Fp32Net:
         # called with a parameter's name once the backward pass has issued the last kernel
         # that writes its gradient (a data-parallel wrapper starts bucket all-reduces from it)
         self.grad_hook: Optional[Callable[[str], None]] = None
+        self._step_graph: Optional[int] = None   # capture_step's graph
 
     def _grad_done(self, *names: str) -> None:
         if self.grad_hook is not None:
@@ -687,7 +688,10 @@ class Fp32Net:
             B.add(d.ptr, dsc.ptr, dsum.ptr, incnt)
             dcur = dsum
         dpool = self._buf("g.pool", n * pc * ph * pw * 4)
-        B.maxPool2dBackward(dcur.ptr, idx.ptr, dpool.ptr, n, pc, ph, pw, P, P)
+        # gather form: deterministic, the CPU backend's sums in its order (the reference's GPU
+        # path scatters with atomics)
+        call("omCudaMaxPool2dBackwardGather", dcur.ptr, idx.ptr, dpool.ptr, n, pc, ph, pw, 3, 3,
+             2, 2, 1, 1)
         d = dpool
         for i in reversed(range(len(recs))):
             d = self._conv_bn_backward(f"g.stem{i}", recs[i], d, need_dx=i > 0)
@@ -764,7 +768,39 @@ class Fp32Net:
         call("omCudaCopyD2H", out.ctypes.data, self.param_flat.ptr + off * 4, n * 4)
         return out.reshape(shape)
 
+    def capture_step(self, x_ptr: int, onehot_ptr: int, loss_ptr: int, lr: float = 0.01,
+                     momentum: float = 0.9) -> None:
+        """Capture one whole training step (forward_backward on these device buffers, then the
+        SGD step) as a CUDA graph; :meth:`replay_step` launches it. One rank only: a gradient
+        hook (a data-parallel wrapper's bucket all-reduces) must not be set. Run one eager step
+        first, so that every activation buffer exists; the graph reads and writes the same
+        buffers, and the results are bit-identical to eager steps."""
+        if self.grad_hook is not None:
+            raise ValueError("capture_step: a gradient hook (collectives) is set")
+        if self._step_graph is not None:
+            call("omCudaGraphDestroy", self._step_graph)
+            self._step_graph = None
+        call("omCudaSynchronize")
+        call("omCudaGraphBeginCapture")
+        try:
+            self.forward_backward(x_ptr, onehot_ptr, loss_ptr)
+            self.step(lr, momentum)
+        finally:
+            g = ctypes.c_void_p()
+            st = lib.omCudaGraphEndCapture(ctypes.byref(g))
+        _lib.check(st, "omCudaGraphEndCapture")
+        self._step_graph = g.value
+
+    def replay_step(self) -> None:
+        """Launch the captured training step (asynchronous, on the library's stream)."""
+        if self._step_graph is None:
+            raise RuntimeError("replay_step: no captured step")
+        call("omCudaGraphLaunch", self._step_graph)
+
     def close(self) -> None:
+        if self._step_graph is not None:
+            call("omCudaGraphDestroy", self._step_graph)
+            self._step_graph = None
         for b in self.keep:
             b.free()
         self.keep.clear()

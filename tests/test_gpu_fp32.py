@@ -321,6 +321,12 @@ def test_pooling(gpu):
     wdx = np.empty_like(x)
     orc.O.oracle_maxpool2d_backward(dy.ctypes.data, widx.ctypes.data, wdx.ctypes.data, n, c, P, P, h, h)
     assert rel_err_floor(dx.to_numpy(x.shape), wdx) <= TOL
+    # the gather form: the oracle's sums in the oracle's order, bit for bit
+    from omnimatchdeeplearningtool_b200._lib import call
+    gdx = _out(x.shape)
+    call("omCudaMaxPool2dBackwardGather", _dev(dy).ptr, idx.ptr, gdx.ptr, n, c, h, h, 3, 3, 2, 2,
+         1, 1)
+    assert np.array_equal(gdx.to_numpy(x.shape), wdx)
     # average pool 3/2/1 and its backward
     ay = _out((n, c, P, P))
     B.avgPool2d(dX.ptr, ay.ptr, n, c, h, h, 3, 3, 2, 1)

@@ -135,3 +135,49 @@ def test_guarded_step_clips_like_the_training_loop(gpu):
     assert rel_err(fnet.read_param("fc.weight") - w0, -0.01 * 0.5 * g_fc) < 1e-5
     fnet.close()
     assert gpu.kernel_error() == 0
+
+
+@pytest.mark.parametrize("fused_bn_stats", [False, True])
+def test_captured_training_step_matches_eager(gpu, fused_bn_stats):
+    """Fp32Net.capture_step / replay_step: the whole training step (forward, backward, SGD with
+    momentum) as one CUDA graph. After one eager step on both, two replays on one net and two
+    eager steps on the other give bit-identical loss, parameters, velocities and BatchNorm
+    running statistics."""
+    from omnimatchdeeplearningtool_b200 import synth
+    from omnimatchdeeplearningtool_b200._lib import call
+    from omnimatchdeeplearningtool_b200.backend import DeviceBuffer
+    from omnimatchdeeplearningtool_b200.plan import Fp32Net
+    net = synth.resnet_spec(18, 10)
+    w = synth.make_weights(net)
+    x = DeviceBuffer.from_numpy(synth.normal_input(4, 3, 64, 64, seed=31))
+    y = DeviceBuffer.from_numpy(synth.onehot_labels(4, 10, seed=32))
+    out = []
+    for graph in (False, True):
+        fnet = Fp32Net(net, w, 4, 64, 64, fused_bn_stats=fused_bn_stats)
+        loss = DeviceBuffer.zeros(4)
+        try:
+            fnet.forward_backward(x.ptr, y.ptr, loss.ptr)
+            fnet.step(0.01, 0.9)
+            if graph:
+                fnet.capture_step(x.ptr, y.ptr, loss.ptr, 0.01, 0.9)
+                fnet.replay_step()
+                fnet.replay_step()
+            else:
+                for _ in range(2):
+                    fnet.forward_backward(x.ptr, y.ptr, loss.ptr)
+                    fnet.step(0.01, 0.9)
+            call("omCudaSynchronize")
+            vel = np.empty(fnet.n_params, np.float32)
+            call("omCudaCopyD2H", vel.ctypes.data, fnet.vel_flat.ptr, vel.nbytes)
+            bufs = {k: b.to_numpy((b.nbytes // 4,)) for k, b in fnet.buffers.items()}
+            out.append((loss.to_numpy((1,)), {n: fnet.read_param(n) for n, _ in net.params},
+                        vel, bufs))
+        finally:
+            fnet.close()
+            loss.free()
+    (l0, p0, v0, b0), (l1, p1, v1, b1) = out
+    assert np.array_equal(l0, l1)
+    assert all(np.array_equal(p0[k], p1[k]) for k in p0)
+    assert np.array_equal(v0, v1)
+    assert all(np.array_equal(b0[k], b1[k]) for k in b0)
+    assert gpu.kernel_error() == 0
