@@ -3872,6 +3872,197 @@ __global__ void __launch_bounds__(192, 1)
     }
 }
 
+// Weight gradient for at most 64 output channels, with the operands' roles swapped: M = the
+// tile's 128 (tap, input channel) columns, N = the NY output channels (32 or 64). The plain
+// kernel above puts the output channels on M, where 64 of them would leave half of every
+// 128-row MMA on zero rows (and half of every dY box empty). Same operand boxes, same 3xTF32
+// terms, same partial layout; the epilogue reads one (tap, channel) per TMEM lane and writes the
+// NY output channels of it.
+template <int NY>
+struct WgSwapCfg {
+    static constexpr int Y_BOX = NY * 32 * 4;        // NY output channels x 32 pixels
+    static constexpr int X_BOX = 128 * 32 * 4;       // the tile's 128 columns x 32 pixels
+    static constexpr int STAGE = 2 * Y_BOX + 2 * X_BOX;
+    static constexpr int RAW = (MAX_DYN_SMEM - 2048) / STAGE;
+    static constexpr int STAGES = RAW > 6 ? 6 : RAW;
+    static constexpr int SMEM = STAGES * STAGE + 2048;
+    static constexpr uint32_t TMEM = 2 * NY;         // main + correction accumulators
+};
+
+template <int NY>
+__global__ void __launch_bounds__(192, 1)
+    wgrad_tf32_swap_kernel(const __grid_constant__ CUtensorMap tmY_hi,
+                           const __grid_constant__ CUtensorMap tmY_lo,
+                           const __grid_constant__ CUtensorMap tmX_hi,
+                           const __grid_constant__ CUtensorMap tmX_lo, const WgradParams p) {
+    using C = WgSwapCfg<NY>;
+    constexpr int STAGES = C::STAGES;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE);
+    uint64_t* empty = full + STAGES;
+    uint64_t* done = empty + STAGES;
+    uint64_t* drain = done + 1;
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    const int RS = p.R * p.S;
+    const int group = blockIdx.x / p.cb, cslice = blockIdx.x - group * p.cb;
+    const int bpt = p.csl / 32;              // 32-channel boxes per tap
+    const int z = blockIdx.z;
+    const int kb0 = (int)((long long)z * p.num_kb / p.splits);
+    const int kb1 = (int)((long long)(z + 1) * p.num_kb / p.splits);
+    const int PQ = p.P * p.Q;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < STAGES; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 1);
+        }
+        mbar_init(done, 1);
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        fence_async_smem();
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(tmem_holder)),
+                     "r"(C::TMEM));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_holder;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ------------------------------------------------------------ TMA producer
+            bool ok = true;
+            int n = 0;
+            for (int kb = kb0; kb < kb1; ++kb, ++n) {
+                const int st = n % STAGES;
+                if (!mbar_wait(&empty[st], (uint32_t)(((n / STAGES) & 1) ^ 1), abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                uint8_t* sy = smem + st * C::STAGE;
+                uint8_t* sx = sy + 2 * C::Y_BOX;
+                const int j0 = kb * 32;
+                const int img = j0 / PQ, rem = j0 - img * PQ;
+                const int pp = rem / p.Q, qq = rem - pp * p.Q;
+                const int wb = qq * p.stride - p.pad, hb = pp * p.stride - p.pad;
+                mbar_expect_tx(&full[st], (uint32_t)C::STAGE);
+                tma_load_3d(sy, &tmY_hi, &full[st], 0, j0, 0);
+                tma_load_3d(sy + C::Y_BOX, &tmY_lo, &full[st], 0, j0, 0);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    // box i: tap group * tpt + i / bpt (a tap past the last one reloads the
+                    // last; its rows are never stored), channels from (i % bpt) * 32
+                    const int ti = i / bpt;
+                    int tap = group * p.tpt + ti;
+                    if (tap >= RS) tap = RS - 1;
+                    const int fr = tap / p.S, fs = tap - fr * p.S;
+                    const int c0 = cslice * p.csl + (i - ti * bpt) * 32;
+                    tma_load_im2col(sx + i * 4096, &tmX_hi, &full[st], c0, wb, hb, img,
+                                    (uint16_t)fs, (uint16_t)fr);
+                    tma_load_im2col(sx + C::X_BOX + i * 4096, &tmX_lo, &full[st], c0, wb, hb, img,
+                                    (uint16_t)fs, (uint16_t)fr);
+                }
+            }
+            if (!ok) {
+                atomicOr(p.err, ERRBIT_TC_PRODUCER);
+                *abort_flag = 1;
+            }
+            // no TMA write may land after the CTA exits
+            for (int j = n - STAGES; j < n; ++j) {
+                if (j < 0) continue;
+                if (!mbar_wait_drain(&full[j % STAGES], (uint32_t)((j / STAGES) & 1))) {
+                    atomicOr(p.err, ERRBIT_TC_DRAIN);
+                    break;
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ------------------------------------------------------------ MMA issuer
+            // kind::tf32, M = 128 (tap, channel), N = NY output channels, both MN-major
+            constexpr uint32_t IDESC = instr_desc_tf32<NY>() | (1u << 15) | (1u << 16);
+            const uint64_t xdesc0 =
+                smem_desc(smem_u32(smem + 2 * C::Y_BOX), 4096, 512, LAYOUT_SW128_BASE32B);
+            const uint64_t ydesc0 = smem_desc(smem_u32(smem), 4096, 512, LAYOUT_SW128_BASE32B);
+            bool ok = true;
+            int n = 0;
+            for (int kb = kb0; kb < kb1; ++kb, ++n) {
+                const int st = n % STAGES;
+                if (!mbar_wait(&full[st], (uint32_t)((n / STAGES) & 1), abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint64_t so = (uint64_t)((st * C::STAGE) >> 4);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    // K step k = pixels 8k .. 8k+7 = rows 8k.. of every box: +1024 B
+                    const uint64_t xh = xdesc0 + so + (uint64_t)(k * 64);
+                    const uint64_t yh = ydesc0 + so + (uint64_t)(k * 64);
+                    const uint32_t acc_in = (n > 0 || k > 0) ? 1u : 0u;
+                    tc_mma_tf32(tmem_base + NY, xh + (C::X_BOX >> 4), yh, IDESC, acc_in);
+                    tc_mma_tf32(tmem_base + NY, xh, yh + (C::Y_BOX >> 4), IDESC, 1u);
+                    tc_mma_tf32(tmem_base, xh, yh, IDESC, acc_in);
+                }
+                tc_commit(&empty[st]);
+            }
+            if (!ok) {
+                atomicOr(p.err, ERRBIT_TC_MMA);
+                *abort_flag = 1;
+            }
+            tc_commit(done);
+            tc_commit(drain);
+            if (!mbar_wait_drain(drain, 0)) atomicOr(p.err, ERRBIT_TC_DRAIN);
+        }
+    } else {
+        // ---------------------------------------------------------------- epilogue
+        // lane quarter q = X box q: one tap and 32 input channels; lane = the channel
+        const int quarter = warp & 3;
+        const bool ok = __all_sync(0xffffffffu, mbar_wait(done, 0, abort_flag));
+        if (ok) {
+            tc_fence_after();
+            const int ti = quarter / bpt;
+            const int tap = group * p.tpt + ti;
+            const int ch = cslice * p.csl + (quarter - ti * bpt) * 32 + lane;
+            const uint32_t t = tmem_base + ((uint32_t)(quarter * 32) << 16);
+#pragma unroll 1
+            for (int c = 0; c < NY / 32; ++c) {
+                uint32_t v[32], vc[32];
+                tmem_ld32(t + (uint32_t)(c * 32), v);
+                tmem_ld32(t + (uint32_t)(NY + c * 32), vc);
+                if (tap < RS) {
+                    float* d = p.ws + ((size_t)z * p.K + c * 32) * RS * p.Cs + (size_t)tap * p.Cs + ch;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        if (c * 32 + j < p.K)
+                            d[(size_t)j * RS * p.Cs] =
+                                __uint_as_float(v[j]) + __uint_as_float(vc[j]);
+                }
+            }
+        } else if (lane == 0) {
+            atomicOr(p.err, ERRBIT_TC_EPILOGUE);
+            *abort_flag = 1;
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) {
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                     "r"(C::TMEM));
+    }
+}
+
 // dW[k, c, r, s] = sum over splits (in order) of the partial at (k, tap, ch): for a plain
 // convolution tap = r*S + s and ch = c; for the space-to-depth form (f = 2) tap =
 // (r/2)*tw + s/2 and ch = (c*2 + r%2)*2 + s%2 over the th x tw filter.
@@ -3916,6 +4107,21 @@ static int launch_wgrad(DeviceCtx* c, const CUtensorMap& a_hi, const CUtensorMap
     return after_launch(c);
 }
 
+template <int NY>
+static int launch_wgrad_swap(DeviceCtx* c, const CUtensorMap& y_hi, const CUtensorMap& y_lo,
+                             const CUtensorMap& x_hi, const CUtensorMap& x_lo,
+                             const WgradParams& p, dim3 grid) {
+    using Cf = WgSwapCfg<NY>;
+    auto kern = wgrad_tf32_swap_kernel<NY>;
+    static bool attr_set[64] = {false};
+    if (!attr_set[c->device]) {
+        OMB_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM));
+        attr_set[c->device] = true;
+    }
+    kern<<<grid, 192, Cf::SMEM, c->compute>>>(y_hi, y_lo, x_hi, x_lo, p);
+    return after_launch(c);
+}
+
 // The fp32 weight gradient of a (stride, pad) convolution, NCHW in and out, 3xTF32 on the
 // tensor cores. A stride-2 convolution with Cin * 4 <= 32 (the image stem) runs in its
 // space-to-depth form: 32-channel copy of X, th x tw taps, stride 1 (a quarter of the taps and
@@ -3945,7 +4151,10 @@ int tf32_wgrad(DeviceCtx* c, const float* x, const float* dy, float* dw, int N, 
     const int num_kb = (int)((NPQ + 31) / 32);
     const int m_tiles = (K + 127) / 128;
     const long long tiles = (long long)((RSk + tpt - 1) / tpt) * cb * m_tiles;
-    long long want = (2LL * c->num_sms + tiles - 1) / tiles;
+    // one CTA fits per SM (shared memory), so the CTAs run in waves of num_sms: at most two
+    // full waves (rounding the split count up once made 300 CTAs, three waves, the last with
+    // four CTAs, for a 5-tile layer)
+    long long want = (2LL * c->num_sms) / tiles;
     long long cap = num_kb < 256 ? num_kb : 256;
     const int splits = (int)(want < 1 ? 1 : (want > cap ? cap : want));
     if (tiles * splits >= (1LL << 31)) return OM_ERR_UNSUPPORTED;
@@ -3983,10 +4192,11 @@ int tf32_wgrad(DeviceCtx* c, const float* x, const float* dy, float* dw, int N, 
     }
     CUtensorMap a_hi, a_lo, b_hi, b_lo;
     if (st == OM_OK) {
-        // A: blocked dY as (32, NPQ, Ks/32), box (32, 32, 4)
+        // A: blocked dY as (32, NPQ, Ks/32), box (32, 32, 4); with at most 64 output channels
+        // the swapped kernel takes all Ks/32 blocks as its N operand
         cuuint64_t dims[3] = {32, (cuuint64_t)NPQ, (cuuint64_t)(Ks / 32)};
         cuuint64_t strides[2] = {128, (cuuint64_t)NPQ * 128};
-        cuuint32_t box[3] = {32, 32, 4};
+        cuuint32_t box[3] = {32, 32, Ks <= 64 ? (cuuint32_t)(Ks / 32) : 4u};
         cuuint32_t estr[3] = {1, 1, 1};
         for (int k = 0; k < 2 && st == OM_OK; ++k) {
             CUresult r = g_encode_tiled(k ? &a_lo : &a_hi, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3,
@@ -4025,7 +4235,12 @@ int tf32_wgrad(DeviceCtx* c, const float* x, const float* dy, float* dw, int N, 
         p.splits = splits; p.ws = ws;
         p.err = c->err_word;
         dim3 grid((unsigned)(((RSk + tpt - 1) / tpt) * cb), (unsigned)m_tiles, (unsigned)splits);
-        st = launch_wgrad(c, a_hi, a_lo, b_hi, b_lo, p, grid);
+        if (Ks == 64)
+            st = launch_wgrad_swap<64>(c, a_hi, a_lo, b_hi, b_lo, p, grid);
+        else if (Ks == 32)
+            st = launch_wgrad_swap<32>(c, a_hi, a_lo, b_hi, b_lo, p, grid);
+        else
+            st = launch_wgrad(c, a_hi, a_lo, b_hi, b_lo, p, grid);
     }
     if (st == OM_OK) {
         const long long total = (long long)K * Cin * R * S;
