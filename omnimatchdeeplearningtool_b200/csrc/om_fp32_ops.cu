@@ -270,22 +270,26 @@ __global__ void maxpool_bwd_gather_kernel(const float* __restrict__ dy, const in
                                           float* __restrict__ dx, int N, int C, int H, int W,
                                           int kh, int kw, int sh, int sw, int ph, int pw, int P,
                                           int Q) {
-    const long long total = (long long)N * C * H * W;
-    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
-         i += (long long)gridDim.x * blockDim.x) {
-        const int w = (int)(i % W);
-        const long long t = i / W;
-        const int h = (int)(t % H);
-        const long long nc = t / H;
+    // 32-bit indices (the caller checks N*C*H*W < 2^31): consecutive threads take consecutive
+    // w of a row, so their candidate windows' index and gradient reads are close together
+    const int total = N * C * H * W;
+    const int HW = H * W;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+        const int nc = i / HW;
+        const int hw = i - nc * HW;
+        const int h = hw / W;
+        const int w = hw - h * W;
         // windows p with p*sh - ph <= h <= p*sh - ph + kh - 1, likewise q
         const int a = h + ph - kh + 1, b = w + pw - kw + 1;
         const int p0 = a <= 0 ? 0 : (a + sh - 1) / sh, p1 = min(P - 1, (h + ph) / sh);
         const int q0 = b <= 0 ? 0 : (b + sw - 1) / sw, q1 = min(Q - 1, (w + pw) / sw);
+        const int* ip = idx + nc * P * Q;
+        const float* gp = dy + nc * P * Q;
         float acc = 0.f;
         for (int p = p0; p <= p1; ++p)
             for (int q = q0; q <= q1; ++q) {
-                const long long o = (nc * P + p) * Q + q;
-                if (idx[o] == (int)i) acc += dy[o];
+                const int o = p * Q + q;
+                if (__ldg(ip + o) == i) acc += __ldg(gp + o);
             }
         dx[i] = acc;
     }
