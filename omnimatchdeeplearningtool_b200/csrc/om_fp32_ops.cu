@@ -267,18 +267,16 @@ __global__ void maxpool_bwd_kernel(const float* __restrict__ dy, const int* __re
 // are the sums of the reference CPU backend's sequential scatter loop (cpu_backend.ixx:937-953)
 // in its order, so the result is deterministic and the same bits; no atomics, no zeroing.
 __global__ void maxpool_bwd_gather_kernel(const float* __restrict__ dy, const int* __restrict__ idx,
-                                          float* __restrict__ dx, int N, int C, int H, int W,
-                                          int kh, int kw, int sh, int sw, int ph, int pw, int P,
-                                          int Q) {
+                                          float* __restrict__ dx, int total, FastDiv fhw,
+                                          FastDiv fw, int kh, int kw, int sh, int sw, int ph,
+                                          int pw, int P, int Q) {
     // 32-bit indices (the caller checks N*C*H*W < 2^31): consecutive threads take consecutive
     // w of a row, so their candidate windows' index and gradient reads are close together
-    const int total = N * C * H * W;
-    const int HW = H * W;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
-        const int nc = i / HW;
-        const int hw = i - nc * HW;
-        const int h = hw / W;
-        const int w = hw - h * W;
+        const int nc = (int)fdiv((uint32_t)i, fhw);
+        const int hw = i - nc * (int)fhw.d;
+        const int h = (int)fdiv((uint32_t)hw, fw);
+        const int w = hw - h * (int)fw.d;
         // windows p with p*sh - ph <= h <= p*sh - ph + kh - 1, likewise q
         const int a = h + ph - kh + 1, b = w + pw - kw + 1;
         const int p0 = a <= 0 ? 0 : (a + sh - 1) / sh, p1 = min(P - 1, (h + ph) / sh);
@@ -292,6 +290,52 @@ __global__ void maxpool_bwd_gather_kernel(const float* __restrict__ dy, const in
                 if (__ldg(ip + o) == i) acc += __ldg(gp + o);
             }
         dx[i] = acc;
+    }
+}
+
+// The 3x3 / stride 2 / padding 1 pool (the ResNet stem's): a thread takes the 2x2 input block
+// (2r.., 2s..). Every pixel of it lies in window (r, s); the odd row also in (r + 1, s), the
+// odd column also in (r, s + 1), the odd corner in all four. The four windows' argmax indices
+// and gradients are read once, and each pixel adds its matches in output order (r, s),
+// (r, s + 1), (r + 1, s), (r + 1, s + 1), as the generic kernel and the CPU loop do.
+__global__ void maxpool_bwd_gather_3s2_kernel(const float* __restrict__ dy,
+                                              const int* __restrict__ idx, float* __restrict__ dx,
+                                              int blocks, FastDiv frs, FastDiv fs2, int H, int W,
+                                              int P, int Q) {
+    for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < blocks; t += gridDim.x * blockDim.x) {
+        const int nc = (int)fdiv((uint32_t)t, frs);
+        const int rem = t - nc * (int)frs.d;
+        const int r = (int)fdiv((uint32_t)rem, fs2);
+        const int s = rem - r * (int)fs2.d;
+        const int base_o = nc * P * Q;
+        int iv[4] = {-1, -1, -1, -1};
+        float gv[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int p = r + (k >> 1), q = s + (k & 1);
+            if (p < P && q < Q) {
+                iv[k] = __ldg(idx + base_o + p * Q + q);
+                gv[k] = __ldg(dy + base_o + p * Q + q);
+            }
+        }
+        const int base_i = nc * H * W;
+#pragma unroll
+        for (int dh = 0; dh < 2; ++dh) {
+            const int h = 2 * r + dh;
+            if (h >= H) continue;
+#pragma unroll
+            for (int dw = 0; dw < 2; ++dw) {
+                const int w = 2 * s + dw;
+                if (w >= W) continue;
+                const int pix = base_i + h * W + w;
+                float acc = 0.f;
+                if (iv[0] == pix) acc += gv[0];
+                if (dw && iv[1] == pix) acc += gv[1];
+                if (dh && iv[2] == pix) acc += gv[2];
+                if (dh && dw && iv[3] == pix) acc += gv[3];
+                dx[pix] = acc;
+            }
+        }
     }
 }
 
@@ -891,8 +935,16 @@ extern "C" int omCudaMaxPool2dBackwardGather(const float* pGradOut, const int* p
     if (P <= 0 || Q <= 0) return OM_ERR_INVALID;
     const long long total = (long long)nN * nC * nH * nW;
     if (total >= (1LL << 31)) return OM_ERR_UNSUPPORTED;   // int32 indices
-    maxpool_bwd_gather_kernel<<<OMB_EW(total)>>>(pGradOut, pIndices, pGradIn, nN, nC, nH, nW, nKH,
-                                                 nKW, nSH, nSW, nPH, nPW, P, Q);
+    const FastDiv fhw = make_fastdiv((uint32_t)(nH * nW)), fw = make_fastdiv((uint32_t)nW);
+    if (nKH == 3 && nKW == 3 && nSH == 2 && nSW == 2 && nPH == 1 && nPW == 1) {
+        const int R2 = (nH + 1) / 2, S2 = (nW + 1) / 2;
+        const long long blocks = (long long)nN * nC * R2 * S2;
+        maxpool_bwd_gather_3s2_kernel<<<OMB_EW(blocks)>>>(
+            pGradOut, pIndices, pGradIn, (int)blocks, make_fastdiv((uint32_t)(R2 * S2)),
+            make_fastdiv((uint32_t)S2), nH, nW, P, Q);
+    } else
+        maxpool_bwd_gather_kernel<<<OMB_EW(total)>>>(
+            pGradOut, pIndices, pGradIn, (int)total, fhw, fw, nKH, nKW, nSH, nSW, nPH, nPW, P, Q);
     return after_launch(c);
 }
 

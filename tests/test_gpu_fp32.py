@@ -301,6 +301,33 @@ def test_batchnorm_relu_fused_matches_separate(gpu, shape):
         assert np.array_equal(a, b_)
 
 
+@pytest.mark.parametrize("n,c,h,k,st,pad", [(2, 8, 17, 3, 2, 1), (2, 4, 16, 3, 2, 1),
+                                          (1, 6, 9, 3, 1, 1), (2, 3, 10, 2, 2, 0)])
+def test_maxpool_backward_gather_bit_exact(gpu, n, c, h, k, st, pad):
+    """omCudaMaxPool2dBackwardGather (the 2x2-block kernel for 3x3 / 2 / 1, the generic one
+    otherwise) against the oracle's sequential loop, bit for bit."""
+    import oracle as orc
+    from omnimatchdeeplearningtool_b200._lib import call
+    from omnimatchdeeplearningtool_b200.backend import CUDABackend as B
+    rng = _rng(40 + h + k)
+    # few distinct values, so windows often share their maximum
+    x = rng.integers(0, 6, (n, c, h, h)).astype(np.float32)
+    P = (h + 2 * pad - k) // st + 1
+    y, idx = _out((n, c, P, P)), _out((n, c, P, P), np.int32)
+    B.maxPool2d(_dev(x).ptr, y.ptr, idx.ptr, n, c, h, h, k, k, st, pad)
+    wy, widx = np.empty((n, c, P, P), np.float32), np.empty((n, c, P, P), np.int32)
+    orc.O.oracle_maxpool2d(x.ctypes.data, wy.ctypes.data, widx.ctypes.data, n, c, h, h, k, st, pad)
+    assert np.array_equal(idx.to_numpy(widx.shape, np.int32), widx)
+    dy = rng.standard_normal(wy.shape, dtype=np.float32)
+    gdx = _out(x.shape)
+    call("omCudaMaxPool2dBackwardGather", _dev(dy).ptr, idx.ptr, gdx.ptr, n, c, h, h, k, k, st, st,
+         pad, pad)
+    wdx = np.empty_like(x)
+    orc.O.oracle_maxpool2d_backward(dy.ctypes.data, widx.ctypes.data, wdx.ctypes.data, n, c, P, P,
+                                    h, h)
+    assert np.array_equal(gdx.to_numpy(x.shape), wdx)
+
+
 def test_pooling(gpu):
     import oracle as orc
     from omnimatchdeeplearningtool_b200.backend import CUDABackend as B
