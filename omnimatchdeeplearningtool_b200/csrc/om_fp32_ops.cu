@@ -253,6 +253,45 @@ __global__ void maxpool_kernel(const float* __restrict__ in, float* __restrict__
     }
 }
 
+// The 3x3 / stride 2 / padding 1 pool with 32-bit indices (input < 2^31 elements): the nine
+// taps are loaded together (clamped addresses, out-of-image taps never win) and scanned in
+// the generic kernel's order with its strict '>', so values and argmax indices are the same.
+__global__ void maxpool_3s2_kernel(const float* __restrict__ in, float* __restrict__ out,
+                                   int* __restrict__ idx, int total, FastDiv fpq, FastDiv fq,
+                                   int H, int W, int P, int Q) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+        const int nc = (int)fdiv((uint32_t)i, fpq);
+        const int pq = i - nc * (int)fpq.d;
+        const int p = (int)fdiv((uint32_t)pq, fq);
+        const int q = pq - p * (int)fq.d;
+        const int base = nc * H * W;
+        float v[9];
+        int ii[9];
+        bool ok[9];
+#pragma unroll
+        for (int r = 0; r < 3; ++r)
+#pragma unroll
+            for (int s = 0; s < 3; ++s) {
+                const int ih = 2 * p - 1 + r, iw = 2 * q - 1 + s;
+                const bool in_img = ih >= 0 && ih < H && iw >= 0 && iw < W;
+                const int a = base + min(max(ih, 0), H - 1) * W + min(max(iw, 0), W - 1);
+                v[r * 3 + s] = __ldg(in + a);
+                ii[r * 3 + s] = a;
+                ok[r * 3 + s] = in_img;
+            }
+        float m = -1e30f;
+        int mi = -1;
+#pragma unroll
+        for (int t = 0; t < 9; ++t)
+            if (ok[t] && v[t] > m) {
+                m = v[t];
+                mi = ii[t];
+            }
+        out[i] = m;
+        if (idx) idx[i] = mi;
+    }
+}
+
 __global__ void maxpool_bwd_kernel(const float* __restrict__ dy, const int* __restrict__ idx,
                                    float* __restrict__ dx, long long nout) {
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < nout;
@@ -910,7 +949,13 @@ extern "C" int omCudaMaxPool2d(const float* pIn, float* pOut, int* pIndices, int
     if (P <= 0 || Q <= 0) return OM_ERR_INVALID;
     if ((long long)nN * nC * nH * nW >= (1LL << 31)) return OM_ERR_UNSUPPORTED;  // int32 indices
     long long total = (long long)nN * nC * P * Q;
-    maxpool_kernel<<<OMB_EW(total)>>>(pIn, pOut, pIndices, nN, nC, nH, nW, nKH, nKW, nSH, nSW, nPH, nPW, P, Q);
+    if (nKH == 3 && nKW == 3 && nSH == 2 && nSW == 2 && nPH == 1 && nPW == 1)
+        maxpool_3s2_kernel<<<OMB_EW(total)>>>(pIn, pOut, pIndices, (int)total,
+                                              make_fastdiv((uint32_t)(P * Q)),
+                                              make_fastdiv((uint32_t)Q), nH, nW, P, Q);
+    else
+        maxpool_kernel<<<OMB_EW(total)>>>(pIn, pOut, pIndices, nN, nC, nH, nW, nKH, nKW, nSH, nSW,
+                                          nPH, nPW, P, Q);
     return after_launch(c);
 }
 
