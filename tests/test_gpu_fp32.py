@@ -198,7 +198,8 @@ def test_batchnorm_fwd_bwd(gpu, training, shape):
     (2, 32, 28, 160, 3, 2, 1, 1),    # several 128-wide output tiles, stride 2
     (8, 64, 14, 64, 1, 1, 0, 0),     # 1x1, no activation
     (2, 3, 64, 64, 7, 2, 3, 1),      # the ImageNet stem shape (3 input channels)
-    (4, 64, 56, 64, 3, 1, 1, 1)])    # a ResNet-18 layer-1 conv at batch 4 (392 groups/channel)
+    (4, 64, 56, 64, 3, 1, 1, 1),     # a ResNet-18 layer-1 conv at batch 4 (392 groups/channel)
+    (1, 4, 5, 8, 3, 1, 130, 1)])     # padding the tensor path refuses: the separate kernels
 def test_conv_batchnorm_stats_in_epilogue(gpu, n, c, h, k, r, stride, pad, act):
     """omCudaConv2dBatchNorm2dAct (BatchNorm statistics from the conv epilogue, combined in a
     fixed order) against omCudaConv2d + omCudaBatchNorm2dAct (two-pass statistics): the conv
