@@ -373,7 +373,8 @@ __device__ __forceinline__ uint32_t sw64(int r, int j) {
 // AB = operand copies per stage (2 for MODE_TF32: hi and lo).
 template <int BN, int OCC, int EXTRA = 0, int MT = 1, int EW = 4, int AB = 1>
 struct Cfg {
-    static constexpr int EPI_BYTES = epi_bytes<EW>();
+    // MODE_TF32 (AB = 2) stores its fp32 NCHW output from registers: no staging sub-tiles
+    static constexpr int EPI_BYTES = AB == 2 ? 0 : epi_bytes<EW>();
     static constexpr int A_BYTES = MT * A_STAGE_BYTES * AB;   // A bytes per stage
     static constexpr int B_STAGE_BYTES = BN * BK * 2 * AB;
     static constexpr int STAGE_BYTES = A_BYTES + B_STAGE_BYTES;
@@ -508,7 +509,8 @@ __global__ void __launch_bounds__(cta_threads<MODE, EW>(), OCC)
                   "MT = 2 tiles");
     static_assert(EW == 4 || (EW == 16 && OCC == 1 && MODE != MODE_STEM) || (EW == 8 && OCC == 1),
                   "epilogue warps");
-    static_assert(MODE != MODE_TF32 || (MT == 1 && EW == 4 && OCC == 1), "TF32 tiles");
+    static_assert(MODE != MODE_TF32 || (MT == 1 && EW == 4 && (OCC == 1 || BN <= 64)),
+                  "TF32 tiles");
     using C = Cfg<BN, OCC, extra_bytes<BN, MODE, OCC, EW>(), MT, EW, MODE == MODE_TF32 ? 2 : 1>;
     constexpr int EPI_BUFS = epi_bufs<EW>();
     constexpr int TM = BM * MT;   // output pixels per tile
@@ -3561,8 +3563,10 @@ static int tf32_conv_run(DeviceCtx* c, float* xhi, float* xlo, int N, int Hp, in
     }
     // maps: A_hi, B_hi, B_lo (output slot), A_lo (residual slot)
     switch (bn) {
-        case 32: return launch<32, MODE_TF32, OM_DTYPE_BF16, 1, 1, 4>(c, ta_hi, tb_hi, tb_lo, ta_lo, p);
-        case 64: return launch<64, MODE_TF32, OM_DTYPE_BF16, 1, 1, 4>(c, ta_hi, tb_hi, tb_lo, ta_lo, p);
+        // 32- and 64-wide tiles run two CTAs per SM (two stages each): two pipelines hide more
+        // of the operand loads' latency than one with four stages
+        case 32: return launch<32, MODE_TF32, OM_DTYPE_BF16, 2, 1, 4>(c, ta_hi, tb_hi, tb_lo, ta_lo, p);
+        case 64: return launch<64, MODE_TF32, OM_DTYPE_BF16, 2, 1, 4>(c, ta_hi, tb_hi, tb_lo, ta_lo, p);
         default: return launch<128, MODE_TF32, OM_DTYPE_BF16, 1, 1, 4>(c, ta_hi, tb_hi, tb_lo, ta_lo, p);
     }
 }
