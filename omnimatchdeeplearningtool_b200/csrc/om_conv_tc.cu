@@ -3887,14 +3887,17 @@ struct WgSwapCfg {
     static constexpr int Y_BOX = NY * 32 * 4;        // NY output channels x 32 pixels
     static constexpr int X_BOX = 128 * 32 * 4;       // the tile's 128 columns x 32 pixels
     static constexpr int STAGE = 2 * Y_BOX + 2 * X_BOX;
-    static constexpr int RAW = (MAX_DYN_SMEM - 2048) / STAGE;
+    // two CTAs per SM: two pipelines hide more of the loads' latency than one twice as deep
+    static constexpr int PER_SM = 2;
+    static constexpr int RAW = ((233472 - 2048) / PER_SM - 1024 - 2048) / STAGE;
     static constexpr int STAGES = RAW > 6 ? 6 : RAW;
     static constexpr int SMEM = STAGES * STAGE + 2048;
     static constexpr uint32_t TMEM = 2 * NY;         // main + correction accumulators
+    static_assert(STAGES >= 2, "pipeline depth");
 };
 
 template <int NY>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(192, 2)
     wgrad_tf32_swap_kernel(const __grid_constant__ CUtensorMap tmY_hi,
                            const __grid_constant__ CUtensorMap tmY_lo,
                            const __grid_constant__ CUtensorMap tmX_hi,
@@ -4155,10 +4158,11 @@ int tf32_wgrad(DeviceCtx* c, const float* x, const float* dy, float* dw, int N, 
     const int num_kb = (int)((NPQ + 31) / 32);
     const int m_tiles = (K + 127) / 128;
     const long long tiles = (long long)((RSk + tpt - 1) / tpt) * cb * m_tiles;
-    // one CTA fits per SM (shared memory), so the CTAs run in waves of num_sms: at most two
-    // full waves (rounding the split count up once made 300 CTAs, three waves, the last with
-    // four CTAs, for a 5-tile layer)
-    long long want = (2LL * c->num_sms) / tiles;
+    // one CTA fits per SM (shared memory; two for the swapped kernel), so the CTAs run in
+    // waves of num_sms (2 num_sms): at most two full waves (rounding the split count up once
+    // made 300 CTAs, three waves, the last with four CTAs, for a 5-tile layer)
+    const int per_sm = Ks <= 64 ? 2 : 1;
+    long long want = (2LL * per_sm * c->num_sms) / tiles;
     long long cap = num_kb < 256 ? num_kb : 256;
     const int splits = (int)(want < 1 ? 1 : (want > cap ? cap : want));
     if (tiles * splits >= (1LL << 31)) return OM_ERR_UNSUPPORTED;
