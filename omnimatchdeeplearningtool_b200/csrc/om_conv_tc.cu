@@ -3687,15 +3687,22 @@ struct WgradParams {
     unsigned int* err;
 };
 
+// Column tile of the plain weight-gradient kernel (output channels > 64).
+constexpr int WG_TILE = 64;
+
 template <int BN>
 struct WgCfg {
     static constexpr int A_BOX = 128 * 32 * 4;      // 128 output channels x 32 pixels
     static constexpr int B_BOX = BN * 32 * 4;       // BN channels x 32 pixels
     static constexpr int STAGE = 2 * A_BOX + 2 * B_BOX;
-    static constexpr int RAW = (MAX_DYN_SMEM - 2048) / STAGE;
+    // 64-column tiles run two CTAs per SM (two pipelines of two stages)
+    static constexpr int PER_SM = BN <= 64 ? 2 : 1;
+    static constexpr int RAW =
+        (PER_SM == 1 ? MAX_DYN_SMEM - 2048 : (233472 - 2048) / 2 - 1024 - 2048) / STAGE;
     static constexpr int STAGES = RAW > 6 ? 6 : RAW;
     static constexpr int SMEM = STAGES * STAGE + 2048;
     static constexpr uint32_t TMEM = 2 * BN;        // main + correction accumulators
+    static_assert(STAGES >= 2, "pipeline depth");
 };
 
 template <int BN>
@@ -4103,8 +4110,8 @@ __global__ void wgrad_reduce_kernel(const float* __restrict__ ws, float* __restr
 static int launch_wgrad(DeviceCtx* c, const CUtensorMap& a_hi, const CUtensorMap& a_lo,
                         const CUtensorMap& b_hi, const CUtensorMap& b_lo, const WgradParams& p,
                         dim3 grid) {
-    using Cf = WgCfg<128>;
-    auto kern = wgrad_tf32_kernel<128>;
+    using Cf = WgCfg<WG_TILE>;
+    auto kern = wgrad_tf32_kernel<WG_TILE>;
     static bool attr_set[64] = {false};
     if (!attr_set[c->device]) {
         OMB_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM));
@@ -4150,9 +4157,11 @@ int tf32_wgrad(DeviceCtx* c, const float* x, const float* dy, float* dw, int N, 
         (long long)P * ((Q + 31) / 32) >= (1LL << 31) || !tf32_pad_ok(Rk, Sk, padk))
         return OM_ERR_UNSUPPORTED;
     if (!load_driver_entry_points()) return OM_ERR_DRIVER;
-    // a tile is 128 columns: tpt taps x csl channels, csl the widest of 128, 64, 32 dividing Cs
-    const int csl = Cs % 128 == 0 ? 128 : (Cs % 64 == 0 ? 64 : 32);
-    const int tpt = 128 / csl;
+    // a tile is TW columns: tpt taps x csl channels, csl the widest of TW, 64, 32 dividing Cs
+    // (TW = 128 for the swapped kernel, WG_TILE for the plain one)
+    const int TW = Ks <= 64 ? 128 : WG_TILE;
+    const int csl = Cs % TW == 0 ? TW : (Cs % 64 == 0 ? 64 : 32);
+    const int tpt = TW / csl;
     const int cb = Cs / csl;
     const int RSk = Rk * Sk;
     const int num_kb = (int)((NPQ + 31) / 32);
@@ -4161,7 +4170,7 @@ int tf32_wgrad(DeviceCtx* c, const float* x, const float* dy, float* dw, int N, 
     // one CTA fits per SM (shared memory; two for the swapped kernel), so the CTAs run in
     // waves of num_sms (2 num_sms): at most two full waves (rounding the split count up once
     // made 300 CTAs, three waves, the last with four CTAs, for a 5-tile layer)
-    const int per_sm = Ks <= 64 ? 2 : 1;
+    const int per_sm = Ks <= 64 ? 2 : WgCfg<WG_TILE>::PER_SM;
     long long want = (2LL * per_sm * c->num_sms) / tiles;
     long long cap = num_kb < 256 ? num_kb : 256;
     const int splits = (int)(want < 1 ? 1 : (want > cap ? cap : want));
