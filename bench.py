@@ -251,9 +251,10 @@ def run_train(args, world, rank, local, dist):
     batch = args.batch if args.batch != BATCH else 128
     net = synth.resnet_spec(18, 1000)
     weights = synth.make_weights(net)
-    # BatchNorm statistics from the conv epilogue (omCudaConv2dBatchNorm2dAct); the training
-    # parity test runs this form at config 3
-    fnet = Fp32Net(net, weights, batch, 224, 224, fused_bn_stats=True)
+    # BatchNorm statistics from the conv epilogue (omCudaConv2dBatchNorm2dAct) and the stem in
+    # its space-to-depth form (omCudaStemConv2dBatchNorm2dAct); the training parity test runs
+    # this form at config 3
+    fnet = Fp32Net(net, weights, batch, 224, 224, fused_bn_stats=True, stem_s2d=True)
     comm = NcclCommunicator(rank, world, timeout_ms=120000) if world > 1 else None
     dp = DataParallel(fnet, DistributedConfig(world, rank), comm)
     x = DeviceBuffer.from_numpy(synth.normal_input(batch, seed=rank))

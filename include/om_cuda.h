@@ -218,10 +218,30 @@ int omCudaConv2dBatchNorm2dAct(const float* pInput, const float* pWeight, const 
  * channels padded to 32); 0 when the weight gradient of this shape makes its own copy (stride-2
  * convs of at most 8 input channels) or the arguments are invalid */
 long long omCudaConvInputSplitBytes(int nBatch, int nCin, int nH, int nW, int nStride);
+/* new: omCudaConv2dBatchNorm2dAct for the image stem (stride 2, at most 8 input channels) with
+ * the convolution in its space-to-depth form: a stride-1 ceil(KH/2) x ceil(KW/2) convolution
+ * over a 32-channel copy of the image holding each 2x2 block's pixels as channels (16 taps of 32
+ * channels for the 7x7/2 ImageNet stem instead of 49 taps of 3). Same arguments and outputs;
+ * the sums run in another order, so results agree with omCudaConv2dBatchNorm2dAct to fp32
+ * rounding, not bit for bit. pInputSplit (may be NULL): a device buffer of
+ * omCudaStemInputSplitBytes(...) bytes that keeps that copy for
+ * omCudaConv2dBackwardWeightSplit. OM_ERR_UNSUPPORTED for any other shape. */
+int omCudaStemConv2dBatchNorm2dAct(const float* pInput, const float* pWeight, const float* pBias,
+                                   float* pConvOut, float* pOutput, const float* pGamma,
+                                   const float* pBeta, float* pRunMean, float* pRunVar,
+                                   float* pSavedMean, float* pSavedInvStd, int nBatch, int nCin,
+                                   int nH, int nW, int nCout, int nKH, int nKW, int nStride,
+                                   int nPad, float fEps, float fMomentum, int nAct,
+                                   void* pInputSplit);
+/* new: bytes of the space-to-depth copy omCudaStemConv2dBatchNorm2dAct keeps (hi and lo fp32
+ * parts of [N, P + ceil(KH/2) - 1, Q + ceil(KW/2) - 1, 32]); 0 for shapes it does not take */
+long long omCudaStemInputSplitBytes(int nBatch, int nCin, int nH, int nW, int nKH, int nKW,
+                                    int nStride, int nPad);
 /* new: omCudaConv2dBackwardWeight reading the input's kept copy (pInputSplit, written by the
- * forward omCudaConv2dBatchNorm2dAct of the same pInput and shape, unchanged since) instead of
- * copying pInput again; pInput is still read where the tensor path does not take the shape.
- * Bit-identical to omCudaConv2dBackwardWeight. */
+ * forward omCudaConv2dBatchNorm2dAct of the same pInput and shape, or for the stem shapes by
+ * omCudaStemConv2dBatchNorm2dAct, unchanged since) instead of copying pInput again; pInput is
+ * still read where the tensor path does not take the shape. Bit-identical to
+ * omCudaConv2dBackwardWeight. */
 int omCudaConv2dBackwardWeightSplit(const float* pInput, const void* pInputSplit,
                                     const float* pGradOutput, float* pGradWeight,
                                     float* pGradBias, int nBatch, int nCin, int nH, int nW,

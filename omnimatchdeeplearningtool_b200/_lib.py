@@ -95,6 +95,8 @@ _SIGS = {
     "omCudaBatchNorm2dAct": [P, P, P, P, P, P, P, P, I, I, I, I, F, F, I, I],
     "omCudaConv2dBatchNorm2dAct": [P, P, P, P, P, P, P, P, P, P, P, I, I, I, I, I, I, I, I, I,
                                    F, F, I, P],
+    "omCudaStemConv2dBatchNorm2dAct": [P, P, P, P, P, P, P, P, P, P, P, I, I, I, I, I, I, I, I,
+                                       I, F, F, I, P],
     "omCudaConv2dBackwardWeightSplit": [P, P, P, P, P, I, I, I, I, I, I, I, I, I],
     "omCudaMaxPool2dBackwardGather": [P, P, P, I, I, I, I, I, I, I, I, I, I],
     "omCudaBatchNorm2dBackwardAct": [P, P, P, P, P, P, P, P, P, I, I, I, I, F, I],
@@ -181,10 +183,13 @@ lib.omCudaStoredChannels.argtypes = [I]
 lib.omCudaStoredChannels.restype = c_int
 lib.omCudaConvInputSplitBytes.argtypes = [I, I, I, I, I]
 lib.omCudaConvInputSplitBytes.restype = c_longlong
+lib.omCudaStemInputSplitBytes.argtypes = [I, I, I, I, I, I, I, I]
+lib.omCudaStemInputSplitBytes.restype = c_longlong
 
 EXPORTED = sorted(list(_SIGS) + ["omCudaGetStream", "omCudaPackedConvWeightElems",
                                  "omCudaPackedStemWeightElems", "omCudaStemWorkspaceBytes",
-                                 "omCudaStoredChannels", "omCudaConvInputSplitBytes"])
+                                 "omCudaStoredChannels", "omCudaConvInputSplitBytes",
+                                 "omCudaStemInputSplitBytes"])
 
 
 def check(status: int, fn: str = "omCuda") -> None:

@@ -57,11 +57,24 @@ inline size_t conv_split_half_bytes(long long N, long long H, long long W, long 
 // The kept input copy of tf32_conv's keep_split written on its own (for a forward that did not
 // take the tensor path).
 int tf32_split_input(DeviceCtx* c, const float* x, int N, int C, int H, int W, float* keep_split);
-// Whether tf32_wgrad reads a kept input copy for this shape (it takes the space-to-depth form,
-// with its own copy, for stride-2 convs of at most 8 input channels).
+// Whether tf32_wgrad reads a kept input copy in tf32_conv's layout for this shape: stride-2
+// convs of at most 8 input channels take the space-to-depth form, whose copy only
+// tf32_conv_s2d keeps.
 inline bool wgrad_reads_kept_split(int Cin, int stride) { return !(stride == 2 && Cin * 4 <= 32); }
+// Space-to-depth form of a stride-2 convolution of at most 8 input channels (the image stem):
+// bytes of one half (hi or lo) of its 32-channel input copy [N, Hs, Ws, 32], rounded up to 256
+// (0 for any other shape); the copy written on its own into keep_split; and the forward
+// convolution in that form (arguments as tf32_conv's; OM_ERR_UNSUPPORTED for other shapes),
+// keeping the copy for tf32_wgrad when keep_split is given.
+size_t s2d_split_half_bytes(int N, int Cin, int H, int W, int R, int S, int stride, int pad);
+int tf32_s2d_split_input(DeviceCtx* c, const float* x, int N, int Cin, int H, int W, int R, int S,
+                         int stride, int pad, float* keep_split);
+int tf32_conv_s2d(DeviceCtx* c, const float* x, int N, int Cin, int H, int W, const float* w,
+                  int Kout, int R, int S, int stride, int pad, const float* bias, float* out,
+                  float* bn_part, float* keep_split);
 // 3xTF32 tensor-core weight gradient of a (stride, pad) convolution: dW [K, Cin, R, S] from
-// X [N, Cin, H, W] and dY [N, K, P, Q], all NCHW fp32 (om_conv_tc.cu).
+// X [N, Cin, H, W] and dY [N, K, P, Q], all NCHW fp32 (om_conv_tc.cu). given_split: the kept
+// input copy (tf32_conv's layout, or tf32_conv_s2d's for the space-to-depth shapes).
 int tf32_wgrad(DeviceCtx* c, const float* x, const float* dy, float* dw, int N, int Cin, int H,
                int W, int K, int R, int S, int stride, int pad, const float* given_split = nullptr);
 }  // namespace tc

@@ -3499,6 +3499,85 @@ __global__ void s2d_split_kernel(const float* __restrict__ x, float* __restrict_
     }
 }
 
+// The same stride-2 copy as s2d_split_kernel (identical values), one block per output row
+// (n, u): the block stages the two source rows 2u - pad + {0, 1} of every channel in shared
+// memory with coalesced loads, then writes the row's Ws x 32 channels as float4 vectors (the
+// four channels 4c .. 4c+3 of a vector are channel c at (py, px) = (0,0), (0,1), (1,0), (1,1)).
+// Shared memory: Cin * 2 * W floats (s2d_rows_fit).
+__global__ void s2d_rows_split_kernel(const float* __restrict__ x, float* __restrict__ hi,
+                                      float* __restrict__ lo, int Cin, int H, int W, int Hs,
+                                      int Ws, int pad) {
+    extern __shared__ float rows[];   // [Cin][2][W]
+    const int u = (int)(blockIdx.x % (unsigned)Hs);
+    const int n = (int)(blockIdx.x / (unsigned)Hs);
+    const int per = 2 * W;
+    for (int i = threadIdx.x; i < Cin * per; i += blockDim.x) {
+        const int c = i / per, rem = i - c * per;
+        const int py = rem / W, w = rem - py * W;
+        const int h = 2 * u + py - pad;
+        rows[i] = (h >= 0 && h < H) ? __ldg(x + (((size_t)n * Cin + c) * H + h) * W + w) : 0.f;
+    }
+    __syncthreads();
+    const size_t row0 = ((size_t)n * Hs + u) * Ws * 32;
+    for (int i = threadIdx.x; i < Ws * 8; i += blockDim.x) {
+        const int v = i >> 3, c = i & 7;
+        float val[4] = {0.f, 0.f, 0.f, 0.f};
+        if (c < Cin) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int py = j >> 1, w = 2 * v + (j & 1) - pad;
+                if (w >= 0 && w < W) val[j] = rows[(c * 2 + py) * W + w];
+            }
+        }
+        float4 h4, l4;
+        h4.x = tf32_rna(val[0]); l4.x = tf32_rna(val[0] - h4.x);
+        h4.y = tf32_rna(val[1]); l4.y = tf32_rna(val[1] - h4.y);
+        h4.z = tf32_rna(val[2]); l4.z = tf32_rna(val[2] - h4.z);
+        h4.w = tf32_rna(val[3]); l4.w = tf32_rna(val[3] - h4.w);
+        const size_t o = row0 + (size_t)v * 32 + c * 4;
+        *reinterpret_cast<float4*>(hi + o) = h4;
+        *reinterpret_cast<float4*>(lo + o) = l4;
+    }
+}
+
+static bool s2d_rows_fit(int Cin, int W) { return (long long)Cin * 2 * W * 4 <= 48 * 1024; }
+
+// The stride-2 space-to-depth copy of NCHW x into hi/lo [N, Hs, Ws, 32] (Cin <= 8).
+static void launch_s2d_split(DeviceCtx* c, const float* x, float* hi, float* lo, int N, int Cin,
+                             int H, int W, int Hs, int Ws, int pad) {
+    const long long rows = (long long)N * Hs;
+    if (s2d_rows_fit(Cin, W) && rows < (1LL << 31)) {
+        s2d_rows_split_kernel<<<(unsigned)rows, 256, (size_t)Cin * 2 * W * 4, c->compute>>>(
+            x, hi, lo, Cin, H, W, Hs, Ws, pad);
+        return;
+    }
+    s2d_split_kernel<<<ew_grid(c, rows * Ws * 32, 256), 256, 0, c->compute>>>(
+        x, hi, lo, N, Cin, H, W, Hs, Ws, 2, pad);
+}
+
+// The filter of a stride-2 convolution in its space-to-depth form, packed K-major hi/lo
+// [Kout, th*tw*32] for tf32_conv_run: kk = (tr*tw + ts)*32 + ch with ch = (c*2 + py)*2 + px
+// holding W[o, c, 2*tr + py, 2*ts + px] (0 past R, S or Cin*4).
+__global__ void pack_tf32_s2d_weight_kernel(const float* __restrict__ w, float* __restrict__ hi,
+                                            float* __restrict__ lo, int Kout, int Cin, int R,
+                                            int S, int th, int tw) {
+    const int kpad = th * tw * 32;
+    const long long total = (long long)Kout * kpad;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int o = (int)(i / kpad);
+        const int kk = (int)(i - (long long)o * kpad);
+        const int t = kk >> 5, ch = kk & 31;
+        const int tr = t / tw, ts = t - tr * tw;
+        const int ci = ch >> 2, r = 2 * tr + ((ch >> 1) & 1), s = 2 * ts + (ch & 1);
+        float v = 0.f;
+        if (ci < Cin && r < R && s < S) v = w[(((size_t)o * Cin + ci) * R + r) * S + s];
+        const float h = tf32_rna(v);
+        hi[i] = h;
+        lo[i] = tf32_rna(v - h);
+    }
+}
+
 // A 3xTF32 convolution over prebuilt NHWC hi/lo copies [N, Hp, Wp, Cs] (Cs % 32 == 0) with a
 // packed hi/lo filter [Kout, R*S*Cs]: result NCHW fp32 [N, Kout, P, Q] (+bias).
 static int tf32_conv_run(DeviceCtx* c, float* xhi, float* xlo, int N, int Hp, int Wp, int Cs,
@@ -3637,10 +3716,11 @@ int tf32_split_input(DeviceCtx* c, const float* x, int N, int C, int H, int W, f
 }
 
 // Geometry of the space-to-depth form of a stride-2 convolution (Cin * 4 <= 32): the 32-channel
-// copy is Hs x Ws and the filter th x tw, stride 1, no padding. Only the weight gradient uses
-// it. The forward keeps the plain form: in the batch-4 training parity case, the space-to-depth
-// form's different rounding (no larger) moved a residual sum of ~1e-6 across zero two blocks
-// later, and that one ReLU decision set a BatchNorm gradient several percent off the exact one.
+// copy is Hs x Ws and the filter th x tw, stride 1, no padding. The weight gradient always uses
+// it; the forward only when asked (tf32_conv_s2d): its summation order differs from the plain
+// form's, and in the batch-4 training parity case that rounding (no larger) moved a residual
+// sum of ~1e-6 across zero two blocks later, and that one ReLU decision set a BatchNorm
+// gradient several percent off the exact one.
 struct S2dGeom {
     int P, Q, th, tw, Hs, Ws;
 };
@@ -3654,6 +3734,68 @@ static bool s2d_geom(int Cin, int H, int W, int R, int S, int stride, int pad, S
     g->Hs = g->P + g->th - 1;
     g->Ws = g->Q + g->tw - 1;
     return true;
+}
+
+size_t s2d_split_half_bytes(int N, int Cin, int H, int W, int R, int S, int stride, int pad) {
+    S2dGeom g;
+    if (!s2d_geom(Cin, H, W, R, S, stride, pad, &g)) return 0;
+    return ((size_t)N * g.Hs * g.Ws * 32 * 4 + 255) / 256 * 256;
+}
+
+// The space-to-depth copy on its own, into keep_split (hi at 0, lo at s2d_split_half_bytes).
+int tf32_s2d_split_input(DeviceCtx* c, const float* x, int N, int Cin, int H, int W, int R, int S,
+                         int stride, int pad, float* keep_split) {
+    S2dGeom g;
+    if (!s2d_geom(Cin, H, W, R, S, stride, pad, &g)) return OM_ERR_UNSUPPORTED;
+    const size_t xb = s2d_split_half_bytes(N, Cin, H, W, R, S, stride, pad);
+    launch_s2d_split(c, x, keep_split,
+                     reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(keep_split) + xb), N,
+                     Cin, H, W, g.Hs, g.Ws, pad);
+    return after_launch(c);
+}
+
+// A stride-2 convolution of at most 8 input channels (the image stem) in its space-to-depth
+// form: the 32-channel copy of x (kept in keep_split when given, for tf32_wgrad) convolved at
+// stride 1 with the th x tw repacked filter. The 7x7/2 stem runs 16 taps of 32 channels instead
+// of 49 taps of 3 channels padded to 32.
+int tf32_conv_s2d(DeviceCtx* c, const float* x, int N, int Cin, int H, int W, const float* w,
+                  int Kout, int R, int S, int stride, int pad, const float* bias, float* out,
+                  float* bn_part, float* keep_split) {
+    S2dGeom g;
+    if (!s2d_geom(Cin, H, W, R, S, stride, pad, &g)) return OM_ERR_UNSUPPORTED;
+    const long long Mll = (long long)N * g.P * g.Q;
+    if (Mll >= (1LL << 31) || N > 65535 || (long long)g.Hs * ((g.Ws + 31) / 32) >= (1LL << 31) ||
+        !tf32_pad_ok(g.th, g.tw, 0))
+        return OM_ERR_UNSUPPORTED;
+    if (!load_driver_entry_points()) return OM_ERR_DRIVER;
+    const size_t xb = s2d_split_half_bytes(N, Cin, H, W, R, S, stride, pad);
+    const size_t we = (size_t)Kout * g.th * g.tw * 32;
+    const size_t wb = (we * 4 + 255) / 256 * 256;
+    const size_t xs = keep_split ? 0 : 2 * xb;
+    uint8_t* scratch = nullptr;
+    cudaError_t ae = cudaMallocAsync(&scratch, xs + 2 * wb, c->compute);
+    if (ae == cudaErrorMemoryAllocation) {
+        cudaGetLastError();
+        return OM_ERR_OOM;
+    }
+    if (ae != cudaSuccess) return OM_ERR_CUDA;
+    uint8_t* xbase = keep_split ? reinterpret_cast<uint8_t*>(keep_split) : scratch;
+    float* xhi = reinterpret_cast<float*>(xbase);
+    float* xlo = reinterpret_cast<float*>(xbase + xb);
+    float* whi = reinterpret_cast<float*>(scratch + xs);
+    float* wlo = reinterpret_cast<float*>(scratch + xs + wb);
+    launch_s2d_split(c, x, xhi, xlo, N, Cin, H, W, g.Hs, g.Ws, pad);
+    int st = after_launch(c);
+    if (st == OM_OK) {
+        pack_tf32_s2d_weight_kernel<<<ew_grid(c, (long long)we, 256), 256, 0, c->compute>>>(
+            w, whi, wlo, Kout, Cin, R, S, g.th, g.tw);
+        st = after_launch(c);
+    }
+    if (st == OM_OK)
+        st = tf32_conv_run(c, xhi, xlo, N, g.Hs, g.Ws, 32, whi, wlo, Kout, g.th, g.tw, bias, out,
+                           1, 0, 1, 0, bn_part);
+    cudaFreeAsync(scratch, c->compute);
+    return st;
 }
 
 }  // namespace tc
@@ -4180,9 +4322,9 @@ int tf32_wgrad(DeviceCtx* c, const float* x, const float* dy, float* dw, int N, 
     const size_t we = (size_t)splits * K * RSk * Cs;
     auto r256 = [](size_t b) { return (b + 255) / 256 * 256; };
     const size_t xb = r256(xe * 4), yb = r256(ye * 4), wb = r256(we * 4);
-    // a kept copy of x from its forward conv (tf32_conv keep_split: the same NHWC hi/lo layout)
-    // replaces the split of x; the space-to-depth form makes its own
-    const bool reuse = given_split != nullptr && !s2d;
+    // a kept copy of x from its forward conv (tf32_conv keep_split, the same NHWC hi/lo layout;
+    // tf32_conv_s2d's for the space-to-depth form) replaces the split of x
+    const bool reuse = given_split != nullptr;
     const size_t xs = reuse ? 0 : 2 * xb;
     uint8_t* scratch = nullptr;
     OMB_CHECK(cudaMallocAsync(&scratch, xs + 2 * yb + wb, c->compute));
@@ -4195,9 +4337,8 @@ int tf32_wgrad(DeviceCtx* c, const float* x, const float* dy, float* dw, int N, 
     if (reuse) {
         // nothing to prepare for x
     } else if (s2d) {
-        s2d_split_kernel<<<ew_grid(c, (long long)xe, 256), 256, 0, c->compute>>>(
-            x, const_cast<float*>(xhi), const_cast<float*>(xlo), N, Cin, H, W, g.Hs, g.Ws, 2,
-            pad);
+        launch_s2d_split(c, x, const_cast<float*>(xhi), const_cast<float*>(xlo), N, Cin, H, W,
+                         g.Hs, g.Ws, pad);
     } else {
         launch_split(c, x, const_cast<float*>(xhi), const_cast<float*>(xlo), N, Cin, H, W, H, W,
                      Cs, 0, 0, 1, 0);

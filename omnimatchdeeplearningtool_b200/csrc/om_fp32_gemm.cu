@@ -401,3 +401,10 @@ extern "C" long long omCudaConvInputSplitBytes(int nBatch, int nCin, int nH, int
     if (!omb::tc::wgrad_reads_kept_split(nCin, nStride)) return 0;
     return 2LL * (long long)omb::tc::conv_split_half_bytes(nBatch, nH, nW, nCin);
 }
+
+extern "C" long long omCudaStemInputSplitBytes(int nBatch, int nCin, int nH, int nW, int nKH,
+                                               int nKW, int nStride, int nPad) {
+    if (nBatch <= 0 || nCin <= 0 || nH <= 0 || nW <= 0 || nKH <= 0 || nKW <= 0) return 0;
+    return 2LL * (long long)omb::tc::s2d_split_half_bytes(nBatch, nCin, nH, nW, nKH, nKW, nStride,
+                                                         nPad);
+}

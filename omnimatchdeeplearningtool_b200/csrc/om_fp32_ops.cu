@@ -872,14 +872,14 @@ extern "C" int omCudaBatchNorm2dAct(const float* pInput, float* pOutput, const f
 // Train-mode conv -> BatchNorm (-> ReLU) with the statistics taken in the conv's epilogue: the
 // conv output is written once and read once (by the normalisation), instead of three times
 // (two statistics passes and the normalisation).
-extern "C" int omCudaConv2dBatchNorm2dAct(const float* pInput, const float* pWeight,
-                                          const float* pBias, float* pConvOut, float* pOutput,
-                                          const float* pGamma, const float* pBeta,
-                                          float* pRunMean, float* pRunVar, float* pSavedMean,
-                                          float* pSavedInvStd, int nBatch, int nCin, int nH,
-                                          int nW, int nCout, int nKH, int nKW, int nStride,
-                                          int nPad, float fEps, float fMomentum, int nAct,
-                                          void* pInputSplit) {
+// s2d: the convolution in its space-to-depth form (tf32_conv_s2d; stride-2 shapes of at most 8
+// input channels only), pInputSplit then receiving that form's copy.
+static int conv_bn_act(const float* pInput, const float* pWeight, const float* pBias,
+                       float* pConvOut, float* pOutput, const float* pGamma, const float* pBeta,
+                       float* pRunMean, float* pRunVar, float* pSavedMean, float* pSavedInvStd,
+                       int nBatch, int nCin, int nH, int nW, int nCout, int nKH, int nKW,
+                       int nStride, int nPad, float fEps, float fMomentum, int nAct,
+                       void* pInputSplit, bool s2d) {
     OMB_CTX_OR_FAIL(c);
     if (!pInput || !pWeight || !pConvOut || !pOutput || !pGamma || !pBeta || !pRunMean ||
         !pRunVar || !pSavedMean || !pSavedInvStd || nBatch <= 0 || nCin <= 0 || nCout <= 0 ||
@@ -890,16 +890,21 @@ extern "C" int omCudaConv2dBatchNorm2dAct(const float* pInput, const float* pWei
     if (P <= 0 || Q <= 0) return OM_ERR_INVALID;
     const long long cnt = (long long)nBatch * P * Q;
     if (cnt >= (1LL << 31)) return OM_ERR_UNSUPPORTED;
+    if (s2d && omb::tc::s2d_split_half_bytes(nBatch, nCin, nH, nW, nKH, nKW, nStride, nPad) == 0)
+        return OM_ERR_UNSUPPORTED;
     const long long G = (cnt + 31) / 32;
     float* part = nullptr;
     OMB_CHECK(cudaMallocAsync(&part, sizeof(float) * 2 * (size_t)nCout * G, c->compute));
     // the input's tensor-core copy is kept in pInputSplit for the weight gradient when the
-    // caller gave one (omCudaConvInputSplitBytes says whether the weight gradient reads it)
+    // caller gave one (omCudaConvInputSplitBytes / omCudaStemInputSplitBytes say whether the
+    // weight gradient reads it)
     float* keep = static_cast<float*>(pInputSplit);
-    if (keep && !omb::tc::wgrad_reads_kept_split(nCin, nStride)) keep = nullptr;
-    int st = omb::tc::tf32_conv(c, pInput, nBatch, nCin, nH, nW, nH, nW, 0, 0, 1, pWeight, nCout,
-                                nKH, nKW, false, nCin, pBias, pConvOut, nStride, nPad, 1, 0, 0,
-                                part, keep);
+    if (keep && !s2d && !omb::tc::wgrad_reads_kept_split(nCin, nStride)) keep = nullptr;
+    int st = s2d ? omb::tc::tf32_conv_s2d(c, pInput, nBatch, nCin, nH, nW, pWeight, nCout, nKH,
+                                          nKW, nStride, nPad, pBias, pConvOut, part, keep)
+                 : omb::tc::tf32_conv(c, pInput, nBatch, nCin, nH, nW, nH, nW, 0, 0, 1, pWeight,
+                                      nCout, nKH, nKW, false, nCin, pBias, pConvOut, nStride,
+                                      nPad, 1, 0, 0, part, keep);
     if (st == OM_OK) {
         bn_chan_finalize_kernel<<<nCout, 256, 0, c->compute>>>(part, (int)G, cnt, nCout,
                                                                pRunMean, pRunVar, pSavedMean,
@@ -914,7 +919,9 @@ extern "C" int omCudaConv2dBatchNorm2dAct(const float* pInput, const float* pWei
                           nStride, nPad);
         if (st != OM_OK) return st;
         if (keep) {
-            st = omb::tc::tf32_split_input(c, pInput, nBatch, nCin, nH, nW, keep);
+            st = s2d ? omb::tc::tf32_s2d_split_input(c, pInput, nBatch, nCin, nH, nW, nKH, nKW,
+                                                     nStride, nPad, keep)
+                     : omb::tc::tf32_split_input(c, pInput, nBatch, nCin, nH, nW, keep);
             if (st != OM_OK) return st;
         }
         return omCudaBatchNorm2dAct(pConvOut, pOutput, pGamma, pBeta, pRunMean, pRunVar,
@@ -924,6 +931,33 @@ extern "C" int omCudaConv2dBatchNorm2dAct(const float* pInput, const float* pWei
     if (st != OM_OK) return st;
     return bn_apply(c, pConvOut, pOutput, pGamma, pBeta, pSavedMean, pSavedInvStd,
                     cnt * nCout, nCout, P * Q, nAct == OM_ACT_RELU ? 1 : 0);
+}
+
+extern "C" int omCudaConv2dBatchNorm2dAct(const float* pInput, const float* pWeight,
+                                          const float* pBias, float* pConvOut, float* pOutput,
+                                          const float* pGamma, const float* pBeta,
+                                          float* pRunMean, float* pRunVar, float* pSavedMean,
+                                          float* pSavedInvStd, int nBatch, int nCin, int nH,
+                                          int nW, int nCout, int nKH, int nKW, int nStride,
+                                          int nPad, float fEps, float fMomentum, int nAct,
+                                          void* pInputSplit) {
+    return conv_bn_act(pInput, pWeight, pBias, pConvOut, pOutput, pGamma, pBeta, pRunMean,
+                       pRunVar, pSavedMean, pSavedInvStd, nBatch, nCin, nH, nW, nCout, nKH, nKW,
+                       nStride, nPad, fEps, fMomentum, nAct, pInputSplit, false);
+}
+
+extern "C" int omCudaStemConv2dBatchNorm2dAct(const float* pInput, const float* pWeight,
+                                              const float* pBias, float* pConvOut,
+                                              float* pOutput, const float* pGamma,
+                                              const float* pBeta, float* pRunMean,
+                                              float* pRunVar, float* pSavedMean,
+                                              float* pSavedInvStd, int nBatch, int nCin, int nH,
+                                              int nW, int nCout, int nKH, int nKW, int nStride,
+                                              int nPad, float fEps, float fMomentum, int nAct,
+                                              void* pInputSplit) {
+    return conv_bn_act(pInput, pWeight, pBias, pConvOut, pOutput, pGamma, pBeta, pRunMean,
+                       pRunVar, pSavedMean, pSavedInvStd, nBatch, nCin, nH, nW, nCout, nKH, nKW,
+                       nStride, nPad, fEps, fMomentum, nAct, pInputSplit, true);
 }
 
 extern "C" int omCudaBatchNorm2dBackwardAct(const float* pGradOutput, const float* pInput,

@@ -479,11 +479,17 @@ class Fp32Net:
     """
 
     def __init__(self, net: NetSpec, weights: Dict[str, np.ndarray], batch: int, h: int = 224,
-                 w: int = 224, grad_ptr: Optional[int] = None, fused_bn_stats: bool = False):
+                 w: int = 224, grad_ptr: Optional[int] = None, fused_bn_stats: bool = False,
+                 stem_s2d: bool = False):
         self.net, self.batch, self.h, self.w = net, batch, h, w
         # train-mode BatchNorm statistics from the conv epilogue (omCudaConv2dBatchNorm2dAct);
         # False: the reference's order of calls, conv then omCudaBatchNorm2dAct
         self.fused_bn_stats = fused_bn_stats
+        # the train-mode image stem in its space-to-depth form (omCudaStemConv2dBatchNorm2dAct,
+        # statistics from its epilogue; its input copy kept for the weight gradient). Same
+        # results to fp32 rounding in another summation order, so off by default: the order of
+        # the plain form is the one the small parity case was pinned with
+        self.stem_s2d = stem_s2d
         self.keep: List[DeviceBuffer] = []
         self._guard: Optional[DeviceBuffer] = None  # the gradient guard's status (device)
         self.param = {}
@@ -563,7 +569,14 @@ class Fp32Net:
         rmean = self.buffers[cv.bn + ".running_mean"].ptr
         rvar = self.buffers[cv.bn + ".running_var"].ptr
         xs = None
-        if train and self.fused_bn_stats:
+        nss = (int(lib.omCudaStemInputSplitBytes(n, c, hh, ww, cv.k, cv.k, cv.stride, cv.pad))
+               if train and self.stem_s2d else 0)
+        if nss > 0:
+            xs = self._buf(key + ".xs", nss)
+            call("omCudaStemConv2dBatchNorm2dAct", x.ptr, self.param[cv.name + ".weight"].ptr,
+                 None, z.ptr, y.ptr, gamma, beta, rmean, rvar, mean.ptr, invstd.ptr, n, c, hh,
+                 ww, cv.cout, cv.k, cv.k, cv.stride, cv.pad, 1e-5, 0.1, act, xs.ptr)
+        elif train and self.fused_bn_stats:
             # batch statistics from the conv's epilogue (omCudaConv2dBatchNorm2dAct): z is
             # written once and read once; the conv's tensor-core copy of x is kept for the
             # weight gradient (xs), which then does not make it again

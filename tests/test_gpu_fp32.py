@@ -264,6 +264,79 @@ def test_conv_batchnorm_stats_in_epilogue(gpu, n, c, h, k, r, stride, pad, act):
     assert gpu.kernel_error() == 0
 
 
+@pytest.mark.parametrize("n,c,h,k,r,pad,act", [
+    (2, 3, 64, 64, 7, 3, 1),      # the ImageNet stem, small image
+    (4, 3, 224, 64, 7, 3, 1),     # the ImageNet stem at 224x224 (P = 112)
+    (2, 3, 30, 64, 7, 3, 0),      # 15x15 output, no activation
+    (2, 8, 33, 32, 3, 1, 1),      # 8 channels (all 32 space-to-depth channels), odd image
+    (3, 1, 17, 16, 5, 2, 1),      # one channel, 5x5 filter
+    (1, 8, 776, 8, 3, 1, 1)])     # rows too wide for the row-staged copy: the per-element kernel
+def test_stem_conv_batchnorm_space_to_depth(gpu, n, c, h, k, r, pad, act):
+    """omCudaStemConv2dBatchNorm2dAct (the stride-2 stem in its space-to-depth form) against
+    omCudaConv2dBatchNorm2dAct (the plain form; same results up to fp32 rounding in another
+    summation order) and against the oracle's conv + train-mode BatchNorm; the space-to-depth
+    copy it keeps gives omCudaConv2dBackwardWeightSplit the bits of omCudaConv2dBackwardWeight.
+    Shapes outside its scope get OM_ERR_UNSUPPORTED and no copy size."""
+    from omnimatchdeeplearningtool_b200._lib import lib, call
+    import oracle as orc
+    stride = 2
+    rng = _rng(700 + c + k + h)
+    x = rng.standard_normal((n, c, h, h), dtype=np.float32)
+    w = (rng.standard_normal((k, c, r, r)) * np.sqrt(2.0 / (c * r * r))).astype(np.float32)
+    g = rng.uniform(0.5, 1.5, k).astype(np.float32)
+    b = rng.standard_normal(k).astype(np.float32)
+    rm = (rng.standard_normal(k) * 0.1).astype(np.float32)
+    rv = rng.uniform(0.5, 1.5, k).astype(np.float32)
+    p = (h + 2 * pad - r) // stride + 1
+    dx, dw, dg, db = _dev(x), _dev(w), _dev(g), _dev(b)
+    nxs = int(lib.omCudaStemInputSplitBytes(n, c, h, h, r, r, stride, pad))
+    hs = p + (r + 1) // 2 - 1
+    half = (n * hs * hs * 32 * 4 + 255) // 256 * 256
+    assert nxs == 2 * half
+    xs = _out((nxs // 4,))
+    res = []
+    for s2d in (True, False):
+        z, y, sm, si = _out((n, k, p, p)), _out((n, k, p, p)), _out((k,)), _out((k,))
+        drm, drv = _dev(rm), _dev(rv)
+        fn = "omCudaStemConv2dBatchNorm2dAct" if s2d else "omCudaConv2dBatchNorm2dAct"
+        call(fn, dx.ptr, dw.ptr, None, z.ptr, y.ptr, dg.ptr, db.ptr, drm.ptr, drv.ptr, sm.ptr,
+             si.ptr, n, c, h, h, k, r, r, stride, pad, 1e-5, 0.1, act, xs.ptr if s2d else None)
+        res.append([t.to_numpy(s) for t, s in ((z, (n, k, p, p)), (y, (n, k, p, p)), (sm, (k,)),
+                                                (si, (k,)), (drm, (k,)), (drv, (k,)))])
+    for a, e in zip(res[0], res[1]):
+        assert rel_err_floor(a, e) <= 1e-5
+    fz, fy, fsm, fsi, frm, frv = res[0]
+    zo = orc.conv2d(x, w, None, stride, pad)
+    assert rel_err_floor(fz, zo) <= TOL
+    wy, wrm, wrv = np.empty_like(zo), rm.copy(), rv.copy()
+    wsm, wsi = np.empty(k, np.float32), np.empty(k, np.float32)
+    orc.O.oracle_batchnorm2d(zo.ctypes.data, wy.ctypes.data, g.ctypes.data, b.ctypes.data,
+                             wrm.ctypes.data, wrv.ctypes.data, wsm.ctypes.data, wsi.ctypes.data,
+                             n, k, p, p, 1e-5, 0.1, 1)
+    if act:
+        wy = np.maximum(wy, 0)
+    assert rel_err_floor(fy, wy) <= TOL
+    assert rel_err_floor(fsi, wsi) <= TOL
+    assert rel_err_floor(frm, wrm) <= TOL
+    assert rel_err_floor(frv, wrv) <= TOL
+    ddy = _dev(rng.standard_normal((n, k, p, p), dtype=np.float32))
+    g1, g2 = _out(w.shape), _out(w.shape)
+    call("omCudaConv2dBackwardWeight", dx.ptr, ddy.ptr, g1.ptr, None, n, c, h, h, k, r, r,
+         stride, pad)
+    call("omCudaConv2dBackwardWeightSplit", dx.ptr, xs.ptr, ddy.ptr, g2.ptr, None, n, c, h, h, k,
+         r, r, stride, pad)
+    assert np.array_equal(g1.to_numpy(w.shape), g2.to_numpy(w.shape))
+    assert gpu.kernel_error() == 0
+    # outside the space-to-depth scope: stride 1, or more than 8 input channels
+    assert lib.omCudaStemInputSplitBytes(n, c, h, h, r, r, 1, pad) == 0
+    assert lib.omCudaStemInputSplitBytes(n, 9, h, h, r, r, 2, pad) == 0
+    z = _out((n, k, h, h))
+    st = lib.omCudaStemConv2dBatchNorm2dAct(dx.ptr, dw.ptr, None, z.ptr, z.ptr, dg.ptr, db.ptr,
+                                            drm.ptr, drv.ptr, sm.ptr, si.ptr, n, c, h, h, k, r,
+                                            r, 1, (r - 1) // 2, 1e-5, 0.1, act, None)
+    assert st == -3
+
+
 @pytest.mark.parametrize("shape", [(8, 24, 16, 16), (4, 16, 9, 7)])
 def test_batchnorm_relu_fused_matches_separate(gpu, shape):
     """omCudaBatchNorm2dAct / omCudaBatchNorm2dBackwardAct give the bits of omCudaBatchNorm2d +

@@ -25,7 +25,7 @@ from conftest import rel_err
 pytestmark = pytest.mark.gpu
 
 
-def _run(batch, hw, classes, seed, fused_bn_stats=False):
+def _run(batch, hw, classes, seed, fused_bn_stats=False, stem_s2d=False):
     import oracle as orc
     from omnimatchdeeplearningtool_b200 import synth
     from omnimatchdeeplearningtool_b200._lib import call
@@ -35,7 +35,7 @@ def _run(batch, hw, classes, seed, fused_bn_stats=False):
     w = synth.make_weights(net)
     x = synth.normal_input(batch, 3, hw, hw, seed=seed)
     y = synth.onehot_labels(batch, classes, seed=seed + 1)
-    fnet = Fp32Net(net, w, batch, hw, hw, fused_bn_stats=fused_bn_stats)
+    fnet = Fp32Net(net, w, batch, hw, hw, fused_bn_stats=fused_bn_stats, stem_s2d=stem_s2d)
     dx, dy = DeviceBuffer.from_numpy(x), DeviceBuffer.from_numpy(y)
     dloss = DeviceBuffer.zeros(4)
     fnet.forward_backward(dx.ptr, dy.ptr, dloss.ptr)
@@ -65,15 +65,17 @@ def test_resnet18_training_step_small(gpu):
     assert rel_err(new_conv1, ow["conv1.weight"]) <= 1e-5
 
 
-@pytest.mark.parametrize("fused_bn_stats", [False, True])
-def test_resnet18_training_step_config3(gpu, fused_bn_stats):
+@pytest.mark.parametrize("fused_bn_stats,stem_s2d", [(False, False), (True, False),
+                                                     (True, True)])
+def test_resnet18_training_step_config3(gpu, fused_bn_stats, stem_s2d):
     gold = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "golden.npz"))
     net, loss, grads, new_fc, new_conv1, oloss, ograds, ow = _run(8, 224, 1000, 11,
-                                                                  fused_bn_stats)
+                                                                  fused_bn_stats, stem_s2d)
     assert abs(loss - oloss) <= 1e-4 * abs(oloss), (loss, oloss)
     errs = np.array([rel_err(grads[name], ograds[name]) for name, _ in net.params])
     ref = gold["train_r18_224_ref_grad_err"]
-    print(f"config3 (fused BN statistics: {fused_bn_stats}): loss err "
+    print(f"config3 (fused BN statistics: {fused_bn_stats}, stem space-to-depth: {stem_s2d}): "
+          f"loss err "
           f"{abs(loss - oloss) / abs(oloss):.2e}, gradient error median "
           f"{np.median(errs):.4f} max {errs.max():.4f} (reference fp32: {np.median(ref):.4f}, "
           f"{ref.max():.4f})")
@@ -137,8 +139,9 @@ def test_guarded_step_clips_like_the_training_loop(gpu):
     assert gpu.kernel_error() == 0
 
 
-@pytest.mark.parametrize("fused_bn_stats", [False, True])
-def test_captured_training_step_matches_eager(gpu, fused_bn_stats):
+@pytest.mark.parametrize("fused_bn_stats,stem_s2d", [(False, False), (True, False),
+                                                     (True, True)])
+def test_captured_training_step_matches_eager(gpu, fused_bn_stats, stem_s2d):
     """Fp32Net.capture_step / replay_step: the whole training step (forward, backward, SGD with
     momentum) as one CUDA graph. After one eager step on both, two replays on one net and two
     eager steps on the other give bit-identical loss, parameters, velocities and BatchNorm
@@ -153,7 +156,7 @@ def test_captured_training_step_matches_eager(gpu, fused_bn_stats):
     y = DeviceBuffer.from_numpy(synth.onehot_labels(4, 10, seed=32))
     out = []
     for graph in (False, True):
-        fnet = Fp32Net(net, w, 4, 64, 64, fused_bn_stats=fused_bn_stats)
+        fnet = Fp32Net(net, w, 4, 64, 64, fused_bn_stats=fused_bn_stats, stem_s2d=stem_s2d)
         loss = DeviceBuffer.zeros(4)
         try:
             fnet.forward_backward(x.ptr, y.ptr, loss.ptr)
