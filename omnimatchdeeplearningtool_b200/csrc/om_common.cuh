@@ -50,6 +50,11 @@ int tf32_conv(DeviceCtx* c, const float* src, int N, int Cin, int Hin, int Win, 
               int Cw, const float* bias, float* out, int stride, int pad, int dil = 1,
               int src_ctot = 0, int out_ktot = 0, float* bn_part = nullptr,
               float* keep_split = nullptr);
+// The backward input of a stride-2 convolution (dY [N, Kout, P, Q] and W [Kout, Cin, R, S] to
+// dX [N, Cin, H, W], NCHW fp32) as one stride-1 3xTF32 convolution per output phase over the
+// plain copy of dY. OM_ERR_UNSUPPORTED for shapes it does not take (nothing launched then).
+int tf32_dgrad_s2(DeviceCtx* c, const float* dy, const float* w, float* dx, int N, int Cin,
+                  int H, int W, int Kout, int R, int S, int pad);
 // Bytes of one half (hi or lo) of a kept input copy: N*H*W*ceil32(C) floats, rounded up to 256.
 inline size_t conv_split_half_bytes(long long N, long long H, long long W, long long C) {
     return ((size_t)(N * H * W * ((C + 31) / 32 * 32)) * 4 + 255) / 256 * 256;

@@ -121,6 +121,10 @@ struct Params {
     int act;
     int out_f32;          // 1: fp32 output stored directly (classifier logits)
     int out_ktot;         // MODE_TF32: channels per output image (0: K; a group writes K of them)
+    // MODE_TF32, optional (ph_w = 0: off): one phase of a stride-2 backward-input pass. Output
+    // pixel (pp, qq) of the P x Q phase grid goes to (2*pp, 2*qq) + ph_off of an output image
+    // ph_w wide with ph_hw pixels per channel
+    int ph_w = 0, ph_hw = 0, ph_off = 0;
     // MODE_TF32, optional (nullptr: off): BatchNorm statistics of the output, per 32-pixel group
     // g and channel k: the group's mean at bn_part[k * bn_groups + g] and its sum of squared
     // deviations from that mean at bn_part[(K + k) * bn_groups + g]
@@ -401,14 +405,20 @@ __device__ __forceinline__ void store_chunk_nchw(const Params& p, int m, int n0,
     const int PQ = p.P * p.Q;
     const int img = m / PQ;
     const int ktot = p.out_ktot ? p.out_ktot : p.K;
-    float* base = static_cast<float*>(p.out) + (size_t)img * ktot * PQ + (m - img * PQ);
+    int pix = m - img * PQ, cs = PQ;   // pixel within the output channel, channel stride
+    if (p.ph_w) {
+        const int pp = pix / p.Q;
+        pix = 2 * pp * p.ph_w + 2 * (pix - pp * p.Q) + p.ph_off;
+        cs = p.ph_hw;
+    }
+    float* base = static_cast<float*>(p.out) + (size_t)img * ktot * cs + pix;
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
         const int k = n0 + j;
         if (k >= p.K) break;
         float o = __uint_as_float(v[j]);
         if (p.bias) o += __ldg(p.bias + k);
-        base[(size_t)k * PQ] = apply_act(o, p.act);
+        base[(size_t)k * cs] = apply_act(o, p.act);
     }
 }
 
@@ -3580,12 +3590,18 @@ __global__ void pack_tf32_s2d_weight_kernel(const float* __restrict__ w, float* 
 
 // A 3xTF32 convolution over prebuilt NHWC hi/lo copies [N, Hp, Wp, Cs] (Cs % 32 == 0) with a
 // packed hi/lo filter [Kout, R*S*Cs]: result NCHW fp32 [N, Kout, P, Q] (+bias).
+// pad is the top and left padding; pad_hi_h / pad_hi_w (-1: pad) the bottom and right. With
+// ph_w > 0 the P x Q result is one phase of a stride-2 backward-input pass (Params::ph_w).
 static int tf32_conv_run(DeviceCtx* c, float* xhi, float* xlo, int N, int Hp, int Wp, int Cs,
                          float* whi, float* wlo, int Kout, int R, int S, const float* bias,
                          float* out, int stride, int pad, int dil, int out_ktot = 0,
-                         float* bn_part = nullptr) {
+                         float* bn_part = nullptr, int pad_hi_h = -1, int pad_hi_w = -1,
+                         int ph_w = 0, int ph_hw = 0, int ph_off = 0) {
     const int eR = (R - 1) * dil + 1, eS = (S - 1) * dil + 1;   // dilated filter extent
-    const int P = (Hp + 2 * pad - eR) / stride + 1, Q = (Wp + 2 * pad - eS) / stride + 1;
+    if (pad_hi_h < 0) pad_hi_h = pad;
+    if (pad_hi_w < 0) pad_hi_w = pad;
+    const int P = (Hp + pad + pad_hi_h - eR) / stride + 1;
+    const int Q = (Wp + pad + pad_hi_w - eS) / stride + 1;
     const long long Mll = (long long)N * P * Q;
     const long long kpad = (long long)R * S * Cs;
     const size_t xe = (size_t)N * Hp * Wp * Cs;
@@ -3607,6 +3623,9 @@ static int tf32_conv_run(DeviceCtx* c, float* xhi, float* xlo, int N, int Hp, in
     p.out_ktot = out_ktot;
     p.bn_part = bn_part;
     p.bn_groups = (int)((Mll + 31) / 32);
+    p.ph_w = ph_w;
+    p.ph_hw = ph_hw;
+    p.ph_off = ph_off;
     p.err = c->err_word;
     // A: im2col views of the hi and lo copies, dims innermost-first (Cs, Wp, Hp, N)
     CUtensorMap ta_hi, ta_lo, tb_hi, tb_lo;
@@ -3614,7 +3633,7 @@ static int tf32_conv_run(DeviceCtx* c, float* xhi, float* xlo, int N, int Hp, in
     cuuint64_t a_strides[3] = {(cuuint64_t)Cs * 4, (cuuint64_t)Wp * Cs * 4,
                                (cuuint64_t)Hp * Wp * Cs * 4};
     int lo_c[2] = {-pad, -pad};
-    int hi_c[2] = {pad - (eS - 1), pad - (eR - 1)};
+    int hi_c[2] = {pad_hi_w - (eS - 1), pad_hi_h - (eR - 1)};
     cuuint32_t a_estr[4] = {1, (cuuint32_t)stride, (cuuint32_t)stride, 1};
     for (int k = 0; k < 2; ++k) {
         CUtensorMap* m = k ? &ta_lo : &ta_hi;
@@ -3702,6 +3721,122 @@ int tf32_conv(DeviceCtx* c, const float* src, int N, int Cin, int Hin, int Win, 
     if (st == OM_OK)
         st = tf32_conv_run(c, xhi, xlo, N, Hp, Wp, Cs, whi, wlo, Kout, R, S, bias, out, stride, pad,
                            dil, out_ktot, bn_part);
+    cudaFreeAsync(scratch, c->compute);
+    return st;
+}
+
+// The filter of one phase of a stride-2 backward-input pass, packed K-major hi/lo
+// [Cin, Rt*St*Ks] for tf32_conv_run: row o = input channel, kk = (t*St + u)*Ks + k holding
+// W[k, o, r0 + 2*(Rt-1-t), s0 + 2*(St-1-u)] (the phase's taps, last first; 0 for k >= Kw).
+__global__ void pack_tf32_phase_weight_kernel(const float* __restrict__ w, float* __restrict__ hi,
+                                              float* __restrict__ lo, int Cin, int Kw, int R,
+                                              int S, int Rt, int St, int r0, int s0, int Ks) {
+    const long long kpad = (long long)Rt * St * Ks;
+    const long long total = (long long)Cin * kpad;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int o = (int)(i / kpad);
+        const int kk = (int)(i - (long long)o * kpad);
+        const int tu = kk / Ks, k = kk - tu * Ks;
+        const int t = tu / St, u = tu - t * St;
+        const int r = r0 + 2 * (Rt - 1 - t), s = s0 + 2 * (St - 1 - u);
+        float v = 0.f;
+        if (k < Kw) v = w[(((size_t)k * Cin + o) * R + r) * S + s];
+        const float h = tf32_rna(v);
+        hi[i] = h;
+        lo[i] = tf32_rna(v - h);
+    }
+}
+
+// Taps of one phase along one dimension of a stride-2 backward-input pass: output positions
+// h = 2i + a take filter rows r = r0 + 2t (t < Rt) at dY row i + off - t; as a stride-1
+// correlation over dY (taps last first) that is top padding lo = Rt - 1 - off, and bottom
+// padding hi making the output the n = ceil((H - a) / 2) positions of the phase.
+struct PhaseDim {
+    int r0, Rt, lo, hi, n;
+};
+static PhaseDim phase_dim(int a, int R, int pad, int H, int P) {
+    PhaseDim d;
+    d.r0 = (a + pad) & 1;
+    d.Rt = d.r0 < R ? (R - d.r0 + 1) / 2 : 0;
+    const int off = (a + pad - d.r0) / 2;
+    d.lo = d.Rt - 1 - off;
+    d.n = (H - a + 1) / 2;
+    d.hi = d.n - P - d.lo + d.Rt - 1;
+    return d;
+}
+
+// Backward input of a stride-2 convolution as four stride-1 convolutions, one per output
+// phase (h mod 2, w mod 2), each over the plain NHWC copy of dY with only the taps that reach
+// that phase. The zero-inserted form computes on the inserted zeros (4x the multiply-adds); the
+// phases add the same nonzero products in the same order. Phases without taps (1x1 filters)
+// are zeroed first. OM_ERR_UNSUPPORTED for shapes whose phases need negative padding.
+int tf32_dgrad_s2(DeviceCtx* c, const float* dy, const float* w, float* dx, int N, int Cin,
+                  int H, int W, int Kout, int R, int S, int pad) {
+    const int P = (H + 2 * pad - R) / 2 + 1, Q = (W + 2 * pad - S) / 2 + 1;
+    if (P <= 0 || Q <= 0) return OM_ERR_INVALID;
+    const int Ks = (Kout + 31) / 32 * 32;
+    PhaseDim ph[2][2];   // [dimension h/w][phase]
+    bool any_empty = false;
+    size_t wtot = 0;
+    for (int a = 0; a < 2; ++a) {
+        ph[0][a] = phase_dim(a, R, pad, H, P);
+        ph[1][a] = phase_dim(a, S, pad, W, Q);
+    }
+    for (int ah = 0; ah < 2; ++ah)
+        for (int aw = 0; aw < 2; ++aw) {
+            const PhaseDim& dh = ph[0][ah];
+            const PhaseDim& dw = ph[1][aw];
+            if (dh.n <= 0 || dw.n <= 0) continue;
+            if (dh.Rt == 0 || dw.Rt == 0) {
+                any_empty = true;
+                continue;
+            }
+            // the kernel takes one top/left padding for both dimensions
+            if (dh.lo != dw.lo || dh.lo < 0 || dh.hi < 0 || dw.hi < 0 || dh.lo > 127 ||
+                !tf32_pad_ok(dh.Rt, dw.Rt, 0) || dh.hi - (dh.Rt - 1) > 127 ||
+                dw.hi - (dw.Rt - 1) > 127)
+                return OM_ERR_UNSUPPORTED;
+            wtot += ((size_t)Cin * dh.Rt * dw.Rt * Ks * 4 + 255) / 256 * 256;
+        }
+    const long long M = (long long)N * ph[0][0].n * ph[1][0].n;
+    if (M >= (1LL << 31) || N > 65535 || (long long)P * ((Q + 31) / 32) >= (1LL << 31) ||
+        (long long)N * Cin * H * W >= (1LL << 31))
+        return OM_ERR_UNSUPPORTED;
+    if (!load_driver_entry_points()) return OM_ERR_DRIVER;
+    const size_t yb = ((size_t)N * P * Q * Ks * 4 + 255) / 256 * 256;
+    uint8_t* scratch = nullptr;
+    cudaError_t ae = cudaMallocAsync(&scratch, 2 * yb + 2 * wtot, c->compute);
+    if (ae == cudaErrorMemoryAllocation) {
+        cudaGetLastError();
+        return OM_ERR_OOM;
+    }
+    if (ae != cudaSuccess) return OM_ERR_CUDA;
+    float* yhi = reinterpret_cast<float*>(scratch);
+    float* ylo = reinterpret_cast<float*>(scratch + yb);
+    launch_split(c, dy, yhi, ylo, N, Kout, P, Q, P, Q, Ks, 0, 0, 1, 0);
+    int st = after_launch(c);
+    if (st == OM_OK && any_empty)
+        st = status_of(cudaMemsetAsync(dx, 0, (size_t)N * Cin * H * W * 4, c->compute));
+    size_t woff = 2 * yb;
+    for (int ah = 0; ah < 2 && st == OM_OK; ++ah)
+        for (int aw = 0; aw < 2 && st == OM_OK; ++aw) {
+            const PhaseDim& dh = ph[0][ah];
+            const PhaseDim& dw = ph[1][aw];
+            if (dh.n <= 0 || dw.n <= 0 || dh.Rt == 0 || dw.Rt == 0) continue;
+            const size_t we = (size_t)Cin * dh.Rt * dw.Rt * Ks;
+            const size_t wb = (we * 4 + 255) / 256 * 256;
+            float* whi = reinterpret_cast<float*>(scratch + woff);
+            float* wlo = reinterpret_cast<float*>(scratch + woff + wb);
+            woff += 2 * wb;
+            pack_tf32_phase_weight_kernel<<<ew_grid(c, (long long)we, 256), 256, 0, c->compute>>>(
+                w, whi, wlo, Cin, Kout, R, S, dh.Rt, dw.Rt, dh.r0, dw.r0, Ks);
+            st = after_launch(c);
+            if (st == OM_OK)
+                st = tf32_conv_run(c, yhi, ylo, N, P, Q, Ks, whi, wlo, Cin, dh.Rt, dw.Rt, nullptr,
+                                   dx, 1, dh.lo, 1, 0, nullptr, dh.hi, dw.hi, W, H * W,
+                                   ah * W + aw);
+        }
     cudaFreeAsync(scratch, c->compute);
     return st;
 }

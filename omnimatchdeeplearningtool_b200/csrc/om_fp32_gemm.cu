@@ -311,6 +311,12 @@ extern "C" int omCudaConv2dBackwardInput(const float* pGradOutput, const float* 
     if (!pGradOutput || !pWeight || !pGradInput || nStride <= 0) return OM_ERR_INVALID;
     int P = (nH + 2 * nPad - nKH) / nStride + 1, Q = (nW + 2 * nPad - nKW) / nStride + 1;
     if (P <= 0 || Q <= 0) return OM_ERR_INVALID;
+    // stride 2: one stride-1 convolution per output phase, no inserted zeros
+    if (nStride == 2) {
+        int st = omb::tc::tf32_dgrad_s2(c, pGradOutput, pWeight, pGradInput, nBatch, nCin, nH, nW,
+                                        nCout, nKH, nKW, nPad);
+        if (st != OM_ERR_UNSUPPORTED && st != OM_ERR_OOM) return st;
+    }
     // dX = (zero-inserted, padded dY) convolved with the rotated, transposed filter, stride 1:
     // dY[n,k,p,q] lands at (R-1-pad + p*stride, S-1-pad + q*stride) of an (H+R-1) x (W+S-1) grid
     if (nPad <= nKH - 1 && nPad <= nKW - 1) {

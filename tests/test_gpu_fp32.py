@@ -50,7 +50,7 @@ CONV = [  # n, c, h, k, r, stride, pad, bias
     (2, 64, 8, 128, 1, 2, 0, False),
     (1, 8, 9, 8, 5, 1, 2, True),
     # the tensor-core (3xTF32) path: several 32-channel k-blocks and 32..128-wide output tiles,
-    # partial tiles in both dimensions, stride-2 backward-input through zero insertion
+    # partial tiles in both dimensions, stride-2 backward input by output phase
     (4, 64, 28, 128, 3, 1, 1, False),
     (2, 128, 14, 256, 3, 2, 1, True),
     (8, 96, 16, 40, 1, 1, 0, False),
@@ -65,6 +65,13 @@ CONV = [  # n, c, h, k, r, stride, pad, bias
     (4, 256, 4, 256, 3, 1, 1, False),
     (4, 256, 4, 512, 3, 2, 1, False),
     (4, 512, 2, 512, 3, 1, 1, False),
+    # stride-2 backward input by output phase: odd maps, 1x1 and 2x2 filters, a 3x3 map; a 5x5
+    # filter whose phases need different top and left padding takes zero insertion
+    (2, 32, 15, 64, 3, 2, 1, False),
+    (3, 48, 9, 32, 1, 2, 0, False),
+    (2, 32, 12, 32, 2, 2, 0, False),
+    (2, 64, 3, 64, 3, 2, 1, False),
+    (2, 16, 13, 32, 5, 2, 2, False),
 ]
 
 
@@ -102,6 +109,29 @@ def test_conv2d_fwd_bwd(gpu, case):
                                         want_db.ctypes.data, n, c, h, h, k, r, r, s, p)
     assert rel_err_floor(dw.to_numpy(w.shape), want_dw) <= TOL
     assert rel_err_floor(db.to_numpy((k,)), want_db) <= TOL
+
+
+@pytest.mark.parametrize("n,c,h,k,r,pad", [(4, 64, 28, 128, 3, 1), (4, 64, 16, 128, 1, 0),
+                                            (2, 32, 15, 64, 3, 1), (2, 3, 32, 16, 7, 3),
+                                            (2, 128, 14, 256, 3, 1)])
+def test_stride2_backward_input_phases_match_zero_insertion(gpu, n, c, h, k, r, pad):
+    """The stride-2 backward input runs one stride-1 convolution per output phase (no inserted
+    zeros). It adds the same nonzero products in the same order as the stride-1 backward input
+    of the zero-inserted dY, so the two agree bit for bit."""
+    from omnimatchdeeplearningtool_b200.backend import CUDABackend as B
+    rng = _rng(900 + c + h)
+    w = rng.standard_normal((k, c, r, r), dtype=np.float32) * np.float32(np.sqrt(2 / (c * r * r)))
+    P = (h + 2 * pad - r) // 2 + 1
+    dy = rng.standard_normal((n, k, P, P), dtype=np.float32)
+    P1 = h + 2 * pad - r + 1
+    dy1 = np.zeros((n, k, P1, P1), np.float32)
+    dy1[:, :, 0:2 * P - 1:2, 0:2 * P - 1:2] = dy
+    dW = _dev(w)
+    dx2, dx1 = _out((n, c, h, h)), _out((n, c, h, h))
+    B.conv2dBackwardInput(_dev(dy).ptr, dW.ptr, dx2.ptr, n, c, h, h, k, r, r, pad, pad, 2, 2)
+    B.conv2dBackwardInput(_dev(dy1).ptr, dW.ptr, dx1.ptr, n, c, h, h, k, r, r, pad, pad, 1, 1)
+    assert np.array_equal(dx2.to_numpy((n, c, h, h)), dx1.to_numpy((n, c, h, h)))
+    assert gpu.kernel_error() == 0
 
 
 def test_grouped_depthwise_conv(gpu):
