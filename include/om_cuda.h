@@ -246,7 +246,15 @@ int omCudaConv2dBackwardWeightSplit(const float* pInput, const void* pInputSplit
                                     const float* pGradOutput, float* pGradWeight,
                                     float* pGradBias, int nBatch, int nCin, int nH, int nW,
                                     int nCout, int nKH, int nKW, int nStride, int nPad);
-/* new: the matching backward (the reference calls its ReLU backward, then :3130). pOutput is the
+/* new: a conv's whole backward, omCudaConv2dBackwardInput (skipped when pGradInput is NULL)
+ * then omCudaConv2dBackwardWeightSplit (pInputSplit may be NULL: omCudaConv2dBackwardWeight),
+ * with one tensor-core copy of pGradOutput read by both passes instead of one copy each.
+ * Bit-identical to the two calls. */
+int omCudaConv2dBackwardSplit(const float* pGradOutput, const float* pInput,
+                              const void* pInputSplit, const float* pWeight, float* pGradInput,
+                              float* pGradWeight, float* pGradBias, int nBatch, int nCin, int nH,
+                              int nW, int nCout, int nKH, int nKW, int nStride, int nPad);
+/* new: the backward of omCudaBatchNorm2dAct (the reference calls its ReLU backward, then :3130). pOutput is the
  * forward's activated output: the incoming gradient is zeroed where pOutput <= 0 inside the BN
  * backward passes. Bit-identical to omCudaReLUBackward followed by omCudaBatchNorm2dBackward. */
 int omCudaBatchNorm2dBackwardAct(const float* pGradOutput, const float* pInput,

@@ -98,6 +98,7 @@ _SIGS = {
     "omCudaStemConv2dBatchNorm2dAct": [P, P, P, P, P, P, P, P, P, P, P, I, I, I, I, I, I, I, I,
                                        I, F, F, I, P],
     "omCudaConv2dBackwardWeightSplit": [P, P, P, P, P, I, I, I, I, I, I, I, I, I],
+    "omCudaConv2dBackwardSplit": [P, P, P, P, P, P, P, I, I, I, I, I, I, I, I, I],
     "omCudaMaxPool2dBackwardGather": [P, P, P, I, I, I, I, I, I, I, I, I, I],
     "omCudaBatchNorm2dBackwardAct": [P, P, P, P, P, P, P, P, P, I, I, I, I, F, I],
     "omCudaBatchNorm2dNoAlloc": [P, P, P, P, P, P, P, P, I, I, I, I, F, F, I],

@@ -54,7 +54,8 @@ int tf32_conv(DeviceCtx* c, const float* src, int N, int Cin, int Hin, int Win, 
 // dX [N, Cin, H, W], NCHW fp32) as one stride-1 3xTF32 convolution per output phase over the
 // plain copy of dY. OM_ERR_UNSUPPORTED for shapes it does not take (nothing launched then).
 int tf32_dgrad_s2(DeviceCtx* c, const float* dy, const float* w, float* dx, int N, int Cin,
-                  int H, int W, int Kout, int R, int S, int pad);
+                  int H, int W, int Kout, int R, int S, int pad, const float* yhi_in = nullptr,
+                  const float* ylo_in = nullptr);
 // Bytes of one half (hi or lo) of a kept input copy: N*H*W*ceil32(C) floats, rounded up to 256.
 inline size_t conv_split_half_bytes(long long N, long long H, long long W, long long C) {
     return ((size_t)(N * H * W * ((C + 31) / 32 * 32)) * 4 + 255) / 256 * 256;
@@ -79,9 +80,22 @@ int tf32_conv_s2d(DeviceCtx* c, const float* x, int N, int Cin, int H, int W, co
                   float* bn_part, float* keep_split);
 // 3xTF32 tensor-core weight gradient of a (stride, pad) convolution: dW [K, Cin, R, S] from
 // X [N, Cin, H, W] and dY [N, K, P, Q], all NCHW fp32 (om_conv_tc.cu). given_split: the kept
-// input copy (tf32_conv's layout, or tf32_conv_s2d's for the space-to-depth shapes).
+// input copy (tf32_conv's layout, or tf32_conv_s2d's for the space-to-depth shapes). given_dy:
+// an NHWC hi/lo copy of dY [N, P, Q, ceil32(K)] (hi at byte 0, lo at dy_split_half_bytes),
+// read in place of a copy of its own.
 int tf32_wgrad(DeviceCtx* c, const float* x, const float* dy, float* dw, int N, int Cin, int H,
-               int W, int K, int R, int S, int stride, int pad, const float* given_split = nullptr);
+               int W, int K, int R, int S, int stride, int pad, const float* given_split = nullptr,
+               const float* given_dy = nullptr);
+inline size_t dy_split_half_bytes(long long N, long long P, long long Q, long long K) {
+    return ((size_t)(N * P * Q * ((K + 31) / 32 * 32)) * 4 + 255) / 256 * 256;
+}
+// The backward input from an NHWC hi/lo copy of dY (as tf32_wgrad's given_dy): stride 1 (square
+// filter, pad <= R-1) as one convolution with the rotated filter, stride 2 by output phase.
+// OM_ERR_UNSUPPORTED for other shapes (nothing launched then).
+int tf32_dgrad_split(DeviceCtx* c, const float* yhi, const float* ylo, const float* w, float* dx,
+                     int N, int Cin, int H, int W, int Kout, int R, int S, int stride, int pad);
+// NHWC hi/lo copy of an NCHW tensor [N, C, P, Q] into hi, lo (channels padded to 32).
+void split_nhwc(DeviceCtx* c, const float* x, float* hi, float* lo, int N, int C, int P, int Q);
 }  // namespace tc
 
 inline int status_of(cudaError_t e) { return e == cudaSuccess ? OM_OK : OM_ERR_CUDA; }

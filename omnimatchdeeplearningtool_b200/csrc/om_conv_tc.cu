@@ -3772,7 +3772,8 @@ static PhaseDim phase_dim(int a, int R, int pad, int H, int P) {
 // phases add the same nonzero products in the same order. Phases without taps (1x1 filters)
 // are zeroed first. OM_ERR_UNSUPPORTED for shapes whose phases need negative padding.
 int tf32_dgrad_s2(DeviceCtx* c, const float* dy, const float* w, float* dx, int N, int Cin,
-                  int H, int W, int Kout, int R, int S, int pad) {
+                  int H, int W, int Kout, int R, int S, int pad, const float* yhi_in,
+                  const float* ylo_in) {
     const int P = (H + 2 * pad - R) / 2 + 1, Q = (W + 2 * pad - S) / 2 + 1;
     if (P <= 0 || Q <= 0) return OM_ERR_INVALID;
     const int Ks = (Kout + 31) / 32 * 32;
@@ -3804,7 +3805,9 @@ int tf32_dgrad_s2(DeviceCtx* c, const float* dy, const float* w, float* dx, int 
         (long long)N * Cin * H * W >= (1LL << 31))
         return OM_ERR_UNSUPPORTED;
     if (!load_driver_entry_points()) return OM_ERR_DRIVER;
-    const size_t yb = ((size_t)N * P * Q * Ks * 4 + 255) / 256 * 256;
+    // dY's NHWC copy: the caller's (yhi_in, ylo_in) or made here
+    const bool have_y = yhi_in != nullptr;
+    const size_t yb = have_y ? 0 : dy_split_half_bytes(N, P, Q, Kout);
     uint8_t* scratch = nullptr;
     cudaError_t ae = cudaMallocAsync(&scratch, 2 * yb + 2 * wtot, c->compute);
     if (ae == cudaErrorMemoryAllocation) {
@@ -3812,10 +3815,13 @@ int tf32_dgrad_s2(DeviceCtx* c, const float* dy, const float* w, float* dx, int 
         return OM_ERR_OOM;
     }
     if (ae != cudaSuccess) return OM_ERR_CUDA;
-    float* yhi = reinterpret_cast<float*>(scratch);
-    float* ylo = reinterpret_cast<float*>(scratch + yb);
-    launch_split(c, dy, yhi, ylo, N, Kout, P, Q, P, Q, Ks, 0, 0, 1, 0);
-    int st = after_launch(c);
+    float* yhi = have_y ? const_cast<float*>(yhi_in) : reinterpret_cast<float*>(scratch);
+    float* ylo = have_y ? const_cast<float*>(ylo_in) : reinterpret_cast<float*>(scratch + yb);
+    int st = OM_OK;
+    if (!have_y) {
+        launch_split(c, dy, yhi, ylo, N, Kout, P, Q, P, Q, Ks, 0, 0, 1, 0);
+        st = after_launch(c);
+    }
     if (st == OM_OK && any_empty)
         st = status_of(cudaMemsetAsync(dx, 0, (size_t)N * Cin * H * W * 4, c->compute));
     size_t woff = 2 * yb;
@@ -3837,6 +3843,44 @@ int tf32_dgrad_s2(DeviceCtx* c, const float* dy, const float* w, float* dx, int 
                                    dx, 1, dh.lo, 1, 0, nullptr, dh.hi, dw.hi, W, H * W,
                                    ah * W + aw);
         }
+    cudaFreeAsync(scratch, c->compute);
+    return st;
+}
+
+void split_nhwc(DeviceCtx* c, const float* x, float* hi, float* lo, int N, int C, int P, int Q) {
+    launch_split(c, x, hi, lo, N, C, P, Q, P, Q, (C + 31) / 32 * 32, 0, 0, 1, 0);
+}
+
+int tf32_dgrad_split(DeviceCtx* c, const float* yhi, const float* ylo, const float* w, float* dx,
+                     int N, int Cin, int H, int W, int Kout, int R, int S, int stride, int pad) {
+    if (stride == 2)
+        return tf32_dgrad_s2(c, nullptr, w, dx, N, Cin, H, W, Kout, R, S, pad, yhi, ylo);
+    if (stride != 1 || R != S || pad < 0 || pad > R - 1) return OM_ERR_UNSUPPORTED;
+    const int P = H + 2 * pad - R + 1, Q = W + 2 * pad - S + 1;
+    if (P <= 0 || Q <= 0) return OM_ERR_INVALID;
+    const int Ks = (Kout + 31) / 32 * 32;
+    const int padk = R - 1 - pad;   // the rotated filter's padding: output H x W
+    const long long kpad = (long long)R * S * Ks;
+    if ((long long)N * H * W >= (1LL << 31) || kpad >= (1LL << 31) || N > 65535 ||
+        (long long)P * ((Q + 31) / 32) >= (1LL << 31) || !tf32_pad_ok(R, S, padk))
+        return OM_ERR_UNSUPPORTED;
+    if (!load_driver_entry_points()) return OM_ERR_DRIVER;
+    const size_t we = (size_t)Cin * kpad, wb = (we * 4 + 255) / 256 * 256;
+    uint8_t* scratch = nullptr;
+    cudaError_t ae = cudaMallocAsync(&scratch, 2 * wb, c->compute);
+    if (ae == cudaErrorMemoryAllocation) {
+        cudaGetLastError();
+        return OM_ERR_OOM;
+    }
+    if (ae != cudaSuccess) return OM_ERR_CUDA;
+    float* whi = reinterpret_cast<float*>(scratch);
+    float* wlo = reinterpret_cast<float*>(scratch + wb);
+    pack_tf32_weight_kernel<<<ew_grid(c, (long long)we, 256), 256, 0, c->compute>>>(
+        w, whi, wlo, Cin, Kout, R, S, Ks, 1, Cin);
+    int st = after_launch(c);
+    if (st == OM_OK)
+        st = tf32_conv_run(c, const_cast<float*>(yhi), const_cast<float*>(ylo), N, P, Q, Ks, whi,
+                           wlo, Cin, R, S, nullptr, dx, 1, padk, 1);
     cudaFreeAsync(scratch, c->compute);
     return st;
 }
@@ -4419,7 +4463,8 @@ static int launch_wgrad_swap(DeviceCtx* c, const CUtensorMap& y_hi, const CUtens
 // four times the channel use of the plain form). Scratch (the hi/lo copies of X and dY and the
 // split partials) comes from the stream-ordered pool.
 int tf32_wgrad(DeviceCtx* c, const float* x, const float* dy, float* dw, int N, int Cin, int H,
-               int W, int K, int R, int S, int stride, int pad, const float* given_split) {
+               int W, int K, int R, int S, int stride, int pad, const float* given_split,
+               const float* given_dy) {
     const int P = (H + 2 * pad - R) / stride + 1, Q = (W + 2 * pad - S) / stride + 1;
     if (P <= 0 || Q <= 0) return OM_ERR_INVALID;
     S2dGeom g;
@@ -4461,13 +4506,39 @@ int tf32_wgrad(DeviceCtx* c, const float* x, const float* dy, float* dw, int N, 
     // tf32_conv_s2d's for the space-to-depth form) replaces the split of x
     const bool reuse = given_split != nullptr;
     const size_t xs = reuse ? 0 : 2 * xb;
+    // A: dY's 32-channel blocks as (32, NPQ, Ks/32), box (32, 32, 4); with at most 64 output
+    // channels the swapped kernel takes all Ks/32 blocks as its N operand. An NHWC copy of dY
+    // [NPQ][Ks] (given_dy: hi, lo at yb) is read in place with strides (Ks*4, 128): the boxes
+    // land in shared memory exactly as from the blocked copy [Ks/32][NPQ][32] made otherwise.
+    CUtensorMap a_hi, a_lo, b_hi, b_lo;
+    cuuint32_t abox[3] = {32, 32, Ks <= 64 ? (cuuint32_t)(Ks / 32) : 4u};
+    cuuint32_t aestr[3] = {1, 1, 1};
+    cuuint64_t adims[3] = {32, (cuuint64_t)NPQ, (cuuint64_t)(Ks / 32)};
+    auto encode_a = [&](const float* hi, const float* lo, const cuuint64_t* astr) {
+        for (int k = 0; k < 2; ++k) {
+            CUresult r = g_encode_tiled(k ? &a_lo : &a_hi, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3,
+                                        const_cast<float*>(k ? lo : hi), adims, astr, abox,
+                                        aestr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                        CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B,
+                                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+            if (r != CUDA_SUCCESS) return false;
+        }
+        return true;
+    };
+    bool dy_given = false;
+    if (given_dy) {
+        const cuuint64_t nstr[2] = {(cuuint64_t)Ks * 4, 128};
+        dy_given = encode_a(given_dy, given_dy + yb / 4, nstr);
+    }
+    const size_t ys = dy_given ? 0 : 2 * yb;
     uint8_t* scratch = nullptr;
-    OMB_CHECK(cudaMallocAsync(&scratch, xs + 2 * yb + wb, c->compute));
+    OMB_CHECK(cudaMallocAsync(&scratch, xs + ys + wb, c->compute));
     const float* xhi = reuse ? given_split : reinterpret_cast<float*>(scratch);
     const float* xlo = reuse ? given_split + xb / 4 : reinterpret_cast<float*>(scratch + xb);
     float* yhi = reinterpret_cast<float*>(scratch + xs);
     float* ylo = reinterpret_cast<float*>(scratch + xs + yb);
-    float* ws = reinterpret_cast<float*>(scratch + xs + 2 * yb);
+    float* ws = reinterpret_cast<float*>(scratch + xs + ys);
     int st = OM_OK;
     if (reuse) {
         // nothing to prepare for x
@@ -4479,27 +4550,13 @@ int tf32_wgrad(DeviceCtx* c, const float* x, const float* dy, float* dw, int N, 
                      Cs, 0, 0, 1, 0);
     }
     if (!reuse) st = after_launch(c);
-    if (st == OM_OK) {
+    if (st == OM_OK && !dy_given) {
         launch_split(c, dy, yhi, ylo, N, K, P, Q, P, Q, Ks, 0, 0, 1, 1);
         st = after_launch(c);
+        const cuuint64_t bstr[2] = {128, (cuuint64_t)NPQ * 128};
+        if (st == OM_OK && !encode_a(yhi, ylo, bstr)) st = OM_ERR_DRIVER;
     }
-    CUtensorMap a_hi, a_lo, b_hi, b_lo;
     if (st == OM_OK) {
-        // A: blocked dY as (32, NPQ, Ks/32), box (32, 32, 4); with at most 64 output channels
-        // the swapped kernel takes all Ks/32 blocks as its N operand
-        cuuint64_t dims[3] = {32, (cuuint64_t)NPQ, (cuuint64_t)(Ks / 32)};
-        cuuint64_t strides[2] = {128, (cuuint64_t)NPQ * 128};
-        cuuint32_t box[3] = {32, 32, Ks <= 64 ? (cuuint32_t)(Ks / 32) : 4u};
-        cuuint32_t estr[3] = {1, 1, 1};
-        for (int k = 0; k < 2 && st == OM_OK; ++k) {
-            CUresult r = g_encode_tiled(k ? &a_lo : &a_hi, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3,
-                                        k ? ylo : yhi, dims, strides, box, estr,
-                                        CU_TENSOR_MAP_INTERLEAVE_NONE,
-                                        CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B,
-                                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-            if (r != CUDA_SUCCESS) st = OM_ERR_DRIVER;
-        }
         // B: im2col of the NHWC input copy, 32 pixels x 32 channels per box
         cuuint64_t bd[4] = {(cuuint64_t)Cs, (cuuint64_t)Wk, (cuuint64_t)Hk, (cuuint64_t)N};
         cuuint64_t bs[3] = {(cuuint64_t)Cs * 4, (cuuint64_t)Wk * Cs * 4,

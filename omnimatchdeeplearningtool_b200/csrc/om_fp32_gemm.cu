@@ -331,9 +331,11 @@ extern "C" int omCudaConv2dBackwardInput(const float* pGradOutput, const float* 
 
 // The weight gradient; pInputSplit (optional): the forward's kept tensor-core copy of pInput
 // (omCudaConv2dBatchNorm2dAct), which the tensor path then reads instead of splitting pInput.
+// given_dy (optional): an NHWC hi/lo copy of pGradOutput the tensor path reads in place.
 static int conv_wgrad(const float* pInput, const void* pInputSplit, const float* pGradOutput,
                       float* pGradWeight, float* pGradBias, int nBatch, int nCin, int nH, int nW,
-                      int nCout, int nKH, int nKW, int nStride, int nPad) {
+                      int nCout, int nKH, int nKW, int nStride, int nPad,
+                      const float* given_dy = nullptr) {
     OMB_CTX_OR_FAIL(c);
     if (!pInput || !pGradOutput || !pGradWeight || nStride <= 0) return OM_ERR_INVALID;
     int P = (nH + 2 * nPad - nKH) / nStride + 1, Q = (nW + 2 * nPad - nKW) / nStride + 1;
@@ -344,7 +346,7 @@ static int conv_wgrad(const float* pInput, const void* pInputSplit, const float*
     // tensor cores (3xTF32) first; the SIMT kernel covers what they do not
     int tst = omb::tc::tf32_wgrad(c, pInput, pGradOutput, pGradWeight, nBatch, nCin, nH, nW, nCout,
                                   nKH, nKW, nStride, nPad,
-                                  static_cast<const float*>(pInputSplit));
+                                  static_cast<const float*>(pInputSplit), given_dy);
     if (tst != OM_ERR_UNSUPPORTED) {
         if (tst != OM_OK || !pGradBias) return tst;
         bias_grad_nchw_kernel<<<nCout, 256, 0, c->compute>>>(pGradOutput, pGradBias, nBatch, nCout, P * Q);
@@ -399,6 +401,46 @@ extern "C" int omCudaConv2dBackwardWeightSplit(const float* pInput, const void* 
     if (!pInputSplit) return OM_ERR_INVALID;
     return conv_wgrad(pInput, pInputSplit, pGradOutput, pGradWeight, pGradBias, nBatch, nCin, nH,
                       nW, nCout, nKH, nKW, nStride, nPad);
+}
+
+extern "C" int omCudaConv2dBackwardSplit(const float* pGradOutput, const float* pInput,
+                                         const void* pInputSplit, const float* pWeight,
+                                         float* pGradInput, float* pGradWeight, float* pGradBias,
+                                         int nBatch, int nCin, int nH, int nW, int nCout,
+                                         int nKH, int nKW, int nStride, int nPad) {
+    OMB_CTX_OR_FAIL(c);
+    if (!pGradOutput || !pInput || !pWeight || !pGradWeight || nStride <= 0 || nPad < 0)
+        return OM_ERR_INVALID;
+    const int P = (nH + 2 * nPad - nKH) / nStride + 1, Q = (nW + 2 * nPad - nKW) / nStride + 1;
+    if (P <= 0 || Q <= 0) return OM_ERR_INVALID;
+    // one NHWC hi/lo copy of dY for both passes (each makes its own where this is not possible)
+    const size_t yb = omb::tc::dy_split_half_bytes(nBatch, P, Q, nCout);
+    float* ys = nullptr;
+    if ((long long)nBatch * P * Q + 128 < (1LL << 31) &&
+        cudaMallocAsync(reinterpret_cast<void**>(&ys), 2 * yb, c->compute) != cudaSuccess) {
+        cudaGetLastError();
+        ys = nullptr;
+    }
+    const float* yhi = ys;
+    const float* ylo = ys ? ys + yb / 4 : nullptr;
+    int st = OM_OK;
+    if (ys) {
+        omb::tc::split_nhwc(c, pGradOutput, ys, ys + yb / 4, nBatch, nCout, P, Q);
+        st = after_launch(c);
+    }
+    if (st == OM_OK && pGradInput) {
+        st = ys ? omb::tc::tf32_dgrad_split(c, yhi, ylo, pWeight, pGradInput, nBatch, nCin, nH,
+                                            nW, nCout, nKH, nKW, nStride, nPad)
+                : OM_ERR_UNSUPPORTED;
+        if (st == OM_ERR_UNSUPPORTED || st == OM_ERR_OOM)
+            st = omCudaConv2dBackwardInput(pGradOutput, pWeight, pGradInput, nBatch, nCin, nH, nW,
+                                           nCout, nKH, nKW, nStride, nPad);
+    }
+    if (st == OM_OK)
+        st = conv_wgrad(pInput, pInputSplit, pGradOutput, pGradWeight, pGradBias, nBatch, nCin,
+                        nH, nW, nCout, nKH, nKW, nStride, nPad, yhi);
+    if (ys) cudaFreeAsync(ys, c->compute);
+    return st;
 }
 
 extern "C" long long omCudaConvInputSplitBytes(int nBatch, int nCin, int nH, int nW,

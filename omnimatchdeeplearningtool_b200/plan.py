@@ -482,8 +482,9 @@ class Fp32Net:
                  w: int = 224, grad_ptr: Optional[int] = None, fused_bn_stats: bool = False,
                  stem_s2d: bool = False):
         self.net, self.batch, self.h, self.w = net, batch, h, w
-        # train-mode BatchNorm statistics from the conv epilogue (omCudaConv2dBatchNorm2dAct);
-        # False: the reference's order of calls, conv then omCudaBatchNorm2dAct
+        # train-mode BatchNorm statistics from the conv epilogue (omCudaConv2dBatchNorm2dAct),
+        # and each conv's two backward passes as one call (omCudaConv2dBackwardSplit); False:
+        # the reference's order of calls, conv then omCudaBatchNorm2dAct
         self.fused_bn_stats = fused_bn_stats
         # the train-mode image stem in its space-to-depth form (omCudaStemConv2dBatchNorm2dAct,
         # statistics from its epilogue; its input copy kept for the weight gradient). Same
@@ -721,6 +722,16 @@ class Fp32Net:
         dx = None
         if need_dx:  # the image itself needs no gradient
             dx = self._buf(key + ".dx", n * rec["c"] * rec["h"] * rec["w"] * 4)
+        if self.fused_bn_stats:
+            # both passes in one call, reading one tensor-core copy of dz (bit-identical)
+            xs = rec.get("xs")
+            call("omCudaConv2dBackwardSplit", dz.ptr, rec["x"].ptr,
+                 xs.ptr if xs is not None else None, self.param[cv.name + ".weight"].ptr,
+                 dx.ptr if dx is not None else None, self.grad(cv.name + ".weight"), None, n,
+                 rec["c"], rec["h"], rec["w"], cv.cout, cv.k, cv.k, cv.stride, cv.pad)
+            self._grad_done(cv.name + ".weight")
+            return dx
+        if need_dx:
             B.conv2dBackwardInput(dz.ptr, self.param[cv.name + ".weight"].ptr, dx.ptr, n, rec["c"],
                                   rec["h"], rec["w"], cv.cout, cv.k, cv.k, cv.pad, cv.pad, cv.stride,
                                   cv.stride)

@@ -367,6 +367,53 @@ def test_stem_conv_batchnorm_space_to_depth(gpu, n, c, h, k, r, pad, act):
     assert st == -3
 
 
+@pytest.mark.parametrize("n,c,h,k,r,stride,pad,with_dx", [
+    (4, 64, 28, 64, 3, 1, 1, True),     # stride 1: the rotated filter over the shared copy
+    (4, 64, 14, 128, 3, 2, 1, True),    # stride 2 by output phase over the shared copy
+    (4, 64, 14, 128, 1, 2, 0, True),    # 1x1 stride 2 (memset + one phase)
+    (2, 96, 9, 40, 1, 1, 0, True),      # 1x1 stride 1, channels not a multiple of 32
+    (2, 32, 11, 48, 3, 1, 2, True),     # pad > R-1: the backward input makes its own copy
+    (2, 3, 64, 64, 7, 2, 3, False)])    # the stem: no dX, space-to-depth weight gradient
+def test_conv_backward_one_dy_copy_matches_separate(gpu, n, c, h, k, r, stride, pad, with_dx):
+    """omCudaConv2dBackwardSplit (one tensor-core copy of dY for the backward-input and the
+    weight-gradient passes, the input's kept copy from the forward) gives the bits of
+    omCudaConv2dBackwardInput + omCudaConv2dBackwardWeight (+ bias gradient)."""
+    from omnimatchdeeplearningtool_b200._lib import lib, call
+    rng = _rng(1100 + c + h)
+    x = rng.standard_normal((n, c, h, h), dtype=np.float32)
+    w = (rng.standard_normal((k, c, r, r)) * np.sqrt(2.0 / (c * r * r))).astype(np.float32)
+    p = (h + 2 * pad - r) // stride + 1
+    dy = rng.standard_normal((n, k, p, p), dtype=np.float32)
+    dx_, dw_, ddy = _dev(x), _dev(w), _dev(dy)
+    # the kept input copy, written by the forward
+    stem = stride == 2 and c * 4 <= 32
+    nxs = int(lib.omCudaStemInputSplitBytes(n, c, h, h, r, r, stride, pad) if stem
+              else lib.omCudaConvInputSplitBytes(n, c, h, h, stride))
+    xs = _out((nxs // 4,)) if nxs > 0 else None
+    if xs is not None:
+        g, b = _dev(np.ones(k, np.float32)), _dev(np.zeros(k, np.float32))
+        z, y, sm, si = _out((n, k, p, p)), _out((n, k, p, p)), _out((k,)), _out((k,))
+        rm, rv = _dev(np.zeros(k, np.float32)), _dev(np.ones(k, np.float32))
+        call("omCudaStemConv2dBatchNorm2dAct" if stem else "omCudaConv2dBatchNorm2dAct",
+             dx_.ptr, dw_.ptr, None, z.ptr, y.ptr, g.ptr, b.ptr, rm.ptr, rv.ptr, sm.ptr, si.ptr,
+             n, c, h, h, k, r, r, stride, pad, 1e-5, 0.1, 1, xs.ptr)
+    dx1, dw1, db1 = _out(x.shape), _out(w.shape), _out((k,))
+    dx2, dw2, db2 = _out(x.shape), _out(w.shape), _out((k,))
+    if with_dx:
+        call("omCudaConv2dBackwardInput", ddy.ptr, dw_.ptr, dx1.ptr, n, c, h, h, k, r, r, stride,
+             pad)
+    call("omCudaConv2dBackwardWeight", dx_.ptr, ddy.ptr, dw1.ptr, db1.ptr, n, c, h, h, k, r, r,
+         stride, pad)
+    call("omCudaConv2dBackwardSplit", ddy.ptr, dx_.ptr, xs.ptr if xs is not None else None,
+         dw_.ptr, dx2.ptr if with_dx else None, dw2.ptr, db2.ptr, n, c, h, h, k, r, r, stride,
+         pad)
+    if with_dx:
+        assert np.array_equal(dx1.to_numpy(x.shape), dx2.to_numpy(x.shape))
+    assert np.array_equal(dw1.to_numpy(w.shape), dw2.to_numpy(w.shape))
+    assert np.array_equal(db1.to_numpy((k,)), db2.to_numpy((k,)))
+    assert gpu.kernel_error() == 0
+
+
 @pytest.mark.parametrize("shape", [(8, 24, 16, 16), (4, 16, 9, 7)])
 def test_batchnorm_relu_fused_matches_separate(gpu, shape):
     """omCudaBatchNorm2dAct / omCudaBatchNorm2dBackwardAct give the bits of omCudaBatchNorm2d +
