@@ -213,6 +213,17 @@ int omCudaConv2dBatchNorm2dAct(const float* pInput, const float* pWeight, const 
                                float* pSavedMean, float* pSavedInvStd, int nBatch, int nCin,
                                int nH, int nW, int nCout, int nKH, int nKW, int nStride, int nPad,
                                float fEps, float fMomentum, int nAct, void* pInputSplit);
+/* new: omCudaConv2dBatchNorm2dAct with a residual branch pResidual [N, Cout, P, Q] added to the
+ * normalised output before nAct (a ResNet block's last conv, its shortcut add and the block's
+ * ReLU): pOutput = act(BN(conv) + pResidual). Bit-identical to omCudaConv2dBatchNorm2dAct with
+ * OM_ACT_NONE, omCudaAdd and omCudaReLU; pOutput > 0 is the block ReLU's backward mask. */
+int omCudaConv2dBatchNorm2dAddAct(const float* pInput, const float* pWeight, const float* pBias,
+                                  float* pConvOut, float* pOutput, const float* pGamma,
+                                  const float* pBeta, float* pRunMean, float* pRunVar,
+                                  float* pSavedMean, float* pSavedInvStd, int nBatch, int nCin,
+                                  int nH, int nW, int nCout, int nKH, int nKW, int nStride,
+                                  int nPad, float fEps, float fMomentum, int nAct,
+                                  void* pInputSplit, const float* pResidual);
 /* new: bytes of the kept input copy that omCudaConv2dBatchNorm2dAct writes and
  * omCudaConv2dBackwardWeightSplit reads (the hi and lo fp32 parts of the NHWC input with the
  * channels padded to 32); 0 when the weight gradient of this shape makes its own copy (stride-2

@@ -95,6 +95,8 @@ _SIGS = {
     "omCudaBatchNorm2dAct": [P, P, P, P, P, P, P, P, I, I, I, I, F, F, I, I],
     "omCudaConv2dBatchNorm2dAct": [P, P, P, P, P, P, P, P, P, P, P, I, I, I, I, I, I, I, I, I,
                                    F, F, I, P],
+    "omCudaConv2dBatchNorm2dAddAct": [P, P, P, P, P, P, P, P, P, P, P, I, I, I, I, I, I, I, I,
+                                      I, F, F, I, P, P],
     "omCudaStemConv2dBatchNorm2dAct": [P, P, P, P, P, P, P, P, P, P, P, I, I, I, I, I, I, I, I,
                                        I, F, F, I, P],
     "omCudaConv2dBackwardWeightSplit": [P, P, P, P, P, I, I, I, I, I, I, I, I, I],

@@ -125,10 +125,13 @@ __global__ void bn_finalize_kernel(const float* __restrict__ psum, const float* 
 // relu = 1: the ReLU of the result, written with the reference's expression (v > 0 ? v : 0).
 __device__ __forceinline__ float bn_act(float v, int relu) { return relu ? (v > 0.f ? v : 0.f) : v; }
 template <int V>
+// y = act(gamma * (x - mean) * invstd + beta [+ res]): with res (a residual branch, same shape)
+// the sum is taken before the activation, as an add and then a ReLU would.
 __global__ void bn_apply_kernel(const float* __restrict__ x, float* __restrict__ y,
                                 const float* __restrict__ gamma, const float* __restrict__ beta,
                                 const float* __restrict__ mean, const float* __restrict__ invstd,
-                                long long total, int C, int HW, int relu) {
+                                long long total, int C, int HW, int relu,
+                                const float* __restrict__ res) {
     const long long nv = total / V;
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < nv;
          i += (long long)gridDim.x * blockDim.x) {
@@ -137,13 +140,20 @@ __global__ void bn_apply_kernel(const float* __restrict__ x, float* __restrict__
         else c = (int)((i / HW) % C);
         if constexpr (V == 4) {
             const float4 v = __ldg(reinterpret_cast<const float4*>(x) + i);
-            reinterpret_cast<float4*>(y)[i] = make_float4(
-                bn_act(gamma[c] * (v.x - mean[c]) * invstd[c] + beta[c], relu),
-                bn_act(gamma[c] * (v.y - mean[c]) * invstd[c] + beta[c], relu),
-                bn_act(gamma[c] * (v.z - mean[c]) * invstd[c] + beta[c], relu),
-                bn_act(gamma[c] * (v.w - mean[c]) * invstd[c] + beta[c], relu));
+            float4 o = make_float4(gamma[c] * (v.x - mean[c]) * invstd[c] + beta[c],
+                                   gamma[c] * (v.y - mean[c]) * invstd[c] + beta[c],
+                                   gamma[c] * (v.z - mean[c]) * invstd[c] + beta[c],
+                                   gamma[c] * (v.w - mean[c]) * invstd[c] + beta[c]);
+            if (res) {
+                const float4 r = __ldg(reinterpret_cast<const float4*>(res) + i);
+                o.x += r.x; o.y += r.y; o.z += r.z; o.w += r.w;
+            }
+            reinterpret_cast<float4*>(y)[i] = make_float4(bn_act(o.x, relu), bn_act(o.y, relu),
+                                                          bn_act(o.z, relu), bn_act(o.w, relu));
         } else {
-            y[i] = bn_act(gamma[c] * (x[i] - mean[c]) * invstd[c] + beta[c], relu);
+            float o = gamma[c] * (x[i] - mean[c]) * invstd[c] + beta[c];
+            if (res) o += res[i];
+            y[i] = bn_act(o, relu);
         }
     }
 }
@@ -690,13 +700,13 @@ static int bn_stats(DeviceCtx* c, const float* x, float* part, int N, int C, int
 }
 static int bn_apply(DeviceCtx* c, const float* x, float* y, const float* gamma, const float* beta,
                     const float* mean, const float* invstd, long long total, int C, int HW,
-                    int relu = 0) {
-    if (bn_vec_flat(HW, total, x, y))
+                    int relu = 0, const float* res = nullptr) {
+    if (bn_vec_flat(HW, total, x, y, res))
         bn_apply_kernel<4><<<ew_grid(c, total / 4, 256), 256, 0, c->compute>>>(
-            x, y, gamma, beta, mean, invstd, total, C, HW, relu);
+            x, y, gamma, beta, mean, invstd, total, C, HW, relu, res);
     else
         bn_apply_kernel<1><<<ew_grid(c, total, 256), 256, 0, c->compute>>>(
-            x, y, gamma, beta, mean, invstd, total, C, HW, relu);
+            x, y, gamma, beta, mean, invstd, total, C, HW, relu, res);
     return after_launch(c);
 }
 
@@ -873,13 +883,14 @@ extern "C" int omCudaBatchNorm2dAct(const float* pInput, float* pOutput, const f
 // conv output is written once and read once (by the normalisation), instead of three times
 // (two statistics passes and the normalisation).
 // s2d: the convolution in its space-to-depth form (tf32_conv_s2d; stride-2 shapes of at most 8
-// input channels only), pInputSplit then receiving that form's copy.
+// input channels only), pInputSplit then receiving that form's copy. pResidual (optional): added
+// to the normalised output before the activation.
 static int conv_bn_act(const float* pInput, const float* pWeight, const float* pBias,
                        float* pConvOut, float* pOutput, const float* pGamma, const float* pBeta,
                        float* pRunMean, float* pRunVar, float* pSavedMean, float* pSavedInvStd,
                        int nBatch, int nCin, int nH, int nW, int nCout, int nKH, int nKW,
                        int nStride, int nPad, float fEps, float fMomentum, int nAct,
-                       void* pInputSplit, bool s2d) {
+                       void* pInputSplit, bool s2d, const float* pResidual = nullptr) {
     OMB_CTX_OR_FAIL(c);
     if (!pInput || !pWeight || !pConvOut || !pOutput || !pGamma || !pBeta || !pRunMean ||
         !pRunVar || !pSavedMean || !pSavedInvStd || nBatch <= 0 || nCin <= 0 || nCout <= 0 ||
@@ -924,13 +935,21 @@ static int conv_bn_act(const float* pInput, const float* pWeight, const float* p
                      : omb::tc::tf32_split_input(c, pInput, nBatch, nCin, nH, nW, keep);
             if (st != OM_OK) return st;
         }
-        return omCudaBatchNorm2dAct(pConvOut, pOutput, pGamma, pBeta, pRunMean, pRunVar,
-                                    pSavedMean, pSavedInvStd, nBatch, nCout, P, Q, fEps, fMomentum,
-                                    1, nAct);
+        if (!pResidual)
+            return omCudaBatchNorm2dAct(pConvOut, pOutput, pGamma, pBeta, pRunMean, pRunVar,
+                                        pSavedMean, pSavedInvStd, nBatch, nCout, P, Q, fEps,
+                                        fMomentum, 1, nAct);
+        st = omCudaBatchNorm2dAct(pConvOut, pOutput, pGamma, pBeta, pRunMean, pRunVar, pSavedMean,
+                                  pSavedInvStd, nBatch, nCout, P, Q, fEps, fMomentum, 1,
+                                  OM_ACT_NONE);
+        if (st == OM_OK) st = omCudaAdd(pOutput, pResidual, pOutput, (int)(cnt * nCout));
+        if (st == OM_OK && nAct == OM_ACT_RELU)
+            st = omCudaReLU(pOutput, pOutput, (int)(cnt * nCout));
+        return st;
     }
     if (st != OM_OK) return st;
     return bn_apply(c, pConvOut, pOutput, pGamma, pBeta, pSavedMean, pSavedInvStd,
-                    cnt * nCout, nCout, P * Q, nAct == OM_ACT_RELU ? 1 : 0);
+                    cnt * nCout, nCout, P * Q, nAct == OM_ACT_RELU ? 1 : 0, pResidual);
 }
 
 extern "C" int omCudaConv2dBatchNorm2dAct(const float* pInput, const float* pWeight,
@@ -944,6 +963,23 @@ extern "C" int omCudaConv2dBatchNorm2dAct(const float* pInput, const float* pWei
     return conv_bn_act(pInput, pWeight, pBias, pConvOut, pOutput, pGamma, pBeta, pRunMean,
                        pRunVar, pSavedMean, pSavedInvStd, nBatch, nCin, nH, nW, nCout, nKH, nKW,
                        nStride, nPad, fEps, fMomentum, nAct, pInputSplit, false);
+}
+
+extern "C" int omCudaConv2dBatchNorm2dAddAct(const float* pInput, const float* pWeight,
+                                             const float* pBias, float* pConvOut, float* pOutput,
+                                             const float* pGamma, const float* pBeta,
+                                             float* pRunMean, float* pRunVar, float* pSavedMean,
+                                             float* pSavedInvStd, int nBatch, int nCin, int nH,
+                                             int nW, int nCout, int nKH, int nKW, int nStride,
+                                             int nPad, float fEps, float fMomentum, int nAct,
+                                             void* pInputSplit, const float* pResidual) {
+    if (!pResidual || nStride <= 0) return OM_ERR_INVALID;
+    if ((long long)nBatch * nCout * ((nH + 2 * nPad - nKH) / nStride + 1) *
+            ((nW + 2 * nPad - nKW) / nStride + 1) >= (1LL << 31))
+        return OM_ERR_UNSUPPORTED;   // the fallback's elementwise ops take int counts
+    return conv_bn_act(pInput, pWeight, pBias, pConvOut, pOutput, pGamma, pBeta, pRunMean,
+                       pRunVar, pSavedMean, pSavedInvStd, nBatch, nCin, nH, nW, nCout, nKH, nKW,
+                       nStride, nPad, fEps, fMomentum, nAct, pInputSplit, false, pResidual);
 }
 
 extern "C" int omCudaStemConv2dBatchNorm2dAct(const float* pInput, const float* pWeight,

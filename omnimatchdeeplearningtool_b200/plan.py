@@ -555,7 +555,11 @@ class Fp32Net:
 
     # ------------------------------------------------------------------ forward pieces
     def _conv_bn(self, key, cv: ConvSpec, x: DeviceBuffer, n, c, hh, ww, relu: bool,
-                 train: bool = True):
+                 train: bool = True, residual: Optional[DeviceBuffer] = None):
+        """conv -> BatchNorm (-> ReLU). With residual (train mode, epilogue statistics only): the
+        block's last conv, its shortcut add and the block ReLU, y = relu(BN(conv) + residual)
+        (omCudaConv2dBatchNorm2dAddAct); the record's relu stays False (the BN backward takes
+        no mask of its own: y > 0 is the block ReLU's mask)."""
         p = (hh + 2 * cv.pad - cv.k) // cv.stride + 1
         q = (ww + 2 * cv.pad - cv.k) // cv.stride + 1
         cnt = n * cv.cout * p * q
@@ -583,10 +587,16 @@ class Fp32Net:
             # weight gradient (xs), which then does not make it again
             nxs = int(lib.omCudaConvInputSplitBytes(n, c, hh, ww, cv.stride))
             xs = self._buf(key + ".xs", nxs) if nxs > 0 else None
-            call("omCudaConv2dBatchNorm2dAct", x.ptr, self.param[cv.name + ".weight"].ptr, None,
-                 z.ptr, y.ptr, gamma, beta, rmean, rvar, mean.ptr, invstd.ptr, n, c, hh, ww,
-                 cv.cout, cv.k, cv.k, cv.stride, cv.pad, 1e-5, 0.1, act,
-                 xs.ptr if xs is not None else None)
+            if residual is not None:
+                call("omCudaConv2dBatchNorm2dAddAct", x.ptr, self.param[cv.name + ".weight"].ptr,
+                     None, z.ptr, y.ptr, gamma, beta, rmean, rvar, mean.ptr, invstd.ptr, n, c,
+                     hh, ww, cv.cout, cv.k, cv.k, cv.stride, cv.pad, 1e-5, 0.1, _lib.ACT_RELU,
+                     xs.ptr if xs is not None else None, residual.ptr)
+            else:
+                call("omCudaConv2dBatchNorm2dAct", x.ptr, self.param[cv.name + ".weight"].ptr,
+                     None, z.ptr, y.ptr, gamma, beta, rmean, rvar, mean.ptr, invstd.ptr, n, c,
+                     hh, ww, cv.cout, cv.k, cv.k, cv.stride, cv.pad, 1e-5, 0.1, act,
+                     xs.ptr if xs is not None else None)
         else:
             B.conv2d(x.ptr, self.param[cv.name + ".weight"].ptr, None, z.ptr, n, c, hh, ww,
                      cv.cout, cv.k, cv.k, cv.pad, cv.pad, cv.stride, cv.stride)
@@ -636,17 +646,23 @@ class Fp32Net:
                                                  False, train)
             main = []
             out, oc, oh, ow = inp, ic, ih, iw
+            # train mode with epilogue statistics: the shortcut add and the block ReLU ride on
+            # the last BatchNorm's normalisation pass
+            fuse_add = train and self.fused_bn_stats
             for j, cv in enumerate(blk.convs):
                 last = j == len(blk.convs) - 1
                 out, oh, ow, rec = self._conv_bn(f"b{bi}.c{j}", cv, out, n, oc, oh, ow, not last,
-                                                 train)
+                                                 train, sc if (last and fuse_add) else None)
                 oc = cv.cout
                 main.append(rec)
             cnt = n * oc * oh * ow
-            s = self._buf(f"b{bi}.sum", cnt * 4)
-            B.add(out.ptr, sc.ptr, s.ptr, cnt)
-            a = self._buf(f"b{bi}.out", cnt * 4)
-            B.relu(s.ptr, a.ptr, cnt)
+            if fuse_add:
+                s = a = out   # relu(BN + shortcut); a > 0 where the sum was > 0
+            else:
+                s = self._buf(f"b{bi}.sum", cnt * 4)
+                B.add(out.ptr, sc.ptr, s.ptr, cnt)
+                a = self._buf(f"b{bi}.out", cnt * 4)
+                B.relu(s.ptr, a.ptr, cnt)
             blocks.append(dict(inp=inp, c=ic, h=ih, w=iw, main=main, ds=ds_rec, s=s, oc=oc, oh=oh,
                                ow=ow))
             cur, c, hh, ww = a, oc, oh, ow

@@ -367,6 +367,46 @@ def test_stem_conv_batchnorm_space_to_depth(gpu, n, c, h, k, r, pad, act):
     assert st == -3
 
 
+@pytest.mark.parametrize("n,c,h,k,r,stride,pad,act", [
+    (4, 64, 28, 64, 3, 1, 1, 1),      # a ResNet-18 block's last conv (4-float path)
+    (2, 32, 15, 48, 3, 1, 1, 1),      # odd map: the scalar path
+    (2, 64, 14, 128, 1, 1, 0, 0),     # no activation
+    (1, 4, 5, 8, 3, 1, 130, 1)])      # padding the tensor path refuses: the separate kernels
+def test_conv_batchnorm_residual_relu_matches_separate(gpu, n, c, h, k, r, stride, pad, act):
+    """omCudaConv2dBatchNorm2dAddAct (a block's last conv + BN, the shortcut add and the block
+    ReLU in the normalisation pass) gives the bits of omCudaConv2dBatchNorm2dAct (no
+    activation), omCudaAdd and omCudaReLU."""
+    from omnimatchdeeplearningtool_b200._lib import call
+    rng = _rng(1300 + c + h)
+    x = rng.standard_normal((n, c, h, h), dtype=np.float32)
+    w = (rng.standard_normal((k, c, r, r)) * np.sqrt(2.0 / (c * r * r))).astype(np.float32)
+    g = rng.uniform(0.5, 1.5, k).astype(np.float32)
+    b = rng.standard_normal(k).astype(np.float32)
+    p = (h + 2 * pad - r) // stride + 1
+    res = rng.standard_normal((n, k, p, p), dtype=np.float32)
+    dx, dw, dg, db, dres = _dev(x), _dev(w), _dev(g), _dev(b), _dev(res)
+    outs = []
+    for fused in (True, False):
+        z, y, sm, si = _out((n, k, p, p)), _out((n, k, p, p)), _out((k,)), _out((k,))
+        rm, rv = _dev(np.zeros(k, np.float32)), _dev(np.ones(k, np.float32))
+        if fused:
+            call("omCudaConv2dBatchNorm2dAddAct", dx.ptr, dw.ptr, None, z.ptr, y.ptr, dg.ptr,
+                 db.ptr, rm.ptr, rv.ptr, sm.ptr, si.ptr, n, c, h, h, k, r, r, stride, pad, 1e-5,
+                 0.1, act, None, dres.ptr)
+        else:
+            call("omCudaConv2dBatchNorm2dAct", dx.ptr, dw.ptr, None, z.ptr, y.ptr, dg.ptr, db.ptr,
+                 rm.ptr, rv.ptr, sm.ptr, si.ptr, n, c, h, h, k, r, r, stride, pad, 1e-5, 0.1, 0,
+                 None)
+            call("omCudaAdd", y.ptr, dres.ptr, y.ptr, n * k * p * p)
+            if act:
+                call("omCudaReLU", y.ptr, y.ptr, n * k * p * p)
+        outs.append([t.to_numpy(sh) for t, sh in ((z, (n, k, p, p)), (y, (n, k, p, p)),
+                                                   (sm, (k,)), (si, (k,)), (rm, (k,)), (rv, (k,)))])
+    for a, e in zip(outs[0], outs[1]):
+        assert np.array_equal(a, e)
+    assert gpu.kernel_error() == 0
+
+
 @pytest.mark.parametrize("n,c,h,k,r,stride,pad,with_dx", [
     (4, 64, 28, 64, 3, 1, 1, True),     # stride 1: the rotated filter over the shared copy
     (4, 64, 14, 128, 3, 2, 1, True),    # stride 2 by output phase over the shared copy
