@@ -4401,30 +4401,33 @@ __global__ void __launch_bounds__(192, 2)
 // dW[k, c, r, s] = sum over splits (in order) of the partial at (k, tap, ch): for a plain
 // convolution tap = r*S + s and ch = c; for the space-to-depth form (f = 2) tap =
 // (r/2)*tw + s/2 and ch = (c*2 + r%2)*2 + s%2 over the th x tw filter.
+// Threads walk the partials' layout (k, tap, ch), so neighbouring threads read neighbouring
+// floats of every split; each one sums its element's splits in order and writes dw[k, c, r, s]
+// (entries of the padded channels or taps are skipped).
 __global__ void wgrad_reduce_kernel(const float* __restrict__ ws, float* __restrict__ dw, int K,
                                     int C, int R, int S, int RSg, int tw, int Cs, int splits,
                                     int f) {
-    const long long total = (long long)K * C * R * S;
     const size_t split_elems = (size_t)K * RSg * Cs;
-    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
-         i += (long long)gridDim.x * blockDim.x) {
-        const int sx = (int)(i % S);
-        long long t = i / S;
-        const int r = (int)(t % R);
-        t /= R;
-        const int c = (int)(t % C), k = (int)(t / C);
-        int tap, ch;
+    for (long long o = blockIdx.x * (long long)blockDim.x + threadIdx.x; o < (long long)split_elems;
+         o += (long long)gridDim.x * blockDim.x) {
+        const int ch = (int)(o % Cs);
+        const long long t = o / Cs;
+        const int tap = (int)(t % RSg), k = (int)(t / RSg);
+        int c, r, sx;
         if (f == 1) {
-            tap = r * S + sx;
-            ch = c;
+            c = ch;
+            r = tap / S;
+            sx = tap - r * S;
         } else {
-            tap = (r / f) * tw + sx / f;
-            ch = (c * f + r % f) * f + sx % f;
+            c = ch / (f * f);
+            r = (tap / tw) * f + (ch / f) % f;
+            sx = (tap % tw) * f + ch % f;
         }
-        const size_t o = ((size_t)k * RSg + tap) * Cs + ch;
+        if (c >= C || r >= R || sx >= S) continue;
         float sum = 0.f;
-        for (int z = 0; z < splits; ++z) sum += ws[z * split_elems + o];
-        dw[i] = sum;
+#pragma unroll 4
+        for (int z = 0; z < splits; ++z) sum += __ldg(ws + z * split_elems + o);
+        dw[(((size_t)k * C + c) * R + r) * S + sx] = sum;
     }
 }
 
@@ -4593,7 +4596,7 @@ int tf32_wgrad(DeviceCtx* c, const float* x, const float* dy, float* dw, int N, 
             st = launch_wgrad(c, a_hi, a_lo, b_hi, b_lo, p, grid);
     }
     if (st == OM_OK) {
-        const long long total = (long long)K * Cin * R * S;
+        const long long total = (long long)K * RSk * Cs;
         wgrad_reduce_kernel<<<ew_grid(c, total, 256), 256, 0, c->compute>>>(
             ws, dw, K, Cin, R, S, RSk, Sk, Cs, splits, s2d ? 2 : 1);
         st = after_launch(c);
