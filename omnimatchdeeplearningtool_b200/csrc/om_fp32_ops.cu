@@ -124,9 +124,11 @@ __global__ void bn_finalize_kernel(const float* __restrict__ psum, const float* 
 // (HW % 4 == 0), one 32-bit division per vector (total < 2^32); V = 1: any shape.
 // relu = 1: the ReLU of the result, written with the reference's expression (v > 0 ? v : 0).
 __device__ __forceinline__ float bn_act(float v, int relu) { return relu ? (v > 0.f ? v : 0.f) : v; }
-template <int V>
 // y = act(gamma * (x - mean) * invstd + beta [+ res]): with res (a residual branch, same shape)
-// the sum is taken before the activation, as an add and then a ReLU would.
+// the sum is taken before the activation, as an add and then a ReLU would. V = 4: float4
+// vectors; PE: a vector may span channels (HW % 4 != 0), each element looks up its own channel.
+// Every element gets the same expression as with V = 1.
+template <int V, bool PE = false>
 __global__ void bn_apply_kernel(const float* __restrict__ x, float* __restrict__ y,
                                 const float* __restrict__ gamma, const float* __restrict__ beta,
                                 const float* __restrict__ mean, const float* __restrict__ invstd,
@@ -139,11 +141,19 @@ __global__ void bn_apply_kernel(const float* __restrict__ x, float* __restrict__
         if constexpr (V == 4) c = (int)(((unsigned)i * 4u / (unsigned)HW) % (unsigned)C);
         else c = (int)((i / HW) % C);
         if constexpr (V == 4) {
+            int c1 = c, c2 = c, c3 = c;
+            if constexpr (PE) {
+                const unsigned e = (unsigned)i * 4u;
+                c = (int)((e / (unsigned)HW) % (unsigned)C);
+                c1 = (int)(((e + 1u) / (unsigned)HW) % (unsigned)C);
+                c2 = (int)(((e + 2u) / (unsigned)HW) % (unsigned)C);
+                c3 = (int)(((e + 3u) / (unsigned)HW) % (unsigned)C);
+            }
             const float4 v = __ldg(reinterpret_cast<const float4*>(x) + i);
             float4 o = make_float4(gamma[c] * (v.x - mean[c]) * invstd[c] + beta[c],
-                                   gamma[c] * (v.y - mean[c]) * invstd[c] + beta[c],
-                                   gamma[c] * (v.z - mean[c]) * invstd[c] + beta[c],
-                                   gamma[c] * (v.w - mean[c]) * invstd[c] + beta[c]);
+                                   gamma[c1] * (v.y - mean[c1]) * invstd[c1] + beta[c1],
+                                   gamma[c2] * (v.z - mean[c2]) * invstd[c2] + beta[c2],
+                                   gamma[c3] * (v.w - mean[c3]) * invstd[c3] + beta[c3]);
             if (res) {
                 const float4 r = __ldg(reinterpret_cast<const float4*>(res) + i);
                 o.x += r.x; o.y += r.y; o.z += r.z; o.w += r.w;
@@ -233,7 +243,7 @@ __global__ void bn_bwd_finalize_kernel(const float* __restrict__ pg, const float
 }
 
 // dx = gamma*invstd/M * (M*dy - dbeta - xhat*dgamma)   (cpu_backend.ixx:847-892)
-template <int V>
+template <int V, bool PE = false>   // V and PE as in bn_apply_kernel
 __global__ void bn_bwd_apply_kernel(const float* __restrict__ dy, const float* __restrict__ x,
                                     const float* __restrict__ mean, const float* __restrict__ invstd,
                                     const float* __restrict__ gamma, const float* __restrict__ dgamma,
@@ -256,11 +266,23 @@ __global__ void bn_bwd_apply_kernel(const float* __restrict__ dy, const float* _
                 g.z = m.z > 0.f ? g.z : 0.f; g.w = m.w > 0.f ? g.w : 0.f;
             }
             const float4 v = __ldg(reinterpret_cast<const float4*>(x) + i);
-            reinterpret_cast<float4*>(dx)[i] =
-                make_float4(k * (M * g.x - db - (v.x - mu) * is * dg),
-                            k * (M * g.y - db - (v.y - mu) * is * dg),
-                            k * (M * g.z - db - (v.z - mu) * is * dg),
-                            k * (M * g.w - db - (v.w - mu) * is * dg));
+            if constexpr (PE) {
+                float o[4];
+                const float gv[4] = {g.x, g.y, g.z, g.w}, xv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int ce = (int)((((unsigned)i * 4u + e) / (unsigned)HW) % (unsigned)C);
+                    const float ise = invstd[ce], mue = mean[ce], ke = gamma[ce] * ise / M;
+                    o[e] = ke * (M * gv[e] - dbeta[ce] - (xv[e] - mue) * ise * dgamma[ce]);
+                }
+                reinterpret_cast<float4*>(dx)[i] = make_float4(o[0], o[1], o[2], o[3]);
+            } else {
+                reinterpret_cast<float4*>(dx)[i] =
+                    make_float4(k * (M * g.x - db - (v.x - mu) * is * dg),
+                                k * (M * g.y - db - (v.y - mu) * is * dg),
+                                k * (M * g.z - db - (v.z - mu) * is * dg),
+                                k * (M * g.w - db - (v.w - mu) * is * dg));
+            }
         } else {
             const float xh = (x[i] - mu) * is;
             const float g = mask ? (mask[i] > 0.f ? dy[i] : 0.f) : dy[i];
@@ -717,6 +739,11 @@ static int bn_splits(DeviceCtx* c, int C, long long cnt) {
 static bool aligned16f(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 // 4-float vectors for the elementwise BN kernels: whole vectors share a channel, every pointer is
 // 16-byte aligned and the 32-bit vector index math holds
+// 4-float vectors that may span channels (the kernels' PE form): whole vectors, aligned pointers
+static bool bn_vec_any(long long total, const void* a, const void* b, const void* d = nullptr) {
+    return total % 4 == 0 && aligned16f(a) && aligned16f(b) && (!d || aligned16f(d)) &&
+           total < (1LL << 32);
+}
 static bool bn_vec_flat(int HW, long long total, const void* a, const void* b,
                         const void* d = nullptr) {
     return HW % 4 == 0 && aligned16f(a) && aligned16f(b) && (!d || aligned16f(d)) &&
@@ -741,6 +768,9 @@ static int bn_apply(DeviceCtx* c, const float* x, float* y, const float* gamma, 
                     int relu = 0, const float* res = nullptr) {
     if (bn_vec_flat(HW, total, x, y, res))
         bn_apply_kernel<4><<<ew_grid(c, total / 4, 256), 256, 0, c->compute>>>(
+            x, y, gamma, beta, mean, invstd, total, C, HW, relu, res);
+    else if (bn_vec_any(total, x, y, res))
+        bn_apply_kernel<4, true><<<ew_grid(c, total / 4, 256), 256, 0, c->compute>>>(
             x, y, gamma, beta, mean, invstd, total, C, HW, relu, res);
     else
         bn_apply_kernel<1><<<ew_grid(c, total, 256), 256, 0, c->compute>>>(
@@ -886,6 +916,10 @@ static int bn_backward(const float* pGradOutput, const float* pInput, const floa
     const long long total = cnt * nChannels;
     if (bn_vec_flat(HW, total, pGradOutput, pInput, pGradInput) && (!pMask || aligned16f(pMask)))
         bn_bwd_apply_kernel<4><<<ew_grid(c, total / 4, 256), 256, 0, c->compute>>>(
+            pGradOutput, pInput, pMean, pInvStd, pGamma, pGradGamma, pGradBeta, pGradInput, total,
+            nChannels, HW, (float)cnt, pMask);
+    else if (bn_vec_any(total, pGradOutput, pInput, pGradInput) && (!pMask || aligned16f(pMask)))
+        bn_bwd_apply_kernel<4, true><<<ew_grid(c, total / 4, 256), 256, 0, c->compute>>>(
             pGradOutput, pInput, pMean, pInvStd, pGamma, pGradGamma, pGradBeta, pGradInput, total,
             nChannels, HW, (float)cnt, pMask);
     else
